@@ -1,0 +1,312 @@
+// Parity oracle - TEST INFRASTRUCTURE ONLY. See oracle.h for the reference map.
+//
+// The wave is restated literally, one simulation at a time, in the reference's order. All
+// arithmetic is fp32 with one rounding per operation (built with -ffp-contract=off), in the
+// operand order the reference's torch expressions evaluate.
+#include "oracle.h"
+#include "gomoku_rules.h"
+#include "synth_eval.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <vector>
+
+namespace {
+
+struct Tree {
+  int cap, size, cells, actions;
+  oracle_config cfg{};
+  oracle_eval_fn eval = nullptr;
+  void* ctx = nullptr;
+  int num_nodes = 0;
+  std::vector<int32_t> N, VL, parent, action, child_start, child_count, mc;
+  std::vector<float> W, P;
+  std::vector<uint8_t> terminal;
+  std::vector<int8_t> player, boards;
+  oracle_result res{};
+  std::vector<float> feat, pol, val;
+
+  Tree(int cap_, int size_) : cap(cap_), size(size_), cells(size_ * size_), actions(size_ * size_) {
+    N.assign(cap, 0); VL.assign(cap, 0); parent.assign(cap, -2); action.assign(cap, -1);
+    child_start.assign(cap, 0); child_count.assign(cap, 0); mc.assign(cap, 0);
+    W.assign(cap, 0.f); P.assign(cap, 0.f); terminal.assign(cap, 0);
+    player.assign(cap, 0); boards.assign((size_t)cap * cells, 0);
+  }
+
+  const int8_t* board(int n) const { return &boards[(size_t)n * cells]; }
+
+  void features(int n, float* out) const {
+    oracle::gomoku_features(board(n), size, player[n], mc[n], n == 0 ? -1 : action[n], out);
+  }
+
+  // evaluator call on a list of nodes (one evaluate_batch call)
+  void evaluate(const std::vector<int>& nodes) {
+    const int n = (int)nodes.size();
+    if (n == 0) return;
+    feat.assign((size_t)n * oracle::kPlanes * cells, 0.f);
+    pol.assign((size_t)n * actions, 0.f);
+    val.assign(n, 0.f);
+    for (int i = 0; i < n; ++i) features(nodes[i], &feat[(size_t)i * oracle::kPlanes * cells]);
+    if (eval)
+      eval(ctx, n, feat.data(), pol.data(), val.data());
+    else
+      oracle_synth_eval(n, oracle::kPlanes, cells, actions, feat.data(), pol.data(), val.data());
+    res.eval_calls++;
+    res.eval_positions += n;
+  }
+
+  float vl_value() const { return -std::fabs(cfg.virtual_loss); }
+  int vl_count(int c) const { return cfg.enable_virtual_loss ? VL[c] : 0; }
+
+  // UCB score of child c under parent visit count np (wave_search.py:1287-1296, 1059-1072;
+  // node_data_manager.py:379-390).
+  float score(int c, int32_t np) const {
+    float ne = (float)(N[c] + vl_count(c));
+    float we = W[c];
+    if (cfg.enable_virtual_loss) we = W[c] + (float)VL[c] * vl_value();
+    float q = ne > 0.0f ? we / ne : 0.0f;
+    float sq = std::sqrt(std::max((float)np, 1.0f));
+    float u = ((cfg.c_puct * P[c]) * sq) / (1.0f + ne);
+    return q + u;
+  }
+
+  void add_vl(int c) { if (cfg.enable_virtual_loss) VL[c] += 1; }
+
+  // wave_search.py:779-979 + csr_tree.py:391-449 for the unique, ascending `leaves`.
+  int expand(const std::vector<int>& leaves) {
+    std::vector<int> todo;
+    for (int n : leaves)
+      if (n >= 0 && n < num_nodes && child_count[n] == 0 && !terminal[n]) todo.push_back(n);
+    if (todo.empty()) return 0;
+    evaluate(todo);
+    std::vector<float> pol_copy = pol;
+    for (size_t i = 0; i < todo.size(); ++i) {
+      const int n = todo[i];
+      const float* p = &pol_copy[i * actions];
+      const int8_t* b = board(n);
+      std::vector<int> legal;
+      for (int a = 0; a < actions; ++a)
+        if (b[a] == 0) legal.push_back(a);
+      if (legal.empty()) continue;
+      float sum = 0.0f;
+      for (int a : legal) sum += p[a];
+      const float denom = sum + 1e-8f;
+      const int k = (int)legal.size();
+      if (num_nodes + k > cap) return 1;  // "Tree full" (csr_tree.py:405-406)
+      child_start[n] = num_nodes;
+      child_count[n] = k;
+      for (int j = 0; j < k; ++j) {
+        const int c = num_nodes++;
+        const int a = legal[j];
+        N[c] = 0; W[c] = 0.f; VL[c] = 0; P[c] = p[a] / denom;
+        parent[c] = n; action[c] = a; child_count[c] = 0;
+        std::memcpy(&boards[(size_t)c * cells], b, cells);
+        boards[(size_t)c * cells + a] = player[n];
+        player[c] = (int8_t)(3 - player[n]);
+        mc[c] = mc[n] + 1;
+        terminal[c] = oracle::gomoku_terminal(board(c), size) ? 1 : 0;
+      }
+    }
+    return 0;
+  }
+
+  int begin(const oracle_config* c, const int8_t* root, oracle_eval_fn e, void* x) {
+    cfg = *c;
+    if (cfg.board_size != size || cfg.max_nodes > cap || cfg.max_wave_size <= 0) return 2;
+    eval = e; ctx = x;
+    res = oracle_result{};
+    num_nodes = 1;
+    N[0] = 0; W[0] = 0.f; VL[0] = 0; P[0] = 1.0f; parent[0] = -1; action[0] = -1;
+    child_count[0] = 0; terminal[0] = 0;
+    int stones = 0;
+    for (int i = 0; i < cells; ++i) { boards[i] = root[i]; stones += root[i] != 0; }
+    player[0] = (stones % 2 == 0) ? 1 : 2;
+    mc[0] = stones;
+    int st = expand({0});
+    res.status = st;
+    return st;
+  }
+
+  int wave(int w) {
+    const int D = cfg.max_depth;
+    std::vector<int> path((size_t)w * D, 0), len(w, 1), cur(w, 0);
+    std::vector<char> active(w, 1);
+    // --- selection (wave_search.py:711-777, 1104-1335)
+    for (int depth = 1; depth < D; ++depth) {
+      std::map<int, std::vector<int>> groups;  // parent -> sims (ascending)
+      for (int s = 0; s < w; ++s)
+        if (active[s]) groups[cur[s]].push_back(s);
+      if (groups.empty()) break;
+      for (auto& g : groups) {
+        const int p = g.first;
+        const std::vector<int>& sims = g.second;
+        std::vector<int> kids;
+        for (int j = 0; j < child_count[p]; ++j) {
+          int c = child_start[p] + j;
+          if (p > 0 && board(p)[action[c]] != 0) continue;  // legal filter (no-op in Gomoku)
+          kids.push_back(c);
+        }
+        if (kids.empty()) {
+          for (int s : sims) active[s] = 0;
+          continue;
+        }
+        const int n = (int)kids.size(), k = (int)sims.size();
+        std::vector<float> sc(n);
+        for (int i = 0; i < n; ++i) sc[i] = score(kids[i], N[p]);
+        std::vector<int> order(n);
+        for (int i = 0; i < n; ++i) order[i] = i;
+        std::stable_sort(order.begin(), order.end(),
+                         [&](int a, int b) { return sc[a] > sc[b]; });
+        std::vector<int> sel(k);
+        int used;  // number of leading ranks that receive simulations
+        int boundary;
+        if (k <= n) {
+          for (int i = 0; i < k; ++i) sel[i] = kids[order[i]];
+          used = k; boundary = k;
+        } else {
+          const int base = k / n, extra = k % n;
+          int idx = 0;
+          for (int i = 0; i < n; ++i) {
+            int cnt = base + (i < extra ? 1 : 0);
+            for (int t = 0; t < cnt; ++t) sel[idx++] = kids[order[i]];
+          }
+          used = n; boundary = extra;
+        }
+        if (boundary > 0 && boundary < n && sc[order[boundary - 1]] == sc[order[boundary]])
+          res.boundary_ties++;
+        for (int i = 1; i < used; ++i)
+          if (sc[order[i - 1]] == sc[order[i]]) res.order_ties++;
+        for (int i = 0; i < k; ++i) add_vl(sel[i]);
+        for (int i = 0; i < k; ++i) {
+          const int s = sims[i];
+          path[(size_t)s * D + depth] = sel[i];
+          len[s] = depth + 1;
+          cur[s] = sel[i];
+        }
+      }
+    }
+    std::vector<int> leaf(w);
+    for (int s = 0; s < w; ++s) leaf[s] = path[(size_t)s * D + len[s] - 1];
+    // --- expansion (wave_search.py:779-979)
+    std::vector<int> uniq(leaf);
+    std::sort(uniq.begin(), uniq.end());
+    uniq.erase(std::unique(uniq.begin(), uniq.end()), uniq.end());
+    if (expand(uniq)) { res.status = 1; return 1; }
+    // --- child pick (wave_search.py:981-1102)
+    std::vector<int> fin(leaf);
+    for (int n : uniq) {
+      if (child_count[n] == 0) continue;
+      int best = -1;
+      float bs = 0.f;
+      for (int j = 0; j < child_count[n]; ++j) {
+        int c = child_start[n] + j;
+        if (board(n)[action[c]] != 0) continue;
+        float s = score(c, N[n]);
+        if (best < 0 || s > bs) { best = c; bs = s; }
+      }
+      if (best < 0) continue;
+      add_vl(best);  // one non-accumulating += for all simulations at n
+      for (int s = 0; s < w; ++s)
+        if (leaf[s] == n) {
+          fin[s] = best;
+          if (len[s] < D) { path[(size_t)s * D + len[s]] = best; len[s] += 1; }
+        }
+    }
+    // --- evaluation (wave_search.py:1337-1457): every simulation, duplicates included
+    evaluate(fin);
+    std::vector<float> v(val);
+    // --- backup (mcts_gpu_accelerator.py:378-393), sequential fp32
+    for (int s = 0; s < w; ++s)
+      for (int d = 0; d < len[s]; ++d) {
+        int n = path[(size_t)s * D + d];
+        N[n] += 1;
+        W[n] += (d % 2 == 0) ? v[s] : -v[s];
+      }
+    // --- virtual-loss revert (wave_search.py:1513-1552)
+    if (cfg.enable_virtual_loss)
+      for (int s = 0; s < w; ++s)
+        for (int d = 1; d < len[s]; ++d) {
+          int n = path[(size_t)s * D + d];
+          VL[n] = std::max(VL[n] - 1, 0);
+        }
+    res.waves++;
+    return 0;
+  }
+};
+
+}  // namespace
+
+extern "C" {
+
+void* oracle_tree_create(int max_nodes, int board_size) {
+  if (max_nodes < 1 || board_size < 5 || board_size > 19) return nullptr;
+  return new Tree(max_nodes, board_size);
+}
+
+void oracle_tree_destroy(void* t) { delete static_cast<Tree*>(t); }
+
+int oracle_begin(void* t, const oracle_config* cfg, const int8_t* root, oracle_eval_fn e, void* x) {
+  return static_cast<Tree*>(t)->begin(cfg, root, e, x);
+}
+
+int oracle_wave(void* t, int w) {
+  Tree* tr = static_cast<Tree*>(t);
+  if (w <= 0) return 2;
+  return tr->wave(w);
+}
+
+void oracle_get_result(void* t, oracle_result* out) {
+  Tree* tr = static_cast<Tree*>(t);
+  *out = tr->res;
+  out->num_nodes = tr->num_nodes;
+}
+
+int oracle_search(void* t, const oracle_config* cfg, const int8_t* root, oracle_eval_fn e,
+                  void* x, oracle_result* out) {
+  Tree* tr = static_cast<Tree*>(t);
+  int st = tr->begin(cfg, root, e, x);
+  int done = 0;
+  while (st == 0 && done < cfg->num_simulations) {
+    int w = std::min(cfg->max_wave_size, cfg->num_simulations - done);
+    st = tr->wave(w);
+    done += w;
+  }
+  tr->res.status = st;
+  if (out) oracle_get_result(t, out);
+  return st;
+}
+
+int oracle_export(void* t, int32_t* visits, float* wsum, float* priors, int32_t* vl,
+                  int32_t* parent, int32_t* action, uint8_t* terminal) {
+  Tree* tr = static_cast<Tree*>(t);
+  const size_t n = tr->num_nodes;
+  if (visits) std::memcpy(visits, tr->N.data(), n * 4);
+  if (wsum) std::memcpy(wsum, tr->W.data(), n * 4);
+  if (priors) std::memcpy(priors, tr->P.data(), n * 4);
+  if (vl) std::memcpy(vl, tr->VL.data(), n * 4);
+  if (parent) std::memcpy(parent, tr->parent.data(), n * 4);
+  if (action) std::memcpy(action, tr->action.data(), n * 4);
+  if (terminal) std::memcpy(terminal, tr->terminal.data(), n);
+  return (int)n;
+}
+
+int oracle_root_policy(void* t, double* policy) {
+  Tree* tr = static_cast<Tree*>(t);
+  const int A = tr->actions;
+  for (int a = 0; a < A; ++a) policy[a] = 0.0;
+  long long total = 0;
+  for (int j = 0; j < tr->child_count[0]; ++j) total += tr->N[tr->child_start[0] + j];
+  const int n = tr->child_count[0];
+  if (n == 0) {
+    for (int a = 0; a < A; ++a) policy[a] = 1.0 / A;
+    return 0;
+  }
+  for (int j = 0; j < n; ++j) {
+    int c = tr->child_start[0] + j;
+    policy[tr->action[c]] = total > 0 ? (double)tr->N[c] / (double)total : 1.0 / n;
+  }
+  return 0;
+}
+}

@@ -1,0 +1,180 @@
+"""Generate the golden search fixtures from the REFERENCE implementation itself.
+
+Runs the reference's deterministic CPU search path
+    MCTS(MCTSConfig(backend='gpu', device='cpu', wave_async_expansion=False, dirichlet_epsilon=0,
+                    enable_subtree_reuse=False, ...), evaluator).search(board)
+(python/mcts/core/mcts.py:924, python/mcts/core/wave_search.py:555) imported from the reference
+source tree, driven by the integer-exact synthetic evaluator (numpy twin in oracle/pyoracle.py).
+Each case is written to tests/golden/search_<name>.npz with:
+  * the root board and configuration,
+  * the root policy (fp64) and root-children visit counts / value sums,
+  * SHA-256 digests of the whole tree (visit counts, value sums, priors, virtual-loss counts,
+    parent ids, parent actions, children table),
+  * the full node arrays for small trees,
+  * a digest of every feature tensor the reference passed to its evaluator, in call order.
+
+Usage (needs the reference tree and its C++ game engines built by `make -C oracle ref`):
+    python tests/golden/make_golden.py [--reference /root/reference] [--only NAME ...]
+This runs only in the build container; the GPU box never reads the reference.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import os
+import sys
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+FULL_ARRAYS_MAX_NODES = 6000
+
+
+def digest(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def dense_board(seed: int, empties: int) -> np.ndarray:
+    """A nearly full board without five in a row: colour = 1 + ((r + 2c) % 4 >= 2)."""
+    r, c = np.mgrid[0:15, 0:15]
+    b = (1 + ((r + 2 * c) % 4 >= 2)).astype(np.int8)
+    rng = np.random.default_rng(seed)
+    b.flat[rng.choice(225, empties, replace=False)] = 0
+    return b
+
+
+def open_four_board() -> np.ndarray:
+    b = np.zeros((15, 15), np.int8)
+    b[7, 3:7] = 1                      # black to move has an open four on row 7
+    b[2, 2], b[3, 10], b[11, 4], b[12, 12] = 2, 2, 2, 2
+    return b
+
+
+def root_five_board() -> np.ndarray:
+    b = np.zeros((15, 15), np.int8)
+    b[7, 3:8] = 1                      # the root already contains a black five
+    b[1, 1], b[2, 9], b[10, 3], b[12, 7], b[13, 13] = 2, 2, 2, 2, 2
+    return b
+
+
+def cases():
+    from omoknuni_quantum_b200.roots import random_root
+    return [
+        # name, board, sims, wave, c_puct, virtual_loss, enable_vl, capacity
+        ("cfg0_seed0", random_root(0), 800, 256, 1.4, 1.0, True, 200000),
+        ("cfg0_seed1", random_root(1), 800, 256, 1.4, 1.0, True, 200000),
+        ("ragged_seed2", random_root(2), 300, 128, 1.4, 1.0, True, 200000),
+        ("wave16_seed3", random_root(3), 256, 16, 1.4, 1.0, True, 200000),
+        ("dense", dense_board(7, 30), 200, 32, 1.4, 1.0, True, 200000),
+        ("empty_root", np.zeros((15, 15), np.int8), 128, 64, 1.4, 1.0, True, 200000),
+        ("open_four", open_four_board(), 200, 64, 1.4, 1.0, True, 200000),
+        ("root_five", root_five_board(), 64, 32, 1.4, 1.0, True, 200000),
+        ("novl_c25_seed4", random_root(4), 200, 64, 2.5, 1.0, False, 200000),
+        ("wave1_seed6", random_root(6), 12, 1, 1.4, 1.0, True, 200000),
+        ("cfg1_seed5", random_root(5), 1600, 256, 1.4, 1.0, True, 400000),
+    ]
+
+
+class TracingSynthEvaluator:
+    """Reference-facing evaluator: numpy synthetic evaluator + a digest of each call's features."""
+
+    def __init__(self):
+        from oracle.pyoracle import synth_eval
+        self._eval = synth_eval
+        self.calls = 0
+        self.positions = 0
+        self._h = hashlib.sha256()
+
+    def evaluate_batch(self, features):
+        import torch
+        f = features.cpu().numpy() if hasattr(features, "cpu") else np.asarray(features)
+        f = np.ascontiguousarray(f, dtype=np.float32)
+        self.calls += 1
+        self.positions += f.shape[0]
+        self._h.update(hashlib.sha256(f.tobytes()).digest())
+        p, v = self._eval(f)
+        return torch.from_numpy(p), torch.from_numpy(v)
+
+    def trace_digest(self) -> str:
+        return self._h.hexdigest()
+
+
+def run_reference(board, sims, wave, c_puct, vl, enable_vl, cap):
+    from mcts.core.mcts import MCTS
+    from mcts.core.mcts_config import MCTSConfig
+    from mcts.gpu.gpu_game_states import GameType
+    cfg = MCTSConfig(backend="gpu", device="cpu", wave_async_expansion=False,
+                     dirichlet_epsilon=0.0, enable_subtree_reuse=False, max_wave_size=wave,
+                     c_puct=c_puct, virtual_loss=vl, enable_virtual_loss=enable_vl,
+                     num_simulations=sims, max_tree_nodes=cap, initial_tree_nodes=cap,
+                     game_type=GameType.GOMOKU, board_size=15)
+    ev = TracingSynthEvaluator()
+    m = MCTS(cfg, ev)
+    t0 = time.time()
+    policy = m.search(board.copy())
+    dt = time.time() - t0
+    tree = m.tree
+    n = int(tree.num_nodes)
+    nd = tree.node_data
+    out = dict(
+        visits=nd.visit_counts[:n].numpy().astype(np.int32),
+        value_sums=nd.value_sums[:n].numpy().astype(np.float32),
+        priors=nd.node_priors[:n].numpy().astype(np.float32),
+        virtual_loss=nd.virtual_loss_counts[:n].numpy().astype(np.int32),
+        parent=nd.parent_indices[:n].numpy().astype(np.int32),
+        action=nd.parent_actions[:n].numpy().astype(np.int32),
+        children=tree.children[:n].numpy().astype(np.int32),
+    )
+    return np.asarray(policy, np.float64), out, ev, dt
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("OMQ_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", nargs="*")
+    args = ap.parse_args()
+    sys.dont_write_bytecode = True
+    sys.path.insert(0, REPO)
+    sys.path.insert(0, os.path.join(REPO, "oracle", "_ref"))
+    sys.path.insert(0, os.path.join(args.reference, "python"))
+    import logging
+    logging.disable(logging.WARNING)
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+
+    for name, board, sims, wave, c, vl, evl, cap in cases():
+        if args.only and name not in args.only:
+            continue
+        policy, arr, ev, dt = run_reference(board, sims, wave, c, vl, evl, cap)
+        n = arr["visits"].shape[0]
+        # the dense children table must be the one implied by (parent, action)
+        ch = np.full_like(arr["children"], -1)
+        ch[arr["parent"][1:], arr["action"][1:]] = np.arange(1, n, dtype=np.int32)
+        assert np.array_equal(ch, arr["children"]), name
+        root_kids = np.nonzero(arr["parent"] == 0)[0]
+        rec = dict(
+            board=board.astype(np.int8), sims=sims, wave=wave, c_puct=np.float32(c),
+            virtual_loss=np.float32(vl), enable_vl=int(evl), capacity=cap,
+            num_nodes=n, policy=policy, final_move=int(np.argmax(policy)),
+            root_visits=arr["visits"][0], root_value_sum=arr["value_sums"][0],
+            root_children=root_kids.astype(np.int32),
+            root_children_visits=arr["visits"][root_kids],
+            root_children_value_sums=arr["value_sums"][root_kids],
+            eval_calls=ev.calls, eval_positions=ev.positions, eval_trace=ev.trace_digest(),
+            reference_seconds=dt,
+        )
+        for k in ("visits", "value_sums", "priors", "virtual_loss", "parent", "action", "children"):
+            rec["sha_" + k] = digest(arr[k])
+        if n <= FULL_ARRAYS_MAX_NODES:
+            for k in ("visits", "value_sums", "priors", "virtual_loss", "parent", "action"):
+                rec["full_" + k] = arr[k]
+        path = os.path.join(HERE, f"search_{name}.npz")
+        np.savez_compressed(path, **rec)
+        print(f"{name}: nodes={n} move={rec['final_move']} evals={ev.calls}/{ev.positions} "
+              f"{dt:.1f}s -> {os.path.basename(path)} ({os.path.getsize(path)} B)")
+
+
+if __name__ == "__main__":
+    main()

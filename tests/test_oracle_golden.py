@@ -1,0 +1,69 @@
+"""Pin the C++ oracle against the reference's own search (fixtures from tests/golden/make_golden.py).
+
+Bit-exact on every node array (visit counts, value sums, priors, virtual-loss counts, parent ids,
+parent actions, the dense children table), the root policy, the final move, and the exact
+sequence of feature tensors handed to the evaluator.
+"""
+import hashlib
+
+import numpy as np
+import pytest
+
+from golden_cases import children_table, digest, load, names
+
+
+def _run_oracle(pyoracle, g, trace=False):
+    o = pyoracle.Oracle(int(g["capacity"]))
+    h = hashlib.sha256()
+
+    def ev(f):
+        f = np.ascontiguousarray(f, np.float32)
+        h.update(hashlib.sha256(f.tobytes()).digest())
+        return pyoracle.synth_eval(f)
+
+    t = o.search(g["board"], int(g["sims"]), int(g["wave"]), evaluator=ev if trace else None,
+                 c_puct=float(g["c_puct"]), virtual_loss=float(g["virtual_loss"]),
+                 enable_vl=bool(g["enable_vl"]))
+    return t, h.hexdigest()
+
+
+@pytest.mark.parametrize("name", names())
+def test_oracle_matches_reference(oracle_lib, name):
+    g = load(name)
+    big = int(g["num_nodes"]) > 200000
+    t, trace = _run_oracle(oracle_lib, g, trace=not big)
+    assert t.result["status"] == 0
+    assert t.result["boundary_ties"] == 0
+    assert t.visits.shape[0] == int(g["num_nodes"])
+    assert digest(t.visits) == str(g["sha_visits"])
+    assert digest(t.value_sums) == str(g["sha_value_sums"])
+    assert digest(t.priors) == str(g["sha_priors"])
+    assert digest(t.virtual_loss) == str(g["sha_virtual_loss"])
+    assert digest(t.parent) == str(g["sha_parent"])
+    assert digest(t.action) == str(g["sha_action"])
+    assert digest(children_table(t.parent, t.action)) == str(g["sha_children"])
+    assert np.array_equal(t.policy, g["policy"])
+    assert int(np.argmax(t.policy)) == int(g["final_move"])
+    assert t.result["eval_calls"] == int(g["eval_calls"])
+    assert t.result["eval_positions"] == int(g["eval_positions"])
+    if not big:
+        assert trace == str(g["eval_trace"])
+
+
+def test_synthetic_evaluator_numpy_equals_c(oracle_lib):
+    rng = np.random.default_rng(3)
+    f = np.zeros((64, 19, 15, 15), np.float32)
+    f[:, 0] = rng.random((64, 15, 15)) < 0.3
+    f[:, 1] = rng.integers(1, 3, (64, 1, 1))
+    f[:, 2].reshape(64, -1)[np.arange(64), rng.integers(0, 225, 64)] = 1
+    p1, v1 = oracle_lib.synth_eval(f)
+    p2, v2 = oracle_lib.c_synth_eval(f)
+    assert np.array_equal(p1, p2) and np.array_equal(v1, v2)
+    # legal priors are distinct multiples of 2^-24 whose sum is exact, values on a 2^-12 grid
+    q = p1 * 2.0 ** 24
+    assert np.array_equal(q, np.round(q))
+    for row, legal in zip(q, f[:, 0].reshape(64, -1) == 0):
+        vals = row[legal]
+        assert len(np.unique(vals)) == len(vals)
+        assert vals.sum() <= 2 ** 24
+    assert np.array_equal(v1 * 4096, np.round(v1 * 4096)) and np.all(np.abs(v1) < 1)
