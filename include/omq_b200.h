@@ -1,0 +1,141 @@
+/*
+ * omq_b200.h - C ABI of the B200-native wave-MCTS hot path (libomq_b200.so).
+ *
+ * Plain pointers, sizes and a caller-supplied cudaStream_t (passed as void*); no C++ or torch
+ * types cross this boundary. Every function returns an omq_status. Device pointers are marked
+ * d_; host pointers h_. Kernels launch on the given stream and never synchronize it unless the
+ * comment says so (functions that report a device-side status read it back and therefore
+ * synchronize that stream).
+ *
+ * Reference interfaces replaced (paths relative to the reference project):
+ *   - pybind module mcts_cuda_kernels (python/mcts/gpu/mcts_kernels.cu:2342-2409) and
+ *     fused_mcts_kernel.cu:252-254: per-op tensor kernels with silent early returns
+ *     (mcts_kernels.cu:1437-1443). Here: explicit status codes, caller streams.
+ *   - CSRTree / NodeDataManager storage (python/mcts/gpu/csr_tree.py:37-86,
+ *     node_data_manager.py:88-113): device-resident trees owned by an omq_engine.
+ *   - WaveSearch.run_wave (python/mcts/core/wave_search.py:555-615): omq_wave_* phases.
+ *   - RequestBatchingCoordinator / GPUEvaluatorService (python/mcts/utils/
+ *     batch_evaluation_coordinator.py:48-500): the engine's on-device leaf queues.
+ *   - ResNetModel.forward (python/mcts/neural_networks/resnet_model.py:247-271) under
+ *     ResNetEvaluator._forward_model (resnet_evaluator.py:231-265): omq_resnet_forward.
+ */
+#ifndef OMQ_B200_H
+#define OMQ_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define OMQ_API __attribute__((visibility("default")))
+#else
+#define OMQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  OMQ_OK = 0,
+  OMQ_TREE_FULL = 1,       /* capacity exhausted (reference: "Tree full", csr_tree.py:405) */
+  OMQ_QUEUE_OVERFLOW = 2,  /* a per-wave scratch list overflowed (visit log, leaf queue) */
+  OMQ_TIMEOUT = 3,         /* a bounded device wait ran out */
+  OMQ_BAD_ARG = 4,
+  OMQ_CUDA_ERROR = 5,
+  OMQ_NOT_READY = 6        /* phase called out of order */
+} omq_status;
+
+/* Which on-device leaf queue an evaluation call refers to. */
+typedef enum {
+  OMQ_QUEUE_EXPAND = 0, /* leaves to expand: policy + value wanted (wave_search.py:866-871) */
+  OMQ_QUEUE_FINAL = 1   /* picked children: value wanted (wave_search.py:1337-1457) */
+} omq_queue;
+
+typedef struct omq_engine omq_engine;
+
+typedef struct {
+  int32_t num_trees;        /* independent trees searched in lockstep (one root each) */
+  int32_t board_size;       /* Gomoku: 15 */
+  int32_t capacity;         /* nodes per tree (reference max_tree_nodes / initial_tree_nodes) */
+  int32_t max_wave_size;    /* simulations per wave (reference MCTSConfig.max_wave_size) */
+  int32_t max_depth;        /* path buffer width (reference wave_search.py:414, 100) */
+  float c_puct;
+  float virtual_loss;       /* positive; applied as -|virtual_loss| (mcts.py:643) */
+  int32_t enable_virtual_loss;
+  int32_t device;           /* CUDA device ordinal */
+} omq_engine_config;
+
+OMQ_API const char* omq_status_string(int status);
+OMQ_API const char* omq_last_error(void); /* thread-local detail for the last non-OK status */
+
+/* Allocates all device memory of the engine (trees + per-wave scratch + queues).
+ * Replaces CSRTree(CSRTreeConfig) (csr_tree.py:86) and WaveSearch.allocate_buffers (:414). */
+OMQ_API int omq_engine_create(const omq_engine_config* cfg, omq_engine** out);
+OMQ_API int omq_engine_destroy(omq_engine* e);
+/* Bytes of device memory held by the engine. */
+OMQ_API int omq_engine_memory(const omq_engine* e, uint64_t* h_bytes);
+
+/* Reset every tree and set its root from d_boards[num_trees][n][n] (int8, 0/1/2); the side to
+ * move is black when the stone count is even (mcts.py:1509-1519). Queues the roots for their
+ * forced expansion (mcts.py:1659-1691): evaluate OMQ_QUEUE_EXPAND, then call
+ * omq_root_expand. */
+OMQ_API int omq_begin(omq_engine* e, const int8_t* d_boards, void* stream);
+OMQ_API int omq_root_expand(omq_engine* e, void* stream);
+
+/* One wave of `wave_size` simulations in every tree (wave_search.py:555-615), in phases:
+ *   omq_wave_select  : selection with virtual loss (wave_search.py:711-777, 1104-1335) and the
+ *                      expansion queue (unique leaves, ascending node id per tree);
+ *   <evaluate OMQ_QUEUE_EXPAND>
+ *   omq_wave_expand  : children in action order, prefix-scan child ids (wave_search.py:779-979,
+ *                      csr_tree.py:391-449), child pick (wave_search.py:981-1102) and the final
+ *                      queue;
+ *   <evaluate OMQ_QUEUE_FINAL>
+ *   omq_wave_backup  : sign-alternating backup in the reference's per-simulation order
+ *                      (mcts_gpu_accelerator.py:378-393) and virtual-loss revert
+ *                      (wave_search.py:1513-1552). */
+OMQ_API int omq_wave_select(omq_engine* e, int32_t wave_size, void* stream);
+OMQ_API int omq_wave_expand(omq_engine* e, void* stream);
+OMQ_API int omq_wave_backup(omq_engine* e, void* stream);
+
+/* Device buffers of a leaf queue: entries int32 [cap][2] = {tree, node}; policy fp32
+ * [cap][actions] (probabilities, as evaluate_batch returns them); value fp32 [cap]; and the
+ * device int32 entry count. An external evaluator fills policy/value for the first count
+ * entries. */
+OMQ_API int omq_queue_buffers(omq_engine* e, int32_t queue, int32_t** d_entries, float** d_policy,
+                      float** d_value, int32_t** d_count, int32_t* h_capacity);
+/* Synchronizes the stream and returns the entry count. */
+OMQ_API int omq_queue_count(omq_engine* e, int32_t queue, int32_t* h_count, void* stream);
+
+/* Reference feature tensor (gpu_game_states.py:534-600, 19 planes) of the queue entries,
+ * fp32 [count][19][n][n] into d_out (capacity rows). */
+OMQ_API int omq_queue_features(omq_engine* e, int32_t queue, float* d_out, void* stream);
+/* Built-in integer-exact synthetic evaluator on the queue (policy for OMQ_QUEUE_EXPAND, value
+ * for both). */
+OMQ_API int omq_queue_eval_synthetic(omq_engine* e, int32_t queue, void* stream);
+
+/* Whole search with the built-in synthetic evaluator: begin, forced root expansion and
+ * ceil(num_simulations / max_wave_size) waves (mcts.py:1020-1063). Synchronizes the stream
+ * once at the end to report device status. */
+OMQ_API int omq_search_synthetic(omq_engine* e, const int8_t* d_boards, int32_t num_simulations,
+                         void* stream);
+
+/* Root statistics: visit counts of the root's children scattered by action,
+ * d_visits int32 [num_trees][actions] (0 for illegal actions), and the root's own N and W
+ * (d_root_nw float [num_trees][2]). Replaces tree_ops.get_root_children_info
+ * (tree_operations.py:154-187). */
+OMQ_API int omq_root_visits(omq_engine* e, int32_t* d_visits, float* d_root_nw, void* stream);
+
+/* Device status word and node count of each tree: d_status int32 [num_trees],
+ * d_num_nodes int32 [num_trees]. */
+OMQ_API int omq_tree_status(omq_engine* e, int32_t* d_status, int32_t* d_num_nodes, void* stream);
+
+/* Node arrays of tree `tree` in creation order, `count` nodes from index 0 (the layout the
+ * reference's NodeDataManager holds: visit_counts, value_sums, node_priors,
+ * virtual_loss_counts, parent_indices, parent_actions). Any pointer may be NULL. */
+OMQ_API int omq_export_tree(omq_engine* e, int32_t tree, int32_t count, int32_t* d_visits,
+                    float* d_value_sums, float* d_priors, int32_t* d_virtual_loss,
+                    int32_t* d_parent, int32_t* d_action, uint8_t* d_terminal, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OMQ_B200_H */

@@ -1,0 +1,193 @@
+// Leaf-queue evaluation kernels: the reference feature tensor and the built-in synthetic
+// evaluator.
+//
+// Positions are never stored per node. A queued node's board is rebuilt from its tree's root
+// board plus the actions on its parent chain (at most max_depth dependent loads), which is all
+// the reference's features carry: occupancy, the side to move, and the last move (child states
+// do not inherit full_move_history, python/mcts/gpu/gpu_game_states.py:325-327, 443-446).
+#include "omq_internal.cuh"
+
+namespace omq {
+
+constexpr int kEvalDepthCap = 128;
+
+// Planes of the reference's 8-move history block (gpu_game_states.py:560-600) that hold this
+// state's single recorded move, as a bitmask over the 19 planes. A state made by apply_moves
+// records only its own move at index move_count-1; the clamp of :568 makes that entry reappear
+// for k >= 1 when move_count == 1.
+__device__ __forceinline__ uint32_t history_planes(int mc, int depth, int full_history) {
+  uint32_t m = 0;
+  if (depth < 1) return 0;
+  for (int k = 0; k < 8; ++k) {
+    int idx = mc - 1 - k;
+    idx = idx < 0 ? 0 : idx;
+    idx = idx > full_history - 1 ? full_history - 1 : idx;
+    if (idx < mc && idx == mc - 1) m |= 1u << ((k % 2 == 0) ? 2 + k / 2 : 10 + k / 2);
+  }
+  return m;
+}
+
+struct WarpPos {
+  int16_t acts[kEvalDepthCap];
+  int8_t board[kMaxCells + 3];
+  uint64_t words[kMaxWords];
+};
+
+// Rebuild the board of `node` of tree r into wp.board. Returns depth (or -1 on a bad chain).
+__device__ int warp_rebuild(const EngineView& v, int r, int node, WarpPos& wp) {
+  const int lane = threadIdx.x & 31;
+  int d = 0;
+  if (lane == 0) d = path_actions(v.topo + (size_t)r * v.T, node, kEvalDepthCap - 1, wp.acts);
+  d = __shfl_sync(0xFFFFFFFFu, d, 0);
+  if (d < 0) return -1;
+  const TreeHeader& H = v.hdr[r];
+  for (int c = lane; c < v.C; c += 32) wp.board[c] = v.root_board[(size_t)r * v.C + c];
+  __syncwarp();
+  for (int j = lane; j < d; j += 32)
+    wp.board[wp.acts[j]] = (int8_t)((j % 2 == 0) ? H.root_player : 3 - H.root_player);
+  __syncwarp();
+  return d;
+}
+
+__device__ __forceinline__ int64_t exp_step(uint64_t r) {
+  const int64_t s = (int64_t)(r & 0xFFFF) + (int64_t)((r >> 16) & 0xFFFF) +
+                    (int64_t)((r >> 32) & 0xFFFF) + (int64_t)((r >> 48) & 0xFFFF) - 131072;
+  return (s * 160) >> 16;
+}
+
+__constant__ uint32_t c_exp2[64] = {
+    1048576u,1059994u,1071537u,1083205u,1095000u,1106924u,1118978u,1131163u,1143480u,1155932u,
+    1168519u,1181244u,1194106u,1207109u,1220254u,1233542u,1246974u,1260553u,1274279u,1288155u,
+    1302182u,1316362u,1330696u,1345187u,1359835u,1374642u,1389611u,1404743u,1420040u,1435503u,
+    1451135u,1466937u,1482910u,1499058u,1515382u,1531883u,1548564u,1565427u,1582474u,1599706u,
+    1617125u,1634735u,1652536u,1670531u,1688722u,1707110u,1725700u,1744491u,1763488u,1782691u,
+    1802103u,1821727u,1841564u,1861617u,1881889u,1902381u,1923097u,1944038u,1965207u,1986607u,
+    2008240u,2030108u,2052214u,2074562u};
+
+__device__ __forceinline__ uint64_t exp2_fixed(int64_t t) {
+  return (uint64_t)c_exp2[t & 63] << ((t >> 6) + 6);
+}
+
+// Built-in synthetic evaluator (integer-exact definition: policy on a 2^-24 grid with distinct
+// legal priors, value tanh(z/2) on a 2^-12 grid), keyed by a 64-bit hash of the reference feature
+// planes of the position. One warp per queued position.
+constexpr int kSynthWarps = 4;
+constexpr int kMaxActionsPerLane = 12;  // ceil(362 / 32)
+
+__global__ void __launch_bounds__(kSynthWarps * 32) k_synth(EngineView v, int queue) {
+  __shared__ WarpPos wps[kSynthWarps];
+  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
+  const int q = blockIdx.x * kSynthWarps + wl;
+  const int count = v.q_count[queue];
+  if (q >= count) return;
+  WarpPos& wp = wps[wl];
+  const int2 ent = v.q_entries[queue][q];
+  const int r = ent.x, node = ent.y;
+  const int d = warp_rebuild(v, r, node, wp);
+  if (d < 0) { if (lane == 0) v.hdr[r].status = OMQ_BAD_ARG; return; }
+  const TreeHeader& H = v.hdr[r];
+  const int player = (d % 2 == 0) ? H.root_player : 3 - H.root_player;
+  const int mc = H.root_mc + d;
+  const int nwords = (v.C + 63) / 64;
+  if (lane < nwords) {
+    uint64_t w = 0;
+    for (int b = 0; b < 64; ++b) {
+      const int c = lane * 64 + b;
+      if (c < v.C && wp.board[c] != 0) w |= 1ull << b;
+    }
+    wp.words[lane] = w;
+  }
+  __syncwarp();
+  uint64_t h = 0;
+  if (lane == 0) {
+    h = 0x243F6A8885A308D3ull;
+    for (int j = 0; j < nwords; ++j) h = mix64(h ^ wp.words[j]);
+    h = mix64(h ^ (uint64_t)player);
+    const uint32_t hp = history_planes(mc, d, kFullHistoryGomoku);
+    const int last = d >= 1 ? wp.acts[d - 1] : -1;
+    for (int c = 2; c < kPlanes; ++c)
+      for (int j = 0; j < nwords; ++j) {
+        uint64_t word = 0;
+        if ((hp >> c) & 1u) {
+          if (last >= 64 * j && last < 64 * j + 64) word = 1ull << (last - 64 * j);
+        }
+        h = mix64(h ^ word);
+      }
+  }
+  h = __shfl_sync(0xFFFFFFFFu, h, 0);
+  if (queue == 0) {
+    uint64_t wv[kMaxActionsPerLane];
+    uint64_t tot = 0;
+#pragma unroll
+    for (int t = 0; t < kMaxActionsPerLane; ++t) {
+      const int a = t * 32 + lane;
+      wv[t] = 0;
+      if (a < v.A && (a >= v.C || wp.board[a] == 0)) {
+        wv[t] = exp2_fixed(exp_step(mix64(h + 0x9E3779B97F4A7C15ull * (uint64_t)(a + 1))));
+        tot += wv[t];
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xFFFFFFFFu, tot, o);
+    int idx_base = 0;
+    float* out = v.q_policy[0] + (size_t)q * v.A;
+#pragma unroll
+    for (int t = 0; t < kMaxActionsPerLane; ++t) {
+      const int a = t * 32 + lane;
+      const bool legal = a < v.A && (a >= v.C || wp.board[a] == 0);
+      const unsigned m = __ballot_sync(0xFFFFFFFFu, legal);
+      if (a < v.A) {
+        float p = 0.0f;
+        if (legal) {
+          const uint64_t idx = (uint64_t)(idx_base + __popc(m & ((1u << lane) - 1)));
+          const uint64_t qa = 512ull * ((wv[t] * 32640ull) / tot) + idx;
+          p = __fmul_rn(__ull2float_rn(qa), 1.0f / 16777216.0f);
+        }
+        out[a] = p;
+      }
+      idx_base += __popc(m);
+    }
+  }
+  if (lane == 0) {
+    const int64_t e = (int64_t)exp2_fixed(exp_step(mix64(h ^ 0xD1B54A32D192ED03ull)));
+    const int64_t dd = (int64_t)1 << 26;
+    const int64_t val = ((e - dd) * 4096) / (e + dd);
+    v.q_value[queue][q] = __fmul_rn(__ll2float_rn(val), 1.0f / 4096.0f);
+  }
+}
+
+// Reference feature tensor, fp32 [count][19][C]. One warp per queued position.
+__global__ void __launch_bounds__(kSynthWarps * 32) k_features(EngineView v, int queue, float* out) {
+  __shared__ WarpPos wps[kSynthWarps];
+  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
+  const int q = blockIdx.x * kSynthWarps + wl;
+  const int count = v.q_count[queue];
+  if (q >= count) return;
+  WarpPos& wp = wps[wl];
+  const int2 ent = v.q_entries[queue][q];
+  const int r = ent.x;
+  const int d = warp_rebuild(v, r, ent.y, wp);
+  if (d < 0) { if (lane == 0) v.hdr[r].status = OMQ_BAD_ARG; return; }
+  const TreeHeader& H = v.hdr[r];
+  const float player = (float)((d % 2 == 0) ? H.root_player : 3 - H.root_player);
+  const uint32_t hp = history_planes(H.root_mc + d, d, kFullHistoryGomoku);
+  const int last = d >= 1 ? wp.acts[d - 1] : -1;
+  float* o = out + (size_t)q * kPlanes * v.C;
+  for (int c = lane; c < v.C; c += 32) {
+    o[c] = wp.board[c] != 0 ? 1.0f : 0.0f;
+    o[v.C + c] = player;
+    for (int p = 2; p < kPlanes; ++p)
+      o[(size_t)p * v.C + c] = (((hp >> p) & 1u) && c == last) ? 1.0f : 0.0f;
+  }
+}
+
+void launch_synth_eval(const EngineView& v, int queue, cudaStream_t s) {
+  const int cap = v.R * v.WCAP;
+  k_synth<<<(cap + kSynthWarps - 1) / kSynthWarps, kSynthWarps * 32, 0, s>>>(v, queue);
+}
+
+void launch_features(const EngineView& v, int queue, float* out, cudaStream_t s) {
+  const int cap = v.R * v.WCAP;
+  k_features<<<(cap + kSynthWarps - 1) / kSynthWarps, kSynthWarps * 32, 0, s>>>(v, queue, out);
+}
+
+}  // namespace omq

@@ -1,0 +1,611 @@
+// Tree kernels of the wave search: root reset, selection, expansion + child pick, backup.
+//
+// One CTA per tree; all trees of an engine advance in lockstep, their leaves meeting in the
+// engine's on-device leaf queues (the role of the reference's BatchEvaluationCoordinator,
+// python/mcts/utils/batch_evaluation_coordinator.py:48-500).
+//
+// Selection is not simulated one path at a time. The reference's rank distribution
+// (python/mcts/core/wave_search.py:1300-1319) hands the simulations at a parent - always a
+// contiguous index range [lo, lo+k) - to its UCB-sorted children in rank order, so a wave is a
+// frontier of (node, lo, k, depth) records per depth level. Every visited node appears in
+// exactly one record per wave, which makes backup free of atomics and lets it add the values
+// of [lo, lo+k) in ascending simulation order - the reference's sequential order
+// (python/mcts/gpu/mcts_gpu_accelerator.py:378-393) - so W is bit-exact for any evaluator.
+#include "omq_internal.cuh"
+
+namespace omq {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+// ---------------------------------------------------------------------------------------------
+// Gomoku rules on a shared-memory board
+// ---------------------------------------------------------------------------------------------
+// True when placing `p` at cell `a` of board `b` (which does not yet hold that stone) makes five
+// or more in a row through `a`. For a non-terminal parent this equals the reference's
+// full-board scan (python/mcts/utils/fast_terminal_check.py:233-332): any new five must
+// contain the new stone.
+__device__ bool five_through(const int8_t* b, int S, int a, int p) {
+  const int r0 = a / S, c0 = a % S;
+  const int dr[4] = {0, 1, 1, 1}, dc[4] = {1, 0, 1, -1};
+  for (int d = 0; d < 4; ++d) {
+    int run = 1;
+    for (int s = 1; s < 5; ++s) {
+      int r = r0 + dr[d] * s, c = c0 + dc[d] * s;
+      if (r < 0 || r >= S || c < 0 || c >= S || b[r * S + c] != p) break;
+      ++run;
+    }
+    for (int s = 1; s < 5; ++s) {
+      int r = r0 - dr[d] * s, c = c0 - dc[d] * s;
+      if (r < 0 || r >= S || c < 0 || c >= S || b[r * S + c] != p) break;
+      ++run;
+    }
+    if (run >= 5) return true;
+  }
+  return false;
+}
+
+// Five in a row starting at cell i in any of the 4 forward directions.
+__device__ bool five_from(const int8_t* b, int S, int i) {
+  const int p = b[i];
+  if (p == 0) return false;
+  const int r0 = i / S, c0 = i % S;
+  const int dr[4] = {0, 1, 1, 1}, dc[4] = {1, 0, 1, -1};
+  for (int d = 0; d < 4; ++d) {
+    int s = 1;
+    for (; s < 5; ++s) {
+      int r = r0 + dr[d] * s, c = c0 + dc[d] * s;
+      if (r < 0 || r >= S || c < 0 || c >= S || b[r * S + c] != p) break;
+    }
+    if (s == 5) return true;
+  }
+  return false;
+}
+
+// ---------------------------------------------------------------------------------------------
+// block helpers
+// ---------------------------------------------------------------------------------------------
+// Exclusive scan of vals[0..n) in place (n <= kThreads * 4), returns the total.
+__device__ int block_exclusive_scan(int* vals, int n, int* warp_tot) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = 4;
+  int loc[per];
+  int sum = 0;
+  for (int j = 0; j < per; ++j) {
+    int i = tid * per + j;
+    loc[j] = i < n ? vals[i] : 0;
+    sum += loc[j];
+  }
+  int inc = sum;
+  for (int o = 1; o < 32; o <<= 1) {
+    int t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    if (lane >= o) inc += t;
+  }
+  if (lane == 31) warp_tot[warp] = inc;
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int w = 0; w < kWarps; ++w) { int t = warp_tot[w]; warp_tot[w] = acc; acc += t; }
+    warp_tot[kWarps] = acc;
+  }
+  __syncthreads();
+  int run = warp_tot[warp] + inc - sum;
+  for (int j = 0; j < per; ++j) {
+    int i = tid * per + j;
+    if (i < n) vals[i] = run;
+    run += loc[j];
+  }
+  __syncthreads();
+  return warp_tot[kWarps];
+}
+
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long x) {
+  for (int o = 16; o > 0; o >>= 1) {
+    unsigned long long y = __shfl_xor_sync(0xFFFFFFFFu, x, o);
+    x = y > x ? y : x;
+  }
+  return x;
+}
+
+// Descending bitonic sort of keys[0..p2) by one warp (p2 a power of two).
+__device__ void warp_sort_desc(unsigned long long* keys, int p2) {
+  const int lane = threadIdx.x & 31;
+  for (int size = 2; size <= p2; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = lane; i < (p2 >> 1); i += 32) {
+        const int j = 2 * i - (i & (stride - 1));
+        const int l = j + stride;
+        const bool desc = (j & size) == 0;
+        unsigned long long a = keys[j], b = keys[l];
+        if ((a < b) == desc) { keys[j] = b; keys[l] = a; }
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// begin: reset trees, install roots, queue the roots for the forced root expansion
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) k_begin(EngineView v, const int8_t* boards) {
+  const int r = blockIdx.x, tid = threadIdx.x;
+  __shared__ int8_t sb[kMaxCells];
+  __shared__ int s_stones, s_five;
+  if (tid == 0) { s_stones = 0; s_five = 0; }
+  __syncthreads();
+  int cnt = 0;
+  for (int i = tid; i < v.C; i += kThreads) {
+    int8_t x = boards[(size_t)r * v.C + i];
+    sb[i] = x;
+    v.root_board[(size_t)r * v.C + i] = x;
+    cnt += x != 0;
+  }
+  atomicAdd(&s_stones, cnt);
+  __syncthreads();
+  int five = 0;
+  for (int i = tid; i < v.C; i += kThreads) five |= five_from(sb, v.S, i) ? 1 : 0;
+  if (five) atomicOr(&s_five, 1);
+  __syncthreads();
+  if (tid == 0) {
+    TreeHeader h{};
+    h.num_nodes = 1;
+    h.status = OMQ_OK;
+    h.root_player = (s_stones % 2 == 0) ? 1 : 2;
+    h.root_mc = s_stones;
+    h.root_five = s_five;
+    h.nleaves = 1;
+    h.exp_off = r;
+    h.exp_cnt = 1;
+    v.hdr[r] = h;
+    const size_t base = (size_t)r * v.T;
+    v.stats[base] = NodeStats{0, 0.0f, 1.0f, 0};
+    v.topo[base] = NodeTopo{-1, pack_act_depth(-1, 0), 0, pack_cnt_flags(0, 0)};
+    v.leaves[(size_t)r * v.WCAP] = Visit{0, 0, 0, 0};
+    v.leaf_final[(size_t)r * v.WCAP] = make_int2(0, r);
+    v.q_entries[0][r] = make_int2(r, 0);
+    if (r == 0) { v.q_count[0] = v.R; v.q_count[1] = 0; }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// selection
+// ---------------------------------------------------------------------------------------------
+struct SelectShared {
+  int cnt[2];
+  int nleaf;
+  int nlog;
+  int overflow;
+  int warp_tot[kWarps + 1];
+};
+
+__device__ __forceinline__ void emit_child(const EngineView& v, int r, Visit* next, int* next_cnt,
+                                           Visit* log, int* nlog, int* overflow, int child, int lo,
+                                           int k, int depth) {
+  const size_t base = (size_t)r * v.T;
+  if (v.enable_vl) v.stats[base + child].VL += k;  // only this warp touches this child this wave
+  const int fi = atomicAdd(next_cnt, 1);
+  const Visit x{child, lo, k, depth};
+  next[fi] = x;
+  const int li = atomicAdd(nlog, 1);
+  if (li < v.LOGCAP) log[li] = x; else *overflow = 1;
+}
+
+__global__ void __launch_bounds__(kThreads) k_select(EngineView v, int wave) {
+  extern __shared__ unsigned char smem_raw[];
+  SelectShared& sh = *reinterpret_cast<SelectShared*>(smem_raw);
+  int p2 = 1;
+  while (p2 < v.A) p2 <<= 1;
+  unsigned long long* keys_all =
+      reinterpret_cast<unsigned long long*>(smem_raw + ((sizeof(SelectShared) + 15) & ~15));
+  Visit* s_leaves = reinterpret_cast<Visit*>(keys_all + (size_t)kWarps * p2);
+  int* s_scan = reinterpret_cast<int*>(s_leaves + v.WCAP);
+
+  const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  TreeHeader* H = &v.hdr[r];
+  if (H->status != OMQ_OK) return;
+  const size_t base = (size_t)r * v.T;
+  Visit* F[2] = {v.frontier + (size_t)r * 2 * v.WCAP, v.frontier + (size_t)r * 2 * v.WCAP + v.WCAP};
+  Visit* log = v.vlog + (size_t)r * v.LOGCAP;
+  unsigned long long* keys = keys_all + (size_t)warp * p2;
+
+  if (tid == 0) {
+    const Visit root{0, 0, wave, 0};
+    F[0][0] = root;
+    log[0] = root;
+    sh.cnt[0] = 1; sh.cnt[1] = 0;
+    sh.nleaf = 0; sh.nlog = 1; sh.overflow = 0;
+  }
+  __syncthreads();
+  int cur = 0;
+  for (int depth = 1; depth < v.max_depth; ++depth) {
+    const int n_cur = sh.cnt[cur];
+    if (n_cur == 0) break;
+    for (int i = warp; i < n_cur; i += kWarps) {
+      const Visit e = F[cur][i];
+      const NodeTopo tp = v.topo[base + e.node];
+      const int n = topo_count(tp);
+      if (n == 0) {  // no children: the simulation stops here (wave_search.py:762-768)
+        if (lane == 0) {
+          int li = atomicAdd(&sh.nleaf, 1);
+          if (li < v.WCAP) s_leaves[li] = e; else sh.overflow = 1;
+        }
+        continue;
+      }
+      const int cs = tp.child_start;
+      const int32_t np = v.stats[base + e.node].N;
+      for (int j = lane; j < n; j += 32) {
+        const NodeStats st = v.stats[base + cs + j];
+        keys[j] = rank_key(ucb_score(st, np, v.c_puct, v.vl_value, v.enable_vl), j);
+      }
+      __syncwarp();
+      if (e.k <= n && e.k <= 8) {
+        // k best children, one simulation each, by repeated arg-max
+        for (int rr = 0; rr < e.k; ++rr) {
+          unsigned long long best = 0;
+          for (int j = lane; j < n; j += 32) best = keys[j] > best ? keys[j] : best;
+          best = warp_max_u64(best);
+          const int slot = key_slot(best);
+          if (lane == 0) {
+            keys[slot] = 0;
+            emit_child(v, r, F[cur ^ 1], &sh.cnt[cur ^ 1], log, &sh.nlog, &sh.overflow,
+                       cs + slot, e.lo + rr, 1, e.depth + 1);
+          }
+          __syncwarp();
+        }
+      } else {
+        for (int j = n + lane; j < p2; j += 32) keys[j] = 0;
+        __syncwarp();
+        warp_sort_desc(keys, p2);
+        if (e.k <= n) {
+          for (int rr = lane; rr < e.k; rr += 32)
+            emit_child(v, r, F[cur ^ 1], &sh.cnt[cur ^ 1], log, &sh.nlog, &sh.overflow,
+                       cs + key_slot(keys[rr]), e.lo + rr, 1, e.depth + 1);
+        } else {
+          const int basek = e.k / n, extra = e.k % n;
+          for (int rr = lane; rr < n; rr += 32) {
+            const int c = basek + (rr < extra ? 1 : 0);
+            const int off = rr * basek + (rr < extra ? rr : extra);
+            emit_child(v, r, F[cur ^ 1], &sh.cnt[cur ^ 1], log, &sh.nlog, &sh.overflow,
+                       cs + key_slot(keys[rr]), e.lo + off, c, e.depth + 1);
+          }
+        }
+      }
+      __syncwarp();
+    }
+    __syncthreads();
+    if (tid == 0) sh.cnt[cur] = 0;
+    cur ^= 1;
+    __syncthreads();
+  }
+  // depth limit reached: the remaining simulations stop at nodes that still have children
+  for (int i = tid; i < sh.cnt[cur]; i += kThreads) {
+    int li = atomicAdd(&sh.nleaf, 1);
+    if (li < v.WCAP) s_leaves[li] = F[cur][i]; else sh.overflow = 1;
+  }
+  __syncthreads();
+  const int nleaf = min(sh.nleaf, v.WCAP);
+  // sort leaves ascending by node id (each node is a leaf at most once per wave)
+  Visit* gleaves = v.leaves + (size_t)r * v.WCAP;
+  for (int i = tid; i < nleaf; i += kThreads) {
+    const int key = s_leaves[i].node;
+    int rank = 0;
+    for (int j = 0; j < nleaf; ++j) rank += s_leaves[j].node < key;
+    gleaves[rank] = s_leaves[i];
+  }
+  __syncthreads();
+  // expandable leaves: no children, not terminal (wave_search.py:829-855)
+  for (int i = tid; i < nleaf; i += kThreads) {
+    const NodeTopo tp = v.topo[base + gleaves[i].node];
+    s_scan[i] = (topo_count(tp) == 0 && !(topo_flags(tp) & kFlagTerminal)) ? 1 : 0;
+  }
+  __syncthreads();
+  // keep the flags (scan overwrites them): stash in leaf_final.y as 0/1 first
+  int2* lf = v.leaf_final + (size_t)r * v.WCAP;
+  for (int i = tid; i < nleaf; i += kThreads) lf[i] = make_int2(-1, s_scan[i]);
+  __syncthreads();
+  const int nexp = block_exclusive_scan(s_scan, nleaf, sh.warp_tot);
+  __shared__ int s_qbase;
+  if (tid == 0) s_qbase = nexp > 0 ? atomicAdd(&v.q_count[0], nexp) : 0;
+  __syncthreads();
+  const int qbase = s_qbase;
+  for (int i = tid; i < nleaf; i += kThreads) {
+    if (lf[i].y) {
+      const int q = qbase + s_scan[i];
+      v.q_entries[0][q] = make_int2(r, gleaves[i].node);
+      lf[i] = make_int2(-1, q);
+    } else {
+      lf[i] = make_int2(-1, -1);
+    }
+  }
+  if (tid == 0) {
+    H->nleaves = nleaf;
+    H->nlog = min(sh.nlog, v.LOGCAP);
+    H->exp_off = qbase;
+    H->exp_cnt = nexp;
+    H->wave = wave;
+    if (sh.overflow) H->status = OMQ_QUEUE_OVERFLOW;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// expansion + child pick
+// ---------------------------------------------------------------------------------------------
+constexpr int kMaxDepthCap = 128;
+
+struct ExpandWarpSmem {
+  int16_t acts[kMaxDepthCap];
+  int16_t legal[kMaxCells + 1];
+  float pv[kMaxCells + 1];
+  int8_t board[kMaxCells + 3];
+};
+
+// Sum of the legal-move policy in the engine's fixed order: lane L adds slots L, L+32, ...
+// sequentially, then a butterfly over the 32 partial sums. Exact for the synthetic evaluator
+// (all partial sums are exact fp32 integers times 2^-24); for a general evaluator the oracle
+// reproduces this order.
+__device__ float warp_fixed_order_sum(const float* pv, int n) {
+  const int lane = threadIdx.x & 31;
+  float s = 0.0f;
+  for (int j = lane; j < n; j += 32) s = __fadd_rn(s, pv[j]);
+  for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, o));
+  return s;
+}
+
+__global__ void __launch_bounds__(kThreads) k_expand(EngineView v, int root_mode) {
+  __shared__ ExpandWarpSmem ws[kWarps];
+  __shared__ int s_cnt[1024];
+  __shared__ int warp_tot[kWarps + 1];
+  __shared__ int s_fbase;
+  const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  TreeHeader* H = &v.hdr[r];
+  if (H->status != OMQ_OK) return;
+  const size_t base = (size_t)r * v.T;
+  const int nleaf = H->nleaves;
+  const int num_nodes = H->num_nodes;
+  Visit* leaves = v.leaves + (size_t)r * v.WCAP;
+  int2* lf = v.leaf_final + (size_t)r * v.WCAP;
+  const float* pol = v.q_policy[0];
+
+  // children per expandable leaf: the empty cells of its board, i.e. C - move_count
+  for (int i = tid; i < nleaf; i += kThreads)
+    s_cnt[i] = lf[i].y >= 0 ? max(v.C - (H->root_mc + leaves[i].depth), 0) : 0;
+  __syncthreads();
+  const int total = block_exclusive_scan(s_cnt, nleaf, warp_tot);
+  if (num_nodes + total > v.T) {  // "Tree full" (csr_tree.py:405-406)
+    if (tid == 0) H->status = OMQ_TREE_FULL;
+    return;
+  }
+  ExpandWarpSmem& W = ws[warp];
+  for (int i = warp; i < nleaf; i += kWarps) {
+    const Visit e = leaves[i];
+    const int q = lf[i].y;
+    int final_node = e.node, ext = 0;
+    if (q >= 0) {
+      // reconstruct the leaf's board: root board + the stones along its path
+      int d = 0;
+      if (lane == 0) d = path_actions(v.topo + base, e.node, kMaxDepthCap - 1, W.acts);
+      d = __shfl_sync(0xFFFFFFFFu, d, 0);
+      if (d < 0) { if (lane == 0) H->status = OMQ_BAD_ARG; continue; }
+      for (int c = lane; c < v.C; c += 32) W.board[c] = v.root_board[(size_t)r * v.C + c];
+      __syncwarp();
+      for (int j = lane; j < d; j += 32)
+        W.board[W.acts[j]] = (int8_t)((j % 2 == 0) ? H->root_player : 3 - H->root_player);
+      __syncwarp();
+      const int player = (d % 2 == 0) ? H->root_player : 3 - H->root_player;
+      const int mc = H->root_mc + d;
+      // legal actions in ascending order and their policy values
+      int n = 0;
+      for (int c0 = 0; c0 < v.C; c0 += 32) {
+        const int c = c0 + lane;
+        const bool legal = c < v.C && W.board[c] == 0;
+        const unsigned m = __ballot_sync(0xFFFFFFFFu, legal);
+        if (legal) {
+          const int j = n + __popc(m & ((1u << lane) - 1));
+          W.legal[j] = (int16_t)c;
+          W.pv[j] = pol[(size_t)q * v.A + c];
+        }
+        n += __popc(m);
+      }
+      __syncwarp();
+      const float denom = __fadd_rn(warp_fixed_order_sum(W.pv, n), 1e-8f);
+      const int start = num_nodes + s_cnt[i];
+      unsigned long long best = 0;
+      const int32_t nleafN = v.stats[base + e.node].N;
+      for (int j = lane; j < n; j += 32) {
+        const int a = W.legal[j];
+        const float P = __fdiv_rn(W.pv[j], denom);
+        const bool term = H->root_five || five_through(W.board, v.S, a, player) || (mc + 1 >= v.C);
+        const int c = start + j;
+        const NodeStats st{0, 0.0f, P, 0};
+        v.stats[base + c] = st;
+        v.topo[base + c] = NodeTopo{e.node, pack_act_depth(a, d + 1), 0,
+                                    pack_cnt_flags(0, term ? kFlagTerminal : 0)};
+        const unsigned long long key =
+            rank_key(ucb_score(st, nleafN, v.c_puct, v.vl_value, v.enable_vl), j);
+        best = key > best ? key : best;
+      }
+      best = warp_max_u64(best);
+      if (lane == 0) {
+        NodeTopo lt = v.topo[base + e.node];
+        lt.child_start = start;
+        lt.cnt_flags = pack_cnt_flags(n, topo_flags(lt));
+        v.topo[base + e.node] = lt;
+      }
+      if (!root_mode && n > 0) {
+        // child pick on the fresh children (wave_search.py:1053-1077): first maximum
+        final_node = start + key_slot(best);
+        ext = (e.depth + 1 < v.max_depth) ? 1 : 0;
+        if (lane == 0 && v.enable_vl) v.stats[base + final_node].VL += 1;
+      }
+    } else if (!root_mode) {
+      const NodeTopo tp = v.topo[base + e.node];
+      const int n = topo_count(tp);
+      if (n > 0) {  // depth-limited leaf that already has children
+        const int32_t np = v.stats[base + e.node].N;
+        unsigned long long best = 0;
+        for (int j = lane; j < n; j += 32) {
+          const NodeStats st = v.stats[base + tp.child_start + j];
+          const unsigned long long key =
+              rank_key(ucb_score(st, np, v.c_puct, v.vl_value, v.enable_vl), j);
+          best = key > best ? key : best;
+        }
+        best = warp_max_u64(best);
+        final_node = tp.child_start + key_slot(best);
+        ext = (e.depth + 1 < v.max_depth) ? 1 : 0;
+        if (lane == 0 && v.enable_vl) v.stats[base + final_node].VL += 1;
+      }
+    }
+    if (lane == 0) lf[i] = make_int2(final_node, ext << 30);
+    __syncwarp();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    H->num_nodes = num_nodes + total;
+    if (!root_mode) {
+      s_fbase = atomicAdd(&v.q_count[1], nleaf);
+      H->fin_off = s_fbase;
+      H->fin_cnt = nleaf;
+    }
+  }
+  __syncthreads();
+  if (!root_mode) {
+    for (int i = tid; i < nleaf; i += kThreads) {
+      const int2 x = lf[i];
+      v.q_entries[1][s_fbase + i] = make_int2(r, x.x);
+      lf[i] = make_int2(x.x, (s_fbase + i) | (x.y & (1 << 30)));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// backup + virtual-loss revert
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void backup_node(const EngineView& v, size_t base, const float* sv,
+                                            const Visit& x) {
+  NodeStats st = v.stats[base + x.node];
+  st.N += x.k;
+  float w = st.W;
+  const bool even = (x.depth % 2) == 0;
+  for (int s = x.lo; s < x.lo + x.k; ++s) {
+    const float val = sv[s];
+    w = __fadd_rn(w, even ? val : -val);
+  }
+  st.W = w;
+  if (x.depth >= 1 && v.enable_vl) st.VL = max(st.VL - x.k, 0);
+  v.stats[base + x.node] = st;
+}
+
+__global__ void __launch_bounds__(kThreads) k_backup(EngineView v) {
+  const int r = blockIdx.x, tid = threadIdx.x;
+  TreeHeader* H = &v.hdr[r];
+  if (H->status != OMQ_OK) return;
+  const size_t base = (size_t)r * v.T;
+  const int nleaf = H->nleaves, nlog = H->nlog;
+  const Visit* leaves = v.leaves + (size_t)r * v.WCAP;
+  const int2* lf = v.leaf_final + (size_t)r * v.WCAP;
+  float* sv = v.simval + (size_t)r * v.WCAP;
+  for (int i = tid; i < nleaf; i += kThreads) {
+    const Visit e = leaves[i];
+    const float val = v.q_value[1][lf[i].y & ((1 << 30) - 1)];
+    for (int s = e.lo; s < e.lo + e.k; ++s) sv[s] = val;
+  }
+  __syncthreads();
+  const Visit* log = v.vlog + (size_t)r * v.LOGCAP;
+  for (int i = tid; i < nlog; i += kThreads) backup_node(v, base, sv, log[i]);
+  for (int i = tid; i < nleaf; i += kThreads) {
+    if (lf[i].y & (1 << 30)) {
+      const Visit e = leaves[i];
+      backup_node(v, base, sv, Visit{lf[i].x, e.lo, e.k, e.depth + 1});
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// readouts
+// ---------------------------------------------------------------------------------------------
+__global__ void k_root_visits(EngineView v, int32_t* visits, float* nw) {
+  const int r = blockIdx.x, tid = threadIdx.x;
+  const size_t base = (size_t)r * v.T;
+  for (int a = tid; a < v.A; a += blockDim.x) visits[(size_t)r * v.A + a] = 0;
+  __syncthreads();
+  const NodeTopo t = v.topo[base];
+  const int n = topo_count(t);
+  for (int j = tid; j < n; j += blockDim.x) {
+    const int c = t.child_start + j;
+    visits[(size_t)r * v.A + topo_action(v.topo[base + c])] = v.stats[base + c].N;
+  }
+  if (tid == 0 && nw) {
+    nw[2 * r] = (float)v.stats[base].N;
+    nw[2 * r + 1] = v.stats[base].W;
+  }
+}
+
+__global__ void k_export(EngineView v, int tree, int count, int32_t* N, float* W, float* P,
+                         int32_t* VL, int32_t* parent, int32_t* action, uint8_t* terminal) {
+  const size_t base = (size_t)tree * v.T;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) {
+    const NodeStats s = v.stats[base + i];
+    const NodeTopo t = v.topo[base + i];
+    if (N) N[i] = s.N;
+    if (W) W[i] = s.W;
+    if (P) P[i] = s.P;
+    if (VL) VL[i] = s.VL;
+    if (parent) parent[i] = t.parent;
+    if (action) action[i] = topo_action(t);
+    if (terminal) terminal[i] = (topo_flags(t) & kFlagTerminal) ? 1 : 0;
+  }
+}
+
+__global__ void k_status(EngineView v, int32_t* status, int32_t* num_nodes) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < v.R) {
+    if (status) status[r] = v.hdr[r].status;
+    if (num_nodes) num_nodes[r] = v.hdr[r].num_nodes;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// launchers
+// ---------------------------------------------------------------------------------------------
+static size_t select_smem(const EngineView& v) {
+  int p2 = 1;
+  while (p2 < v.A) p2 <<= 1;
+  return ((sizeof(SelectShared) + 15) & ~(size_t)15) + (size_t)kWarps * p2 * 8 +
+         (size_t)v.WCAP * sizeof(Visit) + (size_t)v.WCAP * sizeof(int);
+}
+
+void launch_begin(const EngineView& v, const int8_t* boards, cudaStream_t s) {
+  k_begin<<<v.R, kThreads, 0, s>>>(v, boards);
+}
+
+void launch_select(const EngineView& v, int wave, cudaStream_t s) {
+  const size_t sm = select_smem(v);
+  if (sm > 48 * 1024)
+    cudaFuncSetAttribute(k_select, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  cudaMemsetAsync(v.q_count, 0, sizeof(int32_t), s);
+  k_select<<<v.R, kThreads, sm, s>>>(v, wave);
+}
+
+void launch_expand(const EngineView& v, int root_mode, cudaStream_t s) {
+  if (!root_mode) cudaMemsetAsync(v.q_count + 1, 0, sizeof(int32_t), s);
+  k_expand<<<v.R, kThreads, 0, s>>>(v, root_mode);
+}
+
+void launch_backup(const EngineView& v, cudaStream_t s) { k_backup<<<v.R, kThreads, 0, s>>>(v); }
+
+void launch_root_visits(const EngineView& v, int32_t* visits, float* nw, cudaStream_t s) {
+  k_root_visits<<<v.R, 256, 0, s>>>(v, visits, nw);
+}
+
+void launch_export(const EngineView& v, int tree, int count, int32_t* N, float* W, float* P,
+                   int32_t* VL, int32_t* parent, int32_t* action, uint8_t* terminal,
+                   cudaStream_t s) {
+  const int blocks = max(1, min(1024, (count + 255) / 256));
+  k_export<<<blocks, 256, 0, s>>>(v, tree, count, N, W, P, VL, parent, action, terminal);
+}
+
+void launch_status(const EngineView& v, int32_t* status, int32_t* num_nodes, cudaStream_t s) {
+  k_status<<<(v.R + 255) / 256, 256, 0, s>>>(v, status, num_nodes);
+}
+
+}  // namespace omq

@@ -1,0 +1,244 @@
+"""Device-resident wave-MCTS engine: a set of independent trees searched in lockstep.
+
+Python holds a handle and torch tensors for inputs/outputs; every step runs in
+libomq_b200.so on the current CUDA stream. One engine = one device.
+
+The evaluator between the select/expand/backup phases is one of
+  * ``"synthetic"`` - the built-in integer-exact synthetic evaluator kernel;
+  * an object with ``forward_queue(engine, queue)`` (the device ResNet evaluator of this
+    package, which reads the queue in place and writes the queue's policy/value buffers);
+  * any object with the reference evaluator protocol
+    ``evaluate_batch(features[B,19,H,W]) -> (policy[B,A] probabilities, value[B] or [B,1])``
+    (python/mcts/core/wave_search.py:866-871, 1381-1383); features are handed over as a CUDA
+    fp32 tensor, results are copied into the queue buffers.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib
+
+PLANES = 19
+
+
+def _stream_ptr(stream=None) -> ctypes.c_void_p:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+class WaveEngine:
+    def __init__(self, num_trees: int, board_size: int = 15, capacity: int = 200000,
+                 max_wave_size: int = 256, c_puct: float = 1.4, virtual_loss: float = 1.0,
+                 enable_virtual_loss: bool = True, max_depth: int = 100, device=None):
+        if not torch.cuda.is_available():
+            raise RuntimeError("WaveEngine needs a CUDA device (B200); there is no CPU fallback")
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
+        self.L = _lib.load()
+        self.num_trees = int(num_trees)
+        self.board_size = int(board_size)
+        self.cells = self.board_size ** 2
+        self.actions = self.cells
+        self.capacity = int(capacity)
+        self.max_wave_size = int(max_wave_size)
+        cfg = _lib.EngineConfig(self.num_trees, self.board_size, self.capacity, self.max_wave_size,
+                                int(max_depth), float(c_puct), float(virtual_loss),
+                                int(bool(enable_virtual_loss)), dev.index or 0)
+        self.cfg = cfg
+        h = ctypes.c_void_p()
+        with torch.cuda.device(dev):
+            _lib.check(self.L.omq_engine_create(ctypes.byref(cfg), ctypes.byref(h)), "omq_engine_create")
+        self._h = h
+        self.queue_capacity = self.num_trees * self.max_wave_size
+        self._features = None
+        self._visits = torch.zeros(self.num_trees, self.actions, dtype=torch.int32, device=dev)
+        self._root_nw = torch.zeros(self.num_trees, 2, dtype=torch.float32, device=dev)
+        self._status = torch.zeros(self.num_trees, dtype=torch.int32, device=dev)
+        self._nodes = torch.zeros(self.num_trees, dtype=torch.int32, device=dev)
+
+    # -- lifetime ------------------------------------------------------------------------------
+    def close(self):
+        if getattr(self, "_h", None) and self._h.value:
+            self.L.omq_engine_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def memory_bytes(self) -> int:
+        b = ctypes.c_uint64()
+        _lib.check(self.L.omq_engine_memory(self._h, ctypes.byref(b)), "omq_engine_memory")
+        return int(b.value)
+
+    # -- queue access --------------------------------------------------------------------------
+    def queue_buffers(self, queue: int):
+        """(entries int32 [cap,2], policy fp32 [cap,A], value fp32 [cap], count int32 [1]) as
+        tensors aliasing the engine's device memory."""
+        e, p, v, c = (ctypes.c_void_p() for _ in range(4))
+        cap = ctypes.c_int32()
+        _lib.check(self.L.omq_queue_buffers(self._h, queue, ctypes.byref(e), ctypes.byref(p),
+                                            ctypes.byref(v), ctypes.byref(c), ctypes.byref(cap)),
+                   "omq_queue_buffers")
+        n = cap.value
+        return (_wrap(e.value, (n, 2), torch.int32, self.device),
+                _wrap(p.value, (n, self.actions), torch.float32, self.device),
+                _wrap(v.value, (n,), torch.float32, self.device),
+                _wrap(c.value, (1,), torch.int32, self.device))
+
+    def queue_count(self, queue: int) -> int:
+        n = ctypes.c_int32()
+        _lib.check(self.L.omq_queue_count(self._h, queue, ctypes.byref(n), _stream_ptr()), "omq_queue_count")
+        return int(n.value)
+
+    def queue_features(self, queue: int) -> torch.Tensor:
+        """Reference feature tensor of the queued positions, fp32 [count, 19, n, n] (syncs)."""
+        count = self.queue_count(queue)
+        if self._features is None:
+            self._features = torch.empty(self.queue_capacity, PLANES, self.board_size,
+                                         self.board_size, dtype=torch.float32, device=self.device)
+        _lib.check(self.L.omq_queue_features(self._h, queue, ctypes.c_void_p(self._features.data_ptr()),
+                                             _stream_ptr()), "omq_queue_features")
+        return self._features[:count]
+
+    def evaluate_queue(self, queue: int, evaluator) -> None:
+        if isinstance(evaluator, str):
+            if evaluator != "synthetic":
+                raise ValueError(f"unknown built-in evaluator {evaluator!r}")
+            _lib.check(self.L.omq_queue_eval_synthetic(self._h, queue, _stream_ptr()),
+                       "omq_queue_eval_synthetic")
+            return
+        if hasattr(evaluator, "forward_queue"):
+            evaluator.forward_queue(self, queue)
+            return
+        feats = self.queue_features(queue)
+        n = feats.shape[0]
+        if n == 0:
+            return
+        policy, value = evaluator.evaluate_batch(feats)
+        _, qp, qv, _ = self.queue_buffers(queue)
+        qp[:n].copy_(torch.as_tensor(np.asarray(policy) if not torch.is_tensor(policy) else policy)
+                     .reshape(n, self.actions).to(self.device, torch.float32))
+        qv[:n].copy_(torch.as_tensor(np.asarray(value) if not torch.is_tensor(value) else value)
+                     .reshape(n).to(self.device, torch.float32))
+
+    # -- search phases -------------------------------------------------------------------------
+    def begin(self, boards: torch.Tensor) -> None:
+        b = boards.to(self.device, torch.int8).contiguous()
+        if b.shape != (self.num_trees, self.board_size, self.board_size):
+            raise ValueError(f"boards must be [{self.num_trees}, {self.board_size}, {self.board_size}]")
+        self._boards = b
+        _lib.check(self.L.omq_begin(self._h, ctypes.c_void_p(b.data_ptr()), _stream_ptr()), "omq_begin")
+
+    def root_expand(self, evaluator="synthetic") -> None:
+        self.evaluate_queue(_lib.QUEUE_EXPAND, evaluator)
+        _lib.check(self.L.omq_root_expand(self._h, _stream_ptr()), "omq_root_expand")
+
+    def wave(self, wave_size: int, evaluator="synthetic") -> None:
+        s = _stream_ptr()
+        _lib.check(self.L.omq_wave_select(self._h, int(wave_size), s), "omq_wave_select")
+        self.evaluate_queue(_lib.QUEUE_EXPAND, evaluator)
+        _lib.check(self.L.omq_wave_expand(self._h, s), "omq_wave_expand")
+        self.evaluate_queue(_lib.QUEUE_FINAL, evaluator)
+        _lib.check(self.L.omq_wave_backup(self._h, s), "omq_wave_backup")
+
+    def search(self, boards: torch.Tensor, num_simulations: int, evaluator="synthetic") -> None:
+        """begin + forced root expansion + ceil(sims / max_wave_size) waves
+        (python/mcts/core/mcts.py:1020-1063). Raises on a device status (e.g. TreeFullError)."""
+        if isinstance(evaluator, str) and evaluator == "synthetic":
+            b = boards.to(self.device, torch.int8).contiguous()
+            self._boards = b
+            _lib.check(self.L.omq_search_synthetic(self._h, ctypes.c_void_p(b.data_ptr()),
+                                                   int(num_simulations), _stream_ptr()),
+                       "omq_search_synthetic")
+            return
+        self.begin(boards)
+        self.root_expand(evaluator)
+        done = 0
+        while done < num_simulations:
+            w = min(self.max_wave_size, num_simulations - done)
+            self.wave(w, evaluator)
+            done += w
+        self.check_status()
+
+    # -- readouts ------------------------------------------------------------------------------
+    def tree_status(self):
+        _lib.check(self.L.omq_tree_status(self._h, ctypes.c_void_p(self._status.data_ptr()),
+                                          ctypes.c_void_p(self._nodes.data_ptr()), _stream_ptr()),
+                   "omq_tree_status")
+        return self._status, self._nodes
+
+    def check_status(self) -> None:
+        st, nodes = self.tree_status()
+        st = st.cpu().numpy()
+        bad = np.nonzero(st)[0]
+        if len(bad):
+            r = int(bad[0])
+            code = int(st[r])
+            msg = f"tree {r}: {int(nodes[r])} nodes of {self.capacity}"
+            if code == _lib.OMQ_TREE_FULL:
+                raise _lib.TreeFullError(code, f"Tree full: {msg}")
+            raise _lib.OmqError(code, f"device status {code} in {msg}")
+
+    def root_visits(self) -> torch.Tensor:
+        """int32 [num_trees, actions]: root-child visit counts scattered by action."""
+        _lib.check(self.L.omq_root_visits(self._h, ctypes.c_void_p(self._visits.data_ptr()),
+                                          ctypes.c_void_p(self._root_nw.data_ptr()), _stream_ptr()),
+                   "omq_root_visits")
+        return self._visits
+
+    def root_nw(self) -> torch.Tensor:
+        self.root_visits()
+        return self._root_nw
+
+    def num_nodes(self) -> torch.Tensor:
+        return self.tree_status()[1]
+
+    def export_tree(self, tree: int) -> dict:
+        """Node arrays of one tree in creation order (numpy, host)."""
+        n = int(self.num_nodes()[tree])
+        d = self.device
+        out = dict(visits=torch.empty(n, dtype=torch.int32, device=d),
+                   value_sums=torch.empty(n, dtype=torch.float32, device=d),
+                   priors=torch.empty(n, dtype=torch.float32, device=d),
+                   virtual_loss=torch.empty(n, dtype=torch.int32, device=d),
+                   parent=torch.empty(n, dtype=torch.int32, device=d),
+                   action=torch.empty(n, dtype=torch.int32, device=d),
+                   terminal=torch.empty(n, dtype=torch.uint8, device=d))
+        ptr = [ctypes.c_void_p(out[k].data_ptr()) for k in
+               ("visits", "value_sums", "priors", "virtual_loss", "parent", "action", "terminal")]
+        _lib.check(self.L.omq_export_tree(self._h, int(tree), n, *ptr, _stream_ptr()), "omq_export_tree")
+        return {k: v.cpu().numpy() for k, v in out.items()}
+
+    @staticmethod
+    def policy_from_visits(visits: np.ndarray) -> np.ndarray:
+        """N_child / sum N_child in fp64 (python/mcts/core/mcts.py:1069-1137)."""
+        v = np.asarray(visits)
+        squeeze = v.ndim == 1
+        v = np.atleast_2d(v).astype(np.float64)
+        tot = v.sum(axis=1, keepdims=True)
+        pol = np.where(tot > 0, v / np.where(tot > 0, tot, 1.0), 1.0 / v.shape[1])
+        return pol[0] if squeeze else pol
+
+
+def _wrap(ptr: int, shape, dtype, device) -> torch.Tensor:
+    """A tensor view of engine-owned device memory (no copy, no ownership)."""
+    n = int(np.prod(shape))
+    if n == 0:
+        return torch.empty(shape, dtype=dtype, device=device)
+    itemsize = torch.empty((), dtype=dtype).element_size()
+    t = torch.as_tensor(_DeviceBuffer(ptr, n * itemsize), device=device)
+    return t.view(dtype).reshape(shape)
+
+
+class _DeviceBuffer:
+    """Minimal __cuda_array_interface__ exporter for a raw device pointer (uint8 bytes)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1",
+                                         "data": (ptr, False), "version": 3, "strides": None}

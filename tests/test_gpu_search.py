@@ -1,0 +1,151 @@
+"""GPU parity of the device wave search against the reference fixtures and the oracle.
+
+Bit-exact: visit counts, value sums, priors, virtual-loss counts, parent ids, parent actions,
+the implied children table, the root policy and the final move.
+"""
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+from golden_cases import children_table, digest, load, names
+
+pytestmark = pytest.mark.gpu
+
+
+def _engine(g, trees=1, **kw):
+    from omoknuni_quantum_b200.engine import WaveEngine
+    return WaveEngine(trees, capacity=int(g["capacity"]), max_wave_size=int(g["wave"]),
+                      c_puct=float(g["c_puct"]), virtual_loss=float(g["virtual_loss"]),
+                      enable_virtual_loss=bool(g["enable_vl"]), **kw)
+
+
+def _assert_tree_matches(t, g):
+    assert t["visits"].shape[0] == int(g["num_nodes"])
+    for k in ("visits", "value_sums", "priors", "virtual_loss", "parent", "action"):
+        assert digest(t[k]) == str(g["sha_" + k]), k
+    assert digest(children_table(t["parent"], t["action"])) == str(g["sha_children"])
+
+
+@pytest.mark.parametrize("name", names())
+def test_search_matches_reference_fixture(name):
+    g = load(name)
+    eng = _engine(g)
+    boards = torch.from_numpy(g["board"][None]).cuda()
+    eng.search(boards, int(g["sims"]))
+    t = eng.export_tree(0)
+    _assert_tree_matches(t, g)
+    visits = eng.root_visits()[0].cpu().numpy()
+    pol = eng.policy_from_visits(visits)
+    assert np.array_equal(pol, g["policy"])
+    assert int(np.argmax(pol)) == int(g["final_move"])
+
+
+def test_multi_tree_lockstep_matches_oracle(oracle_lib):
+    from omoknuni_quantum_b200.engine import WaveEngine
+    from omoknuni_quantum_b200.roots import random_roots
+    R, sims, wave = 6, 300, 64
+    roots = random_roots(11, R)
+    roots[2] = 0                                  # an empty root in the same batch
+    eng = WaveEngine(R, capacity=120000, max_wave_size=wave)
+    eng.search(torch.from_numpy(roots).cuda(), sims)
+    visits = eng.root_visits().cpu().numpy()
+    for r in range(R):
+        o = oracle_lib.Oracle(120000).search(roots[r], sims, wave)
+        t = eng.export_tree(r)
+        assert np.array_equal(t["visits"], o.visits)
+        assert np.array_equal(t["value_sums"], o.value_sums)
+        assert np.array_equal(t["parent"], o.parent) and np.array_equal(t["action"], o.action)
+        assert np.array_equal(eng.policy_from_visits(visits[r]), o.policy)
+
+
+class _RecordingTorchEvaluator:
+    """A float-valued evaluator on the GPU (fixed random linear policy/value heads on the
+    features). Records every output keyed by the feature bytes so that the oracle can replay
+    exactly the same evaluator outputs."""
+
+    def __init__(self, seed=0):
+        g = torch.Generator().manual_seed(seed)
+        self.wp = (torch.randn(19 * 225, 225, generator=g) * 0.05).cuda()
+        self.wv = (torch.randn(19 * 225, generator=g) * 0.05).cuda()
+        self.table = {}
+
+    def evaluate_batch(self, feats):
+        x = feats.reshape(feats.shape[0], -1)
+        logits = x @ self.wp
+        pol = torch.softmax(logits, dim=1)
+        val = torch.tanh(x @ self.wv)
+        fc = feats.cpu().numpy().astype(np.float32)
+        pc, vc = pol.cpu().numpy(), val.cpu().numpy()
+        for i in range(fc.shape[0]):
+            self.table[hashlib.sha256(fc[i].tobytes()).digest()] = (pc[i].copy(), vc[i])
+        return pol, val
+
+    def replay(self, feats):
+        n = feats.shape[0]
+        p = np.zeros((n, 225), np.float32)
+        v = np.zeros(n, np.float32)
+        for i in range(n):
+            p[i], v[i] = self.table[hashlib.sha256(np.ascontiguousarray(feats[i], np.float32).tobytes()).digest()]
+        return p, v
+
+
+def test_float_evaluator_replay_is_bit_exact(oracle_lib):
+    """Same evaluator outputs -> identical trees, W included (fp32 sums in the reference's
+    per-simulation order)."""
+    from omoknuni_quantum_b200.engine import WaveEngine
+    from omoknuni_quantum_b200.roots import random_root
+    board = random_root(21)
+    ev = _RecordingTorchEvaluator()
+    eng = WaveEngine(1, capacity=150000, max_wave_size=128)
+    eng.search(torch.from_numpy(board[None]).cuda(), 640, evaluator=ev)
+    t = eng.export_tree(0)
+    o = oracle_lib.Oracle(150000).search(board, 640, 128, evaluator=ev.replay)
+    assert o.result["boundary_ties"] == 0
+    assert np.array_equal(t["parent"], o.parent) and np.array_equal(t["action"], o.action)
+    assert np.array_equal(t["priors"], o.priors)
+    assert np.array_equal(t["visits"], o.visits)
+    assert np.array_equal(t["value_sums"], o.value_sums)
+
+
+def test_generic_evaluator_path_equals_builtin_synthetic(oracle_lib):
+    """The reference evaluator protocol (features -> evaluate_batch) gives the same tree as the
+    built-in synthetic kernel, and the device features equal the oracle's feature tensors."""
+    from omoknuni_quantum_b200.engine import WaveEngine
+    from omoknuni_quantum_b200.roots import random_root
+    board = random_root(5)
+
+    class NumpySynth:
+        def evaluate_batch(self, f):
+            return oracle_lib.synth_eval(f.cpu().numpy())
+
+    e1 = WaveEngine(1, capacity=80000, max_wave_size=64)
+    e1.search(torch.from_numpy(board[None]).cuda(), 256, evaluator=NumpySynth())
+    e2 = WaveEngine(1, capacity=80000, max_wave_size=64)
+    e2.search(torch.from_numpy(board[None]).cuda(), 256)
+    a, b = e1.export_tree(0), e2.export_tree(0)
+    for k in a:
+        assert np.array_equal(a[k], b[k]), k
+
+
+def test_tree_full_raises():
+    from omoknuni_quantum_b200._lib import TreeFullError
+    from omoknuni_quantum_b200.engine import WaveEngine
+    from omoknuni_quantum_b200.roots import random_root
+    eng = WaveEngine(1, capacity=5000, max_wave_size=256)
+    with pytest.raises(TreeFullError, match="Tree full"):
+        eng.search(torch.from_numpy(random_root(0)[None]).cuda(), 800)
+
+
+def test_virtual_loss_is_reverted_every_wave():
+    from omoknuni_quantum_b200.engine import WaveEngine
+    from omoknuni_quantum_b200.roots import random_root
+    eng = WaveEngine(1, capacity=100000, max_wave_size=128)
+    eng.begin(torch.from_numpy(random_root(3)[None]).cuda())
+    eng.root_expand()
+    for _ in range(3):
+        eng.wave(128)
+        t = eng.export_tree(0)
+        assert (t["virtual_loss"] == 0).all()
+        assert t["visits"][0] == t["visits"][t["parent"] == 0].sum()
