@@ -135,6 +135,59 @@ OMQ_API int omq_export_tree(omq_engine* e, int32_t tree, int32_t count, int32_t*
                     float* d_value_sums, float* d_priors, int32_t* d_virtual_loss,
                     int32_t* d_parent, int32_t* d_action, uint8_t* d_terminal, void* stream);
 
+
+/* ---------------------------------------------------------------------------------------------
+ * ResNet policy/value evaluator (reference: ResNetModel, python/mcts/neural_networks/
+ * resnet_model.py:26-271; ResNetEvaluator._forward_model, resnet_evaluator.py:231-265).
+ * bf16 weights/activations, fp32 accumulation, BatchNorm folded (eval mode).
+ * ------------------------------------------------------------------------------------------- */
+typedef struct omq_resnet omq_resnet;
+
+typedef struct {
+  int32_t board_size;        /* 15 Gomoku */
+  int32_t input_channels;    /* feature planes (19 for the reference's basic features), <= 64 */
+  int32_t num_blocks;        /* residual blocks */
+  int32_t filters;           /* 128 or 256 */
+  int32_t num_actions;       /* policy size (225 Gomoku) */
+  int32_t fc_policy_hidden;  /* PolicyHead fc1 width (reference default 256) */
+  int32_t fc_value_hidden;   /* ValueHead fc1 width (reference default 256) */
+  int32_t max_batch;         /* positions per forward call (activation buffers are sized for it) */
+  int32_t device;
+} omq_resnet_config;
+
+OMQ_API int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out);
+OMQ_API int omq_resnet_destroy(omq_resnet* net);
+OMQ_API int omq_resnet_memory(const omq_resnet* net, uint64_t* h_bytes);
+/* Element counts of the three packed parameter blobs omq_resnet_load expects:
+ *  conv_w (bf16): input conv [F][9][64] (input channels zero-padded to 64), then per block
+ *                 conv1 [F][9][F], conv2 [F][9][F]; K index = tap * Cin + channel, tap = 3*ky+kx;
+ *                 BatchNorm scale folded in.
+ *  conv_b (fp32): folded BatchNorm shift, [1 + 2*num_blocks][F].
+ *  head   (fp32): w1x1 [3][F] (policy ch0, policy ch1, value), b1x1 [3], policy fc1^T [2*HW][Hp],
+ *                 b [Hp], policy fc2^T [Hp][A], b [A], value fc1^T [HW][Hv], b [Hv],
+ *                 value fc2 [Hv], b [1]. */
+OMQ_API int omq_resnet_param_sizes(const omq_resnet* net, uint64_t* conv_w, uint64_t* conv_b,
+                                   uint64_t* head);
+OMQ_API int omq_resnet_load(omq_resnet* net, const uint16_t* d_conv_w, const float* d_conv_b,
+                            const float* d_head, void* stream);
+/* Forward on reference-layout features fp32 [batch][input_channels][n][n]
+ * -> policy probabilities fp32 [batch][num_actions], value fp32 [batch]. */
+OMQ_API int omq_resnet_forward_features(omq_resnet* net, const float* d_features, int32_t batch,
+                                        float* d_policy, float* d_value, void* stream);
+/* Forward on an already packed bf16 input [batch][(n+1)^2][64] (the padded pixel layout; NULL
+ * = the net's own input buffer). The batch is *d_count when d_count is not NULL (clamped to
+ * `batch`), which keeps the call free of host synchronisation. */
+OMQ_API int omq_resnet_forward_packed(omq_resnet* net, const uint16_t* d_input,
+                                      const int32_t* d_count, int32_t batch, float* d_policy,
+                                      float* d_value, void* stream);
+OMQ_API int omq_resnet_input_buffer(omq_resnet* net, uint16_t** d_input);
+/* Evaluate an engine leaf queue in place: the queued positions are packed on the device and
+ * the queue's policy/value buffers are written; no host synchronisation. */
+OMQ_API int omq_resnet_forward_queue(omq_resnet* net, omq_engine* engine, int32_t queue,
+                                     void* stream);
+/* Device error word of the net (OMQ_TIMEOUT after a bounded wait gave up); synchronizes. */
+OMQ_API int omq_resnet_error(omq_resnet* net, int32_t* h_error, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -42,6 +42,14 @@ class EngineConfig(ctypes.Structure):
                 ("device", ctypes.c_int32)]
 
 
+class ResNetConfig(ctypes.Structure):
+    _fields_ = [("board_size", ctypes.c_int32), ("input_channels", ctypes.c_int32),
+                ("num_blocks", ctypes.c_int32), ("filters", ctypes.c_int32),
+                ("num_actions", ctypes.c_int32), ("fc_policy_hidden", ctypes.c_int32),
+                ("fc_value_hidden", ctypes.c_int32), ("max_batch", ctypes.c_int32),
+                ("device", ctypes.c_int32)]
+
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int32
 
@@ -66,6 +74,17 @@ SIGNATURES = {
     "omq_root_visits": [_P, _P, _P, _P],
     "omq_tree_status": [_P, _P, _P, _P],
     "omq_export_tree": [_P, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P],
+    "omq_resnet_create": [ctypes.POINTER(ResNetConfig), ctypes.POINTER(_P)],
+    "omq_resnet_destroy": [_P],
+    "omq_resnet_memory": [_P, ctypes.POINTER(ctypes.c_uint64)],
+    "omq_resnet_param_sizes": [_P, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
+                               ctypes.POINTER(ctypes.c_uint64)],
+    "omq_resnet_load": [_P, _P, _P, _P, _P],
+    "omq_resnet_forward_features": [_P, _P, _I, _P, _P, _P],
+    "omq_resnet_forward_packed": [_P, _P, _P, _I, _P, _P, _P],
+    "omq_resnet_input_buffer": [_P, ctypes.POINTER(_P)],
+    "omq_resnet_forward_queue": [_P, _P, _I, _P],
+    "omq_resnet_error": [_P, ctypes.POINTER(_I), _P],
 }
 _RESTYPES = {"omq_status_string": ctypes.c_char_p, "omq_last_error": ctypes.c_char_p}
 

@@ -23,19 +23,6 @@ int cuda_status(cudaError_t e, const char* what) {
   return OMQ_CUDA_ERROR;
 }
 
-struct DeviceGuard {
-  int prev = -1;
-  explicit DeviceGuard(int dev) {
-    cudaGetDevice(&prev);
-    if (prev != dev) cudaSetDevice(dev);
-  }
-  ~DeviceGuard() {
-    int cur = -1;
-    cudaGetDevice(&cur);
-    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
-  }
-};
-
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 }  // namespace omq

@@ -180,6 +180,49 @@ __global__ void __launch_bounds__(kSynthWarps * 32) k_features(EngineView v, int
   }
 }
 
+// ResNet input: the same planes as k_features, bf16, channels padded to 64, in the padded pixel
+// space [(S+1) x (S+1)] whose last row and column stay zero. One warp per queued position.
+__global__ void __launch_bounds__(kSynthWarps * 32) k_pack_queue(EngineView v, int queue, int P, uint4* out) {
+  __shared__ WarpPos wps[kSynthWarps];
+  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
+  const int q = blockIdx.x * kSynthWarps + wl;
+  const int count = v.q_count[queue];
+  if (q >= count) return;
+  WarpPos& wp = wps[wl];
+  const int2 ent = v.q_entries[queue][q];
+  const int r = ent.x;
+  const int d = warp_rebuild(v, r, ent.y, wp);
+  if (d < 0) { if (lane == 0) v.hdr[r].status = OMQ_BAD_ARG; return; }
+  const TreeHeader& H = v.hdr[r];
+  const uint16_t player = ((d % 2 == 0) ? H.root_player : 3 - H.root_player) == 1 ? 0x3F80 : 0x4000;
+  const uint32_t hp = history_planes(H.root_mc + d, d, kFullHistoryGomoku);
+  const int last = d >= 1 ? wp.acts[d - 1] : -1;
+  const int S = v.S;
+  uint4* o = out + (size_t)q * P * 8;
+  for (int i = lane; i < P * 8; i += 32) {
+    const int pix = i >> 3, chunk = i & 7;
+    const int y = pix / (S + 1), x = pix - y * (S + 1);
+    uint16_t h[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (y < S && x < S) {
+      const int c = y * S + x;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int ch = chunk * 8 + e;
+        if (ch == 0) h[e] = wp.board[c] != 0 ? 0x3F80 : 0;
+        else if (ch == 1) h[e] = player;
+        else if (ch < kPlanes) h[e] = (((hp >> ch) & 1u) && c == last) ? 0x3F80 : 0;
+      }
+    }
+    o[i] = *reinterpret_cast<uint4*>(h);
+  }
+}
+
+void launch_pack_queue(const EngineView& v, int queue, int P, void* out, cudaStream_t s) {
+  const int cap = v.R * v.WCAP;
+  k_pack_queue<<<(cap + kSynthWarps - 1) / kSynthWarps, kSynthWarps * 32, 0, s>>>(
+      v, queue, P, reinterpret_cast<uint4*>(out));
+}
+
 void launch_synth_eval(const EngineView& v, int queue, cudaStream_t s) {
   const int cap = v.R * v.WCAP;
   k_synth<<<(cap + kSynthWarps - 1) / kSynthWarps, kSynthWarps * 32, 0, s>>>(v, queue);

@@ -155,6 +155,20 @@ struct omq_engine {
 };
 
 namespace omq {
+// Makes `dev` current for the lifetime of the guard, restoring the caller's device after.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
 void set_error(const char* fmt, ...);
 int cuda_status(cudaError_t e, const char* what);
 
@@ -168,4 +182,6 @@ void launch_export(const EngineView& v, int tree, int count, int32_t* N, float* 
 void launch_status(const EngineView& v, int32_t* status, int32_t* num_nodes, cudaStream_t s);
 void launch_features(const EngineView& v, int queue, float* out, cudaStream_t s);
 void launch_synth_eval(const EngineView& v, int queue, cudaStream_t s);
+// queue positions -> bf16 [count][P][64] padded pixel layout (ResNet input)
+void launch_pack_queue(const EngineView& v, int queue, int P, void* out, cudaStream_t s);
 }  // namespace omq

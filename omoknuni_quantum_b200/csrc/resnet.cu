@@ -1,0 +1,703 @@
+// AlphaZero ResNet policy/value forward on B200 (reference: ResNetModel.forward,
+// python/mcts/neural_networks/resnet_model.py:247-271, evaluated as in
+// ResNetEvaluator._forward_model, resnet_evaluator.py:231-265 -> policy = exp(log_softmax)).
+//
+// Trunk: every 3x3 convolution (BN folded into weight + bias) is one persistent implicit-GEMM
+// kernel on the 5th-generation tensor cores:
+//   M = positions x padded pixels, N = output channels, K = 9 taps x input channels.
+// Activations live in a padded pixel space: each position is a (S+1) x (S+1) grid whose last
+// row and last column are zero (S = board size). Flattened row-major, the grid makes every 3x3
+// tap a constant row shift (dy*(S+1) + dx) of the same matrix - the zero column serves as both
+// the left and the right border, and the zero row of position b as the top border of b+1 - so
+// each A tile is one plain 2D TMA box (rows before the tensor start read as zeros). For 15x15
+// Gomoku the padded grid is 16x16 = 256 rows = two 128-row tiles per position.
+// Warp roles per CTA: warp 0 TMA producer, warp 1 MMA issuer (single thread, tcgen05.mma with
+// both operands in 128B-swizzled shared memory), warps 2-5 epilogue (TMEM -> registers, + bias,
+// + residual, ReLU, zero the pad pixels, bf16 store). Accumulators are double-buffered in TMEM
+// so the epilogue of one tile overlaps the MMAs of the next.
+// Heads: 1x1 convolutions (2 policy + 1 value channel, BN folded) and the small FC layers run
+// as SIMT fp32 kernels over groups of positions.
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <cstring>
+#include <new>
+
+#include "omq_internal.cuh"
+#include "sm100_ptx.cuh"
+
+namespace omq {
+
+constexpr int kConvThreads = 192;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait before giving up
+constexpr int kTileM = 128;
+constexpr int kBlockK = 64;     // 64 bf16 = one 128-byte swizzle row
+constexpr int kInPad = 64;      // input planes padded to one K block
+
+struct ConvArgs {
+  const float* bias;
+  const __nv_bfloat16* residual;
+  __nv_bfloat16* out;
+  const int32_t* d_count;
+  int32_t count;
+  int32_t P;
+  int32_t S;
+  int32_t kb_per_tap;
+  int32_t relu;
+  int32_t* error;
+};
+
+template <int BN>
+struct ConvCfg {
+  static constexpr int kA = kTileM * kBlockK * 2;
+  static constexpr int kB = BN * kBlockK * 2;
+  static constexpr int kStage = kA + kB;
+  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kSmem = kStages * kStage + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kConvThreads, 1)
+    k_conv3x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              ConvArgs args) {
+  using Cfg = ConvCfg<BN>;
+  constexpr int kStages = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * Cfg::kStage);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_pos = args.d_count ? min(*args.d_count, args.count) : args.count;
+  const int rows = n_pos * args.P;
+  const int tiles = (rows + kTileM - 1) / kTileM;
+  const int KB = 9 * args.kb_per_tap;
+  const int rowstride = args.S + 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) { ptx::mbar_init(&full[s], 1); ptx::mbar_init(&empty[s], 1); }
+    for (int i = 0; i < 2; ++i) { ptx::mbar_init(&tfull[i], 1); ptx::mbar_init(&tempty[i], 4); }
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    ptx::fence_barrier_init();
+    ptx::prefetch_tmap(&tmA);
+    ptx::prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, 2 * BN);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    int s = 0;
+    uint32_t ph = 0;
+    int issued[kStages];
+    for (int i = 0; i < kStages; ++i) issued[i] = -1;
+    for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+      const int m0 = tile * kTileM;
+      for (int kb = 0; kb < KB; ++kb) {
+        if (!ptx::mbar_wait(&empty[s], ph ^ 1, abort_flag, kWaitLimitNs)) goto producer_done;
+        const int tap = kb / args.kb_per_tap, cb = kb - tap * args.kb_per_tap;
+        const int dy = tap / 3 - 1, dx = tap % 3 - 1;
+        ptx::mbar_arrive_expect_tx(&full[s], Cfg::kStage);
+        ptx::tma_load_2d(smem + s * Cfg::kStage, &tmA, &full[s], cb * kBlockK,
+                         m0 + dy * rowstride + dx);
+        ptx::tma_load_2d(smem + s * Cfg::kStage + Cfg::kA, &tmB, &full[s], kb * kBlockK, 0);
+        issued[s] = (int)ph;
+        if (++s == kStages) { s = 0; ph ^= 1; }
+      }
+    }
+  producer_done:
+    // never leave with copies in flight: wait (bounded) for every issued stage to land
+    for (int i = 0; i < kStages; ++i)
+      if (issued[i] >= 0) {
+        volatile int dummy = 0;
+        ptx::mbar_wait(&full[i], (uint32_t)issued[i], &dummy, kWaitLimitNs);
+      }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    constexpr uint32_t idesc = ptx::idesc_bf16_f32(kTileM, BN);
+    int s = 0;
+    uint32_t ph = 0;
+    bool any = false;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+      const int ab = t & 1;
+      const uint32_t aph = (t >> 1) & 1;
+      if (!ptx::mbar_wait(&tempty[ab], aph ^ 1, abort_flag, kWaitLimitNs)) break;
+      ptx::tc_fence_after();
+      const uint32_t d = tmem + ab * BN;
+      bool ok = true;
+      for (int kb = 0; kb < KB; ++kb) {
+        if (!ptx::mbar_wait(&full[s], ph, abort_flag, kWaitLimitNs)) { ok = false; break; }
+        ptx::tc_fence_after();
+        const uint32_t a_addr = ptx::smem_u32(smem + s * Cfg::kStage);
+        const uint32_t b_addr = a_addr + Cfg::kA;
+#pragma unroll
+        for (int k = 0; k < kBlockK / 16; ++k)
+          ptx::mma_bf16(d, ptx::smem_desc_sw128(a_addr + k * 32),
+                        ptx::smem_desc_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
+        any = true;
+        ptx::mma_commit(&empty[s]);
+        if (++s == kStages) { s = 0; ph ^= 1; }
+      }
+      if (!ok) break;
+      ptx::mma_commit(&tfull[ab]);
+    }
+    if (any) {  // drain outstanding MMAs before TMEM is released
+      ptx::mma_commit(drain);
+      volatile int dummy = 0;
+      ptx::mbar_wait(drain, 0, &dummy, kWaitLimitNs);
+    }
+  } else if (warp >= 2) {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+      const int ab = t & 1;
+      const uint32_t aph = (t >> 1) & 1;
+      if (!ptx::mbar_wait(&tfull[ab], aph, abort_flag, kWaitLimitNs)) break;
+      ptx::tc_fence_after();
+      const int m = tile * kTileM + q * 32 + lane;
+      const bool valid = m < rows;
+      const int pix = m % args.P;
+      const int y = pix / rowstride, x = pix - y * rowstride;
+      const bool pad = (y == args.S) || (x == args.S);
+      __nv_bfloat16* orow = args.out + (size_t)m * BN;
+      const __nv_bfloat16* rrow = args.residual ? args.residual + (size_t)m * BN : nullptr;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + ab * BN + c0, r);
+        ptx::tmem_ld_wait();
+        if (!valid) continue;
+        uint4 packed[4];
+        uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
+        if (pad) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) pw[j] = 0u;
+        } else {
+          float res[32];
+          if (rrow) {
+            const uint4* rp = reinterpret_cast<const uint4*>(rrow + c0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 u = rp[j];
+              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                float2 f = __bfloat1622float2(h[e]);
+                res[8 * j + 2 * e] = f.x;
+                res[8 * j + 2 * e + 1] = f.y;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) res[j] = 0.0f;
+          }
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            float v0 = __uint_as_float(r[j]) + __ldg(args.bias + c0 + j) + res[j];
+            float v1 = __uint_as_float(r[j + 1]) + __ldg(args.bias + c0 + j + 1) + res[j + 1];
+            if (args.relu) { v0 = fmaxf(v0, 0.0f); v1 = fmaxf(v1, 0.0f); }
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
+            pw[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+        }
+        uint4* op = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) op[j] = packed[j];
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&tempty[ab]);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 2 * BN);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(args.error, OMQ_TIMEOUT);
+}
+
+// ---------------------------------------------------------------------------------------------
+// input packing: reference fp32 features [n][19][S][S] -> bf16 [n][P][64] padded pixel space
+// ---------------------------------------------------------------------------------------------
+__global__ void k_pack_features(const float* feat, int planes, int S, int P, const int32_t* d_count,
+                                int count, __nv_bfloat16* out) {
+  const int n = d_count ? min(*d_count, count) : count;
+  const int total = n * P;
+  const int C = S * S;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total * 8; i += gridDim.x * blockDim.x) {
+    const int row = i >> 3, chunk = i & 7;   // 8 chunks of 8 channels per pixel
+    const int b = row / P, pix = row - b * P;
+    const int y = pix / (S + 1), x = pix - y * (S + 1);
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (y < S && x < S) {
+      __nv_bfloat16 h[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int c = chunk * 8 + e;
+        const float v = c < planes ? feat[((size_t)b * planes + c) * C + y * S + x] : 0.0f;
+        h[e] = __float2bfloat16_rn(v);
+      }
+      u = *reinterpret_cast<uint4*>(h);
+    }
+    reinterpret_cast<uint4*>(out)[(size_t)row * 8 + chunk] = u;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// heads
+// ---------------------------------------------------------------------------------------------
+constexpr int kHeadPos = 8;       // positions per block
+constexpr int kHeadThreads = 256;
+
+struct HeadArgs {
+  const __nv_bfloat16* act;   // [rows][C]
+  int C, S, P, A, Hp, Hv;
+  const float* w1x1;          // [3][C]
+  const float* b1x1;          // [3]
+  const float* fc1p;          // [2*HW][Hp]
+  const float* b1p;           // [Hp]
+  const float* fc2p;          // [Hp][A]
+  const float* b2p;           // [A]
+  const float* fc1v;          // [HW][Hv]
+  const float* b1v;           // [Hv]
+  const float* fc2v;          // [Hv]
+  const float* b2v;           // [1]
+  const int32_t* d_count;
+  int count;
+  float* policy;              // [n][A]
+  float* value;               // [n]
+};
+
+__global__ void __launch_bounds__(kHeadThreads) k_heads(HeadArgs a) {
+  extern __shared__ float hsm[];
+  const int HW = a.S * a.S;
+  float* h3 = hsm;                                // [kHeadPos][3*HW]
+  float* hp = h3 + kHeadPos * 3 * HW;             // [kHeadPos][Hp]
+  float* lg = hp + kHeadPos * a.Hp;               // [kHeadPos][A]
+  float* hv = lg + kHeadPos * a.A;                // [kHeadPos][Hv]
+  float* w1 = hv + kHeadPos * a.Hv;               // [3][C]
+  const int n = a.d_count ? min(*a.d_count, a.count) : a.count;
+  const int p0 = blockIdx.x * kHeadPos;
+  if (p0 >= n) return;
+  const int np = min(kHeadPos, n - p0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < 3 * a.C; i += kHeadThreads) w1[i] = a.w1x1[i];
+  __syncthreads();
+  // 1x1 convolutions + folded BN + ReLU -> h3[pos][ch*HW + cell]
+  for (int i = tid; i < np * HW; i += kHeadThreads) {
+    const int pl = i / HW, cell = i - pl * HW;
+    const int yy = cell / a.S, xx = cell - yy * a.S;
+    const __nv_bfloat16* row = a.act + ((size_t)(p0 + pl) * a.P + yy * (a.S + 1) + xx) * a.C;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+    for (int c = 0; c < a.C; c += 8) {
+      uint4 u = *reinterpret_cast<const uint4*>(row + c);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __bfloat1622float2(h[e]);
+        const int cc = c + 2 * e;
+        s0 += f.x * w1[cc] + f.y * w1[cc + 1];
+        s1 += f.x * w1[a.C + cc] + f.y * w1[a.C + cc + 1];
+        s2 += f.x * w1[2 * a.C + cc] + f.y * w1[2 * a.C + cc + 1];
+      }
+    }
+    float* o = h3 + (size_t)pl * 3 * HW;
+    o[cell] = fmaxf(s0 + a.b1x1[0], 0.f);
+    o[HW + cell] = fmaxf(s1 + a.b1x1[1], 0.f);
+    o[2 * HW + cell] = fmaxf(s2 + a.b1x1[2], 0.f);
+  }
+  __syncthreads();
+  // policy fc1 (2*HW -> Hp) + ReLU
+  for (int j = tid; j < a.Hp; j += kHeadThreads) {
+    float acc[kHeadPos];
+#pragma unroll
+    for (int p = 0; p < kHeadPos; ++p) acc[p] = 0.f;
+    for (int k = 0; k < 2 * HW; ++k) {
+      const float w = __ldg(a.fc1p + (size_t)k * a.Hp + j);
+#pragma unroll
+      for (int p = 0; p < kHeadPos; ++p) acc[p] += w * h3[(size_t)p * 3 * HW + k];
+    }
+    for (int p = 0; p < kHeadPos; ++p) hp[p * a.Hp + j] = fmaxf(acc[p] + a.b1p[j], 0.f);
+  }
+  // value fc1 (HW -> Hv) + ReLU
+  for (int j = tid; j < a.Hv; j += kHeadThreads) {
+    float acc[kHeadPos];
+#pragma unroll
+    for (int p = 0; p < kHeadPos; ++p) acc[p] = 0.f;
+    for (int k = 0; k < HW; ++k) {
+      const float w = __ldg(a.fc1v + (size_t)k * a.Hv + j);
+#pragma unroll
+      for (int p = 0; p < kHeadPos; ++p) acc[p] += w * h3[(size_t)p * 3 * HW + 2 * HW + k];
+    }
+    for (int p = 0; p < kHeadPos; ++p) hv[p * a.Hv + j] = fmaxf(acc[p] + a.b1v[j], 0.f);
+  }
+  __syncthreads();
+  // policy fc2 (Hp -> A)
+  for (int j = tid; j < a.A; j += kHeadThreads) {
+    float acc[kHeadPos];
+#pragma unroll
+    for (int p = 0; p < kHeadPos; ++p) acc[p] = 0.f;
+    for (int k = 0; k < a.Hp; ++k) {
+      const float w = __ldg(a.fc2p + (size_t)k * a.A + j);
+#pragma unroll
+      for (int p = 0; p < kHeadPos; ++p) acc[p] += w * hp[p * a.Hp + k];
+    }
+    for (int p = 0; p < kHeadPos; ++p) lg[p * a.A + j] = acc[p] + a.b2p[j];
+  }
+  __syncthreads();
+  // softmax (= exp(log_softmax)) and value fc2 + tanh: one warp per position
+  if (warp < np) {
+    const int p = warp;
+    const float* l = lg + p * a.A;
+    float mx = -INFINITY;
+    for (int j = lane; j < a.A; j += 32) mx = fmaxf(mx, l[j]);
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    float sum = 0.f;
+    for (int j = lane; j < a.A; j += 32) sum += expf(l[j] - mx);
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+    const float inv = 1.0f / sum;
+    float* out = a.policy + (size_t)(p0 + p) * a.A;
+    for (int j = lane; j < a.A; j += 32) out[j] = expf(l[j] - mx) * inv;
+    float v = 0.f;
+    for (int k = lane; k < a.Hv; k += 32) v += hv[p * a.Hv + k] * a.fc2v[k];
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    if (lane == 0) a.value[p0 + p] = tanhf(v + a.b2v[0]);
+  }
+}
+
+}  // namespace omq
+
+// =============================================================================================
+// network object + C ABI
+// =============================================================================================
+using namespace omq;
+
+typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                      const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                      const cuuint32_t*, CUtensorMapInterleave,
+                                      CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                      CUtensorMapFloatOOBfill);
+
+struct omq_resnet {
+  omq_resnet_config cfg;
+  int S, P, HW, A, C, NB, Hp, Hv, max_batch;
+  size_t rows;
+  int sm_count;
+  void* arena;
+  size_t bytes;
+  __nv_bfloat16* conv_w;   // (1 + 2*NB) convs
+  float* conv_b;
+  float* head;
+  __nv_bfloat16* x_in;     // [rows][64]
+  __nv_bfloat16* act[3];   // [rows][C]
+  int32_t* error;
+  CUtensorMap tmA_in, tmA[3], tmB_in;
+  CUtensorMap* tmB;        // [2*NB]
+  int loaded;
+};
+
+static PFN_encodeTiled_t get_encode() {
+  static PFN_encodeTiled_t fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled_t>(p);
+  }
+  return fn;
+}
+
+// 2D bf16 tensor map: inner dim `inner` elements, `outer` rows, box {64, box_rows}, 128B swizzle.
+static int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint32_t box_rows) {
+  PFN_encodeTiled_t enc = get_encode();
+  if (!enc) { set_error("cuTensorMapEncodeTiled unavailable"); return OMQ_CUDA_ERROR; }
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                   box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) { set_error("cuTensorMapEncodeTiled failed (%d)", (int)r); return OMQ_CUDA_ERROR; }
+  return OMQ_OK;
+}
+
+static size_t head_floats(const omq_resnet* n) {
+  return (size_t)3 * n->C + 3 + (size_t)2 * n->HW * n->Hp + n->Hp + (size_t)n->Hp * n->A + n->A +
+         (size_t)n->HW * n->Hv + n->Hv + n->Hv + 1;
+}
+
+static size_t head_smem(const omq_resnet* n) {
+  return sizeof(float) * ((size_t)kHeadPos * (3 * n->HW + n->Hp + n->A + n->Hv) + 3 * n->C);
+}
+
+extern "C" {
+
+int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
+  if (!cfg || !out) { set_error("null argument"); return OMQ_BAD_ARG; }
+  *out = nullptr;
+  const omq_resnet_config c = *cfg;
+  if (c.board_size < 5 || c.board_size > 19 || c.input_channels < 1 || c.input_channels > kInPad ||
+      (c.filters != 128 && c.filters != 256) || c.num_blocks < 0 || c.num_blocks > 64 ||
+      c.num_actions < 1 || c.num_actions > 4096 || c.fc_policy_hidden < 1 ||
+      c.fc_policy_hidden > 1024 || c.fc_value_hidden < 1 || c.fc_value_hidden > 1024 ||
+      c.max_batch < 1) {
+    set_error("bad resnet config");
+    return OMQ_BAD_ARG;
+  }
+  DeviceGuard g(c.device);
+  omq_resnet* n = new (std::nothrow) omq_resnet();
+  if (!n) return OMQ_BAD_ARG;
+  n->cfg = c;
+  n->S = c.board_size;
+  n->P = (c.board_size + 1) * (c.board_size + 1);
+  n->HW = c.board_size * c.board_size;
+  n->A = c.num_actions;
+  n->C = c.filters;
+  n->NB = c.num_blocks;
+  n->Hp = c.fc_policy_hidden;
+  n->Hv = c.fc_value_hidden;
+  n->max_batch = c.max_batch;
+  n->rows = (size_t)c.max_batch * n->P;
+  cudaDeviceGetAttribute(&n->sm_count, cudaDevAttrMultiProcessorCount, c.device);
+  const size_t nconv_w = (size_t)n->C * 9 * kInPad + (size_t)2 * n->NB * n->C * 9 * n->C;
+  const size_t nconv_b = (size_t)(1 + 2 * n->NB) * n->C;
+  size_t off[8], k = 0, tot = 0;
+  auto take = [&](size_t b) { off[k++] = tot; tot += (b + 1023) & ~(size_t)1023; };
+  take(nconv_w * 2);
+  take(nconv_b * 4);
+  take(head_floats(n) * 4);
+  take(n->rows * kInPad * 2);
+  for (int i = 0; i < 3; ++i) take(n->rows * n->C * 2);
+  take(16);
+  void* arena = nullptr;
+  cudaError_t e = cudaMalloc(&arena, tot);
+  if (e != cudaSuccess) { delete n; return cuda_status(e, "cudaMalloc(resnet)"); }
+  char* b = static_cast<char*>(arena);
+  n->arena = arena;
+  n->bytes = tot;
+  n->conv_w = reinterpret_cast<__nv_bfloat16*>(b + off[0]);
+  n->conv_b = reinterpret_cast<float*>(b + off[1]);
+  n->head = reinterpret_cast<float*>(b + off[2]);
+  n->x_in = reinterpret_cast<__nv_bfloat16*>(b + off[3]);
+  for (int i = 0; i < 3; ++i) n->act[i] = reinterpret_cast<__nv_bfloat16*>(b + off[4 + i]);
+  n->error = reinterpret_cast<int32_t*>(b + off[7]);
+  cudaMemset(n->error, 0, 16);
+  // activations start zeroed so that never-written padding rows read as zeros
+  cudaMemset(b + off[3], 0, tot - off[3]);
+  n->tmB = new (std::nothrow) CUtensorMap[2 * n->NB + 1];
+  int st = make_map(&n->tmA_in, n->x_in, kInPad, n->rows, kTileM);
+  for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n->tmA[i], n->act[i], n->C, n->rows, kTileM);
+  if (st == OMQ_OK) st = make_map(&n->tmB_in, n->conv_w, 9 * kInPad, n->C, n->C);
+  const __nv_bfloat16* wb = n->conv_w + (size_t)n->C * 9 * kInPad;
+  for (int i = 0; st == OMQ_OK && i < 2 * n->NB; ++i)
+    st = make_map(&n->tmB[i], wb + (size_t)i * n->C * 9 * n->C, 9 * n->C, n->C, n->C);
+  if (st != OMQ_OK) {
+    cudaFree(arena);
+    delete[] n->tmB;
+    delete n;
+    return st;
+  }
+  *out = n;
+  return OMQ_OK;
+}
+
+int omq_resnet_destroy(omq_resnet* n) {
+  if (!n) return OMQ_OK;
+  DeviceGuard g(n->cfg.device);
+  cudaError_t e = cudaFree(n->arena);
+  delete[] n->tmB;
+  delete n;
+  return cuda_status(e, "cudaFree(resnet)");
+}
+
+int omq_resnet_param_sizes(const omq_resnet* n, uint64_t* conv_w, uint64_t* conv_b, uint64_t* head) {
+  if (!n) { set_error("null argument"); return OMQ_BAD_ARG; }
+  if (conv_w) *conv_w = (uint64_t)n->C * 9 * kInPad + (uint64_t)2 * n->NB * n->C * 9 * n->C;
+  if (conv_b) *conv_b = (uint64_t)(1 + 2 * n->NB) * n->C;
+  if (head) *head = head_floats(n);
+  return OMQ_OK;
+}
+
+int omq_resnet_load(omq_resnet* n, const uint16_t* d_conv_w, const float* d_conv_b,
+                    const float* d_head, void* stream) {
+  if (!n || !d_conv_w || !d_conv_b || !d_head) { set_error("null argument"); return OMQ_BAD_ARG; }
+  DeviceGuard g(n->cfg.device);
+  uint64_t a, b, h;
+  omq_resnet_param_sizes(n, &a, &b, &h);
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemcpyAsync(n->conv_w, d_conv_w, a * 2, cudaMemcpyDeviceToDevice, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(n->conv_b, d_conv_b, b * 4, cudaMemcpyDeviceToDevice, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(n->head, d_head, h * 4, cudaMemcpyDeviceToDevice, s);
+  if (e != cudaSuccess) return cuda_status(e, "omq_resnet_load");
+  n->loaded = 1;
+  return OMQ_OK;
+}
+
+int omq_resnet_memory(const omq_resnet* n, uint64_t* bytes) {
+  if (!n || !bytes) { set_error("null argument"); return OMQ_BAD_ARG; }
+  *bytes = n->bytes;
+  return OMQ_OK;
+}
+
+}  // extern "C"
+
+namespace omq {
+
+template <int BN>
+static int launch_conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB,
+                       const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
+                       int kb_per_tap, const int32_t* d_count, int count, cudaStream_t s) {
+  using Cfg = ConvCfg<BN>;
+  static int attr_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (attr_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(k_conv3x3<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::kSmem);
+    if (e != cudaSuccess) return cuda_status(e, "conv smem attribute");
+    attr_dev = dev;
+  }
+  ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
+  const int max_tiles = (int)((n->rows + kTileM - 1) / kTileM);
+  const int grid = max(1, min(max_tiles, n->sm_count));
+  k_conv3x3<BN><<<grid, kConvThreads, Cfg::kSmem, s>>>(tA, tB, a);
+  return cuda_status(cudaGetLastError(), "k_conv3x3");
+}
+
+static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB, const float* bias,
+                const __nv_bfloat16* res, __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count,
+                int count, cudaStream_t s) {
+  if (n->C == 128) return launch_conv<128>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
+  return launch_conv<256>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
+}
+
+// trunk + heads on n->x_in (already packed), count from d_count (device) or `count`.
+int resnet_run(omq_resnet* n, const int32_t* d_count, int count, float* policy, float* value,
+               cudaStream_t s) {
+  if (!n->loaded) { set_error("omq_resnet_load was not called"); return OMQ_NOT_READY; }
+  int st = conv(n, n->tmA_in, n->tmB_in, n->conv_b, nullptr, n->act[0], 1, d_count, count, s);
+  int x = 0;
+  for (int i = 0; st == OMQ_OK && i < n->NB; ++i) {
+    const int t = (x + 1) % 3, y = (x + 2) % 3;
+    st = conv(n, n->tmA[x], n->tmB[2 * i], n->conv_b + (size_t)(1 + 2 * i) * n->C, nullptr,
+              n->act[t], n->C / kBlockK, d_count, count, s);
+    if (st) break;
+    st = conv(n, n->tmA[t], n->tmB[2 * i + 1], n->conv_b + (size_t)(2 + 2 * i) * n->C, n->act[x],
+              n->act[y], n->C / kBlockK, d_count, count, s);
+    x = y;
+  }
+  if (st) return st;
+  HeadArgs h{};
+  h.act = n->act[x];
+  h.C = n->C; h.S = n->S; h.P = n->P; h.A = n->A; h.Hp = n->Hp; h.Hv = n->Hv;
+  const float* p = n->head;
+  h.w1x1 = p; p += 3 * n->C;
+  h.b1x1 = p; p += 3;
+  h.fc1p = p; p += (size_t)2 * n->HW * n->Hp;
+  h.b1p = p; p += n->Hp;
+  h.fc2p = p; p += (size_t)n->Hp * n->A;
+  h.b2p = p; p += n->A;
+  h.fc1v = p; p += (size_t)n->HW * n->Hv;
+  h.b1v = p; p += n->Hv;
+  h.fc2v = p; p += n->Hv;
+  h.b2v = p;
+  h.d_count = d_count;
+  h.count = count;
+  h.policy = policy;
+  h.value = value;
+  const size_t sm = head_smem(n);
+  if (sm > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_heads, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) return cuda_status(e, "heads smem attribute");
+  }
+  const int blocks = (count + kHeadPos - 1) / kHeadPos;
+  k_heads<<<blocks, kHeadThreads, sm, s>>>(h);
+  return cuda_status(cudaGetLastError(), "k_heads");
+}
+
+}  // namespace omq
+
+extern "C" {
+
+int omq_resnet_forward_features(omq_resnet* n, const float* d_features, int32_t batch,
+                                float* d_policy, float* d_value, void* stream) {
+  if (!n || !d_features || !d_policy || !d_value) { set_error("null argument"); return OMQ_BAD_ARG; }
+  if (batch < 0 || batch > n->max_batch) {
+    set_error("batch %d outside [0, %d]", batch, n->max_batch);
+    return OMQ_BAD_ARG;
+  }
+  if (batch == 0) return OMQ_OK;
+  DeviceGuard g(n->cfg.device);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int total = batch * n->P * 8;
+  k_pack_features<<<min((total + 255) / 256, 8192), 256, 0, s>>>(
+      d_features, n->cfg.input_channels, n->S, n->P, nullptr, batch, n->x_in);
+  int st = cuda_status(cudaGetLastError(), "k_pack_features");
+  if (st) return st;
+  return resnet_run(n, nullptr, batch, d_policy, d_value, s);
+}
+
+int omq_resnet_forward_packed(omq_resnet* n, const uint16_t* d_input, const int32_t* d_count,
+                              int32_t batch, float* d_policy, float* d_value, void* stream) {
+  if (!n || !d_policy || !d_value) { set_error("null argument"); return OMQ_BAD_ARG; }
+  if (batch < 0 || batch > n->max_batch) { set_error("batch outside capacity"); return OMQ_BAD_ARG; }
+  DeviceGuard g(n->cfg.device);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (d_input && d_input != reinterpret_cast<const uint16_t*>(n->x_in)) {
+    cudaError_t e = cudaMemcpyAsync(n->x_in, d_input, (size_t)batch * n->P * kInPad * 2,
+                                    cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return cuda_status(e, "omq_resnet_forward_packed copy");
+  }
+  return resnet_run(n, d_count, batch, d_policy, d_value, s);
+}
+
+int omq_resnet_input_buffer(omq_resnet* n, uint16_t** d_input) {
+  if (!n || !d_input) { set_error("null argument"); return OMQ_BAD_ARG; }
+  *d_input = reinterpret_cast<uint16_t*>(n->x_in);
+  return OMQ_OK;
+}
+
+int omq_resnet_forward_queue(omq_resnet* n, omq_engine* e, int32_t queue, void* stream) {
+  if (!n || !e || queue < 0 || queue > 1) { set_error("bad argument"); return OMQ_BAD_ARG; }
+  const int cap = e->v.R * e->v.WCAP;
+  if (n->max_batch < cap) {
+    set_error("resnet max_batch %d < engine queue capacity %d", n->max_batch, cap);
+    return OMQ_BAD_ARG;
+  }
+  if (n->S != e->v.S || n->A != e->v.A) { set_error("resnet / engine board mismatch"); return OMQ_BAD_ARG; }
+  DeviceGuard g(n->cfg.device);
+  cudaStream_t s = (cudaStream_t)stream;
+  launch_pack_queue(e->v, queue, n->P, n->x_in, s);
+  int st = cuda_status(cudaGetLastError(), "pack queue");
+  if (st) return st;
+  return resnet_run(n, e->v.q_count + queue, cap, e->v.q_policy[queue], e->v.q_value[queue], s);
+}
+
+int omq_resnet_error(omq_resnet* n, int32_t* h_error, void* stream) {
+  if (!n || !h_error) { set_error("null argument"); return OMQ_BAD_ARG; }
+  DeviceGuard g(n->cfg.device);
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemcpyAsync(h_error, n->error, 4, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  return cuda_status(e, "omq_resnet_error");
+}
+
+}  // extern "C"

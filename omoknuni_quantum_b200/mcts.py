@@ -1,0 +1,198 @@
+"""MCTS - drop-in for the reference's ``MCTS(config, evaluator, game_interface).search()``.
+
+Same constructor, methods and return types as python/mcts/core/mcts.py (``search`` 924,
+``select_action`` 1167, ``update_root`` 1205, ``get_root_value`` 1139, ``clear`` 1387,
+``get_statistics`` 1429), with the whole search on the device: one ``WaveEngine`` holds the
+tree(s), every wave runs as select -> evaluate leaf queue -> expand + pick -> evaluate final
+queue -> backup without a host round trip (except for host-protocol evaluators, which receive the
+queue's feature tensor).
+
+Results equal the reference's deterministic CPU path (``backend='gpu', device='cpu',
+wave_async_expansion=False``) for the same evaluator outputs: visit counts, tree layout and the
+root policy bit for bit.
+
+Evaluators:
+  * ``SyntheticEvaluator()`` - built-in integer-exact synthetic evaluator (device kernel);
+  * ``ResNetEvaluator`` of this package - tcgen05 bf16 ResNet reading the leaf queue in place;
+  * a ``torch.nn.Module`` with the reference ResNetModel layout (e.g. ``single_gpu_mode=True``
+    with a model, mcts.py:113-122) - its weights are folded and packed into a ResNetEvaluator;
+  * any object with the reference protocol ``evaluate_batch(features) -> (policy, value)``.
+"""
+from __future__ import annotations
+
+import time
+from typing import Any, Dict, Optional
+
+import numpy as np
+import torch
+
+from .engine import WaveEngine
+from .mcts_config import GameType, MCTSConfig
+
+
+class SyntheticEvaluator:
+    """Marker for the built-in device synthetic evaluator (policy ~ softmax of N(0,1) logits
+    seeded by a 64-bit hash of the feature planes, masked to legal moves; value = tanh of a
+    hash-seeded N(0, 0.5) draw; integer-exact, see eval_kernels.cu)."""
+
+    builtin = "synthetic"
+
+    def evaluate_batch(self, features):  # pragma: no cover - device-only
+        raise NotImplementedError("SyntheticEvaluator runs inside the device engine")
+
+
+def _resolve_evaluator(evaluator):
+    if isinstance(evaluator, SyntheticEvaluator) or evaluator == "synthetic":
+        return "synthetic"
+    if isinstance(evaluator, torch.nn.Module) and hasattr(evaluator, "residual_blocks"):
+        from .resnet import ResNetEvaluator
+        return ResNetEvaluator.from_module(evaluator)
+    return evaluator
+
+
+class MCTS:
+    def __init__(self, config: MCTSConfig, evaluator: Any, game_interface: Any = None,
+                 single_gpu_mode: bool = False):
+        self.config = config
+        self.game_interface = game_interface
+        self.single_gpu_mode = single_gpu_mode
+        if config.game_type != GameType.GOMOKU:
+            raise NotImplementedError(
+                f"device rules exist for Gomoku only; got {GameType(config.game_type).name}")
+        self.evaluator = evaluator
+        self._eval = _resolve_evaluator(evaluator)
+        if hasattr(evaluator, "_return_torch_tensors"):
+            evaluator._return_torch_tensors = True          # mcts.py:120-121
+        dev = config.device if config.device != "cpu" else "cuda"
+        self.device = torch.device(dev)
+        if self.device.type == "cuda" and self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self._engines: Dict[int, WaveEngine] = {}
+        self._last_tree = None          # (engine, index) of the last single search
+        self._root_state = None
+        self.stats = dict(total_searches=0, total_simulations=0, total_time=0.0,
+                          last_search_sims_per_second=0.0, peak_sims_per_second=0.0,
+                          avg_sims_per_second=0.0)
+
+    # -- engines -------------------------------------------------------------------------------
+    @property
+    def action_size(self) -> int:
+        return self.config.board_size ** 2
+
+    def _engine(self, num_trees: int) -> WaveEngine:
+        eng = self._engines.get(num_trees)
+        if eng is None:
+            c = self.config
+            eng = WaveEngine(num_trees, board_size=c.board_size, capacity=c.tree_capacity,
+                             max_wave_size=c.max_wave_size, c_puct=c.c_puct,
+                             virtual_loss=c.virtual_loss, enable_virtual_loss=c.enable_virtual_loss,
+                             max_depth=c.max_depth, device=self.device)
+            self._engines[num_trees] = eng
+        return eng
+
+    def _boards(self, state) -> np.ndarray:
+        n = self.config.board_size
+        if torch.is_tensor(state):
+            state = state.cpu().numpy()
+        if isinstance(state, np.ndarray):
+            if state.shape[-2:] != (n, n):
+                raise ValueError(f"Invalid state shape: {state.shape}, expected {(n, n)}")
+            return state.astype(np.int8, copy=False)
+        raise TypeError("state must be a numpy/torch board [n, n] with 0 empty, 1 black, 2 white")
+
+    # -- search --------------------------------------------------------------------------------
+    def search(self, state: Any, num_simulations: Optional[int] = None) -> np.ndarray:
+        """Policy (fp64 [board_size**2]) = root-child visit share (mcts.py:924-979)."""
+        board = self._boards(state)
+        pol = self.search_batch(board[None], num_simulations)[0]
+        self._root_state = board
+        return pol
+
+    def search_batch(self, states, num_simulations: Optional[int] = None) -> np.ndarray:
+        """Independent searches of several roots in lockstep on the device; policies [R, A]."""
+        boards = self._boards(states)
+        if boards.ndim == 2:
+            boards = boards[None]
+        sims = int(num_simulations or self.config.num_simulations)
+        R = boards.shape[0]
+        if sims == 0:                                        # mcts.py:1023-1031
+            return np.full((R, self.action_size), 1.0 / self.action_size)
+        eng = self._engine(R)
+        t0 = time.perf_counter()
+        eng.search(torch.from_numpy(np.ascontiguousarray(boards)).to(self.device), sims, self._eval)
+        visits = eng.root_visits().cpu().numpy()
+        dt = time.perf_counter() - t0
+        self._last_tree = (eng, 0)
+        self._update_statistics(sims * R, dt)
+        return self._policies(visits, eng)
+
+    def _policies(self, visits: np.ndarray, eng: WaveEngine) -> np.ndarray:
+        out = WaveEngine.policy_from_visits(visits)
+        # a root without children yields the uniform policy (mcts.py:1081-1087)
+        return out
+
+    # -- reference API -------------------------------------------------------------------------
+    def get_root_value(self) -> float:
+        if self._last_tree is None:
+            return 0.0
+        eng, r = self._last_tree
+        n, w = eng.root_nw()[r].tolist()
+        return 0.0 if n == 0 else w / n
+
+    def select_action(self, state: Any, temperature: float = 1.0,
+                      policy: Optional[np.ndarray] = None) -> int:
+        """mcts.py:1167-1203."""
+        if policy is None:
+            policy = self.search(state)
+        if temperature == 0:
+            return int(np.argmax(policy)) if policy.max() > 0 else 0
+        p = np.power(policy, 1.0 / temperature)
+        p /= p.sum()
+        return int(np.random.choice(len(policy), p=p))
+
+    def update_root(self, action: int, new_state: Any = None) -> None:
+        """mcts.py:1205-1246. Subtree reuse is not implemented: the next search starts a fresh
+        tree from ``new_state`` (the reference's fallback path, mcts.py:1242-1246)."""
+        if action < 0 or action >= self.action_size:
+            raise ValueError(f"Invalid action {action}. Must be in range [0, {self.action_size})")
+        self._last_tree = None
+        if new_state is not None:
+            self._root_state = self._boards(new_state)
+
+    def clear(self) -> None:
+        self._last_tree = None
+        self._root_state = None
+
+    def reset_tree(self) -> None:
+        self.clear()
+
+    def get_statistics(self) -> Dict[str, Any]:
+        s = dict(self.stats)
+        if self._last_tree is not None:
+            eng, r = self._last_tree
+            s["tree_nodes"] = int(eng.num_nodes()[r])
+            s["tree_capacity"] = eng.capacity
+        s["device_memory_bytes"] = sum(e.memory_bytes() for e in self._engines.values())
+        return s
+
+    def _update_statistics(self, sims: int, dt: float) -> None:   # mcts.py:1442-1456
+        st = self.stats
+        st["total_searches"] += 1
+        st["total_simulations"] += sims
+        st["total_time"] += dt
+        rate = sims / dt if dt > 0 else 0.0
+        st["last_search_sims_per_second"] = rate
+        st["peak_sims_per_second"] = max(st["peak_sims_per_second"], rate)
+        st["avg_sims_per_second"] = st["total_simulations"] / st["total_time"] if st["total_time"] else 0.0
+
+    def shutdown(self) -> None:
+        for e in self._engines.values():
+            e.close()
+        self._engines.clear()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.shutdown()
+        return False

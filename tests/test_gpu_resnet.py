@@ -1,0 +1,81 @@
+"""ResNet on the B200: tcgen05 bf16 kernels against the fp32 restatement of the reference model
+(tolerance 2e-2 absolute on policy probabilities and values), batch invariance, and the
+device leaf-queue path against the host protocol path."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+
+
+def _features(n, seed=0):
+    """Reference-layout features of random legal-looking positions: occupancy, player plane,
+    last move."""
+    g = np.random.default_rng(seed)
+    f = np.zeros((n, 19, 15, 15), np.float32)
+    for i in range(n):
+        occ = g.random((15, 15)) < g.uniform(0.05, 0.5)
+        f[i, 0] = occ
+        f[i, 1] = g.integers(1, 3)
+        ys, xs = np.nonzero(occ)
+        if len(ys):
+            j = g.integers(len(ys))
+            f[i, 2, ys[j], xs[j]] = 1
+    return torch.from_numpy(f)
+
+
+@pytest.mark.parametrize("blocks,filters,hv", [(10, 128, 128), (2, 256, 256)])
+def test_forward_matches_fp32_reference(blocks, filters, hv):
+    from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec, init_state_dict, reference_forward_fp32
+    spec = ResNetSpec(num_blocks=blocks, filters=filters, fc_value_hidden=hv)
+    sd = init_state_dict(spec, seed=7)
+    ev = ResNetEvaluator(sd, max_batch=512)
+    x = _features(333, seed=blocks)
+    p, v = ev.evaluate_batch(x.cuda())
+    torch.cuda.synchronize()
+    assert ev.error() == 0
+    sd_gpu = {k: t.cuda() for k, t in sd.items()}
+    pr, vr = reference_forward_fp32(sd_gpu, x.cuda())
+    dp = (p - pr).abs().max().item()
+    dv = (v - vr).abs().max().item()
+    assert torch.isfinite(p).all() and torch.isfinite(v).all()
+    assert dp < TOL and dv < TOL, (dp, dv)
+    # the policy is a distribution
+    assert torch.allclose(p.sum(1), torch.ones_like(p[:, 0]), atol=1e-4)
+
+
+def test_forward_is_batch_invariant():
+    from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec
+    ev = ResNetEvaluator.random(ResNetSpec(num_blocks=3, filters=128), seed=3, max_batch=512)
+    x = _features(257, seed=5).cuda()
+    p1, v1 = ev.evaluate_batch(x)
+    perm = torch.randperm(257, generator=torch.Generator().manual_seed(0)).cuda()
+    p2, v2 = ev.evaluate_batch(x[perm])
+    assert torch.equal(p1[perm], p2) and torch.equal(v1[perm], v2)
+    p3, v3 = ev.evaluate_batch(x[:5])
+    assert torch.equal(p1[:5], p3) and torch.equal(v1[:5], v3)
+
+
+def test_queue_path_equals_protocol_path():
+    """forward_queue (device packing from the tree) == evaluate_batch on the engine's reference
+    feature tensor: identical trees."""
+    from omoknuni_quantum_b200.engine import WaveEngine
+    from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec
+    from omoknuni_quantum_b200.roots import random_roots
+    ev = ResNetEvaluator.random(ResNetSpec(num_blocks=2, filters=128), seed=1, max_batch=1024)
+
+    class Protocol:
+        def evaluate_batch(self, f):
+            return ev.evaluate_batch(f)
+
+    roots = torch.from_numpy(random_roots(4, 3)).cuda()
+    e1 = WaveEngine(3, capacity=60000, max_wave_size=64)
+    e1.search(roots, 192, evaluator=ev)
+    e2 = WaveEngine(3, capacity=60000, max_wave_size=64)
+    e2.search(roots, 192, evaluator=Protocol())
+    for r in range(3):
+        a, b = e1.export_tree(r), e2.export_tree(r)
+        for k in a:
+            assert np.array_equal(a[k], b[k]), (r, k)
