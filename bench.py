@@ -1,0 +1,371 @@
+#!/usr/bin/env python
+"""Benchmark of the wave-MCTS hot path: MCTS simulations/s on B200 (device-timed, whole box).
+
+Workload (one GPU): Gomoku 15x15 single-tree searches, 1600 simulations per
+root, max_wave_size 256, c_puct 1.4, virtual loss 1.0, ResNet evaluator 10 blocks x 128 filters
+(value head FC 225 -> 128 -> 1), bf16 weights/activations with fp32 accumulation, seeded He-init
+weights. Roots: 20 stones placed uniformly at random, colours alternating, from a seed. Each GPU
+searches `--roots` independent roots in lockstep (the on-device leaf queue batches their leaves
+into one ResNet call per phase); one step = one complete search of every root. Multi-GPU: one
+process per GPU, roots sharded (weak scaling), weights broadcast once over NCCL, no per-wave
+collective.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Prints one JSON line (rank 0). `--impl reference` times the reference algorithm's CPU path on the
+host cores (the C++ restatement in oracle/ of the reference's torch WaveSearch, with the ResNet
+forward in fp32 torch on the CPU) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "MCTS simulations/sec (device-timed, whole box)"
+UNIT = "simulations/s"
+WORKLOAD = ("config1: Gomoku 15x15 single-tree searches, 1600 sims/root, wave 256, c_puct 1.4, "
+            "VL 1.0, ResNet 10x128 bf16 evaluator; independent roots searched in lockstep per GPU")
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--roots", type=int, default=256, help="roots per GPU searched in lockstep")
+    ap.add_argument("--sims", type=int, default=1600)
+    ap.add_argument("--wave", type=int, default=256)
+    ap.add_argument("--capacity", type=int, default=400000, help="tree nodes per root")
+    ap.add_argument("--blocks", type=int, default=10)
+    ap.add_argument("--filters", type=int, default=128)
+    ap.add_argument("--value-hidden", type=int, default=128)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-seconds", type=float, default=20.0, help="CPU baseline sample budget")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------------------------
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def profile_value(name: str, key: str):
+    """A number recorded in a committed ncu summary under profiles/ ('key: value' line)."""
+    path = os.path.join(REPO, "profiles", name)
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        for line in f:
+            line = line.strip().lstrip("-* ")
+            if line.startswith(key + ":"):
+                try:
+                    return float(line.split(":", 1)[1].split()[0].replace(",", ""))
+                except ValueError:
+                    return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        with open(self.file.name) as f:
+            rows = [r.strip().split(", ") for r in f if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.strip() == "Active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        busy = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(busy), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_spec(args):
+    from omoknuni_quantum_b200.resnet import ResNetSpec
+    return ResNetSpec(board_size=15, input_channels=19, num_blocks=args.blocks, filters=args.filters,
+                      num_actions=225, fc_policy_hidden=256, fc_value_hidden=args.value_hidden)
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU arms
+# ---------------------------------------------------------------------------------------------
+def cpu_search_rate(args, sd, budget_s: float):
+    """Reference algorithm on the host: oracle tree search (C++ restatement of the reference's
+    torch WaveSearch) + fp32 torch ResNet forward on all host cores. Searches seeded roots of
+    the workload until `budget_s` of work is done; returns (sims/s, sims, seconds, threads)."""
+    from oracle import pyoracle
+    from omoknuni_quantum_b200.resnet import reference_forward_fp32
+    from omoknuni_quantum_b200.roots import random_root
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sd32 = {k: v.float() for k, v in sd.items()}
+
+    def ev(f):
+        with torch.no_grad():
+            p, v = reference_forward_fp32(sd32, torch.from_numpy(f))
+        return p.numpy(), v.numpy()
+
+    sims_done, t0 = 0, time.perf_counter()
+    r = 0
+    while True:
+        o = pyoracle.Oracle(args.capacity)
+        cfg = o.config(args.sims, args.wave)
+        if o.begin(random_root(args.seed * 7919 + r), cfg, evaluator=ev) != 0:
+            raise RuntimeError("oracle begin failed")
+        done = 0
+        while done < args.sims:
+            w = min(args.wave, args.sims - done)
+            if o.wave(w) != 0:
+                raise RuntimeError("oracle wave failed")
+            done += w
+            sims_done += w
+            if time.perf_counter() - t0 > budget_s:
+                break
+        r += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return sims_done / dt, sims_done, dt, threads
+
+
+def run_reference_arm(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    from omoknuni_quantum_b200.resnet import init_state_dict
+    sd = init_state_dict(make_spec(args), seed=args.seed)
+    budget = max(2.0, args.cpu_seconds / max(1, args.steps))
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_search_rate(args, sd, 1.0)
+    rates, sims_total, secs_total = [], 0, 0.0
+    threads = 1
+    for _ in range(args.steps):
+        rate, sims, secs, threads = cpu_search_rate(args, sd, budget)
+        rates.append(rate)
+        sims_total += sims
+        secs_total += secs
+    value = sims_total / secs_total
+    sample = (f"{sims_total} simulations of config-1 searches (seeded roots, 1600 sims each, "
+              f"wave 256) in {secs_total:.1f} s, fp32 CPU ResNet 10x128")
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * secs_total / max(1, args.steps),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded roots, seeded He-init weights)", "impl": "reference",
+            "config": {"workload": WORKLOAD, "sims": args.sims, "wave": args.wave,
+                       "model": f"resnet{args.blocks}x{args.filters}", "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------------------------
+def run_b200(args):
+    ws, rank, local = dist_env()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py --impl b200 needs a CUDA device")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    from omoknuni_quantum_b200 import _lib, parallel
+    from omoknuni_quantum_b200.engine import WaveEngine
+    from omoknuni_quantum_b200.mcts import MCTS
+    from omoknuni_quantum_b200.mcts_config import MCTSConfig
+    from omoknuni_quantum_b200.resnet import ResNetEvaluator, init_state_dict
+    from omoknuni_quantum_b200.roots import random_roots
+
+    spec = make_spec(args)
+    # weights: rank 0's seeded weights, broadcast once over NCCL (the only data collective)
+    sd = parallel.broadcast_state_dict(init_state_dict(spec, seed=args.seed), dev)
+    R = args.roots
+    ev = ResNetEvaluator(sd, board_size=15, max_batch=R * args.wave, device=dev)
+    roots = torch.from_numpy(random_roots(args.seed * 1000 + rank, R)).to(dev)
+    eng = WaveEngine(R, board_size=15, capacity=args.capacity, max_wave_size=args.wave, c_puct=1.4,
+                     virtual_loss=1.0, device=dev)
+
+    def barrier():
+        if ws > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        eng.search(roots, args.sims, evaluator=ev)
+    barrier()
+    ev.profile(1 << 14)
+    launches0 = _lib.kernel_launches()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        start.record()
+        for _ in range(args.steps):
+            eng.search(roots, args.sims, evaluator=ev)
+        end.record()
+        barrier()
+    launches = _lib.kernel_launches() - launches0
+    ms = start.elapsed_time(end)
+    trunk_ms, counts = ev.profile_read()
+    ev.profile(0)
+    ms_max = parallel.max_over_ranks(ms, dev)
+    total_sims = args.sims * R * args.steps * ws
+    value = total_sims / (ms_max / 1000.0)
+    positions = int(parallel.sum_over_ranks(int(counts.sum()), dev)) // ws  # per-rank mean
+    nodes = int(eng.num_nodes().max())
+
+    # roofline of the dominant kernel (the tcgen05 conv): algorithmic FLOPs per launch / avg launch
+    peaks, peak_kind = measured_peaks()
+    conv_launches = len(trunk_ms) * ev.conv_launches_per_call
+    flops = positions * ev.trunk_flops_per_position()
+    avg_launch_s = float(trunk_ms.sum()) / 1000.0 / max(1, conv_launches)
+    achieved = (flops / max(1, conv_launches)) / avg_launch_s / 1e12 if avg_launch_s > 0 else 0.0
+    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    traffic_per_pos = profile_value("conv3x3_resnet10x128.md", "dram_bytes_per_position_per_launch")
+    traffic = None
+    if traffic_per_pos is not None and conv_launches:
+        traffic = traffic_per_pos * positions / len(trunk_ms)
+    roofline = {"kernel": "k_conv3x3<128> (tcgen05 implicit-GEMM 3x3 conv)", "bound": "tensor",
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_kind": f"bf16_tflops_sustained of {peak_kind}", "traffic": traffic,
+                "algorithmic_flops_per_launch": flops / max(1, conv_launches),
+                "avg_launch_ms": avg_launch_s * 1e3, "launches": conv_launches}
+
+    # end to end through the public API: host boards (pinned) in, host policies out
+    e2e = None
+    if not args.no_e2e:
+        cfg = MCTSConfig(num_simulations=args.sims, max_wave_size=args.wave, c_puct=1.4,
+                         virtual_loss=1.0, initial_tree_nodes=args.capacity, device=str(dev),
+                         enable_subtree_reuse=False, dirichlet_epsilon=0.0)
+        mcts = MCTS(cfg, ev)
+        mcts._engines[R] = eng
+        host_boards = roots.cpu().pin_memory()
+        mcts.search_batch(host_boards)
+        barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(args.steps):
+            pol = mcts.search_batch(host_boards)
+        e2.record()
+        barrier()
+        ms2 = parallel.max_over_ranks(s2.elapsed_time(e2), dev)
+        assert pol.shape == (R, 225) and np.allclose(pol.sum(1), 1.0)
+        e2e = {"value": total_sims / (ms2 / 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": R * 225, "d2h_bytes_per_step": R * 225 * 4,
+               "api": "MCTS(config, ResNetEvaluator).search_batch(pinned host boards) -> numpy policies"}
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        rate, sims, secs, threads = cpu_search_rate(args, sd, args.cpu_seconds)
+        cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{sims} simulations of config-1 searches in {secs:.1f} s (oracle C++ tree "
+                         f"+ fp32 torch CPU ResNet 10x128)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded roots, seeded He-init weights)",
+            "config": {"workload": WORKLOAD, "roots_per_gpu": R, "global_batch": R * ws,
+                       "sims": args.sims, "wave": args.wave, "capacity": args.capacity,
+                       "model": f"resnet{args.blocks}x{args.filters} (value fc {args.value_hidden})",
+                       "parallelism": f"dp{ws} (independent trees per GPU, weights NCCL-broadcast once)",
+                       "l2": "inputs larger than L2 (multi-GB activations per ResNet call)"},
+            "leaf_evals_per_s": positions * ws / (ms_max / 1000.0),
+            "max_tree_nodes": nodes,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
+            "gpu_launches": launches,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -66,6 +66,8 @@ typedef struct {
 
 OMQ_API const char* omq_status_string(int status);
 OMQ_API const char* omq_last_error(void); /* thread-local detail for the last non-OK status */
+/* Number of kernels this library has launched in the calling process so far. */
+OMQ_API int omq_kernel_launches(uint64_t* h_count);
 
 /* Allocates all device memory of the engine (trees + per-wave scratch + queues).
  * Replaces CSRTree(CSRTreeConfig) (csr_tree.py:86) and WaveSearch.allocate_buffers (:414). */
@@ -185,6 +187,12 @@ OMQ_API int omq_resnet_input_buffer(omq_resnet* net, uint16_t** d_input);
  * the queue's policy/value buffers are written; no host synchronisation. */
 OMQ_API int omq_resnet_forward_queue(omq_resnet* net, omq_engine* engine, int32_t queue,
                                      void* stream);
+/* Record CUDA events around the convolution trunk of the next `capacity` forward calls
+ * (0 disables; re-arming resets). omq_resnet_profile_read synchronizes on the last event and
+ * returns, per call, the trunk's device time in ms and the number of positions evaluated. */
+OMQ_API int omq_resnet_profile(omq_resnet* net, int32_t capacity);
+OMQ_API int omq_resnet_profile_read(omq_resnet* net, int32_t* h_calls, float* h_trunk_ms,
+                                    int32_t* h_counts, int32_t max);
 /* Device error word of the net (OMQ_TIMEOUT after a bounded wait gave up); synchronizes. */
 OMQ_API int omq_resnet_error(omq_resnet* net, int32_t* h_error, void* stream);
 

@@ -85,6 +85,9 @@ SIGNATURES = {
     "omq_resnet_input_buffer": [_P, ctypes.POINTER(_P)],
     "omq_resnet_forward_queue": [_P, _P, _I, _P],
     "omq_resnet_error": [_P, ctypes.POINTER(_I), _P],
+    "omq_resnet_profile": [_P, _I],
+    "omq_resnet_profile_read": [_P, ctypes.POINTER(_I), _P, _P, _I],
+    "omq_kernel_launches": [ctypes.POINTER(ctypes.c_uint64)],
 }
 _RESTYPES = {"omq_status_string": ctypes.c_char_p, "omq_last_error": ctypes.c_char_p}
 
@@ -113,6 +116,13 @@ def load(build_if_missing: bool = True):
         fn.restype = _RESTYPES.get(name, ctypes.c_int)
     _lib = L
     return L
+
+
+def kernel_launches() -> int:
+    """Kernels launched by libomq_b200.so in this process so far."""
+    n = ctypes.c_uint64()
+    check(load().omq_kernel_launches(ctypes.byref(n)), "omq_kernel_launches")
+    return int(n.value)
 
 
 def check(status: int, what: str = "") -> None:

@@ -1,4 +1,5 @@
 // C ABI of the wave-MCTS engine (declarations and reference map in include/omq_b200.h).
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -22,6 +23,10 @@ int cuda_status(cudaError_t e, const char* what) {
   set_error("%s: %s", what, cudaGetErrorString(e));
   return OMQ_CUDA_ERROR;
 }
+
+static std::atomic<unsigned long long> g_launches{0};
+
+void count_launches(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
@@ -51,6 +56,12 @@ const char* omq_status_string(int s) {
 }
 
 const char* omq_last_error(void) { return g_err; }
+
+int omq_kernel_launches(uint64_t* h_count) {
+  if (!h_count) { set_error("null argument"); return OMQ_BAD_ARG; }
+  *h_count = g_launches.load();
+  return OMQ_OK;
+}
 
 int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   if (!cfg || !out) { set_error("null argument"); return OMQ_BAD_ARG; }

@@ -219,17 +219,20 @@ __global__ void __launch_bounds__(kSynthWarps * 32) k_pack_queue(EngineView v, i
 
 void launch_pack_queue(const EngineView& v, int queue, int P, void* out, cudaStream_t s) {
   const int cap = v.R * v.WCAP;
+  count_launches(1);
   k_pack_queue<<<(cap + kSynthWarps - 1) / kSynthWarps, kSynthWarps * 32, 0, s>>>(
       v, queue, P, reinterpret_cast<uint4*>(out));
 }
 
 void launch_synth_eval(const EngineView& v, int queue, cudaStream_t s) {
   const int cap = v.R * v.WCAP;
+  count_launches(1);
   k_synth<<<(cap + kSynthWarps - 1) / kSynthWarps, kSynthWarps * 32, 0, s>>>(v, queue);
 }
 
 void launch_features(const EngineView& v, int queue, float* out, cudaStream_t s) {
   const int cap = v.R * v.WCAP;
+  count_launches(1);
   k_features<<<(cap + kSynthWarps - 1) / kSynthWarps, kSynthWarps * 32, 0, s>>>(v, queue, out);
 }
 

@@ -170,6 +170,8 @@ struct DeviceGuard {
 };
 
 void set_error(const char* fmt, ...);
+// Process-wide count of kernels this library has launched (reported by omq_kernel_launches).
+void count_launches(int n);
 int cuda_status(cudaError_t e, const char* what);
 
 void launch_begin(const EngineView& v, const int8_t* boards, cudaStream_t s);

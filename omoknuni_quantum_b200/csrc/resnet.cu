@@ -410,6 +410,11 @@ struct omq_resnet {
   CUtensorMap tmA_in, tmA[3], tmB_in;
   CUtensorMap* tmB;        // [2*NB]
   int loaded;
+  // optional timing of the conv trunk of each forward call (CUDA events on the caller's stream)
+  int prof_cap, prof_n;
+  cudaEvent_t* prof_ev;    // [2 * prof_cap]
+  int32_t* prof_counts;    // device [prof_cap]: positions evaluated by each call
+  int32_t* prof_host_counts;
 };
 
 static PFN_encodeTiled_t get_encode() {
@@ -519,9 +524,21 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
   return OMQ_OK;
 }
 
+static void prof_free(omq_resnet* n) {
+  for (int i = 0; i < 2 * n->prof_cap; ++i) cudaEventDestroy(n->prof_ev[i]);
+  delete[] n->prof_ev;
+  delete[] n->prof_host_counts;
+  if (n->prof_counts) cudaFree(n->prof_counts);
+  n->prof_ev = nullptr;
+  n->prof_host_counts = nullptr;
+  n->prof_counts = nullptr;
+  n->prof_cap = n->prof_n = 0;
+}
+
 int omq_resnet_destroy(omq_resnet* n) {
   if (!n) return OMQ_OK;
   DeviceGuard g(n->cfg.device);
+  prof_free(n);
   cudaError_t e = cudaFree(n->arena);
   delete[] n->tmB;
   delete n;
@@ -578,6 +595,7 @@ static int launch_conv(const omq_resnet* n, const CUtensorMap& tA, const CUtenso
   ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
   const int max_tiles = (int)((n->rows + kTileM - 1) / kTileM);
   const int grid = max(1, min(max_tiles, n->sm_count));
+  count_launches(1);
   k_conv3x3<BN><<<grid, kConvThreads, Cfg::kSmem, s>>>(tA, tB, a);
   return cuda_status(cudaGetLastError(), "k_conv3x3");
 }
@@ -593,6 +611,14 @@ static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& t
 int resnet_run(omq_resnet* n, const int32_t* d_count, int count, float* policy, float* value,
                cudaStream_t s) {
   if (!n->loaded) { set_error("omq_resnet_load was not called"); return OMQ_NOT_READY; }
+  const int pi = (n->prof_cap > 0 && n->prof_n < n->prof_cap) ? n->prof_n++ : -1;
+  if (pi >= 0) {
+    if (d_count)
+      cudaMemcpyAsync(n->prof_counts + pi, d_count, 4, cudaMemcpyDeviceToDevice, s);
+    else
+      n->prof_host_counts[pi] = count;
+    cudaEventRecord(n->prof_ev[2 * pi], s);
+  }
   int st = conv(n, n->tmA_in, n->tmB_in, n->conv_b, nullptr, n->act[0], 1, d_count, count, s);
   int x = 0;
   for (int i = 0; st == OMQ_OK && i < n->NB; ++i) {
@@ -605,6 +631,7 @@ int resnet_run(omq_resnet* n, const int32_t* d_count, int count, float* policy, 
     x = y;
   }
   if (st) return st;
+  if (pi >= 0) cudaEventRecord(n->prof_ev[2 * pi + 1], s);
   HeadArgs h{};
   h.act = n->act[x];
   h.C = n->C; h.S = n->S; h.P = n->P; h.A = n->A; h.Hp = n->Hp; h.Hv = n->Hv;
@@ -629,6 +656,7 @@ int resnet_run(omq_resnet* n, const int32_t* d_count, int count, float* policy, 
     if (e != cudaSuccess) return cuda_status(e, "heads smem attribute");
   }
   const int blocks = (count + kHeadPos - 1) / kHeadPos;
+  count_launches(1);
   k_heads<<<blocks, kHeadThreads, sm, s>>>(h);
   return cuda_status(cudaGetLastError(), "k_heads");
 }
@@ -648,6 +676,7 @@ int omq_resnet_forward_features(omq_resnet* n, const float* d_features, int32_t 
   DeviceGuard g(n->cfg.device);
   cudaStream_t s = (cudaStream_t)stream;
   const int total = batch * n->P * 8;
+  count_launches(1);
   k_pack_features<<<min((total + 255) / 256, 8192), 256, 0, s>>>(
       d_features, n->cfg.input_channels, n->S, n->P, nullptr, batch, n->x_in);
   int st = cuda_status(cudaGetLastError(), "k_pack_features");
@@ -689,6 +718,40 @@ int omq_resnet_forward_queue(omq_resnet* n, omq_engine* e, int32_t queue, void* 
   int st = cuda_status(cudaGetLastError(), "pack queue");
   if (st) return st;
   return resnet_run(n, e->v.q_count + queue, cap, e->v.q_policy[queue], e->v.q_value[queue], s);
+}
+
+int omq_resnet_profile(omq_resnet* n, int32_t capacity) {
+  if (!n || capacity < 0 || capacity > (1 << 20)) { set_error("bad argument"); return OMQ_BAD_ARG; }
+  DeviceGuard g(n->cfg.device);
+  prof_free(n);
+  if (capacity == 0) return OMQ_OK;
+  n->prof_ev = new (std::nothrow) cudaEvent_t[2 * capacity];
+  n->prof_host_counts = new (std::nothrow) int32_t[capacity];
+  if (!n->prof_ev || !n->prof_host_counts) { set_error("host allocation failed"); return OMQ_BAD_ARG; }
+  for (int i = 0; i < 2 * capacity; ++i) cudaEventCreate(&n->prof_ev[i]);
+  cudaError_t e = cudaMalloc(&n->prof_counts, 4 * (size_t)capacity);
+  if (e == cudaSuccess) e = cudaMemset(n->prof_counts, 0xFF, 4 * (size_t)capacity);
+  n->prof_cap = capacity;
+  for (int i = 0; i < capacity; ++i) n->prof_host_counts[i] = -1;
+  return cuda_status(e, "omq_resnet_profile");
+}
+
+int omq_resnet_profile_read(omq_resnet* n, int32_t* h_calls, float* h_trunk_ms, int32_t* h_counts,
+                            int32_t max) {
+  if (!n || !h_calls) { set_error("null argument"); return OMQ_BAD_ARG; }
+  DeviceGuard g(n->cfg.device);
+  const int k = n->prof_n < max ? n->prof_n : max;
+  *h_calls = k;
+  if (k == 0) return OMQ_OK;
+  cudaError_t e = cudaEventSynchronize(n->prof_ev[2 * (k - 1) + 1]);
+  for (int i = 0; e == cudaSuccess && i < k; ++i)
+    if (h_trunk_ms) e = cudaEventElapsedTime(&h_trunk_ms[i], n->prof_ev[2 * i], n->prof_ev[2 * i + 1]);
+  if (e == cudaSuccess && h_counts) {
+    e = cudaMemcpy(h_counts, n->prof_counts, 4 * (size_t)k, cudaMemcpyDeviceToHost);
+    for (int i = 0; i < k; ++i)
+      if (n->prof_host_counts[i] >= 0) h_counts[i] = n->prof_host_counts[i];
+  }
+  return cuda_status(e, "omq_resnet_profile_read");
 }
 
 int omq_resnet_error(omq_resnet* n, int32_t* h_error, void* stream) {

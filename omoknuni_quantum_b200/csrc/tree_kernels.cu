@@ -575,6 +575,7 @@ static size_t select_smem(const EngineView& v) {
 }
 
 void launch_begin(const EngineView& v, const int8_t* boards, cudaStream_t s) {
+  count_launches(1);
   k_begin<<<v.R, kThreads, 0, s>>>(v, boards);
 }
 
@@ -583,17 +584,20 @@ void launch_select(const EngineView& v, int wave, cudaStream_t s) {
   if (sm > 48 * 1024)
     cudaFuncSetAttribute(k_select, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   cudaMemsetAsync(v.q_count, 0, sizeof(int32_t), s);
+  count_launches(1);
   k_select<<<v.R, kThreads, sm, s>>>(v, wave);
 }
 
 void launch_expand(const EngineView& v, int root_mode, cudaStream_t s) {
   if (!root_mode) cudaMemsetAsync(v.q_count + 1, 0, sizeof(int32_t), s);
+  count_launches(1);
   k_expand<<<v.R, kThreads, 0, s>>>(v, root_mode);
 }
 
 void launch_backup(const EngineView& v, cudaStream_t s) { k_backup<<<v.R, kThreads, 0, s>>>(v); }
 
 void launch_root_visits(const EngineView& v, int32_t* visits, float* nw, cudaStream_t s) {
+  count_launches(1);
   k_root_visits<<<v.R, 256, 0, s>>>(v, visits, nw);
 }
 
@@ -601,10 +605,12 @@ void launch_export(const EngineView& v, int tree, int count, int32_t* N, float* 
                    int32_t* VL, int32_t* parent, int32_t* action, uint8_t* terminal,
                    cudaStream_t s) {
   const int blocks = max(1, min(1024, (count + 255) / 256));
+  count_launches(1);
   k_export<<<blocks, 256, 0, s>>>(v, tree, count, N, W, P, VL, parent, action, terminal);
 }
 
 void launch_status(const EngineView& v, int32_t* status, int32_t* num_nodes, cudaStream_t s) {
+  count_launches(1);
   k_status<<<(v.R + 255) / 256, 256, 0, s>>>(v, status, num_nodes);
 }
 

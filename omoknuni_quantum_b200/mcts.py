@@ -64,9 +64,7 @@ class MCTS:
         if hasattr(evaluator, "_return_torch_tensors"):
             evaluator._return_torch_tensors = True          # mcts.py:120-121
         dev = config.device if config.device != "cpu" else "cuda"
-        self.device = torch.device(dev)
-        if self.device.type == "cuda" and self.device.index is None:
-            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.device = torch.device(dev)   # device index resolved when the first engine is made
         self._engines: Dict[int, WaveEngine] = {}
         self._last_tree = None          # (engine, index) of the last single search
         self._root_state = None
@@ -82,6 +80,10 @@ class MCTS:
     def _engine(self, num_trees: int) -> WaveEngine:
         eng = self._engines.get(num_trees)
         if eng is None:
+            if not torch.cuda.is_available():
+                raise RuntimeError("MCTS search needs a CUDA device (B200); there is no CPU fallback")
+            if self.device.index is None:
+                self.device = torch.device("cuda", torch.cuda.current_device())
             c = self.config
             eng = WaveEngine(num_trees, board_size=c.board_size, capacity=c.tree_capacity,
                              max_wave_size=c.max_wave_size, c_puct=c.c_puct,
@@ -93,7 +95,10 @@ class MCTS:
     def _boards(self, state) -> np.ndarray:
         n = self.config.board_size
         if torch.is_tensor(state):
-            state = state.cpu().numpy()
+            if state.shape[-2:] != (n, n):
+                raise ValueError(f"Invalid state shape: {tuple(state.shape)}, expected {(n, n)}")
+            return state
+        
         if isinstance(state, np.ndarray):
             if state.shape[-2:] != (n, n):
                 raise ValueError(f"Invalid state shape: {state.shape}, expected {(n, n)}")
@@ -105,6 +110,8 @@ class MCTS:
         """Policy (fp64 [board_size**2]) = root-child visit share (mcts.py:924-979)."""
         board = self._boards(state)
         pol = self.search_batch(board[None], num_simulations)[0]
+        if torch.is_tensor(board):
+            board = board.cpu().numpy()
         self._root_state = board
         return pol
 
@@ -119,7 +126,11 @@ class MCTS:
             return np.full((R, self.action_size), 1.0 / self.action_size)
         eng = self._engine(R)
         t0 = time.perf_counter()
-        eng.search(torch.from_numpy(np.ascontiguousarray(boards)).to(self.device), sims, self._eval)
+        if torch.is_tensor(boards):   # host tensor (pinned for an asynchronous copy) or device
+            dev_boards = boards.to(self.device, torch.int8, non_blocking=True)
+        else:
+            dev_boards = torch.from_numpy(np.ascontiguousarray(boards)).to(self.device)
+        eng.search(dev_boards, sims, self._eval)
         visits = eng.root_visits().cpu().numpy()
         dt = time.perf_counter() - t0
         self._last_tree = (eng, 0)

@@ -253,6 +253,28 @@ class ResNetEvaluator:
         _lib.check(self.L.omq_resnet_forward_queue(self._net, engine._h, int(queue), _stream_ptr()),
                    "omq_resnet_forward_queue")
 
+    def profile(self, capacity: int) -> None:
+        """Time the convolution trunk of the next ``capacity`` forward calls with CUDA events."""
+        _lib.check(self.L.omq_resnet_profile(self._net, int(capacity)), "omq_resnet_profile")
+
+    def profile_read(self, max_calls: int = 1 << 16):
+        """(trunk_ms [calls], positions [calls]) of the profiled calls (synchronizes)."""
+        import numpy as np
+        n = ctypes.c_int32()
+        ms = np.zeros(max_calls, np.float32)
+        cnt = np.zeros(max_calls, np.int32)
+        _lib.check(self.L.omq_resnet_profile_read(self._net, ctypes.byref(n), ms.ctypes.data,
+                                                  cnt.ctypes.data, max_calls), "omq_resnet_profile_read")
+        return ms[:n.value], cnt[:n.value]
+
+    @property
+    def conv_launches_per_call(self) -> int:
+        return 1 + 2 * self.spec.num_blocks
+
+    def trunk_flops_per_position(self) -> int:
+        s = self.spec
+        return 2 * s.hw * 9 * (s.input_channels * s.filters + 2 * s.num_blocks * s.filters * s.filters)
+
     def error(self) -> int:
         e = ctypes.c_int32()
         _lib.check(self.L.omq_resnet_error(self._net, ctypes.byref(e), _stream_ptr()), "omq_resnet_error")

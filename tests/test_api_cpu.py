@@ -1,0 +1,74 @@
+"""Host-side API of the drop-in (no GPU needed): MCTSConfig compatibility with the reference's
+field names and defaults, MCTS method semantics that do not touch the device, and the
+no-fallback rule (the search itself fails loudly without CUDA)."""
+import numpy as np
+import pytest
+import torch
+
+
+def test_config_defaults_follow_reference():
+    from omoknuni_quantum_b200.mcts_config import GameType, MCTSConfig
+    c = MCTSConfig()
+    # python/mcts/core/mcts_config.py:33-39, 53, 64, 68-69, 72-73, 79-80, 84-87, 155
+    assert (c.num_simulations, c.c_puct, c.max_depth, c.max_wave_size) == (10000, 1.414, 100, 1024)
+    assert (c.dirichlet_alpha, c.dirichlet_epsilon, c.virtual_loss) == (0.3, 0.25, 1.0)
+    assert c.enable_virtual_loss and c.enable_subtree_reuse and c.wave_async_expansion
+    assert (c.max_tree_nodes, c.initial_tree_nodes, c.tree_capacity) == (2000000, 100000, 100000)
+    assert c.game_type == GameType.GOMOKU and c.board_size == 15
+    assert c.use_cuda_graphs and c.block_size == 128 and c.batch_size == 256  # passthrough fields
+
+
+def test_config_accepts_reference_kwargs_and_rejects_unknown():
+    from omoknuni_quantum_b200.mcts_config import MCTSConfig
+    c = MCTSConfig(backend="gpu", device="cpu", wave_async_expansion=False, dirichlet_epsilon=0.0,
+                   enable_subtree_reuse=False, max_wave_size=256, c_puct=1.4, num_simulations=800,
+                   enable_kernel_fusion=False, tree_reuse_validation_level="full", game_type="gomoku")
+    assert c.enable_kernel_fusion is False and c.tree_reuse_validation_level == "full"
+    assert c.to_dict()["max_wave_size"] == 256
+    with pytest.raises(TypeError):
+        MCTSConfig(not_a_field=1)
+    with pytest.raises(ValueError):
+        MCTSConfig(backend="tpu")
+    assert MCTSConfig(enable_dynamic_allocation=False).tree_capacity == 2000000
+
+
+def test_mcts_host_methods_and_no_cpu_fallback():
+    from omoknuni_quantum_b200 import MCTS, MCTSConfig, SyntheticEvaluator
+    m = MCTS(MCTSConfig(num_simulations=8, max_wave_size=4), SyntheticEvaluator())
+    pol = np.zeros(225)
+    pol[17] = 0.7
+    pol[3] = 0.3
+    assert m.select_action(None, temperature=0, policy=pol) == 17
+    np.random.seed(0)
+    assert m.select_action(None, temperature=1.0, policy=pol) in (3, 17)
+    with pytest.raises(ValueError):
+        m.update_root(225)
+    m.update_root(5, np.zeros((15, 15), np.int8))
+    assert m.get_root_value() == 0.0
+    with pytest.raises(ValueError):
+        m.search(np.zeros((9, 9), np.int8))
+    assert np.allclose(m.search(np.zeros((15, 15), np.int8), num_simulations=0), 1 / 225)
+    if not torch.cuda.is_available():
+        with pytest.raises(RuntimeError, match="CUDA"):
+            m.search(np.zeros((15, 15), np.int8))
+
+
+def test_policy_from_visits():
+    from omoknuni_quantum_b200.engine import WaveEngine
+    v = np.zeros((2, 225), np.int32)
+    v[0, [4, 9]] = [3, 1]
+    p = WaveEngine.policy_from_visits(v)
+    assert p.dtype == np.float64 and p[0, 4] == 0.75 and p[0, 9] == 0.25
+    assert np.allclose(p[1], 1 / 225)
+
+
+def test_roots_are_seeded_and_five_free():
+    from omoknuni_quantum_b200.roots import has_five, random_root, random_roots
+    a, b = random_root(3), random_root(3)
+    assert np.array_equal(a, b) and (a == 1).sum() == 10 and (a == 2).sum() == 10
+    rs = random_roots(1, 50)
+    assert not any(has_five(r) for r in rs)
+    five = np.zeros((15, 15), np.int8)
+    five[2, 4:9] = 2
+    assert has_five(five) and has_five(five.T) and has_five(np.eye(15, dtype=np.int8))
+    assert has_five(np.fliplr(np.eye(15, dtype=np.int8)))
