@@ -120,7 +120,7 @@ class MCTS:
         boards = self._boards(states)
         if boards.ndim == 2:
             boards = boards[None]
-        sims = int(num_simulations or self.config.num_simulations)
+        sims = int(num_simulations or self.config.num_simulations)  # as mcts.py:941
         R = boards.shape[0]
         if sims == 0:                                        # mcts.py:1023-1031
             return np.full((R, self.action_size), 1.0 / self.action_size)

@@ -47,7 +47,9 @@ def test_mcts_host_methods_and_no_cpu_fallback():
     assert m.get_root_value() == 0.0
     with pytest.raises(ValueError):
         m.search(np.zeros((9, 9), np.int8))
-    assert np.allclose(m.search(np.zeros((15, 15), np.int8), num_simulations=0), 1 / 225)
+    # a zero-simulation config returns the uniform policy (mcts.py:1023-1031)
+    m0 = MCTS(MCTSConfig(num_simulations=0), SyntheticEvaluator())
+    assert np.allclose(m0.search(np.zeros((15, 15), np.int8)), 1 / 225)
     if not torch.cuda.is_available():
         with pytest.raises(RuntimeError, match="CUDA"):
             m.search(np.zeros((15, 15), np.int8))
