@@ -193,6 +193,21 @@ OMQ_API int omq_resnet_forward_queue(omq_resnet* net, omq_engine* engine, int32_
 OMQ_API int omq_resnet_profile(omq_resnet* net, int32_t capacity);
 OMQ_API int omq_resnet_profile_read(omq_resnet* net, int32_t* h_calls, float* h_trunk_ms,
                                     int32_t* h_counts, int32_t max);
+/* ResNet forward that allocates nothing (no counterpart in the reference). For callers that must
+ * not let a library allocate device memory: a process whose own allocator owns the whole device
+ * heap, or a latency-critical thread where cudaMalloc/cudaFree would synchronise the device.
+ * Same computation as omq_resnet_forward_features, but the caller passes the packed parameter
+ * blobs (layouts as for omq_resnet_load), the features and the outputs, and the activations live
+ * in one fixed 8 MiB device array built into the library, held by every GPU that loads it until
+ * the process exits. Batches beyond what that array holds (36 positions at 128 filters, 19 at
+ * 256, for 15x15) are rejected with OMQ_BAD_ARG. The first call on a device looks up the
+ * array's device address; make that first call before any stream capture. All calls share the
+ * array: calls that overlap on the GPU (other streams, other threads) race and must be
+ * serialised by the caller. */
+OMQ_API int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const uint16_t* d_conv_w,
+                                       const float* d_conv_b, const float* d_head,
+                                       const float* d_features, int32_t batch, float* d_policy,
+                                       float* d_value, void* stream);
 /* Device error word of the net (OMQ_TIMEOUT after a bounded wait gave up); synchronizes. */
 OMQ_API int omq_resnet_error(omq_resnet* net, int32_t* h_error, void* stream);
 

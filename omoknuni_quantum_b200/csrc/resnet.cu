@@ -764,3 +764,115 @@ int omq_resnet_error(omq_resnet* n, int32_t* h_error, void* stream) {
 }
 
 }  // extern "C"
+
+// =============================================================================================
+// Forward pass that allocates nothing
+// =============================================================================================
+// Some callers cannot let a library call cudaMalloc: processes whose own memory manager owns the
+// whole device heap (a serving process that reserves all of HBM for its pool up front), and
+// latency-critical threads, where cudaMalloc / cudaFree would synchronise the device and stall
+// every other stream. omq_resnet_forward_noalloc serves them: the caller passes the packed
+// weights, the input features and the output buffers, and the activations live in one fixed
+// device array compiled into this library. That array (kNoAllocScratchBytes) is held by every
+// GPU that loads the library until the process exits, and every call shares it.
+namespace omq {
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB of activations + the error word
+}
+static __device__ __align__(256) uint8_t g_noalloc_scratch[omq::kNoAllocScratchBytes];
+
+namespace omq {
+constexpr int kMaxDevices = 64;
+// Device address of g_noalloc_scratch per device ordinal, looked up once per device with that
+// device current. In host code the array's name is only a host-side stand-in, never a usable
+// device address.
+static uint8_t* g_noalloc_ptr[kMaxDevices];
+
+static int noalloc_scratch(int dev, uint8_t** out) {
+  if (dev < 0 || dev >= kMaxDevices) { set_error("device ordinal %d out of range", dev); return OMQ_BAD_ARG; }
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    g_noalloc_ptr[dev] = static_cast<uint8_t*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return OMQ_OK;
+}
+}  // namespace omq
+
+extern "C" int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const uint16_t* d_conv_w,
+                                          const float* d_conv_b, const float* d_head,
+                                          const float* d_features, int32_t batch,
+                                          float* d_policy, float* d_value, void* stream) {
+  if (!cfg || !d_conv_w || !d_conv_b || !d_head || !d_features || !d_policy || !d_value) {
+    set_error("null argument");
+    return OMQ_BAD_ARG;
+  }
+  const omq_resnet_config c = *cfg;
+  if (c.board_size < 5 || c.board_size > 19 || c.input_channels < 1 || c.input_channels > kInPad ||
+      (c.filters != 128 && c.filters != 256) || c.num_blocks < 0 || c.num_blocks > 64 ||
+      c.num_actions < 1 || c.num_actions > 4096 || c.fc_policy_hidden < 1 ||
+      c.fc_policy_hidden > 1024 || c.fc_value_hidden < 1 || c.fc_value_hidden > 1024) {
+    set_error("bad resnet config");
+    return OMQ_BAD_ARG;
+  }
+  const int P = (c.board_size + 1) * (c.board_size + 1);
+  // scratch: the packed input [rows][64] + three activation buffers [rows][F] (bf16) + error word
+  const size_t per_pos = (size_t)P * (kInPad + 3 * (size_t)c.filters) * 2;
+  const int max_batch = (int)((kNoAllocScratchBytes - 1024) / per_pos);
+  if (batch < 0 || batch > max_batch) {
+    set_error("omq_resnet_forward_noalloc: batch %d exceeds the fixed scratch limit of %d positions "
+              "(%zu-byte scratch, %d filters)", batch, max_batch, kNoAllocScratchBytes, c.filters);
+    return OMQ_BAD_ARG;
+  }
+  if (batch == 0) return OMQ_OK;
+  DeviceGuard g(c.device);
+  uint8_t* base = nullptr;
+  int st = noalloc_scratch(c.device, &base);
+  if (st) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  // a view of the library's net object over caller weights and the fixed scratch (host stack only)
+  omq_resnet n{};
+  CUtensorMap maps[2 * 64];
+  n.cfg = c;
+  n.S = c.board_size;
+  n.P = P;
+  n.HW = c.board_size * c.board_size;
+  n.A = c.num_actions;
+  n.C = c.filters;
+  n.NB = c.num_blocks;
+  n.Hp = c.fc_policy_hidden;
+  n.Hv = c.fc_value_hidden;
+  n.max_batch = max_batch;
+  n.rows = (size_t)max_batch * P;
+  cudaDeviceGetAttribute(&n.sm_count, cudaDevAttrMultiProcessorCount, c.device);
+  n.conv_w = reinterpret_cast<__nv_bfloat16*>(const_cast<uint16_t*>(d_conv_w));
+  n.conv_b = const_cast<float*>(d_conv_b);
+  n.head = const_cast<float*>(d_head);
+  n.x_in = reinterpret_cast<__nv_bfloat16*>(base);
+  size_t off = ((n.rows * kInPad * 2) + 255) & ~(size_t)255;
+  for (int i = 0; i < 3; ++i) {
+    n.act[i] = reinterpret_cast<__nv_bfloat16*>(base + off);
+    off += ((n.rows * n.C * 2) + 255) & ~(size_t)255;
+  }
+  n.error = reinterpret_cast<int32_t*>(base + kNoAllocScratchBytes - 256);
+  n.tmB = maps;
+  n.loaded = 1;
+  st = make_map(&n.tmA_in, n.x_in, kInPad, n.rows, kTileM);
+  for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n.tmA[i], n.act[i], n.C, n.rows, kTileM);
+  if (st == OMQ_OK) st = make_map(&n.tmB_in, n.conv_w, 9 * kInPad, n.C, n.C);
+  const __nv_bfloat16* wb = n.conv_w + (size_t)n.C * 9 * kInPad;
+  for (int i = 0; st == OMQ_OK && i < 2 * n.NB; ++i)
+    st = make_map(&n.tmB[i], wb + (size_t)i * n.C * 9 * n.C, 9 * n.C, n.C, n.C);
+  if (st) return st;
+  // the error word keeps the previous call's value: clear it
+  cudaError_t e = cudaMemsetAsync(n.error, 0, sizeof(int32_t), s);
+  if (e != cudaSuccess) return cuda_status(e, "omq_resnet_forward_noalloc: clearing the error word");
+  const int total = batch * P * 8;
+  count_launches(1);
+  k_pack_features<<<min((total + 255) / 256, 8192), 256, 0, s>>>(
+      d_features, c.input_channels, n.S, P, nullptr, batch, n.x_in);
+  st = cuda_status(cudaGetLastError(), "k_pack_features");
+  if (st) return st;
+  return resnet_run(&n, nullptr, batch, d_policy, d_value, s);
+}
