@@ -28,7 +28,6 @@
 
 namespace omq {
 
-constexpr int kConvThreads = 192;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait before giving up
 constexpr int kTileM = 128;
 constexpr int kBlockK = 64;     // 64 bf16 = one 128-byte swizzle row
@@ -47,20 +46,28 @@ struct ConvArgs {
   int32_t* error;
 };
 
-template <int BN>
+// BN = output channels per tile (all of them); SUB = 128-row UMMA sub-tiles per CTA tile that
+// share each B (weight) stage. SUB = 2 halves the shared-memory bytes per FLOP of the N = 128
+// net; TMEM holds 2 (double buffer) x SUB x BN fp32 columns <= 512.
+template <int BN, int SUB>
 struct ConvCfg {
-  static constexpr int kA = kTileM * kBlockK * 2;
+  static constexpr int kRows = kTileM * SUB;
+  static constexpr int kA = kRows * kBlockK * 2;
   static constexpr int kB = BN * kBlockK * 2;
   static constexpr int kStage = kA + kB;
-  static constexpr int kStages = (BN == 256) ? 4 : 6;
-  static constexpr int kSmem = kStages * kStage + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kStages = (196608 / kStage) < 8 ? (196608 / kStage) : 8;
+  static constexpr int kEpiWarps = 4 * SUB;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kTmemCols = 2 * SUB * BN;
+  static constexpr int kSmem = kStages * kStage + 1024 /*align*/ + 256 /*barriers*/ + BN * 4;
+  static_assert(kTmemCols <= 512, "TMEM holds 512 fp32 columns");
 };
 
-template <int BN>
-__global__ void __launch_bounds__(kConvThreads, 1)
+template <int BN, int SUB>
+__global__ void __launch_bounds__(ConvCfg<BN, SUB>::kThreads, 1)
     k_conv3x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               ConvArgs args) {
-  using Cfg = ConvCfg<BN>;
+  using Cfg = ConvCfg<BN, SUB>;
   constexpr int kStages = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -72,25 +79,27 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_bias = reinterpret_cast<float*>(smem + kStages * Cfg::kStage + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_pos = args.d_count ? min(*args.d_count, args.count) : args.count;
   const int rows = n_pos * args.P;
-  const int tiles = (rows + kTileM - 1) / kTileM;
+  const int tiles = (rows + Cfg::kRows - 1) / Cfg::kRows;
   const int KB = 9 * args.kb_per_tap;
   const int rowstride = args.S + 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) { ptx::mbar_init(&full[s], 1); ptx::mbar_init(&empty[s], 1); }
-    for (int i = 0; i < 2; ++i) { ptx::mbar_init(&tfull[i], 1); ptx::mbar_init(&tempty[i], 4); }
+    for (int i = 0; i < 2; ++i) { ptx::mbar_init(&tfull[i], 1); ptx::mbar_init(&tempty[i], Cfg::kEpiWarps); }
     ptx::mbar_init(drain, 1);
     *abort_flag = 0;
     ptx::fence_barrier_init();
     ptx::prefetch_tmap(&tmA);
     ptx::prefetch_tmap(&tmB);
   }
+  for (int i = threadIdx.x; i < BN; i += blockDim.x) s_bias[i] = args.bias[i];
   if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, 2 * BN);
+    ptx::tmem_alloc(tmem_slot, Cfg::kTmemCols);
     ptx::tmem_relinquish();
   }
   ptx::tc_fence_before();
@@ -105,7 +114,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     int issued[kStages];
     for (int i = 0; i < kStages; ++i) issued[i] = -1;
     for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
-      const int m0 = tile * kTileM;
+      const int m0 = tile * Cfg::kRows;
       for (int kb = 0; kb < KB; ++kb) {
         if (!ptx::mbar_wait(&empty[s], ph ^ 1, abort_flag, kWaitLimitNs)) goto producer_done;
         const int tap = kb / args.kb_per_tap, cb = kb - tap * args.kb_per_tap;
@@ -137,7 +146,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       const uint32_t aph = (t >> 1) & 1;
       if (!ptx::mbar_wait(&tempty[ab], aph ^ 1, abort_flag, kWaitLimitNs)) break;
       ptx::tc_fence_after();
-      const uint32_t d = tmem + ab * BN;
+      const uint32_t d = tmem + ab * SUB * BN;
       bool ok = true;
       for (int kb = 0; kb < KB; ++kb) {
         if (!ptx::mbar_wait(&full[s], ph, abort_flag, kWaitLimitNs)) { ok = false; break; }
@@ -145,9 +154,13 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const uint32_t a_addr = ptx::smem_u32(smem + s * Cfg::kStage);
         const uint32_t b_addr = a_addr + Cfg::kA;
 #pragma unroll
-        for (int k = 0; k < kBlockK / 16; ++k)
-          ptx::mma_bf16(d, ptx::smem_desc_sw128(a_addr + k * 32),
-                        ptx::smem_desc_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
+        for (int k = 0; k < kBlockK / 16; ++k) {
+          const uint64_t bdesc = ptx::smem_desc_sw128(b_addr + k * 32);
+#pragma unroll
+          for (int sub = 0; sub < SUB; ++sub)
+            ptx::mma_bf16(d + sub * BN, ptx::smem_desc_sw128(a_addr + sub * (kTileM * 128) + k * 32),
+                          bdesc, idesc, (kb | k) != 0);
+        }
         any = true;
         ptx::mma_commit(&empty[s]);
         if (++s == kStages) { s = 0; ph ^= 1; }
@@ -161,15 +174,16 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       ptx::mbar_wait(drain, 0, &dummy, kWaitLimitNs);
     }
   } else if (warp >= 2) {
-    // ---------------- epilogue ----------------
-    const int q = warp & 3;
+    // ---------------- epilogue: warp 2 + 4*sub + q handles rows sub*128 + 32q .. +31 ----------
+    const int sub = (warp - 2) >> 2;
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
     int t = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
       const int ab = t & 1;
       const uint32_t aph = (t >> 1) & 1;
       if (!ptx::mbar_wait(&tfull[ab], aph, abort_flag, kWaitLimitNs)) break;
       ptx::tc_fence_after();
-      const int m = tile * kTileM + q * 32 + lane;
+      const int m = tile * Cfg::kRows + sub * kTileM + q * 32 + lane;
       const bool valid = m < rows;
       const int pix = m % args.P;
       const int y = pix / rowstride, x = pix - y * rowstride;
@@ -179,7 +193,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + ab * BN + c0, r);
+        ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + ab * SUB * BN + sub * BN + c0, r);
         ptx::tmem_ld_wait();
         if (!valid) continue;
         uint4 packed[4];
@@ -208,8 +222,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           }
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            float v0 = __uint_as_float(r[j]) + __ldg(args.bias + c0 + j) + res[j];
-            float v1 = __uint_as_float(r[j + 1]) + __ldg(args.bias + c0 + j + 1) + res[j + 1];
+            float v0 = __uint_as_float(r[j]) + s_bias[c0 + j] + res[j];
+            float v1 = __uint_as_float(r[j + 1]) + s_bias[c0 + j + 1] + res[j + 1];
             if (args.relu) { v0 = fmaxf(v0, 0.0f); v1 = fmaxf(v1, 0.0f); }
             __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
             pw[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
@@ -227,10 +241,13 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   __syncthreads();
   if (warp == 1) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem, 2 * BN);
+    ptx::tmem_dealloc(tmem, Cfg::kTmemCols);
   }
   if (threadIdx.x == 0 && *abort_flag) atomicExch(args.error, OMQ_TIMEOUT);
 }
+
+// Sub-tiles per CTA tile for a given filter count (must match the A tensor maps' box height).
+__host__ __device__ constexpr int conv_sub(int filters) { return filters == 128 ? 2 : 1; }
 
 // ---------------------------------------------------------------------------------------------
 // input packing: reference fp32 features [n][19][S][S] -> bf16 [n][P][64] padded pixel space
@@ -508,8 +525,9 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
   // activations start zeroed so that never-written padding rows read as zeros
   cudaMemset(b + off[3], 0, tot - off[3]);
   n->tmB = new (std::nothrow) CUtensorMap[2 * n->NB + 1];
-  int st = make_map(&n->tmA_in, n->x_in, kInPad, n->rows, kTileM);
-  for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n->tmA[i], n->act[i], n->C, n->rows, kTileM);
+  const uint32_t box_rows = kTileM * conv_sub(n->C);
+  int st = make_map(&n->tmA_in, n->x_in, kInPad, n->rows, box_rows);
+  for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n->tmA[i], n->act[i], n->C, n->rows, box_rows);
   if (st == OMQ_OK) st = make_map(&n->tmB_in, n->conv_w, 9 * kInPad, n->C, n->C);
   const __nv_bfloat16* wb = n->conv_w + (size_t)n->C * 9 * kInPad;
   for (int i = 0; st == OMQ_OK && i < 2 * n->NB; ++i)
@@ -578,33 +596,33 @@ int omq_resnet_memory(const omq_resnet* n, uint64_t* bytes) {
 
 namespace omq {
 
-template <int BN>
+template <int BN, int SUB>
 static int launch_conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB,
                        const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
                        int kb_per_tap, const int32_t* d_count, int count, cudaStream_t s) {
-  using Cfg = ConvCfg<BN>;
+  using Cfg = ConvCfg<BN, SUB>;
   static int attr_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (attr_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(k_conv3x3<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(k_conv3x3<BN, SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::kSmem);
     if (e != cudaSuccess) return cuda_status(e, "conv smem attribute");
     attr_dev = dev;
   }
   ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
-  const int max_tiles = (int)((n->rows + kTileM - 1) / kTileM);
+  const int max_tiles = (int)((n->rows + Cfg::kRows - 1) / Cfg::kRows);
   const int grid = max(1, min(max_tiles, n->sm_count));
   count_launches(1);
-  k_conv3x3<BN><<<grid, kConvThreads, Cfg::kSmem, s>>>(tA, tB, a);
+  k_conv3x3<BN, SUB><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(tA, tB, a);
   return cuda_status(cudaGetLastError(), "k_conv3x3");
 }
 
 static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB, const float* bias,
                 const __nv_bfloat16* res, __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count,
                 int count, cudaStream_t s) {
-  if (n->C == 128) return launch_conv<128>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
-  return launch_conv<256>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
+  if (n->C == 128) return launch_conv<128, conv_sub(128)>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
+  return launch_conv<256, conv_sub(256)>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
 }
 
 // trunk + heads on n->x_in (already packed), count from d_count (device) or `count`.
@@ -858,8 +876,9 @@ extern "C" int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const ui
   n.error = reinterpret_cast<int32_t*>(base + kNoAllocScratchBytes - 256);
   n.tmB = maps;
   n.loaded = 1;
-  st = make_map(&n.tmA_in, n.x_in, kInPad, n.rows, kTileM);
-  for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n.tmA[i], n.act[i], n.C, n.rows, kTileM);
+  const uint32_t box_rows = kTileM * conv_sub(n.C);
+  st = make_map(&n.tmA_in, n.x_in, kInPad, n.rows, box_rows);
+  for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n.tmA[i], n.act[i], n.C, n.rows, box_rows);
   if (st == OMQ_OK) st = make_map(&n.tmB_in, n.conv_w, 9 * kInPad, n.C, n.C);
   const __nv_bfloat16* wb = n.conv_w + (size_t)n.C * 9 * kInPad;
   for (int i = 0; st == OMQ_OK && i < 2 * n.NB; ++i)
