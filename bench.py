@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--evaluator", choices=["resnet", "synthetic"], default="resnet",
+                    help="synthetic = BASELINE config 0 (tree kernels only; 800 sims, 200k nodes)")
     return ap.parse_args()
 
 
@@ -359,8 +361,54 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+def run_b200_synthetic(args):
+    """BASELINE config 0 on the device: the integer-exact synthetic evaluator, so the step is the
+    tree kernels alone (select, expand, backup, evaluation kernel)."""
+    from omoknuni_quantum_b200 import _lib, parallel
+    from omoknuni_quantum_b200.engine import WaveEngine
+    from omoknuni_quantum_b200.roots import random_roots
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    R = args.roots
+    roots = torch.from_numpy(random_roots(args.seed * 1000 + rank, R)).to(dev)
+    eng = WaveEngine(R, capacity=args.capacity, max_wave_size=args.wave, device=dev)
+    for _ in range(args.warmup):
+        eng.search(roots, args.sims)
+    torch.cuda.synchronize()
+    n0 = _lib.kernel_launches()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        s0.record()
+        for _ in range(args.steps):
+            eng.search(roots, args.sims)
+        s1.record()
+        torch.cuda.synchronize()
+    ms = parallel.max_over_ranks(s0.elapsed_time(s1), dev)
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": args.sims * R * args.steps * ws / (ms / 1000.0), "unit": UNIT,
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32/int32",
+            "data": "synthetic (seeded roots, integer-exact synthetic evaluator)",
+            "config": {"workload": f"config0: Gomoku 15x15, {args.sims} sims/root, wave {args.wave}, "
+                                   "synthetic evaluator; roots searched in lockstep per GPU",
+                       "roots_per_gpu": R, "capacity": args.capacity, "parallelism": f"dp{ws}"},
+            "roofline": None, "cpu_baseline": None, "e2e": None, "clocks": clk.summary(),
+            "gpu_launches": _lib.kernel_launches() - n0}), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
+    if args.evaluator == "synthetic" and args.impl == "b200":
+        run_b200_synthetic(args)
+        return
     if args.impl == "reference":
         run_reference_arm(args)
     else:
