@@ -20,6 +20,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <new>
 
@@ -246,6 +247,214 @@ __global__ void __launch_bounds__(ConvCfg<BN, SUB>::kThreads, 1)
   if (threadIdx.x == 0 && *abort_flag) atomicExch(args.error, OMQ_TIMEOUT);
 }
 
+// CTA-pair variant (cta_group::2). A cluster of 2 CTAs computes 256-row tiles with one UMMA of
+// M = 256: each CTA stages its own 128 rows of A and half (BN/2 rows) of the weight tile, so a
+// K=16 step reads 4 KB + BN/2 * 32 B of shared memory per SM instead of 4 KB + BN * 32 B - the
+// shared-memory feed that limits the single-CTA N = 128 kernel. The leader (rank 0) issues the
+// MMAs; both CTAs' TMA loads complete on the leader's stage barrier; the leader's commits arrive
+// on both CTAs' barriers (one plain commit per CTA, no multicast); each CTA's epilogue drains its
+// own TMEM rows and arrives on the leader's accumulator-empty barrier.
+template <int BN>
+struct PairCfg {
+  static constexpr int kA = kTileM * kBlockK * 2;          // 16 KB
+  static constexpr int kB = (BN / 2) * kBlockK * 2;        // this CTA's half of the weights
+  static constexpr int kStage = kA + kB;
+  static constexpr int kStages = (196608 / kStage) < 8 ? (196608 / kStage) : 8;
+  static constexpr int kThreads = 192;                     // producer, MMA, 4 epilogue warps
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kSmem = kStages * kStage + 1024 + 256 + BN * 4;
+};
+
+template <int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::kThreads, 1)
+    k_conv3x3_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   ConvArgs args) {
+  using Cfg = PairCfg<BN>;
+  constexpr int kStages = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * Cfg::kStage);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_bias = reinterpret_cast<float*>(smem + kStages * Cfg::kStage + 256);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = ptx::cluster_ctarank();
+  const int pair = (int)ptx::cluster_id_x(), npairs = (int)ptx::nclusters_x();
+  const int n_pos = args.d_count ? min(*args.d_count, args.count) : args.count;
+  const int rows = n_pos * args.P;
+  const int tiles = (rows + 2 * kTileM - 1) / (2 * kTileM);
+  const int KB = 9 * args.kb_per_tap;
+  const int rowstride = args.S + 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) { ptx::mbar_init(&full[s], 1); ptx::mbar_init(&empty[s], 1); }
+    for (int i = 0; i < 2; ++i) { ptx::mbar_init(&tfull[i], 1); ptx::mbar_init(&tempty[i], 8); }
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    ptx::fence_barrier_init();
+    ptx::prefetch_tmap(&tmA);
+    ptx::prefetch_tmap(&tmB);
+  }
+  for (int i = threadIdx.x; i < BN; i += blockDim.x) s_bias[i] = args.bias[i];
+  ptx::cluster_sync();  // both CTAs' barriers exist before any remote arrive
+  if (warp == 1) {
+    ptx::tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+    ptx::tmem_relinquish_pair();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    int s = 0;
+    uint32_t ph = 0;
+    int issued[kStages];
+    for (int i = 0; i < kStages; ++i) issued[i] = -1;
+    for (int tile = pair; tile < tiles && !*abort_flag; tile += npairs) {
+      const int m0 = tile * 2 * kTileM + (int)rank * kTileM;
+      for (int kb = 0; kb < KB; ++kb) {
+        if (!ptx::mbar_wait(&empty[s], ph ^ 1, abort_flag, kWaitLimitNs)) goto producer_done;
+        const int tap = kb / args.kb_per_tap, cb = kb - tap * args.kb_per_tap;
+        const int dy = tap / 3 - 1, dx = tap % 3 - 1;
+        const uint32_t bar = ptx::mapa(ptx::smem_u32(&full[s]), 0);
+        if (rank == 0) ptx::mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStage);
+        ptx::tma_load_2d_pair(smem + s * Cfg::kStage, &tmA, bar, cb * kBlockK, m0 + dy * rowstride + dx);
+        ptx::tma_load_2d_pair(smem + s * Cfg::kStage + Cfg::kA, &tmB, bar, kb * kBlockK,
+                              (int)rank * (BN / 2));
+        issued[s] = (int)ph;
+        if (++s == kStages) { s = 0; ph ^= 1; }
+      }
+    }
+  producer_done:
+    // the leader waits (bounded) until every issued stage has landed before it may leave
+    if (rank == 0)
+      for (int i = 0; i < kStages; ++i)
+        if (issued[i] >= 0) {
+          volatile int dummy = 0;
+          ptx::mbar_wait(&full[i], (uint32_t)issued[i], &dummy, kWaitLimitNs);
+        }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ---------------- MMA issuer (leader only) ----------------
+    constexpr uint32_t idesc = ptx::idesc_bf16_f32(2 * kTileM, BN);
+    int s = 0;
+    uint32_t ph = 0;
+    bool any = false;
+    int t = 0;
+    for (int tile = pair; tile < tiles; tile += npairs, ++t) {
+      const int ab = t & 1;
+      const uint32_t aph = (t >> 1) & 1;
+      if (!ptx::mbar_wait_cluster(&tempty[ab], aph ^ 1, abort_flag, kWaitLimitNs)) break;
+      ptx::tc_fence_after();
+      const uint32_t d = tmem + ab * BN;
+      bool ok = true;
+      for (int kb = 0; kb < KB; ++kb) {
+        if (!ptx::mbar_wait(&full[s], ph, abort_flag, kWaitLimitNs)) { ok = false; break; }
+        ptx::tc_fence_after();
+        const uint32_t a_addr = ptx::smem_u32(smem + s * Cfg::kStage);
+        const uint32_t b_addr = a_addr + Cfg::kA;
+#pragma unroll
+        for (int k = 0; k < kBlockK / 16; ++k)
+          ptx::mma_bf16_pair(d, ptx::smem_desc_sw128(a_addr + k * 32),
+                             ptx::smem_desc_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
+        any = true;
+        const uint32_t e_local = ptx::smem_u32(&empty[s]);
+        ptx::mma_commit_pair(e_local);
+        ptx::mma_commit_pair(ptx::mapa(e_local, 1));
+        if (++s == kStages) { s = 0; ph ^= 1; }
+      }
+      if (!ok) break;
+      const uint32_t f_local = ptx::smem_u32(&tfull[ab]);
+      ptx::mma_commit_pair(f_local);
+      ptx::mma_commit_pair(ptx::mapa(f_local, 1));
+    }
+    if (any) {
+      ptx::mma_commit_pair(ptx::smem_u32(drain));
+      volatile int dummy = 0;
+      ptx::mbar_wait(drain, 0, &dummy, kWaitLimitNs);
+    }
+  } else if (warp >= 2) {
+    // ---------------- epilogue (both CTAs, own 128 rows) ----------------
+    const int q = warp & 3;
+    const uint32_t tempty_leader0 = ptx::mapa(ptx::smem_u32(&tempty[0]), 0);
+    const uint32_t tempty_leader1 = ptx::mapa(ptx::smem_u32(&tempty[1]), 0);
+    int t = 0;
+    for (int tile = pair; tile < tiles; tile += npairs, ++t) {
+      const int ab = t & 1;
+      const uint32_t aph = (t >> 1) & 1;
+      if (!ptx::mbar_wait(&tfull[ab], aph, abort_flag, kWaitLimitNs)) break;
+      ptx::tc_fence_after();
+      const int m = tile * 2 * kTileM + (int)rank * kTileM + q * 32 + lane;
+      const bool valid = m < rows;
+      const int pix = m % args.P;
+      const int y = pix / rowstride, x = pix - y * rowstride;
+      const bool pad = (y == args.S) || (x == args.S);
+      __nv_bfloat16* orow = args.out + (size_t)m * BN;
+      const __nv_bfloat16* rrow = args.residual ? args.residual + (size_t)m * BN : nullptr;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + ab * BN + c0, r);
+        ptx::tmem_ld_wait();
+        if (!valid) continue;
+        uint4 packed[4];
+        uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
+        if (pad) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) pw[j] = 0u;
+        } else {
+          float res[32];
+          if (rrow) {
+            const uint4* rp = reinterpret_cast<const uint4*>(rrow + c0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 u = rp[j];
+              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                float2 f = __bfloat1622float2(h[e]);
+                res[8 * j + 2 * e] = f.x;
+                res[8 * j + 2 * e + 1] = f.y;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) res[j] = 0.0f;
+          }
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            float v0 = __uint_as_float(r[j]) + s_bias[c0 + j] + res[j];
+            float v1 = __uint_as_float(r[j + 1]) + s_bias[c0 + j + 1] + res[j + 1];
+            if (args.relu) { v0 = fmaxf(v0, 0.0f); v1 = fmaxf(v1, 0.0f); }
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
+            pw[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+        }
+        uint4* op = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) op[j] = packed[j];
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive_cluster(ab ? tempty_leader1 : tempty_leader0);
+    }
+  }
+  __syncthreads();
+  ptx::cluster_sync();  // neither CTA leaves while the pair still reads its shared memory
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc_pair(tmem, Cfg::kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(args.error, OMQ_TIMEOUT);
+}
+
 // Sub-tiles per CTA tile for a given filter count (must match the A tensor maps' box height).
 __host__ __device__ constexpr int conv_sub(int filters) { return filters == 128 ? 2 : 1; }
 
@@ -427,6 +636,7 @@ struct omq_resnet {
   CUtensorMap tmA_in, tmA[3], tmB_in;
   CUtensorMap* tmB;        // [2*NB]
   int loaded;
+  int pair;                // 1: CTA-pair conv kernel (cta_group::2), 0: single-CTA kernel
   // optional timing of the conv trunk of each forward call (CUDA events on the caller's stream)
   int prof_cap, prof_n;
   cudaEvent_t* prof_ev;    // [2 * prof_cap]
@@ -459,6 +669,31 @@ static int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t o
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) { set_error("cuTensorMapEncodeTiled failed (%d)", (int)r); return OMQ_CUDA_ERROR; }
   return OMQ_OK;
+}
+
+// Conv kernel variant per filter count: the CTA-pair kernel for 256 filters (measured 1.10 vs
+// 1.01 PFLOP/s), the single-CTA M = 256 kernel for 128 filters (0.80-0.87 vs 0.68-0.73).
+// OMQ_CONV_KERNEL=single|pair forces one variant (for measurements).
+static int conv_pair_mode(int filters) {
+  const char* v = getenv("OMQ_CONV_KERNEL");
+  if (v && strcmp(v, "single") == 0) return 0;
+  if (v && strcmp(v, "pair") == 0) return 1;
+  return filters == 256 ? 1 : 0;
+}
+
+// Tensor maps of a net's activation buffers and weights. Box heights follow the kernel variant:
+// A boxes are 128 rows (pair) or 128 * conv_sub(C) rows (single CTA); weight boxes are the CTA's
+// half of the output channels (pair) or all of them.
+static int build_maps(omq_resnet* n) {
+  const uint32_t a_rows = n->pair ? kTileM : kTileM * conv_sub(n->C);
+  const uint32_t b_rows = n->pair ? n->C / 2 : n->C;
+  int st = make_map(&n->tmA_in, n->x_in, kInPad, n->rows, a_rows);
+  for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n->tmA[i], n->act[i], n->C, n->rows, a_rows);
+  if (st == OMQ_OK) st = make_map(&n->tmB_in, n->conv_w, 9 * kInPad, n->C, b_rows);
+  const __nv_bfloat16* wb = n->conv_w + (size_t)n->C * 9 * kInPad;
+  for (int i = 0; st == OMQ_OK && i < 2 * n->NB; ++i)
+    st = make_map(&n->tmB[i], wb + (size_t)i * n->C * 9 * n->C, 9 * n->C, n->C, b_rows);
+  return st;
 }
 
 static size_t head_floats(const omq_resnet* n) {
@@ -525,13 +760,8 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
   // activations start zeroed so that never-written padding rows read as zeros
   cudaMemset(b + off[3], 0, tot - off[3]);
   n->tmB = new (std::nothrow) CUtensorMap[2 * n->NB + 1];
-  const uint32_t box_rows = kTileM * conv_sub(n->C);
-  int st = make_map(&n->tmA_in, n->x_in, kInPad, n->rows, box_rows);
-  for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n->tmA[i], n->act[i], n->C, n->rows, box_rows);
-  if (st == OMQ_OK) st = make_map(&n->tmB_in, n->conv_w, 9 * kInPad, n->C, n->C);
-  const __nv_bfloat16* wb = n->conv_w + (size_t)n->C * 9 * kInPad;
-  for (int i = 0; st == OMQ_OK && i < 2 * n->NB; ++i)
-    st = make_map(&n->tmB[i], wb + (size_t)i * n->C * 9 * n->C, 9 * n->C, n->C, n->C);
+  n->pair = conv_pair_mode(n->C);
+  int st = build_maps(n);
   if (st != OMQ_OK) {
     cudaFree(arena);
     delete[] n->tmB;
@@ -618,9 +848,35 @@ static int launch_conv(const omq_resnet* n, const CUtensorMap& tA, const CUtenso
   return cuda_status(cudaGetLastError(), "k_conv3x3");
 }
 
+template <int BN>
+static int launch_conv_pair(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB,
+                            const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
+                            int kb_per_tap, const int32_t* d_count, int count, cudaStream_t s) {
+  using Cfg = PairCfg<BN>;
+  static int attr_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (attr_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(k_conv3x3_pair<BN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+    if (e != cudaSuccess) return cuda_status(e, "pair conv smem attribute");
+    attr_dev = dev;
+  }
+  ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
+  const int max_tiles = (int)((n->rows + 2 * kTileM - 1) / (2 * kTileM));
+  const int pairs = max(1, min(max_tiles, n->sm_count / 2));
+  count_launches(1);
+  k_conv3x3_pair<BN><<<2 * pairs, Cfg::kThreads, Cfg::kSmem, s>>>(tA, tB, a);
+  return cuda_status(cudaGetLastError(), "k_conv3x3_pair");
+}
+
 static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB, const float* bias,
                 const __nv_bfloat16* res, __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count,
                 int count, cudaStream_t s) {
+  if (n->pair) {
+    if (n->C == 128) return launch_conv_pair<128>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
+    return launch_conv_pair<256>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
+  }
   if (n->C == 128) return launch_conv<128, conv_sub(128)>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
   return launch_conv<256, conv_sub(256)>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
 }
@@ -876,13 +1132,8 @@ extern "C" int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const ui
   n.error = reinterpret_cast<int32_t*>(base + kNoAllocScratchBytes - 256);
   n.tmB = maps;
   n.loaded = 1;
-  const uint32_t box_rows = kTileM * conv_sub(n.C);
-  st = make_map(&n.tmA_in, n.x_in, kInPad, n.rows, box_rows);
-  for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n.tmA[i], n.act[i], n.C, n.rows, box_rows);
-  if (st == OMQ_OK) st = make_map(&n.tmB_in, n.conv_w, 9 * kInPad, n.C, n.C);
-  const __nv_bfloat16* wb = n.conv_w + (size_t)n.C * 9 * kInPad;
-  for (int i = 0; st == OMQ_OK && i < 2 * n.NB; ++i)
-    st = make_map(&n.tmB[i], wb + (size_t)i * n.C * 9 * n.C, 9 * n.C, n.C, n.C);
+  n.pair = conv_pair_mode(n.C);
+  st = build_maps(&n);
   if (st) return st;
   // the error word keeps the previous call's value: clear it
   cudaError_t e = cudaMemsetAsync(n.error, 0, sizeof(int32_t), s);
