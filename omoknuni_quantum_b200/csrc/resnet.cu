@@ -455,6 +455,202 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::kThread
   if (threadIdx.x == 0 && *abort_flag) atomicExch(args.error, OMQ_TIMEOUT);
 }
 
+// Transposed variant for 128 filters: D^T = W * A^T. Output channels are the UMMA's M (128 TMEM
+// lanes) and the tile's 256 pixel rows are its N, so every MMA is 128 x 256 x 16 - the shape
+// that keeps the tensor pipe fed - while a K step still reads only 4 KB of weights plus 8 KB of
+// activations from shared memory. The epilogue turns each warp's 32 channels x 32 pixels block
+// around through a padded shared-memory tile so that stores stay row-contiguous.
+struct TCfg {
+  static constexpr int kPix = 256;                         // pixel rows per tile (UMMA N)
+  static constexpr int kW = 128 * kBlockK * 2;             // weights, 16 KB (UMMA A)
+  static constexpr int kX = kPix * kBlockK * 2;            // activations, 32 KB (UMMA B)
+  static constexpr int kStage = kW + kX;
+  static constexpr int kStages = 4;
+  static constexpr int kThreads = 192;
+  static constexpr int kTmemCols = 2 * kPix;
+  static constexpr int kTransposeFloats = 32 * 33;         // per epilogue warp
+  static constexpr int kSmem = kStages * kStage + 1024 + 256 + 128 * 4 + 4 * kTransposeFloats * 4;
+};
+
+__global__ void __launch_bounds__(TCfg::kThreads, 1)
+    k_conv3x3_t(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                ConvArgs args) {
+  constexpr int BN = 128;
+  constexpr int kStages = TCfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * TCfg::kStage);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_bias = reinterpret_cast<float*>(smem + kStages * TCfg::kStage + 256);
+  float* s_tr = s_bias + BN;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_pos = args.d_count ? min(*args.d_count, args.count) : args.count;
+  const int rows = n_pos * args.P;
+  const int tiles = (rows + TCfg::kPix - 1) / TCfg::kPix;
+  const int KB = 9 * args.kb_per_tap;
+  const int rowstride = args.S + 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) { ptx::mbar_init(&full[s], 1); ptx::mbar_init(&empty[s], 1); }
+    for (int i = 0; i < 2; ++i) { ptx::mbar_init(&tfull[i], 1); ptx::mbar_init(&tempty[i], 4); }
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    ptx::fence_barrier_init();
+    ptx::prefetch_tmap(&tmA);
+    ptx::prefetch_tmap(&tmB);
+  }
+  for (int i = threadIdx.x; i < BN; i += blockDim.x) s_bias[i] = args.bias[i];
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, TCfg::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    int s = 0;
+    uint32_t ph = 0;
+    int issued[kStages];
+    for (int i = 0; i < kStages; ++i) issued[i] = -1;
+    for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+      const int m0 = tile * TCfg::kPix;
+      for (int kb = 0; kb < KB; ++kb) {
+        if (!ptx::mbar_wait(&empty[s], ph ^ 1, abort_flag, kWaitLimitNs)) goto producer_done;
+        const int tap = kb / args.kb_per_tap, cb = kb - tap * args.kb_per_tap;
+        const int dy = tap / 3 - 1, dx = tap % 3 - 1;
+        ptx::mbar_arrive_expect_tx(&full[s], TCfg::kStage);
+        ptx::tma_load_2d(smem + s * TCfg::kStage, &tmB, &full[s], kb * kBlockK, 0);
+        ptx::tma_load_2d(smem + s * TCfg::kStage + TCfg::kW, &tmA, &full[s], cb * kBlockK,
+                         m0 + dy * rowstride + dx);
+        issued[s] = (int)ph;
+        if (++s == kStages) { s = 0; ph ^= 1; }
+      }
+    }
+  producer_done:
+    for (int i = 0; i < kStages; ++i)
+      if (issued[i] >= 0) {
+        volatile int dummy = 0;
+        ptx::mbar_wait(&full[i], (uint32_t)issued[i], &dummy, kWaitLimitNs);
+      }
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = ptx::idesc_bf16_f32(128, TCfg::kPix);
+    int s = 0;
+    uint32_t ph = 0;
+    bool any = false;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+      const int ab = t & 1;
+      const uint32_t aph = (t >> 1) & 1;
+      if (!ptx::mbar_wait(&tempty[ab], aph ^ 1, abort_flag, kWaitLimitNs)) break;
+      ptx::tc_fence_after();
+      const uint32_t d = tmem + ab * TCfg::kPix;
+      bool ok = true;
+      for (int kb = 0; kb < KB; ++kb) {
+        if (!ptx::mbar_wait(&full[s], ph, abort_flag, kWaitLimitNs)) { ok = false; break; }
+        ptx::tc_fence_after();
+        const uint32_t w_addr = ptx::smem_u32(smem + s * TCfg::kStage);
+        const uint32_t x_addr = w_addr + TCfg::kW;
+#pragma unroll
+        for (int k = 0; k < kBlockK / 16; ++k)
+          ptx::mma_bf16(d, ptx::smem_desc_sw128(w_addr + k * 32), ptx::smem_desc_sw128(x_addr + k * 32),
+                        idesc, (kb | k) != 0);
+        any = true;
+        ptx::mma_commit(&empty[s]);
+        if (++s == kStages) { s = 0; ph ^= 1; }
+      }
+      if (!ok) break;
+      ptx::mma_commit(&tfull[ab]);
+    }
+    if (any) {
+      ptx::mma_commit(drain);
+      volatile int dummy = 0;
+      ptx::mbar_wait(drain, 0, &dummy, kWaitLimitNs);
+    }
+  } else if (warp >= 2) {
+    // warp q owns output channels 32q..32q+31 (its TMEM lane quarter) for all 256 pixels
+    const int q = warp & 3;
+    float* tr = s_tr + (warp - 2) * TCfg::kTransposeFloats;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+      const int ab = t & 1;
+      const uint32_t aph = (t >> 1) & 1;
+      if (!ptx::mbar_wait(&tfull[ab], aph, abort_flag, kWaitLimitNs)) break;
+      ptx::tc_fence_after();
+#pragma unroll 1
+      for (int j0 = 0; j0 < TCfg::kPix; j0 += 32) {
+        uint32_t r[32];
+        ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + ab * TCfg::kPix + j0, r);
+        ptx::tmem_ld_wait();
+        // r[jj] = channel (32q + lane) of pixel j0 + jj  ->  tr[jj][lane]
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) tr[jj * 33 + lane] = __uint_as_float(r[jj]);
+        __syncwarp();
+        const int m = tile * TCfg::kPix + j0 + lane;  // this lane's pixel row
+        if (m < rows) {
+          const int pix = m % args.P;
+          const int y = pix / rowstride, x = pix - y * rowstride;
+          const bool pad = (y == args.S) || (x == args.S);
+          uint4 packed[4];
+          uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
+          if (pad) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) pw[j] = 0u;
+          } else {
+            float res[32];
+            if (args.residual) {
+              const uint4* rp = reinterpret_cast<const uint4*>(args.residual + (size_t)m * BN + q * 32);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                uint4 u = rp[j];
+                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  float2 f = __bfloat1622float2(h[e]);
+                  res[8 * j + 2 * e] = f.x;
+                  res[8 * j + 2 * e + 1] = f.y;
+                }
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) res[j] = 0.0f;
+            }
+#pragma unroll
+            for (int c = 0; c < 32; c += 2) {
+              float v0 = tr[lane * 33 + c] + s_bias[q * 32 + c] + res[c];
+              float v1 = tr[lane * 33 + c + 1] + s_bias[q * 32 + c + 1] + res[c + 1];
+              if (args.relu) { v0 = fmaxf(v0, 0.0f); v1 = fmaxf(v1, 0.0f); }
+              __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
+              pw[c / 2] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+          }
+          uint4* op = reinterpret_cast<uint4*>(args.out + (size_t)m * BN + q * 32);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) op[j] = packed[j];
+        }
+        __syncwarp();
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&tempty[ab]);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, TCfg::kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(args.error, OMQ_TIMEOUT);
+}
+
 // Sub-tiles per CTA tile for a given filter count (must match the A tensor maps' box height).
 __host__ __device__ constexpr int conv_sub(int filters) { return filters == 128 ? 2 : 1; }
 
@@ -636,7 +832,7 @@ struct omq_resnet {
   CUtensorMap tmA_in, tmA[3], tmB_in;
   CUtensorMap* tmB;        // [2*NB]
   int loaded;
-  int pair;                // 1: CTA-pair conv kernel (cta_group::2), 0: single-CTA kernel
+  int pair;                // conv variant: 0 single CTA, 1 CTA pair (cta_group::2), 2 transposed
   // optional timing of the conv trunk of each forward call (CUDA events on the caller's stream)
   int prof_cap, prof_n;
   cudaEvent_t* prof_ev;    // [2 * prof_cap]
@@ -671,13 +867,14 @@ static int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t o
   return OMQ_OK;
 }
 
-// Conv kernel variant per filter count: the CTA-pair kernel for 256 filters (measured 1.10 vs
-// 1.01 PFLOP/s), the single-CTA M = 256 kernel for 128 filters (0.80-0.87 vs 0.68-0.73).
-// OMQ_CONV_KERNEL=single|pair forces one variant (for measurements).
-static int conv_pair_mode(int filters) {
+// Conv kernel variant per filter count (OMQ_CONV_KERNEL=single|pair|transposed forces one, for
+// measurements): 0 = single-CTA kernel, 1 = CTA-pair kernel (default for 256 filters, measured
+// 1.10 vs 1.01 PFLOP/s), 2 = transposed kernel (128 filters only).
+static int conv_variant(int filters) {
   const char* v = getenv("OMQ_CONV_KERNEL");
   if (v && strcmp(v, "single") == 0) return 0;
   if (v && strcmp(v, "pair") == 0) return 1;
+  if (v && strcmp(v, "transposed") == 0 && filters == 128) return 2;
   return filters == 256 ? 1 : 0;
 }
 
@@ -685,8 +882,8 @@ static int conv_pair_mode(int filters) {
 // A boxes are 128 rows (pair) or 128 * conv_sub(C) rows (single CTA); weight boxes are the CTA's
 // half of the output channels (pair) or all of them.
 static int build_maps(omq_resnet* n) {
-  const uint32_t a_rows = n->pair ? kTileM : kTileM * conv_sub(n->C);
-  const uint32_t b_rows = n->pair ? n->C / 2 : n->C;
+  const uint32_t a_rows = n->pair == 1 ? kTileM : kTileM * conv_sub(n->C);
+  const uint32_t b_rows = n->pair == 1 ? n->C / 2 : n->C;
   int st = make_map(&n->tmA_in, n->x_in, kInPad, n->rows, a_rows);
   for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n->tmA[i], n->act[i], n->C, n->rows, a_rows);
   if (st == OMQ_OK) st = make_map(&n->tmB_in, n->conv_w, 9 * kInPad, n->C, b_rows);
@@ -760,7 +957,7 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
   // activations start zeroed so that never-written padding rows read as zeros
   cudaMemset(b + off[3], 0, tot - off[3]);
   n->tmB = new (std::nothrow) CUtensorMap[2 * n->NB + 1];
-  n->pair = conv_pair_mode(n->C);
+  n->pair = conv_variant(n->C);
   int st = build_maps(n);
   if (st != OMQ_OK) {
     cudaFree(arena);
@@ -848,6 +1045,26 @@ static int launch_conv(const omq_resnet* n, const CUtensorMap& tA, const CUtenso
   return cuda_status(cudaGetLastError(), "k_conv3x3");
 }
 
+static int launch_conv_t(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB,
+                         const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
+                         int kb_per_tap, const int32_t* d_count, int count, cudaStream_t s) {
+  static int attr_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (attr_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(k_conv3x3_t, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         TCfg::kSmem);
+    if (e != cudaSuccess) return cuda_status(e, "transposed conv smem attribute");
+    attr_dev = dev;
+  }
+  ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
+  const int max_tiles = (int)((n->rows + TCfg::kPix - 1) / TCfg::kPix);
+  const int grid = max(1, min(max_tiles, n->sm_count));
+  count_launches(1);
+  k_conv3x3_t<<<grid, TCfg::kThreads, TCfg::kSmem, s>>>(tA, tB, a);
+  return cuda_status(cudaGetLastError(), "k_conv3x3_t");
+}
+
 template <int BN>
 static int launch_conv_pair(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB,
                             const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
@@ -873,7 +1090,8 @@ static int launch_conv_pair(const omq_resnet* n, const CUtensorMap& tA, const CU
 static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB, const float* bias,
                 const __nv_bfloat16* res, __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count,
                 int count, cudaStream_t s) {
-  if (n->pair) {
+  if (n->pair == 2) return launch_conv_t(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
+  if (n->pair == 1) {
     if (n->C == 128) return launch_conv_pair<128>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
     return launch_conv_pair<256>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
   }
@@ -1132,7 +1350,7 @@ extern "C" int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const ui
   n.error = reinterpret_cast<int32_t*>(base + kNoAllocScratchBytes - 256);
   n.tmB = maps;
   n.loaded = 1;
-  n.pair = conv_pair_mode(n.C);
+  n.pair = conv_variant(n.C);
   st = build_maps(&n);
   if (st) return st;
   // the error word keeps the previous call's value: clear it

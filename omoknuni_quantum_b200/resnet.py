@@ -279,3 +279,30 @@ class ResNetEvaluator:
         e = ctypes.c_int32()
         _lib.check(self.L.omq_resnet_error(self._net, ctypes.byref(e), _stream_ptr()), "omq_resnet_error")
         return int(e.value)
+
+
+def _main(argv=None) -> None:
+    """Standalone forward passes on seeded random weights and features, e.g. as a profiling
+    target: ``python -m omoknuni_quantum_b200.resnet --batch 4096 --blocks 10 --filters 128``."""
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=4096)
+    ap.add_argument("--blocks", type=int, default=10)
+    ap.add_argument("--filters", type=int, default=128)
+    ap.add_argument("--iters", type=int, default=3)
+    a = ap.parse_args(argv)
+    spec = ResNetSpec(num_blocks=a.blocks, filters=a.filters, fc_value_hidden=128)
+    ev = ResNetEvaluator.random(spec, seed=0, max_batch=a.batch)
+    g = torch.Generator().manual_seed(0)
+    x = torch.zeros(a.batch, 19, 15, 15)
+    x[:, 0] = (torch.rand(a.batch, 15, 15, generator=g) < 0.2).float()
+    x[:, 1] = 1.0
+    x = x.to(ev.device)
+    for _ in range(a.iters):
+        ev.evaluate_batch(x)
+    torch.cuda.synchronize()
+    print(f"ok batch={a.batch} error={ev.error()}")
+
+
+if __name__ == "__main__":
+    _main()
