@@ -60,27 +60,30 @@ struct ConvCfg {
   static constexpr int kEpiWarps = 4 * SUB;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr int kTmemCols = 2 * SUB * BN;
-  static constexpr int kSmem = kStages * kStage + 1024 /*align*/ + 256 /*barriers*/ + BN * 4;
+  static constexpr int kStaging = kEpiWarps * 2 * 2048;  // per epilogue warp: 2 x (32 rows x 64 B)
+  static constexpr int kSmem = kStages * kStage + kStaging + 1024 /*align*/ + 256 /*barriers*/ + BN * 4;
   static_assert(kTmemCols <= 512, "TMEM holds 512 fp32 columns");
+  static_assert(kSmem <= 232448, "227 KB of shared memory per CTA");
 };
 
 template <int BN, int SUB>
 __global__ void __launch_bounds__(ConvCfg<BN, SUB>::kThreads, 1)
     k_conv3x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-              ConvArgs args) {
+              const __grid_constant__ CUtensorMap tmO, ConvArgs args) {
   using Cfg = ConvCfg<BN, SUB>;
   constexpr int kStages = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * Cfg::kStage);
+  uint8_t* staging = smem + kStages * Cfg::kStage;  // 1024-aligned (64B-swizzle atoms need 512)
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + Cfg::kStaging);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* s_bias = reinterpret_cast<float*>(smem + kStages * Cfg::kStage + 256);
+  float* s_bias = reinterpret_cast<float*>(staging + Cfg::kStaging + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_pos = args.d_count ? min(*args.d_count, args.count) : args.count;
@@ -97,6 +100,7 @@ __global__ void __launch_bounds__(ConvCfg<BN, SUB>::kThreads, 1)
     ptx::fence_barrier_init();
     ptx::prefetch_tmap(&tmA);
     ptx::prefetch_tmap(&tmB);
+    ptx::prefetch_tmap(&tmO);
   }
   for (int i = threadIdx.x; i < BN; i += blockDim.x) s_bias[i] = args.bias[i];
   if (warp == 1) {
@@ -176,27 +180,30 @@ __global__ void __launch_bounds__(ConvCfg<BN, SUB>::kThreads, 1)
     }
   } else if (warp >= 2) {
     // ---------------- epilogue: warp 2 + 4*sub + q handles rows sub*128 + 32q .. +31 ----------
+    // Each 32 rows x 32 channels chunk is staged in shared memory (64-byte swizzle, two buffers
+    // per warp) and written by one TMA store, instead of 32 scattered 16-byte row stores.
     const int sub = (warp - 2) >> 2;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    uint8_t* my_stage = staging + (warp - 2) * 2 * 2048;
+    int buf = 0;
     int t = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
       const int ab = t & 1;
       const uint32_t aph = (t >> 1) & 1;
       if (!ptx::mbar_wait(&tfull[ab], aph, abort_flag, kWaitLimitNs)) break;
       ptx::tc_fence_after();
-      const int m = tile * Cfg::kRows + sub * kTileM + q * 32 + lane;
+      const int row0 = tile * Cfg::kRows + sub * kTileM + q * 32;
+      const int m = row0 + lane;
       const bool valid = m < rows;
       const int pix = m % args.P;
       const int y = pix / rowstride, x = pix - y * rowstride;
-      const bool pad = (y == args.S) || (x == args.S);
-      __nv_bfloat16* orow = args.out + (size_t)m * BN;
+      const bool pad = !valid || (y == args.S) || (x == args.S);
       const __nv_bfloat16* rrow = args.residual ? args.residual + (size_t)m * BN : nullptr;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
         ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + ab * SUB * BN + sub * BN + c0, r);
         ptx::tmem_ld_wait();
-        if (!valid) continue;
         uint4 packed[4];
         uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
         if (pad) {
@@ -230,14 +237,26 @@ __global__ void __launch_bounds__(ConvCfg<BN, SUB>::kThreads, 1)
             pw[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
           }
         }
-        uint4* op = reinterpret_cast<uint4*>(orow + c0);
+        // the buffer about to be written must no longer be read by an earlier store
+        if (lane == 0) ptx::bulk_wait_read<1>();
+        __syncwarp();
+        uint8_t* sb = my_stage + buf * 2048;
+        const int sw = (lane >> 1) & 3;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) op[j] = packed[j];
+        for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(sb + lane * 64 + ((j ^ sw) * 16)) = packed[j];
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          ptx::tma_store_2d(&tmO, sb, c0, row0);
+          ptx::bulk_commit();
+        }
+        buf ^= 1;
       }
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&tempty[ab]);
     }
+    if (lane == 0) ptx::bulk_wait<0>();
   }
   __syncthreads();
   if (warp == 1) {
@@ -830,6 +849,7 @@ struct omq_resnet {
   __nv_bfloat16* act[3];   // [rows][C]
   int32_t* error;
   CUtensorMap tmA_in, tmA[3], tmB_in;
+  CUtensorMap tmO[3];      // output maps of the activation buffers (TMA-store epilogue)
   CUtensorMap* tmB;        // [2*NB]
   int loaded;
   int pair;                // conv variant: 0 single CTA, 1 CTA pair (cta_group::2), 2 transposed
@@ -850,6 +870,21 @@ static PFN_encodeTiled_t get_encode() {
       fn = reinterpret_cast<PFN_encodeTiled_t>(p);
   }
   return fn;
+}
+
+// 2D bf16 tensor map for the epilogue's TMA stores: box {32 channels, 32 rows}, 64B swizzle.
+static int make_out_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer) {
+  PFN_encodeTiled_t enc = get_encode();
+  if (!enc) { set_error("cuTensorMapEncodeTiled unavailable"); return OMQ_CUDA_ERROR; }
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                   box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) { set_error("cuTensorMapEncodeTiled (output) failed (%d)", (int)r); return OMQ_CUDA_ERROR; }
+  return OMQ_OK;
 }
 
 // 2D bf16 tensor map: inner dim `inner` elements, `outer` rows, box {64, box_rows}, 128B swizzle.
@@ -886,6 +921,7 @@ static int build_maps(omq_resnet* n) {
   const uint32_t b_rows = n->pair == 1 ? n->C / 2 : n->C;
   int st = make_map(&n->tmA_in, n->x_in, kInPad, n->rows, a_rows);
   for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n->tmA[i], n->act[i], n->C, n->rows, a_rows);
+  for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_out_map(&n->tmO[i], n->act[i], n->C, n->rows);
   if (st == OMQ_OK) st = make_map(&n->tmB_in, n->conv_w, 9 * kInPad, n->C, b_rows);
   const __nv_bfloat16* wb = n->conv_w + (size_t)n->C * 9 * kInPad;
   for (int i = 0; st == OMQ_OK && i < 2 * n->NB; ++i)
@@ -1025,7 +1061,7 @@ namespace omq {
 
 template <int BN, int SUB>
 static int launch_conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB,
-                       const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
+                       const CUtensorMap& tO, const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
                        int kb_per_tap, const int32_t* d_count, int count, cudaStream_t s) {
   using Cfg = ConvCfg<BN, SUB>;
   static int attr_dev = -1;
@@ -1041,7 +1077,7 @@ static int launch_conv(const omq_resnet* n, const CUtensorMap& tA, const CUtenso
   const int max_tiles = (int)((n->rows + Cfg::kRows - 1) / Cfg::kRows);
   const int grid = max(1, min(max_tiles, n->sm_count));
   count_launches(1);
-  k_conv3x3<BN, SUB><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(tA, tB, a);
+  k_conv3x3<BN, SUB><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(tA, tB, tO, a);
   return cuda_status(cudaGetLastError(), "k_conv3x3");
 }
 
@@ -1087,7 +1123,8 @@ static int launch_conv_pair(const omq_resnet* n, const CUtensorMap& tA, const CU
   return cuda_status(cudaGetLastError(), "k_conv3x3_pair");
 }
 
-static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB, const float* bias,
+static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tO,
+                const float* bias,
                 const __nv_bfloat16* res, __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count,
                 int count, cudaStream_t s) {
   if (n->pair == 2) return launch_conv_t(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
@@ -1095,8 +1132,8 @@ static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& t
     if (n->C == 128) return launch_conv_pair<128>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
     return launch_conv_pair<256>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
   }
-  if (n->C == 128) return launch_conv<128, conv_sub(128)>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
-  return launch_conv<256, conv_sub(256)>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
+  if (n->C == 128) return launch_conv<128, conv_sub(128)>(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
+  return launch_conv<256, conv_sub(256)>(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
 }
 
 // trunk + heads on n->x_in (already packed), count from d_count (device) or `count`.
@@ -1111,14 +1148,14 @@ int resnet_run(omq_resnet* n, const int32_t* d_count, int count, float* policy, 
       n->prof_host_counts[pi] = count;
     cudaEventRecord(n->prof_ev[2 * pi], s);
   }
-  int st = conv(n, n->tmA_in, n->tmB_in, n->conv_b, nullptr, n->act[0], 1, d_count, count, s);
+  int st = conv(n, n->tmA_in, n->tmB_in, n->tmO[0], n->conv_b, nullptr, n->act[0], 1, d_count, count, s);
   int x = 0;
   for (int i = 0; st == OMQ_OK && i < n->NB; ++i) {
     const int t = (x + 1) % 3, y = (x + 2) % 3;
-    st = conv(n, n->tmA[x], n->tmB[2 * i], n->conv_b + (size_t)(1 + 2 * i) * n->C, nullptr,
+    st = conv(n, n->tmA[x], n->tmB[2 * i], n->tmO[t], n->conv_b + (size_t)(1 + 2 * i) * n->C, nullptr,
               n->act[t], n->C / kBlockK, d_count, count, s);
     if (st) break;
-    st = conv(n, n->tmA[t], n->tmB[2 * i + 1], n->conv_b + (size_t)(2 + 2 * i) * n->C, n->act[x],
+    st = conv(n, n->tmA[t], n->tmB[2 * i + 1], n->tmO[y], n->conv_b + (size_t)(2 + 2 * i) * n->C, n->act[x],
               n->act[y], n->C / kBlockK, d_count, count, s);
     x = y;
   }
