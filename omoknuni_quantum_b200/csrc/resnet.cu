@@ -281,26 +281,29 @@ struct PairCfg {
   static constexpr int kStages = (196608 / kStage) < 8 ? (196608 / kStage) : 8;
   static constexpr int kThreads = 192;                     // producer, MMA, 4 epilogue warps
   static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kSmem = kStages * kStage + 1024 + 256 + BN * 4;
+  static constexpr int kStaging = 4 * 2 * 2048;             // per epilogue warp: 2 x (32 x 64 B)
+  static constexpr int kSmem = kStages * kStage + kStaging + 1024 + 256 + BN * 4;
+  static_assert(kSmem <= 232448, "227 KB of shared memory per CTA");
 };
 
 template <int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::kThreads, 1)
     k_conv3x3_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   ConvArgs args) {
+                   const __grid_constant__ CUtensorMap tmO, ConvArgs args) {
   using Cfg = PairCfg<BN>;
   constexpr int kStages = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * Cfg::kStage);
+  uint8_t* staging = smem + kStages * Cfg::kStage;
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + Cfg::kStaging);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* s_bias = reinterpret_cast<float*>(smem + kStages * Cfg::kStage + 256);
+  float* s_bias = reinterpret_cast<float*>(staging + Cfg::kStaging + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = ptx::cluster_ctarank();
@@ -319,6 +322,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::kThread
     ptx::fence_barrier_init();
     ptx::prefetch_tmap(&tmA);
     ptx::prefetch_tmap(&tmB);
+    ptx::prefetch_tmap(&tmO);
   }
   for (int i = threadIdx.x; i < BN; i += blockDim.x) s_bias[i] = args.bias[i];
   ptx::cluster_sync();  // both CTAs' barriers exist before any remote arrive
@@ -400,29 +404,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::kThread
       ptx::mbar_wait(drain, 0, &dummy, kWaitLimitNs);
     }
   } else if (warp >= 2) {
-    // ---------------- epilogue (both CTAs, own 128 rows) ----------------
+    // ---------------- epilogue (both CTAs, own 128 rows; TMA-store staging as above) ---------
     const int q = warp & 3;
     const uint32_t tempty_leader0 = ptx::mapa(ptx::smem_u32(&tempty[0]), 0);
     const uint32_t tempty_leader1 = ptx::mapa(ptx::smem_u32(&tempty[1]), 0);
+    uint8_t* my_stage = staging + (warp - 2) * 2 * 2048;
+    int buf = 0;
     int t = 0;
     for (int tile = pair; tile < tiles; tile += npairs, ++t) {
       const int ab = t & 1;
       const uint32_t aph = (t >> 1) & 1;
       if (!ptx::mbar_wait(&tfull[ab], aph, abort_flag, kWaitLimitNs)) break;
       ptx::tc_fence_after();
-      const int m = tile * 2 * kTileM + (int)rank * kTileM + q * 32 + lane;
+      const int row0 = tile * 2 * kTileM + (int)rank * kTileM + q * 32;
+      const int m = row0 + lane;
       const bool valid = m < rows;
       const int pix = m % args.P;
       const int y = pix / rowstride, x = pix - y * rowstride;
-      const bool pad = (y == args.S) || (x == args.S);
-      __nv_bfloat16* orow = args.out + (size_t)m * BN;
+      const bool pad = !valid || (y == args.S) || (x == args.S);
       const __nv_bfloat16* rrow = args.residual ? args.residual + (size_t)m * BN : nullptr;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
         ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + ab * BN + c0, r);
         ptx::tmem_ld_wait();
-        if (!valid) continue;
         uint4 packed[4];
         uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
         if (pad) {
@@ -456,14 +461,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::kThread
             pw[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
           }
         }
-        uint4* op = reinterpret_cast<uint4*>(orow + c0);
+        if (lane == 0) ptx::bulk_wait_read<1>();
+        __syncwarp();
+        uint8_t* sb = my_stage + buf * 2048;
+        const int sw = (lane >> 1) & 3;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) op[j] = packed[j];
+        for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(sb + lane * 64 + ((j ^ sw) * 16)) = packed[j];
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          ptx::tma_store_2d(&tmO, sb, c0, row0);
+          ptx::bulk_commit();
+        }
+        buf ^= 1;
       }
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_cluster(ab ? tempty_leader1 : tempty_leader0);
     }
+    if (lane == 0) ptx::bulk_wait<0>();
   }
   __syncthreads();
   ptx::cluster_sync();  // neither CTA leaves while the pair still reads its shared memory
@@ -1103,7 +1119,7 @@ static int launch_conv_t(const omq_resnet* n, const CUtensorMap& tA, const CUten
 
 template <int BN>
 static int launch_conv_pair(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB,
-                            const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
+                            const CUtensorMap& tO, const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
                             int kb_per_tap, const int32_t* d_count, int count, cudaStream_t s) {
   using Cfg = PairCfg<BN>;
   static int attr_dev = -1;
@@ -1119,7 +1135,7 @@ static int launch_conv_pair(const omq_resnet* n, const CUtensorMap& tA, const CU
   const int max_tiles = (int)((n->rows + 2 * kTileM - 1) / (2 * kTileM));
   const int pairs = max(1, min(max_tiles, n->sm_count / 2));
   count_launches(1);
-  k_conv3x3_pair<BN><<<2 * pairs, Cfg::kThreads, Cfg::kSmem, s>>>(tA, tB, a);
+  k_conv3x3_pair<BN><<<2 * pairs, Cfg::kThreads, Cfg::kSmem, s>>>(tA, tB, tO, a);
   return cuda_status(cudaGetLastError(), "k_conv3x3_pair");
 }
 
@@ -1129,8 +1145,8 @@ static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& t
                 int count, cudaStream_t s) {
   if (n->pair == 2) return launch_conv_t(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
   if (n->pair == 1) {
-    if (n->C == 128) return launch_conv_pair<128>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
-    return launch_conv_pair<256>(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
+    if (n->C == 128) return launch_conv_pair<128>(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
+    return launch_conv_pair<256>(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
   }
   if (n->C == 128) return launch_conv<128, conv_sub(128)>(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
   return launch_conv<256, conv_sub(256)>(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
