@@ -15,7 +15,10 @@
 
 namespace omq {
 
-constexpr int kThreads = 256;
+// Block size of the per-tree kernels, chosen at launch: 32 warps per tree when the trees fit in
+// about two waves of the SMs (latency: one tree's parents and leaves spread over 32 warps), 8
+// warps otherwise (several trees share an SM). Kernels use blockDim, bounded by kThreads.
+constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
 
 // ---------------------------------------------------------------------------------------------
@@ -85,8 +88,8 @@ __device__ int block_exclusive_scan(int* vals, int n, int* warp_tot) {
   __syncthreads();
   if (tid == 0) {
     int acc = 0;
-    for (int w = 0; w < kWarps; ++w) { int t = warp_tot[w]; warp_tot[w] = acc; acc += t; }
-    warp_tot[kWarps] = acc;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { int t = warp_tot[w]; warp_tot[w] = acc; acc += t; }
+    warp_tot[blockDim.x >> 5] = acc;
   }
   __syncthreads();
   int run = warp_tot[warp] + inc - sum;
@@ -96,7 +99,7 @@ __device__ int block_exclusive_scan(int* vals, int n, int* warp_tot) {
     run += loc[j];
   }
   __syncthreads();
-  return warp_tot[kWarps];
+  return warp_tot[blockDim.x >> 5];
 }
 
 __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long x) {
@@ -134,7 +137,7 @@ __global__ void __launch_bounds__(kThreads) k_begin(EngineView v, const int8_t* 
   if (tid == 0) { s_stones = 0; s_five = 0; }
   __syncthreads();
   int cnt = 0;
-  for (int i = tid; i < v.C; i += kThreads) {
+  for (int i = tid; i < v.C; i += blockDim.x) {
     int8_t x = boards[(size_t)r * v.C + i];
     sb[i] = x;
     v.root_board[(size_t)r * v.C + i] = x;
@@ -143,7 +146,7 @@ __global__ void __launch_bounds__(kThreads) k_begin(EngineView v, const int8_t* 
   atomicAdd(&s_stones, cnt);
   __syncthreads();
   int five = 0;
-  for (int i = tid; i < v.C; i += kThreads) five |= five_from(sb, v.S, i) ? 1 : 0;
+  for (int i = tid; i < v.C; i += blockDim.x) five |= five_from(sb, v.S, i) ? 1 : 0;
   if (five) atomicOr(&s_five, 1);
   __syncthreads();
   if (tid == 0) {
@@ -190,14 +193,14 @@ __device__ __forceinline__ void emit_child(const EngineView& v, int r, Visit* ne
   if (li < v.LOGCAP) log[li] = x; else *overflow = 1;
 }
 
-__global__ void __launch_bounds__(kThreads) k_select(EngineView v, int wave) {
+__global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) {
   extern __shared__ unsigned char smem_raw[];
   SelectShared& sh = *reinterpret_cast<SelectShared*>(smem_raw);
   int p2 = 1;
   while (p2 < v.A) p2 <<= 1;
   unsigned long long* keys_all =
       reinterpret_cast<unsigned long long*>(smem_raw + ((sizeof(SelectShared) + 15) & ~15));
-  Visit* s_leaves = reinterpret_cast<Visit*>(keys_all + (size_t)kWarps * p2);
+  Visit* s_leaves = reinterpret_cast<Visit*>(keys_all + (size_t)(blockDim.x >> 5) * p2);
   int* s_scan = reinterpret_cast<int*>(s_leaves + v.WCAP);
 
   const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -220,7 +223,7 @@ __global__ void __launch_bounds__(kThreads) k_select(EngineView v, int wave) {
   for (int depth = 1; depth < v.max_depth; ++depth) {
     const int n_cur = sh.cnt[cur];
     if (n_cur == 0) break;
-    for (int i = warp; i < n_cur; i += kWarps) {
+    for (int i = warp; i < n_cur; i += (int)(blockDim.x >> 5)) {
       const Visit e = F[cur][i];
       const NodeTopo tp = v.topo[base + e.node];
       const int n = topo_count(tp);
@@ -278,7 +281,7 @@ __global__ void __launch_bounds__(kThreads) k_select(EngineView v, int wave) {
     __syncthreads();
   }
   // depth limit reached: the remaining simulations stop at nodes that still have children
-  for (int i = tid; i < sh.cnt[cur]; i += kThreads) {
+  for (int i = tid; i < sh.cnt[cur]; i += blockDim.x) {
     int li = atomicAdd(&sh.nleaf, 1);
     if (li < v.WCAP) s_leaves[li] = F[cur][i]; else sh.overflow = 1;
   }
@@ -286,7 +289,7 @@ __global__ void __launch_bounds__(kThreads) k_select(EngineView v, int wave) {
   const int nleaf = min(sh.nleaf, v.WCAP);
   // sort leaves ascending by node id (each node is a leaf at most once per wave)
   Visit* gleaves = v.leaves + (size_t)r * v.WCAP;
-  for (int i = tid; i < nleaf; i += kThreads) {
+  for (int i = tid; i < nleaf; i += blockDim.x) {
     const int key = s_leaves[i].node;
     int rank = 0;
     for (int j = 0; j < nleaf; ++j) rank += s_leaves[j].node < key;
@@ -294,21 +297,21 @@ __global__ void __launch_bounds__(kThreads) k_select(EngineView v, int wave) {
   }
   __syncthreads();
   // expandable leaves: no children, not terminal (wave_search.py:829-855)
-  for (int i = tid; i < nleaf; i += kThreads) {
+  for (int i = tid; i < nleaf; i += blockDim.x) {
     const NodeTopo tp = v.topo[base + gleaves[i].node];
     s_scan[i] = (topo_count(tp) == 0 && !(topo_flags(tp) & kFlagTerminal)) ? 1 : 0;
   }
   __syncthreads();
   // keep the flags (scan overwrites them): stash in leaf_final.y as 0/1 first
   int2* lf = v.leaf_final + (size_t)r * v.WCAP;
-  for (int i = tid; i < nleaf; i += kThreads) lf[i] = make_int2(-1, s_scan[i]);
+  for (int i = tid; i < nleaf; i += blockDim.x) lf[i] = make_int2(-1, s_scan[i]);
   __syncthreads();
   const int nexp = block_exclusive_scan(s_scan, nleaf, sh.warp_tot);
   __shared__ int s_qbase;
   if (tid == 0) s_qbase = nexp > 0 ? atomicAdd(&v.q_count[0], nexp) : 0;
   __syncthreads();
   const int qbase = s_qbase;
-  for (int i = tid; i < nleaf; i += kThreads) {
+  for (int i = tid; i < nleaf; i += blockDim.x) {
     if (lf[i].y) {
       const int q = qbase + s_scan[i];
       v.q_entries[0][q] = make_int2(r, gleaves[i].node);
@@ -351,8 +354,9 @@ __device__ float warp_fixed_order_sum(const float* pv, int n) {
   return s;
 }
 
-__global__ void __launch_bounds__(kThreads) k_expand(EngineView v, int root_mode) {
-  __shared__ ExpandWarpSmem ws[kWarps];
+__global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_mode) {
+  extern __shared__ unsigned char expand_smem[];
+  ExpandWarpSmem* ws = reinterpret_cast<ExpandWarpSmem*>(expand_smem);  // [warps]
   __shared__ int s_cnt[1024];
   __shared__ int warp_tot[kWarps + 1];
   __shared__ int s_fbase;
@@ -367,7 +371,7 @@ __global__ void __launch_bounds__(kThreads) k_expand(EngineView v, int root_mode
   const float* pol = v.q_policy[0];
 
   // children per expandable leaf: the empty cells of its board, i.e. C - move_count
-  for (int i = tid; i < nleaf; i += kThreads)
+  for (int i = tid; i < nleaf; i += blockDim.x)
     s_cnt[i] = lf[i].y >= 0 ? max(v.C - (H->root_mc + leaves[i].depth), 0) : 0;
   __syncthreads();
   const int total = block_exclusive_scan(s_cnt, nleaf, warp_tot);
@@ -376,7 +380,7 @@ __global__ void __launch_bounds__(kThreads) k_expand(EngineView v, int root_mode
     return;
   }
   ExpandWarpSmem& W = ws[warp];
-  for (int i = warp; i < nleaf; i += kWarps) {
+  for (int i = warp; i < nleaf; i += (int)(blockDim.x >> 5)) {
     const Visit e = leaves[i];
     const int q = lf[i].y;
     int final_node = e.node, ext = 0;
@@ -469,7 +473,7 @@ __global__ void __launch_bounds__(kThreads) k_expand(EngineView v, int root_mode
   }
   __syncthreads();
   if (!root_mode) {
-    for (int i = tid; i < nleaf; i += kThreads) {
+    for (int i = tid; i < nleaf; i += blockDim.x) {
       const int2 x = lf[i];
       v.q_entries[1][s_fbase + i] = make_int2(r, x.x);
       lf[i] = make_int2(x.x, (s_fbase + i) | (x.y & (1 << 30)));
@@ -504,15 +508,15 @@ __global__ void __launch_bounds__(kThreads) k_backup(EngineView v) {
   const Visit* leaves = v.leaves + (size_t)r * v.WCAP;
   const int2* lf = v.leaf_final + (size_t)r * v.WCAP;
   float* sv = v.simval + (size_t)r * v.WCAP;
-  for (int i = tid; i < nleaf; i += kThreads) {
+  for (int i = tid; i < nleaf; i += blockDim.x) {
     const Visit e = leaves[i];
     const float val = v.q_value[1][lf[i].y & ((1 << 30) - 1)];
     for (int s = e.lo; s < e.lo + e.k; ++s) sv[s] = val;
   }
   __syncthreads();
   const Visit* log = v.vlog + (size_t)r * v.LOGCAP;
-  for (int i = tid; i < nlog; i += kThreads) backup_node(v, base, sv, log[i]);
-  for (int i = tid; i < nleaf; i += kThreads) {
+  for (int i = tid; i < nlog; i += blockDim.x) backup_node(v, base, sv, log[i]);
+  for (int i = tid; i < nleaf; i += blockDim.x) {
     if (lf[i].y & (1 << 30)) {
       const Visit e = leaves[i];
       backup_node(v, base, sv, Visit{lf[i].x, e.lo, e.k, e.depth + 1});
@@ -567,16 +571,27 @@ __global__ void k_status(EngineView v, int32_t* status, int32_t* num_nodes) {
 // ---------------------------------------------------------------------------------------------
 // launchers
 // ---------------------------------------------------------------------------------------------
+static int tree_threads(const EngineView& v) {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  return v.R >= 2 * sms ? 256 : kThreads;
+}
+
 static size_t select_smem(const EngineView& v) {
   int p2 = 1;
   while (p2 < v.A) p2 <<= 1;
-  return ((sizeof(SelectShared) + 15) & ~(size_t)15) + (size_t)kWarps * p2 * 8 +
+  return ((sizeof(SelectShared) + 15) & ~(size_t)15) + (size_t)(tree_threads(v) / 32) * p2 * 8 +
          (size_t)v.WCAP * sizeof(Visit) + (size_t)v.WCAP * sizeof(int);
 }
 
 void launch_begin(const EngineView& v, const int8_t* boards, cudaStream_t s) {
   count_launches(1);
-  k_begin<<<v.R, kThreads, 0, s>>>(v, boards);
+  k_begin<<<v.R, tree_threads(v), 0, s>>>(v, boards);
 }
 
 void launch_select(const EngineView& v, int wave, cudaStream_t s) {
@@ -585,16 +600,18 @@ void launch_select(const EngineView& v, int wave, cudaStream_t s) {
     cudaFuncSetAttribute(k_select, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   cudaMemsetAsync(v.q_count, 0, sizeof(int32_t), s);
   count_launches(1);
-  k_select<<<v.R, kThreads, sm, s>>>(v, wave);
+  k_select<<<v.R, tree_threads(v), sm, s>>>(v, wave);
 }
 
 void launch_expand(const EngineView& v, int root_mode, cudaStream_t s) {
   if (!root_mode) cudaMemsetAsync(v.q_count + 1, 0, sizeof(int32_t), s);
   count_launches(1);
-  k_expand<<<v.R, kThreads, 0, s>>>(v, root_mode);
+  const int sm = (int)((tree_threads(v) / 32) * sizeof(ExpandWarpSmem));
+  cudaFuncSetAttribute(k_expand, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  k_expand<<<v.R, tree_threads(v), sm, s>>>(v, root_mode);
 }
 
-void launch_backup(const EngineView& v, cudaStream_t s) { k_backup<<<v.R, kThreads, 0, s>>>(v); }
+void launch_backup(const EngineView& v, cudaStream_t s) { k_backup<<<v.R, tree_threads(v), 0, s>>>(v); }
 
 void launch_root_visits(const EngineView& v, int32_t* visits, float* nw, cudaStream_t s) {
   count_launches(1);
