@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--workload", choices=["config1", "config2"], default="config1",
+                    help="config2 = batched self-play: 512 games (sharded), 800 sims, wave 64, 20x256")
     ap.add_argument("--evaluator", choices=["resnet", "synthetic"], default="resnet",
                     help="synthetic = BASELINE config 0 (tree kernels only; 800 sims, 200k nodes)")
     return ap.parse_args()
@@ -404,8 +406,78 @@ def run_b200_synthetic(args):
         dist.destroy_process_group()
 
 
+def run_b200_selfplay(args):
+    """512 concurrent self-play games sharded over the ranks (total fixed),
+    800 simulations per move, max_wave_size 64 (leaf batches up to games x 64), ResNet 20 x 256
+    bf16; one step = one move of every game (temperature-1 sampling from the visit policy)."""
+    from omoknuni_quantum_b200 import _lib, parallel
+    from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec, init_state_dict
+    from omoknuni_quantum_b200.selfplay import BatchedSelfPlay
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    games_total, sims, wave = 512, 800, 64
+    shard = parallel.shard_range(games_total, ws, rank)
+    G = len(shard)
+    spec = ResNetSpec(num_blocks=20, filters=256, fc_value_hidden=128)
+    sd = parallel.broadcast_state_dict(init_state_dict(spec, seed=args.seed), dev)
+    ev = ResNetEvaluator(sd, max_batch=G * wave, device=dev)
+    sp = BatchedSelfPlay(G, num_simulations=sims, wave_size=wave, evaluator=ev, capacity=200000,
+                         temperature=1.0, temperature_threshold=30, seed=args.seed * 1000 + rank,
+                         device=dev)
+    for _ in range(args.warmup):
+        sp.step()
+    torch.cuda.synchronize()
+    ev.profile(1 << 14)
+    n0 = _lib.kernel_launches()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        if ws > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        s0.record()
+        moved = 0
+        for _ in range(args.steps):
+            moved += sp.step()
+        s1.record()
+        torch.cuda.synchronize()
+    ms = parallel.max_over_ranks(s0.elapsed_time(s1), dev)
+    total_moves = parallel.sum_over_ranks(moved, dev)
+    trunk_ms, counts = ev.profile_read()
+    peaks, kind = measured_peaks()
+    launches = len(trunk_ms) * ev.conv_launches_per_call
+    flops = int(counts.sum()) * ev.trunk_flops_per_position()
+    avg_s = float(trunk_ms.sum()) / 1000.0 / max(1, launches)
+    achieved = flops / max(1, launches) / avg_s / 1e12 if avg_s > 0 else 0.0
+    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": total_moves * sims / (ms / 1000.0), "unit": UNIT, "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (empty-board self-play, seeded sampling, seeded He-init weights)",
+            "config": {"workload": "config2: batched Gomoku self-play, 512 games sharded across GPUs, "
+                                   "800 sims/move, wave 64, ResNet 20x256 bf16; step = one move of every game",
+                       "games_per_gpu": G, "global_batch": games_total, "parallelism": f"dp{ws}"},
+            "leaf_evals_per_s": int(counts.sum()) * ws / (ms / 1000.0),
+            "roofline": {"kernel": "k_conv3x3_pair<256> (cta_group::2 tcgen05 conv)", "bound": "tensor",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                         "peak_kind": f"bf16_tflops_sustained of {kind}", "traffic": None},
+            "cpu_baseline": None, "e2e": None, "clocks": clk.summary(),
+            "gpu_launches": _lib.kernel_launches() - n0}), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
+    if args.workload == "config2" and args.impl == "b200":
+        run_b200_selfplay(args)
+        return
     if args.evaluator == "synthetic" and args.impl == "b200":
         run_b200_synthetic(args)
         return

@@ -149,3 +149,14 @@ def test_virtual_loss_is_reverted_every_wave():
         t = eng.export_tree(0)
         assert (t["virtual_loss"] == 0).all()
         assert t["visits"][0] == t["visits"][t["parent"] == 0].sum()
+
+
+def test_selfplay_moves_match_oracle(oracle_lib):
+    """Each move's policy in batched device self-play equals the oracle's search of that board."""
+    from omoknuni_quantum_b200.selfplay import BatchedSelfPlay
+    sp = BatchedSelfPlay(4, num_simulations=96, wave_size=32, capacity=40000, seed=3)
+    recs = sp.play(3)
+    for r in recs:
+        for ex in r.examples:
+            o = oracle_lib.Oracle(40000).search(ex["state"], 96, 32)
+            assert np.array_equal(ex["policy"], o.policy)

@@ -1,0 +1,52 @@
+"""Self-play bookkeeping on CPU with a fake searcher: temperature sampling then arg-max,
+legal moves, five detection, outcome values from each player's perspective, reproducibility."""
+import numpy as np
+
+from omoknuni_quantum_b200.selfplay import BatchedSelfPlay, board_after, game_result
+
+
+def _fake_search(boards):
+    """Visits favour the lowest empty cell strongly, then the next ones (deterministic)."""
+    out = np.zeros((boards.shape[0], 225), np.int64)
+    for i, b in enumerate(boards):
+        empty = np.nonzero(b.reshape(-1) == 0)[0]
+        out[i, empty[:3]] = [50, 30, 20]
+    return out
+
+
+def test_selfplay_moves_values_and_determinism():
+    sp = BatchedSelfPlay(3, search=_fake_search, temperature_threshold=2, seed=7)
+    recs = sp.play(12)
+    for r in recs:
+        b = np.zeros((15, 15), np.int8)
+        for m in r.moves:
+            assert b.reshape(-1)[m] == 0
+            b = board_after(b, m)
+        assert len(r.examples) == len(r.moves)
+        # after the temperature moves the arg-max (the lowest empty cell) is played
+        assert r.moves[2] == min(np.nonzero(r.examples[2]["state"].reshape(-1) == 0)[0])
+        assert all(abs(e["policy"].sum() - 1) < 1e-12 for e in r.examples)
+    sp2 = BatchedSelfPlay(3, search=_fake_search, temperature_threshold=2, seed=7)
+    assert [r.moves for r in sp2.play(12)] == [r.moves for r in recs]
+    # arg-max play where black fills row 0 and white row 1: black's five ends the game at move 9
+    def rows(boards):
+        out = np.zeros((boards.shape[0], 225), np.int64)
+        for i, b in enumerate(boards):
+            row = 0 if int((b != 0).sum()) % 2 == 0 else 1
+            out[i, row * 15 + int((b[row] != 0).sum())] = 1
+        return out
+    sp3 = BatchedSelfPlay(1, search=rows, temperature_threshold=0)
+    r = sp3.play(20)[0]
+    assert r.finished and r.winner == 1 and len(r.moves) == 9
+    ex = r.training_examples()
+    assert all(e.value == (r.winner if i % 2 == 0 else -r.winner) for i, e in enumerate(ex))
+
+
+def test_game_result():
+    b = np.zeros((15, 15), np.int8)
+    assert game_result(b) is None
+    b[3, 2:7] = 1
+    b[9, 0:4] = 2
+    assert game_result(b) == 1
+    full = (1 + (np.add.outer(np.arange(15), 2 * np.arange(15)) % 4 >= 2)).astype(np.int8)
+    assert game_result(full) == 0
