@@ -686,6 +686,251 @@ __global__ void __launch_bounds__(TCfg::kThreads, 1)
   if (threadIdx.x == 0 && *abort_flag) atomicExch(args.error, OMQ_TIMEOUT);
 }
 
+// Halo variant for 128 filters: the 9 taps of a 3x3 conv read 9 row-shifted copies of the same
+// activation rows. Here one TMA load per 64-channel block brings the union of those rows (the
+// tile's 256 rows plus a (S+2)-row halo on each side, 304 rows) into shared memory once, and each
+// tap's UMMA reads a row-shifted window of it (the descriptor simply starts `off` rows in). The
+// weights still stream per tap.
+// L2 -> SM traffic per 256-row tile drops from 18 x (32 + 16) KB to 2 x 38 KB + 18 x 16 KB.
+struct HaloCfg {
+  static constexpr int kRows = 256;                          // output rows per tile
+  static constexpr int kLead = 24;                           // halo rows before the tile (>= S+2, multiple of 8)
+  static constexpr int kHaloRows = 304;                      // kLead + 256 + 24
+  static constexpr int kHaloBox = 152;                       // two TMA boxes of 152 rows
+  static constexpr int kA = kHaloRows * 128;                 // 38,912 B
+  static constexpr int kAStages = 2;
+  static constexpr int kB = 128 * 128;                       // one tap's weights, 16 KB
+  static constexpr int kBStages = 6;
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kTmemCols = 512;                      // 2 buffers x 2 sub-tiles x 128
+  static constexpr int kStaging = kEpiWarps * 2 * 2048;
+  static constexpr int kSmem = kAStages * kA + kBStages * kB + kStaging + 1024 + 512 + 128 * 4;
+  static_assert(kSmem <= 232448, "227 KB of shared memory per CTA");
+};
+
+__global__ void __launch_bounds__(HaloCfg::kThreads, 1)
+    k_conv3x3_halo(const __grid_constant__ CUtensorMap tmH, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmO, ConvArgs args) {
+  using Cfg = HaloCfg;
+  constexpr int BN = 128;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* a_ring = smem;                                     // 2 x 38,912 (38 x 1024)
+  uint8_t* b_ring = smem + Cfg::kAStages * Cfg::kA;           // 6 x 16 KB
+  uint8_t* staging = b_ring + Cfg::kBStages * Cfg::kB;
+  uint64_t* afull = reinterpret_cast<uint64_t*>(staging + Cfg::kStaging);
+  uint64_t* aempty = afull + Cfg::kAStages;
+  uint64_t* bfull = aempty + Cfg::kAStages;
+  uint64_t* bempty = bfull + Cfg::kBStages;
+  uint64_t* tfull = bempty + Cfg::kBStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_bias = reinterpret_cast<float*>(staging + Cfg::kStaging + 512);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_pos = args.d_count ? min(*args.d_count, args.count) : args.count;
+  const int rows = n_pos * args.P;
+  const int tiles = (rows + Cfg::kRows - 1) / Cfg::kRows;
+  const int CB = args.kb_per_tap;
+  const int rowstride = args.S + 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kAStages; ++s) { ptx::mbar_init(&afull[s], 1); ptx::mbar_init(&aempty[s], 1); }
+    for (int s = 0; s < Cfg::kBStages; ++s) { ptx::mbar_init(&bfull[s], 1); ptx::mbar_init(&bempty[s], 1); }
+    for (int i = 0; i < 2; ++i) { ptx::mbar_init(&tfull[i], 1); ptx::mbar_init(&tempty[i], Cfg::kEpiWarps); }
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    ptx::fence_barrier_init();
+    ptx::prefetch_tmap(&tmH);
+    ptx::prefetch_tmap(&tmB);
+    ptx::prefetch_tmap(&tmO);
+  }
+  for (int i = threadIdx.x; i < BN; i += blockDim.x) s_bias[i] = args.bias[i];
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer: per 64-channel block one halo, then 9 weight taps -------
+    int sa = 0, sb = 0;
+    uint32_t pa = 0, pb = 0;
+    int a_issued[Cfg::kAStages], b_issued[Cfg::kBStages];
+    for (int i = 0; i < Cfg::kAStages; ++i) a_issued[i] = -1;
+    for (int i = 0; i < Cfg::kBStages; ++i) b_issued[i] = -1;
+    for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+      const int h0 = tile * Cfg::kRows - Cfg::kLead;
+      for (int cb = 0; cb < CB; ++cb) {
+        if (!ptx::mbar_wait(&aempty[sa], pa ^ 1, abort_flag, kWaitLimitNs)) goto producer_done;
+        ptx::mbar_arrive_expect_tx(&afull[sa], Cfg::kA);
+        uint8_t* dst = a_ring + sa * Cfg::kA;
+        ptx::tma_load_2d(dst, &tmH, &afull[sa], cb * kBlockK, h0);
+        ptx::tma_load_2d(dst + Cfg::kHaloBox * 128, &tmH, &afull[sa], cb * kBlockK, h0 + Cfg::kHaloBox);
+        a_issued[sa] = (int)pa;
+        if (++sa == Cfg::kAStages) { sa = 0; pa ^= 1; }
+        for (int tap = 0; tap < 9; ++tap) {
+          if (!ptx::mbar_wait(&bempty[sb], pb ^ 1, abort_flag, kWaitLimitNs)) goto producer_done;
+          ptx::mbar_arrive_expect_tx(&bfull[sb], Cfg::kB);
+          ptx::tma_load_2d(b_ring + sb * Cfg::kB, &tmB, &bfull[sb], (tap * CB + cb) * kBlockK, 0);
+          b_issued[sb] = (int)pb;
+          if (++sb == Cfg::kBStages) { sb = 0; pb ^= 1; }
+        }
+      }
+    }
+  producer_done:
+    for (int i = 0; i < Cfg::kAStages; ++i)
+      if (a_issued[i] >= 0) {
+        volatile int dummy = 0;
+        ptx::mbar_wait(&afull[i], (uint32_t)a_issued[i], &dummy, kWaitLimitNs);
+      }
+    for (int i = 0; i < Cfg::kBStages; ++i)
+      if (b_issued[i] >= 0) {
+        volatile int dummy = 0;
+        ptx::mbar_wait(&bfull[i], (uint32_t)b_issued[i], &dummy, kWaitLimitNs);
+      }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    constexpr uint32_t idesc = ptx::idesc_bf16_f32(kTileM, BN);
+    int sa = 0, sb = 0;
+    uint32_t pa = 0, pb = 0;
+    bool any = false;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+      const int ab = t & 1;
+      const uint32_t aph = (t >> 1) & 1;
+      if (!ptx::mbar_wait(&tempty[ab], aph ^ 1, abort_flag, kWaitLimitNs)) break;
+      ptx::tc_fence_after();
+      const uint32_t d = tmem + ab * 2 * BN;
+      bool ok = true;
+      for (int cb = 0; cb < CB && ok; ++cb) {
+        if (!ptx::mbar_wait(&afull[sa], pa, abort_flag, kWaitLimitNs)) { ok = false; break; }
+        ptx::tc_fence_after();
+        const uint32_t a_base = ptx::smem_u32(a_ring + sa * Cfg::kA);
+        for (int tap = 0; tap < 9; ++tap) {
+          if (!ptx::mbar_wait(&bfull[sb], pb, abort_flag, kWaitLimitNs)) { ok = false; break; }
+          ptx::tc_fence_after();
+          const int off = Cfg::kLead + (tap / 3 - 1) * rowstride + (tap % 3 - 1);
+          const uint32_t b_addr = ptx::smem_u32(b_ring + sb * Cfg::kB);
+#pragma unroll
+          for (int k = 0; k < kBlockK / 16; ++k) {
+            const uint64_t bdesc = ptx::smem_desc_sw128(b_addr + k * 32);
+#pragma unroll
+            for (int sub = 0; sub < 2; ++sub)
+              ptx::mma_bf16(d + sub * BN, ptx::smem_desc_sw128_rows(a_base, off + sub * kTileM, k * 32),
+                            bdesc, idesc, (cb | tap | k) != 0);
+          }
+          any = true;
+          ptx::mma_commit(&bempty[sb]);
+          if (++sb == Cfg::kBStages) { sb = 0; pb ^= 1; }
+        }
+        if (!ok) break;
+        ptx::mma_commit(&aempty[sa]);
+        if (++sa == Cfg::kAStages) { sa = 0; pa ^= 1; }
+      }
+      if (!ok) break;
+      ptx::mma_commit(&tfull[ab]);
+    }
+    if (any) {
+      ptx::mma_commit(drain);
+      volatile int dummy = 0;
+      ptx::mbar_wait(drain, 0, &dummy, kWaitLimitNs);
+    }
+  } else if (warp >= 2) {
+    // ---------------- epilogue: warp 2 + 4*sub + q handles rows sub*128 + 32q .. +31 ----------
+    // Each 32 rows x 32 channels chunk is staged in shared memory (64-byte swizzle, two buffers
+    // per warp) and written by one TMA store, instead of 32 scattered 16-byte row stores.
+    const int sub = (warp - 2) >> 2;
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    uint8_t* my_stage = staging + (warp - 2) * 2 * 2048;
+    int buf = 0;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+      const int ab = t & 1;
+      const uint32_t aph = (t >> 1) & 1;
+      if (!ptx::mbar_wait(&tfull[ab], aph, abort_flag, kWaitLimitNs)) break;
+      ptx::tc_fence_after();
+      const int row0 = tile * Cfg::kRows + sub * kTileM + q * 32;
+      const int m = row0 + lane;
+      const bool valid = m < rows;
+      const int pix = m % args.P;
+      const int y = pix / rowstride, x = pix - y * rowstride;
+      const bool pad = !valid || (y == args.S) || (x == args.S);
+      const __nv_bfloat16* rrow = args.residual ? args.residual + (size_t)m * BN : nullptr;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + ab * 2 * BN + sub * BN + c0, r);
+        ptx::tmem_ld_wait();
+        uint4 packed[4];
+        uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
+        if (pad) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) pw[j] = 0u;
+        } else {
+          float res[32];
+          if (rrow) {
+            const uint4* rp = reinterpret_cast<const uint4*>(rrow + c0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 u = rp[j];
+              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                float2 f = __bfloat1622float2(h[e]);
+                res[8 * j + 2 * e] = f.x;
+                res[8 * j + 2 * e + 1] = f.y;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) res[j] = 0.0f;
+          }
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            float v0 = __uint_as_float(r[j]) + s_bias[c0 + j] + res[j];
+            float v1 = __uint_as_float(r[j + 1]) + s_bias[c0 + j + 1] + res[j + 1];
+            if (args.relu) { v0 = fmaxf(v0, 0.0f); v1 = fmaxf(v1, 0.0f); }
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
+            pw[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+        }
+        // the buffer about to be written must no longer be read by an earlier store
+        if (lane == 0) ptx::bulk_wait_read<1>();
+        __syncwarp();
+        uint8_t* sb = my_stage + buf * 2048;
+        const int sw = (lane >> 1) & 3;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(sb + lane * 64 + ((j ^ sw) * 16)) = packed[j];
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          ptx::tma_store_2d(&tmO, sb, c0, row0);
+          ptx::bulk_commit();
+        }
+        buf ^= 1;
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&tempty[ab]);
+    }
+    if (lane == 0) ptx::bulk_wait<0>();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(args.error, OMQ_TIMEOUT);
+}
+
 // Sub-tiles per CTA tile for a given filter count (must match the A tensor maps' box height).
 __host__ __device__ constexpr int conv_sub(int filters) { return filters == 128 ? 2 : 1; }
 
@@ -918,22 +1163,23 @@ static int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t o
   return OMQ_OK;
 }
 
-// Conv kernel variant per filter count (OMQ_CONV_KERNEL=single|pair|transposed forces one, for
-// measurements): 0 = single-CTA kernel, 1 = CTA-pair kernel (default for 256 filters, measured
-// 1.10 vs 1.01 PFLOP/s), 2 = transposed kernel (128 filters only).
+// Conv kernel variant per filter count (OMQ_CONV_KERNEL=single|pair|transposed|halo forces one,
+// for measurements): 0 = single CTA, 1 = CTA pair (default for 256 filters: 1.16 vs 1.07 PFLOP/s),
+// 2 = transposed, 3 = halo (default for 128 filters: 1.00 vs 0.94 PFLOP/s at batch 4096).
 static int conv_variant(int filters) {
   const char* v = getenv("OMQ_CONV_KERNEL");
   if (v && strcmp(v, "single") == 0) return 0;
   if (v && strcmp(v, "pair") == 0) return 1;
   if (v && strcmp(v, "transposed") == 0 && filters == 128) return 2;
-  return filters == 256 ? 1 : 0;
+  if (v && strcmp(v, "halo") == 0 && filters == 128) return 3;
+  return filters == 256 ? 1 : 3;
 }
 
 // Tensor maps of a net's activation buffers and weights. Box heights follow the kernel variant:
 // A boxes are 128 rows (pair) or 128 * conv_sub(C) rows (single CTA); weight boxes are the CTA's
 // half of the output channels (pair) or all of them.
 static int build_maps(omq_resnet* n) {
-  const uint32_t a_rows = n->pair == 1 ? kTileM : kTileM * conv_sub(n->C);
+  const uint32_t a_rows = n->pair == 1 ? kTileM : n->pair == 3 ? HaloCfg::kHaloBox : kTileM * conv_sub(n->C);
   const uint32_t b_rows = n->pair == 1 ? n->C / 2 : n->C;
   int st = make_map(&n->tmA_in, n->x_in, kInPad, n->rows, a_rows);
   for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n->tmA[i], n->act[i], n->C, n->rows, a_rows);
@@ -1097,6 +1343,27 @@ static int launch_conv(const omq_resnet* n, const CUtensorMap& tA, const CUtenso
   return cuda_status(cudaGetLastError(), "k_conv3x3");
 }
 
+static int launch_conv_halo(const omq_resnet* n, const CUtensorMap& tH, const CUtensorMap& tB,
+                            const CUtensorMap& tO, const float* bias, const __nv_bfloat16* res,
+                            __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count, int count,
+                            cudaStream_t s) {
+  static int attr_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (attr_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(k_conv3x3_halo, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         HaloCfg::kSmem);
+    if (e != cudaSuccess) return cuda_status(e, "halo conv smem attribute");
+    attr_dev = dev;
+  }
+  ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
+  const int max_tiles = (int)((n->rows + HaloCfg::kRows - 1) / HaloCfg::kRows);
+  const int grid = max(1, min(max_tiles, n->sm_count));
+  count_launches(1);
+  k_conv3x3_halo<<<grid, HaloCfg::kThreads, HaloCfg::kSmem, s>>>(tH, tB, tO, a);
+  return cuda_status(cudaGetLastError(), "k_conv3x3_halo");
+}
+
 static int launch_conv_t(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB,
                          const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
                          int kb_per_tap, const int32_t* d_count, int count, cudaStream_t s) {
@@ -1143,6 +1410,7 @@ static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& t
                 const float* bias,
                 const __nv_bfloat16* res, __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count,
                 int count, cudaStream_t s) {
+  if (n->pair == 3) return launch_conv_halo(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
   if (n->pair == 2) return launch_conv_t(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
   if (n->pair == 1) {
     if (n->C == 128) return launch_conv_pair<128>(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);

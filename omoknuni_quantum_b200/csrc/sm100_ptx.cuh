@@ -176,6 +176,14 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
   return d;
 }
 
+// Descriptor of a K-major 128B-swizzled tile that starts `row` 128-byte rows (any row, not only
+// multiples of 8) into a 1024-byte-aligned buffer written by TMA. The swizzle phase follows from
+// the absolute shared-memory address, as with TMA's own swizzle, so the base-offset field stays
+// 0 (measured on B200: setting it to row & 7 gives wrong products).
+__device__ __forceinline__ uint64_t smem_desc_sw128_rows(uint32_t aligned_base, int row, int kbytes) {
+  return smem_desc_sw128(aligned_base + (uint32_t)row * 128u + (uint32_t)kbytes);
+}
+
 // Instruction descriptor of kind::f16: D fp32, A/B bf16, both K-major, shape M x N.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
   return (1u << 4)                      // D format: f32
