@@ -62,6 +62,13 @@ typedef struct {
   float virtual_loss;       /* positive; applied as -|virtual_loss| (mcts.py:643) */
   int32_t enable_virtual_loss;
   int32_t device;           /* CUDA device ordinal */
+  /* Root Dirichlet noise (wave_search.py:1160-1170): when dirichlet_epsilon > 0, every wave's
+   * root selection mixes one fresh Dirichlet(alpha) vector into the root priors,
+   * P' = (1 - eps) * P + eps * noise. Drawn on the device from a counter-based generator keyed by
+   * (noise_seed, search, wave, tree, child); 0 disables. */
+  float dirichlet_alpha;
+  float dirichlet_epsilon;
+  uint64_t noise_seed;
 } omq_engine_config;
 
 OMQ_API const char* omq_status_string(int status);
@@ -125,6 +132,10 @@ OMQ_API int omq_search_synthetic(omq_engine* e, const int8_t* d_boards, int32_t 
  * (d_root_nw float [num_trees][2]). Replaces tree_ops.get_root_children_info
  * (tree_operations.py:154-187). */
 OMQ_API int omq_root_visits(omq_engine* e, int32_t* d_visits, float* d_root_nw, void* stream);
+
+/* The Dirichlet noise the last wave mixed into each root's priors, scattered by action:
+ * d_noise fp32 [num_trees][actions] (0 where the root has no child or noise is off). */
+OMQ_API int omq_root_noise(omq_engine* e, float* d_noise, void* stream);
 
 /* Device status word and node count of each tree: d_status int32 [num_trees],
  * d_num_nodes int32 [num_trees]. */

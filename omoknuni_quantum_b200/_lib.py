@@ -39,7 +39,8 @@ class EngineConfig(ctypes.Structure):
                 ("capacity", ctypes.c_int32), ("max_wave_size", ctypes.c_int32),
                 ("max_depth", ctypes.c_int32), ("c_puct", ctypes.c_float),
                 ("virtual_loss", ctypes.c_float), ("enable_virtual_loss", ctypes.c_int32),
-                ("device", ctypes.c_int32)]
+                ("device", ctypes.c_int32), ("dirichlet_alpha", ctypes.c_float),
+                ("dirichlet_epsilon", ctypes.c_float), ("noise_seed", ctypes.c_uint64)]
 
 
 class ResNetConfig(ctypes.Structure):
@@ -73,6 +74,7 @@ SIGNATURES = {
     "omq_search_synthetic": [_P, _P, _I, _P],
     "omq_root_visits": [_P, _P, _P, _P],
     "omq_tree_status": [_P, _P, _P, _P],
+    "omq_root_noise": [_P, _P, _P],
     "omq_export_tree": [_P, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P],
     "omq_resnet_create": [ctypes.POINTER(ResNetConfig), ctypes.POINTER(_P)],
     "omq_resnet_destroy": [_P],

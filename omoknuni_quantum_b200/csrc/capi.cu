@@ -67,6 +67,10 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   if (!cfg || !out) { set_error("null argument"); return OMQ_BAD_ARG; }
   *out = nullptr;
   const omq_engine_config c = *cfg;
+  if (c.dirichlet_epsilon > 0 && !(c.dirichlet_alpha > 0)) {
+    set_error("dirichlet_alpha must be > 0 when dirichlet_epsilon > 0");
+    return OMQ_BAD_ARG;
+  }
   if (c.num_trees < 1 || c.board_size < 5 || c.board_size > 19 || c.capacity < 2 ||
       c.max_wave_size < 1 || c.max_wave_size > 1024 || c.max_depth < 2 || c.max_depth > 127) {
     set_error("bad engine config: trees=%d board=%d capacity=%d wave=%d depth=%d", c.num_trees,
@@ -89,8 +93,12 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   v.enable_vl = c.enable_virtual_loss ? 1 : 0;
   v.c_puct = c.c_puct;
   v.vl_value = -(c.virtual_loss < 0 ? -c.virtual_loss : c.virtual_loss);
+  v.noise_alpha = c.dirichlet_alpha;
+  v.noise_eps = c.dirichlet_epsilon > 0 ? c.dirichlet_epsilon : 0.0f;
+  v.noise_keep = (float)(1.0 - (double)v.noise_eps);
+  v.noise_seed = c.noise_seed;
   const size_t R = v.R, T = v.T, W = v.WCAP, QC = R * W;
-  size_t off[20], n = 0, tot = 0;
+  size_t off[24], n = 0, tot = 0;
   auto take = [&](size_t bytes) { off[n++] = tot; tot += align256(bytes); };
   take(R * T * sizeof(NodeStats));            // 0 stats
   take(R * T * sizeof(NodeTopo));             // 1 topo
@@ -108,6 +116,7 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   take(QC * sizeof(float));                   // 13 value expand
   take(QC * sizeof(float));                   // 14 value final
   take(2 * sizeof(int32_t));                  // 15 counts
+  take(R * (size_t)v.A * sizeof(float));      // 16 root noise
   void* arena = nullptr;
   cudaError_t err = cudaMalloc(&arena, tot);
   if (err != cudaSuccess) {
@@ -131,8 +140,10 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   v.q_value[0] = reinterpret_cast<float*>(b + off[13]);
   v.q_value[1] = reinterpret_cast<float*>(b + off[14]);
   v.q_count = reinterpret_cast<int32_t*>(b + off[15]);
+  v.root_noise = reinterpret_cast<float*>(b + off[16]);
   err = cudaMemset(v.hdr, 0, R * sizeof(TreeHeader));
   if (err == cudaSuccess) err = cudaMemset(v.q_count, 0, 2 * sizeof(int32_t));
+  if (err == cudaSuccess) err = cudaMemset(v.root_noise, 0, R * (size_t)v.A * sizeof(float));
   if (err != cudaSuccess) {
     cudaFree(arena);
     delete e;
@@ -162,7 +173,7 @@ int omq_engine_memory(const omq_engine* e, uint64_t* bytes) {
 int omq_begin(omq_engine* e, const int8_t* d_boards, void* stream) {
   if (!e || !d_boards) { set_error("null argument"); return OMQ_BAD_ARG; }
   DeviceGuard g(e->cfg.device);
-  launch_begin(e->v, d_boards, (cudaStream_t)stream);
+  launch_begin(e->v, d_boards, e->searches++, (cudaStream_t)stream);
   OMQ_CHECK_LAUNCH("omq_begin");
   e->phase = 1;
   return OMQ_OK;
@@ -245,6 +256,14 @@ int omq_queue_eval_synthetic(omq_engine* e, int32_t queue, void* stream) {
   launch_synth_eval(e->v, queue, (cudaStream_t)stream);
   OMQ_CHECK_LAUNCH("omq_queue_eval_synthetic");
   return OMQ_OK;
+}
+
+int omq_root_noise(omq_engine* e, float* d_noise, void* stream) {
+  if (!e || !d_noise) { set_error("null argument"); return OMQ_BAD_ARG; }
+  DeviceGuard g(e->cfg.device);
+  return cuda_status(cudaMemcpyAsync(d_noise, e->v.root_noise, sizeof(float) * e->v.R * e->v.A,
+                                     cudaMemcpyDeviceToDevice, (cudaStream_t)stream),
+                     "omq_root_noise");
 }
 
 int omq_tree_status(omq_engine* e, int32_t* d_status, int32_t* d_num_nodes, void* stream) {

@@ -60,7 +60,9 @@ struct TreeHeader {
   int32_t fin_off;
   int32_t fin_cnt;
   int32_t wave;
-  int32_t pad[4];
+  int32_t wave_idx;      // waves run in the current search (root-noise counter)
+  int32_t search_idx;    // searches begun on this engine (root-noise counter)
+  int32_t pad[2];
 };
 
 constexpr int kPlanes = 19;
@@ -72,6 +74,9 @@ constexpr int kMaxWords = 6;  // ceil(361 / 64)
 struct EngineView {
   int R, T, S, C, A, WCAP, LOGCAP, max_depth, enable_vl;
   float c_puct, vl_value;
+  float noise_alpha, noise_eps, noise_keep;  // keep = (float)(1 - (double)eps), as the reference rounds it
+  uint64_t noise_seed;
+  float* root_noise;     // [R][A] noise of the last wave, by action
   NodeStats* stats;      // [R*T]
   NodeTopo* topo;        // [R*T]
   int8_t* root_board;    // [R*C]
@@ -150,6 +155,7 @@ struct omq_engine {
   omq::EngineView v;
   int32_t wave;          // wave size of the wave in flight
   int32_t phase;         // 0 idle, 1 begun, 2 root expanded, 3 selected, 4 expanded
+  int32_t searches;      // omq_begin calls so far
   uint64_t bytes;
   void* arena;           // single device allocation backing every buffer
 };
@@ -174,7 +180,7 @@ void set_error(const char* fmt, ...);
 void count_launches(int n);
 int cuda_status(cudaError_t e, const char* what);
 
-void launch_begin(const EngineView& v, const int8_t* boards, cudaStream_t s);
+void launch_begin(const EngineView& v, const int8_t* boards, int search_id, cudaStream_t s);
 void launch_select(const EngineView& v, int wave, cudaStream_t s);
 void launch_expand(const EngineView& v, int root_mode, cudaStream_t s);
 void launch_backup(const EngineView& v, cudaStream_t s);

@@ -130,7 +130,7 @@ __device__ void warp_sort_desc(unsigned long long* keys, int p2) {
 // ---------------------------------------------------------------------------------------------
 // begin: reset trees, install roots, queue the roots for the forced root expansion
 // ---------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads) k_begin(EngineView v, const int8_t* boards) {
+__global__ void __launch_bounds__(kThreads) k_begin(EngineView v, const int8_t* boards, int search_id) {
   const int r = blockIdx.x, tid = threadIdx.x;
   __shared__ int8_t sb[kMaxCells];
   __shared__ int s_stones, s_five;
@@ -159,6 +159,8 @@ __global__ void __launch_bounds__(kThreads) k_begin(EngineView v, const int8_t* 
     h.nleaves = 1;
     h.exp_off = r;
     h.exp_cnt = 1;
+    h.wave_idx = 0;
+    h.search_idx = search_id;
     v.hdr[r] = h;
     const size_t base = (size_t)r * v.T;
     v.stats[base] = NodeStats{0, 0.0f, 1.0f, 0};
@@ -168,6 +170,37 @@ __global__ void __launch_bounds__(kThreads) k_begin(EngineView v, const int8_t* 
     v.q_entries[0][r] = make_int2(r, 0);
     if (r == 0) { v.q_count[0] = v.R; v.q_count[1] = 0; }
   }
+}
+
+// ---------------------------------------------------------------------------------------------
+// root Dirichlet noise
+// ---------------------------------------------------------------------------------------------
+// Uniform in (0, 1) from a 64-bit counter hash (24 significant bits).
+__device__ __forceinline__ float unit_uniform(uint64_t key) {
+  return ((float)(mix64(key) >> 40) + 0.5f) * (1.0f / 16777216.0f);
+}
+
+// Gamma(alpha, 1) by Marsaglia & Tsang (2000, "A simple method for generating gamma variables"),
+// with the alpha < 1 boost Gamma(alpha) = Gamma(alpha + 1) * U^(1/alpha). Normal deviates by
+// Box-Muller. The rejection loop is bounded (16 rounds; acceptance is > 95% per round), after
+// which the mode of Gamma(alpha + 1) stands in.
+__device__ float gamma_sample(uint64_t key, float alpha) {
+  const float a = alpha < 1.0f ? alpha + 1.0f : alpha;
+  const float d = a - 1.0f / 3.0f;
+  const float c = rsqrtf(9.0f * d);
+  float g = d;
+  for (int it = 0; it < 16; ++it) {
+    const uint64_t k = key + 0x9E3779B97F4A7C15ull * (uint64_t)(4 * it + 1);
+    const float u1 = unit_uniform(k), u2 = unit_uniform(k + 1);
+    const float x = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+    float t = 1.0f + c * x;
+    if (t <= 0.0f) continue;
+    t = t * t * t;
+    const float u = unit_uniform(k + 2);
+    if (logf(u) < 0.5f * x * x + d - d * t + d * logf(t)) { g = d * t; break; }
+  }
+  if (alpha < 1.0f) g *= powf(unit_uniform(key ^ 0xA0761D6478BD642Full), 1.0f / alpha);
+  return g;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -236,9 +269,38 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
       }
       const int cs = tp.child_start;
       const int32_t np = v.stats[base + e.node].N;
-      for (int j = lane; j < n; j += 32) {
-        const NodeStats st = v.stats[base + cs + j];
-        keys[j] = rank_key(ucb_score(st, np, v.c_puct, v.vl_value, v.enable_vl), j);
+      if (e.node == 0 && v.noise_eps > 0.0f) {
+        // One Dirichlet(alpha) vector per wave at the root (wave_search.py:1160-1170): gamma draws
+        // normalised in the engine's fixed summation order (lane-strided partials, butterfly).
+        float g[12];
+        float part = 0.0f;
+        const uint64_t wkey = v.noise_seed ^ mix64(((uint64_t)(uint32_t)H->search_idx << 32) |
+                                                   (uint32_t)H->wave_idx) ^ mix64((uint64_t)r + 0x51ED27ull);
+#pragma unroll
+        for (int t = 0; t < 12; ++t) {
+          const int j = lane + 32 * t;
+          g[t] = j < n ? gamma_sample(mix64(wkey + (uint64_t)j * 0xD1B54A32D192ED03ull), v.noise_alpha) : 0.0f;
+          part = __fadd_rn(part, g[t]);
+        }
+        for (int o = 16; o > 0; o >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xFFFFFFFFu, part, o));
+        float* out = v.root_noise + (size_t)r * v.A;
+        for (int a = lane; a < v.A; a += 32) out[a] = 0.0f;
+        __syncwarp();
+#pragma unroll
+        for (int t = 0; t < 12; ++t) {
+          const int j = lane + 32 * t;
+          if (j >= n) continue;
+          const float noise = __fdiv_rn(g[t], part);
+          NodeStats st = v.stats[base + cs + j];
+          st.P = __fadd_rn(__fmul_rn(v.noise_keep, st.P), __fmul_rn(v.noise_eps, noise));
+          keys[j] = rank_key(ucb_score(st, np, v.c_puct, v.vl_value, v.enable_vl), j);
+          out[topo_action(v.topo[base + cs + j])] = noise;
+        }
+      } else {
+        for (int j = lane; j < n; j += 32) {
+          const NodeStats st = v.stats[base + cs + j];
+          keys[j] = rank_key(ucb_score(st, np, v.c_puct, v.vl_value, v.enable_vl), j);
+        }
       }
       __syncwarp();
       if (e.k <= n && e.k <= 8) {
@@ -326,6 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
     H->exp_off = qbase;
     H->exp_cnt = nexp;
     H->wave = wave;
+    H->wave_idx += 1;
     if (sh.overflow) H->status = OMQ_QUEUE_OVERFLOW;
   }
 }
@@ -589,9 +652,9 @@ static size_t select_smem(const EngineView& v) {
          (size_t)v.WCAP * sizeof(Visit) + (size_t)v.WCAP * sizeof(int);
 }
 
-void launch_begin(const EngineView& v, const int8_t* boards, cudaStream_t s) {
+void launch_begin(const EngineView& v, const int8_t* boards, int search_id, cudaStream_t s) {
   count_launches(1);
-  k_begin<<<v.R, tree_threads(v), 0, s>>>(v, boards);
+  k_begin<<<v.R, tree_threads(v), 0, s>>>(v, boards, search_id);
 }
 
 void launch_select(const EngineView& v, int wave, cudaStream_t s) {

@@ -32,7 +32,8 @@ def _stream_ptr(stream=None) -> ctypes.c_void_p:
 class WaveEngine:
     def __init__(self, num_trees: int, board_size: int = 15, capacity: int = 200000,
                  max_wave_size: int = 256, c_puct: float = 1.4, virtual_loss: float = 1.0,
-                 enable_virtual_loss: bool = True, max_depth: int = 100, device=None):
+                 enable_virtual_loss: bool = True, max_depth: int = 100, device=None,
+                 dirichlet_alpha: float = 0.3, dirichlet_epsilon: float = 0.0, noise_seed: int = 0):
         if not torch.cuda.is_available():
             raise RuntimeError("WaveEngine needs a CUDA device (B200); there is no CPU fallback")
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -46,7 +47,9 @@ class WaveEngine:
         self.max_wave_size = int(max_wave_size)
         cfg = _lib.EngineConfig(self.num_trees, self.board_size, self.capacity, self.max_wave_size,
                                 int(max_depth), float(c_puct), float(virtual_loss),
-                                int(bool(enable_virtual_loss)), dev.index or 0)
+                                int(bool(enable_virtual_loss)), dev.index or 0,
+                                float(dirichlet_alpha), float(dirichlet_epsilon),
+                                int(noise_seed) & 0xFFFFFFFFFFFFFFFF)
         self.cfg = cfg
         h = ctypes.c_void_p()
         with torch.cuda.device(dev):
@@ -191,6 +194,14 @@ class WaveEngine:
                                           ctypes.c_void_p(self._root_nw.data_ptr()), _stream_ptr()),
                    "omq_root_visits")
         return self._visits
+
+    def root_noise(self) -> torch.Tensor:
+        """fp32 [num_trees, actions]: the Dirichlet noise mixed into each root's priors by the last
+        wave (zeros when the noise is off)."""
+        out = torch.zeros(self.num_trees, self.actions, dtype=torch.float32, device=self.device)
+        _lib.check(self.L.omq_root_noise(self._h, ctypes.c_void_p(out.data_ptr()), _stream_ptr()),
+                   "omq_root_noise")
+        return out
 
     def root_nw(self) -> torch.Tensor:
         self.root_visits()

@@ -66,6 +66,9 @@ class MCTS:
         dev = config.device if config.device != "cpu" else "cuda"
         self.device = torch.device(dev)   # device index resolved when the first engine is made
         self._engines: Dict[int, WaveEngine] = {}
+        # root-noise generator seed, drawn from numpy's global RNG (the reference draws the noise
+        # itself from torch's global RNG)
+        self._noise_seed = int(np.random.randint(0, 2 ** 62))
         self._last_tree = None          # (engine, index) of the last single search
         self._root_state = None
         self.stats = dict(total_searches=0, total_simulations=0, total_time=0.0,
@@ -88,7 +91,9 @@ class MCTS:
             eng = WaveEngine(num_trees, board_size=c.board_size, capacity=c.tree_capacity,
                              max_wave_size=c.max_wave_size, c_puct=c.c_puct,
                              virtual_loss=c.virtual_loss, enable_virtual_loss=c.enable_virtual_loss,
-                             max_depth=c.max_depth, device=self.device)
+                             max_depth=c.max_depth, device=self.device,
+                             dirichlet_alpha=c.dirichlet_alpha, dirichlet_epsilon=c.dirichlet_epsilon,
+                             noise_seed=self._noise_seed)
             self._engines[num_trees] = eng
         return eng
 

@@ -27,6 +27,8 @@ struct Tree {
   std::vector<int8_t> player, boards;
   oracle_result res{};
   std::vector<float> feat, pol, val;
+  std::vector<float> root_noise;  // by action, for the next wave only
+  float noise_eps = 0.0f, noise_keep = 1.0f;
 
   Tree(int cap_, int size_) : cap(cap_), size(size_), cells(size_ * size_), actions(size_ * size_) {
     N.assign(cap, 0); VL.assign(cap, 0); parent.assign(cap, -2); action.assign(cap, -1);
@@ -164,6 +166,15 @@ struct Tree {
         const int n = (int)kids.size(), k = (int)sims.size();
         std::vector<float> sc(n);
         for (int i = 0; i < n; ++i) sc[i] = score(kids[i], N[p]);
+        if (p == 0 && !root_noise.empty()) {  // (1 - eps) * valid_priors + eps * noise
+          for (int i = 0; i < n; ++i) {
+            const int c = kids[i];
+            const float saved = P[c];
+            P[c] = noise_keep * P[c] + noise_eps * root_noise[action[c]];
+            sc[i] = score(c, N[p]);
+            P[c] = saved;
+          }
+        }
         std::vector<int> order(n);
         for (int i = 0; i < n; ++i) order[i] = i;
         std::stable_sort(order.begin(), order.end(),
@@ -241,6 +252,7 @@ struct Tree {
           VL[n] = std::max(VL[n] - 1, 0);
         }
     res.waves++;
+    root_noise.clear();
     return 0;
   }
 };
@@ -258,6 +270,14 @@ void oracle_tree_destroy(void* t) { delete static_cast<Tree*>(t); }
 
 int oracle_begin(void* t, const oracle_config* cfg, const int8_t* root, oracle_eval_fn e, void* x) {
   return static_cast<Tree*>(t)->begin(cfg, root, e, x);
+}
+
+int oracle_set_root_noise(void* t, float eps, float keep, const float* noise) {
+  Tree* tr = static_cast<Tree*>(t);
+  tr->noise_eps = eps;
+  tr->noise_keep = keep;
+  tr->root_noise.assign(noise, noise + tr->actions);
+  return 0;
 }
 
 int oracle_wave(void* t, int w) {

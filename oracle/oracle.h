@@ -55,6 +55,10 @@ int oracle_begin(void* tree, const oracle_config* cfg, const int8_t* root_board,
                  oracle_eval_fn eval, void* ctx);
 // One run_wave(wave_size) (wave_search.py:555-615).
 int oracle_wave(void* tree, int wave_size);
+// Root Dirichlet noise for the next oracle_wave only (wave_search.py:1160-1170): the root's
+// priors become keep * P + eps * noise[action] in fp32, where keep is (float)(1 - (double)eps) as
+// the reference computes it in Python. Used to replay the noise a device run drew.
+int oracle_set_root_noise(void* tree, float eps, float keep, const float* noise_by_action);
 // Full search = begin + ceil(sims / max_wave_size) waves.
 int oracle_search(void* tree, const oracle_config* cfg, const int8_t* root_board,
                   oracle_eval_fn eval, void* ctx, oracle_result* out);

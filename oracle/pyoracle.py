@@ -153,6 +153,7 @@ def lib():
         L.oracle_begin.argtypes = [ctypes.c_void_p, ctypes.POINTER(OracleConfig), ctypes.c_void_p,
                                    EVAL_FN, ctypes.c_void_p]
         L.oracle_wave.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        L.oracle_set_root_noise.argtypes = [ctypes.c_void_p, ctypes.c_float, ctypes.c_float, ctypes.c_void_p]
         L.oracle_search.argtypes = [ctypes.c_void_p, ctypes.POINTER(OracleConfig), ctypes.c_void_p,
                                     EVAL_FN, ctypes.c_void_p, ctypes.POINTER(OracleResult)]
         L.oracle_get_result.argtypes = [ctypes.c_void_p, ctypes.POINTER(OracleResult)]
@@ -234,7 +235,11 @@ class Oracle:
         self._board = b
         return self._L.oracle_begin(self._t, ctypes.byref(cfg), b.ctypes.data, self._cb, None)
 
-    def wave(self, w: int) -> int:
+    def wave(self, w: int, root_noise=None, eps: float = 0.0) -> int:
+        """One wave; ``root_noise`` (fp32 [actions]) replays a Dirichlet vector at the root."""
+        if root_noise is not None:
+            nz = np.ascontiguousarray(root_noise, np.float32)
+            self._L.oracle_set_root_noise(self._t, eps, np.float32(1.0 - eps), nz.ctypes.data)
         return self._L.oracle_wave(self._t, w)
 
     def search(self, board, sims, wave, evaluator=None, **kw) -> OracleTree:
