@@ -160,3 +160,46 @@ def test_selfplay_moves_match_oracle(oracle_lib):
         for ex in r.examples:
             o = oracle_lib.Oracle(40000).search(ex["state"], 96, 32)
             assert np.array_equal(ex["policy"], o.policy)
+
+
+def test_root_dirichlet_noise_replays_bit_exact_in_oracle(oracle_lib):
+    """With eps > 0 every wave mixes a fresh Dirichlet vector into the root priors. Replaying the
+    vector each device wave drew makes the oracle's tree identical; the vectors are proper
+    distributions over the root's children, differ between waves, and repeat for a fixed seed."""
+    from omoknuni_quantum_b200.engine import WaveEngine
+    from omoknuni_quantum_b200.roots import random_root
+    board = random_root(8)
+    eps, wave, waves = 0.25, 64, 4
+
+    def run(seed):
+        eng = WaveEngine(1, capacity=60000, max_wave_size=wave, dirichlet_alpha=0.3,
+                         dirichlet_epsilon=eps, noise_seed=seed)
+        eng.begin(torch.from_numpy(board[None]).cuda())
+        eng.root_expand()
+        noise = []
+        for _ in range(waves):
+            eng.wave(wave)
+            noise.append(eng.root_noise()[0].cpu().numpy())
+        return eng, noise
+
+    eng, noise = run(123)
+    o = oracle_lib.Oracle(60000)
+    assert o.begin(board, o.config(waves * wave, wave)) == 0
+    for nz in noise:
+        assert o.wave(wave, root_noise=nz, eps=eps) == 0
+    t, ot = eng.export_tree(0), o.export()
+    for k in ("visits", "value_sums", "priors", "parent", "action"):
+        assert np.array_equal(t[k], getattr(ot, k)), k
+    legal = board.reshape(-1) == 0
+    for nz in noise:
+        assert abs(nz.sum() - 1.0) < 1e-5 and (nz >= 0).all() and (nz[~legal] == 0).all()
+    assert not np.array_equal(noise[0], noise[1])
+    _, again = run(123)
+    _, other = run(124)
+    assert all(np.array_equal(a, b) for a, b in zip(noise, again))
+    assert not np.array_equal(noise[0], other[0])
+    # without noise the same waves reproduce the noiseless oracle
+    e0 = WaveEngine(1, capacity=60000, max_wave_size=wave, dirichlet_epsilon=0.0)
+    e0.search(torch.from_numpy(board[None]).cuda(), waves * wave)
+    o0 = oracle_lib.Oracle(60000).search(board, waves * wave, wave)
+    assert np.array_equal(e0.export_tree(0)["visits"], o0.visits)
