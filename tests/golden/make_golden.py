@@ -130,6 +130,55 @@ def run_reference(board, sims, wave, c_puct, vl, enable_vl, cap):
     return np.asarray(policy, np.float64), out, ev, dt
 
 
+def reuse_cases():
+    from omoknuni_quantum_b200.roots import random_root
+    return [
+        # name, board, sims, wave, min_visits (subtree_reuse_min_visits)
+        ("seed10", random_root(10), 256, 64, 10),
+        ("seed11_w32", random_root(11), 320, 32, 10),
+        ("empty", np.zeros((15, 15), np.int8), 192, 64, 10),
+        ("reset_seed12", random_root(12), 128, 64, 1000000),
+    ]
+
+
+def run_reference_reuse(board, sims, wave, min_visits, cap=200000):
+    """search(board) -> update_root(argmax, new board) -> search(new board), subtree reuse on
+    (tree_operations.py:53-152, csr_tree.py:1020-1229, mcts.py:1205-1260). In the reference this
+    path ends in a full reset: shift_root returns a tensor, `if mapping and len(mapping) == 1`
+    (tree_operations.py:120) raises, and _try_optimized_subtree_reuse falls back to
+    _efficient_tree_reset (mcts.py:1250-1260). The fixtures record that observable behaviour."""
+    from mcts.core.mcts import MCTS
+    from mcts.core.mcts_config import MCTSConfig
+    from mcts.gpu.gpu_game_states import GameType
+    cfg = MCTSConfig(backend="gpu", device="cpu", wave_async_expansion=False,
+                     dirichlet_epsilon=0.0, enable_subtree_reuse=True, max_wave_size=wave,
+                     c_puct=1.4, virtual_loss=1.0, num_simulations=sims, max_tree_nodes=cap,
+                     initial_tree_nodes=cap, game_type=GameType.GOMOKU, board_size=15,
+                     subtree_reuse_min_visits=min_visits)
+    ev = TracingSynthEvaluator()
+    m = MCTS(cfg, ev)
+    pol1 = np.asarray(m.search(board.copy()), np.float64)
+    action = int(np.argmax(pol1))
+    child_visits = int(m.tree.node_data.visit_counts[m.tree.children[0, action]].item())
+    b2 = board.copy()
+    b2.reshape(-1)[action] = 1 if int((board != 0).sum()) % 2 == 0 else 2
+    m.update_root(action, b2)
+    kept = int(m.tree.num_nodes)
+    pol2 = np.asarray(m.search(b2.copy()), np.float64)
+    tree, nd = m.tree, m.tree.node_data
+    n = int(tree.num_nodes)
+    arr = dict(
+        visits=nd.visit_counts[:n].numpy().astype(np.int32),
+        value_sums=nd.value_sums[:n].numpy().astype(np.float32),
+        priors=nd.node_priors[:n].numpy().astype(np.float32),
+        virtual_loss=nd.virtual_loss_counts[:n].numpy().astype(np.int32),
+        parent=nd.parent_indices[:n].numpy().astype(np.int32),
+        action=nd.parent_actions[:n].numpy().astype(np.int32),
+        children=tree.children[:n].numpy().astype(np.int32),
+    )
+    return pol1, action, child_visits, kept, b2, pol2, arr, ev
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("OMQ_REFERENCE", "/root/reference"))
@@ -143,6 +192,22 @@ def main():
     logging.disable(logging.WARNING)
     import torch
     torch.set_num_threads(os.cpu_count() or 1)
+
+    for name, board, sims, wave, minv in reuse_cases():
+        if args.only and name not in args.only:
+            continue
+        pol1, action, child_visits, kept, b2, pol2, arr, ev = run_reference_reuse(board, sims, wave, minv)
+        n = arr["visits"].shape[0]
+        rec = dict(board=board.astype(np.int8), sims=sims, wave=wave, min_visits=minv,
+                   policy1=pol1, action=action, child_visits=child_visits, kept=kept,
+                   board2=b2.astype(np.int8), policy2=pol2, num_nodes=n,
+                   eval_calls=ev.calls, eval_positions=ev.positions, eval_trace=ev.trace_digest())
+        for k in ("visits", "value_sums", "priors", "virtual_loss", "parent", "action", "children"):
+            rec["sha_" + k] = digest(arr[k])
+        path = os.path.join(HERE, f"reuse_{name}.npz")  # reuse_<case>.npz
+        np.savez_compressed(path, **rec)
+        print(f"{name}: action={action} child_visits={child_visits} kept={kept} nodes={n} "
+              f"evals={ev.calls}/{ev.positions} -> {os.path.basename(path)}")
 
     for name, board, sims, wave, c, vl, evl, cap in cases():
         if args.only and name not in args.only:

@@ -1,0 +1,52 @@
+"""update_root with subtree reuse enabled, pinned to the reference's observable behaviour.
+
+The reference's reuse path never keeps a subtree: shift_root returns a tensor and
+tree_operations.py:120 (`if mapping and len(mapping) == 1`) raises, so _try_optimized_subtree_reuse
+falls back to a full reset (mcts.py:1250-1260). Fixtures recorded from the reference (search ->
+update_root(arg-max) -> search) show the second search equals a fresh search of the new board;
+the drop-in's update_root does exactly that."""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from golden_cases import GOLDEN, digest
+
+
+def _cases():
+    return sorted(os.path.basename(p)[6:-4] for p in glob.glob(os.path.join(GOLDEN, "reuse_*.npz")))
+
+
+def _load(name):
+    z = np.load(os.path.join(GOLDEN, f"reuse_{name}.npz"))
+    return {k: z[k] for k in z.files}
+
+
+@pytest.mark.parametrize("name", _cases())
+def test_oracle_second_search_is_fresh(oracle_lib, name):
+    g = _load(name)
+    first = oracle_lib.Oracle(200000).search(g["board"], int(g["sims"]), int(g["wave"]))
+    assert np.array_equal(first.policy, g["policy1"]) and int(np.argmax(first.policy)) == int(g["action"])
+    t = oracle_lib.Oracle(200000).search(g["board2"], int(g["sims"]), int(g["wave"]))
+    for k in ("visits", "value_sums", "priors", "parent", "action"):
+        assert digest(getattr(t, k)) == str(g["sha_" + k]), k
+    assert np.array_equal(t.policy, g["policy2"])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", _cases())
+def test_dropin_update_root_matches_reference(name):
+    from omoknuni_quantum_b200 import MCTS, MCTSConfig, SyntheticEvaluator
+    g = _load(name)
+    cfg = MCTSConfig(num_simulations=int(g["sims"]), max_wave_size=int(g["wave"]), c_puct=1.4,
+                     dirichlet_epsilon=0.0, enable_subtree_reuse=True, initial_tree_nodes=200000,
+                     subtree_reuse_min_visits=int(g["min_visits"]))
+    m = MCTS(cfg, SyntheticEvaluator())
+    p1 = m.search(g["board"])
+    assert np.array_equal(p1, g["policy1"])
+    action = int(np.argmax(p1))
+    m.update_root(action, g["board2"])
+    p2 = m.search(g["board2"])
+    assert np.array_equal(p2, g["policy2"])
