@@ -1064,8 +1064,7 @@ __global__ void __launch_bounds__(kHeadThreads) k_heads(HeadArgs a) {
   }
   __syncthreads();
   // softmax (= exp(log_softmax)) and value fc2 + tanh: one warp per position
-  if (warp < np) {
-    const int p = warp;
+  for (int p = warp; p < np; p += kHeadThreads / 32) {
     const float* l = lg + p * a.A;
     float mx = -INFINITY;
     for (int j = lane; j < a.A; j += 32) mx = fmaxf(mx, l[j]);
