@@ -163,8 +163,33 @@ def lib():
         L.oracle_feature_hash.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
         L.oracle_synth_eval.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        L.oracle_go_play.restype = ctypes.c_int
+        L.oracle_go_play.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                     ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]
+        L.oracle_go_legal.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_void_p]
         _lib = L
     return _lib
+
+
+def go_play(board: np.ndarray, player: int, action: int, ko: int = -1):
+    """Go move (go_rules.cpp): returns (new board, new ko point) or None when illegal."""
+    b = np.ascontiguousarray(board, np.int8)
+    n = b.shape[-1]
+    out = np.zeros_like(b)
+    k = ctypes.c_int(-1)
+    ok = lib().oracle_go_play(b.ctypes.data, n, int(player), int(action), int(ko), out.ctypes.data,
+                              ctypes.byref(k))
+    return (out, k.value) if ok else None
+
+
+def go_legal(board: np.ndarray, player: int, ko: int = -1) -> np.ndarray:
+    """Legal-action mask [n*n + 1] (pass last) under the oracle's Go rules."""
+    b = np.ascontiguousarray(board, np.int8)
+    n = b.shape[-1]
+    m = np.zeros(n * n + 1, np.uint8)
+    lib().oracle_go_legal(b.ctypes.data, n, int(player), int(ko), m.ctypes.data)
+    return m.astype(bool)
 
 
 def c_synth_eval(features: np.ndarray, actions: int | None = None):
