@@ -50,6 +50,15 @@ typedef enum {
   OMQ_QUEUE_FINAL = 1   /* picked children: value wanted (wave_search.py:1337-1457) */
 } omq_queue;
 
+/* Game of an engine. Gomoku: actions = n*n, 19 feature planes (the reference's basic
+ * representation). Go: actions = n*n + 1 (pass last, the reference's NN action space for Go),
+ * 17 feature planes; rules of GoState with Chinese rules and superko off
+ * (src/games/go/go_state.cpp:227-420, 502-506). */
+typedef enum {
+  OMQ_GAME_GOMOKU = 0,
+  OMQ_GAME_GO = 1
+} omq_game;
+
 typedef struct omq_engine omq_engine;
 
 typedef struct {
@@ -69,6 +78,7 @@ typedef struct {
   float dirichlet_alpha;
   float dirichlet_epsilon;
   uint64_t noise_seed;
+  int32_t game;             /* omq_game */
 } omq_engine_config;
 
 OMQ_API const char* omq_status_string(int status);
@@ -88,6 +98,13 @@ OMQ_API int omq_engine_memory(const omq_engine* e, uint64_t* h_bytes);
  * forced expansion (mcts.py:1659-1691): evaluate OMQ_QUEUE_EXPAND, then call
  * omq_root_expand. */
 OMQ_API int omq_begin(omq_engine* e, const int8_t* d_boards, void* stream);
+/* Go engines: reset every tree and set its root from d_history int8 [num_trees][8][n][n]
+ * (index 0 = the root position, index k = the position k plies earlier, all-zero before the
+ * game started; they feed the 17 history planes) and d_meta int32 [num_trees][3] = {side to move
+ * (1 black, 2 white), ko point (-1 none), consecutive passes}. Replaces MCTS._initialize_root
+ * for GameType.GO (mcts.py:1495-1519), which takes the GoState. Then as omq_begin. */
+OMQ_API int omq_begin_go(omq_engine* e, const int8_t* d_history, const int32_t* d_meta,
+                         void* stream);
 OMQ_API int omq_root_expand(omq_engine* e, void* stream);
 
 /* One wave of `wave_size` simulations in every tree (wave_search.py:555-615), in phases:
@@ -114,8 +131,10 @@ OMQ_API int omq_queue_buffers(omq_engine* e, int32_t queue, int32_t** d_entries,
 /* Synchronizes the stream and returns the entry count. */
 OMQ_API int omq_queue_count(omq_engine* e, int32_t queue, int32_t* h_count, void* stream);
 
-/* Reference feature tensor (gpu_game_states.py:534-600, 19 planes) of the queue entries,
- * fp32 [count][19][n][n] into d_out (capacity rows). */
+/* Feature tensor of the queue entries into d_out (capacity rows): Gomoku, the reference's
+ * (gpu_game_states.py:534-600) fp32 [count][19][n][n]; Go, fp32 [count][17][n][n] with planes
+ * 0-7 the side to move's stones now and 1..7 plies ago, 8-15 the opponent's, 16 all ones when
+ * black is to move. */
 OMQ_API int omq_queue_features(omq_engine* e, int32_t queue, float* d_out, void* stream);
 /* Built-in integer-exact synthetic evaluator on the queue (policy for OMQ_QUEUE_EXPAND, value
  * for both). */
@@ -126,6 +145,9 @@ OMQ_API int omq_queue_eval_synthetic(omq_engine* e, int32_t queue, void* stream)
  * once at the end to report device status. */
 OMQ_API int omq_search_synthetic(omq_engine* e, const int8_t* d_boards, int32_t num_simulations,
                          void* stream);
+/* The same for Go engines, with the roots of omq_begin_go. */
+OMQ_API int omq_search_synthetic_go(omq_engine* e, const int8_t* d_history, const int32_t* d_meta,
+                                    int32_t num_simulations, void* stream);
 
 /* Root statistics: visit counts of the root's children scattered by action,
  * d_visits int32 [num_trees][actions] (0 for illegal actions), and the root's own N and W

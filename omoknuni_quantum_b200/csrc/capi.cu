@@ -72,9 +72,10 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
     return OMQ_BAD_ARG;
   }
   if (c.num_trees < 1 || c.board_size < 5 || c.board_size > 19 || c.capacity < 2 ||
-      c.max_wave_size < 1 || c.max_wave_size > 1024 || c.max_depth < 2 || c.max_depth > 127) {
-    set_error("bad engine config: trees=%d board=%d capacity=%d wave=%d depth=%d", c.num_trees,
-              c.board_size, c.capacity, c.max_wave_size, c.max_depth);
+      c.max_wave_size < 1 || c.max_wave_size > 1024 || c.max_depth < 2 || c.max_depth > 127 ||
+      (c.game != OMQ_GAME_GOMOKU && c.game != OMQ_GAME_GO)) {
+    set_error("bad engine config: trees=%d board=%d capacity=%d wave=%d depth=%d game=%d",
+              c.num_trees, c.board_size, c.capacity, c.max_wave_size, c.max_depth, c.game);
     return OMQ_BAD_ARG;
   }
   DeviceGuard g(c.device);
@@ -86,7 +87,8 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   v.T = c.capacity;
   v.S = c.board_size;
   v.C = c.board_size * c.board_size;
-  v.A = v.C;
+  v.game = c.game;
+  v.A = c.game == OMQ_GAME_GO ? v.C + 1 : v.C;
   v.WCAP = c.max_wave_size;
   v.LOGCAP = c.max_wave_size * c.max_depth;
   v.max_depth = c.max_depth;
@@ -98,11 +100,11 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   v.noise_keep = (float)(1.0 - (double)v.noise_eps);
   v.noise_seed = c.noise_seed;
   const size_t R = v.R, T = v.T, W = v.WCAP, QC = R * W;
-  size_t off[24], n = 0, tot = 0;
+  size_t off[32], n = 0, tot = 0;
   auto take = [&](size_t bytes) { off[n++] = tot; tot += align256(bytes); };
   take(R * T * sizeof(NodeStats));            // 0 stats
   take(R * T * sizeof(NodeTopo));             // 1 topo
-  take(R * v.C);                              // 2 root boards
+  take(R * v.C * (c.game == OMQ_GAME_GO ? 8 : 1));  // 2 root boards (Go: with history)
   take(R * sizeof(TreeHeader));               // 3 headers
   take(R * 2 * W * sizeof(Visit));            // 4 frontier
   take(R * (size_t)v.LOGCAP * sizeof(Visit)); // 5 visit log
@@ -117,6 +119,7 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   take(QC * sizeof(float));                   // 14 value final
   take(2 * sizeof(int32_t));                  // 15 counts
   take(R * (size_t)v.A * sizeof(float));      // 16 root noise
+  take(c.game == OMQ_GAME_GO ? R * W * 16 * sizeof(uint32_t) : 16);  // 17 Go legal masks
   void* arena = nullptr;
   cudaError_t err = cudaMalloc(&arena, tot);
   if (err != cudaSuccess) {
@@ -141,6 +144,7 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   v.q_value[1] = reinterpret_cast<float*>(b + off[14]);
   v.q_count = reinterpret_cast<int32_t*>(b + off[15]);
   v.root_noise = reinterpret_cast<float*>(b + off[16]);
+  v.go_mask = reinterpret_cast<uint32_t*>(b + off[17]);
   err = cudaMemset(v.hdr, 0, R * sizeof(TreeHeader));
   if (err == cudaSuccess) err = cudaMemset(v.q_count, 0, 2 * sizeof(int32_t));
   if (err == cudaSuccess) err = cudaMemset(v.root_noise, 0, R * (size_t)v.A * sizeof(float));
@@ -172,9 +176,20 @@ int omq_engine_memory(const omq_engine* e, uint64_t* bytes) {
 
 int omq_begin(omq_engine* e, const int8_t* d_boards, void* stream) {
   if (!e || !d_boards) { set_error("null argument"); return OMQ_BAD_ARG; }
+  if (e->v.game != OMQ_GAME_GOMOKU) { set_error("Go engine: use omq_begin_go"); return OMQ_BAD_ARG; }
   DeviceGuard g(e->cfg.device);
   launch_begin(e->v, d_boards, e->searches++, (cudaStream_t)stream);
   OMQ_CHECK_LAUNCH("omq_begin");
+  e->phase = 1;
+  return OMQ_OK;
+}
+
+int omq_begin_go(omq_engine* e, const int8_t* d_history, const int32_t* d_meta, void* stream) {
+  if (!e || !d_history || !d_meta) { set_error("null argument"); return OMQ_BAD_ARG; }
+  if (e->v.game != OMQ_GAME_GO) { set_error("omq_begin_go on a non-Go engine"); return OMQ_BAD_ARG; }
+  DeviceGuard g(e->cfg.device);
+  launch_begin_go(e->v, d_history, d_meta, e->searches++, (cudaStream_t)stream);
+  OMQ_CHECK_LAUNCH("omq_begin_go");
   e->phase = 1;
   return OMQ_OK;
 }
@@ -290,11 +305,26 @@ static int first_tree_status(omq_engine* e, cudaStream_t s) {
   return st;
 }
 
+static int search_synthetic_waves(omq_engine* e, int32_t sims, void* stream);
+
 int omq_search_synthetic(omq_engine* e, const int8_t* d_boards, int32_t sims, void* stream) {
   if (!e || !d_boards || sims < 0) { set_error("bad argument"); return OMQ_BAD_ARG; }
-  cudaStream_t s = (cudaStream_t)stream;
   int st = omq_begin(e, d_boards, stream);
   if (st) return st;
+  return search_synthetic_waves(e, sims, stream);
+}
+
+int omq_search_synthetic_go(omq_engine* e, const int8_t* d_history, const int32_t* d_meta,
+                            int32_t sims, void* stream) {
+  if (!e || !d_history || !d_meta || sims < 0) { set_error("bad argument"); return OMQ_BAD_ARG; }
+  int st = omq_begin_go(e, d_history, d_meta, stream);
+  if (st) return st;
+  return search_synthetic_waves(e, sims, stream);
+}
+
+static int search_synthetic_waves(omq_engine* e, int32_t sims, void* stream) {
+  cudaStream_t s = (cudaStream_t)stream;
+  int st;
   if ((st = omq_queue_eval_synthetic(e, OMQ_QUEUE_EXPAND, stream))) return st;
   if ((st = omq_root_expand(e, stream))) return st;
   for (int done = 0; done < sims;) {

@@ -5,6 +5,7 @@
 // board plus the actions on its parent chain (at most max_depth dependent loads), which is all
 // the reference's features carry: occupancy, the side to move, and the last move (child states
 // do not inherit full_move_history, python/mcts/gpu/gpu_game_states.py:325-327, 443-446).
+#include "go_device.cuh"
 #include "omq_internal.cuh"
 
 namespace omq {
@@ -74,6 +75,50 @@ __device__ __forceinline__ uint64_t exp2_fixed(int64_t t) {
 constexpr int kSynthWarps = 4;
 constexpr int kMaxActionsPerLane = 12;  // ceil(362 / 32)
 
+// Policy (queue 0) and value of queue entry q from the position hash h; legal = empty points of
+// `board` plus any action past the board (Go pass). Warp-collective.
+__device__ void synth_emit(const EngineView& v, int queue, int q, uint64_t h, const int8_t* board) {
+  const int lane = threadIdx.x & 31;
+  if (queue == 0) {
+    uint64_t wv[kMaxActionsPerLane];
+    uint64_t tot = 0;
+#pragma unroll
+    for (int t = 0; t < kMaxActionsPerLane; ++t) {
+      const int a = t * 32 + lane;
+      wv[t] = 0;
+      if (a < v.A && (a >= v.C || board[a] == 0)) {
+        wv[t] = exp2_fixed(exp_step(mix64(h + 0x9E3779B97F4A7C15ull * (uint64_t)(a + 1))));
+        tot += wv[t];
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xFFFFFFFFu, tot, o);
+    int idx_base = 0;
+    float* out = v.q_policy[0] + (size_t)q * v.A;
+#pragma unroll
+    for (int t = 0; t < kMaxActionsPerLane; ++t) {
+      const int a = t * 32 + lane;
+      const bool legal = a < v.A && (a >= v.C || board[a] == 0);
+      const unsigned m = __ballot_sync(0xFFFFFFFFu, legal);
+      if (a < v.A) {
+        float p = 0.0f;
+        if (legal) {
+          const uint64_t idx = (uint64_t)(idx_base + __popc(m & ((1u << lane) - 1)));
+          const uint64_t qa = 512ull * ((wv[t] * 32640ull) / tot) + idx;
+          p = __fmul_rn(__ull2float_rn(qa), 1.0f / 16777216.0f);
+        }
+        out[a] = p;
+      }
+      idx_base += __popc(m);
+    }
+  }
+  if (lane == 0) {
+    const int64_t e = (int64_t)exp2_fixed(exp_step(mix64(h ^ 0xD1B54A32D192ED03ull)));
+    const int64_t dd = (int64_t)1 << 26;
+    const int64_t val = ((e - dd) * 4096) / (e + dd);
+    v.q_value[queue][q] = __fmul_rn(__ll2float_rn(val), 1.0f / 4096.0f);
+  }
+}
+
 __global__ void __launch_bounds__(kSynthWarps * 32) k_synth(EngineView v, int queue) {
   __shared__ WarpPos wps[kSynthWarps];
   const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
@@ -115,44 +160,7 @@ __global__ void __launch_bounds__(kSynthWarps * 32) k_synth(EngineView v, int qu
       }
   }
   h = __shfl_sync(0xFFFFFFFFu, h, 0);
-  if (queue == 0) {
-    uint64_t wv[kMaxActionsPerLane];
-    uint64_t tot = 0;
-#pragma unroll
-    for (int t = 0; t < kMaxActionsPerLane; ++t) {
-      const int a = t * 32 + lane;
-      wv[t] = 0;
-      if (a < v.A && (a >= v.C || wp.board[a] == 0)) {
-        wv[t] = exp2_fixed(exp_step(mix64(h + 0x9E3779B97F4A7C15ull * (uint64_t)(a + 1))));
-        tot += wv[t];
-      }
-    }
-    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xFFFFFFFFu, tot, o);
-    int idx_base = 0;
-    float* out = v.q_policy[0] + (size_t)q * v.A;
-#pragma unroll
-    for (int t = 0; t < kMaxActionsPerLane; ++t) {
-      const int a = t * 32 + lane;
-      const bool legal = a < v.A && (a >= v.C || wp.board[a] == 0);
-      const unsigned m = __ballot_sync(0xFFFFFFFFu, legal);
-      if (a < v.A) {
-        float p = 0.0f;
-        if (legal) {
-          const uint64_t idx = (uint64_t)(idx_base + __popc(m & ((1u << lane) - 1)));
-          const uint64_t qa = 512ull * ((wv[t] * 32640ull) / tot) + idx;
-          p = __fmul_rn(__ull2float_rn(qa), 1.0f / 16777216.0f);
-        }
-        out[a] = p;
-      }
-      idx_base += __popc(m);
-    }
-  }
-  if (lane == 0) {
-    const int64_t e = (int64_t)exp2_fixed(exp_step(mix64(h ^ 0xD1B54A32D192ED03ull)));
-    const int64_t dd = (int64_t)1 << 26;
-    const int64_t val = ((e - dd) * 4096) / (e + dd);
-    v.q_value[queue][q] = __fmul_rn(__ll2float_rn(val), 1.0f / 4096.0f);
-  }
+  synth_emit(v, queue, q, h, wp.board);
 }
 
 // Reference feature tensor, fp32 [count][19][C]. One warp per queued position.
@@ -217,7 +225,113 @@ __global__ void __launch_bounds__(kSynthWarps * 32) k_pack_queue(EngineView v, i
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Go: 17 history planes from the replayed position (go_device.cuh)
+// ---------------------------------------------------------------------------------------------
+struct GoWarpPos {
+  GoPos pos;
+  int8_t ring[kGoHistory * kMaxCells];
+  uint64_t words[kGoPlanes * kMaxWords];
+};
+
+// Bit of plane p at cell c of the Go features (planes 0-7 own stones k plies ago, 8-15 the
+// opponent's, 16 black to move).
+__device__ __forceinline__ bool go_plane_bit(const EngineView& v, int r, const GoWarpPos& w, int p,
+                                             int c) {
+  if (p == 16) return w.pos.player == 1;
+  const int k = p & 7;
+  const int8_t s = go_hist_board(v, r, w.pos, w.ring, k)[c];
+  return s == (p < 8 ? w.pos.player : 3 - w.pos.player);
+}
+
+__device__ int go_queue_replay(const EngineView& v, int queue, int q, GoWarpPos& w, int& r) {
+  const int2 ent = v.q_entries[queue][q];
+  r = ent.x;
+  const int d = warp_go_replay(v, r, ent.y, w.pos, w.ring);
+  if (d < 0 && (threadIdx.x & 31) == 0) v.hdr[r].status = OMQ_BAD_ARG;
+  return d;
+}
+
+constexpr int kGoWarps = 4;
+
+// Synthetic evaluator on Go positions: hash folded over the 17 binarised planes, plane by plane,
+// 64-cell words in order (oracle_feature_hash_go); legal = empty points plus pass.
+__global__ void __launch_bounds__(kGoWarps * 32) k_synth_go(EngineView v, int queue) {
+  __shared__ GoWarpPos wps[kGoWarps];
+  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
+  const int q = blockIdx.x * kGoWarps + wl;
+  if (q >= v.q_count[queue]) return;
+  GoWarpPos& w = wps[wl];
+  int r;
+  if (go_queue_replay(v, queue, q, w, r) < 0) return;
+  const int nwords = (v.C + 63) / 64;
+  for (int i = lane; i < kGoPlanes * nwords; i += 32) {
+    const int p = i / nwords, j = i - p * nwords;
+    uint64_t word = 0;
+    for (int b = 0; b < 64; ++b) {
+      const int c = j * 64 + b;
+      if (c < v.C && go_plane_bit(v, r, w, p, c)) word |= 1ull << b;
+    }
+    w.words[i] = word;
+  }
+  __syncwarp();
+  uint64_t h = 0;
+  if (lane == 0) {
+    h = 0x243F6A8885A308D3ull;
+    for (int i = 0; i < kGoPlanes * nwords; ++i) h = mix64(h ^ w.words[i]);
+  }
+  h = __shfl_sync(0xFFFFFFFFu, h, 0);
+  synth_emit(v, queue, q, h, w.pos.board);
+}
+
+__global__ void __launch_bounds__(kGoWarps * 32) k_features_go(EngineView v, int queue, float* out) {
+  __shared__ GoWarpPos wps[kGoWarps];
+  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
+  const int q = blockIdx.x * kGoWarps + wl;
+  if (q >= v.q_count[queue]) return;
+  GoWarpPos& w = wps[wl];
+  int r;
+  if (go_queue_replay(v, queue, q, w, r) < 0) return;
+  float* o = out + (size_t)q * kGoPlanes * v.C;
+  for (int p = 0; p < kGoPlanes; ++p)
+    for (int c = lane; c < v.C; c += 32) o[(size_t)p * v.C + c] = go_plane_bit(v, r, w, p, c) ? 1.0f : 0.0f;
+}
+
+// ResNet input for Go: the 17 planes as bf16, channels padded to 64, padded pixel layout.
+__global__ void __launch_bounds__(kGoWarps * 32) k_pack_queue_go(EngineView v, int queue, int P, uint4* out) {
+  __shared__ GoWarpPos wps[kGoWarps];
+  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
+  const int q = blockIdx.x * kGoWarps + wl;
+  if (q >= v.q_count[queue]) return;
+  GoWarpPos& w = wps[wl];
+  int r;
+  if (go_queue_replay(v, queue, q, w, r) < 0) return;
+  const int S = v.S;
+  uint4* o = out + (size_t)q * P * 8;
+  for (int i = lane; i < P * 8; i += 32) {
+    const int pix = i >> 3, chunk = i & 7;
+    const int y = pix / (S + 1), x = pix - y * (S + 1);
+    uint16_t h[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (y < S && x < S && chunk < 3) {
+      const int c = y * S + x;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int ch = chunk * 8 + e;
+        if (ch < kGoPlanes) h[e] = go_plane_bit(v, r, w, ch, c) ? 0x3F80 : 0;
+      }
+    }
+    o[i] = *reinterpret_cast<uint4*>(h);
+  }
+}
+
 void launch_pack_queue(const EngineView& v, int queue, int P, void* out, cudaStream_t s) {
+  if (v.game == OMQ_GAME_GO) {
+    const int cap = v.R * v.WCAP;
+    count_launches(1);
+    k_pack_queue_go<<<(cap + kGoWarps - 1) / kGoWarps, kGoWarps * 32, 0, s>>>(
+        v, queue, P, reinterpret_cast<uint4*>(out));
+    return;
+  }
   const int cap = v.R * v.WCAP;
   count_launches(1);
   k_pack_queue<<<(cap + kSynthWarps - 1) / kSynthWarps, kSynthWarps * 32, 0, s>>>(
@@ -227,12 +341,20 @@ void launch_pack_queue(const EngineView& v, int queue, int P, void* out, cudaStr
 void launch_synth_eval(const EngineView& v, int queue, cudaStream_t s) {
   const int cap = v.R * v.WCAP;
   count_launches(1);
+  if (v.game == OMQ_GAME_GO) {
+    k_synth_go<<<(cap + kGoWarps - 1) / kGoWarps, kGoWarps * 32, 0, s>>>(v, queue);
+    return;
+  }
   k_synth<<<(cap + kSynthWarps - 1) / kSynthWarps, kSynthWarps * 32, 0, s>>>(v, queue);
 }
 
 void launch_features(const EngineView& v, int queue, float* out, cudaStream_t s) {
   const int cap = v.R * v.WCAP;
   count_launches(1);
+  if (v.game == OMQ_GAME_GO) {
+    k_features_go<<<(cap + kGoWarps - 1) / kGoWarps, kGoWarps * 32, 0, s>>>(v, queue, out);
+    return;
+  }
   k_features<<<(cap + kSynthWarps - 1) / kSynthWarps, kSynthWarps * 32, 0, s>>>(v, queue, out);
 }
 

@@ -62,7 +62,8 @@ struct TreeHeader {
   int32_t wave;
   int32_t wave_idx;      // waves run in the current search (root-noise counter)
   int32_t search_idx;    // searches begun on this engine (root-noise counter)
-  int32_t pad[2];
+  int32_t root_ko;       // Go: ko point of the root position (-1 none)
+  int32_t root_passes;   // Go: consecutive passes that led to the root position
 };
 
 constexpr int kPlanes = 19;
@@ -72,6 +73,7 @@ constexpr int kMaxWords = 6;  // ceil(361 / 64)
 
 // Device-side view of one engine, passed by value to kernels.
 struct EngineView {
+  int game;              // OMQ_GAME_GOMOKU or OMQ_GAME_GO
   int R, T, S, C, A, WCAP, LOGCAP, max_depth, enable_vl;
   float c_puct, vl_value;
   float noise_alpha, noise_eps, noise_keep;  // keep = (float)(1 - (double)eps), as the reference rounds it
@@ -79,7 +81,8 @@ struct EngineView {
   float* root_noise;     // [R][A] noise of the last wave, by action
   NodeStats* stats;      // [R*T]
   NodeTopo* topo;        // [R*T]
-  int8_t* root_board;    // [R*C]
+  int8_t* root_board;    // Gomoku [R][C]; Go [R][8][C] (root position and 7 earlier ones)
+  uint32_t* go_mask;     // Go: [R][WCAP][16] legal bits (12 words) + passes of each leaf
   TreeHeader* hdr;       // [R]
   Visit* frontier;       // [R][2][WCAP]
   Visit* vlog;           // [R][LOGCAP]
@@ -181,6 +184,8 @@ void count_launches(int n);
 int cuda_status(cudaError_t e, const char* what);
 
 void launch_begin(const EngineView& v, const int8_t* boards, int search_id, cudaStream_t s);
+void launch_begin_go(const EngineView& v, const int8_t* history, const int32_t* meta, int search_id,
+                     cudaStream_t s);
 void launch_select(const EngineView& v, int wave, cudaStream_t s);
 void launch_expand(const EngineView& v, int root_mode, cudaStream_t s);
 void launch_backup(const EngineView& v, cudaStream_t s);

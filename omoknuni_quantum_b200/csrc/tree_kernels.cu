@@ -11,6 +11,7 @@
 // exactly one record per wave, which makes backup free of atomics and lets it add the values
 // of [lo, lo+k) in ascending simulation order - the reference's sequential order
 // (python/mcts/gpu/mcts_gpu_accelerator.py:378-393) - so W is bit-exact for any evaluator.
+#include "go_device.cuh"
 #include "omq_internal.cuh"
 
 namespace omq {
@@ -165,6 +166,37 @@ __global__ void __launch_bounds__(kThreads) k_begin(EngineView v, const int8_t* 
     const size_t base = (size_t)r * v.T;
     v.stats[base] = NodeStats{0, 0.0f, 1.0f, 0};
     v.topo[base] = NodeTopo{-1, pack_act_depth(-1, 0), 0, pack_cnt_flags(0, 0)};
+    v.leaves[(size_t)r * v.WCAP] = Visit{0, 0, 0, 0};
+    v.leaf_final[(size_t)r * v.WCAP] = make_int2(0, r);
+    v.q_entries[0][r] = make_int2(r, 0);
+    if (r == 0) { v.q_count[0] = v.R; v.q_count[1] = 0; }
+  }
+}
+
+// Go roots: history boards [R][8][C] and {side to move, ko, passes} per tree. A root reached by
+// two passes is terminal and gets no children.
+__global__ void k_begin_go(EngineView v, const int8_t* hist, const int32_t* meta, int search_id) {
+  const int r = blockIdx.x, tid = threadIdx.x;
+  const size_t n = (size_t)kGoHistory * v.C;
+  for (size_t i = tid; i < n; i += blockDim.x) v.root_board[(size_t)r * n + i] = hist[(size_t)r * n + i];
+  if (tid == 0) {
+    TreeHeader h{};
+    h.num_nodes = 1;
+    h.status = OMQ_OK;
+    const int player = meta[3 * r], ko = meta[3 * r + 1], passes = meta[3 * r + 2];
+    if ((player != 1 && player != 2) || ko < -1 || ko >= v.C || passes < 0) h.status = OMQ_BAD_ARG;
+    h.root_player = player;
+    h.root_ko = ko;
+    h.root_passes = passes;
+    h.nleaves = 1;
+    h.exp_off = r;
+    h.exp_cnt = 1;
+    h.search_idx = search_id;
+    v.hdr[r] = h;
+    const size_t base = (size_t)r * v.T;
+    v.stats[base] = NodeStats{0, 0.0f, 1.0f, 0};
+    v.topo[base] = NodeTopo{-1, pack_act_depth(-1, 0), 0,
+                            pack_cnt_flags(0, passes >= 2 ? kFlagTerminal : 0)};
     v.leaves[(size_t)r * v.WCAP] = Visit{0, 0, 0, 0};
     v.leaf_final[(size_t)r * v.WCAP] = make_int2(0, r);
     v.q_entries[0][r] = make_int2(r, 0);
@@ -433,9 +465,32 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
   int2* lf = v.leaf_final + (size_t)r * v.WCAP;
   const float* pol = v.q_policy[0];
 
-  // children per expandable leaf: the empty cells of its board, i.e. C - move_count
-  for (int i = tid; i < nleaf; i += blockDim.x)
-    s_cnt[i] = lf[i].y >= 0 ? max(v.C - (H->root_mc + leaves[i].depth), 0) : 0;
+  const bool go = v.game == OMQ_GAME_GO;
+  GoPos* gpos = reinterpret_cast<GoPos*>(expand_smem + (blockDim.x >> 5) * sizeof(ExpandWarpSmem));
+  if (go) {
+    // Go: children are the legal moves of the leaf position (replayed from the root); the
+    // legal bits and the leaf's pass count go to a per-leaf scratch for the second pass
+    GoPos& gp = gpos[warp];
+    for (int i = warp; i < nleaf; i += (int)(blockDim.x >> 5)) {
+      int n = 0;
+      if (lf[i].y >= 0 && !(topo_flags(v.topo[base + leaves[i].node]) & kFlagTerminal)) {
+        const int d = warp_go_replay(v, r, leaves[i].node, gp, nullptr);
+        if (d < 0) { if (lane == 0) H->status = OMQ_BAD_ARG; n = 0; }
+        else {
+          uint32_t* m = v.go_mask + ((size_t)r * v.WCAP + i) * 16;
+          warp_go_analyze(gp.board, v.S, gp.g);
+          n = warp_go_legal(gp.board, v.S, gp.player, gp.ko, gp.g, m);
+          if (lane == 0) m[12] = (uint32_t)gp.passes;
+        }
+      }
+      if (lane == 0) s_cnt[i] = n;
+      __syncwarp();
+    }
+  } else {
+    // children per expandable leaf: the empty cells of its board, i.e. C - move_count
+    for (int i = tid; i < nleaf; i += blockDim.x)
+      s_cnt[i] = lf[i].y >= 0 ? max(v.C - (H->root_mc + leaves[i].depth), 0) : 0;
+  }
   __syncthreads();
   const int total = block_exclusive_scan(s_cnt, nleaf, warp_tot);
   if (num_nodes + total > v.T) {  // "Tree full" (csr_tree.py:405-406)
@@ -447,7 +502,55 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
     const Visit e = leaves[i];
     const int q = lf[i].y;
     int final_node = e.node, ext = 0;
-    if (q >= 0) {
+    if (q >= 0 && go) {
+      const uint32_t* m = v.go_mask + ((size_t)r * v.WCAP + i) * 16;
+      const int leaf_passes = (int)m[12];
+      int n = 0;
+      if (!(topo_flags(v.topo[base + e.node]) & kFlagTerminal)) {
+        for (int w = 0; w < kGoMaskWords && w * 32 < v.A; ++w) {
+          const int c = w * 32 + lane;
+          const bool legal = c < v.A && ((m[w] >> lane) & 1u);
+          const unsigned bm = __ballot_sync(0xFFFFFFFFu, legal);
+          if (legal) {
+            const int j = n + __popc(bm & ((1u << lane) - 1));
+            W.legal[j] = (int16_t)c;
+            W.pv[j] = pol[(size_t)q * v.A + c];
+          }
+          n += __popc(bm);
+        }
+      }
+      __syncwarp();
+      const float denom = __fadd_rn(warp_fixed_order_sum(W.pv, n), 1e-8f);
+      const int start = num_nodes + s_cnt[i];
+      const int d = e.depth;
+      unsigned long long best = 0;
+      const int32_t nleafN = v.stats[base + e.node].N;
+      for (int j = lane; j < n; j += 32) {
+        const int a = W.legal[j];
+        const float P = __fdiv_rn(W.pv[j], denom);
+        const bool term = a == v.C && leaf_passes >= 1;  // second consecutive pass
+        const int c = start + j;
+        const NodeStats st{0, 0.0f, P, 0};
+        v.stats[base + c] = st;
+        v.topo[base + c] = NodeTopo{e.node, pack_act_depth(a, d + 1), 0,
+                                    pack_cnt_flags(0, term ? kFlagTerminal : 0)};
+        const unsigned long long key =
+            rank_key(ucb_score(st, nleafN, v.c_puct, v.vl_value, v.enable_vl), j);
+        best = key > best ? key : best;
+      }
+      best = warp_max_u64(best);
+      if (lane == 0) {
+        NodeTopo lt = v.topo[base + e.node];
+        lt.child_start = start;
+        lt.cnt_flags = pack_cnt_flags(n, topo_flags(lt));
+        v.topo[base + e.node] = lt;
+      }
+      if (!root_mode && n > 0) {
+        final_node = start + key_slot(best);
+        ext = (e.depth + 1 < v.max_depth) ? 1 : 0;
+        if (lane == 0 && v.enable_vl) v.stats[base + final_node].VL += 1;
+      }
+    } else if (q >= 0) {
       // reconstruct the leaf's board: root board + the stones along its path
       int d = 0;
       if (lane == 0) d = path_actions(v.topo + base, e.node, kMaxDepthCap - 1, W.acts);
@@ -657,6 +760,12 @@ void launch_begin(const EngineView& v, const int8_t* boards, int search_id, cuda
   k_begin<<<v.R, tree_threads(v), 0, s>>>(v, boards, search_id);
 }
 
+void launch_begin_go(const EngineView& v, const int8_t* history, const int32_t* meta, int search_id,
+                     cudaStream_t s) {
+  count_launches(1);
+  k_begin_go<<<v.R, 256, 0, s>>>(v, history, meta, search_id);
+}
+
 void launch_select(const EngineView& v, int wave, cudaStream_t s) {
   const size_t sm = select_smem(v);
   if (sm > 48 * 1024)
@@ -669,12 +778,16 @@ void launch_select(const EngineView& v, int wave, cudaStream_t s) {
 void launch_expand(const EngineView& v, int root_mode, cudaStream_t s) {
   if (!root_mode) cudaMemsetAsync(v.q_count + 1, 0, sizeof(int32_t), s);
   count_launches(1);
-  const int sm = (int)((tree_threads(v) / 32) * sizeof(ExpandWarpSmem));
+  const int sm = (int)((tree_threads(v) / 32) *
+                       (sizeof(ExpandWarpSmem) + (v.game == OMQ_GAME_GO ? sizeof(GoPos) : 0)));
   cudaFuncSetAttribute(k_expand, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
   k_expand<<<v.R, tree_threads(v), sm, s>>>(v, root_mode);
 }
 
-void launch_backup(const EngineView& v, cudaStream_t s) { k_backup<<<v.R, tree_threads(v), 0, s>>>(v); }
+void launch_backup(const EngineView& v, cudaStream_t s) {
+  count_launches(1);
+  k_backup<<<v.R, tree_threads(v), 0, s>>>(v);
+}
 
 void launch_root_visits(const EngineView& v, int32_t* visits, float* nw, cudaStream_t s) {
   count_launches(1);

@@ -8,9 +8,13 @@ The evaluator between the select/expand/backup phases is one of
   * an object with ``forward_queue(engine, queue)`` (the device ResNet evaluator of this
     package, which reads the queue in place and writes the queue's policy/value buffers);
   * any object with the reference evaluator protocol
-    ``evaluate_batch(features[B,19,H,W]) -> (policy[B,A] probabilities, value[B] or [B,1])``
+    ``evaluate_batch(features[B,planes,H,W]) -> (policy[B,A] probabilities, value[B] or [B,1])``
     (python/mcts/core/wave_search.py:866-871, 1381-1383); features are handed over as a CUDA
     fp32 tensor, results are copied into the queue buffers.
+
+Games: ``"gomoku"`` (A = n*n, the reference's 19 feature planes) and ``"go"`` (A = n*n + 1 with
+pass last, 17 history planes; roots carry 8 history boards, the side to move, the ko point and
+the consecutive-pass count - see ``go_meta``).
 """
 from __future__ import annotations
 
@@ -22,6 +26,19 @@ import torch
 from . import _lib
 
 PLANES = 19
+GO_PLANES = 17
+GO_HISTORY = 8
+
+
+def go_meta(to_move, ko=None, passes=None, num_trees=None) -> torch.Tensor:
+    """int32 [R, 3] root records {side to move (1 black, 2 white), ko point (-1), passes}."""
+    tm = torch.as_tensor(np.asarray(to_move, np.int32).reshape(-1))
+    R = tm.numel() if num_trees is None else num_trees
+    if tm.numel() == 1 and R > 1:
+        tm = tm.repeat(R)
+    k = torch.full((R,), -1, dtype=torch.int32) if ko is None else torch.as_tensor(np.asarray(ko, np.int32).reshape(-1))
+    p = torch.zeros(R, dtype=torch.int32) if passes is None else torch.as_tensor(np.asarray(passes, np.int32).reshape(-1))
+    return torch.stack([tm.to(torch.int32), k.to(torch.int32), p.to(torch.int32)], dim=1).contiguous()
 
 
 def _stream_ptr(stream=None) -> ctypes.c_void_p:
@@ -33,7 +50,8 @@ class WaveEngine:
     def __init__(self, num_trees: int, board_size: int = 15, capacity: int = 200000,
                  max_wave_size: int = 256, c_puct: float = 1.4, virtual_loss: float = 1.0,
                  enable_virtual_loss: bool = True, max_depth: int = 100, device=None,
-                 dirichlet_alpha: float = 0.3, dirichlet_epsilon: float = 0.0, noise_seed: int = 0):
+                 dirichlet_alpha: float = 0.3, dirichlet_epsilon: float = 0.0, noise_seed: int = 0,
+                 game: str = "gomoku"):
         if not torch.cuda.is_available():
             raise RuntimeError("WaveEngine needs a CUDA device (B200); there is no CPU fallback")
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -42,14 +60,19 @@ class WaveEngine:
         self.num_trees = int(num_trees)
         self.board_size = int(board_size)
         self.cells = self.board_size ** 2
-        self.actions = self.cells
+        if game not in _lib.GAMES:
+            raise ValueError(f"unknown game {game!r} (gomoku, go)")
+        self.game = game
+        self.is_go = game == "go"
+        self.actions = self.cells + (1 if self.is_go else 0)
+        self.planes = GO_PLANES if self.is_go else PLANES
         self.capacity = int(capacity)
         self.max_wave_size = int(max_wave_size)
         cfg = _lib.EngineConfig(self.num_trees, self.board_size, self.capacity, self.max_wave_size,
                                 int(max_depth), float(c_puct), float(virtual_loss),
                                 int(bool(enable_virtual_loss)), dev.index or 0,
                                 float(dirichlet_alpha), float(dirichlet_epsilon),
-                                int(noise_seed) & 0xFFFFFFFFFFFFFFFF)
+                                int(noise_seed) & 0xFFFFFFFFFFFFFFFF, _lib.GAMES[game])
         self.cfg = cfg
         h = ctypes.c_void_p()
         with torch.cuda.device(dev):
@@ -100,10 +123,10 @@ class WaveEngine:
         return int(n.value)
 
     def queue_features(self, queue: int) -> torch.Tensor:
-        """Reference feature tensor of the queued positions, fp32 [count, 19, n, n] (syncs)."""
+        """Feature tensor of the queued positions, fp32 [count, planes, n, n] (syncs)."""
         count = self.queue_count(queue)
         if self._features is None:
-            self._features = torch.empty(self.queue_capacity, PLANES, self.board_size,
+            self._features = torch.empty(self.queue_capacity, self.planes, self.board_size,
                                          self.board_size, dtype=torch.float32, device=self.device)
         _lib.check(self.L.omq_queue_features(self._h, queue, ctypes.c_void_p(self._features.data_ptr()),
                                              _stream_ptr()), "omq_queue_features")
@@ -131,7 +154,26 @@ class WaveEngine:
                      .reshape(n).to(self.device, torch.float32))
 
     # -- search phases -------------------------------------------------------------------------
-    def begin(self, boards: torch.Tensor) -> None:
+    def _go_roots(self, boards, meta):
+        n, R = self.board_size, self.num_trees
+        b = torch.as_tensor(boards).to(self.device, torch.int8)
+        if b.dim() == 3:  # no earlier positions
+            b = torch.cat([b[:, None], torch.zeros(R, GO_HISTORY - 1, n, n, dtype=torch.int8,
+                                                  device=self.device)], dim=1)
+        if tuple(b.shape) != (R, GO_HISTORY, n, n):
+            raise ValueError(f"Go roots must be [{R}, {GO_HISTORY}, {n}, {n}] (or [{R}, {n}, {n}])")
+        if meta is None:
+            raise ValueError("Go roots need meta = go_meta(to_move, ko, passes)")
+        m = torch.as_tensor(meta).to(self.device, torch.int32).reshape(R, 3).contiguous()
+        return b.contiguous(), m
+
+    def begin(self, boards: torch.Tensor, meta=None) -> None:
+        if self.is_go:
+            b, m = self._go_roots(boards, meta)
+            self._boards, self._meta = b, m
+            _lib.check(self.L.omq_begin_go(self._h, ctypes.c_void_p(b.data_ptr()),
+                                           ctypes.c_void_p(m.data_ptr()), _stream_ptr()), "omq_begin_go")
+            return
         b = boards.to(self.device, torch.int8).contiguous()
         if b.shape != (self.num_trees, self.board_size, self.board_size):
             raise ValueError(f"boards must be [{self.num_trees}, {self.board_size}, {self.board_size}]")
@@ -150,9 +192,19 @@ class WaveEngine:
         self.evaluate_queue(_lib.QUEUE_FINAL, evaluator)
         _lib.check(self.L.omq_wave_backup(self._h, s), "omq_wave_backup")
 
-    def search(self, boards: torch.Tensor, num_simulations: int, evaluator="synthetic") -> None:
+    def search(self, boards: torch.Tensor, num_simulations: int, evaluator="synthetic",
+               meta=None) -> None:
         """begin + forced root expansion + ceil(sims / max_wave_size) waves
-        (python/mcts/core/mcts.py:1020-1063). Raises on a device status (e.g. TreeFullError)."""
+        (python/mcts/core/mcts.py:1020-1063). Raises on a device status (e.g. TreeFullError).
+        Go engines take history boards and ``meta`` (see ``begin``)."""
+        if isinstance(evaluator, str) and evaluator == "synthetic" and self.is_go:
+            b, m = self._go_roots(boards, meta)
+            self._boards, self._meta = b, m
+            _lib.check(self.L.omq_search_synthetic_go(self._h, ctypes.c_void_p(b.data_ptr()),
+                                                      ctypes.c_void_p(m.data_ptr()),
+                                                      int(num_simulations), _stream_ptr()),
+                       "omq_search_synthetic_go")
+            return
         if isinstance(evaluator, str) and evaluator == "synthetic":
             b = boards.to(self.device, torch.int8).contiguous()
             self._boards = b
@@ -160,7 +212,7 @@ class WaveEngine:
                                                    int(num_simulations), _stream_ptr()),
                        "omq_search_synthetic")
             return
-        self.begin(boards)
+        self.begin(boards, meta)
         self.root_expand(evaluator)
         done = 0
         while done < num_simulations:

@@ -1,0 +1,136 @@
+"""Host-side Go position: root construction and move application between searches.
+
+The rules are those the device engine searches with - the reference's GoState with Chinese rules
+and positional superko off (src/games/go/go_state.cpp:227-420, go_rules.cpp:34-110, isTerminal
+:502-506): no play on an occupied point or on the ko point; opponent groups without liberties
+are captured; suicide is illegal; capturing exactly one stone makes its point the ko point; pass
+is always legal, clears the ko point, and two consecutive passes end the game. Actions are
+y * n + x, pass = n * n (the NN action space; GoState itself encodes pass as -1).
+
+This is host bookkeeping for a handful of moves per search (root positions, the move a search
+chose); the search itself never calls it.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+HISTORY = 8
+
+
+class GoPosition:
+    def __init__(self, board_size: int = 19):
+        self.n = int(board_size)
+        self.board = np.zeros((self.n, self.n), np.int8)
+        self.to_move = 1
+        self.ko = -1
+        self.passes = 0
+        self.history = [self.board.copy()]  # most recent last
+
+    @property
+    def pass_action(self) -> int:
+        return self.n * self.n
+
+    def copy(self) -> "GoPosition":
+        g = GoPosition(self.n)
+        g.board = self.board.copy()
+        g.to_move, g.ko, g.passes = self.to_move, self.ko, self.passes
+        g.history = [h.copy() for h in self.history[-HISTORY:]]
+        return g
+
+    def is_terminal(self) -> bool:
+        return self.passes >= 2
+
+    def _group(self, b, y, x):
+        """Stones of the group at (y, x) and whether it has a liberty."""
+        color = b[y, x]
+        stack, seen, lib = [(y, x)], {(y, x)}, False
+        while stack:
+            cy, cx = stack.pop()
+            for ny, nx in ((cy - 1, cx), (cy + 1, cx), (cy, cx - 1), (cy, cx + 1)):
+                if 0 <= ny < self.n and 0 <= nx < self.n and (ny, nx) not in seen:
+                    if b[ny, nx] == 0:
+                        lib = True
+                    elif b[ny, nx] == color:
+                        seen.add((ny, nx))
+                        stack.append((ny, nx))
+        return seen, lib
+
+    def _try(self, action: int):
+        """(new board, new ko) or None if illegal; does not change the position."""
+        if action == self.pass_action:
+            return self.board.copy(), -1
+        if not 0 <= action < self.pass_action or action == self.ko:
+            return None
+        y, x = divmod(action, self.n)
+        if self.board[y, x] != 0:
+            return None
+        b = self.board.copy()
+        b[y, x] = self.to_move
+        opp = 3 - self.to_move
+        groups, captured, last = 0, 0, -1
+        for ny, nx in ((y - 1, x), (y + 1, x), (y, x - 1), (y, x + 1)):
+            if 0 <= ny < self.n and 0 <= nx < self.n and b[ny, nx] == opp:
+                stones, lib = self._group(b, ny, nx)
+                if not lib:
+                    groups += 1
+                    captured += len(stones)
+                    for sy, sx in stones:
+                        b[sy, sx] = 0
+                    last = next(iter(stones))
+        if captured == 0 and not self._group(b, y, x)[1]:
+            return None  # suicide
+        ko = last[0] * self.n + last[1] if (groups == 1 and captured == 1) else -1
+        return b, ko
+
+    def is_legal(self, action: int) -> bool:
+        return self._try(int(action)) is not None
+
+    def legal_mask(self) -> np.ndarray:
+        """bool [n*n + 1], pass last."""
+        m = np.zeros(self.pass_action + 1, bool)
+        for a in np.flatnonzero(self.board.reshape(-1) == 0):
+            m[a] = self._try(int(a)) is not None
+        m[self.pass_action] = True
+        return m
+
+    def play(self, action: int) -> None:
+        res = self._try(int(action))
+        if res is None:
+            raise ValueError(f"illegal Go move {action} for player {self.to_move}")
+        self.board, self.ko = res
+        self.passes = self.passes + 1 if action == self.pass_action else 0
+        self.to_move = 3 - self.to_move
+        self.history.append(self.board.copy())
+        del self.history[:-HISTORY]
+
+    def history_planes(self) -> np.ndarray:
+        """int8 [8, n, n]: [0] = this position, [k] = k plies earlier (zeros before the game)."""
+        h = np.zeros((HISTORY, self.n, self.n), np.int8)
+        for k, b in enumerate(reversed(self.history[-HISTORY:])):
+            h[k] = b
+        return h
+
+    def meta(self) -> np.ndarray:
+        """int32 [3]: side to move, ko point, consecutive passes (the engine's root record)."""
+        return np.array([self.to_move, self.ko, self.passes], np.int32)
+
+
+def random_position(seed: int, moves: int = 60, board_size: int = 19) -> GoPosition:
+    """``moves`` uniformly random legal non-pass moves from the empty board, colours alternating
+    from black, captures resolved by the rules (BASELINE config 3's "60 stones placed at random
+    under the legality rules"); numpy.random.default_rng(seed)."""
+    rng = np.random.default_rng(seed)
+    g = GoPosition(board_size)
+    for _ in range(moves):
+        cand = np.flatnonzero(g.legal_mask()[:-1])
+        if len(cand) == 0:
+            break
+        g.play(int(cand[rng.integers(len(cand))]))
+    return g
+
+
+def random_roots(seed: int, count: int, moves: int = 60, board_size: int = 19):
+    """``count`` seeded Go roots (root i uses seed ``seed * 1_000_003 + i``):
+    (history int8 [count, 8, n, n], meta int32 [count, 3])."""
+    ps = [random_position(seed * 1_000_003 + i, moves, board_size) for i in range(count)]
+    return np.stack([p.history_planes() for p in ps]), np.stack([p.meta() for p in ps])

@@ -70,6 +70,16 @@ void go_legal(const int8_t* b, int n, int player, int ko, uint8_t* mask) {
   mask[cells] = 1;
 }
 
+void go_features(const int8_t* const* hist, int cells, int to_move, float* out) {
+  const int opp = 3 - to_move;
+  for (int k = 0; k < 8; ++k)
+    for (int c = 0; c < cells; ++c) {
+      out[(size_t)k * cells + c] = hist[k][c] == to_move ? 1.0f : 0.0f;
+      out[(size_t)(8 + k) * cells + c] = hist[k][c] == opp ? 1.0f : 0.0f;
+    }
+  for (int c = 0; c < cells; ++c) out[(size_t)16 * cells + c] = to_move == 1 ? 1.0f : 0.0f;
+}
+
 }  // namespace oracle
 
 extern "C" int oracle_go_play(const int8_t* b, int n, int player, int action, int ko, int8_t* out,

@@ -13,6 +13,14 @@ namespace oracle {
 bool go_play(const int8_t* b, int n, int player, int action, int ko, int8_t* out, int* ko_out);
 // mask[n * n + 1]: legal actions of `player` (pass included).
 void go_legal(const int8_t* b, int n, int player, int ko, uint8_t* mask);
+
+// Network input for Go, 17 planes of `cells` (AlphaGo Zero layout; the reference has no Go
+// encoding of this size, so this is the engine's own definition): plane k (k = 0..7) holds the
+// side to move's stones k plies ago, plane 8 + k the opponent's, plane 16 is 1 when black
+// (player 1) is to move. hist[k] is the board k plies before the position (all-zero boards
+// before the game started).
+constexpr int kGoPlanes = 17;
+void go_features(const int8_t* const* hist, int cells, int to_move, float* out);
 }  // namespace oracle
 
 extern "C" {

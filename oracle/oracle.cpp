@@ -4,6 +4,7 @@
 // arithmetic is fp32 with one rounding per operation (built with -ffp-contract=off), in the
 // operand order the reference's torch expressions evaluate.
 #include "oracle.h"
+#include "go_rules.h"
 #include "gomoku_rules.h"
 #include "synth_eval.h"
 
@@ -30,7 +31,14 @@ struct Tree {
   std::vector<float> root_noise;  // by action, for the next wave only
   float noise_eps = 0.0f, noise_keep = 1.0f;
 
+  // Go (game == 1): actions = cells + 1 (pass last); per-node ko point and consecutive passes;
+  // positions before the root come from root_hist[1..7].
+  int game = 0, planes = oracle::kPlanes;
+  std::vector<int32_t> ko, passes;
+  std::vector<int8_t> root_hist;
+
   Tree(int cap_, int size_) : cap(cap_), size(size_), cells(size_ * size_), actions(size_ * size_) {
+    ko.assign(cap, -1); passes.assign(cap, 0);
     N.assign(cap, 0); VL.assign(cap, 0); parent.assign(cap, -2); action.assign(cap, -1);
     child_start.assign(cap, 0); child_count.assign(cap, 0); mc.assign(cap, 0);
     W.assign(cap, 0.f); P.assign(cap, 0.f); terminal.assign(cap, 0);
@@ -40,6 +48,14 @@ struct Tree {
   const int8_t* board(int n) const { return &boards[(size_t)n * cells]; }
 
   void features(int n, float* out) const {
+    if (game == 1) {
+      const int8_t* hist[8];
+      int cur = n, k = 0;
+      for (; k < 8 && cur >= 0; ++k, cur = parent[cur]) hist[k] = board(cur);
+      for (int j = 1; k < 8; ++k, ++j) hist[k] = &root_hist[(size_t)j * cells];
+      oracle::go_features(hist, cells, player[n], out);
+      return;
+    }
     oracle::gomoku_features(board(n), size, player[n], mc[n], n == 0 ? -1 : action[n], out);
   }
 
@@ -47,12 +63,14 @@ struct Tree {
   void evaluate(const std::vector<int>& nodes) {
     const int n = (int)nodes.size();
     if (n == 0) return;
-    feat.assign((size_t)n * oracle::kPlanes * cells, 0.f);
+    feat.assign((size_t)n * planes * cells, 0.f);
     pol.assign((size_t)n * actions, 0.f);
     val.assign(n, 0.f);
-    for (int i = 0; i < n; ++i) features(nodes[i], &feat[(size_t)i * oracle::kPlanes * cells]);
+    for (int i = 0; i < n; ++i) features(nodes[i], &feat[(size_t)i * planes * cells]);
     if (eval)
       eval(ctx, n, feat.data(), pol.data(), val.data());
+    else if (game == 1)
+      oracle_synth_eval_go(n, cells, actions, feat.data(), pol.data(), val.data());
     else
       oracle_synth_eval(n, oracle::kPlanes, cells, actions, feat.data(), pol.data(), val.data());
     res.eval_calls++;
@@ -89,8 +107,15 @@ struct Tree {
       const float* p = &pol_copy[i * actions];
       const int8_t* b = board(n);
       std::vector<int> legal;
-      for (int a = 0; a < actions; ++a)
-        if (b[a] == 0) legal.push_back(a);
+      if (game == 1) {
+        std::vector<uint8_t> m(actions);
+        oracle::go_legal(b, size, player[n], ko[n], m.data());
+        for (int a = 0; a < actions; ++a)
+          if (m[a]) legal.push_back(a);
+      } else {
+        for (int a = 0; a < actions; ++a)
+          if (b[a] == 0) legal.push_back(a);
+      }
       if (legal.empty()) continue;
       // priors = p[legal] / (sum(p[legal]) + 1e-8) (wave_search.py:894-895). The reference sums
       // with torch.sum; the summation order is fixed here as 32 strided partial sums (slot j
@@ -113,17 +138,54 @@ struct Tree {
         const int a = legal[j];
         N[c] = 0; W[c] = 0.f; VL[c] = 0; P[c] = p[a] / denom;
         parent[c] = n; action[c] = a; child_count[c] = 0;
-        std::memcpy(&boards[(size_t)c * cells], b, cells);
-        boards[(size_t)c * cells + a] = player[n];
         player[c] = (int8_t)(3 - player[n]);
         mc[c] = mc[n] + 1;
+        if (game == 1) {
+          int k2 = -1;
+          oracle::go_play(b, size, player[n], a, ko[n], &boards[(size_t)c * cells], &k2);
+          ko[c] = k2;
+          passes[c] = a == cells ? passes[n] + 1 : 0;
+          terminal[c] = passes[c] >= 2 ? 1 : 0;  // GoState::isTerminal (go_state.cpp:502-506)
+          continue;
+        }
+        std::memcpy(&boards[(size_t)c * cells], b, cells);
+        boards[(size_t)c * cells + a] = player[n];
         terminal[c] = oracle::gomoku_terminal(board(c), size) ? 1 : 0;
       }
     }
     return 0;
   }
 
+  // Go root: hist[8][cells] (hist[0] = the root position, hist[k] = k plies earlier, zeros where
+  // the game had not started), side to move, ko point (-1 none), consecutive passes.
+  int begin_go(const oracle_config* c, const int8_t* hist, int to_move, int root_ko,
+               int root_passes, oracle_eval_fn e, void* x) {
+    game = 1;
+    planes = oracle::kGoPlanes;
+    actions = cells + 1;
+    root_hist.assign(hist, hist + (size_t)8 * cells);
+    cfg = *c;
+    if (cfg.board_size != size || cfg.max_nodes > cap || cfg.max_wave_size <= 0) return 2;
+    eval = e; ctx = x;
+    res = oracle_result{};
+    num_nodes = 1;
+    N[0] = 0; W[0] = 0.f; VL[0] = 0; P[0] = 1.0f; parent[0] = -1; action[0] = -1;
+    child_count[0] = 0;
+    std::memcpy(boards.data(), hist, cells);
+    player[0] = (int8_t)to_move;
+    ko[0] = root_ko;
+    passes[0] = root_passes;
+    mc[0] = 0;
+    terminal[0] = root_passes >= 2 ? 1 : 0;
+    int st = expand({0});
+    res.status = st;
+    return st;
+  }
+
   int begin(const oracle_config* c, const int8_t* root, oracle_eval_fn e, void* x) {
+    game = 0;
+    planes = oracle::kPlanes;
+    actions = cells;
     cfg = *c;
     if (cfg.board_size != size || cfg.max_nodes > cap || cfg.max_wave_size <= 0) return 2;
     eval = e; ctx = x;
@@ -156,7 +218,7 @@ struct Tree {
         std::vector<int> kids;
         for (int j = 0; j < child_count[p]; ++j) {
           int c = child_start[p] + j;
-          if (p > 0 && board(p)[action[c]] != 0) continue;  // legal filter (no-op in Gomoku)
+          if (game == 0 && p > 0 && board(p)[action[c]] != 0) continue;  // legal filter (no-op in Gomoku)
           kids.push_back(c);
         }
         if (kids.empty()) {
@@ -222,7 +284,7 @@ struct Tree {
       float bs = 0.f;
       for (int j = 0; j < child_count[n]; ++j) {
         int c = child_start[n] + j;
-        if (board(n)[action[c]] != 0) continue;
+        if (game == 0 && board(n)[action[c]] != 0) continue;
         float s = score(c, N[n]);
         if (best < 0 || s > bs) { best = c; bs = s; }
       }
@@ -292,10 +354,26 @@ void oracle_get_result(void* t, oracle_result* out) {
   out->num_nodes = tr->num_nodes;
 }
 
+int oracle_begin_go(void* t, const oracle_config* cfg, const int8_t* hist, int to_move, int ko,
+                    int passes, oracle_eval_fn e, void* x) {
+  return static_cast<Tree*>(t)->begin_go(cfg, hist, to_move, ko, passes, e, x);
+}
+
+static int run_waves(Tree* tr, const oracle_config* cfg, int st, void* t, oracle_result* out);
+
+int oracle_search_go(void* t, const oracle_config* cfg, const int8_t* hist, int to_move, int ko,
+                     int passes, oracle_eval_fn e, void* x, oracle_result* out) {
+  Tree* tr = static_cast<Tree*>(t);
+  return run_waves(tr, cfg, tr->begin_go(cfg, hist, to_move, ko, passes, e, x), t, out);
+}
+
 int oracle_search(void* t, const oracle_config* cfg, const int8_t* root, oracle_eval_fn e,
                   void* x, oracle_result* out) {
   Tree* tr = static_cast<Tree*>(t);
-  int st = tr->begin(cfg, root, e, x);
+  return run_waves(tr, cfg, tr->begin(cfg, root, e, x), t, out);
+}
+
+static int run_waves(Tree* tr, const oracle_config* cfg, int st, void* t, oracle_result* out) {
   int done = 0;
   while (st == 0 && done < cfg->num_simulations) {
     int w = std::min(cfg->max_wave_size, cfg->num_simulations - done);
@@ -320,6 +398,8 @@ int oracle_export(void* t, int32_t* visits, float* wsum, float* priors, int32_t*
   if (terminal) std::memcpy(terminal, tr->terminal.data(), n);
   return (int)n;
 }
+
+int oracle_actions(void* t) { return static_cast<Tree*>(t)->actions; }
 
 int oracle_root_policy(void* t, double* policy) {
   Tree* tr = static_cast<Tree*>(t);

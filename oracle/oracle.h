@@ -59,6 +59,15 @@ int oracle_wave(void* tree, int wave_size);
 // priors become keep * P + eps * noise[action] in fp32, where keep is (float)(1 - (double)eps) as
 // the reference computes it in Python. Used to replay the noise a device run drew.
 int oracle_set_root_noise(void* tree, float eps, float keep, const float* noise_by_action);
+// Go root (go_rules.h): hist [8][board_size^2] (hist[0] = root position, hist[k] = k plies
+// earlier), side to move, ko point (-1 none), consecutive passes. Actions = cells + 1 (pass last).
+// Children are the rules' legal moves; a child whose pass makes two in a row is terminal.
+int oracle_begin_go(void* tree, const oracle_config* cfg, const int8_t* hist, int to_move, int ko,
+                    int passes, oracle_eval_fn eval, void* ctx);
+int oracle_search_go(void* tree, const oracle_config* cfg, const int8_t* hist, int to_move, int ko,
+                     int passes, oracle_eval_fn eval, void* ctx, oracle_result* out);
+// Action count of the last begun game (cells for Gomoku, cells + 1 for Go).
+int oracle_actions(void* tree);
 // Full search = begin + ceil(sims / max_wave_size) waves.
 int oracle_search(void* tree, const oracle_config* cfg, const int8_t* root_board,
                   oracle_eval_fn eval, void* ctx, oracle_result* out);
@@ -67,6 +76,6 @@ void oracle_get_result(void* tree, oracle_result* out);
 // Node arrays (length num_nodes). Any pointer may be NULL.
 int oracle_export(void* tree, int32_t* visits, float* value_sums, float* priors,
                   int32_t* virtual_loss, int32_t* parent, int32_t* action, uint8_t* terminal);
-// Root policy N_child / sum N_child in fp64 over board_size^2 actions (mcts.py:1069-1137).
+// Root policy N_child / sum N_child in fp64 over oracle_actions() actions (mcts.py:1069-1137).
 int oracle_root_policy(void* tree, double* policy);
 }

@@ -163,6 +163,17 @@ def lib():
         L.oracle_feature_hash.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
         L.oracle_synth_eval.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        L.oracle_begin_go.argtypes = [ctypes.c_void_p, ctypes.POINTER(OracleConfig), ctypes.c_void_p,
+                                      ctypes.c_int, ctypes.c_int, ctypes.c_int, EVAL_FN,
+                                      ctypes.c_void_p]
+        L.oracle_search_go.argtypes = [ctypes.c_void_p, ctypes.POINTER(OracleConfig),
+                                       ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                       EVAL_FN, ctypes.c_void_p, ctypes.POINTER(OracleResult)]
+        L.oracle_actions.argtypes = [ctypes.c_void_p]
+        L.oracle_feature_hash_go.restype = ctypes.c_uint64
+        L.oracle_feature_hash_go.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        L.oracle_synth_eval_go.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                           ctypes.c_void_p, ctypes.c_void_p]
         L.oracle_go_play.restype = ctypes.c_int
         L.oracle_go_play.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                      ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]
@@ -203,6 +214,17 @@ def c_synth_eval(features: np.ndarray, actions: int | None = None):
     return pol, val
 
 
+def c_synth_eval_go(features: np.ndarray):
+    """Go synthetic evaluator on 17-plane features [n, 17, H, W] -> (policy [n, H*W+1], value)."""
+    f = np.ascontiguousarray(features, dtype=np.float32)
+    B = f.shape[0]
+    cells = int(np.prod(f.shape[2:]))
+    pol = np.zeros((B, cells + 1), np.float32)
+    val = np.zeros(B, np.float32)
+    lib().oracle_synth_eval_go(B, cells, cells + 1, f.ctypes.data, pol.ctypes.data, val.ctypes.data)
+    return pol, val
+
+
 @dataclass
 class OracleTree:
     """Search result of the oracle: node arrays in creation order plus run statistics."""
@@ -217,6 +239,13 @@ class OracleTree:
     result: dict
 
 
+def _go_hist(hist, n):
+    h = np.asarray(hist, dtype=np.int8)
+    if h.ndim == 2:
+        h = np.concatenate([h[None], np.zeros((7, n, n), np.int8)])
+    return np.ascontiguousarray(h.reshape(8, n, n))
+
+
 class Oracle:
     """One oracle tree. ``evaluator`` is None (built-in synthetic) or a callable
     features[n,19,H,W] -> (policy[n,A], value[n])."""
@@ -228,6 +257,7 @@ class Oracle:
             raise ValueError("oracle_tree_create failed")
         self.max_nodes = max_nodes
         self.board_size = board_size
+        self.game = "gomoku"
         self._cb = None
 
     def __del__(self):
@@ -241,10 +271,12 @@ class Oracle:
         if evaluator is None:
             return EVAL_FN()
         H = self.board_size
-        A = H * H
+        go = self.game == "go"
+        A = H * H + (1 if go else 0)
+        planes = 17 if go else PLANES
 
         def cb(_ctx, n, feat, pol, val):
-            f = np.ctypeslib.as_array(feat, shape=(n, PLANES, H, H)).copy()
+            f = np.ctypeslib.as_array(feat, shape=(n, planes, H, H)).copy()
             p, v = evaluator(f)
             np.ctypeslib.as_array(pol, shape=(n, A))[:] = np.asarray(p, np.float32).reshape(n, A)
             np.ctypeslib.as_array(val, shape=(n,))[:] = np.asarray(v, np.float32).reshape(n)
@@ -254,7 +286,28 @@ class Oracle:
         return OracleConfig(self.board_size, sims, wave, c_puct, virtual_loss, int(enable_vl),
                             self.max_nodes, max_depth)
 
+    def begin_go(self, hist, to_move, cfg: OracleConfig, ko=-1, passes=0, evaluator=None) -> int:
+        """Go root: ``hist`` int8 [8, n, n] (hist[0] = the root position, hist[k] k plies
+        earlier); a single [n, n] board means no earlier positions."""
+        self.game = "go"
+        h = _go_hist(hist, self.board_size)
+        self._cb = self._make_cb(evaluator)
+        self._board = h
+        return self._L.oracle_begin_go(self._t, ctypes.byref(cfg), h.ctypes.data, int(to_move),
+                                       int(ko), int(passes), self._cb, None)
+
+    def search_go(self, hist, to_move, sims, wave, ko=-1, passes=0, evaluator=None, **kw) -> OracleTree:
+        self.game = "go"
+        cfg = self.config(sims, wave, **kw)
+        h = _go_hist(hist, self.board_size)
+        self._cb = self._make_cb(evaluator)
+        res = OracleResult()
+        self._L.oracle_search_go(self._t, ctypes.byref(cfg), h.ctypes.data, int(to_move), int(ko),
+                                 int(passes), self._cb, None, ctypes.byref(res))
+        return self.export()
+
     def begin(self, board, cfg: OracleConfig, evaluator=None) -> int:
+        self.game = "gomoku"
         b = np.ascontiguousarray(board, dtype=np.int8)
         self._cb = self._make_cb(evaluator)
         self._board = b
@@ -268,6 +321,7 @@ class Oracle:
         return self._L.oracle_wave(self._t, w)
 
     def search(self, board, sims, wave, evaluator=None, **kw) -> OracleTree:
+        self.game = "gomoku"
         cfg = self.config(sims, wave, **kw)
         b = np.ascontiguousarray(board, dtype=np.int8)
         self._cb = self._make_cb(evaluator)
@@ -287,7 +341,7 @@ class Oracle:
         self._L.oracle_export(self._t, *[arr[k].ctypes.data for k in
                                          ("visits", "value_sums", "priors", "virtual_loss",
                                           "parent", "action", "terminal")])
-        pol = np.zeros(self.board_size ** 2, np.float64)
+        pol = np.zeros(self._L.oracle_actions(self._t), np.float64)
         self._L.oracle_root_policy(self._t, pol.ctypes.data)
         result = {f: getattr(res, f) for f, _ in OracleResult._fields_}
         return OracleTree(policy=pol, result=result, **arr)

@@ -91,3 +91,30 @@ extern "C" void oracle_synth_eval(int n, int planes, int cells, int actions, con
     oracle::synth_from_hash(h, actions, legal.data(), policy + (size_t)i * actions, value + i);
   }
 }
+
+extern "C" uint64_t oracle_feature_hash_go(const float* f, int cells) {
+  uint64_t h = oracle::kHashSeed;
+  const int words = (cells + 63) / 64;
+  for (int c = 0; c < 17; ++c) {
+    const float* p = f + (size_t)c * cells;
+    for (int j = 0; j < words; ++j) {
+      uint64_t word = 0;
+      for (int b = 0; b < 64 && 64 * j + b < cells; ++b)
+        if (p[64 * j + b] != 0.0f) word |= 1ull << b;
+      h = oracle::mix64(h ^ word);
+    }
+  }
+  return h;
+}
+
+extern "C" void oracle_synth_eval_go(int n, int cells, int actions, const float* features,
+                                     float* policy, float* value) {
+  std::vector<uint8_t> legal(actions);
+  for (int i = 0; i < n; ++i) {
+    const float* f = features + (size_t)i * 17 * cells;
+    for (int a = 0; a < actions; ++a)
+      legal[a] = (a >= cells) || (f[a] == 0.0f && f[(size_t)8 * cells + a] == 0.0f);
+    uint64_t h = oracle_feature_hash_go(f, cells);
+    oracle::synth_from_hash(h, actions, legal.data(), policy + (size_t)i * actions, value + i);
+  }
+}

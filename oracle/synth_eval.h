@@ -23,9 +23,15 @@
 extern "C" {
 uint64_t oracle_feature_hash(const float* features, int planes, int cells);
 // features [n, planes, cells] fp32 -> policy [n, actions] fp32 (0 on illegal), value [n] fp32.
-// Legal = plane-0 cell empty (Gomoku/Go board actions); actions beyond `cells` (Go pass) get 0.
+// Legal = plane-0 cell empty (Gomoku/Go board actions); actions beyond `cells` count as legal.
 void oracle_synth_eval(int n, int planes, int cells, int actions, const float* features,
                        float* policy, float* value);
+// Go variant on the 17-plane Go features [n, 17, cells]: the hash folds all 17 planes binarised
+// (no special plane), and the legal set is the empty points (planes 0 and 8 clear) plus pass
+// (action == cells). Expansion renormalises over the rules' legal set afterwards.
+uint64_t oracle_feature_hash_go(const float* features, int cells);
+void oracle_synth_eval_go(int n, int cells, int actions, const float* features, float* policy,
+                          float* value);
 }
 
 namespace oracle {

@@ -52,3 +52,54 @@ def test_go_illegal_moves_and_ko(oracle_lib):
     assert not oracle_lib.go_legal(nb, 2, ko)[ko]
     assert oracle_lib.go_legal(nb, 2, -1)[ko]           # legal once the ko point is cleared
     assert oracle_lib.go_play(nb, 2, 25, ko)[1] == -1   # pass clears the ko
+
+
+def test_host_go_position_replays_reference_games():
+    """The package's host-side Go position (root construction, moves between searches) follows
+    the same reference games."""
+    from omoknuni_quantum_b200.go import GoPosition
+    for n, boards, players, legal, moves in _games():
+        g = GoPosition(n)
+        for t in range(len(moves)):
+            assert np.array_equal(g.board, boards[t]) and g.to_move == players[t]
+            if t % 7 == 0:  # the full mask is slow in pure Python; sample plies
+                assert np.array_equal(g.legal_mask(), legal[t]), (n, t)
+            g.play(int(moves[t]))
+
+
+def test_go_roots_are_seeded_and_legal(oracle_lib):
+    from omoknuni_quantum_b200.go import random_roots
+    h, m = random_roots(3, 2, moves=60, board_size=9)
+    h2, m2 = random_roots(3, 2, moves=60, board_size=9)
+    assert np.array_equal(h, h2) and np.array_equal(m, m2)
+    assert h.shape == (2, 8, 9, 9) and m.shape == (2, 3)
+    assert (m[:, 0] == 1).all()                      # 60 moves: black to move
+    for i in range(2):
+        # consecutive history boards differ by one legal move each
+        for k in range(7, 0, -1):
+            prev, nxt = h[i, k], h[i, k - 1]
+            mover = 1 if (60 - k) % 2 == 0 else 2
+            a = np.flatnonzero((prev.reshape(-1) == 0) & (nxt.reshape(-1) == mover))
+            assert len(a) == 1
+            res = oracle_lib.go_play(prev, mover, int(a[0]))
+            assert res is not None and np.array_equal(res[0], nxt)
+
+
+def test_oracle_go_search_invariants(oracle_lib):
+    """Oracle Go search: children of every expanded node are exactly the rules' legal moves (pass
+    included, ascending), priors sum to 1, visits add up, double-pass children are terminal."""
+    from omoknuni_quantum_b200.go import random_position
+    g = random_position(5, moves=30, board_size=9)
+    o = oracle_lib.Oracle(60000, 9)
+    t = o.search_go(g.history_planes(), g.to_move, 256, 64, ko=g.ko, passes=g.passes)
+    assert t.result["status"] == 0
+    assert t.visits[0] == 256 and t.policy.shape == (82,)
+    kids = t.parent == 0
+    assert np.array_equal(np.sort(t.action[kids]), np.flatnonzero(g.legal_mask()))
+    assert abs(t.priors[kids].sum() - 1.0) < 1e-5
+    assert t.visits[0] == t.visits[kids].sum() + 0  # every simulation passes through a child
+    # a pass child of a pass child is terminal
+    pass_nodes = np.flatnonzero(t.action == 81)
+    for c in pass_nodes:
+        p = t.parent[c]
+        assert bool(t.terminal[c]) == (p > 0 and t.action[p] == 81)
