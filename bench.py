@@ -35,6 +35,9 @@ sys.path.insert(0, REPO)
 
 METRIC = "MCTS simulations/sec (device-timed, whole box)"
 UNIT = "simulations/s"
+WORKLOAD_GO = ("config3: Go 19x19 (captures, no suicide, simple ko, pass), 3200 sims/root, wave 512, "
+               "1M-node trees, ResNet 20x256 bf16 on 17 history planes, 362 actions; 256 roots sharded "
+               "across GPUs, searched in lockstep")
 WORKLOAD = ("config1: Gomoku 15x15 single-tree searches, 1600 sims/root, wave 256, c_puct 1.4, "
             "VL 1.0, ResNet 10x128 bf16 evaluator; independent roots searched in lockstep per GPU")
 
@@ -56,8 +59,9 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", choices=["config1", "config2"], default="config1",
-                    help="config2 = batched self-play: 512 games (sharded), 800 sims, wave 64, 20x256")
+    ap.add_argument("--workload", choices=["config1", "config2", "config3"], default="config1",
+                    help="config2 = batched self-play: 512 games (sharded), 800 sims, wave 64, 20x256; "
+                         "config3 = Go 19x19: 256 roots (sharded), 3200 sims, wave 512, 1M nodes, 20x256")
     ap.add_argument("--evaluator", choices=["resnet", "synthetic"], default="resnet",
                     help="synthetic = BASELINE config 0 (tree kernels only; 800 sims, 200k nodes)")
     return ap.parse_args()
@@ -159,18 +163,30 @@ class ClockSampler:
 
 def make_spec(args):
     from omoknuni_quantum_b200.resnet import ResNetSpec
+    if args.workload == "config3":
+        return ResNetSpec(board_size=19, input_channels=17, num_blocks=args.blocks,
+                          filters=args.filters, num_actions=362, fc_policy_hidden=256,
+                          fc_value_hidden=args.value_hidden)
     return ResNetSpec(board_size=15, input_channels=19, num_blocks=args.blocks, filters=args.filters,
                       num_actions=225, fc_policy_hidden=256, fc_value_hidden=args.value_hidden)
+
+
+def apply_config3(args):
+    """Go 19x19, 3200 sims per root, wave 512, 1M-node trees, ResNet 20x256
+    (value FC 361 -> 256 -> 1); 256 roots sharded across the GPUs."""
+    args.sims, args.wave, args.capacity = 3200, 512, 1_000_000
+    args.blocks, args.filters, args.value_hidden = 20, 256, 256
 
 
 # ---------------------------------------------------------------------------------------------
 # CPU arms
 # ---------------------------------------------------------------------------------------------
-def cpu_search_rate(args, sd, budget_s: float):
+def cpu_search_rate(args, sd, budget_s: float, game: str = "gomoku"):
     """Reference algorithm on the host: oracle tree search (C++ restatement of the reference's
     torch WaveSearch) + fp32 torch ResNet forward on all host cores. Searches seeded roots of
     the workload until `budget_s` of work is done; returns (sims/s, sims, seconds, threads)."""
     from oracle import pyoracle
+    from omoknuni_quantum_b200 import go as gomod
     from omoknuni_quantum_b200.resnet import reference_forward_fp32
     from omoknuni_quantum_b200.roots import random_root
     threads = os.cpu_count() or 1
@@ -185,9 +201,16 @@ def cpu_search_rate(args, sd, budget_s: float):
     sims_done, t0 = 0, time.perf_counter()
     r = 0
     while True:
-        o = pyoracle.Oracle(args.capacity)
-        cfg = o.config(args.sims, args.wave)
-        if o.begin(random_root(args.seed * 7919 + r), cfg, evaluator=ev) != 0:
+        if game == "go":
+            o = pyoracle.Oracle(args.capacity, 19)
+            cfg = o.config(args.sims, args.wave)
+            g = gomod.random_position(args.seed * 7919 + r, 60, 19)
+            st = o.begin_go(g.history_planes(), g.to_move, cfg, ko=g.ko, passes=g.passes, evaluator=ev)
+        else:
+            o = pyoracle.Oracle(args.capacity)
+            cfg = o.config(args.sims, args.wave)
+            st = o.begin(random_root(args.seed * 7919 + r), cfg, evaluator=ev)
+        if st != 0:
             raise RuntimeError("oracle begin failed")
         done = 0
         while done < args.sims:
@@ -210,26 +233,30 @@ def run_reference_arm(args):
     if rank != 0:
         return
     from omoknuni_quantum_b200.resnet import init_state_dict
+    game = "go" if args.workload == "config3" else "gomoku"
+    if game == "go":
+        apply_config3(args)
     sd = init_state_dict(make_spec(args), seed=args.seed)
     budget = max(2.0, args.cpu_seconds / max(1, args.steps))
     for _ in range(max(0, min(args.warmup, 1))):
-        cpu_search_rate(args, sd, 1.0)
+        cpu_search_rate(args, sd, 1.0, game)
     rates, sims_total, secs_total = [], 0, 0.0
     threads = 1
     for _ in range(args.steps):
-        rate, sims, secs, threads = cpu_search_rate(args, sd, budget)
+        rate, sims, secs, threads = cpu_search_rate(args, sd, budget, game)
         rates.append(rate)
         sims_total += sims
         secs_total += secs
     value = sims_total / secs_total
-    sample = (f"{sims_total} simulations of config-1 searches (seeded roots, 1600 sims each, "
-              f"wave 256) in {secs_total:.1f} s, fp32 CPU ResNet 10x128")
+    sample = (f"{sims_total} simulations of {args.workload} searches (seeded roots, {args.sims} sims "
+              f"each, wave {args.wave}) in {secs_total:.1f} s, fp32 CPU ResNet {args.blocks}x{args.filters}")
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 * secs_total / max(1, args.steps),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded roots, seeded He-init weights)", "impl": "reference",
-            "config": {"workload": WORKLOAD, "sims": args.sims, "wave": args.wave,
-                       "model": f"resnet{args.blocks}x{args.filters}", "parallelism": "host threads"},
+            "config": {"workload": WORKLOAD_GO if game == "go" else WORKLOAD, "sims": args.sims,
+                       "wave": args.wave, "model": f"resnet{args.blocks}x{args.filters}",
+                       "parallelism": "host threads"},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -473,8 +500,134 @@ def run_b200_selfplay(args):
         dist.destroy_process_group()
 
 
+def run_b200_go(args):
+    """Config 3 on the device: Go roots (60 random legal moves each), ResNet 20x256 evaluator."""
+    ws, rank, local = dist_env()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py --impl b200 needs a CUDA device")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    from omoknuni_quantum_b200 import _lib, parallel
+    from omoknuni_quantum_b200 import go as gomod
+    from omoknuni_quantum_b200.engine import WaveEngine
+    from omoknuni_quantum_b200.mcts import MCTS
+    from omoknuni_quantum_b200.mcts_config import GameType, MCTSConfig
+    from omoknuni_quantum_b200.resnet import ResNetEvaluator, init_state_dict
+
+    apply_config3(args)
+    spec = make_spec(args)
+    sd = parallel.broadcast_state_dict(init_state_dict(spec, seed=args.seed), dev)
+    total_roots = args.roots
+    R = total_roots // ws + (1 if rank < total_roots % ws else 0)
+    first = sum(total_roots // ws + (1 if q < total_roots % ws else 0) for q in range(rank))
+    positions_host = [gomod.random_position(args.seed * 1_000_003 + first + i, 60, 19) for i in range(R)]
+    hist = torch.from_numpy(np.stack([g.history_planes() for g in positions_host])).to(dev)
+    meta = torch.from_numpy(np.stack([g.meta() for g in positions_host])).to(dev)
+    ev = ResNetEvaluator(sd, board_size=19, max_batch=R * args.wave, device=dev)
+    eng = WaveEngine(R, board_size=19, capacity=args.capacity, max_wave_size=args.wave, c_puct=1.4,
+                     virtual_loss=1.0, device=dev, game="go")
+
+    def barrier():
+        if ws > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        eng.search(hist, args.sims, evaluator=ev, meta=meta)
+    barrier()
+    ev.profile(1 << 14)
+    launches0 = _lib.kernel_launches()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        start.record()
+        for _ in range(args.steps):
+            eng.search(hist, args.sims, evaluator=ev, meta=meta)
+        end.record()
+        barrier()
+    launches = _lib.kernel_launches() - launches0
+    ms = start.elapsed_time(end)
+    trunk_ms, counts = ev.profile_read()
+    ev.profile(0)
+    ms_max = parallel.max_over_ranks(ms, dev)
+    total_sims = int(parallel.sum_over_ranks(args.sims * R * args.steps, dev))
+    value = total_sims / (ms_max / 1000.0)
+    positions = int(counts.sum())
+    nodes = int(eng.num_nodes().max())
+
+    peaks, peak_kind = measured_peaks()
+    conv_launches = len(trunk_ms) * ev.conv_launches_per_call
+    flops = positions * ev.trunk_flops_per_position()
+    avg_launch_s = float(trunk_ms.sum()) / 1000.0 / max(1, conv_launches)
+    achieved = (flops / max(1, conv_launches)) / avg_launch_s / 1e12 if avg_launch_s > 0 else 0.0
+    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    roofline = {"kernel": "k_conv3x3_pair<256> (tcgen05 cta_group::2 implicit-GEMM 3x3 conv, 20x20 "
+                          "padded pixel grid)", "bound": "tensor", "achieved": achieved, "peak": peak,
+                "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_kind": f"bf16_tflops_sustained of {peak_kind}", "traffic": None,
+                "algorithmic_flops_per_launch": flops / max(1, conv_launches),
+                "avg_launch_ms": avg_launch_s * 1e3, "launches": conv_launches}
+
+    e2e = None
+    if not args.no_e2e:
+        cfg = MCTSConfig(game_type=GameType.GO, board_size=19, num_simulations=args.sims,
+                         max_wave_size=args.wave, c_puct=1.4, virtual_loss=1.0,
+                         initial_tree_nodes=args.capacity, device=str(dev),
+                         enable_subtree_reuse=False, dirichlet_epsilon=0.0)
+        mcts = MCTS(cfg, ev)
+        mcts._engines[R] = eng
+        mcts.search_batch(positions_host)
+        barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(args.steps):
+            pol = mcts.search_batch(positions_host)
+        e2.record()
+        barrier()
+        ms2 = parallel.max_over_ranks(s2.elapsed_time(e2), dev)
+        assert pol.shape == (R, 362) and np.allclose(pol.sum(1), 1.0)
+        e2e = {"value": total_sims / (ms2 / 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": R * (8 * 361 + 12), "d2h_bytes_per_step": R * 362 * 4,
+               "api": "MCTS(MCTSConfig(game_type=GO), ResNetEvaluator).search_batch(GoPositions) -> numpy policies"}
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        rate, sims, secs, threads = cpu_search_rate(args, sd, args.cpu_seconds, "go")
+        cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{sims} simulations of config-3 Go searches in {secs:.1f} s (oracle C++ tree "
+                         f"with Go rules + fp32 torch CPU ResNet 20x256)"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded Go roots, seeded He-init weights)",
+            "config": {"workload": WORKLOAD_GO, "roots_total": total_roots, "roots_per_gpu": R,
+                       "sims": args.sims, "wave": args.wave, "capacity": args.capacity,
+                       "model": "resnet20x256 (17 planes, 362 actions, value fc 256)",
+                       "parallelism": f"dp{ws} (roots sharded, weights NCCL-broadcast once)",
+                       "l2": "inputs larger than L2 (multi-GB activations per ResNet call)"},
+            "leaf_evals_per_s": positions / (ms / 1000.0) * ws,
+            "max_tree_nodes": nodes,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
+            "gpu_launches": launches,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
+    if args.workload == "config3" and args.impl == "b200":
+        run_b200_go(args)
+        return
     if args.workload == "config2" and args.impl == "b200":
         run_b200_selfplay(args)
         return

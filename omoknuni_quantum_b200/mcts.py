@@ -56,9 +56,10 @@ class MCTS:
         self.config = config
         self.game_interface = game_interface
         self.single_gpu_mode = single_gpu_mode
-        if config.game_type != GameType.GOMOKU:
+        if config.game_type not in (GameType.GOMOKU, GameType.GO):
             raise NotImplementedError(
-                f"device rules exist for Gomoku only; got {GameType(config.game_type).name}")
+                f"device rules exist for Gomoku and Go; got {GameType(config.game_type).name}")
+        self.is_go = config.game_type == GameType.GO
         self.evaluator = evaluator
         self._eval = _resolve_evaluator(evaluator)
         if hasattr(evaluator, "_return_torch_tensors"):
@@ -78,7 +79,7 @@ class MCTS:
     # -- engines -------------------------------------------------------------------------------
     @property
     def action_size(self) -> int:
-        return self.config.board_size ** 2
+        return self.config.board_size ** 2 + (1 if self.is_go else 0)
 
     def _engine(self, num_trees: int) -> WaveEngine:
         eng = self._engines.get(num_trees)
@@ -93,7 +94,7 @@ class MCTS:
                              virtual_loss=c.virtual_loss, enable_virtual_loss=c.enable_virtual_loss,
                              max_depth=c.max_depth, device=self.device,
                              dirichlet_alpha=c.dirichlet_alpha, dirichlet_epsilon=c.dirichlet_epsilon,
-                             noise_seed=self._noise_seed)
+                             noise_seed=self._noise_seed, game="go" if self.is_go else "gomoku")
             self._engines[num_trees] = eng
         return eng
 
@@ -110,9 +111,48 @@ class MCTS:
             return state.astype(np.int8, copy=False)
         raise TypeError("state must be a numpy/torch board [n, n] with 0 empty, 1 black, 2 white")
 
+    def _go_root(self, state):
+        """(history int8 [8, n, n], meta int32 [3]) of a Go root: a GoPosition of this package,
+        an object with the reference IGameState interface (rebuilt by replaying
+        get_move_history(), pass = -1, from the empty board), or a bare board (side to move by
+        stone parity as mcts.py:1509-1519, no ko, no earlier positions)."""
+        from .go import GoPosition
+        n = self.config.board_size
+        if isinstance(state, GoPosition):
+            return state.history_planes(), state.meta()
+        if hasattr(state, "get_move_history"):
+            g = GoPosition(n)
+            for m in state.get_move_history():
+                g.play(g.pass_action if int(m) < 0 else int(m))
+            return g.history_planes(), g.meta()
+        b = self._boards(state)
+        b = b.cpu().numpy() if torch.is_tensor(b) else np.asarray(b)
+        h = np.zeros((8, n, n), np.int8)
+        h[0] = b
+        stones = int((b != 0).sum())
+        return h, np.array([1 if stones % 2 == 0 else 2, -1, 0], np.int32)
+
+    def _search_go(self, states, sims: int) -> np.ndarray:
+        roots = [self._go_root(s) for s in states]
+        R = len(roots)
+        if sims == 0:
+            return np.full((R, self.action_size), 1.0 / self.action_size)
+        eng = self._engine(R)
+        t0 = time.perf_counter()
+        hist = torch.from_numpy(np.stack([r[0] for r in roots])).to(self.device)
+        meta = torch.from_numpy(np.stack([r[1] for r in roots])).to(self.device)
+        eng.search(hist, sims, self._eval, meta=meta)
+        visits = eng.root_visits().cpu().numpy()
+        self._last_tree = (eng, 0)
+        self._update_statistics(sims * R, time.perf_counter() - t0)
+        return self._policies(visits, eng)
+
     # -- search --------------------------------------------------------------------------------
     def search(self, state: Any, num_simulations: Optional[int] = None) -> np.ndarray:
-        """Policy (fp64 [board_size**2]) = root-child visit share (mcts.py:924-979)."""
+        """Policy (fp64 [actions]) = root-child visit share (mcts.py:924-979)."""
+        if self.is_go:
+            self._root_state = state
+            return self._search_go([state], int(num_simulations or self.config.num_simulations))[0]
         board = self._boards(state)
         pol = self.search_batch(board[None], num_simulations)[0]
         if torch.is_tensor(board):
@@ -122,6 +162,8 @@ class MCTS:
 
     def search_batch(self, states, num_simulations: Optional[int] = None) -> np.ndarray:
         """Independent searches of several roots in lockstep on the device; policies [R, A]."""
+        if self.is_go:
+            return self._search_go(list(states), int(num_simulations or self.config.num_simulations))
         boards = self._boards(states)
         if boards.ndim == 2:
             boards = boards[None]
@@ -173,7 +215,7 @@ class MCTS:
             raise ValueError(f"Invalid action {action}. Must be in range [0, {self.action_size})")
         self._last_tree = None
         if new_state is not None:
-            self._root_state = self._boards(new_state)
+            self._root_state = new_state if self.is_go else self._boards(new_state)
 
     def clear(self) -> None:
         self._last_tree = None

@@ -74,3 +74,39 @@ def test_roots_are_seeded_and_five_free():
     five[2, 4:9] = 2
     assert has_five(five) and has_five(five.T) and has_five(np.eye(15, dtype=np.int8))
     assert has_five(np.fliplr(np.eye(15, dtype=np.int8)))
+
+
+def test_mcts_go_roots_from_positions_and_move_histories():
+    """MCTS(GameType.GO): 362 actions; a reference-style state (IGameState.get_move_history, pass
+    = -1) is rebuilt into the same root record as the package's GoPosition; chess is refused."""
+    import numpy as np
+    import pytest
+    from omoknuni_quantum_b200.go import GoPosition, random_position
+    from omoknuni_quantum_b200.mcts import MCTS
+    from omoknuni_quantum_b200.mcts_config import GameType, MCTSConfig
+    m = MCTS(MCTSConfig(game_type=GameType.GO, board_size=9), "synthetic")
+    assert m.action_size == 82
+    g = random_position(4, moves=20, board_size=9)
+    g.play(g.pass_action)
+    moves = []
+    replay = GoPosition(9)
+    # reconstruct the move list from the position's history is not possible in general; record it
+    rng = np.random.default_rng(4)
+    for _ in range(20):
+        cand = np.flatnonzero(replay.legal_mask()[:-1])
+        a = int(cand[rng.integers(len(cand))])
+        replay.play(a)
+        moves.append(a)
+    replay.play(replay.pass_action)
+    moves.append(-1)
+
+    class FakeGoState:
+        def get_move_history(self):
+            return list(moves)
+
+    h1, m1 = m._go_root(FakeGoState())
+    h2, m2 = m._go_root(g)
+    assert np.array_equal(h1, h2) and np.array_equal(m1, m2)
+    assert m1[2] == 1                                     # one pass made
+    with pytest.raises(NotImplementedError):
+        MCTS(MCTSConfig(game_type=GameType.CHESS), "synthetic")
