@@ -174,6 +174,14 @@ def lib():
         L.oracle_feature_hash_go.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.oracle_synth_eval_go.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                            ctypes.c_void_p, ctypes.c_void_p]
+        L.oracle_chess_from_fen.argtypes = [ctypes.c_char_p, ctypes.c_void_p]
+        L.oracle_chess_legal.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        L.oracle_chess_play.argtypes = [ctypes.c_void_p, ctypes.c_int32]
+        L.oracle_chess_terminal.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+        L.oracle_chess_same.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        L.oracle_chess_action.argtypes = [ctypes.c_void_p, ctypes.c_int32]
+        L.oracle_chess_move.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        L.oracle_chess_features.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         L.oracle_go_play.restype = ctypes.c_int
         L.oracle_go_play.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                      ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]
@@ -181,6 +189,56 @@ def lib():
                                       ctypes.c_void_p]
         _lib = L
     return _lib
+
+
+CHESS_POS = np.dtype([("sq", np.int8, 64), ("side", np.int8), ("castle", np.int8), ("ep", np.int8),
+                      ("reps", np.int8), ("halfmove", np.int16), ("fullmove", np.int16)])
+
+
+def chess_from_fen(fen: str) -> np.ndarray:
+    """Oracle chess position record (chess_rules.h) from a FEN string."""
+    p = np.zeros(1, CHESS_POS)
+    if lib().oracle_chess_from_fen(fen.encode(), p.ctypes.data) != 0:
+        raise ValueError(f"bad FEN {fen!r}")
+    return p[0]
+
+
+def _pos_buf(p):
+    return np.ascontiguousarray(np.array(p, dtype=CHESS_POS).reshape(1))
+
+
+def chess_legal(p) -> np.ndarray:
+    """Legal moves in the reference encoding (promotion << 12 | from << 6 | to), sorted."""
+    b = _pos_buf(p)
+    m = np.zeros(320, np.int32)
+    n = lib().oracle_chess_legal(b.ctypes.data, m.ctypes.data)
+    return np.sort(m[:n])
+
+
+def chess_play(p, move: int) -> np.ndarray:
+    b = _pos_buf(p)
+    lib().oracle_chess_play(b.ctypes.data, int(move))
+    return b[0]
+
+
+def chess_terminal(p, reps: int = 1):
+    b = _pos_buf(p)
+    r = ctypes.c_int(0)
+    t = lib().oracle_chess_terminal(b.ctypes.data, int(reps), ctypes.byref(r))
+    return bool(t), int(r.value)
+
+
+def chess_same(a, b) -> bool:
+    x, y = _pos_buf(a), _pos_buf(b)
+    return bool(lib().oracle_chess_same(x.ctypes.data, y.ctypes.data))
+
+
+def chess_action(p, move: int) -> int:
+    return int(lib().oracle_chess_action(_pos_buf(p).ctypes.data, int(move)))
+
+
+def chess_move(p, action: int) -> int:
+    return int(lib().oracle_chess_move(_pos_buf(p).ctypes.data, int(action)))
 
 
 def go_play(board: np.ndarray, player: int, action: int, ko: int = -1):

@@ -1,0 +1,49 @@
+"""The oracle's chess rules replay the reference engine's games (tests/golden/chess_rules.npz, made
+by tests/golden/make_golden_chess.py from alphazero_py.ChessState): every ply's legal move list,
+terminal flag and result, and every resulting position (board, side, castling rights, en-passant
+square, clocks), bit for bit - including the engine's mirrored pawn-attack test and the
+repetition rule over the game's positions."""
+import os
+
+import numpy as np
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "chess_rules.npz")
+
+
+def _games():
+    z = np.load(GOLD)
+    go, off = z["game_off"], z["legal_off"]
+    for g in range(len(go) - 1):
+        yield [(str(z["fens"][i]), z["legal"][off[i]:off[i + 1]], bool(z["terminal"][i]),
+                int(z["result"][i]), int(z["moves"][i])) for i in range(go[g], go[g + 1])]
+
+
+def test_chess_oracle_replays_reference_games(oracle_lib):
+    plies = terminal = 0
+    for game in _games():
+        pos = oracle_lib.chess_from_fen(game[0][0])
+        seen = [pos]
+        for t, (fen, legal, term, res, move) in enumerate(game):
+            want = oracle_lib.chess_from_fen(fen)
+            assert oracle_lib.chess_same(pos, want), (fen, t)
+            assert pos["halfmove"] == want["halfmove"] and pos["fullmove"] == want["fullmove"], fen
+            assert np.array_equal(oracle_lib.chess_legal(pos), legal), fen
+            reps = sum(oracle_lib.chess_same(pos, q) for q in seen)
+            assert oracle_lib.chess_terminal(pos, reps) == (term, res if term else 0), fen
+            plies += 1
+            terminal += term
+            if move < 0:
+                break
+            pos = oracle_lib.chess_play(pos, move)
+            seen.append(pos)
+    assert plies > 2000 and terminal >= 15
+
+
+def test_chess_action_encoding_round_trips(oracle_lib):
+    """Every legal move of the fixture positions maps to a distinct action in [0, 4672) and back."""
+    for game in list(_games())[:14]:
+        for fen, legal, *_ in game[:40]:
+            pos = oracle_lib.chess_from_fen(fen)
+            acts = [oracle_lib.chess_action(pos, int(m)) for m in legal]
+            assert all(0 <= a < 4672 for a in acts) and len(set(acts)) == len(acts)
+            assert [oracle_lib.chess_move(pos, a) for a in acts] == [int(m) for m in legal]
