@@ -324,7 +324,8 @@ __global__ void __launch_bounds__(kGoWarps * 32) k_pack_queue_go(EngineView v, i
   }
 }
 
-void launch_pack_queue(const EngineView& v, int queue, int P, void* out, cudaStream_t s) {
+void launch_pack_queue(const EngineView& v, int queue, int P, int in_pad, void* out, cudaStream_t s) {
+  (void)in_pad;  // Gomoku and Go pack 64 channels
   if (v.game == OMQ_GAME_GO) {
     const int cap = v.R * v.WCAP;
     count_launches(1);

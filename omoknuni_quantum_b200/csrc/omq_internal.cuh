@@ -195,6 +195,8 @@ void launch_export(const EngineView& v, int tree, int count, int32_t* N, float* 
 void launch_status(const EngineView& v, int32_t* status, int32_t* num_nodes, cudaStream_t s);
 void launch_features(const EngineView& v, int queue, float* out, cudaStream_t s);
 void launch_synth_eval(const EngineView& v, int queue, cudaStream_t s);
-// queue positions -> bf16 [count][P][64] padded pixel layout (ResNet input)
-void launch_pack_queue(const EngineView& v, int queue, int P, void* out, cudaStream_t s);
+// queue positions -> bf16 [count][P][in_pad] padded pixel layout (ResNet input)
+void launch_pack_queue(const EngineView& v, int queue, int P, int in_pad, void* out, cudaStream_t s);
+// feature planes of the engine's game (19 Gomoku, 17 Go)
+inline int engine_planes(const EngineView& v) { return v.game == OMQ_GAME_GO ? 17 : 19; }
 }  // namespace omq

@@ -32,7 +32,10 @@ namespace omq {
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait before giving up
 constexpr int kTileM = 128;
 constexpr int kBlockK = 64;     // 64 bf16 = one 128-byte swizzle row
-constexpr int kInPad = 64;      // input planes padded to one K block
+constexpr int kInPad = 64;      // input planes padded to one K block (two for more than 64 planes)
+__host__ __device__ constexpr int in_pad_of(int planes) { return planes <= kInPad ? kInPad : 2 * kInPad; }
+constexpr int kMaxInputPlanes = 2 * kInPad;
+constexpr int kMaxActions = 5000;
 
 struct ConvArgs {
   const float* bias;
@@ -935,15 +938,16 @@ __global__ void __launch_bounds__(HaloCfg::kThreads, 1)
 __host__ __device__ constexpr int conv_sub(int filters) { return filters == 128 ? 2 : 1; }
 
 // ---------------------------------------------------------------------------------------------
-// input packing: reference fp32 features [n][19][S][S] -> bf16 [n][P][64] padded pixel space
+// input packing: reference fp32 features [n][planes][S][S] -> bf16 [n][P][in_pad] padded pixel space
 // ---------------------------------------------------------------------------------------------
 __global__ void k_pack_features(const float* feat, int planes, int S, int P, const int32_t* d_count,
                                 int count, __nv_bfloat16* out) {
   const int n = d_count ? min(*d_count, count) : count;
   const int total = n * P;
   const int C = S * S;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total * 8; i += gridDim.x * blockDim.x) {
-    const int row = i >> 3, chunk = i & 7;   // 8 chunks of 8 channels per pixel
+  const int chunks = in_pad_of(planes) / 8;  // chunks of 8 channels per pixel
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total * chunks; i += gridDim.x * blockDim.x) {
+    const int row = i / chunks, chunk = i - row * chunks;
     const int b = row / P, pix = row - b * P;
     const int y = pix / (S + 1), x = pix - y * (S + 1);
     uint4 u = make_uint4(0, 0, 0, 0);
@@ -957,7 +961,7 @@ __global__ void k_pack_features(const float* feat, int planes, int S, int P, con
       }
       u = *reinterpret_cast<uint4*>(h);
     }
-    reinterpret_cast<uint4*>(out)[(size_t)row * 8 + chunk] = u;
+    reinterpret_cast<uint4*>(out)[(size_t)row * chunks + chunk] = u;
   }
 }
 
@@ -1105,7 +1109,8 @@ struct omq_resnet {
   __nv_bfloat16* conv_w;   // (1 + 2*NB) convs
   float* conv_b;
   float* head;
-  __nv_bfloat16* x_in;     // [rows][64]
+  __nv_bfloat16* x_in;     // [rows][in_pad]
+  int in_pad;              // input channels padded to 64 or 128
   __nv_bfloat16* act[3];   // [rows][C]
   int32_t* error;
   CUtensorMap tmA_in, tmA[3], tmB_in;
@@ -1180,11 +1185,11 @@ static int conv_variant(int filters) {
 static int build_maps(omq_resnet* n) {
   const uint32_t a_rows = n->pair == 1 ? kTileM : n->pair == 3 ? HaloCfg::kHaloBox : kTileM * conv_sub(n->C);
   const uint32_t b_rows = n->pair == 1 ? n->C / 2 : n->C;
-  int st = make_map(&n->tmA_in, n->x_in, kInPad, n->rows, a_rows);
+  int st = make_map(&n->tmA_in, n->x_in, n->in_pad, n->rows, a_rows);
   for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n->tmA[i], n->act[i], n->C, n->rows, a_rows);
   for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_out_map(&n->tmO[i], n->act[i], n->C, n->rows);
-  if (st == OMQ_OK) st = make_map(&n->tmB_in, n->conv_w, 9 * kInPad, n->C, b_rows);
-  const __nv_bfloat16* wb = n->conv_w + (size_t)n->C * 9 * kInPad;
+  if (st == OMQ_OK) st = make_map(&n->tmB_in, n->conv_w, 9 * n->in_pad, n->C, b_rows);
+  const __nv_bfloat16* wb = n->conv_w + (size_t)n->C * 9 * n->in_pad;
   for (int i = 0; st == OMQ_OK && i < 2 * n->NB; ++i)
     st = make_map(&n->tmB[i], wb + (size_t)i * n->C * 9 * n->C, 9 * n->C, n->C, b_rows);
   return st;
@@ -1205,9 +1210,9 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
   if (!cfg || !out) { set_error("null argument"); return OMQ_BAD_ARG; }
   *out = nullptr;
   const omq_resnet_config c = *cfg;
-  if (c.board_size < 5 || c.board_size > 19 || c.input_channels < 1 || c.input_channels > kInPad ||
+  if (c.board_size < 5 || c.board_size > 19 || c.input_channels < 1 || c.input_channels > kMaxInputPlanes ||
       (c.filters != 128 && c.filters != 256) || c.num_blocks < 0 || c.num_blocks > 64 ||
-      c.num_actions < 1 || c.num_actions > 4096 || c.fc_policy_hidden < 1 ||
+      c.num_actions < 1 || c.num_actions > kMaxActions || c.fc_policy_hidden < 1 ||
       c.fc_policy_hidden > 1024 || c.fc_value_hidden < 1 || c.fc_value_hidden > 1024 ||
       c.max_batch < 1) {
     set_error("bad resnet config");
@@ -1227,15 +1232,21 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
   n->Hv = c.fc_value_hidden;
   n->max_batch = c.max_batch;
   n->rows = (size_t)c.max_batch * n->P;
+  n->in_pad = in_pad_of(c.input_channels);
+  if (head_smem(n) > 227 * 1024) {
+    set_error("heads need %zu bytes of shared memory (policy size %d)", head_smem(n), n->A);
+    delete n;
+    return OMQ_BAD_ARG;
+  }
   cudaDeviceGetAttribute(&n->sm_count, cudaDevAttrMultiProcessorCount, c.device);
-  const size_t nconv_w = (size_t)n->C * 9 * kInPad + (size_t)2 * n->NB * n->C * 9 * n->C;
+  const size_t nconv_w = (size_t)n->C * 9 * n->in_pad + (size_t)2 * n->NB * n->C * 9 * n->C;
   const size_t nconv_b = (size_t)(1 + 2 * n->NB) * n->C;
   size_t off[8], k = 0, tot = 0;
   auto take = [&](size_t b) { off[k++] = tot; tot += (b + 1023) & ~(size_t)1023; };
   take(nconv_w * 2);
   take(nconv_b * 4);
   take(head_floats(n) * 4);
-  take(n->rows * kInPad * 2);
+  take(n->rows * n->in_pad * 2);
   for (int i = 0; i < 3; ++i) take(n->rows * n->C * 2);
   take(16);
   void* arena = nullptr;
@@ -1289,7 +1300,7 @@ int omq_resnet_destroy(omq_resnet* n) {
 
 int omq_resnet_param_sizes(const omq_resnet* n, uint64_t* conv_w, uint64_t* conv_b, uint64_t* head) {
   if (!n) { set_error("null argument"); return OMQ_BAD_ARG; }
-  if (conv_w) *conv_w = (uint64_t)n->C * 9 * kInPad + (uint64_t)2 * n->NB * n->C * 9 * n->C;
+  if (conv_w) *conv_w = (uint64_t)n->C * 9 * n->in_pad + (uint64_t)2 * n->NB * n->C * 9 * n->C;
   if (conv_b) *conv_b = (uint64_t)(1 + 2 * n->NB) * n->C;
   if (head) *head = head_floats(n);
   return OMQ_OK;
@@ -1431,7 +1442,8 @@ int resnet_run(omq_resnet* n, const int32_t* d_count, int count, float* policy, 
       n->prof_host_counts[pi] = count;
     cudaEventRecord(n->prof_ev[2 * pi], s);
   }
-  int st = conv(n, n->tmA_in, n->tmB_in, n->tmO[0], n->conv_b, nullptr, n->act[0], 1, d_count, count, s);
+  int st = conv(n, n->tmA_in, n->tmB_in, n->tmO[0], n->conv_b, nullptr, n->act[0], n->in_pad / kBlockK,
+                d_count, count, s);
   int x = 0;
   for (int i = 0; st == OMQ_OK && i < n->NB; ++i) {
     const int t = (x + 1) % 3, y = (x + 2) % 3;
@@ -1487,7 +1499,7 @@ int omq_resnet_forward_features(omq_resnet* n, const float* d_features, int32_t 
   if (batch == 0) return OMQ_OK;
   DeviceGuard g(n->cfg.device);
   cudaStream_t s = (cudaStream_t)stream;
-  const int total = batch * n->P * 8;
+  const int total = batch * n->P * (n->in_pad / 8);
   count_launches(1);
   k_pack_features<<<min((total + 255) / 256, 8192), 256, 0, s>>>(
       d_features, n->cfg.input_channels, n->S, n->P, nullptr, batch, n->x_in);
@@ -1503,7 +1515,7 @@ int omq_resnet_forward_packed(omq_resnet* n, const uint16_t* d_input, const int3
   DeviceGuard g(n->cfg.device);
   cudaStream_t s = (cudaStream_t)stream;
   if (d_input && d_input != reinterpret_cast<const uint16_t*>(n->x_in)) {
-    cudaError_t e = cudaMemcpyAsync(n->x_in, d_input, (size_t)batch * n->P * kInPad * 2,
+    cudaError_t e = cudaMemcpyAsync(n->x_in, d_input, (size_t)batch * n->P * n->in_pad * 2,
                                     cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) return cuda_status(e, "omq_resnet_forward_packed copy");
   }
@@ -1523,10 +1535,14 @@ int omq_resnet_forward_queue(omq_resnet* n, omq_engine* e, int32_t queue, void* 
     set_error("resnet max_batch %d < engine queue capacity %d", n->max_batch, cap);
     return OMQ_BAD_ARG;
   }
-  if (n->S != e->v.S || n->A != e->v.A) { set_error("resnet / engine board mismatch"); return OMQ_BAD_ARG; }
+  if (n->S != e->v.S || n->A != e->v.A || n->cfg.input_channels != engine_planes(e->v)) {
+    set_error("resnet / engine mismatch: board %d/%d, actions %d/%d, planes %d/%d", n->S, e->v.S,
+              n->A, e->v.A, n->cfg.input_channels, engine_planes(e->v));
+    return OMQ_BAD_ARG;
+  }
   DeviceGuard g(n->cfg.device);
   cudaStream_t s = (cudaStream_t)stream;
-  launch_pack_queue(e->v, queue, n->P, n->x_in, s);
+  launch_pack_queue(e->v, queue, n->P, n->in_pad, n->x_in, s);
   int st = cuda_status(cudaGetLastError(), "pack queue");
   if (st) return st;
   return resnet_run(n, e->v.q_count + queue, cap, e->v.q_policy[queue], e->v.q_value[queue], s);
@@ -1621,16 +1637,17 @@ extern "C" int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const ui
     return OMQ_BAD_ARG;
   }
   const omq_resnet_config c = *cfg;
-  if (c.board_size < 5 || c.board_size > 19 || c.input_channels < 1 || c.input_channels > kInPad ||
+  if (c.board_size < 5 || c.board_size > 19 || c.input_channels < 1 || c.input_channels > kMaxInputPlanes ||
       (c.filters != 128 && c.filters != 256) || c.num_blocks < 0 || c.num_blocks > 64 ||
-      c.num_actions < 1 || c.num_actions > 4096 || c.fc_policy_hidden < 1 ||
+      c.num_actions < 1 || c.num_actions > kMaxActions || c.fc_policy_hidden < 1 ||
       c.fc_policy_hidden > 1024 || c.fc_value_hidden < 1 || c.fc_value_hidden > 1024) {
     set_error("bad resnet config");
     return OMQ_BAD_ARG;
   }
   const int P = (c.board_size + 1) * (c.board_size + 1);
   // scratch: the packed input [rows][64] + three activation buffers [rows][F] (bf16) + error word
-  const size_t per_pos = (size_t)P * (kInPad + 3 * (size_t)c.filters) * 2;
+  const int in_pad = in_pad_of(c.input_channels);
+  const size_t per_pos = (size_t)P * (in_pad + 3 * (size_t)c.filters) * 2;
   const int max_batch = (int)((kNoAllocScratchBytes - 1024) / per_pos);
   if (batch < 0 || batch > max_batch) {
     set_error("omq_resnet_forward_noalloc: batch %d exceeds the fixed scratch limit of %d positions "
@@ -1657,12 +1674,14 @@ extern "C" int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const ui
   n.Hv = c.fc_value_hidden;
   n.max_batch = max_batch;
   n.rows = (size_t)max_batch * P;
+  n.in_pad = in_pad;
+  if (head_smem(&n) > 227 * 1024) { set_error("heads need too much shared memory"); return OMQ_BAD_ARG; }
   cudaDeviceGetAttribute(&n.sm_count, cudaDevAttrMultiProcessorCount, c.device);
   n.conv_w = reinterpret_cast<__nv_bfloat16*>(const_cast<uint16_t*>(d_conv_w));
   n.conv_b = const_cast<float*>(d_conv_b);
   n.head = const_cast<float*>(d_head);
   n.x_in = reinterpret_cast<__nv_bfloat16*>(base);
-  size_t off = ((n.rows * kInPad * 2) + 255) & ~(size_t)255;
+  size_t off = ((n.rows * in_pad * 2) + 255) & ~(size_t)255;
   for (int i = 0; i < 3; ++i) {
     n.act[i] = reinterpret_cast<__nv_bfloat16*>(base + off);
     off += ((n.rows * n.C * 2) + 255) & ~(size_t)255;
@@ -1676,7 +1695,7 @@ extern "C" int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const ui
   // the error word keeps the previous call's value: clear it
   cudaError_t e = cudaMemsetAsync(n.error, 0, sizeof(int32_t), s);
   if (e != cudaSuccess) return cuda_status(e, "omq_resnet_forward_noalloc: clearing the error word");
-  const int total = batch * P * 8;
+  const int total = batch * P * (in_pad / 8);
   count_launches(1);
   k_pack_features<<<min((total + 255) / 256, 8192), 256, 0, s>>>(
       d_features, c.input_channels, n.S, P, nullptr, batch, n.x_in);

@@ -25,6 +25,11 @@ BN_EPS = 1e-5
 IN_PAD = 64
 
 
+def in_pad(input_channels: int) -> int:
+    """Input channels padded to one 64-channel K block, or two for more than 64 planes (chess)."""
+    return IN_PAD if input_channels <= IN_PAD else 2 * IN_PAD
+
+
 @dataclass(frozen=True)
 class ResNetSpec:
     board_size: int = 15
@@ -148,7 +153,7 @@ def pack_parameters(sd: Dict[str, torch.Tensor], spec: ResNetSpec):
         return k.reshape(cout, 9 * cin_pad)
 
     w, b = _fold(sd, "conv_input", "bn_input")
-    ws.append(pack_conv(w, IN_PAD)); bs.append(b)
+    ws.append(pack_conv(w, in_pad(spec.input_channels))); bs.append(b)
     for i in range(spec.num_blocks):
         p = f"residual_blocks.{i}."
         for c, n in (("conv1", "bn1"), ("conv2", "bn2")):

@@ -4,6 +4,7 @@
 // arithmetic is fp32 with one rounding per operation (built with -ffp-contract=off), in the
 // operand order the reference's torch expressions evaluate.
 #include "oracle.h"
+#include "chess_rules.h"
 #include "go_rules.h"
 #include "gomoku_rules.h"
 #include "synth_eval.h"
@@ -36,6 +37,9 @@ struct Tree {
   int game = 0, planes = oracle::kPlanes;
   std::vector<int32_t> ko, passes;
   std::vector<int8_t> root_hist;
+  // Chess (game == 2): a position record per node, the game's positions before the root (most
+  // recent first) for the history planes and the repetition count.
+  std::vector<oracle_chess_pos> cpos, prior;
 
   Tree(int cap_, int size_) : cap(cap_), size(size_), cells(size_ * size_), actions(size_ * size_) {
     ko.assign(cap, -1); passes.assign(cap, 0);
@@ -47,7 +51,24 @@ struct Tree {
 
   const int8_t* board(int n) const { return &boards[(size_t)n * cells]; }
 
+  // Occurrences of node n's position: itself, its ancestors, and the positions before the root
+  // (the repetition key is the piece placement, chess_rules.h).
+  int chess_reps(int n, const oracle_chess_pos& p) const {
+    int r = 1;
+    for (int a = parent[n]; a >= 0; a = parent[a]) r += oracle_chess_same(&cpos[a], &p);
+    for (const auto& q : prior) r += oracle_chess_same(&q, &p);
+    return r;
+  }
+
   void features(int n, float* out) const {
+    if (game == 2) {
+      const oracle_chess_pos* hist[8];
+      int cur = n, k = 0;
+      for (; k < 8 && cur >= 0; ++k, cur = parent[cur]) hist[k] = &cpos[cur];
+      for (size_t j = 0; k < 8; ++k, ++j) hist[k] = j < prior.size() ? &prior[j] : nullptr;
+      oracle_chess_features(hist, out);
+      return;
+    }
     if (game == 1) {
       const int8_t* hist[8];
       int cur = n, k = 0;
@@ -71,6 +92,8 @@ struct Tree {
       eval(ctx, n, feat.data(), pol.data(), val.data());
     else if (game == 1)
       oracle_synth_eval_go(n, cells, actions, feat.data(), pol.data(), val.data());
+    else if (game == 2)
+      oracle_synth_eval_chess(n, feat.data(), pol.data(), val.data());
     else
       oracle_synth_eval(n, oracle::kPlanes, cells, actions, feat.data(), pol.data(), val.data());
     res.eval_calls++;
@@ -107,7 +130,18 @@ struct Tree {
       const float* p = &pol_copy[i * actions];
       const int8_t* b = board(n);
       std::vector<int> legal;
-      if (game == 1) {
+      std::vector<int32_t> chess_moves;  // by action, for game == 2
+      if (game == 2) {
+        // terminal positions are discovered when first expanded (ChessState::isTerminal order)
+        int res = 0;
+        if (oracle_chess_terminal(&cpos[n], cpos[n].reps, &res)) { terminal[n] = 1; continue; }
+        int32_t mv[320];
+        const int k = oracle_chess_legal(&cpos[n], mv);
+        std::vector<std::pair<int, int32_t>> am;
+        for (int j = 0; j < k; ++j) am.push_back({oracle_chess_action(&cpos[n], mv[j]), mv[j]});
+        std::sort(am.begin(), am.end());
+        for (auto& x : am) { legal.push_back(x.first); chess_moves.push_back(x.second); }
+      } else if (game == 1) {
         std::vector<uint8_t> m(actions);
         oracle::go_legal(b, size, player[n], ko[n], m.data());
         for (int a = 0; a < actions; ++a)
@@ -140,6 +174,14 @@ struct Tree {
         parent[c] = n; action[c] = a; child_count[c] = 0;
         player[c] = (int8_t)(3 - player[n]);
         mc[c] = mc[n] + 1;
+        if (game == 2) {
+          oracle_chess_pos q = cpos[n];
+          oracle_chess_play(&q, chess_moves[j]);
+          cpos[c] = q;
+          cpos[c].reps = (int8_t)chess_reps(c, q);
+          terminal[c] = 0;
+          continue;
+        }
         if (game == 1) {
           int k2 = -1;
           oracle::go_play(b, size, player[n], a, ko[n], &boards[(size_t)c * cells], &k2);
@@ -177,6 +219,31 @@ struct Tree {
     passes[0] = root_passes;
     mc[0] = 0;
     terminal[0] = root_passes >= 2 ? 1 : 0;
+    int st = expand({0});
+    res.status = st;
+    return st;
+  }
+
+  // Chess root: its record (reps = occurrences in the game so far, itself included) and the
+  // game's earlier positions, most recent first.
+  int begin_chess(const oracle_config* c, const oracle_chess_pos* root, const oracle_chess_pos* pr,
+                  int nprior, oracle_eval_fn e, void* x) {
+    game = 2;
+    planes = oracle::kChessPlanes;
+    actions = oracle::kChessActions;
+    cfg = *c;
+    if (cfg.board_size != 8 || size != 8 || cfg.max_nodes > cap || cfg.max_wave_size <= 0) return 2;
+    cpos.assign(cap, oracle_chess_pos{});
+    prior.assign(pr, pr + (nprior > 0 ? nprior : 0));
+    eval = e; ctx = x;
+    res = oracle_result{};
+    num_nodes = 1;
+    N[0] = 0; W[0] = 0.f; VL[0] = 0; P[0] = 1.0f; parent[0] = -1; action[0] = -1;
+    child_count[0] = 0;
+    terminal[0] = 0;
+    cpos[0] = *root;
+    player[0] = root->side;
+    mc[0] = 0;
     int st = expand({0});
     res.status = st;
     return st;
@@ -352,6 +419,11 @@ void oracle_get_result(void* t, oracle_result* out) {
   Tree* tr = static_cast<Tree*>(t);
   *out = tr->res;
   out->num_nodes = tr->num_nodes;
+}
+
+int oracle_begin_chess(void* t, const oracle_config* cfg, const oracle_chess_pos* root,
+                       const oracle_chess_pos* prior, int nprior, oracle_eval_fn e, void* x) {
+  return static_cast<Tree*>(t)->begin_chess(cfg, root, prior, nprior, e, x);
 }
 
 int oracle_begin_go(void* t, const oracle_config* cfg, const int8_t* hist, int to_move, int ko,

@@ -19,6 +19,8 @@
 #pragma once
 #include <cstdint>
 
+#include "chess_rules.h"
+
 extern "C" {
 
 // Evaluator callback: features [n, planes, cells] fp32 -> policy [n, actions], value [n].
@@ -66,6 +68,12 @@ int oracle_begin_go(void* tree, const oracle_config* cfg, const int8_t* hist, in
                     int passes, oracle_eval_fn eval, void* ctx);
 int oracle_search_go(void* tree, const oracle_config* cfg, const int8_t* hist, int to_move, int ko,
                      int passes, oracle_eval_fn eval, void* ctx, oracle_result* out);
+// Chess root (chess_rules.h): the root record (reps = occurrences so far, itself included) and
+// the game's earlier positions, most recent first (history planes, repetition count). Board
+// size 8; actions 4672 (the engine's AlphaZero encoding); children in ascending action order;
+// a node's terminal status is found when it is first expanded (it then gets no children).
+int oracle_begin_chess(void* tree, const oracle_config* cfg, const oracle_chess_pos* root,
+                       const oracle_chess_pos* prior, int nprior, oracle_eval_fn eval, void* ctx);
 // Action count of the last begun game (cells for Gomoku, cells + 1 for Go).
 int oracle_actions(void* tree);
 // Full search = begin + ceil(sims / max_wave_size) waves.

@@ -170,6 +170,11 @@ def lib():
                                        ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                        EVAL_FN, ctypes.c_void_p, ctypes.POINTER(OracleResult)]
         L.oracle_actions.argtypes = [ctypes.c_void_p]
+        L.oracle_begin_chess.argtypes = [ctypes.c_void_p, ctypes.POINTER(OracleConfig), ctypes.c_void_p,
+                                         ctypes.c_void_p, ctypes.c_int, EVAL_FN, ctypes.c_void_p]
+        L.oracle_feature_hash_chess.restype = ctypes.c_uint64
+        L.oracle_feature_hash_chess.argtypes = [ctypes.c_void_p]
+        L.oracle_synth_eval_chess.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         L.oracle_feature_hash_go.restype = ctypes.c_uint64
         L.oracle_feature_hash_go.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.oracle_synth_eval_go.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
@@ -272,6 +277,25 @@ def c_synth_eval(features: np.ndarray, actions: int | None = None):
     return pol, val
 
 
+def c_synth_eval_chess(features: np.ndarray):
+    """Chess synthetic evaluator on 119-plane features [n, 119, 8, 8] -> (policy [n, 4672], value)."""
+    f = np.ascontiguousarray(features, dtype=np.float32)
+    B = f.shape[0]
+    pol = np.zeros((B, 4672), np.float32)
+    val = np.zeros(B, np.float32)
+    lib().oracle_synth_eval_chess(B, f.ctypes.data, pol.ctypes.data, val.ctypes.data)
+    return pol, val
+
+
+def chess_features(hist) -> np.ndarray:
+    """119 planes [119, 8, 8] from position records hist[0..7] (None where absent)."""
+    bufs = [None if h is None else _pos_buf(h) for h in list(hist) + [None] * (8 - len(hist))]
+    ptrs = (ctypes.c_void_p * 8)(*[None if b is None else b.ctypes.data for b in bufs])
+    out = np.zeros((119, 8, 8), np.float32)
+    lib().oracle_chess_features(ptrs, out.ctypes.data)
+    return out
+
+
 def c_synth_eval_go(features: np.ndarray):
     """Go synthetic evaluator on 17-plane features [n, 17, H, W] -> (policy [n, H*W+1], value)."""
     f = np.ascontiguousarray(features, dtype=np.float32)
@@ -332,6 +356,8 @@ class Oracle:
         go = self.game == "go"
         A = H * H + (1 if go else 0)
         planes = 17 if go else PLANES
+        if self.game == "chess":
+            A, planes = 4672, 119
 
         def cb(_ctx, n, feat, pol, val):
             f = np.ctypeslib.as_array(feat, shape=(n, planes, H, H)).copy()
@@ -362,6 +388,32 @@ class Oracle:
         res = OracleResult()
         self._L.oracle_search_go(self._t, ctypes.byref(cfg), h.ctypes.data, int(to_move), int(ko),
                                  int(passes), self._cb, None, ctypes.byref(res))
+        return self.export()
+
+    def begin_chess(self, root, cfg: OracleConfig, prior=(), evaluator=None) -> int:
+        """Chess root: an oracle position record (``CHESS_POS``) and the game's earlier positions,
+        most recent first."""
+        self.game = "chess"
+        r = _pos_buf(root)
+        pr = np.ascontiguousarray(np.array(list(prior), dtype=CHESS_POS).reshape(-1))
+        if pr.size == 0:
+            pr = np.zeros(1, CHESS_POS)
+            npr = 0
+        else:
+            npr = pr.size
+        self._cb = self._make_cb(evaluator)
+        self._board = (r, pr)
+        return self._L.oracle_begin_chess(self._t, ctypes.byref(cfg), r.ctypes.data, pr.ctypes.data,
+                                          npr, self._cb, None)
+
+    def search_chess(self, root, sims, wave, prior=(), evaluator=None, **kw) -> OracleTree:
+        cfg = self.config(sims, wave, **kw)
+        st = self.begin_chess(root, cfg, prior, evaluator)
+        done = 0
+        while st == 0 and done < sims:
+            w = min(wave, sims - done)
+            st = self._L.oracle_wave(self._t, w)
+            done += w
         return self.export()
 
     def begin(self, board, cfg: OracleConfig, evaluator=None) -> int:

@@ -118,3 +118,22 @@ extern "C" void oracle_synth_eval_go(int n, int cells, int actions, const float*
     oracle::synth_from_hash(h, actions, legal.data(), policy + (size_t)i * actions, value + i);
   }
 }
+
+extern "C" uint64_t oracle_feature_hash_chess(const float* f) {
+  uint64_t h = oracle::kHashSeed;
+  for (int c = 0; c < 119; ++c) {
+    uint64_t word = 0;
+    for (int b = 0; b < 64; ++b)
+      if (f[(size_t)c * 64 + b] != 0.0f) word |= 1ull << b;
+    h = oracle::mix64(h ^ word);
+  }
+  return h;
+}
+
+extern "C" void oracle_synth_eval_chess(int n, const float* features, float* policy, float* value) {
+  std::vector<uint8_t> legal(4672, 1);
+  for (int i = 0; i < n; ++i) {
+    const uint64_t h = oracle_feature_hash_chess(features + (size_t)i * 119 * 64);
+    oracle::synth_from_hash(h, 4672, legal.data(), policy + (size_t)i * 4672, value + i);
+  }
+}

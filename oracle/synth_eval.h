@@ -32,6 +32,11 @@ void oracle_synth_eval(int n, int planes, int cells, int actions, const float* f
 uint64_t oracle_feature_hash_go(const float* features, int cells);
 void oracle_synth_eval_go(int n, int cells, int actions, const float* features, float* policy,
                           float* value);
+// Chess variant on the 119-plane features [n, 119, 64]: the hash folds all 119 planes binarised
+// (value != 0), one 64-bit word per plane; the policy covers all 4672 actions (the features do
+// not carry legality; expansion renormalises over the legal moves).
+uint64_t oracle_feature_hash_chess(const float* features);
+void oracle_synth_eval_chess(int n, const float* features, float* policy, float* value);
 }
 
 namespace oracle {

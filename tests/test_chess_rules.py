@@ -47,3 +47,37 @@ def test_chess_action_encoding_round_trips(oracle_lib):
             acts = [oracle_lib.chess_action(pos, int(m)) for m in legal]
             assert all(0 <= a < 4672 for a in acts) and len(set(acts)) == len(acts)
             assert [oracle_lib.chess_move(pos, a) for a in acts] == [int(m) for m in legal]
+
+
+def test_host_chess_position_replays_reference_games(oracle_lib):
+    """The package's host-side chess position (roots, moves between searches) follows the same
+    reference games: legal lists, terminal results, FENs and the 4672 encoding."""
+    from omoknuni_quantum_b200.chess import ChessPosition
+    games = list(_games())
+    for gi, game in enumerate(games):
+        pos = ChessPosition(game[0][0])
+        for t, (fen, legal, term, res, move) in enumerate(game):
+            assert pos.fen() == fen, (gi, t)
+            if t % 5 == 0 or term or move < 0:
+                assert pos.legal_moves() == [int(m) for m in legal], fen
+                assert pos.result() == (res if term else 0), fen
+                o = oracle_lib.chess_from_fen(fen)
+                assert [pos.move_to_action(int(m)) for m in legal] == \
+                    [oracle_lib.chess_action(o, int(m)) for m in legal]
+            if move < 0:
+                break
+            pos.play(move)
+
+
+def test_chess_roots_are_seeded_and_records_match_oracle(oracle_lib):
+    from omoknuni_quantum_b200.chess import random_position, random_roots
+    r1, n1 = random_roots(5, 3)
+    r2, n2 = random_roots(5, 3)
+    assert np.array_equal(r1, r2) and np.array_equal(n1, n2)
+    p = random_position(5 * 1_000_003 + 1)
+    o = oracle_lib.chess_from_fen(p.fen())
+    assert oracle_lib.chess_same(o, r1[1, 0]) and r1[1, 0]["side"] == o["side"]
+    assert 10 <= n1.min() and n1.max() <= 40
+    # the prior positions are the game's, most recent first
+    q = p.copy()
+    assert np.array_equal(np.asarray(r1[1, 1]["sq"]), np.asarray(q.prior[0]["sq"]))
