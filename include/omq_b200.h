@@ -56,7 +56,8 @@ typedef enum {
  * (src/games/go/go_state.cpp:227-420, 502-506). */
 typedef enum {
   OMQ_GAME_GOMOKU = 0,
-  OMQ_GAME_GO = 1
+  OMQ_GAME_GO = 1,
+  OMQ_GAME_CHESS = 2  /* board_size 8; 4672 actions (8x8x73, mover's frame); 119 planes */
 } omq_game;
 
 typedef struct omq_engine omq_engine;
@@ -98,6 +99,17 @@ OMQ_API int omq_engine_memory(const omq_engine* e, uint64_t* h_bytes);
  * forced expansion (mcts.py:1659-1691): evaluate OMQ_QUEUE_EXPAND, then call
  * omq_root_expand. */
 OMQ_API int omq_begin(omq_engine* e, const int8_t* d_boards, void* stream);
+/* Chess engines: reset every tree and set its root from d_records, 72-byte position records
+ * [num_trees][101] (record 0 = the root, records 1..100 = the game's earlier positions, most
+ * recent first; layout: int8 squares[64] (rank 0 = the eighth rank; 0 empty, piece type 1..6 =
+ * P N B R Q K, +8 for black), int8 side (1 white, 2 black), int8 castling bits (1 K, 2 Q, 4 k,
+ * 8 q), int8 en-passant square (-1 none), int8 occurrences of the position so far, int16 halfmove
+ * clock, int16 fullmove number) and d_nprior int32 [num_trees] (earlier positions present).
+ * Replaces MCTS._initialize_root for GameType.CHESS (mcts.py:1495-1519) with the rules of the
+ * reference's ChessState (chess_state.cpp, chess_rules.cpp) in place of the placeholder
+ * gpu_game_states.py:397-405. A node's terminal status is found when it is first expanded. */
+OMQ_API int omq_begin_chess(omq_engine* e, const void* d_records, const int32_t* d_nprior,
+                            void* stream);
 /* Go engines: reset every tree and set its root from d_history int8 [num_trees][8][n][n]
  * (index 0 = the root position, index k = the position k plies earlier, all-zero before the
  * game started; they feed the 17 history planes) and d_meta int32 [num_trees][3] = {side to move
@@ -134,7 +146,10 @@ OMQ_API int omq_queue_count(omq_engine* e, int32_t queue, int32_t* h_count, void
 /* Feature tensor of the queue entries into d_out (capacity rows): Gomoku, the reference's
  * (gpu_game_states.py:534-600) fp32 [count][19][n][n]; Go, fp32 [count][17][n][n] with planes
  * 0-7 the side to move's stones now and 1..7 plies ago, 8-15 the opponent's, 16 all ones when
- * black is to move. */
+ * black is to move; chess, fp32 [count][119][8][8] in the mover's frame: for k = 0..7 plies ago
+ * planes 14k+0..5 the mover's P N B R Q K, 14k+6..11 the opponent's, 14k+12/13 position seen
+ * >= 2 / >= 3 times; then white to move, fullmove / 100, mover's castling K/Q, opponent's K/Q,
+ * halfmove / 100. */
 OMQ_API int omq_queue_features(omq_engine* e, int32_t queue, float* d_out, void* stream);
 /* Built-in integer-exact synthetic evaluator on the queue (policy for OMQ_QUEUE_EXPAND, value
  * for both). */
@@ -145,6 +160,9 @@ OMQ_API int omq_queue_eval_synthetic(omq_engine* e, int32_t queue, void* stream)
  * once at the end to report device status. */
 OMQ_API int omq_search_synthetic(omq_engine* e, const int8_t* d_boards, int32_t num_simulations,
                          void* stream);
+/* The same for chess engines, with the roots of omq_begin_chess. */
+OMQ_API int omq_search_synthetic_chess(omq_engine* e, const void* d_records, const int32_t* d_nprior,
+                                       int32_t num_simulations, void* stream);
 /* The same for Go engines, with the roots of omq_begin_go. */
 OMQ_API int omq_search_synthetic_go(omq_engine* e, const int8_t* d_history, const int32_t* d_meta,
                                     int32_t num_simulations, void* stream);

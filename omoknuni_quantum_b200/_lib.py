@@ -46,7 +46,8 @@ class EngineConfig(ctypes.Structure):
 
 GAME_GOMOKU = 0
 GAME_GO = 1
-GAMES = {"gomoku": GAME_GOMOKU, "go": GAME_GO}
+GAME_CHESS = 2
+GAMES = {"gomoku": GAME_GOMOKU, "go": GAME_GO, "chess": GAME_CHESS}
 
 
 class ResNetConfig(ctypes.Structure):
@@ -69,6 +70,7 @@ SIGNATURES = {
     "omq_engine_memory": [_P, ctypes.POINTER(ctypes.c_uint64)],
     "omq_begin": [_P, _P, _P],
     "omq_begin_go": [_P, _P, _P, _P],
+    "omq_begin_chess": [_P, _P, _P, _P],
     "omq_root_expand": [_P, _P],
     "omq_wave_select": [_P, _I, _P],
     "omq_wave_expand": [_P, _P],
@@ -80,6 +82,7 @@ SIGNATURES = {
     "omq_queue_eval_synthetic": [_P, _I, _P],
     "omq_search_synthetic": [_P, _P, _I, _P],
     "omq_search_synthetic_go": [_P, _P, _P, _I, _P],
+    "omq_search_synthetic_chess": [_P, _P, _P, _I, _P],
     "omq_root_visits": [_P, _P, _P, _P],
     "omq_tree_status": [_P, _P, _P, _P],
     "omq_root_noise": [_P, _P, _P],

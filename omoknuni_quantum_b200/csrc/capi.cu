@@ -71,9 +71,10 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
     set_error("dirichlet_alpha must be > 0 when dirichlet_epsilon > 0");
     return OMQ_BAD_ARG;
   }
-  if (c.num_trees < 1 || c.board_size < 5 || c.board_size > 19 || c.capacity < 2 ||
+  if (c.num_trees < 1 || c.board_size < (c.game == OMQ_GAME_CHESS ? 8 : 5) || c.board_size > 19 || c.capacity < 2 ||
       c.max_wave_size < 1 || c.max_wave_size > 1024 || c.max_depth < 2 || c.max_depth > 127 ||
-      (c.game != OMQ_GAME_GOMOKU && c.game != OMQ_GAME_GO)) {
+      (c.game != OMQ_GAME_GOMOKU && c.game != OMQ_GAME_GO && c.game != OMQ_GAME_CHESS) ||
+      (c.game == OMQ_GAME_CHESS && c.board_size != 8)) {
     set_error("bad engine config: trees=%d board=%d capacity=%d wave=%d depth=%d game=%d",
               c.num_trees, c.board_size, c.capacity, c.max_wave_size, c.max_depth, c.game);
     return OMQ_BAD_ARG;
@@ -88,7 +89,8 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   v.S = c.board_size;
   v.C = c.board_size * c.board_size;
   v.game = c.game;
-  v.A = c.game == OMQ_GAME_GO ? v.C + 1 : v.C;
+  v.A = c.game == OMQ_GAME_GO ? v.C + 1 : c.game == OMQ_GAME_CHESS ? 4672 : v.C;
+  v.max_children = c.game == OMQ_GAME_CHESS ? 256 : v.A;
   v.WCAP = c.max_wave_size;
   v.LOGCAP = c.max_wave_size * c.max_depth;
   v.max_depth = c.max_depth;
@@ -104,7 +106,8 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   auto take = [&](size_t bytes) { off[n++] = tot; tot += align256(bytes); };
   take(R * T * sizeof(NodeStats));            // 0 stats
   take(R * T * sizeof(NodeTopo));             // 1 topo
-  take(R * v.C * (c.game == OMQ_GAME_GO ? 8 : 1));  // 2 root boards (Go: with history)
+  const bool chess = c.game == OMQ_GAME_CHESS;
+  take(chess ? R * 101 * 72 : R * v.C * (c.game == OMQ_GAME_GO ? 8 : 1));  // 2 roots (+ history)
   take(R * sizeof(TreeHeader));               // 3 headers
   take(R * 2 * W * sizeof(Visit));            // 4 frontier
   take(R * (size_t)v.LOGCAP * sizeof(Visit)); // 5 visit log
@@ -119,7 +122,9 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   take(QC * sizeof(float));                   // 14 value final
   take(2 * sizeof(int32_t));                  // 15 counts
   take(R * (size_t)v.A * sizeof(float));      // 16 root noise
-  take(c.game == OMQ_GAME_GO ? R * W * 16 * sizeof(uint32_t) : 16);  // 17 Go legal masks
+  take(c.game == OMQ_GAME_GO ? R * W * 16 * sizeof(uint32_t)
+       : chess ? R * W * 148 * sizeof(uint32_t) : 16);                    // 17 per-leaf legal masks
+  take(chess ? R * 100 * sizeof(uint64_t) : 16);                          // 18 chess prior hashes
   void* arena = nullptr;
   cudaError_t err = cudaMalloc(&arena, tot);
   if (err != cudaSuccess) {
@@ -145,6 +150,7 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   v.q_count = reinterpret_cast<int32_t*>(b + off[15]);
   v.root_noise = reinterpret_cast<float*>(b + off[16]);
   v.go_mask = reinterpret_cast<uint32_t*>(b + off[17]);
+  v.chess_prior_hash = reinterpret_cast<uint64_t*>(b + off[18]);
   err = cudaMemset(v.hdr, 0, R * sizeof(TreeHeader));
   if (err == cudaSuccess) err = cudaMemset(v.q_count, 0, 2 * sizeof(int32_t));
   if (err == cudaSuccess) err = cudaMemset(v.root_noise, 0, R * (size_t)v.A * sizeof(float));
@@ -176,10 +182,23 @@ int omq_engine_memory(const omq_engine* e, uint64_t* bytes) {
 
 int omq_begin(omq_engine* e, const int8_t* d_boards, void* stream) {
   if (!e || !d_boards) { set_error("null argument"); return OMQ_BAD_ARG; }
-  if (e->v.game != OMQ_GAME_GOMOKU) { set_error("Go engine: use omq_begin_go"); return OMQ_BAD_ARG; }
+  if (e->v.game != OMQ_GAME_GOMOKU) {
+    set_error("omq_begin is for Gomoku engines (omq_begin_go / omq_begin_chess)");
+    return OMQ_BAD_ARG;
+  }
   DeviceGuard g(e->cfg.device);
   launch_begin(e->v, d_boards, e->searches++, (cudaStream_t)stream);
   OMQ_CHECK_LAUNCH("omq_begin");
+  e->phase = 1;
+  return OMQ_OK;
+}
+
+int omq_begin_chess(omq_engine* e, const void* d_records, const int32_t* d_nprior, void* stream) {
+  if (!e || !d_records || !d_nprior) { set_error("null argument"); return OMQ_BAD_ARG; }
+  if (e->v.game != OMQ_GAME_CHESS) { set_error("omq_begin_chess on a non-chess engine"); return OMQ_BAD_ARG; }
+  DeviceGuard g(e->cfg.device);
+  launch_begin_chess(e->v, d_records, d_nprior, e->searches++, (cudaStream_t)stream);
+  OMQ_CHECK_LAUNCH("omq_begin_chess");
   e->phase = 1;
   return OMQ_OK;
 }
@@ -310,6 +329,14 @@ static int search_synthetic_waves(omq_engine* e, int32_t sims, void* stream);
 int omq_search_synthetic(omq_engine* e, const int8_t* d_boards, int32_t sims, void* stream) {
   if (!e || !d_boards || sims < 0) { set_error("bad argument"); return OMQ_BAD_ARG; }
   int st = omq_begin(e, d_boards, stream);
+  if (st) return st;
+  return search_synthetic_waves(e, sims, stream);
+}
+
+int omq_search_synthetic_chess(omq_engine* e, const void* d_records, const int32_t* d_nprior,
+                               int32_t sims, void* stream) {
+  if (!e || !d_records || !d_nprior || sims < 0) { set_error("bad argument"); return OMQ_BAD_ARG; }
+  int st = omq_begin_chess(e, d_records, d_nprior, stream);
   if (st) return st;
   return search_synthetic_waves(e, sims, stream);
 }

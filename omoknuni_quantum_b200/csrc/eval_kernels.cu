@@ -5,6 +5,9 @@
 // board plus the actions on its parent chain (at most max_depth dependent loads), which is all
 // the reference's features carry: occupancy, the side to move, and the last move (child states
 // do not inherit full_move_history, python/mcts/gpu/gpu_game_states.py:325-327, 443-446).
+#include <cuda_bf16.h>
+
+#include "chess_device.cuh"
 #include "go_device.cuh"
 #include "omq_internal.cuh"
 
@@ -324,8 +327,109 @@ __global__ void __launch_bounds__(kGoWarps * 32) k_pack_queue_go(EngineView v, i
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Chess: 119 planes from the replayed position (chess_device.cuh)
+// ---------------------------------------------------------------------------------------------
+constexpr int kChessWarps = 4;
+
+__device__ int chess_queue_replay(const EngineView& v, int queue, int q, ChessReplay& w, int& r) {
+  const int2 ent = v.q_entries[queue][q];
+  r = ent.x;
+  const int d = warp_ch_replay(v, r, ent.y, w, true);
+  if (d < 0 && (threadIdx.x & 31) == 0) v.hdr[r].status = OMQ_BAD_ARG;
+  return d;
+}
+
+// Synthetic evaluator on chess positions: hash folded over the 119 binarised planes (one 64-bit
+// word per plane, oracle_feature_hash_chess); the policy covers all 4672 actions, so action a
+// has rank a among the "legal" ones.
+__global__ void __launch_bounds__(kChessWarps * 32) k_synth_chess(EngineView v, int queue) {
+  __shared__ ChessReplay wps[kChessWarps];
+  __shared__ uint64_t words[kChessWarps][kChessPlanes];
+  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
+  const int q = blockIdx.x * kChessWarps + wl;
+  if (q >= v.q_count[queue]) return;
+  ChessReplay& w = wps[wl];
+  int r;
+  if (chess_queue_replay(v, queue, q, w, r) < 0) return;
+  for (int c = lane; c < kChessPlanes; c += 32) {
+    uint64_t word = 0;
+    for (int s = 0; s < 64; ++s)
+      if (ch_plane(v, r, w, c, s) != 0.0f) word |= 1ull << s;
+    words[wl][c] = word;
+  }
+  __syncwarp();
+  uint64_t h = 0;
+  if (lane == 0) {
+    h = 0x243F6A8885A308D3ull;
+    for (int c = 0; c < kChessPlanes; ++c) h = mix64(h ^ words[wl][c]);
+  }
+  h = __shfl_sync(0xFFFFFFFFu, h, 0);
+  if (queue == 0) {
+    uint64_t tot = 0;
+    for (int a = lane; a < kChessActions; a += 32)
+      tot += exp2_fixed(exp_step(mix64(h + 0x9E3779B97F4A7C15ull * (uint64_t)(a + 1))));
+    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xFFFFFFFFu, tot, o);
+    float* out = v.q_policy[0] + (size_t)q * v.A;
+    for (int a = lane; a < kChessActions; a += 32) {
+      const uint64_t wa = exp2_fixed(exp_step(mix64(h + 0x9E3779B97F4A7C15ull * (uint64_t)(a + 1))));
+      const uint64_t qa = 512ull * ((wa * 32640ull) / tot) + (uint64_t)a;
+      out[a] = __fmul_rn(__ull2float_rn(qa), 1.0f / 16777216.0f);
+    }
+  }
+  if (lane == 0) {
+    const int64_t e = (int64_t)exp2_fixed(exp_step(mix64(h ^ 0xD1B54A32D192ED03ull)));
+    const int64_t dd = (int64_t)1 << 26;
+    const int64_t val = ((e - dd) * 4096) / (e + dd);
+    v.q_value[queue][q] = __fmul_rn(__ll2float_rn(val), 1.0f / 4096.0f);
+  }
+}
+
+__global__ void __launch_bounds__(kChessWarps * 32) k_features_chess(EngineView v, int queue, float* out) {
+  __shared__ ChessReplay wps[kChessWarps];
+  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
+  const int q = blockIdx.x * kChessWarps + wl;
+  if (q >= v.q_count[queue]) return;
+  ChessReplay& w = wps[wl];
+  int r;
+  if (chess_queue_replay(v, queue, q, w, r) < 0) return;
+  float* o = out + (size_t)q * kChessPlanes * 64;
+  for (int i = lane; i < kChessPlanes * 64; i += 32) o[i] = ch_plane(v, r, w, i >> 6, i & 63);
+}
+
+// ResNet input for chess: 119 planes as bf16, channels padded to 128, padded 9x9 pixel grid.
+__global__ void __launch_bounds__(kChessWarps * 32) k_pack_queue_chess(EngineView v, int queue, int P, uint4* out) {
+  __shared__ ChessReplay wps[kChessWarps];
+  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
+  const int q = blockIdx.x * kChessWarps + wl;
+  if (q >= v.q_count[queue]) return;
+  ChessReplay& w = wps[wl];
+  int r;
+  if (chess_queue_replay(v, queue, q, w, r) < 0) return;
+  uint4* o = out + (size_t)q * P * 16;
+  for (int i = lane; i < P * 16; i += 32) {
+    const int pix = i >> 4, chunk = i & 15;
+    const int y = pix / 9, x = pix - y * 9;
+    __nv_bfloat16 h[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int ch = chunk * 8 + e;
+      const float val = (y < 8 && x < 8 && ch < kChessPlanes) ? ch_plane(v, r, w, ch, y * 8 + x) : 0.0f;
+      h[e] = __float2bfloat16_rn(val);
+    }
+    o[i] = *reinterpret_cast<uint4*>(h);
+  }
+}
+
 void launch_pack_queue(const EngineView& v, int queue, int P, int in_pad, void* out, cudaStream_t s) {
-  (void)in_pad;  // Gomoku and Go pack 64 channels
+  if (v.game == OMQ_GAME_CHESS) {
+    (void)in_pad;  // 128
+    const int cap = v.R * v.WCAP;
+    count_launches(1);
+    k_pack_queue_chess<<<(cap + kChessWarps - 1) / kChessWarps, kChessWarps * 32, 0, s>>>(
+        v, queue, P, reinterpret_cast<uint4*>(out));
+    return;
+  }
   if (v.game == OMQ_GAME_GO) {
     const int cap = v.R * v.WCAP;
     count_launches(1);
@@ -346,6 +450,10 @@ void launch_synth_eval(const EngineView& v, int queue, cudaStream_t s) {
     k_synth_go<<<(cap + kGoWarps - 1) / kGoWarps, kGoWarps * 32, 0, s>>>(v, queue);
     return;
   }
+  if (v.game == OMQ_GAME_CHESS) {
+    k_synth_chess<<<(cap + kChessWarps - 1) / kChessWarps, kChessWarps * 32, 0, s>>>(v, queue);
+    return;
+  }
   k_synth<<<(cap + kSynthWarps - 1) / kSynthWarps, kSynthWarps * 32, 0, s>>>(v, queue);
 }
 
@@ -354,6 +462,10 @@ void launch_features(const EngineView& v, int queue, float* out, cudaStream_t s)
   count_launches(1);
   if (v.game == OMQ_GAME_GO) {
     k_features_go<<<(cap + kGoWarps - 1) / kGoWarps, kGoWarps * 32, 0, s>>>(v, queue, out);
+    return;
+  }
+  if (v.game == OMQ_GAME_CHESS) {
+    k_features_chess<<<(cap + kChessWarps - 1) / kChessWarps, kChessWarps * 32, 0, s>>>(v, queue, out);
     return;
   }
   k_features<<<(cap + kSynthWarps - 1) / kSynthWarps, kSynthWarps * 32, 0, s>>>(v, queue, out);

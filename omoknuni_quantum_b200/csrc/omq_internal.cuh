@@ -64,6 +64,8 @@ struct TreeHeader {
   int32_t search_idx;    // searches begun on this engine (root-noise counter)
   int32_t root_ko;       // Go: ko point of the root position (-1 none)
   int32_t root_passes;   // Go: consecutive passes that led to the root position
+  int32_t root_prior;    // chess: earlier game positions stored with the root
+  int32_t pad[3];
 };
 
 constexpr int kPlanes = 19;
@@ -81,8 +83,12 @@ struct EngineView {
   float* root_noise;     // [R][A] noise of the last wave, by action
   NodeStats* stats;      // [R*T]
   NodeTopo* topo;        // [R*T]
-  int8_t* root_board;    // Gomoku [R][C]; Go [R][8][C] (root position and 7 earlier ones)
-  uint32_t* go_mask;     // Go: [R][WCAP][16] legal bits (12 words) + passes of each leaf
+  int8_t* root_board;    // Gomoku [R][C]; Go [R][8][C] (root position and 7 earlier ones);
+                         // chess [R][1 + 100] position records (root, then earlier positions)
+  uint32_t* go_mask;     // per-leaf legal bits: Go [R][WCAP][16] (12 words + the leaf's passes),
+                         // chess [R][WCAP][148]
+  uint64_t* chess_prior_hash;  // chess: [R][100] placement hashes of the earlier positions
+  int max_children;      // most children a node can have (sizes the selection sort)
   TreeHeader* hdr;       // [R]
   Visit* frontier;       // [R][2][WCAP]
   Visit* vlog;           // [R][LOGCAP]
@@ -184,6 +190,8 @@ void count_launches(int n);
 int cuda_status(cudaError_t e, const char* what);
 
 void launch_begin(const EngineView& v, const int8_t* boards, int search_id, cudaStream_t s);
+void launch_begin_chess(const EngineView& v, const void* records, const int32_t* nprior, int search_id,
+                        cudaStream_t s);
 void launch_begin_go(const EngineView& v, const int8_t* history, const int32_t* meta, int search_id,
                      cudaStream_t s);
 void launch_select(const EngineView& v, int wave, cudaStream_t s);
@@ -198,5 +206,7 @@ void launch_synth_eval(const EngineView& v, int queue, cudaStream_t s);
 // queue positions -> bf16 [count][P][in_pad] padded pixel layout (ResNet input)
 void launch_pack_queue(const EngineView& v, int queue, int P, int in_pad, void* out, cudaStream_t s);
 // feature planes of the engine's game (19 Gomoku, 17 Go)
-inline int engine_planes(const EngineView& v) { return v.game == OMQ_GAME_GO ? 17 : 19; }
+inline int engine_planes(const EngineView& v) {
+  return v.game == OMQ_GAME_GO ? 17 : v.game == OMQ_GAME_CHESS ? 119 : 19;
+}
 }  // namespace omq

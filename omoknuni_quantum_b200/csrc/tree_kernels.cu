@@ -11,6 +11,7 @@
 // exactly one record per wave, which makes backup free of atomics and lets it add the values
 // of [lo, lo+k) in ascending simulation order - the reference's sequential order
 // (python/mcts/gpu/mcts_gpu_accelerator.py:378-393) - so W is bit-exact for any evaluator.
+#include "chess_device.cuh"
 #include "go_device.cuh"
 #include "omq_internal.cuh"
 
@@ -204,6 +205,41 @@ __global__ void k_begin_go(EngineView v, const int8_t* hist, const int32_t* meta
   }
 }
 
+// Chess roots: position records [R][101] (root + earlier positions) and the number of earlier
+// positions; their placement hashes are kept for the repetition count.
+__global__ void k_begin_chess(EngineView v, const ChessRec* rec, const int32_t* nprior, int search_id) {
+  const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const size_t per = 1 + kChessPrior;
+  ChessRec* dst = reinterpret_cast<ChessRec*>(v.root_board) + (size_t)r * per;
+  const int np = min(max(nprior[r], 0), kChessPrior);
+  for (size_t i = tid; i < per; i += blockDim.x) dst[i] = rec[(size_t)r * per + i];
+  for (int i = warp; i < np; i += (int)(blockDim.x >> 5)) {
+    const uint64_t h = warp_ch_hash(rec[(size_t)r * per + 1 + i]);
+    if (lane == 0) v.chess_prior_hash[(size_t)r * kChessPrior + i] = h;
+  }
+  if (tid == 0) {
+    TreeHeader h{};
+    h.num_nodes = 1;
+    h.status = OMQ_OK;
+    const int side = rec[(size_t)r * per].side;
+    if ((side != 1 && side != 2) || nprior[r] < 0 || nprior[r] > kChessPrior) h.status = OMQ_BAD_ARG;
+    h.root_player = side;
+    h.root_prior = np;
+    h.nleaves = 1;
+    h.exp_off = r;
+    h.exp_cnt = 1;
+    h.search_idx = search_id;
+    v.hdr[r] = h;
+    const size_t base = (size_t)r * v.T;
+    v.stats[base] = NodeStats{0, 0.0f, 1.0f, 0};
+    v.topo[base] = NodeTopo{-1, pack_act_depth(-1, 0), 0, pack_cnt_flags(0, 0)};
+    v.leaves[(size_t)r * v.WCAP] = Visit{0, 0, 0, 0};
+    v.leaf_final[(size_t)r * v.WCAP] = make_int2(0, r);
+    v.q_entries[0][r] = make_int2(r, 0);
+    if (r == 0) { v.q_count[0] = v.R; v.q_count[1] = 0; }
+  }
+}
+
 // ---------------------------------------------------------------------------------------------
 // root Dirichlet noise
 // ---------------------------------------------------------------------------------------------
@@ -262,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
   extern __shared__ unsigned char smem_raw[];
   SelectShared& sh = *reinterpret_cast<SelectShared*>(smem_raw);
   int p2 = 1;
-  while (p2 < v.A) p2 <<= 1;
+  while (p2 < v.max_children) p2 <<= 1;
   unsigned long long* keys_all =
       reinterpret_cast<unsigned long long*>(smem_raw + ((sizeof(SelectShared) + 15) & ~15));
   Visit* s_leaves = reinterpret_cast<Visit*>(keys_all + (size_t)(blockDim.x >> 5) * p2);
@@ -430,6 +466,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
 // ---------------------------------------------------------------------------------------------
 constexpr int kMaxDepthCap = 128;
 
+struct ChessWarpSmem {
+  ChessReplay rep;
+  uint32_t mask[kChessMaskWords];
+};
+
 struct ExpandWarpSmem {
   int16_t acts[kMaxDepthCap];
   int16_t legal[kMaxCells + 1];
@@ -466,8 +507,35 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
   const float* pol = v.q_policy[0];
 
   const bool go = v.game == OMQ_GAME_GO;
+  const bool chs = v.game == OMQ_GAME_CHESS;
   GoPos* gpos = reinterpret_cast<GoPos*>(expand_smem + (blockDim.x >> 5) * sizeof(ExpandWarpSmem));
-  if (go) {
+  ChessWarpSmem* cws = reinterpret_cast<ChessWarpSmem*>(expand_smem + (blockDim.x >> 5) * sizeof(ExpandWarpSmem));
+  if (chs) {
+    // chess: replay the leaf, find its legal moves; a terminal leaf (ChessState::isTerminal)
+    // is flagged here and gets no children
+    ChessWarpSmem& cw = cws[warp];
+    for (int i = warp; i < nleaf; i += (int)(blockDim.x >> 5)) {
+      int n = 0;
+      const int node = leaves[i].node;
+      if (lf[i].y >= 0 && !(topo_flags(v.topo[base + node]) & kFlagTerminal)) {
+        const int d = warp_ch_replay(v, r, node, cw.rep, false);
+        if (d < 0) { if (lane == 0) H->status = OMQ_BAD_ARG; }
+        else {
+          n = warp_ch_legal(cw.rep.pos, cw.mask);
+          if (lane == 0 && ch_terminal(cw.rep.pos, n)) {
+            NodeTopo lt = v.topo[base + node];
+            lt.cnt_flags = pack_cnt_flags(topo_count(lt), topo_flags(lt) | kFlagTerminal);
+            v.topo[base + node] = lt;
+          }
+          if (ch_terminal(cw.rep.pos, n)) n = 0;
+          uint32_t* m = v.go_mask + ((size_t)r * v.WCAP + i) * kChessMaskWords;
+          for (int w = lane; w < kChessMaskWords; w += 32) m[w] = n ? cw.mask[w] : 0u;
+        }
+      }
+      if (lane == 0) s_cnt[i] = n;
+      __syncwarp();
+    }
+  } else if (go) {
     // Go: children are the legal moves of the leaf position (replayed from the root); the
     // legal bits and the leaf's pass count go to a per-leaf scratch for the second pass
     GoPos& gp = gpos[warp];
@@ -502,12 +570,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
     const Visit e = leaves[i];
     const int q = lf[i].y;
     int final_node = e.node, ext = 0;
-    if (q >= 0 && go) {
-      const uint32_t* m = v.go_mask + ((size_t)r * v.WCAP + i) * 16;
-      const int leaf_passes = (int)m[12];
+    if (q >= 0 && (go || chs)) {
+      const uint32_t* m = v.go_mask + ((size_t)r * v.WCAP + i) * (chs ? kChessMaskWords : 16);
+      const int leaf_passes = go ? (int)m[12] : 0;
       int n = 0;
       if (!(topo_flags(v.topo[base + e.node]) & kFlagTerminal)) {
-        for (int w = 0; w < kGoMaskWords && w * 32 < v.A; ++w) {
+        for (int w = 0; w < (chs ? kChessMaskWords : kGoMaskWords) && w * 32 < v.A; ++w) {
           const int c = w * 32 + lane;
           const bool legal = c < v.A && ((m[w] >> lane) & 1u);
           const unsigned bm = __ballot_sync(0xFFFFFFFFu, legal);
@@ -528,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
       for (int j = lane; j < n; j += 32) {
         const int a = W.legal[j];
         const float P = __fdiv_rn(W.pv[j], denom);
-        const bool term = a == v.C && leaf_passes >= 1;  // second consecutive pass
+        const bool term = go && a == v.C && leaf_passes >= 1;  // second consecutive pass
         const int c = start + j;
         const NodeStats st{0, 0.0f, P, 0};
         v.stats[base + c] = st;
@@ -750,7 +818,7 @@ static int tree_threads(const EngineView& v) {
 
 static size_t select_smem(const EngineView& v) {
   int p2 = 1;
-  while (p2 < v.A) p2 <<= 1;
+  while (p2 < v.max_children) p2 <<= 1;
   return ((sizeof(SelectShared) + 15) & ~(size_t)15) + (size_t)(tree_threads(v) / 32) * p2 * 8 +
          (size_t)v.WCAP * sizeof(Visit) + (size_t)v.WCAP * sizeof(int);
 }
@@ -758,6 +826,12 @@ static size_t select_smem(const EngineView& v) {
 void launch_begin(const EngineView& v, const int8_t* boards, int search_id, cudaStream_t s) {
   count_launches(1);
   k_begin<<<v.R, tree_threads(v), 0, s>>>(v, boards, search_id);
+}
+
+void launch_begin_chess(const EngineView& v, const void* records, const int32_t* nprior, int search_id,
+                        cudaStream_t s) {
+  count_launches(1);
+  k_begin_chess<<<v.R, 256, 0, s>>>(v, reinterpret_cast<const ChessRec*>(records), nprior, search_id);
 }
 
 void launch_begin_go(const EngineView& v, const int8_t* history, const int32_t* meta, int search_id,
@@ -778,8 +852,9 @@ void launch_select(const EngineView& v, int wave, cudaStream_t s) {
 void launch_expand(const EngineView& v, int root_mode, cudaStream_t s) {
   if (!root_mode) cudaMemsetAsync(v.q_count + 1, 0, sizeof(int32_t), s);
   count_launches(1);
-  const int sm = (int)((tree_threads(v) / 32) *
-                       (sizeof(ExpandWarpSmem) + (v.game == OMQ_GAME_GO ? sizeof(GoPos) : 0)));
+  const size_t extra = v.game == OMQ_GAME_GO ? sizeof(GoPos)
+                       : v.game == OMQ_GAME_CHESS ? sizeof(ChessWarpSmem) : 0;
+  const int sm = (int)((tree_threads(v) / 32) * (sizeof(ExpandWarpSmem) + extra));
   cudaFuncSetAttribute(k_expand, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
   k_expand<<<v.R, tree_threads(v), sm, s>>>(v, root_mode);
 }

@@ -12,9 +12,11 @@ The evaluator between the select/expand/backup phases is one of
     (python/mcts/core/wave_search.py:866-871, 1381-1383); features are handed over as a CUDA
     fp32 tensor, results are copied into the queue buffers.
 
-Games: ``"gomoku"`` (A = n*n, the reference's 19 feature planes) and ``"go"`` (A = n*n + 1 with
+Games: ``"gomoku"`` (A = n*n, the reference's 19 feature planes), ``"go"`` (A = n*n + 1 with
 pass last, 17 history planes; roots carry 8 history boards, the side to move, the ko point and
-the consecutive-pass count - see ``go_meta``).
+the consecutive-pass count - see ``go_meta``) and ``"chess"`` (board 8, A = 4672 in the mover's
+frame, 119 planes; roots are position records with the game's earlier positions - see
+``omoknuni_quantum_b200.chess``).
 """
 from __future__ import annotations
 
@@ -64,8 +66,11 @@ class WaveEngine:
             raise ValueError(f"unknown game {game!r} (gomoku, go)")
         self.game = game
         self.is_go = game == "go"
-        self.actions = self.cells + (1 if self.is_go else 0)
-        self.planes = GO_PLANES if self.is_go else PLANES
+        self.is_chess = game == "chess"
+        if self.is_chess and self.board_size != 8:
+            raise ValueError("chess engines have board_size 8")
+        self.actions = 4672 if self.is_chess else self.cells + (1 if self.is_go else 0)
+        self.planes = GO_PLANES if self.is_go else 119 if self.is_chess else PLANES
         self.capacity = int(capacity)
         self.max_wave_size = int(max_wave_size)
         cfg = _lib.EngineConfig(self.num_trees, self.board_size, self.capacity, self.max_wave_size,
@@ -167,7 +172,27 @@ class WaveEngine:
         m = torch.as_tensor(meta).to(self.device, torch.int32).reshape(R, 3).contiguous()
         return b.contiguous(), m
 
+    def _chess_roots(self, records, nprior):
+        """records: POS_DTYPE [R, 101] (numpy) or uint8 [R, 101*72]; nprior int32 [R]."""
+        R = self.num_trees
+        if isinstance(records, np.ndarray) and records.dtype.names:
+            records = np.ascontiguousarray(records).view(np.uint8).reshape(R, -1)
+        b = torch.as_tensor(records).to(self.device, torch.uint8).reshape(R, -1).contiguous()
+        if b.shape[1] != 101 * 72:
+            raise ValueError("chess roots must be 101 position records of 72 bytes per tree")
+        if nprior is None:
+            raise ValueError("chess roots need meta = the number of earlier positions per tree")
+        m = torch.as_tensor(np.asarray(nprior, np.int32) if not torch.is_tensor(nprior) else nprior)
+        m = m.to(self.device, torch.int32).reshape(R).contiguous()
+        return b, m
+
     def begin(self, boards: torch.Tensor, meta=None) -> None:
+        if self.is_chess:
+            b, m = self._chess_roots(boards, meta)
+            self._boards, self._meta = b, m
+            _lib.check(self.L.omq_begin_chess(self._h, ctypes.c_void_p(b.data_ptr()),
+                                              ctypes.c_void_p(m.data_ptr()), _stream_ptr()), "omq_begin_chess")
+            return
         if self.is_go:
             b, m = self._go_roots(boards, meta)
             self._boards, self._meta = b, m
@@ -197,6 +222,14 @@ class WaveEngine:
         """begin + forced root expansion + ceil(sims / max_wave_size) waves
         (python/mcts/core/mcts.py:1020-1063). Raises on a device status (e.g. TreeFullError).
         Go engines take history boards and ``meta`` (see ``begin``)."""
+        if isinstance(evaluator, str) and evaluator == "synthetic" and self.is_chess:
+            b, m = self._chess_roots(boards, meta)
+            self._boards, self._meta = b, m
+            _lib.check(self.L.omq_search_synthetic_chess(self._h, ctypes.c_void_p(b.data_ptr()),
+                                                         ctypes.c_void_p(m.data_ptr()),
+                                                         int(num_simulations), _stream_ptr()),
+                       "omq_search_synthetic_chess")
+            return
         if isinstance(evaluator, str) and evaluator == "synthetic" and self.is_go:
             b, m = self._go_roots(boards, meta)
             self._boards, self._meta = b, m
