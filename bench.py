@@ -38,6 +38,9 @@ UNIT = "simulations/s"
 WORKLOAD_GO = ("config3: Go 19x19 (captures, no suicide, simple ko, pass), 3200 sims/root, wave 512, "
                "1M-node trees, ResNet 20x256 bf16 on 17 history planes, 362 actions; 256 roots sharded "
                "across GPUs, searched in lockstep")
+WORKLOAD_CHESS = ("config4: chess (the reference engine's rules), 1600 sims/root, wave 256, 500k-node "
+                  "trees, ResNet 20x256 bf16 on 119 history planes, 4672 actions (8x8x73); 1024 roots "
+                  "from 10-40 random plies, sharded across GPUs, searched in lockstep")
 WORKLOAD = ("config1: Gomoku 15x15 single-tree searches, 1600 sims/root, wave 256, c_puct 1.4, "
             "VL 1.0, ResNet 10x128 bf16 evaluator; independent roots searched in lockstep per GPU")
 
@@ -59,9 +62,10 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", choices=["config1", "config2", "config3"], default="config1",
+    ap.add_argument("--workload", choices=["config1", "config2", "config3", "config4"], default="config1",
                     help="config2 = batched self-play: 512 games (sharded), 800 sims, wave 64, 20x256; "
-                         "config3 = Go 19x19: 256 roots (sharded), 3200 sims, wave 512, 1M nodes, 20x256")
+                         "config3 = Go 19x19: 256 roots (sharded), 3200 sims, wave 512, 1M nodes, 20x256; "
+                         "config4 = chess: 1024 roots (sharded), 1600 sims, wave 256, 500k nodes, 20x256")
     ap.add_argument("--evaluator", choices=["resnet", "synthetic"], default="resnet",
                     help="synthetic = BASELINE config 0 (tree kernels only; 800 sims, 200k nodes)")
     return ap.parse_args()
@@ -163,12 +167,25 @@ class ClockSampler:
 
 def make_spec(args):
     from omoknuni_quantum_b200.resnet import ResNetSpec
+    if args.workload == "config4":
+        return ResNetSpec(board_size=8, input_channels=119, num_blocks=args.blocks,
+                          filters=args.filters, num_actions=4672, fc_policy_hidden=256,
+                          fc_value_hidden=args.value_hidden)
     if args.workload == "config3":
         return ResNetSpec(board_size=19, input_channels=17, num_blocks=args.blocks,
                           filters=args.filters, num_actions=362, fc_policy_hidden=256,
                           fc_value_hidden=args.value_hidden)
     return ResNetSpec(board_size=15, input_channels=19, num_blocks=args.blocks, filters=args.filters,
                       num_actions=225, fc_policy_hidden=256, fc_value_hidden=args.value_hidden)
+
+
+def apply_config4(args):
+    """chess, 1600 sims per root, wave 256, 500k-node trees, ResNet 20x256 on
+    119 planes with a 4672-way policy; 1024 roots (10-40 random plies) sharded across the GPUs."""
+    args.sims, args.wave, args.capacity = 1600, 256, 500_000
+    args.blocks, args.filters, args.value_hidden = 20, 256, 256
+    if args.roots == 256:
+        args.roots = 1024
 
 
 def apply_config3(args):
@@ -201,7 +218,13 @@ def cpu_search_rate(args, sd, budget_s: float, game: str = "gomoku"):
     sims_done, t0 = 0, time.perf_counter()
     r = 0
     while True:
-        if game == "go":
+        if game == "chess":
+            from omoknuni_quantum_b200 import chess as chessmod
+            o = pyoracle.Oracle(args.capacity, 8)
+            cfg = o.config(args.sims, args.wave)
+            cp = chessmod.random_position(args.seed * 7919 + r)
+            st = o.begin_chess(cp.record(), cfg, prior=cp.prior, evaluator=ev)
+        elif game == "go":
             o = pyoracle.Oracle(args.capacity, 19)
             cfg = o.config(args.sims, args.wave)
             g = gomod.random_position(args.seed * 7919 + r, 60, 19)
@@ -233,9 +256,11 @@ def run_reference_arm(args):
     if rank != 0:
         return
     from omoknuni_quantum_b200.resnet import init_state_dict
-    game = "go" if args.workload == "config3" else "gomoku"
+    game = {"config3": "go", "config4": "chess"}.get(args.workload, "gomoku")
     if game == "go":
         apply_config3(args)
+    if game == "chess":
+        apply_config4(args)
     sd = init_state_dict(make_spec(args), seed=args.seed)
     budget = max(2.0, args.cpu_seconds / max(1, args.steps))
     for _ in range(max(0, min(args.warmup, 1))):
@@ -254,7 +279,7 @@ def run_reference_arm(args):
             "warmup": args.warmup, "ms_per_step": 1000.0 * secs_total / max(1, args.steps),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded roots, seeded He-init weights)", "impl": "reference",
-            "config": {"workload": WORKLOAD_GO if game == "go" else WORKLOAD, "sims": args.sims,
+            "config": {"workload": {"go": WORKLOAD_GO, "chess": WORKLOAD_CHESS}.get(game, WORKLOAD), "sims": args.sims,
                        "wave": args.wave, "model": f"resnet{args.blocks}x{args.filters}",
                        "parallelism": "host threads"},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
@@ -500,8 +525,9 @@ def run_b200_selfplay(args):
         dist.destroy_process_group()
 
 
-def run_b200_go(args):
-    """Config 3 on the device: Go roots (60 random legal moves each), ResNet 20x256 evaluator."""
+def run_b200_go(args, game="go"):
+    """Configs 3 and 4 on the device: Go roots (60 random legal moves each) or chess roots (10-40
+    random plies), ResNet 20x256 evaluator."""
     ws, rank, local = dist_env()
     if not torch.cuda.is_available():
         raise SystemExit("bench.py --impl b200 needs a CUDA device")
@@ -517,18 +543,27 @@ def run_b200_go(args):
     from omoknuni_quantum_b200.mcts_config import GameType, MCTSConfig
     from omoknuni_quantum_b200.resnet import ResNetEvaluator, init_state_dict
 
-    apply_config3(args)
+    from omoknuni_quantum_b200 import chess as chessmod
+    chess = game == "chess"
+    (apply_config4 if chess else apply_config3)(args)
+    n_board, n_act = (8, 4672) if chess else (19, 362)
     spec = make_spec(args)
     sd = parallel.broadcast_state_dict(init_state_dict(spec, seed=args.seed), dev)
     total_roots = args.roots
     R = total_roots // ws + (1 if rank < total_roots % ws else 0)
     first = sum(total_roots // ws + (1 if q < total_roots % ws else 0) for q in range(rank))
-    positions_host = [gomod.random_position(args.seed * 1_000_003 + first + i, 60, 19) for i in range(R)]
-    hist = torch.from_numpy(np.stack([g.history_planes() for g in positions_host])).to(dev)
-    meta = torch.from_numpy(np.stack([g.meta() for g in positions_host])).to(dev)
-    ev = ResNetEvaluator(sd, board_size=19, max_batch=R * args.wave, device=dev)
-    eng = WaveEngine(R, board_size=19, capacity=args.capacity, max_wave_size=args.wave, c_puct=1.4,
-                     virtual_loss=1.0, device=dev, game="go")
+    if chess:
+        positions_host = [chessmod.random_position(args.seed * 1_000_003 + first + i) for i in range(R)]
+        hist = torch.from_numpy(np.stack([p.root_records() for p in positions_host]).view(np.uint8)
+                                .reshape(R, -1)).to(dev)
+        meta = torch.tensor([len(p.prior) for p in positions_host], dtype=torch.int32, device=dev)
+    else:
+        positions_host = [gomod.random_position(args.seed * 1_000_003 + first + i, 60, 19) for i in range(R)]
+        hist = torch.from_numpy(np.stack([g.history_planes() for g in positions_host])).to(dev)
+        meta = torch.from_numpy(np.stack([g.meta() for g in positions_host])).to(dev)
+    ev = ResNetEvaluator(sd, board_size=n_board, max_batch=R * args.wave, device=dev)
+    eng = WaveEngine(R, board_size=n_board, capacity=args.capacity, max_wave_size=args.wave, c_puct=1.4,
+                     virtual_loss=1.0, device=dev, game=game)
 
     def barrier():
         if ws > 1:
@@ -565,8 +600,8 @@ def run_b200_go(args):
     avg_launch_s = float(trunk_ms.sum()) / 1000.0 / max(1, conv_launches)
     achieved = (flops / max(1, conv_launches)) / avg_launch_s / 1e12 if avg_launch_s > 0 else 0.0
     peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
-    roofline = {"kernel": "k_conv3x3_pair<256> (tcgen05 cta_group::2 implicit-GEMM 3x3 conv, 20x20 "
-                          "padded pixel grid)", "bound": "tensor", "achieved": achieved, "peak": peak,
+    roofline = {"kernel": f"k_conv3x3_pair<256> (tcgen05 cta_group::2 implicit-GEMM 3x3 conv, "
+                          f"{n_board + 1}x{n_board + 1} padded pixel grid)", "bound": "tensor", "achieved": achieved, "peak": peak,
                 "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_kind": f"bf16_tflops_sustained of {peak_kind}", "traffic": None,
                 "algorithmic_flops_per_launch": flops / max(1, conv_launches),
@@ -574,7 +609,8 @@ def run_b200_go(args):
 
     e2e = None
     if not args.no_e2e:
-        cfg = MCTSConfig(game_type=GameType.GO, board_size=19, num_simulations=args.sims,
+        cfg = MCTSConfig(game_type=GameType.CHESS if chess else GameType.GO, board_size=n_board,
+                         num_simulations=args.sims,
                          max_wave_size=args.wave, c_puct=1.4, virtual_loss=1.0,
                          initial_tree_nodes=args.capacity, device=str(dev),
                          enable_subtree_reuse=False, dirichlet_epsilon=0.0)
@@ -589,26 +625,29 @@ def run_b200_go(args):
         e2.record()
         barrier()
         ms2 = parallel.max_over_ranks(s2.elapsed_time(e2), dev)
-        assert pol.shape == (R, 362) and np.allclose(pol.sum(1), 1.0)
+        assert pol.shape == (R, n_act) and np.allclose(pol.sum(1), 1.0)
         e2e = {"value": total_sims / (ms2 / 1000.0), "unit": UNIT,
-               "h2d_bytes_per_step": R * (8 * 361 + 12), "d2h_bytes_per_step": R * 362 * 4,
-               "api": "MCTS(MCTSConfig(game_type=GO), ResNetEvaluator).search_batch(GoPositions) -> numpy policies"}
+               "h2d_bytes_per_step": R * (101 * 72 + 4) if chess else R * (8 * 361 + 12),
+               "d2h_bytes_per_step": R * n_act * 4,
+               "api": (f"MCTS(MCTSConfig(game_type={'CHESS' if chess else 'GO'}), ResNetEvaluator)"
+                       f".search_batch({'ChessPositions' if chess else 'GoPositions'}) -> numpy policies")}
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        rate, sims, secs, threads = cpu_search_rate(args, sd, args.cpu_seconds, "go")
+        rate, sims, secs, threads = cpu_search_rate(args, sd, args.cpu_seconds, game)
         cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{sims} simulations of config-3 Go searches in {secs:.1f} s (oracle C++ tree "
-                         f"with Go rules + fp32 torch CPU ResNet 20x256)"}
+               "sample": f"{sims} simulations of {args.workload} {game} searches in {secs:.1f} s (oracle "
+                         f"C++ tree with the {game} rules + fp32 torch CPU ResNet 20x256)"}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded Go roots, seeded He-init weights)",
-            "config": {"workload": WORKLOAD_GO, "roots_total": total_roots, "roots_per_gpu": R,
-                       "sims": args.sims, "wave": args.wave, "capacity": args.capacity,
-                       "model": "resnet20x256 (17 planes, 362 actions, value fc 256)",
+            "data": f"synthetic (seeded {game} roots, seeded He-init weights)",
+            "config": {"workload": WORKLOAD_CHESS if chess else WORKLOAD_GO, "roots_total": total_roots,
+                       "roots_per_gpu": R, "sims": args.sims, "wave": args.wave, "capacity": args.capacity,
+                       "model": ("resnet20x256 (119 planes, 4672 actions, value fc 256)" if chess else
+                                 "resnet20x256 (17 planes, 362 actions, value fc 256)"),
                        "parallelism": f"dp{ws} (roots sharded, weights NCCL-broadcast once)",
                        "l2": "inputs larger than L2 (multi-GB activations per ResNet call)"},
             "leaf_evals_per_s": positions / (ms / 1000.0) * ws,
@@ -625,8 +664,8 @@ def run_b200_go(args):
 
 def main():
     args = parse()
-    if args.workload == "config3" and args.impl == "b200":
-        run_b200_go(args)
+    if args.workload in ("config3", "config4") and args.impl == "b200":
+        run_b200_go(args, "go" if args.workload == "config3" else "chess")
         return
     if args.workload == "config2" and args.impl == "b200":
         run_b200_selfplay(args)

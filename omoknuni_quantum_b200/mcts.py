@@ -56,10 +56,10 @@ class MCTS:
         self.config = config
         self.game_interface = game_interface
         self.single_gpu_mode = single_gpu_mode
-        if config.game_type not in (GameType.GOMOKU, GameType.GO):
-            raise NotImplementedError(
-                f"device rules exist for Gomoku and Go; got {GameType(config.game_type).name}")
         self.is_go = config.game_type == GameType.GO
+        self.is_chess = config.game_type == GameType.CHESS
+        if self.is_chess and config.board_size != 8:
+            config.board_size = 8
         self.evaluator = evaluator
         self._eval = _resolve_evaluator(evaluator)
         if hasattr(evaluator, "_return_torch_tensors"):
@@ -79,6 +79,8 @@ class MCTS:
     # -- engines -------------------------------------------------------------------------------
     @property
     def action_size(self) -> int:
+        if self.is_chess:
+            return 4672
         return self.config.board_size ** 2 + (1 if self.is_go else 0)
 
     def _engine(self, num_trees: int) -> WaveEngine:
@@ -94,7 +96,8 @@ class MCTS:
                              virtual_loss=c.virtual_loss, enable_virtual_loss=c.enable_virtual_loss,
                              max_depth=c.max_depth, device=self.device,
                              dirichlet_alpha=c.dirichlet_alpha, dirichlet_epsilon=c.dirichlet_epsilon,
-                             noise_seed=self._noise_seed, game="go" if self.is_go else "gomoku")
+                             noise_seed=self._noise_seed,
+                             game="go" if self.is_go else "chess" if self.is_chess else "gomoku")
             self._engines[num_trees] = eng
         return eng
 
@@ -132,6 +135,37 @@ class MCTS:
         stones = int((b != 0).sum())
         return h, np.array([1 if stones % 2 == 0 else 2, -1, 0], np.int32)
 
+    def _chess_root(self, state):
+        """(records POS_DTYPE [101], earlier positions) of a chess root: a ChessPosition of this
+        package, a FEN string, or an object with the reference IGameState interface (rebuilt by
+        replaying get_move_history() - reference move encoding - from the start position)."""
+        from .chess import ChessPosition
+        if isinstance(state, str):
+            state = ChessPosition(state)
+        elif not isinstance(state, ChessPosition) and hasattr(state, "get_move_history"):
+            p = ChessPosition()
+            for m in state.get_move_history():
+                p.play(int(m))
+            state = p
+        if not isinstance(state, ChessPosition):
+            raise TypeError("chess state must be a ChessPosition, a FEN string or an IGameState")
+        return state.root_records(), len(state.prior)
+
+    def _search_chess(self, states, sims: int) -> np.ndarray:
+        roots = [self._chess_root(s) for s in states]
+        R = len(roots)
+        if sims == 0:
+            return np.full((R, self.action_size), 1.0 / self.action_size)
+        eng = self._engine(R)
+        t0 = time.perf_counter()
+        rec = np.stack([r[0] for r in roots])
+        npr = np.array([r[1] for r in roots], np.int32)
+        eng.search(rec, sims, self._eval, meta=npr)
+        visits = eng.root_visits().cpu().numpy()
+        self._last_tree = (eng, 0)
+        self._update_statistics(sims * R, time.perf_counter() - t0)
+        return self._policies(visits, eng)
+
     def _search_go(self, states, sims: int) -> np.ndarray:
         roots = [self._go_root(s) for s in states]
         R = len(roots)
@@ -150,9 +184,10 @@ class MCTS:
     # -- search --------------------------------------------------------------------------------
     def search(self, state: Any, num_simulations: Optional[int] = None) -> np.ndarray:
         """Policy (fp64 [actions]) = root-child visit share (mcts.py:924-979)."""
-        if self.is_go:
+        if self.is_go or self.is_chess:
             self._root_state = state
-            return self._search_go([state], int(num_simulations or self.config.num_simulations))[0]
+            fn = self._search_go if self.is_go else self._search_chess
+            return fn([state], int(num_simulations or self.config.num_simulations))[0]
         board = self._boards(state)
         pol = self.search_batch(board[None], num_simulations)[0]
         if torch.is_tensor(board):
@@ -162,8 +197,9 @@ class MCTS:
 
     def search_batch(self, states, num_simulations: Optional[int] = None) -> np.ndarray:
         """Independent searches of several roots in lockstep on the device; policies [R, A]."""
-        if self.is_go:
-            return self._search_go(list(states), int(num_simulations or self.config.num_simulations))
+        if self.is_go or self.is_chess:
+            fn = self._search_go if self.is_go else self._search_chess
+            return fn(list(states), int(num_simulations or self.config.num_simulations))
         boards = self._boards(states)
         if boards.ndim == 2:
             boards = boards[None]
@@ -215,7 +251,7 @@ class MCTS:
             raise ValueError(f"Invalid action {action}. Must be in range [0, {self.action_size})")
         self._last_tree = None
         if new_state is not None:
-            self._root_state = new_state if self.is_go else self._boards(new_state)
+            self._root_state = new_state if (self.is_go or self.is_chess) else self._boards(new_state)
 
     def clear(self) -> None:
         self._last_tree = None

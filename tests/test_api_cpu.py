@@ -108,5 +108,30 @@ def test_mcts_go_roots_from_positions_and_move_histories():
     h2, m2 = m._go_root(g)
     assert np.array_equal(h1, h2) and np.array_equal(m1, m2)
     assert m1[2] == 1                                     # one pass made
-    with pytest.raises(NotImplementedError):
-        MCTS(MCTSConfig(game_type=GameType.CHESS), "synthetic")
+
+
+def test_mcts_chess_roots_from_positions_fens_and_move_histories():
+    import numpy as np
+    from omoknuni_quantum_b200.chess import ChessPosition, random_position
+    from omoknuni_quantum_b200.mcts import MCTS
+    from omoknuni_quantum_b200.mcts_config import GameType, MCTSConfig
+    m = MCTS(MCTSConfig(game_type=GameType.CHESS), "synthetic")
+    assert m.action_size == 4672
+    rng = np.random.default_rng(1)
+    p, moves = ChessPosition(), []
+    for _ in range(12):
+        ms = p.legal_moves()
+        a = ms[int(rng.integers(len(ms)))]
+        p.play(a)
+        moves.append(a)
+
+    class FakeChessState:
+        def get_move_history(self):
+            return list(moves)
+
+    r1, n1 = m._chess_root(FakeChessState())
+    r2, n2 = m._chess_root(p)
+    assert np.array_equal(r1, r2) and n1 == n2 == 12
+    r3, n3 = m._chess_root(p.fen())
+    assert np.array_equal(r3[0], r2[0]) and n3 == 0      # a FEN carries no earlier positions
+    assert random_position(3).record()["side"] in (1, 2)
