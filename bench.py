@@ -356,7 +356,9 @@ def run_b200(args):
     traffic = None
     if traffic_per_pos is not None and conv_launches:
         traffic = traffic_per_pos * positions / len(trunk_ms)
-    roofline = {"kernel": "k_conv3x3<128> (tcgen05 implicit-GEMM 3x3 conv)", "bound": "tensor",
+    roofline = {"kernel": ("k_conv3x3_halo<128> (tcgen05 implicit-GEMM 3x3 conv, one halo load per channel block)"
+                          if args.filters == 128 else "k_conv3x3_pair<256> (tcgen05 cta_group::2 implicit-GEMM 3x3 conv)"),
+                "bound": "tensor",
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_kind": f"bf16_tflops_sustained of {peak_kind}", "traffic": traffic,
                 "algorithmic_flops_per_launch": flops / max(1, conv_launches),
