@@ -356,7 +356,7 @@ def run_b200(args):
     traffic = None
     if traffic_per_pos is not None and conv_launches:
         traffic = traffic_per_pos * positions / len(trunk_ms)
-    roofline = {"kernel": ("k_conv3x3_halo<128> (tcgen05 implicit-GEMM 3x3 conv, one halo load per channel block)"
+    roofline = {"kernel": ("k_conv3x3_halo_t (tcgen05 implicit-GEMM 3x3 conv, 128 ch x 256 px UMMAs over one halo load per channel block)"
                           if args.filters == 128 else "k_conv3x3_pair<256> (tcgen05 cta_group::2 implicit-GEMM 3x3 conv)"),
                 "bound": "tensor",
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,

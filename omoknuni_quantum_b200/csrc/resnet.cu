@@ -64,6 +64,7 @@ struct ConvCfg {
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr int kTmemCols = 2 * SUB * BN;
   static constexpr int kStaging = kEpiWarps * 2 * 2048;  // per epilogue warp: 2 x (32 rows x 64 B)
+  static constexpr int kStageBufs = 2;                       // epilogue staging buffers per warp
   static constexpr int kSmem = kStages * kStage + kStaging + 1024 /*align*/ + 256 /*barriers*/ + BN * 4;
   static_assert(kTmemCols <= 512, "TMEM holds 512 fp32 columns");
   static_assert(kSmem <= 232448, "227 KB of shared memory per CTA");
@@ -187,7 +188,7 @@ __global__ void __launch_bounds__(ConvCfg<BN, SUB>::kThreads, 1)
     // per warp) and written by one TMA store, instead of 32 scattered 16-byte row stores.
     const int sub = (warp - 2) >> 2;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    uint8_t* my_stage = staging + (warp - 2) * 2 * 2048;
+    uint8_t* my_stage = staging + (warp - 2) * Cfg::kStageBufs * 2048;
     int buf = 0;
     int t = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
@@ -285,6 +286,7 @@ struct PairCfg {
   static constexpr int kThreads = 192;                     // producer, MMA, 4 epilogue warps
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kStaging = 4 * 2 * 2048;             // per epilogue warp: 2 x (32 x 64 B)
+  static constexpr int kStageBufs = 2;                       // epilogue staging buffers per warp
   static constexpr int kSmem = kStages * kStage + kStaging + 1024 + 256 + BN * 4;
   static_assert(kSmem <= 232448, "227 KB of shared memory per CTA");
 };
@@ -411,7 +413,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::kThread
     const int q = warp & 3;
     const uint32_t tempty_leader0 = ptx::mapa(ptx::smem_u32(&tempty[0]), 0);
     const uint32_t tempty_leader1 = ptx::mapa(ptx::smem_u32(&tempty[1]), 0);
-    uint8_t* my_stage = staging + (warp - 2) * 2 * 2048;
+    uint8_t* my_stage = staging + (warp - 2) * Cfg::kStageBufs * 2048;
     int buf = 0;
     int t = 0;
     for (int tile = pair; tile < tiles; tile += npairs, ++t) {
@@ -695,7 +697,8 @@ __global__ void __launch_bounds__(TCfg::kThreads, 1)
 // tap's UMMA reads a row-shifted window of it (the descriptor simply starts `off` rows in). The
 // weights still stream per tap.
 // L2 -> SM traffic per 256-row tile drops from 18 x (32 + 16) KB to 2 x 38 KB + 18 x 16 KB.
-struct HaloCfg {
+template <int BS, int SB, int EW = 8>
+struct HaloCfgT {
   static constexpr int kRows = 256;                          // output rows per tile
   static constexpr int kLead = 24;                           // halo rows before the tile (>= S+2, multiple of 8)
   static constexpr int kHaloRows = 304;                      // kLead + 256 + 24
@@ -703,19 +706,22 @@ struct HaloCfg {
   static constexpr int kA = kHaloRows * 128;                 // 38,912 B
   static constexpr int kAStages = 2;
   static constexpr int kB = 128 * 128;                       // one tap's weights, 16 KB
-  static constexpr int kBStages = 6;
-  static constexpr int kEpiWarps = 8;
+  static constexpr int kBStages = BS;                         // weight stages in flight
+  static constexpr int kEpiWarps = EW;                         // a multiple of 4 (TMEM lane quarters)
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr int kTmemCols = 512;                      // 2 buffers x 2 sub-tiles x 128
-  static constexpr int kStaging = kEpiWarps * 2 * 2048;
+  static constexpr int kStageBufs = SB;                      // epilogue staging buffers per warp
+  static constexpr int kStaging = kEpiWarps * SB * 2048;
   static constexpr int kSmem = kAStages * kA + kBStages * kB + kStaging + 1024 + 512 + 128 * 4;
   static_assert(kSmem <= 232448, "227 KB of shared memory per CTA");
 };
+using HaloCfg = HaloCfgT<6, 2>;
 
-__global__ void __launch_bounds__(HaloCfg::kThreads, 1)
+template <int BS, int SB, int EW>
+__global__ void __launch_bounds__(HaloCfgT<BS, SB, EW>::kThreads, 1)
     k_conv3x3_halo(const __grid_constant__ CUtensorMap tmH, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO, ConvArgs args) {
-  using Cfg = HaloCfg;
+  using Cfg = HaloCfgT<BS, SB, EW>;
   constexpr int BN = 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -802,6 +808,10 @@ __global__ void __launch_bounds__(HaloCfg::kThreads, 1)
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer ----------------
     constexpr uint32_t idesc = ptx::idesc_bf16_f32(kTileM, BN);
+    const uint64_t b_desc0 = ptx::smem_desc_sw128(ptx::smem_u32(b_ring));
+    int tap_row[9];
+#pragma unroll
+    for (int tap = 0; tap < 9; ++tap) tap_row[tap] = (tap / 3 - 1) * rowstride + (tap % 3 - 1);
     int sa = 0, sb = 0;
     uint32_t pa = 0, pb = 0;
     bool any = false;
@@ -816,19 +826,24 @@ __global__ void __launch_bounds__(HaloCfg::kThreads, 1)
       for (int cb = 0; cb < CB && ok; ++cb) {
         if (!ptx::mbar_wait(&afull[sa], pa, abort_flag, kWaitLimitNs)) { ok = false; break; }
         ptx::tc_fence_after();
-        const uint32_t a_base = ptx::smem_u32(a_ring + sa * Cfg::kA);
+        // Descriptors are advanced by adding (byte offset >> 4) to the start-address field: the
+        // single issuing thread must spend as few instructions per MMA as possible (measured: a
+        // few extra integer instructions per MMA leave the tensor pipe idle a third of the time).
+        const uint64_t a_desc0 = ptx::smem_desc_sw128(ptx::smem_u32(a_ring + sa * Cfg::kA));
+#pragma unroll
         for (int tap = 0; tap < 9; ++tap) {
           if (!ptx::mbar_wait(&bfull[sb], pb, abort_flag, kWaitLimitNs)) { ok = false; break; }
           ptx::tc_fence_after();
-          const int off = Cfg::kLead + (tap / 3 - 1) * rowstride + (tap % 3 - 1);
-          const uint32_t b_addr = ptx::smem_u32(b_ring + sb * Cfg::kB);
+          const int off = Cfg::kLead + tap_row[tap];
+          const uint64_t ad = a_desc0 + (uint64_t)(off * 8);           // off rows of 128 B
+          const uint64_t bd = b_desc0 + (uint64_t)(sb * (Cfg::kB >> 4));
+          const uint32_t acc0 = (cb | tap) != 0;
+          ptx::mma_bf16(d, ad, bd, idesc, acc0);
+          ptx::mma_bf16(d + BN, ad + 1024, bd, idesc, acc0);             // + 128 rows
 #pragma unroll
-          for (int k = 0; k < kBlockK / 16; ++k) {
-            const uint64_t bdesc = ptx::smem_desc_sw128(b_addr + k * 32);
-#pragma unroll
-            for (int sub = 0; sub < 2; ++sub)
-              ptx::mma_bf16(d + sub * BN, ptx::smem_desc_sw128_rows(a_base, off + sub * kTileM, k * 32),
-                            bdesc, idesc, (cb | tap | k) != 0);
+          for (int k = 1; k < kBlockK / 16; ++k) {
+            ptx::mma_bf16(d, ad + 2 * k, bd + 2 * k, idesc, 1u);         // + 32 B along K
+            ptx::mma_bf16(d + BN, ad + 1024 + 2 * k, bd + 2 * k, idesc, 1u);
           }
           any = true;
           ptx::mma_commit(&bempty[sb]);
@@ -847,12 +862,15 @@ __global__ void __launch_bounds__(HaloCfg::kThreads, 1)
       ptx::mbar_wait(drain, 0, &dummy, kWaitLimitNs);
     }
   } else if (warp >= 2) {
-    // ---------------- epilogue: warp 2 + 4*sub + q handles rows sub*128 + 32q .. +31 ----------
-    // Each 32 rows x 32 channels chunk is staged in shared memory (64-byte swizzle, two buffers
-    // per warp) and written by one TMA store, instead of 32 scattered 16-byte row stores.
-    const int sub = (warp - 2) >> 2;
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    uint8_t* my_stage = staging + (warp - 2) * 2 * 2048;
+    // ---------------- epilogue ----------------
+    // Warp w may read TMEM lanes 32q..32q+31 with q = w % 4 (rows 32q.. of each 128-row sub-tile).
+    // The kEpiWarps / 4 warps of a lane quarter split its 8 units (2 sub-tiles x 4 chunks of 32
+    // channels). Each 32 rows x 32 channels chunk is staged in shared memory (64-byte swizzle)
+    // and written by one TMA store, instead of 32 scattered 16-byte row stores.
+    constexpr int kPerQ = Cfg::kEpiWarps / 4;
+    const int q = warp & 3;
+    const int wq = (warp - 2) >> 2;
+    uint8_t* my_stage = staging + (warp - 2) * Cfg::kStageBufs * 2048;
     int buf = 0;
     int t = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
@@ -860,6 +878,9 @@ __global__ void __launch_bounds__(HaloCfg::kThreads, 1)
       const uint32_t aph = (t >> 1) & 1;
       if (!ptx::mbar_wait(&tfull[ab], aph, abort_flag, kWaitLimitNs)) break;
       ptx::tc_fence_after();
+#pragma unroll 1
+      for (int u = wq; u < 8; u += kPerQ) {
+      const int sub = u >> 2, c0 = (u & 3) * 32;
       const int row0 = tile * Cfg::kRows + sub * kTileM + q * 32;
       const int m = row0 + lane;
       const bool valid = m < rows;
@@ -867,8 +888,7 @@ __global__ void __launch_bounds__(HaloCfg::kThreads, 1)
       const int y = pix / rowstride, x = pix - y * rowstride;
       const bool pad = !valid || (y == args.S) || (x == args.S);
       const __nv_bfloat16* rrow = args.residual ? args.residual + (size_t)m * BN : nullptr;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      {
         uint32_t r[32];
         ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + ab * 2 * BN + sub * BN + c0, r);
         ptx::tmem_ld_wait();
@@ -906,7 +926,7 @@ __global__ void __launch_bounds__(HaloCfg::kThreads, 1)
           }
         }
         // the buffer about to be written must no longer be read by an earlier store
-        if (lane == 0) ptx::bulk_wait_read<1>();
+        if (lane == 0) ptx::bulk_wait_read<Cfg::kStageBufs - 1>();
         __syncwarp();
         uint8_t* sb = my_stage + buf * 2048;
         const int sw = (lane >> 1) & 3;
@@ -918,7 +938,8 @@ __global__ void __launch_bounds__(HaloCfg::kThreads, 1)
           ptx::tma_store_2d(&tmO, sb, c0, row0);
           ptx::bulk_commit();
         }
-        buf ^= 1;
+        buf = buf + 1 == Cfg::kStageBufs ? 0 : buf + 1;
+      }
       }
       ptx::tc_fence_before();
       __syncwarp();
@@ -936,6 +957,263 @@ __global__ void __launch_bounds__(HaloCfg::kThreads, 1)
 
 // Sub-tiles per CTA tile for a given filter count (must match the A tensor maps' box height).
 __host__ __device__ constexpr int conv_sub(int filters) { return filters == 128 ? 2 : 1; }
+
+
+// Transposed halo variant for 128 filters: D[channel][pixel] = W[channel][K] . X[pixel][K]^T, so
+// each UMMA is M = 128 output channels x N = 256 pixels x K = 16. The pixel operand is the same
+// row-shifted window of the halo buffer as in k_conv3x3_halo (one 304-row TMA load per 64-channel
+// block). A 128 x 256 x 16 UMMA keeps the tensor pipe busy for 128 cycles, twice as long as a
+// 128 x 128 x 16 one, which leaves the single issuing thread enough time for its barrier waits and
+// commits (measured on B200: with 128 x 128 x 16 UMMAs any per-step work of the issuer idles the
+// tensor pipe; with 128 x 256 x 16 none does). The epilogue receives channel-major accumulators
+// (TMEM lane = channel) and transposes them through a swizzled fp32 buffer per warp, so that each
+// lane then owns one pixel row: residual loads, padding and the TMA-store staging stay row-major.
+struct HaloTCfg {
+  static constexpr int kRows = 256;                          // pixels per tile (UMMA N)
+  static constexpr int kLead = 24;                           // halo rows before the tile (>= S+2)
+  static constexpr int kHaloRows = 304;
+  static constexpr int kHaloBox = 152;
+  static constexpr int kX = kHaloRows * 128;                 // one 64-channel halo block, 38,912 B
+  static constexpr int kXStages = 2;
+  static constexpr int kW = 128 * 128;                       // one tap's weights (128 ch x 64 K), 16 KB
+  static constexpr int kWStages = 4;
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kTmemCols = 512;                      // 2 buffers x 256 pixel columns
+  static constexpr int kStagePerWarp = 2 * 2048 + 4096;      // 2 bf16 store buffers + fp32 transpose
+  static constexpr int kStaging = kEpiWarps * kStagePerWarp;
+  static constexpr int kSmem = kXStages * kX + kWStages * kW + kStaging + 1024 + 512 + 128 * 4;
+  static_assert(kSmem <= 232448, "227 KB of shared memory per CTA");
+};
+
+__global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
+    k_conv3x3_halo_t(const __grid_constant__ CUtensorMap tmH, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmO, ConvArgs args) {
+  using Cfg = HaloTCfg;
+  constexpr int BN = 128;  // output channels
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* x_ring = smem;                                     // 2 x 38,912
+  uint8_t* w_ring = smem + Cfg::kXStages * Cfg::kX;           // 4 x 16 KB
+  uint8_t* staging = w_ring + Cfg::kWStages * Cfg::kW;
+  uint64_t* xfull = reinterpret_cast<uint64_t*>(staging + Cfg::kStaging);
+  uint64_t* xempty = xfull + Cfg::kXStages;
+  uint64_t* wfull = xempty + Cfg::kXStages;
+  uint64_t* wempty = wfull + Cfg::kWStages;
+  uint64_t* tfull = wempty + Cfg::kWStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_bias = reinterpret_cast<float*>(staging + Cfg::kStaging + 512);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_pos = args.d_count ? min(*args.d_count, args.count) : args.count;
+  const int rows = n_pos * args.P;
+  const int tiles = (rows + Cfg::kRows - 1) / Cfg::kRows;
+  const int CB = args.kb_per_tap;
+  const int rowstride = args.S + 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kXStages; ++s) { ptx::mbar_init(&xfull[s], 1); ptx::mbar_init(&xempty[s], 1); }
+    for (int s = 0; s < Cfg::kWStages; ++s) { ptx::mbar_init(&wfull[s], 1); ptx::mbar_init(&wempty[s], 1); }
+    for (int i = 0; i < 2; ++i) { ptx::mbar_init(&tfull[i], 1); ptx::mbar_init(&tempty[i], Cfg::kEpiWarps); }
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    ptx::fence_barrier_init();
+    ptx::prefetch_tmap(&tmH);
+    ptx::prefetch_tmap(&tmB);
+    ptx::prefetch_tmap(&tmO);
+  }
+  for (int i = threadIdx.x; i < BN; i += blockDim.x) s_bias[i] = args.bias[i];
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer: per 64-channel block one halo, then 9 weight taps -------
+    int sx = 0, sw = 0;
+    uint32_t px = 0, pw = 0;
+    int x_issued[Cfg::kXStages], w_issued[Cfg::kWStages];
+    for (int i = 0; i < Cfg::kXStages; ++i) x_issued[i] = -1;
+    for (int i = 0; i < Cfg::kWStages; ++i) w_issued[i] = -1;
+    for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+      const int h0 = tile * Cfg::kRows - Cfg::kLead;
+      for (int cb = 0; cb < CB; ++cb) {
+        if (!ptx::mbar_wait(&xempty[sx], px ^ 1, abort_flag, kWaitLimitNs)) goto producer_done;
+        ptx::mbar_arrive_expect_tx(&xfull[sx], Cfg::kX);
+        uint8_t* dst = x_ring + sx * Cfg::kX;
+        ptx::tma_load_2d(dst, &tmH, &xfull[sx], cb * kBlockK, h0);
+        ptx::tma_load_2d(dst + Cfg::kHaloBox * 128, &tmH, &xfull[sx], cb * kBlockK, h0 + Cfg::kHaloBox);
+        x_issued[sx] = (int)px;
+        if (++sx == Cfg::kXStages) { sx = 0; px ^= 1; }
+        for (int tap = 0; tap < 9; ++tap) {
+          if (!ptx::mbar_wait(&wempty[sw], pw ^ 1, abort_flag, kWaitLimitNs)) goto producer_done;
+          ptx::mbar_arrive_expect_tx(&wfull[sw], Cfg::kW);
+          ptx::tma_load_2d(w_ring + sw * Cfg::kW, &tmB, &wfull[sw], (tap * CB + cb) * kBlockK, 0);
+          w_issued[sw] = (int)pw;
+          if (++sw == Cfg::kWStages) { sw = 0; pw ^= 1; }
+        }
+      }
+    }
+  producer_done:
+    for (int i = 0; i < Cfg::kXStages; ++i)
+      if (x_issued[i] >= 0) {
+        volatile int dummy = 0;
+        ptx::mbar_wait(&xfull[i], (uint32_t)x_issued[i], &dummy, kWaitLimitNs);
+      }
+    for (int i = 0; i < Cfg::kWStages; ++i)
+      if (w_issued[i] >= 0) {
+        volatile int dummy = 0;
+        ptx::mbar_wait(&wfull[i], (uint32_t)w_issued[i], &dummy, kWaitLimitNs);
+      }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer: A = weights (M = 128 channels), B = pixel window (N = 256) ----
+    constexpr uint32_t idesc = ptx::idesc_bf16_f32(BN, Cfg::kRows);
+    const uint64_t w_desc0 = ptx::smem_desc_sw128(ptx::smem_u32(w_ring));
+    int sx = 0, sw = 0;
+    uint32_t px = 0, pw = 0;
+    bool any = false;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+      const int ab = t & 1;
+      const uint32_t aph = (t >> 1) & 1;
+      if (!ptx::mbar_wait(&tempty[ab], aph ^ 1, abort_flag, kWaitLimitNs)) break;
+      ptx::tc_fence_after();
+      const uint32_t d = tmem + ab * Cfg::kRows;
+      bool ok = true;
+      for (int cb = 0; cb < CB && ok; ++cb) {
+        if (!ptx::mbar_wait(&xfull[sx], px, abort_flag, kWaitLimitNs)) { ok = false; break; }
+        ptx::tc_fence_after();
+        const uint64_t x_desc0 = ptx::smem_desc_sw128(ptx::smem_u32(x_ring + sx * Cfg::kX));
+#pragma unroll
+        for (int tap = 0; tap < 9; ++tap) {
+          if (!ptx::mbar_wait(&wfull[sw], pw, abort_flag, kWaitLimitNs)) { ok = false; break; }
+          ptx::tc_fence_after();
+          const int off = Cfg::kLead + (tap / 3 - 1) * rowstride + (tap % 3 - 1);
+          const uint64_t xd = x_desc0 + (uint64_t)(off * 8);             // off rows of 128 B
+          const uint64_t wd = w_desc0 + (uint64_t)(sw * (Cfg::kW >> 4));
+          ptx::mma_bf16(d, wd, xd, idesc, (cb | tap) != 0);
+#pragma unroll
+          for (int k = 1; k < kBlockK / 16; ++k) ptx::mma_bf16(d, wd + 2 * k, xd + 2 * k, idesc, 1u);
+          any = true;
+          ptx::mma_commit(&wempty[sw]);
+          if (++sw == Cfg::kWStages) { sw = 0; pw ^= 1; }
+        }
+        if (!ok) break;
+        ptx::mma_commit(&xempty[sx]);
+        if (++sx == Cfg::kXStages) { sx = 0; px ^= 1; }
+      }
+      if (!ok) break;
+      ptx::mma_commit(&tfull[ab]);
+    }
+    if (any) {
+      ptx::mma_commit(drain);
+      volatile int dummy = 0;
+      ptx::mbar_wait(drain, 0, &dummy, kWaitLimitNs);
+    }
+  } else if (warp >= 2) {
+    // ---------------- epilogue ----------------
+    // Warp w reads TMEM lanes (= output channels) 32q..32q+31, q = w % 4; the two warps of a lane
+    // quarter take alternate 32-pixel column chunks of the tile.
+    const int q = warp & 3;
+    const int wq = (warp - 2) >> 2;
+    uint8_t* my_stage = staging + (warp - 2) * Cfg::kStagePerWarp;
+    float* tr = reinterpret_cast<float*>(my_stage + 2 * 2048);  // [32 px][32 ch] fp32, swizzled
+    const float bias = s_bias[q * 32 + lane];
+    int buf = 0;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+      const int ab = t & 1;
+      const uint32_t aph = (t >> 1) & 1;
+      if (!ptx::mbar_wait(&tfull[ab], aph, abort_flag, kWaitLimitNs)) break;
+      ptx::tc_fence_after();
+#pragma unroll 1
+      for (int j = wq; j < Cfg::kRows / 32; j += 2) {
+        uint32_t r[32];
+        ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + ab * Cfg::kRows + j * 32, r);
+        ptx::tmem_ld_wait();
+        // transpose: this lane holds channel c = lane for pixels 0..31 of the chunk; word (p, c)
+        // lives at p * 32 + ((c / 4) ^ (p % 8)) * 4 + c % 4 (conflict-free both ways)
+        __syncwarp();
+#pragma unroll
+        for (int p = 0; p < 32; ++p)
+          tr[p * 32 + (((lane >> 2) ^ (p & 7)) << 2) + (lane & 3)] = __uint_as_float(r[p]) + bias;
+        __syncwarp();
+        const int row0 = tile * Cfg::kRows + j * 32;
+        const int m = row0 + lane;
+        const bool valid = m < rows;
+        const int pix = m % args.P;
+        const int y = pix / rowstride, x = pix - y * rowstride;
+        const bool pad = !valid || (y == args.S) || (x == args.S);
+        uint4 packed[4];
+        uint32_t* pwd = reinterpret_cast<uint32_t*>(packed);
+        if (pad) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pwd[i] = 0u;
+        } else {
+          float v[32];
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4) {
+            const float4 f = *reinterpret_cast<const float4*>(tr + lane * 32 + ((c4 ^ (lane & 7)) << 2));
+            v[4 * c4] = f.x; v[4 * c4 + 1] = f.y; v[4 * c4 + 2] = f.z; v[4 * c4 + 3] = f.w;
+          }
+          if (args.residual) {
+            const uint4* rp = reinterpret_cast<const uint4*>(args.residual + (size_t)m * BN + q * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint4 u = rp[i];
+              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = __bfloat1622float2(h[e]);
+                v[8 * i + 2 * e] += f.x;
+                v[8 * i + 2 * e + 1] += f.y;
+              }
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            float v0 = v[i], v1 = v[i + 1];
+            if (args.relu) { v0 = fmaxf(v0, 0.0f); v1 = fmaxf(v1, 0.0f); }
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
+            pwd[i / 2] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+        }
+        // the buffer about to be written must no longer be read by an earlier store
+        if (lane == 0) ptx::bulk_wait_read<1>();
+        __syncwarp();
+        uint8_t* sbuf = my_stage + buf * 2048;
+        const int swz = (lane >> 1) & 3;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(sbuf + lane * 64 + ((i ^ swz) * 16)) = packed[i];
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          ptx::tma_store_2d(&tmO, sbuf, q * 32, row0);
+          ptx::bulk_commit();
+        }
+        buf ^= 1;
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&tempty[ab]);
+    }
+    if (lane == 0) ptx::bulk_wait<0>();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(args.error, OMQ_TIMEOUT);
+}
 
 // ---------------------------------------------------------------------------------------------
 // input packing: reference fp32 features [n][planes][S][S] -> bf16 [n][P][in_pad] padded pixel space
@@ -1167,23 +1445,26 @@ static int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t o
   return OMQ_OK;
 }
 
-// Conv kernel variant per filter count (OMQ_CONV_KERNEL=single|pair|transposed|halo forces one,
+// Conv kernel variant per filter count (OMQ_CONV_KERNEL=single|pair|transposed|halo|halot forces one,
 // for measurements): 0 = single CTA, 1 = CTA pair (default for 256 filters: 1.16 vs 1.07 PFLOP/s),
-// 2 = transposed, 3 = halo (default for 128 filters: 1.00 vs 0.94 PFLOP/s at batch 4096).
+// 2 = transposed, 3 = halo, 4 = transposed halo (default for 128 filters: 1.12 vs 0.94 PFLOP/s for
+// the halo kernel at batch 65,536, power-capped).
 static int conv_variant(int filters) {
   const char* v = getenv("OMQ_CONV_KERNEL");
   if (v && strcmp(v, "single") == 0) return 0;
   if (v && strcmp(v, "pair") == 0) return 1;
   if (v && strcmp(v, "transposed") == 0 && filters == 128) return 2;
   if (v && strcmp(v, "halo") == 0 && filters == 128) return 3;
-  return filters == 256 ? 1 : 3;
+  if (v && strcmp(v, "halot") == 0 && filters == 128) return 4;
+  return filters == 256 ? 1 : 4;
 }
 
 // Tensor maps of a net's activation buffers and weights. Box heights follow the kernel variant:
 // A boxes are 128 rows (pair) or 128 * conv_sub(C) rows (single CTA); weight boxes are the CTA's
 // half of the output channels (pair) or all of them.
 static int build_maps(omq_resnet* n) {
-  const uint32_t a_rows = n->pair == 1 ? kTileM : n->pair == 3 ? HaloCfg::kHaloBox : kTileM * conv_sub(n->C);
+  const uint32_t a_rows = n->pair == 1 ? kTileM : (n->pair == 3 || n->pair == 4) ? HaloCfg::kHaloBox
+                                                                                : kTileM * conv_sub(n->C);
   const uint32_t b_rows = n->pair == 1 ? n->C / 2 : n->C;
   int st = make_map(&n->tmA_in, n->x_in, n->in_pad, n->rows, a_rows);
   for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n->tmA[i], n->act[i], n->C, n->rows, a_rows);
@@ -1353,25 +1634,74 @@ static int launch_conv(const omq_resnet* n, const CUtensorMap& tA, const CUtenso
   return cuda_status(cudaGetLastError(), "k_conv3x3");
 }
 
-static int launch_conv_halo(const omq_resnet* n, const CUtensorMap& tH, const CUtensorMap& tB,
-                            const CUtensorMap& tO, const float* bias, const __nv_bfloat16* res,
-                            __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count, int count,
-                            cudaStream_t s) {
+template <int BS, int SB, int EW>
+static int launch_conv_halo_t(const omq_resnet* n, const CUtensorMap& tH, const CUtensorMap& tB,
+                              const CUtensorMap& tO, const ConvArgs& a, cudaStream_t s) {
+  using Cfg = HaloCfgT<BS, SB, EW>;
   static int attr_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (attr_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(k_conv3x3_halo, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         HaloCfg::kSmem);
+    cudaError_t e = cudaFuncSetAttribute(k_conv3x3_halo<BS, SB, EW>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
     if (e != cudaSuccess) return cuda_status(e, "halo conv smem attribute");
     attr_dev = dev;
   }
-  ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
-  const int max_tiles = (int)((n->rows + HaloCfg::kRows - 1) / HaloCfg::kRows);
+  const int max_tiles = (int)((n->rows + Cfg::kRows - 1) / Cfg::kRows);
   const int grid = max(1, min(max_tiles, n->sm_count));
   count_launches(1);
-  k_conv3x3_halo<<<grid, HaloCfg::kThreads, HaloCfg::kSmem, s>>>(tH, tB, tO, a);
+  k_conv3x3_halo<BS, SB, EW><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(tH, tB, tO, a);
   return cuda_status(cudaGetLastError(), "k_conv3x3_halo");
+}
+
+// Weight stages x staging buffers x epilogue warps of the halo kernel
+// (OMQ_HALO_PIPE=6x2|8x1|6x2e12|4x2e16|5x1e16).
+static int halo_pipe() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("OMQ_HALO_PIPE");
+    v = 0;
+    if (e && strcmp(e, "8x1") == 0) v = 2;
+    if (e && strcmp(e, "6x2e12") == 0) v = 3;
+    if (e && strcmp(e, "4x2e16") == 0) v = 4;
+    if (e && strcmp(e, "5x1e16") == 0) v = 5;
+  }
+  return v;
+}
+
+static int launch_conv_halo(const omq_resnet* n, const CUtensorMap& tH, const CUtensorMap& tB,
+                            const CUtensorMap& tO, const float* bias, const __nv_bfloat16* res,
+                            __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count, int count,
+                            cudaStream_t s) {
+  ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
+  switch (halo_pipe()) {
+    case 2: return launch_conv_halo_t<8, 1, 8>(n, tH, tB, tO, a, s);
+    case 3: return launch_conv_halo_t<6, 2, 12>(n, tH, tB, tO, a, s);
+    case 4: return launch_conv_halo_t<4, 2, 16>(n, tH, tB, tO, a, s);
+    case 5: return launch_conv_halo_t<5, 1, 16>(n, tH, tB, tO, a, s);
+    default: return launch_conv_halo_t<6, 2, 8>(n, tH, tB, tO, a, s);
+  }
+}
+
+static int launch_conv_halo_tr(const omq_resnet* n, const CUtensorMap& tH, const CUtensorMap& tB,
+                               const CUtensorMap& tO, const float* bias, const __nv_bfloat16* res,
+                               __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count, int count,
+                               cudaStream_t s) {
+  static int attr_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (attr_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(k_conv3x3_halo_t, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         HaloTCfg::kSmem);
+    if (e != cudaSuccess) return cuda_status(e, "transposed halo conv smem attribute");
+    attr_dev = dev;
+  }
+  ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
+  const int max_tiles = (int)((n->rows + HaloTCfg::kRows - 1) / HaloTCfg::kRows);
+  const int grid = max(1, min(max_tiles, n->sm_count));
+  count_launches(1);
+  k_conv3x3_halo_t<<<grid, HaloTCfg::kThreads, HaloTCfg::kSmem, s>>>(tH, tB, tO, a);
+  return cuda_status(cudaGetLastError(), "k_conv3x3_halo_t");
 }
 
 static int launch_conv_t(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB,
@@ -1420,6 +1750,7 @@ static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& t
                 const float* bias,
                 const __nv_bfloat16* res, __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count,
                 int count, cudaStream_t s) {
+  if (n->pair == 4) return launch_conv_halo_tr(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
   if (n->pair == 3) return launch_conv_halo(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
   if (n->pair == 2) return launch_conv_t(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
   if (n->pair == 1) {
