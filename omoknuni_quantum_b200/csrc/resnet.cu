@@ -1268,22 +1268,38 @@ struct HeadArgs {
   float* value;               // [n]
 };
 
+// acc[p] += w * x[p] for p < HP, x 16-byte aligned in shared memory (HP / 4 broadcast loads).
+template <int HP>
+__device__ __forceinline__ void fma_row(float (&acc)[HP], float w, const float* x) {
+#pragma unroll
+  for (int i = 0; i < HP / 4; ++i) {
+    const float4 v = reinterpret_cast<const float4*>(x)[i];
+    acc[4 * i] += w * v.x; acc[4 * i + 1] += w * v.y; acc[4 * i + 2] += w * v.z; acc[4 * i + 3] += w * v.w;
+  }
+}
+
+template <int HP>
 __global__ void __launch_bounds__(kHeadThreads) k_heads(HeadArgs a) {
+  static_assert(HP % 4 == 0, "positions per block: a multiple of 4 (16-byte broadcast loads)");
   extern __shared__ float hsm[];
   const int HW = a.S * a.S;
-  float* h3 = hsm;                                // [kHeadPos][3*HW]
-  float* hp = h3 + kHeadPos * 3 * HW;             // [kHeadPos][Hp]
-  float* lg = hp + kHeadPos * a.Hp;               // [kHeadPos][A]
-  float* hv = lg + kHeadPos * a.A;                // [kHeadPos][Hv]
-  float* w1 = hv + kHeadPos * a.Hv;               // [3][C]
+  // Activations are kept position-minor ([k][8]) so that one k's 8 positions are two 16-byte
+  // broadcast loads per 8 FMAs in the fully connected layers.
+  float* h3 = hsm;                                // [3*HW][HP]
+  float* hp = h3 + HP * 3 * HW;             // [Hp][HP]
+  float* lg = hp + HP * a.Hp;               // [HP][A]
+  float* hv = lg + HP * a.A;                // [HP][Hv]
+  float* w1 = hv + HP * a.Hv;               // [3][C]
   const int n = a.d_count ? min(*a.d_count, a.count) : a.count;
-  const int p0 = blockIdx.x * kHeadPos;
+  const int p0 = blockIdx.x * HP;
   if (p0 >= n) return;
-  const int np = min(kHeadPos, n - p0);
+  const int np = min(HP, n - p0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < 3 * a.C; i += kHeadThreads) w1[i] = a.w1x1[i];
+  // positions past the batch end compute on zeros (their outputs are not written)
+  for (int i = tid; i < 3 * HW * HP; i += kHeadThreads) h3[i] = 0.f;
   __syncthreads();
-  // 1x1 convolutions + folded BN + ReLU -> h3[pos][ch*HW + cell]
+  // 1x1 convolutions + folded BN + ReLU -> h3[ch*HW + cell][pos]
   for (int i = tid; i < np * HW; i += kHeadThreads) {
     const int pl = i / HW, cell = i - pl * HW;
     const int yy = cell / a.S, xx = cell - yy * a.S;
@@ -1292,57 +1308,64 @@ __global__ void __launch_bounds__(kHeadThreads) k_heads(HeadArgs a) {
     for (int c = 0; c < a.C; c += 8) {
       uint4 u = *reinterpret_cast<const uint4*>(row + c);
       const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+      float x[8];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        float2 f = __bfloat1622float2(h[e]);
-        const int cc = c + 2 * e;
-        s0 += f.x * w1[cc] + f.y * w1[cc + 1];
-        s1 += f.x * w1[a.C + cc] + f.y * w1[a.C + cc + 1];
-        s2 += f.x * w1[2 * a.C + cc] + f.y * w1[2 * a.C + cc + 1];
+        const float2 f = __bfloat1622float2(h[e]);
+        x[2 * e] = f.x;
+        x[2 * e + 1] = f.y;
+      }
+      const float4* w4 = reinterpret_cast<const float4*>(w1 + c);
+      const float4* w4b = reinterpret_cast<const float4*>(w1 + a.C + c);
+      const float4* w4c = reinterpret_cast<const float4*>(w1 + 2 * a.C + c);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float4 p = w4[e], q = w4b[e], r = w4c[e];
+        s0 += x[4 * e] * p.x + x[4 * e + 1] * p.y + x[4 * e + 2] * p.z + x[4 * e + 3] * p.w;
+        s1 += x[4 * e] * q.x + x[4 * e + 1] * q.y + x[4 * e + 2] * q.z + x[4 * e + 3] * q.w;
+        s2 += x[4 * e] * r.x + x[4 * e + 1] * r.y + x[4 * e + 2] * r.z + x[4 * e + 3] * r.w;
       }
     }
-    float* o = h3 + (size_t)pl * 3 * HW;
-    o[cell] = fmaxf(s0 + a.b1x1[0], 0.f);
-    o[HW + cell] = fmaxf(s1 + a.b1x1[1], 0.f);
-    o[2 * HW + cell] = fmaxf(s2 + a.b1x1[2], 0.f);
+    h3[(size_t)cell * HP + pl] = fmaxf(s0 + a.b1x1[0], 0.f);
+    h3[(size_t)(HW + cell) * HP + pl] = fmaxf(s1 + a.b1x1[1], 0.f);
+    h3[(size_t)(2 * HW + cell) * HP + pl] = fmaxf(s2 + a.b1x1[2], 0.f);
   }
   __syncthreads();
   // policy fc1 (2*HW -> Hp) + ReLU
   for (int j = tid; j < a.Hp; j += kHeadThreads) {
-    float acc[kHeadPos];
+    float acc[HP];
 #pragma unroll
-    for (int p = 0; p < kHeadPos; ++p) acc[p] = 0.f;
+    for (int p = 0; p < HP; ++p) acc[p] = 0.f;
     for (int k = 0; k < 2 * HW; ++k) {
       const float w = __ldg(a.fc1p + (size_t)k * a.Hp + j);
-#pragma unroll
-      for (int p = 0; p < kHeadPos; ++p) acc[p] += w * h3[(size_t)p * 3 * HW + k];
+      fma_row<HP>(acc, w, h3 + (size_t)k * HP);
     }
-    for (int p = 0; p < kHeadPos; ++p) hp[p * a.Hp + j] = fmaxf(acc[p] + a.b1p[j], 0.f);
+    const float b = a.b1p[j];
+#pragma unroll
+    for (int p = 0; p < HP; ++p) hp[(size_t)j * HP + p] = fmaxf(acc[p] + b, 0.f);
   }
   // value fc1 (HW -> Hv) + ReLU
   for (int j = tid; j < a.Hv; j += kHeadThreads) {
-    float acc[kHeadPos];
+    float acc[HP];
 #pragma unroll
-    for (int p = 0; p < kHeadPos; ++p) acc[p] = 0.f;
+    for (int p = 0; p < HP; ++p) acc[p] = 0.f;
     for (int k = 0; k < HW; ++k) {
       const float w = __ldg(a.fc1v + (size_t)k * a.Hv + j);
-#pragma unroll
-      for (int p = 0; p < kHeadPos; ++p) acc[p] += w * h3[(size_t)p * 3 * HW + 2 * HW + k];
+      fma_row<HP>(acc, w, h3 + (size_t)(2 * HW + k) * HP);
     }
-    for (int p = 0; p < kHeadPos; ++p) hv[p * a.Hv + j] = fmaxf(acc[p] + a.b1v[j], 0.f);
+    for (int p = 0; p < HP; ++p) hv[p * a.Hv + j] = fmaxf(acc[p] + a.b1v[j], 0.f);
   }
   __syncthreads();
   // policy fc2 (Hp -> A)
   for (int j = tid; j < a.A; j += kHeadThreads) {
-    float acc[kHeadPos];
+    float acc[HP];
 #pragma unroll
-    for (int p = 0; p < kHeadPos; ++p) acc[p] = 0.f;
+    for (int p = 0; p < HP; ++p) acc[p] = 0.f;
     for (int k = 0; k < a.Hp; ++k) {
       const float w = __ldg(a.fc2p + (size_t)k * a.A + j);
-#pragma unroll
-      for (int p = 0; p < kHeadPos; ++p) acc[p] += w * hp[p * a.Hp + k];
+      fma_row<HP>(acc, w, hp + (size_t)k * HP);
     }
-    for (int p = 0; p < kHeadPos; ++p) lg[p * a.A + j] = acc[p] + a.b2p[j];
+    for (int p = 0; p < HP; ++p) lg[p * a.A + j] = acc[p] + a.b2p[j];
   }
   __syncthreads();
   // softmax (= exp(log_softmax)) and value fc2 + tanh: one warp per position
@@ -1481,8 +1504,16 @@ static size_t head_floats(const omq_resnet* n) {
          (size_t)n->HW * n->Hv + n->Hv + n->Hv + 1;
 }
 
-static size_t head_smem(const omq_resnet* n) {
-  return sizeof(float) * ((size_t)kHeadPos * (3 * n->HW + n->Hp + n->A + n->Hv) + 3 * n->C);
+static size_t head_smem_for(const omq_resnet* n, int hp) {
+  return sizeof(float) * ((size_t)hp * (3 * n->HW + n->Hp + n->A + n->Hv) + 3 * n->C);
+}
+static size_t head_smem(const omq_resnet* n) { return head_smem_for(n, kHeadPos); }
+// Positions per heads block: 8 (measured on B200 for ResNet 10x128 at 16,384 positions: 1.00 ms
+// with 8, 1.09 ms with 16; OMQ_HEAD_POS=16 selects 16 where it fits).
+static int head_pos(const omq_resnet* n) {
+  const char* e = getenv("OMQ_HEAD_POS");
+  if (e && strcmp(e, "16") == 0 && head_smem_for(n, 16) <= 227 * 1024) return 16;
+  return 8;
 }
 
 extern "C" {
@@ -1805,14 +1836,15 @@ int resnet_run(omq_resnet* n, const int32_t* d_count, int count, float* policy, 
   h.count = count;
   h.policy = policy;
   h.value = value;
-  const size_t sm = head_smem(n);
-  if (sm > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(k_heads, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    if (e != cudaSuccess) return cuda_status(e, "heads smem attribute");
-  }
-  const int blocks = (count + kHeadPos - 1) / kHeadPos;
+  const int hpos = head_pos(n);
+  const size_t sm = head_smem_for(n, hpos);
+  cudaError_t e = cudaFuncSetAttribute(hpos == 16 ? k_heads<16> : k_heads<8>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  if (e != cudaSuccess) return cuda_status(e, "heads smem attribute");
+  const int blocks = (count + hpos - 1) / hpos;
   count_launches(1);
-  k_heads<<<blocks, kHeadThreads, sm, s>>>(h);
+  if (hpos == 16) k_heads<16><<<blocks, kHeadThreads, sm, s>>>(h);
+  else k_heads<8><<<blocks, kHeadThreads, sm, s>>>(h);
   return cuda_status(cudaGetLastError(), "k_heads");
 }
 
