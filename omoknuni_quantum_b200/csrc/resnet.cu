@@ -1243,6 +1243,260 @@ __global__ void k_pack_features(const float* feat, int planes, int S, int P, con
   }
 }
 
+
+// ---------------------------------------------------------------------------------------------
+// heads on the tensor cores: 1x1 convolutions into bf16 rows, then one tcgen05 dense layer per
+// fully connected layer (M = 128 positions x N <= 256 outputs per UMMA, bf16 in, fp32 accumulate)
+// with the layer's epilogue fused (bias + ReLU -> bf16, softmax, or the value dot + tanh).
+// ---------------------------------------------------------------------------------------------
+enum DenseMode { kDenseReluBf16 = 0, kDenseSoftmax = 1, kDenseLogits = 2, kDenseValue = 3 };
+
+struct DenseArgs {
+  const float* bias;       // [n_total]
+  const float* w2;         // value mode: fc2 weights [n_total]
+  const float* b2;         // value mode: fc2 bias [1]
+  void* out;               // bf16 [rows][ld] | fp32 [rows][ld] | value fp32 [rows]
+  int ld;                  // output row length (elements)
+  int n_total;             // valid outputs
+  int kblocks;             // K / 64
+  const int32_t* d_count;
+  int count;
+  int32_t* error;
+};
+
+constexpr int kDenseStages = 2;
+constexpr int kDenseThreads = 192;  // TMA warp, MMA warp, 4 epilogue warps
+// Shared memory requested by every dense launch: two stages of the widest tile, so that at most
+// two CTAs (2 x 256 TMEM columns) share an SM.
+constexpr int kDenseSmem = kDenseStages * (128 * 128 + 256 * 128) + 1024 + 256;
+
+template <int NT, int MODE>
+__global__ void __launch_bounds__(kDenseThreads)
+    k_dense(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, DenseArgs a) {
+  constexpr int kA = 128 * 128, kW = NT * 128;            // bytes per 64-wide K block
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* ring = smem;                                    // kDenseStages x (kA + kW)
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kDenseStages * (kA + kW));
+  uint64_t* empty = full + kDenseStages;
+  uint64_t* tfull = empty + kDenseStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int n = a.d_count ? min(*a.d_count, a.count) : a.count;
+  const int row0 = blockIdx.x * 128, col0 = blockIdx.y * NT;
+  if (row0 >= n) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kDenseStages; ++s) { ptx::mbar_init(&full[s], 1); ptx::mbar_init(&empty[s], 1); }
+    ptx::mbar_init(tfull, 1);
+    *abort_flag = 0;
+    ptx::fence_barrier_init();
+    ptx::prefetch_tmap(&tmA);
+    ptx::prefetch_tmap(&tmW);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, 256);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    int issued[kDenseStages] = {-1, -1};
+    for (int kb = 0; kb < a.kblocks; ++kb) {
+      const int s = kb % kDenseStages;
+      const uint32_t ph = (uint32_t)((kb / kDenseStages) & 1);
+      if (!ptx::mbar_wait(&empty[s], ph ^ 1, abort_flag, kWaitLimitNs)) break;
+      ptx::mbar_arrive_expect_tx(&full[s], kA + kW);
+      ptx::tma_load_2d(ring + s * (kA + kW), &tmA, &full[s], kb * kBlockK, row0);
+      ptx::tma_load_2d(ring + s * (kA + kW) + kA, &tmW, &full[s], kb * kBlockK, col0);
+      issued[s] = (int)ph;
+    }
+    for (int s = 0; s < kDenseStages; ++s)
+      if (issued[s] >= 0) {
+        volatile int dummy = 0;
+        ptx::mbar_wait(&full[s], (uint32_t)issued[s], &dummy, kWaitLimitNs);
+      }
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = ptx::idesc_bf16_f32(128, NT);
+    const uint64_t d0 = ptx::smem_desc_sw128(ptx::smem_u32(ring));
+    bool ok = true;
+    for (int kb = 0; kb < a.kblocks && ok; ++kb) {
+      const int s = kb % kDenseStages;
+      if (!ptx::mbar_wait(&full[s], (uint32_t)((kb / kDenseStages) & 1), abort_flag, kWaitLimitNs)) { ok = false; break; }
+      ptx::tc_fence_after();
+      const uint64_t ad = d0 + (uint64_t)(s * ((kA + kW) >> 4));
+      const uint64_t wd = ad + (uint64_t)(kA >> 4);
+#pragma unroll
+      for (int k = 0; k < kBlockK / 16; ++k) ptx::mma_bf16(tmem, ad + 2 * k, wd + 2 * k, idesc, (kb | k) != 0);
+      ptx::mma_commit(&empty[s]);
+    }
+    ptx::mma_commit(tfull);
+    // the MMAs must be complete before TMEM is freed at the end
+    volatile int dummy = 0;
+    ptx::mbar_wait(tfull, 0, &dummy, kWaitLimitNs);
+  } else if (warp >= 2) {
+    // epilogue: warp 2 + q reads TMEM lanes 32q.. (rows); one row per thread
+    const int q = warp & 3;
+    const int r = row0 + q * 32 + lane;
+    const bool live = r < n;
+    const bool ok = ptx::mbar_wait(tfull, 0, abort_flag, kWaitLimitNs);
+    ptx::tc_fence_after();
+    const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+    const int ncols = min(NT, a.n_total - col0);
+    if (ok && MODE == kDenseReluBf16) {
+      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (size_t)r * a.ld + col0;
+      for (int c0 = 0; c0 < NT; c0 += 32) {
+        uint32_t v[32];
+        ptx::tmem_ld_32x32b_x32(taddr + c0, v);
+        ptx::tmem_ld_wait();
+        if (live && c0 < ncols) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const float x0 = fmaxf(__uint_as_float(v[j]) + a.bias[col0 + c0 + j], 0.f);
+            const float x1 = fmaxf(__uint_as_float(v[j + 1]) + a.bias[col0 + c0 + j + 1], 0.f);
+            __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+            pk[j / 2] = *reinterpret_cast<uint32_t*>(&h);
+          }
+          uint4* o = reinterpret_cast<uint4*>(out + c0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) o[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+        }
+      }
+    } else if (ok && MODE == kDenseLogits) {
+      float* out = static_cast<float*>(a.out) + (size_t)r * a.ld + col0;
+      for (int c0 = 0; c0 < NT; c0 += 32) {
+        uint32_t v[32];
+        ptx::tmem_ld_32x32b_x32(taddr + c0, v);
+        ptx::tmem_ld_wait();
+        if (live) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (c0 + j < ncols) out[c0 + j] = __uint_as_float(v[j]) + a.bias[col0 + c0 + j];
+        }
+      }
+    } else if (ok && MODE == kDenseSoftmax) {
+      // the whole policy row is this tile's (n_total <= NT): max, sum, then the probabilities
+      float mx = -INFINITY;
+      for (int c0 = 0; c0 < NT; c0 += 32) {
+        uint32_t v[32];
+        ptx::tmem_ld_32x32b_x32(taddr + c0, v);
+        ptx::tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < ncols) mx = fmaxf(mx, __uint_as_float(v[j]) + a.bias[c0 + j]);
+      }
+      float sum = 0.f;
+      for (int c0 = 0; c0 < NT; c0 += 32) {
+        uint32_t v[32];
+        ptx::tmem_ld_32x32b_x32(taddr + c0, v);
+        ptx::tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < ncols) sum += expf(__uint_as_float(v[j]) + a.bias[c0 + j] - mx);
+      }
+      const float inv = 1.0f / sum;
+      float* out = static_cast<float*>(a.out) + (size_t)r * a.ld;
+      for (int c0 = 0; c0 < NT; c0 += 32) {
+        uint32_t v[32];
+        ptx::tmem_ld_32x32b_x32(taddr + c0, v);
+        ptx::tmem_ld_wait();
+        if (live) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (c0 + j < ncols) out[c0 + j] = expf(__uint_as_float(v[j]) + a.bias[c0 + j] - mx) * inv;
+        }
+      }
+    } else if (ok && MODE == kDenseValue) {
+      float acc = 0.f;
+      for (int c0 = 0; c0 < NT; c0 += 32) {
+        uint32_t v[32];
+        ptx::tmem_ld_32x32b_x32(taddr + c0, v);
+        ptx::tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < ncols) acc += fmaxf(__uint_as_float(v[j]) + a.bias[c0 + j], 0.f) * a.w2[c0 + j];
+      }
+      if (live) static_cast<float*>(a.out)[r] = tanhf(acc + a.b2[0]);
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 256);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(a.error, OMQ_TIMEOUT);
+}
+
+// Softmax of fp32 logit rows in place (policies wider than one dense tile). One warp per row.
+__global__ void k_softmax_rows(float* x, int ld, int n_total, const int32_t* d_count, int count) {
+  const int n = d_count ? min(*d_count, count) : count;
+  const int lane = threadIdx.x & 31;
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n; r += gridDim.x * (blockDim.x >> 5)) {
+    float* row = x + (size_t)r * ld;
+    float mx = -INFINITY;
+    for (int j = lane; j < n_total; j += 32) mx = fmaxf(mx, row[j]);
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    float sum = 0.f;
+    for (int j = lane; j < n_total; j += 32) sum += expf(row[j] - mx);
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+    const float inv = 1.0f / sum;
+    for (int j = lane; j < n_total; j += 32) row[j] = expf(row[j] - mx) * inv;
+  }
+}
+
+// 1x1 convolutions (policy 2 channels, value 1) + folded BN + ReLU into the dense layers' bf16
+// input rows: pin[pos][ch * HW + cell] (K padded, pad columns stay zero), vin[pos][cell].
+__global__ void k_head_in(const __nv_bfloat16* act, int C, int S, int P, const float* w1x1,
+                          const float* b1x1, const int32_t* d_count, int count,
+                          __nv_bfloat16* pin, int ld_p, __nv_bfloat16* vin, int ld_v) {
+  extern __shared__ float w1[];  // [3][C]
+  for (int i = threadIdx.x; i < 3 * C; i += blockDim.x) w1[i] = w1x1[i];
+  __syncthreads();
+  const int n = d_count ? min(*d_count, count) : count;
+  const int HW = S * S;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n * HW; i += gridDim.x * blockDim.x) {
+    const int pos = i / HW, cell = i - pos * HW;
+    const int yy = cell / S, xx = cell - yy * S;
+    const __nv_bfloat16* row = act + ((size_t)pos * P + yy * (S + 1) + xx) * C;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+    for (int c = 0; c < C; c += 8) {
+      uint4 u = *reinterpret_cast<const uint4*>(row + c);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+      float x[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        x[2 * e] = f.x;
+        x[2 * e + 1] = f.y;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        s0 += x[e] * w1[c + e];
+        s1 += x[e] * w1[C + c + e];
+        s2 += x[e] * w1[2 * C + c + e];
+      }
+    }
+    pin[(size_t)pos * ld_p + cell] = __float2bfloat16_rn(fmaxf(s0 + b1x1[0], 0.f));
+    pin[(size_t)pos * ld_p + HW + cell] = __float2bfloat16_rn(fmaxf(s1 + b1x1[1], 0.f));
+    vin[(size_t)pos * ld_v + cell] = __float2bfloat16_rn(fmaxf(s2 + b1x1[2], 0.f));
+  }
+}
+
+// Dense-layer weights W[j][k] (bf16, K-major, zero padded to kpad columns and npad rows) from
+// the fp32 head blob's transposed layout src[k][j] (k < kin, j < nout).
+__global__ void k_pack_dense_w(const float* src, int kin, int nout, int kpad, int npad, __nv_bfloat16* dst) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < npad * kpad; i += gridDim.x * blockDim.x) {
+    const int j = i / kpad, k = i - j * kpad;
+    dst[i] = __float2bfloat16_rn((j < nout && k < kin) ? src[(size_t)k * nout + j] : 0.f);
+  }
+}
+
 // ---------------------------------------------------------------------------------------------
 // heads
 // ---------------------------------------------------------------------------------------------
@@ -1418,6 +1672,11 @@ struct omq_resnet {
   CUtensorMap tmO[3];      // output maps of the activation buffers (TMA-store epilogue)
   CUtensorMap* tmB;        // [2*NB]
   int loaded;
+  // tensor-core heads (dense layers): bf16 inputs / hidden rows, bf16 weights, their maps
+  int tc_heads;
+  int k1p, k3p, n1pad, n2pad, n3pad, nt3;  // padded K of fc1 policy / fc1 value, padded rows
+  __nv_bfloat16 *pin, *vin, *hid, *w1b, *w2b, *w3b;
+  CUtensorMap tm_pin, tm_vin, tm_hid, tm_w1, tm_w2, tm_w3;
   int pair;                // conv variant: 0 single CTA, 1 CTA pair (cta_group::2), 2 transposed
   // optional timing of the conv trunk of each forward call (CUDA events on the caller's stream)
   int prof_cap, prof_n;
@@ -1496,6 +1755,14 @@ static int build_maps(omq_resnet* n) {
   const __nv_bfloat16* wb = n->conv_w + (size_t)n->C * 9 * n->in_pad;
   for (int i = 0; st == OMQ_OK && i < 2 * n->NB; ++i)
     st = make_map(&n->tmB[i], wb + (size_t)i * n->C * 9 * n->C, 9 * n->C, n->C, b_rows);
+  if (st == OMQ_OK && n->tc_heads) {
+    st = make_map(&n->tm_pin, n->pin, n->k1p, n->max_batch, 128);
+    if (st == OMQ_OK) st = make_map(&n->tm_vin, n->vin, n->k3p, n->max_batch, 128);
+    if (st == OMQ_OK) st = make_map(&n->tm_hid, n->hid, n->Hp, n->max_batch, 128);
+    if (st == OMQ_OK) st = make_map(&n->tm_w1, n->w1b, n->k1p, n->n1pad, 256);
+    if (st == OMQ_OK) st = make_map(&n->tm_w2, n->w2b, n->Hp, n->n2pad, 256);
+    if (st == OMQ_OK) st = make_map(&n->tm_w3, n->w3b, n->k3p, n->n3pad, n->nt3);
+  }
   return st;
 }
 
@@ -1553,7 +1820,7 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
   cudaDeviceGetAttribute(&n->sm_count, cudaDevAttrMultiProcessorCount, c.device);
   const size_t nconv_w = (size_t)n->C * 9 * n->in_pad + (size_t)2 * n->NB * n->C * 9 * n->C;
   const size_t nconv_b = (size_t)(1 + 2 * n->NB) * n->C;
-  size_t off[8], k = 0, tot = 0;
+  size_t off[16], k = 0, tot = 0;
   auto take = [&](size_t b) { off[k++] = tot; tot += (b + 1023) & ~(size_t)1023; };
   take(nconv_w * 2);
   take(nconv_b * 4);
@@ -1561,6 +1828,22 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
   take(n->rows * n->in_pad * 2);
   for (int i = 0; i < 3; ++i) take(n->rows * n->C * 2);
   take(16);
+  // tensor-core heads: fc1 width a multiple of 64 (it is the next layer's K), value width <= 256
+  n->tc_heads = (n->Hp % 64 == 0 && n->Hp <= 1024 && n->Hv % 16 == 0 && n->Hv <= 256 &&
+                 !(getenv("OMQ_SIMT_HEADS") && strcmp(getenv("OMQ_SIMT_HEADS"), "1") == 0)) ? 1 : 0;
+  n->k1p = (2 * n->HW + 63) / 64 * 64;
+  n->k3p = (n->HW + 63) / 64 * 64;
+  n->n1pad = (n->Hp + 255) / 256 * 256;
+  n->n2pad = (n->A + 255) / 256 * 256;
+  n->nt3 = n->Hv <= 128 ? 128 : 256;
+  n->n3pad = n->nt3;
+  const size_t mb = (size_t)n->max_batch;
+  take(n->tc_heads ? mb * n->k1p * 2 : 16);                      // 8 pin
+  take(n->tc_heads ? mb * n->k3p * 2 : 16);                      // 9 vin
+  take(n->tc_heads ? mb * n->Hp * 2 : 16);                       // 10 hid
+  take(n->tc_heads ? (size_t)n->n1pad * n->k1p * 2 : 16);        // 11 W1
+  take(n->tc_heads ? (size_t)n->n2pad * n->Hp * 2 : 16);         // 12 W2
+  take(n->tc_heads ? (size_t)n->n3pad * n->k3p * 2 : 16);        // 13 W3
   void* arena = nullptr;
   cudaError_t e = cudaMalloc(&arena, tot);
   if (e != cudaSuccess) { delete n; return cuda_status(e, "cudaMalloc(resnet)"); }
@@ -1573,6 +1856,12 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
   n->x_in = reinterpret_cast<__nv_bfloat16*>(b + off[3]);
   for (int i = 0; i < 3; ++i) n->act[i] = reinterpret_cast<__nv_bfloat16*>(b + off[4 + i]);
   n->error = reinterpret_cast<int32_t*>(b + off[7]);
+  n->pin = reinterpret_cast<__nv_bfloat16*>(b + off[8]);
+  n->vin = reinterpret_cast<__nv_bfloat16*>(b + off[9]);
+  n->hid = reinterpret_cast<__nv_bfloat16*>(b + off[10]);
+  n->w1b = reinterpret_cast<__nv_bfloat16*>(b + off[11]);
+  n->w2b = reinterpret_cast<__nv_bfloat16*>(b + off[12]);
+  n->w3b = reinterpret_cast<__nv_bfloat16*>(b + off[13]);
   cudaMemset(n->error, 0, 16);
   // activations start zeroed so that never-written padding rows read as zeros
   cudaMemset(b + off[3], 0, tot - off[3]);
@@ -1629,6 +1918,19 @@ int omq_resnet_load(omq_resnet* n, const uint16_t* d_conv_w, const float* d_conv
   if (e == cudaSuccess) e = cudaMemcpyAsync(n->conv_b, d_conv_b, b * 4, cudaMemcpyDeviceToDevice, s);
   if (e == cudaSuccess) e = cudaMemcpyAsync(n->head, d_head, h * 4, cudaMemcpyDeviceToDevice, s);
   if (e != cudaSuccess) return cuda_status(e, "omq_resnet_load");
+  if (n->tc_heads) {
+    // the dense layers' bf16 weights [out][in], from the blob's transposed fp32 layouts
+    const float* p = n->head + 3 * n->C + 3;
+    const float* fc1p = p;
+    const float* fc2p = fc1p + (size_t)2 * n->HW * n->Hp + n->Hp;
+    const float* fc1v = fc2p + (size_t)n->Hp * n->A + n->A;
+    count_launches(3);
+    k_pack_dense_w<<<256, 256, 0, s>>>(fc1p, 2 * n->HW, n->Hp, n->k1p, n->n1pad, n->w1b);
+    k_pack_dense_w<<<256, 256, 0, s>>>(fc2p, n->Hp, n->A, n->Hp, n->n2pad, n->w2b);
+    k_pack_dense_w<<<256, 256, 0, s>>>(fc1v, n->HW, n->Hv, n->k3p, n->n3pad, n->w3b);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_status(e, "omq_resnet_load: dense weights");
+  }
   n->loaded = 1;
   return OMQ_OK;
 }
@@ -1792,6 +2094,70 @@ static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& t
   return launch_conv<256, conv_sub(256)>(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
 }
 
+template <int NT, int MODE>
+static int launch_dense(const CUtensorMap& tA, const CUtensorMap& tW, const DenseArgs& a, int rows_cap,
+                        int ntiles, cudaStream_t s) {
+  static int attr_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (attr_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(k_dense<NT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDenseSmem);
+    if (e != cudaSuccess) return cuda_status(e, "dense smem attribute");
+    attr_dev = dev;
+  }
+  count_launches(1);
+  k_dense<NT, MODE><<<dim3((rows_cap + 127) / 128, ntiles), kDenseThreads, kDenseSmem, s>>>(tA, tW, a);
+  return cuda_status(cudaGetLastError(), "k_dense");
+}
+
+// Heads on the tensor cores: 1x1 convolutions -> bf16 rows, then fc1 (policy) with ReLU,
+// fc2 (policy) with the softmax fused when the policy fits one 256-wide tile, and the value
+// head's fc1 with the fc2 dot and tanh fused.
+static int run_tc_heads(omq_resnet* n, const __nv_bfloat16* act, const int32_t* d_count, int count,
+                        float* policy, float* value, cudaStream_t s) {
+  const float* p = n->head;
+  const float* w1x1 = p; p += 3 * n->C;
+  const float* b1x1 = p; p += 3;
+  p += (size_t)2 * n->HW * n->Hp;
+  const float* b1p = p; p += n->Hp;
+  p += (size_t)n->Hp * n->A;
+  const float* b2p = p; p += n->A;
+  p += (size_t)n->HW * n->Hv;
+  const float* b1v = p; p += n->Hv;
+  const float* fc2v = p; p += n->Hv;
+  const float* b2v = p;
+  count_launches(1);
+  k_head_in<<<max(1, min((count * n->HW + 255) / 256, 4 * n->sm_count)), 256, 3 * n->C * sizeof(float), s>>>(
+      act, n->C, n->S, n->P, w1x1, b1x1, d_count, count, n->pin, n->k1p, n->vin, n->k3p);
+  int st = cuda_status(cudaGetLastError(), "k_head_in");
+  if (st) return st;
+  DenseArgs a{};
+  a.d_count = d_count;
+  a.count = count;
+  a.error = n->error;
+  // policy fc1 -> hidden (bf16, ReLU)
+  a.bias = b1p; a.out = n->hid; a.ld = n->Hp; a.n_total = n->Hp; a.kblocks = n->k1p / 64;
+  st = launch_dense<256, kDenseReluBf16>(n->tm_pin, n->tm_w1, a, count, n->n1pad / 256, s);
+  if (st) return st;
+  // policy fc2 -> probabilities
+  a.bias = b2p; a.out = policy; a.ld = n->A; a.n_total = n->A; a.kblocks = n->Hp / 64;
+  if (n->A <= 256) {
+    st = launch_dense<256, kDenseSoftmax>(n->tm_hid, n->tm_w2, a, count, 1, s);
+  } else {
+    st = launch_dense<256, kDenseLogits>(n->tm_hid, n->tm_w2, a, count, n->n2pad / 256, s);
+    if (!st) {
+      count_launches(1);
+      k_softmax_rows<<<max(1, min((count + 7) / 8, 8 * n->sm_count)), 256, 0, s>>>(policy, n->A, n->A, d_count, count);
+      st = cuda_status(cudaGetLastError(), "k_softmax_rows");
+    }
+  }
+  if (st) return st;
+  // value fc1 + ReLU, fc2, tanh
+  a.bias = b1v; a.w2 = fc2v; a.b2 = b2v; a.out = value; a.ld = 1; a.n_total = n->Hv; a.kblocks = n->k3p / 64;
+  if (n->nt3 == 128) return launch_dense<128, kDenseValue>(n->tm_vin, n->tm_w3, a, count, 1, s);
+  return launch_dense<256, kDenseValue>(n->tm_vin, n->tm_w3, a, count, 1, s);
+}
+
 // trunk + heads on n->x_in (already packed), count from d_count (device) or `count`.
 int resnet_run(omq_resnet* n, const int32_t* d_count, int count, float* policy, float* value,
                cudaStream_t s) {
@@ -1818,6 +2184,7 @@ int resnet_run(omq_resnet* n, const int32_t* d_count, int count, float* policy, 
   }
   if (st) return st;
   if (pi >= 0) cudaEventRecord(n->prof_ev[2 * pi + 1], s);
+  if (n->tc_heads) return run_tc_heads(n, n->act[x], d_count, count, policy, value, s);
   HeadArgs h{};
   h.act = n->act[x];
   h.C = n->C; h.S = n->S; h.P = n->P; h.A = n->A; h.Hp = n->Hp; h.Hv = n->Hv;
