@@ -1476,10 +1476,13 @@ __global__ void k_head_in(const __nv_bfloat16* act, int C, int S, int P, const f
         x[2 * e + 1] = f.y;
       }
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        s0 += x[e] * w1[c + e];
-        s1 += x[e] * w1[C + c + e];
-        s2 += x[e] * w1[2 * C + c + e];
+      for (int e = 0; e < 2; ++e) {
+        const float4 p = reinterpret_cast<const float4*>(w1 + c)[e];
+        const float4 q = reinterpret_cast<const float4*>(w1 + C + c)[e];
+        const float4 r = reinterpret_cast<const float4*>(w1 + 2 * C + c)[e];
+        s0 += x[4 * e] * p.x + x[4 * e + 1] * p.y + x[4 * e + 2] * p.z + x[4 * e + 3] * p.w;
+        s1 += x[4 * e] * q.x + x[4 * e + 1] * q.y + x[4 * e + 2] * q.z + x[4 * e + 3] * q.w;
+        s2 += x[4 * e] * r.x + x[4 * e + 1] * r.y + x[4 * e + 2] * r.z + x[4 * e + 3] * r.w;
       }
     }
     pin[(size_t)pos * ld_p + cell] = __float2bfloat16_rn(fmaxf(s0 + b1x1[0], 0.f));
