@@ -198,10 +198,10 @@ typedef struct omq_resnet omq_resnet;
 
 typedef struct {
   int32_t board_size;        /* 15 Gomoku */
-  int32_t input_channels;    /* feature planes (19 for the reference's basic features), <= 64 */
+  int32_t input_channels;    /* feature planes: 19 Gomoku, 17 Go, 119 chess; <= 128 */
   int32_t num_blocks;        /* residual blocks */
   int32_t filters;           /* 128 or 256 */
-  int32_t num_actions;       /* policy size (225 Gomoku) */
+  int32_t num_actions;       /* policy size (225 Gomoku, 362 Go 19x19, 4672 chess), <= 5000 */
   int32_t fc_policy_hidden;  /* PolicyHead fc1 width (reference default 256) */
   int32_t fc_value_hidden;   /* ValueHead fc1 width (reference default 256) */
   int32_t max_batch;         /* positions per forward call (activation buffers are sized for it) */
@@ -212,7 +212,8 @@ OMQ_API int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out);
 OMQ_API int omq_resnet_destroy(omq_resnet* net);
 OMQ_API int omq_resnet_memory(const omq_resnet* net, uint64_t* h_bytes);
 /* Element counts of the three packed parameter blobs omq_resnet_load expects:
- *  conv_w (bf16): input conv [F][9][64] (input channels zero-padded to 64), then per block
+ *  conv_w (bf16): input conv [F][9][Cin_pad] (input channels zero-padded to 64, or to 128 for
+ *                 more than 64 planes), then per block
  *                 conv1 [F][9][F], conv2 [F][9][F]; K index = tap * Cin + channel, tap = 3*ky+kx;
  *                 BatchNorm scale folded in.
  *  conv_b (fp32): folded BatchNorm shift, [1 + 2*num_blocks][F].
@@ -221,6 +222,9 @@ OMQ_API int omq_resnet_memory(const omq_resnet* net, uint64_t* h_bytes);
  *                 value fc2 [Hv], b [1]. */
 OMQ_API int omq_resnet_param_sizes(const omq_resnet* net, uint64_t* conv_w, uint64_t* conv_b,
                                    uint64_t* head);
+/* Copies the blobs in. When the fully connected widths allow it (policy fc1 width a multiple of
+ * 64, value fc1 width <= 256, a multiple of 16) the heads then run on the tensor cores from bf16
+ * copies of the fc weights made here; otherwise (and in omq_resnet_forward_noalloc) in fp32. */
 OMQ_API int omq_resnet_load(omq_resnet* net, const uint16_t* d_conv_w, const float* d_conv_b,
                             const float* d_head, void* stream);
 /* Forward on reference-layout features fp32 [batch][input_channels][n][n]
