@@ -167,3 +167,29 @@ def test_chess_resnet_queue_path_equals_protocol_path():
         a, b = e1.export_tree(r), e2.export_tree(r)
         for k in a:
             assert np.array_equal(a[k], b[k]), k
+
+
+def test_chess_root_noise_replays_in_oracle_and_tree_full(oracle_lib):
+    from omoknuni_quantum_b200._lib import TreeFullError
+    from omoknuni_quantum_b200.chess import random_position
+    from omoknuni_quantum_b200.engine import WaveEngine
+    p = random_position(12)
+    rec = p.root_records()[None]
+    npr = np.array([len(p.prior)], np.int32)
+    eng = WaveEngine(1, board_size=8, capacity=40000, max_wave_size=32, game="chess",
+                     dirichlet_alpha=0.3, dirichlet_epsilon=0.25, noise_seed=5)
+    eng.begin(rec, meta=npr)
+    eng.root_expand()
+    o = oracle_lib.Oracle(40000, 8)
+    assert o.begin_chess(p.record(), o.config(96, 32), prior=p.prior) == 0
+    for _ in range(3):
+        eng.wave(32)
+        nz = eng.root_noise()[0].cpu().numpy()
+        assert nz.shape == (4672,) and abs(nz.sum() - 1) < 1e-5
+        assert o.wave(32, root_noise=nz, eps=0.25) == 0
+    t, ot = eng.export_tree(0), o.export()
+    for k in ("visits", "value_sums", "priors", "parent", "action"):
+        assert np.array_equal(t[k], getattr(ot, k)), k
+    small = WaveEngine(1, board_size=8, capacity=100, max_wave_size=64, game="chess")
+    with pytest.raises(TreeFullError):
+        small.search(rec, 256, meta=npr)

@@ -176,3 +176,30 @@ def test_go_resnet_queue_path_equals_protocol_path():
         a, b = e1.export_tree(r), e2.export_tree(r)
         for k in a:
             assert np.array_equal(a[k], b[k]), k
+
+
+def test_go_root_noise_replays_in_oracle_and_tree_full(oracle_lib):
+    """Root Dirichlet noise over the Go root's children (pass included) replays bit-exact in the
+    oracle; a too-small capacity raises TreeFullError."""
+    from omoknuni_quantum_b200._lib import TreeFullError
+    from omoknuni_quantum_b200.engine import WaveEngine
+    n = 9
+    hist, meta = _roots(44, 1, 30, n)
+    eng = WaveEngine(1, board_size=n, capacity=60000, max_wave_size=32, game="go",
+                     dirichlet_alpha=0.03, dirichlet_epsilon=0.25, noise_seed=9)
+    eng.begin(torch.from_numpy(hist).cuda(), meta=torch.from_numpy(meta))
+    eng.root_expand()
+    o = oracle_lib.Oracle(60000, n)
+    assert o.begin_go(hist[0], int(meta[0, 0]), o.config(96, 32), ko=int(meta[0, 1]),
+                      passes=int(meta[0, 2])) == 0
+    for _ in range(3):
+        eng.wave(32)
+        nz = eng.root_noise()[0].cpu().numpy()
+        assert nz.shape == (n * n + 1,) and abs(nz.sum() - 1) < 1e-5
+        assert o.wave(32, root_noise=nz, eps=0.25) == 0
+    t, ot = eng.export_tree(0), o.export()
+    for k in ("visits", "value_sums", "priors", "parent", "action"):
+        assert np.array_equal(t[k], getattr(ot, k)), k
+    small = WaveEngine(1, board_size=n, capacity=500, max_wave_size=64, game="go")
+    with pytest.raises(TreeFullError):
+        small.search(torch.from_numpy(hist).cuda(), 256, meta=torch.from_numpy(meta))
