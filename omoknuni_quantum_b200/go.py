@@ -18,8 +18,9 @@ HISTORY = 8
 
 
 class GoPosition:
-    def __init__(self, board_size: int = 19):
+    def __init__(self, board_size: int = 19, komi: float = 7.5):
         self.n = int(board_size)
+        self.komi = float(komi)
         self.board = np.zeros((self.n, self.n), np.int8)
         self.to_move = 1
         self.ko = -1
@@ -31,7 +32,7 @@ class GoPosition:
         return self.n * self.n
 
     def copy(self) -> "GoPosition":
-        g = GoPosition(self.n)
+        g = GoPosition(self.n, self.komi)
         g.board = self.board.copy()
         g.to_move, g.ko, g.passes = self.to_move, self.ko, self.passes
         g.history = [h.copy() for h in self.history[-HISTORY:]]
@@ -109,6 +110,44 @@ class GoPosition:
         for k, b in enumerate(reversed(self.history[-HISTORY:])):
             h[k] = b
         return h
+
+    def score(self):
+        """(black, white) area scores with Chinese rules (GoRules::calculateScores /
+        getTerritoryOwnership, go_rules.cpp:211-260, 343-380): each stone counts for its colour,
+        each empty region bordered by one colour only counts for that colour, komi goes to
+        white. No stones are marked dead."""
+        b = self.board
+        black = float((b == 1).sum())
+        white = float((b == 2).sum()) + self.komi
+        seen = np.zeros_like(b, dtype=bool)
+        for y in range(self.n):
+            for x in range(self.n):
+                if b[y, x] != 0 or seen[y, x]:
+                    continue
+                stack, region, border = [(y, x)], 0, set()
+                seen[y, x] = True
+                while stack:
+                    cy, cx = stack.pop()
+                    region += 1
+                    for ny, nx in ((cy - 1, cx), (cy + 1, cx), (cy, cx - 1), (cy, cx + 1)):
+                        if 0 <= ny < self.n and 0 <= nx < self.n:
+                            if b[ny, nx] == 0 and not seen[ny, nx]:
+                                seen[ny, nx] = True
+                                stack.append((ny, nx))
+                            elif b[ny, nx] != 0:
+                                border.add(int(b[ny, nx]))
+                if border == {1}:
+                    black += region
+                elif border == {2}:
+                    white += region
+        return black, white
+
+    def result(self) -> int:
+        """The reference's GameResult: 0 ongoing, 1 black wins, 2 white wins, 3 draw."""
+        if not self.is_terminal():
+            return 0
+        black, white = self.score()
+        return 1 if black > white else 2 if white > black else 3
 
     def meta(self) -> np.ndarray:
         """int32 [3]: side to move, ko point, consecutive passes (the engine's root record)."""

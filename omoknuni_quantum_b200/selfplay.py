@@ -1,5 +1,6 @@
-"""Batched self-play driver: many Gomoku games advanced move by move, all searches of a move in
-one device wave loop (512 games, 800 simulations, wave 64, 30 moves).
+"""Batched self-play driver: many games advanced move by move, all searches of a move in one device
+wave loop (512 Gomoku games, 800 simulations, wave 64, 30 moves). Gomoku, Go
+and chess games are supported (``game=``).
 
 Per move it follows the reference's ``SelfPlayGame.play_single_move``
 (python/mcts/neural_networks/self_play_manager.py:218-370): search the current position, record
@@ -72,46 +73,153 @@ def game_result(board: np.ndarray) -> Optional[int]:
     return None
 
 
+class _GomokuGame:
+    """Positions are int8 boards; the side to move follows the stone count."""
+    name = "gomoku"
+
+    def __init__(self, n):
+        self.n = n
+
+    def initial(self, roots, G):
+        if roots is None:
+            return [np.zeros((self.n, self.n), np.int8) for _ in range(G)]
+        return [np.array(r, dtype=np.int8, copy=True) for r in roots]
+
+    def engine_input(self, positions):
+        return np.stack(positions), None
+
+    def player(self, pos):
+        return 1 if int((pos != 0).sum()) % 2 == 0 else 2
+
+    def state(self, pos):
+        return pos.copy()
+
+    def apply(self, pos, action):
+        return board_after(pos, action)
+
+    def outcome(self, pos):
+        return game_result(pos)
+
+
+class _GoGame:
+    """Positions are GoPosition objects; the game ends with two passes, scored by area."""
+    name = "go"
+
+    def __init__(self, n):
+        self.n = n
+
+    def initial(self, roots, G):
+        from .go import GoPosition
+        return [GoPosition(self.n) if roots is None else roots[g].copy() for g in range(G)]
+
+    def engine_input(self, positions):
+        return (np.stack([p.history_planes() for p in positions]),
+                np.stack([p.meta() for p in positions]))
+
+    def player(self, pos):
+        return pos.to_move
+
+    def state(self, pos):
+        return pos.history_planes()
+
+    def apply(self, pos, action):
+        q = pos.copy()
+        q.play(int(action))
+        return q
+
+    def outcome(self, pos):
+        r = pos.result()
+        return None if r == 0 else {1: 1, 2: -1, 3: 0}[r]
+
+
+class _ChessGame:
+    """Positions are ChessPosition objects (the reference engine's rules); actions are the
+    engine's 4672 AlphaZero moves of the position."""
+    name = "chess"
+
+    def __init__(self, n):
+        self.n = 8
+
+    def initial(self, roots, G):
+        from .chess import ChessPosition
+        return [ChessPosition() if roots is None else roots[g].copy() for g in range(G)]
+
+    def engine_input(self, positions):
+        return (np.stack([p.root_records() for p in positions]),
+                np.array([len(p.prior) for p in positions], np.int32))
+
+    def player(self, pos):
+        return int(pos.side)
+
+    def state(self, pos):
+        return pos.record()
+
+    def apply(self, pos, action):
+        q = pos.copy()
+        q.play(q.action_to_move(int(action)))
+        return q
+
+    def outcome(self, pos):
+        r = pos.result()
+        return None if r == 0 else {1: 1, 2: -1, 3: 0}[r]
+
+
+_GAMES = {"gomoku": _GomokuGame, "go": _GoGame, "chess": _ChessGame}
+
+
 class BatchedSelfPlay:
     """Self-play of ``num_games`` games in lockstep.
 
-    ``search(boards [G, n, n] int8) -> visits [G, A] int`` runs one move's searches; by default
-    it is a ``WaveEngine`` search with ``evaluator`` ("synthetic", a ResNetEvaluator, or any
-    evaluate_batch object). Finished games keep their final board and are not searched again.
+    ``search(inputs) -> visits [G, A] int`` runs one move's searches; by default it is a
+    ``WaveEngine`` search with ``evaluator`` ("synthetic", a ResNetEvaluator, or any
+    evaluate_batch object). For Gomoku ``inputs`` is the boards array [G, n, n]; for Go and chess
+    it is the pair (root records, meta) that ``WaveEngine.search`` takes. Finished games keep
+    their final position and are not searched again.
     """
 
     def __init__(self, num_games: int, num_simulations: int = 800, wave_size: int = 64,
                  evaluator="synthetic", capacity: int = 200000, c_puct: float = 1.4,
                  temperature: float = 1.0, temperature_threshold: int = 30, seed: int = 0,
-                 roots: Optional[np.ndarray] = None, board_size: int = 15,
-                 search: Optional[Callable[[np.ndarray], np.ndarray]] = None, device=None):
+                 roots=None, board_size: int = 15,
+                 search: Optional[Callable] = None, device=None, game: str = "gomoku"):
+        if game not in _GAMES:
+            raise ValueError(f"unknown game {game!r}")
+        self.game = _GAMES[game](board_size)
         self.G = int(num_games)
         self.sims = int(num_simulations)
         self.temperature = float(temperature)
         self.temperature_threshold = int(temperature_threshold)
-        self.n = board_size
-        self.boards = (np.zeros((self.G, board_size, board_size), np.int8) if roots is None
-                       else np.array(roots, dtype=np.int8, copy=True))
+        self.n = self.game.n
+        self.positions = self.game.initial(roots, self.G)
         self.rngs = [np.random.default_rng([seed, g]) for g in range(self.G)]
         self.records = [GameRecord(game_id=f"selfplay_{seed}_{g}") for g in range(self.G)]
         self.move_number = 0
         self._search = search
         if search is None:
             self._evaluator = evaluator
-            self._engine_args = dict(board_size=board_size, capacity=capacity, max_wave_size=wave_size,
-                                     c_puct=c_puct, device=device)
+            self._engine_args = dict(board_size=self.n, capacity=capacity, max_wave_size=wave_size,
+                                     c_puct=c_puct, device=device, game=game)
             self._engines: Dict[int, object] = {}
 
     # -- search ----------------------------------------------------------------------------
-    def _device_search(self, boards: np.ndarray) -> np.ndarray:
+    @property
+    def boards(self) -> np.ndarray:
+        """Gomoku: the games' boards [G, n, n]."""
+        return np.stack(self.positions)
+
+    def _device_search(self, inputs) -> np.ndarray:
         import torch
         from .engine import WaveEngine
-        R = boards.shape[0]
+        roots, meta = inputs if isinstance(inputs, tuple) else (inputs, None)
+        R = roots.shape[0]
         eng = self._engines.get(R)
         if eng is None:
             eng = WaveEngine(R, **self._engine_args)
             self._engines[R] = eng
-        eng.search(torch.from_numpy(np.ascontiguousarray(boards)).to(eng.device), self.sims, self._evaluator)
+        if self.game.name == "gomoku":
+            eng.search(torch.from_numpy(np.ascontiguousarray(roots)).to(eng.device), self.sims, self._evaluator)
+        else:
+            eng.search(roots, self.sims, self._evaluator, meta=meta)
         return eng.root_visits().cpu().numpy()
 
     def live(self) -> np.ndarray:
@@ -124,15 +232,16 @@ class BatchedSelfPlay:
         if len(live) == 0:
             return 0
         search = self._search or self._device_search
-        visits = np.asarray(search(self.boards[live]))
+        roots, meta = self.game.engine_input([self.positions[g] for g in live])
+        visits = np.asarray(search(roots if meta is None else (roots, meta)))
         for i, g in enumerate(live):
             v = visits[i].astype(np.float64)
             tot = v.sum()
             policy = v / tot if tot > 0 else np.full(v.shape, 1.0 / v.size)
-            board = self.boards[g]
-            player = 1 if int((board != 0).sum()) % 2 == 0 else 2
+            pos = self.positions[g]
+            player = self.game.player(pos)
             rec = self.records[g]
-            rec.examples.append({"state": board.copy(), "policy": policy, "player": player,
+            rec.examples.append({"state": self.game.state(pos), "policy": policy, "player": player,
                                  "move_number": self.move_number})
             if self.move_number < self.temperature_threshold and self.temperature > 0:
                 p = policy if self.temperature == 1.0 else np.power(policy, 1.0 / self.temperature)
@@ -140,9 +249,9 @@ class BatchedSelfPlay:
                 action = int(self.rngs[g].choice(len(p), p=p))
             else:
                 action = int(np.argmax(policy))
-            self.boards[g] = board_after(board, action)
+            self.positions[g] = self.game.apply(pos, action)
             rec.moves.append(action)
-            res = game_result(self.boards[g])
+            res = self.game.outcome(self.positions[g])
             if res is not None:
                 rec.finished = True
                 rec.winner = res

@@ -193,3 +193,16 @@ def test_chess_root_noise_replays_in_oracle_and_tree_full(oracle_lib):
     small = WaveEngine(1, board_size=8, capacity=100, max_wave_size=64, game="chess")
     with pytest.raises(TreeFullError):
         small.search(rec, 256, meta=npr)
+
+
+def test_chess_selfplay_moves_match_oracle(oracle_lib):
+    from omoknuni_quantum_b200.chess import ChessPosition
+    from omoknuni_quantum_b200.selfplay import BatchedSelfPlay
+    sp = BatchedSelfPlay(3, game="chess", num_simulations=64, wave_size=16, capacity=30000, seed=3)
+    recs = sp.play(5)
+    for r in recs:
+        p = ChessPosition()
+        for i, ex in enumerate(r.examples):
+            o = oracle_lib.Oracle(30000, 8).search_chess(p.record(), 64, 16, prior=p.prior)
+            assert np.array_equal(ex["policy"], o.policy)
+            p.play(p.action_to_move(r.moves[i]))

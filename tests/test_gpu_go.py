@@ -203,3 +203,22 @@ def test_go_root_noise_replays_in_oracle_and_tree_full(oracle_lib):
     small = WaveEngine(1, board_size=n, capacity=500, max_wave_size=64, game="go")
     with pytest.raises(TreeFullError):
         small.search(torch.from_numpy(hist).cuda(), 256, meta=torch.from_numpy(meta))
+
+
+def test_go_selfplay_moves_match_oracle(oracle_lib):
+    """Each move's policy in batched device Go self-play equals the oracle's search of that
+    position (history planes, side to move, ko and passes carried between moves)."""
+    from omoknuni_quantum_b200.selfplay import BatchedSelfPlay
+    sp = BatchedSelfPlay(3, game="go", board_size=7, num_simulations=64, wave_size=16,
+                         capacity=30000, seed=2)
+    recs = sp.play(6)
+    for r in recs:
+        for i, ex in enumerate(r.examples):
+            from omoknuni_quantum_b200.go import GoPosition
+            g = GoPosition(7)
+            for a in r.moves[:i]:
+                g.play(a)
+            assert np.array_equal(g.history_planes(), ex["state"])
+            o = oracle_lib.Oracle(30000, 7).search_go(g.history_planes(), g.to_move, 64, 16,
+                                                     ko=g.ko, passes=g.passes)
+            assert np.array_equal(ex["policy"], o.policy)

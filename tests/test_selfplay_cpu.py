@@ -50,3 +50,64 @@ def test_game_result():
     assert game_result(b) == 1
     full = (1 + (np.add.outer(np.arange(15), 2 * np.arange(15)) % 4 >= 2)).astype(np.int8)
     assert game_result(full) == 0
+
+
+def _uniform_legal_search(sp, game):
+    def search(inputs):
+        live = [p for p, r in zip(sp.positions, sp.records) if not r.finished]
+        out = []
+        for p in live:
+            if game == "go":
+                v = p.legal_mask().astype(np.int64)
+            else:
+                v = np.zeros(4672, np.int64)
+                for m in p.legal_moves():
+                    v[p.move_to_action(m)] = 1
+            out.append(v)
+        return np.stack(out)
+    return search
+
+
+def test_go_selfplay_plays_legal_games_and_scores_them():
+    from omoknuni_quantum_b200.selfplay import BatchedSelfPlay
+    sp = BatchedSelfPlay(3, game="go", board_size=7, seed=4)
+    sp._search = _uniform_legal_search(sp, "go")
+    recs = sp.play(120)
+    assert len(recs) == 3
+    for r in recs:
+        assert len(r.moves) == len(r.examples) > 0
+        assert all(ex["state"].shape == (8, 7, 7) and ex["policy"].shape == (50,) for ex in r.examples)
+        assert [ex["player"] for ex in r.examples[:4]] == [1, 2, 1, 2]
+        if r.finished:
+            assert r.moves[-1] == 49 and r.moves[-2] == 49      # two passes end the game
+            assert r.winner in (1, -1, 0)
+    ex = sp.examples()
+    assert len(ex) == sum(len(r.examples) for r in recs)
+
+
+def test_go_area_score():
+    from omoknuni_quantum_b200.go import GoPosition
+    g = GoPosition(5, komi=0.5)
+    g.board[:, 1] = 1                     # black wall: column 0 is black territory
+    g.board[:, 3] = 2                     # white wall: column 4 is white territory, column 2 neutral
+    assert g.score() == (10.0, 10.5)
+    g.play(g.pass_action)
+    g.play(g.pass_action)
+    assert g.result() == 2
+
+
+def test_chess_selfplay_plays_legal_games():
+    from omoknuni_quantum_b200.selfplay import BatchedSelfPlay
+    sp = BatchedSelfPlay(2, game="chess", seed=1, temperature_threshold=100)
+    sp._search = _uniform_legal_search(sp, "chess")
+    recs = sp.play(40)
+    for r in recs:
+        assert len(r.moves) == len(r.examples) > 0
+        assert r.examples[0]["policy"].shape == (4672,) and r.examples[0]["player"] == 1
+    # replaying the recorded actions from the start reproduces the final positions
+    from omoknuni_quantum_b200.chess import ChessPosition
+    for g, r in enumerate(recs):
+        p = ChessPosition()
+        for a in r.moves:
+            p.play(p.action_to_move(a))
+        assert p.fen() == sp.positions[g].fen()
