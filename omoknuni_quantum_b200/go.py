@@ -1,11 +1,15 @@
 """Host-side Go position: root construction and move application between searches.
 
 The rules are those the device engine searches with - the reference's GoState with Chinese rules
-and positional superko off (src/games/go/go_state.cpp:227-420, go_rules.cpp:34-110, isTerminal
-:502-506): no play on an occupied point or on the ko point; opponent groups without liberties
-are captured; suicide is illegal; capturing exactly one stone makes its point the ko point; pass
-is always legal, clears the ko point, and two consecutive passes end the game. Actions are
-y * n + x, pass = n * n (the NN action space; GoState itself encodes pass as -1).
+(src/games/go/go_state.cpp:227-420, go_rules.cpp:34-110, isTerminal :502-506): no play on an
+occupied point or on the ko point; opponent groups without liberties are captured; suicide is
+illegal; capturing exactly one stone makes its point the ko point; pass is always legal, clears
+the ko point, and two consecutive passes end the game. With positional superko (on by default,
+as GoState's default constructor has it) a move is also refused when the position it makes -
+board after captures plus the new ko point - equals one recorded after an earlier non-pass move
+of the game (GoState::isLegalMove, go_state.cpp:359-418). Positions are keyed by 64-bit Zobrist
+hashes (``position_key``), the keys the device engine uses. Actions are y * n + x, pass = n * n
+(the NN action space; GoState itself encodes pass as -1).
 
 This is host bookkeeping for a handful of moves per search (root positions, the move a search
 chose); the search itself never calls it.
@@ -15,12 +19,52 @@ from __future__ import annotations
 import numpy as np
 
 HISTORY = 8
+_M64 = (1 << 64) - 1
+_KEY_TABLES = {}
+
+
+def _mix64(x: int) -> int:
+    """SplitMix64 finaliser (Steele, Lea & Flood 2014)."""
+    x &= _M64
+    x ^= x >> 30
+    x = (x * 0xBF58476D1CE4E5B9) & _M64
+    x ^= x >> 27
+    x = (x * 0x94D049BB133111EB) & _M64
+    x ^= x >> 31
+    return x
+
+
+def _key_tables(n: int):
+    """uint64 stone keys [n*n, 3] (colour 1, 2) and ko keys [n*n]."""
+    t = _KEY_TABLES.get(n)
+    if t is None:
+        stones = np.zeros((n * n, 3), np.uint64)
+        for c in range(n * n):
+            for col in (1, 2):
+                stones[c, col] = _mix64(0x6A09E667F3BCC909 ^ (c * 4 + col))
+        ko = np.array([_mix64(0xBB67AE8584CAA73B ^ c) for c in range(n * n)], np.uint64)
+        t = _KEY_TABLES[n] = (stones, ko)
+    return t
+
+
+def position_key(board: np.ndarray, ko: int = -1) -> int:
+    """64-bit key of (stones, ko point): XOR of mix64(0x6A09E667F3BCC909 ^ (cell * 4 + colour))
+    over the stones, and mix64(0xBB67AE8584CAA73B ^ ko) when there is a ko point."""
+    b = np.asarray(board).reshape(-1)
+    stones, kok = _key_tables(int(round(np.sqrt(b.size))))
+    idx = np.flatnonzero(b)
+    k = np.bitwise_xor.reduce(stones[idx, b[idx].astype(np.int64)]) if len(idx) else np.uint64(0)
+    if ko >= 0:
+        k = np.uint64(k) ^ kok[ko]
+    return int(k)
 
 
 class GoPosition:
-    def __init__(self, board_size: int = 19, komi: float = 7.5):
+    def __init__(self, board_size: int = 19, komi: float = 7.5, superko: bool = True):
         self.n = int(board_size)
         self.komi = float(komi)
+        self.superko = bool(superko)
+        self.keys = []  # position keys after each non-pass move (GoState::position_history_)
         self.board = np.zeros((self.n, self.n), np.int8)
         self.to_move = 1
         self.ko = -1
@@ -32,7 +76,8 @@ class GoPosition:
         return self.n * self.n
 
     def copy(self) -> "GoPosition":
-        g = GoPosition(self.n, self.komi)
+        g = GoPosition(self.n, self.komi, self.superko)
+        g.keys = list(self.keys)
         g.board = self.board.copy()
         g.to_move, g.ko, g.passes = self.to_move, self.ko, self.passes
         g.history = [h.copy() for h in self.history[-HISTORY:]]
@@ -81,6 +126,8 @@ class GoPosition:
         if captured == 0 and not self._group(b, y, x)[1]:
             return None  # suicide
         ko = last[0] * self.n + last[1] if (groups == 1 and captured == 1) else -1
+        if self.superko and self.keys and position_key(b, ko) in self.keys:
+            return None  # positional superko
         return b, ko
 
     def is_legal(self, action: int) -> bool:
@@ -99,6 +146,8 @@ class GoPosition:
         if res is None:
             raise ValueError(f"illegal Go move {action} for player {self.to_move}")
         self.board, self.ko = res
+        if action != self.pass_action:
+            self.keys.append(position_key(self.board, self.ko))
         self.passes = self.passes + 1 if action == self.pass_action else 0
         self.to_move = 3 - self.to_move
         self.history.append(self.board.copy())
@@ -148,6 +197,10 @@ class GoPosition:
             return 0
         black, white = self.score()
         return 1 if black > white else 2 if white > black else 3
+
+    def root_keys(self) -> np.ndarray:
+        """uint64 [k]: the game's position keys so far (the engine's root history for superko)."""
+        return np.array(self.keys, np.uint64)
 
     def meta(self) -> np.ndarray:
         """int32 [3]: side to move, ko point, consecutive passes (the engine's root record)."""

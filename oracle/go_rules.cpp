@@ -1,5 +1,6 @@
 // Parity oracle (TEST INFRASTRUCTURE ONLY). See go_rules.h.
 #include "go_rules.h"
+#include "synth_eval.h"
 
 #include <cstring>
 #include <vector>
@@ -70,6 +71,28 @@ void go_legal(const int8_t* b, int n, int player, int ko, uint8_t* mask) {
   mask[cells] = 1;
 }
 
+uint64_t go_key(const int8_t* b, int n, int ko) {
+  uint64_t k = 0;
+  for (int c = 0; c < n * n; ++c)
+    if (b[c]) k ^= mix64(0x6A09E667F3BCC909ull ^ (uint64_t)(c * 4 + b[c]));
+  if (ko >= 0) k ^= mix64(0xBB67AE8584CAA73Bull ^ (uint64_t)ko);
+  return k;
+}
+
+void go_legal_superko(const int8_t* b, int n, int player, int ko, const uint64_t* hist, int nhist,
+                      uint8_t* mask) {
+  go_legal(b, n, player, ko, mask);
+  std::vector<int8_t> t(n * n);
+  for (int a = 0; a < n * n; ++a) {
+    if (!mask[a]) continue;
+    int k2 = -1;
+    go_play(b, n, player, a, ko, t.data(), &k2);
+    const uint64_t key = go_key(t.data(), n, k2);
+    for (int i = 0; i < nhist; ++i)
+      if (hist[i] == key) { mask[a] = 0; break; }
+  }
+}
+
 void go_features(const int8_t* const* hist, int cells, int to_move, float* out) {
   const int opp = 3 - to_move;
   for (int k = 0; k < 8; ++k)
@@ -89,4 +112,11 @@ extern "C" int oracle_go_play(const int8_t* b, int n, int player, int action, in
 
 extern "C" void oracle_go_legal(const int8_t* b, int n, int player, int ko, uint8_t* mask) {
   oracle::go_legal(b, n, player, ko, mask);
+}
+
+extern "C" uint64_t oracle_go_key(const int8_t* b, int n, int ko) { return oracle::go_key(b, n, ko); }
+
+extern "C" void oracle_go_legal_superko(const int8_t* b, int n, int player, int ko,
+                                        const uint64_t* hist, int nhist, uint8_t* mask) {
+  oracle::go_legal_superko(b, n, player, ko, hist, nhist, mask);
 }

@@ -37,6 +37,9 @@ struct Tree {
   int game = 0, planes = oracle::kPlanes;
   std::vector<int32_t> ko, passes;
   std::vector<int8_t> root_hist;
+  // Go positional superko: the game's keys before the root, and each node's key (board + ko)
+  int superko = 0;
+  std::vector<uint64_t> root_keys, node_key;
   // Chess (game == 2): a position record per node, the game's positions before the root (most
   // recent first) for the history planes and the repetition count.
   std::vector<oracle_chess_pos> cpos, prior;
@@ -143,7 +146,15 @@ struct Tree {
         for (auto& x : am) { legal.push_back(x.first); chess_moves.push_back(x.second); }
       } else if (game == 1) {
         std::vector<uint8_t> m(actions);
-        oracle::go_legal(b, size, player[n], ko[n], m.data());
+        if (superko) {
+          // keys of the game so far: before the root, then every non-pass position on the path
+          std::vector<uint64_t> h(root_keys);
+          for (int a = n; a > 0; a = parent[a])
+            if (action[a] != cells) h.push_back(node_key[a]);
+          oracle::go_legal_superko(b, size, player[n], ko[n], h.data(), (int)h.size(), m.data());
+        } else {
+          oracle::go_legal(b, size, player[n], ko[n], m.data());
+        }
         for (int a = 0; a < actions; ++a)
           if (m[a]) legal.push_back(a);
       } else {
@@ -186,6 +197,7 @@ struct Tree {
           int k2 = -1;
           oracle::go_play(b, size, player[n], a, ko[n], &boards[(size_t)c * cells], &k2);
           ko[c] = k2;
+          if (superko) node_key[c] = oracle::go_key(&boards[(size_t)c * cells], size, k2);
           passes[c] = a == cells ? passes[n] + 1 : 0;
           terminal[c] = passes[c] >= 2 ? 1 : 0;  // GoState::isTerminal (go_state.cpp:502-506)
           continue;
@@ -201,8 +213,12 @@ struct Tree {
   // Go root: hist[8][cells] (hist[0] = the root position, hist[k] = k plies earlier, zeros where
   // the game had not started), side to move, ko point (-1 none), consecutive passes.
   int begin_go(const oracle_config* c, const int8_t* hist, int to_move, int root_ko,
-               int root_passes, oracle_eval_fn e, void* x) {
+               int root_passes, oracle_eval_fn e, void* x, const uint64_t* keys = nullptr,
+               int nkeys = 0, int sk = 0) {
     game = 1;
+    superko = sk;
+    root_keys.assign(keys, keys + (keys && nkeys > 0 ? nkeys : 0));
+    if (superko) node_key.assign(cap, 0);
     planes = oracle::kGoPlanes;
     actions = cells + 1;
     root_hist.assign(hist, hist + (size_t)8 * cells);
@@ -432,6 +448,12 @@ int oracle_begin_go(void* t, const oracle_config* cfg, const int8_t* hist, int t
 }
 
 static int run_waves(Tree* tr, const oracle_config* cfg, int st, void* t, oracle_result* out);
+
+int oracle_begin_go_sk(void* t, const oracle_config* cfg, const int8_t* hist, int to_move, int ko,
+                       int passes, const uint64_t* keys, int nkeys, int superko, oracle_eval_fn e,
+                       void* x) {
+  return static_cast<Tree*>(t)->begin_go(cfg, hist, to_move, ko, passes, e, x, keys, nkeys, superko);
+}
 
 int oracle_search_go(void* t, const oracle_config* cfg, const int8_t* hist, int to_move, int ko,
                      int passes, oracle_eval_fn e, void* x, oracle_result* out) {

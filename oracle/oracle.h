@@ -66,6 +66,12 @@ int oracle_set_root_noise(void* tree, float eps, float keep, const float* noise_
 // Children are the rules' legal moves; a child whose pass makes two in a row is terminal.
 int oracle_begin_go(void* tree, const oracle_config* cfg, const int8_t* hist, int to_move, int ko,
                     int passes, oracle_eval_fn eval, void* ctx);
+// With positional superko (superko != 0): keys[0..nkeys) are the game's position keys recorded
+// after each non-pass move before the root (go_rules.h go_key); inside the tree every position
+// reached by a non-pass move is added along its path.
+int oracle_begin_go_sk(void* tree, const oracle_config* cfg, const int8_t* hist, int to_move, int ko,
+                       int passes, const uint64_t* keys, int nkeys, int superko,
+                       oracle_eval_fn eval, void* ctx);
 int oracle_search_go(void* tree, const oracle_config* cfg, const int8_t* hist, int to_move, int ko,
                      int passes, oracle_eval_fn eval, void* ctx, oracle_result* out);
 // Chess root (chess_rules.h): the root record (reps = occurrences so far, itself included) and

@@ -187,6 +187,13 @@ def lib():
         L.oracle_chess_action.argtypes = [ctypes.c_void_p, ctypes.c_int32]
         L.oracle_chess_move.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.oracle_chess_features.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        L.oracle_go_key.restype = ctypes.c_uint64
+        L.oracle_go_key.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
+        L.oracle_go_legal_superko.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+        L.oracle_begin_go_sk.argtypes = [ctypes.c_void_p, ctypes.POINTER(OracleConfig), ctypes.c_void_p,
+                                         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                         ctypes.c_int, ctypes.c_int, EVAL_FN, ctypes.c_void_p]
         L.oracle_go_play.restype = ctypes.c_int
         L.oracle_go_play.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                      ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]
@@ -255,6 +262,26 @@ def go_play(board: np.ndarray, player: int, action: int, ko: int = -1):
     ok = lib().oracle_go_play(b.ctypes.data, n, int(player), int(action), int(ko), out.ctypes.data,
                               ctypes.byref(k))
     return (out, k.value) if ok else None
+
+
+def go_key(board: np.ndarray, ko: int = -1) -> int:
+    """64-bit position key (stones + ko point) used by the superko rule."""
+    b = np.ascontiguousarray(board, np.int8)
+    return int(lib().oracle_go_key(b.ctypes.data, b.shape[-1], int(ko)))
+
+
+def go_legal_superko(board: np.ndarray, player: int, ko: int, hist_keys) -> np.ndarray:
+    b = np.ascontiguousarray(board, np.int8)
+    n = b.shape[-1]
+    h = np.ascontiguousarray(np.asarray(list(hist_keys), dtype=np.uint64).reshape(-1))
+    if h.size == 0:
+        h = np.zeros(1, np.uint64)
+        nh = 0
+    else:
+        nh = h.size
+    m = np.zeros(n * n + 1, np.uint8)
+    lib().oracle_go_legal_superko(b.ctypes.data, n, int(player), int(ko), h.ctypes.data, nh, m.ctypes.data)
+    return m.astype(bool)
 
 
 def go_legal(board: np.ndarray, player: int, ko: int = -1) -> np.ndarray:
@@ -370,24 +397,30 @@ class Oracle:
         return OracleConfig(self.board_size, sims, wave, c_puct, virtual_loss, int(enable_vl),
                             self.max_nodes, max_depth)
 
-    def begin_go(self, hist, to_move, cfg: OracleConfig, ko=-1, passes=0, evaluator=None) -> int:
+    def begin_go(self, hist, to_move, cfg: OracleConfig, ko=-1, passes=0, evaluator=None,
+                 superko=True, keys=()) -> int:
         """Go root: ``hist`` int8 [8, n, n] (hist[0] = the root position, hist[k] k plies
-        earlier); a single [n, n] board means no earlier positions."""
+        earlier); a single [n, n] board means no earlier positions. With ``superko`` the moves that
+        recreate a position key of ``keys`` (the game before the root) or of the path are
+        refused."""
         self.game = "go"
         h = _go_hist(hist, self.board_size)
         self._cb = self._make_cb(evaluator)
-        self._board = h
-        return self._L.oracle_begin_go(self._t, ctypes.byref(cfg), h.ctypes.data, int(to_move),
-                                       int(ko), int(passes), self._cb, None)
+        k = np.ascontiguousarray(np.asarray(list(keys), dtype=np.uint64).reshape(-1))
+        self._board = (h, k)
+        return self._L.oracle_begin_go_sk(self._t, ctypes.byref(cfg), h.ctypes.data, int(to_move),
+                                          int(ko), int(passes), k.ctypes.data if k.size else None,
+                                          int(k.size), int(bool(superko)), self._cb, None)
 
-    def search_go(self, hist, to_move, sims, wave, ko=-1, passes=0, evaluator=None, **kw) -> OracleTree:
-        self.game = "go"
+    def search_go(self, hist, to_move, sims, wave, ko=-1, passes=0, evaluator=None, superko=True,
+                  keys=(), **kw) -> OracleTree:
         cfg = self.config(sims, wave, **kw)
-        h = _go_hist(hist, self.board_size)
-        self._cb = self._make_cb(evaluator)
-        res = OracleResult()
-        self._L.oracle_search_go(self._t, ctypes.byref(cfg), h.ctypes.data, int(to_move), int(ko),
-                                 int(passes), self._cb, None, ctypes.byref(res))
+        st = self.begin_go(hist, to_move, cfg, ko, passes, evaluator, superko, keys)
+        done = 0
+        while st == 0 and done < sims:
+            w = min(wave, sims - done)
+            st = self._L.oracle_wave(self._t, w)
+            done += w
         return self.export()
 
     def begin_chess(self, root, cfg: OracleConfig, prior=(), evaluator=None) -> int:

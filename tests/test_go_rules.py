@@ -103,3 +103,44 @@ def test_oracle_go_search_invariants(oracle_lib):
     for c in pass_nodes:
         p = t.parent[c]
         assert bool(t.terminal[c]) == (p > 0 and t.action[p] == 81)
+
+
+SUPERKO = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "go_superko.npz")
+
+
+def _superko_games():
+    g = np.load(SUPERKO)
+    for i in range(int(g["games"])):
+        n = int(g[f"g{i}_n"])
+        yield (n, g[f"g{i}_boards"], g[f"g{i}_players"],
+               np.unpackbits(g[f"g{i}_legal"], axis=1)[:, : n * n + 1].astype(bool), g[f"g{i}_moves"])
+
+
+def test_go_superko_oracle_replays_reference_games(oracle_lib):
+    """GoState with enforce_superko (the reference default): the oracle's legality with the game's
+    position keys equals is_legal_move at every ply, including the double-ko refusal."""
+    refused = 0
+    for n, boards, players, legal, moves in _superko_games():
+        ko, keys = -1, []
+        for t in range(len(moves)):
+            m = oracle_lib.go_legal_superko(boards[t], players[t], ko, keys)
+            assert np.array_equal(m, legal[t]), (n, t)
+            refused += int((oracle_lib.go_legal(boards[t], players[t], ko) & ~m).sum())
+            nb, ko = oracle_lib.go_play(boards[t], players[t], int(moves[t]), ko)
+            if moves[t] != n * n:
+                keys.append(oracle_lib.go_key(nb, ko))
+    assert refused >= 1
+
+
+def test_go_superko_host_position_replays_reference_games(oracle_lib):
+    from omoknuni_quantum_b200.go import GoPosition, position_key
+    for n, boards, players, legal, moves in _superko_games():
+        g = GoPosition(n)
+        for t in range(len(moves)):
+            assert np.array_equal(g.board, boards[t])
+            if t % 5 == 0 or (n == 9 and 18 <= t <= 22):
+                assert np.array_equal(g.legal_mask(), legal[t]), (n, t)
+            g.play(int(moves[t]))
+    # the host keys are the oracle's keys
+    b = boards[-1]
+    assert position_key(b, 5) == oracle_lib.go_key(b, 5) and position_key(b) == oracle_lib.go_key(b, -1)
