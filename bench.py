@@ -563,6 +563,7 @@ def run_b200_go(args, game="go"):
         positions_host = [gomod.random_position(args.seed * 1_000_003 + first + i, 60, 19) for i in range(R)]
         hist = torch.from_numpy(np.stack([g.history_planes() for g in positions_host])).to(dev)
         meta = torch.from_numpy(np.stack([g.meta() for g in positions_host])).to(dev)
+    keys = None if chess else [g.root_keys() for g in positions_host]
     ev = ResNetEvaluator(sd, board_size=n_board, max_batch=R * args.wave, device=dev)
     eng = WaveEngine(R, board_size=n_board, capacity=args.capacity, max_wave_size=args.wave, c_puct=1.4,
                      virtual_loss=1.0, device=dev, game=game)
@@ -574,7 +575,7 @@ def run_b200_go(args, game="go"):
         torch.cuda.synchronize()
 
     for _ in range(args.warmup):
-        eng.search(hist, args.sims, evaluator=ev, meta=meta)
+        eng.search(hist, args.sims, evaluator=ev, meta=meta, keys=keys)
     barrier()
     ev.profile(1 << 14)
     launches0 = _lib.kernel_launches()
@@ -583,7 +584,7 @@ def run_b200_go(args, game="go"):
         barrier()
         start.record()
         for _ in range(args.steps):
-            eng.search(hist, args.sims, evaluator=ev, meta=meta)
+            eng.search(hist, args.sims, evaluator=ev, meta=meta, keys=keys)
         end.record()
         barrier()
     launches = _lib.kernel_launches() - launches0

@@ -80,6 +80,13 @@ typedef struct {
   float dirichlet_epsilon;
   uint64_t noise_seed;
   int32_t game;             /* omq_game */
+  /* Go: positional superko (GoState::isLegalMove with enforce_superko, go_state.cpp:359-418, the
+   * reference's default): a move is refused when the position it makes - board after captures
+   * plus the new ko point - has the key of a position recorded after an earlier non-pass move of
+   * the game (the root's history keys, see omq_begin_go) or of the path from the root. Keys are
+   * 64-bit Zobrist hashes: XOR over stones of mix64(0x6A09E667F3BCC909 ^ (cell * 4 + colour)),
+   * ^ mix64(0xBB67AE8584CAA73B ^ ko) with a ko point (mix64 = the SplitMix64 finaliser). */
+  int32_t go_superko;
 } omq_engine_config;
 
 OMQ_API const char* omq_status_string(int status);
@@ -116,7 +123,11 @@ OMQ_API int omq_begin_chess(omq_engine* e, const void* d_records, const int32_t*
  * (1 black, 2 white), ko point (-1 none), consecutive passes}. Replaces MCTS._initialize_root
  * for GameType.GO (mcts.py:1495-1519), which takes the GoState. Then as omq_begin. */
 OMQ_API int omq_begin_go(omq_engine* e, const int8_t* d_history, const int32_t* d_meta,
-                         void* stream);
+                         const uint64_t* d_keys, const int32_t* d_nkeys, void* stream);
+/* d_keys uint64 [num_trees][OMQ_GO_MAX_KEYS] and d_nkeys int32 [num_trees] (both may be NULL):
+ * the position keys of each root's game so far, one per non-pass move, for superko. When a game
+ * has more, pass its most recent OMQ_GO_MAX_KEYS. */
+#define OMQ_GO_MAX_KEYS 512
 OMQ_API int omq_root_expand(omq_engine* e, void* stream);
 
 /* One wave of `wave_size` simulations in every tree (wave_search.py:555-615), in phases:
@@ -165,6 +176,7 @@ OMQ_API int omq_search_synthetic_chess(omq_engine* e, const void* d_records, con
                                        int32_t num_simulations, void* stream);
 /* The same for Go engines, with the roots of omq_begin_go. */
 OMQ_API int omq_search_synthetic_go(omq_engine* e, const int8_t* d_history, const int32_t* d_meta,
+                                    const uint64_t* d_keys, const int32_t* d_nkeys,
                                     int32_t num_simulations, void* stream);
 
 /* Root statistics: visit counts of the root's children scattered by action,

@@ -41,9 +41,10 @@ class EngineConfig(ctypes.Structure):
                 ("virtual_loss", ctypes.c_float), ("enable_virtual_loss", ctypes.c_int32),
                 ("device", ctypes.c_int32), ("dirichlet_alpha", ctypes.c_float),
                 ("dirichlet_epsilon", ctypes.c_float), ("noise_seed", ctypes.c_uint64),
-                ("game", ctypes.c_int32)]
+                ("game", ctypes.c_int32), ("go_superko", ctypes.c_int32)]
 
 
+GO_MAX_KEYS = 512   # OMQ_GO_MAX_KEYS
 GAME_GOMOKU = 0
 GAME_GO = 1
 GAME_CHESS = 2
@@ -69,7 +70,7 @@ SIGNATURES = {
     "omq_engine_destroy": [_P],
     "omq_engine_memory": [_P, ctypes.POINTER(ctypes.c_uint64)],
     "omq_begin": [_P, _P, _P],
-    "omq_begin_go": [_P, _P, _P, _P],
+    "omq_begin_go": [_P, _P, _P, _P, _P, _P],
     "omq_begin_chess": [_P, _P, _P, _P],
     "omq_root_expand": [_P, _P],
     "omq_wave_select": [_P, _I, _P],
@@ -81,7 +82,7 @@ SIGNATURES = {
     "omq_queue_features": [_P, _I, _P, _P],
     "omq_queue_eval_synthetic": [_P, _I, _P],
     "omq_search_synthetic": [_P, _P, _I, _P],
-    "omq_search_synthetic_go": [_P, _P, _P, _I, _P],
+    "omq_search_synthetic_go": [_P, _P, _P, _P, _P, _I, _P],
     "omq_search_synthetic_chess": [_P, _P, _P, _I, _P],
     "omq_root_visits": [_P, _P, _P, _P],
     "omq_tree_status": [_P, _P, _P, _P],

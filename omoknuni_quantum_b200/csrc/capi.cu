@@ -101,8 +101,9 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   v.noise_eps = c.dirichlet_epsilon > 0 ? c.dirichlet_epsilon : 0.0f;
   v.noise_keep = (float)(1.0 - (double)v.noise_eps);
   v.noise_seed = c.noise_seed;
+  v.go_superko = (c.game == OMQ_GAME_GO && c.go_superko) ? 1 : 0;
   const size_t R = v.R, T = v.T, W = v.WCAP, QC = R * W;
-  size_t off[32], n = 0, tot = 0;
+  size_t off[40], n = 0, tot = 0;
   auto take = [&](size_t bytes) { off[n++] = tot; tot += align256(bytes); };
   take(R * T * sizeof(NodeStats));            // 0 stats
   take(R * T * sizeof(NodeTopo));             // 1 topo
@@ -125,6 +126,8 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   take(c.game == OMQ_GAME_GO ? R * W * 16 * sizeof(uint32_t)
        : chess ? R * W * 148 * sizeof(uint32_t) : 16);                    // 17 per-leaf legal masks
   take(chess ? R * 100 * sizeof(uint64_t) : 16);                          // 18 chess prior hashes
+  take(c.game == OMQ_GAME_GO ? R * OMQ_GO_MAX_KEYS * sizeof(uint64_t) : 16);  // 19 Go superko keys
+  take(c.game == OMQ_GAME_GO ? R * 128 * sizeof(uint32_t) : 16);              // 20 Go key filter
   void* arena = nullptr;
   cudaError_t err = cudaMalloc(&arena, tot);
   if (err != cudaSuccess) {
@@ -151,6 +154,8 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   v.root_noise = reinterpret_cast<float*>(b + off[16]);
   v.go_mask = reinterpret_cast<uint32_t*>(b + off[17]);
   v.chess_prior_hash = reinterpret_cast<uint64_t*>(b + off[18]);
+  v.go_keys = reinterpret_cast<uint64_t*>(b + off[19]);
+  v.go_bloom = reinterpret_cast<uint32_t*>(b + off[20]);
   err = cudaMemset(v.hdr, 0, R * sizeof(TreeHeader));
   if (err == cudaSuccess) err = cudaMemset(v.q_count, 0, 2 * sizeof(int32_t));
   if (err == cudaSuccess) err = cudaMemset(v.root_noise, 0, R * (size_t)v.A * sizeof(float));
@@ -203,11 +208,13 @@ int omq_begin_chess(omq_engine* e, const void* d_records, const int32_t* d_nprio
   return OMQ_OK;
 }
 
-int omq_begin_go(omq_engine* e, const int8_t* d_history, const int32_t* d_meta, void* stream) {
+int omq_begin_go(omq_engine* e, const int8_t* d_history, const int32_t* d_meta,
+                 const uint64_t* d_keys, const int32_t* d_nkeys, void* stream) {
   if (!e || !d_history || !d_meta) { set_error("null argument"); return OMQ_BAD_ARG; }
   if (e->v.game != OMQ_GAME_GO) { set_error("omq_begin_go on a non-Go engine"); return OMQ_BAD_ARG; }
   DeviceGuard g(e->cfg.device);
-  launch_begin_go(e->v, d_history, d_meta, e->searches++, (cudaStream_t)stream);
+  launch_begin_go(e->v, d_history, d_meta, d_nkeys ? d_keys : nullptr, d_keys ? d_nkeys : nullptr,
+                  e->searches++, (cudaStream_t)stream);
   OMQ_CHECK_LAUNCH("omq_begin_go");
   e->phase = 1;
   return OMQ_OK;
@@ -342,9 +349,9 @@ int omq_search_synthetic_chess(omq_engine* e, const void* d_records, const int32
 }
 
 int omq_search_synthetic_go(omq_engine* e, const int8_t* d_history, const int32_t* d_meta,
-                            int32_t sims, void* stream) {
+                            const uint64_t* d_keys, const int32_t* d_nkeys, int32_t sims, void* stream) {
   if (!e || !d_history || !d_meta || sims < 0) { set_error("bad argument"); return OMQ_BAD_ARG; }
-  int st = omq_begin_go(e, d_history, d_meta, stream);
+  int st = omq_begin_go(e, d_history, d_meta, d_keys, d_nkeys, stream);
   if (st) return st;
   return search_synthetic_waves(e, sims, stream);
 }

@@ -25,7 +25,25 @@ constexpr int kGoMaskWords = 12;  // ceil(362 / 32): legal bits, pass at bit `ce
 struct GoScratch {
   int par[kMaxCells + 1];   // union-find parent; after analysis the group root of each stone
   int libs[kMaxCells + 1];  // distinct liberties, indexed by group root
+  unsigned long long gkey[kMaxCells + 1];  // superko: XOR of the group's stone keys, by root
 };
+
+// Superko position keys (64-bit Zobrist): stone keys mix64(0x6A09E667F3BCC909 ^ (cell*4 + colour))
+// and ko-point keys mix64(0xBB67AE8584CAA73B ^ cell).
+__device__ __forceinline__ uint64_t go_stone_key(int c, int colour) {
+  return mix64(0x6A09E667F3BCC909ull ^ (uint64_t)(c * 4 + colour));
+}
+__device__ __forceinline__ uint64_t go_ko_key(int c) { return mix64(0xBB67AE8584CAA73Bull ^ (uint64_t)c); }
+
+// Key of the stones of board b (without a ko point). Warp-collective.
+__device__ inline uint64_t warp_go_board_key(const int8_t* b, int C) {
+  const int lane = threadIdx.x & 31;
+  uint64_t k = 0;
+  for (int c = lane; c < C; c += 32)
+    if (b[c]) k ^= go_stone_key(c, b[c]);
+  for (int o = 16; o > 0; o >>= 1) k ^= __shfl_xor_sync(0xFFFFFFFFu, k, o);
+  return k;
+}
 
 __device__ __forceinline__ int go_find(volatile int* par, int x) {
   for (int it = 0; it < kMaxCells && par[x] != x; ++it) x = par[x];
@@ -54,9 +72,9 @@ __device__ __forceinline__ void go_neighbours(int c, int S, int nb[4]) {
 
 // Label the groups of board b and count their liberties. Warp-collective; on return par[c] is
 // the root of the group holding c (for stones) and libs[root] its liberty count.
-__device__ inline void warp_go_analyze(const int8_t* b, int S, GoScratch& g) {
+__device__ inline void warp_go_analyze(const int8_t* b, int S, GoScratch& g, bool keys = false) {
   const int lane = threadIdx.x & 31, C = S * S;
-  for (int c = lane; c < C; c += 32) { g.par[c] = c; g.libs[c] = 0; }
+  for (int c = lane; c < C; c += 32) { g.par[c] = c; g.libs[c] = 0; if (keys) g.gkey[c] = 0ull; }
   __syncwarp();
   for (int c = lane; c < C; c += 32) {
     const int8_t s = b[c];
@@ -69,6 +87,9 @@ __device__ inline void warp_go_analyze(const int8_t* b, int S, GoScratch& g) {
   for (int c = lane; c < C; c += 32)
     if (b[c]) g.par[c] = go_find(g.par, c);
   __syncwarp();
+  if (keys)
+    for (int c = lane; c < C; c += 32)
+      if (b[c]) atomicXor(&g.gkey[g.par[c]], (unsigned long long)go_stone_key(c, b[c]));
   for (int c = lane; c < C; c += 32) {
     if (b[c]) continue;
     int nb[4];
@@ -164,7 +185,8 @@ struct GoPos {
   int16_t acts[128];
   int8_t board[kMaxCells + 3];
   GoScratch g;
-  int ko, passes, player, depth;
+  uint64_t pkeys[128];  // superko: keys of the path's positions reached by non-pass moves
+  int ko, passes, player, depth, npk;
 };
 
 // Root history of tree r: kGoHistory boards, [0] = the root position.
@@ -175,7 +197,8 @@ __device__ __forceinline__ const int8_t* go_root_hist(const EngineView& v, int r
 // Rebuild `node` of tree r into pos (board after its move, side to move, ko, passes). When ring
 // is not null, ring[j % 8] receives the board at every depth j >= depth - 7 (the history planes).
 // Returns the depth, or -1 on a corrupted parent chain. Warp-collective.
-__device__ inline int warp_go_replay(const EngineView& v, int r, int node, GoPos& pos, int8_t* ring) {
+__device__ inline int warp_go_replay(const EngineView& v, int r, int node, GoPos& pos, int8_t* ring,
+                                     bool keys = false) {
   const int lane = threadIdx.x & 31;
   int d = 0;
   if (lane == 0) d = path_actions(v.topo + (size_t)r * v.T, node, 127, pos.acts);
@@ -188,9 +211,15 @@ __device__ inline int warp_go_replay(const EngineView& v, int r, int node, GoPos
   if (ring && d < kGoHistory)
     for (int c = lane; c < v.C; c += 32) ring[c] = root[c];
   int ko = H.root_ko, passes = H.root_passes, player = H.root_player;
+  int npk = 0;
   for (int j = 0; j < d; ++j) {
     warp_go_play(pos.board, v.S, player, pos.acts[j], pos.g, ko, passes);
     player = 3 - player;
+    if (keys && pos.acts[j] < v.C) {
+      const uint64_t k = warp_go_board_key(pos.board, v.C) ^ (ko >= 0 ? go_ko_key(ko) : 0ull);
+      if ((threadIdx.x & 31) == 0) pos.pkeys[npk] = k;
+      ++npk;
+    }
     if (ring && j + 1 >= d - (kGoHistory - 1)) {
       int8_t* dst = ring + (size_t)((j + 1) % kGoHistory) * v.C;
       for (int c = lane; c < v.C; c += 32) dst[c] = pos.board[c];
@@ -201,7 +230,70 @@ __device__ inline int warp_go_replay(const EngineView& v, int r, int node, GoPos
   pos.passes = passes;
   pos.player = player;
   pos.depth = d;
+  pos.npk = npk;
   return d;
+}
+
+// Positional superko (GoState::isLegalMove with enforce_superko, go_state.cpp:359-418): clears
+// the legal bits of moves whose resulting position (board after captures + new ko point) has the
+// key of a position of the root's game (sorted keys + 4096-bit filter) or of the path (pos.pkeys).
+// Needs warp_go_analyze(..., keys = true) on pos.board. Returns the new legal count.
+// Warp-collective.
+__device__ inline int warp_go_superko(const EngineView& v, int r, const GoPos& pos, uint32_t* mask) {
+  const int lane = threadIdx.x & 31, S = v.S, C = v.C;
+  const int8_t* b = pos.board;
+  const GoScratch& g = pos.g;
+  const int me = pos.player, opp = 3 - me;
+  const uint64_t bkey = warp_go_board_key(b, C);
+  const int nroot = v.hdr[r].root_nkeys;
+  const uint64_t* rk = v.go_keys + (size_t)r * OMQ_GO_MAX_KEYS;
+  const uint32_t* bloom = v.go_bloom + (size_t)r * 128;
+  int total = 0;
+  for (int w = 0; w * 32 <= C; ++w) {
+    const uint32_t m = mask[w];
+    const int c = w * 32 + lane;
+    bool legal = (m >> lane) & 1u;
+    if (legal && c < C) {
+      int nb[4];
+      go_neighbours(c, S, nb);
+      int cap[4];
+      int ncap = 0;
+      uint64_t k = bkey ^ go_stone_key(c, me);
+      for (int q = 0; q < 4; ++q) {
+        const int s = nb[q];
+        if (s < 0 || b[s] != opp) continue;
+        const int root = g.par[s];
+        if (g.libs[root] != 1) continue;
+        bool dup = false;
+        for (int j = 0; j < ncap; ++j) dup |= cap[j] == root;
+        if (!dup) { cap[ncap++] = root; k ^= g.gkey[root]; }
+      }
+      if (ncap == 1) {  // a captured group of one stone (no same-coloured neighbour) is the ko point
+        int snb[4];
+        go_neighbours(cap[0], S, snb);
+        bool single = true;
+        for (int q = 0; q < 4; ++q) single &= snb[q] < 0 || b[snb[q]] != opp;
+        if (single) k ^= go_ko_key(cap[0]);
+      }
+      bool seen = false;
+      for (int i = 0; i < pos.npk && !seen; ++i) seen = pos.pkeys[i] == k;
+      if (!seen && ((bloom[(k & 4095) >> 5] >> (k & 31)) & 1u)) {
+        int lo = 0, hi = nroot;  // binary search in the sorted root keys
+        for (int it = 0; it < 16 && lo < hi; ++it) {
+          const int mid = (lo + hi) >> 1;
+          if (rk[mid] < k) lo = mid + 1; else hi = mid;
+        }
+        seen = lo < nroot && rk[lo] == k;
+      }
+      legal = !seen;
+    }
+    const uint32_t nm = __ballot_sync(0xFFFFFFFFu, legal);
+    __syncwarp();
+    if (lane == 0) mask[w] = nm;
+    total += __popc(nm);
+  }
+  __syncwarp();
+  return total;
 }
 
 // Board k plies before the replayed position (k = 0..7): the ring for k <= depth, else the root

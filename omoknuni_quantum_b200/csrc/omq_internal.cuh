@@ -65,7 +65,8 @@ struct TreeHeader {
   int32_t root_ko;       // Go: ko point of the root position (-1 none)
   int32_t root_passes;   // Go: consecutive passes that led to the root position
   int32_t root_prior;    // chess: earlier game positions stored with the root
-  int32_t pad[3];
+  int32_t root_nkeys;    // Go: superko keys of the root's game (sorted in go_keys)
+  int32_t pad[2];
 };
 
 constexpr int kPlanes = 19;
@@ -88,6 +89,9 @@ struct EngineView {
   uint32_t* go_mask;     // per-leaf legal bits: Go [R][WCAP][16] (12 words + the leaf's passes),
                          // chess [R][WCAP][148]
   uint64_t* chess_prior_hash;  // chess: [R][100] placement hashes of the earlier positions
+  int go_superko;              // Go: positional superko on
+  uint64_t* go_keys;           // Go: [R][OMQ_GO_MAX_KEYS] the root game's position keys, sorted
+  uint32_t* go_bloom;          // Go: [R][128] 4096-bit filter of those keys (key & 4095)
   int max_children;      // most children a node can have (sizes the selection sort)
   TreeHeader* hdr;       // [R]
   Visit* frontier;       // [R][2][WCAP]
@@ -192,8 +196,8 @@ int cuda_status(cudaError_t e, const char* what);
 void launch_begin(const EngineView& v, const int8_t* boards, int search_id, cudaStream_t s);
 void launch_begin_chess(const EngineView& v, const void* records, const int32_t* nprior, int search_id,
                         cudaStream_t s);
-void launch_begin_go(const EngineView& v, const int8_t* history, const int32_t* meta, int search_id,
-                     cudaStream_t s);
+void launch_begin_go(const EngineView& v, const int8_t* history, const int32_t* meta,
+                     const uint64_t* keys, const int32_t* nkeys, int search_id, cudaStream_t s);
 void launch_select(const EngineView& v, int wave, cudaStream_t s);
 void launch_expand(const EngineView& v, int root_mode, cudaStream_t s);
 void launch_backup(const EngineView& v, cudaStream_t s);

@@ -176,10 +176,33 @@ __global__ void __launch_bounds__(kThreads) k_begin(EngineView v, const int8_t* 
 
 // Go roots: history boards [R][8][C] and {side to move, ko, passes} per tree. A root reached by
 // two passes is terminal and gets no children.
-__global__ void k_begin_go(EngineView v, const int8_t* hist, const int32_t* meta, int search_id) {
+__global__ void k_begin_go(EngineView v, const int8_t* hist, const int32_t* meta, const uint64_t* keys,
+                           const int32_t* nkeys, int search_id) {
   const int r = blockIdx.x, tid = threadIdx.x;
   const size_t n = (size_t)kGoHistory * v.C;
   for (size_t i = tid; i < n; i += blockDim.x) v.root_board[(size_t)r * n + i] = hist[(size_t)r * n + i];
+  // superko keys of the root's game: sorted (bitonic, padded with all-ones) plus a 4096-bit filter
+  __shared__ unsigned long long sk[OMQ_GO_MAX_KEYS];
+  __shared__ uint32_t sbloom[128];
+  const int nk = (keys && nkeys) ? min(max(nkeys[r], 0), OMQ_GO_MAX_KEYS) : 0;
+  for (int i = tid; i < OMQ_GO_MAX_KEYS; i += blockDim.x)
+    sk[i] = i < nk ? keys[(size_t)r * OMQ_GO_MAX_KEYS + i] : ~0ull;
+  for (int i = tid; i < 128; i += blockDim.x) sbloom[i] = 0u;
+  __syncthreads();
+  for (int i = tid; i < nk; i += blockDim.x) atomicOr(&sbloom[(sk[i] & 4095) >> 5], 1u << (sk[i] & 31));
+  for (int size = 2; size <= OMQ_GO_MAX_KEYS; size <<= 1)
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      __syncthreads();
+      for (int i = tid; i < OMQ_GO_MAX_KEYS / 2; i += blockDim.x) {
+        const int j = 2 * i - (i & (stride - 1)), l = j + stride;
+        const bool up = (j & size) == 0;
+        const unsigned long long a = sk[j], b = sk[l];
+        if ((a > b) == up) { sk[j] = b; sk[l] = a; }
+      }
+    }
+  __syncthreads();
+  for (int i = tid; i < OMQ_GO_MAX_KEYS; i += blockDim.x) v.go_keys[(size_t)r * OMQ_GO_MAX_KEYS + i] = sk[i];
+  for (int i = tid; i < 128; i += blockDim.x) v.go_bloom[(size_t)r * 128 + i] = sbloom[i];
   if (tid == 0) {
     TreeHeader h{};
     h.num_nodes = 1;
@@ -189,6 +212,7 @@ __global__ void k_begin_go(EngineView v, const int8_t* hist, const int32_t* meta
     h.root_player = player;
     h.root_ko = ko;
     h.root_passes = passes;
+    h.root_nkeys = nk;
     h.nleaves = 1;
     h.exp_off = r;
     h.exp_cnt = 1;
@@ -542,12 +566,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
     for (int i = warp; i < nleaf; i += (int)(blockDim.x >> 5)) {
       int n = 0;
       if (lf[i].y >= 0 && !(topo_flags(v.topo[base + leaves[i].node]) & kFlagTerminal)) {
-        const int d = warp_go_replay(v, r, leaves[i].node, gp, nullptr);
+        const int d = warp_go_replay(v, r, leaves[i].node, gp, nullptr, v.go_superko != 0);
         if (d < 0) { if (lane == 0) H->status = OMQ_BAD_ARG; n = 0; }
         else {
           uint32_t* m = v.go_mask + ((size_t)r * v.WCAP + i) * 16;
-          warp_go_analyze(gp.board, v.S, gp.g);
+          warp_go_analyze(gp.board, v.S, gp.g, v.go_superko != 0);
           n = warp_go_legal(gp.board, v.S, gp.player, gp.ko, gp.g, m);
+          if (v.go_superko) n = warp_go_superko(v, r, gp, m);
           if (lane == 0) m[12] = (uint32_t)gp.passes;
         }
       }
@@ -834,10 +859,10 @@ void launch_begin_chess(const EngineView& v, const void* records, const int32_t*
   k_begin_chess<<<v.R, 256, 0, s>>>(v, reinterpret_cast<const ChessRec*>(records), nprior, search_id);
 }
 
-void launch_begin_go(const EngineView& v, const int8_t* history, const int32_t* meta, int search_id,
-                     cudaStream_t s) {
+void launch_begin_go(const EngineView& v, const int8_t* history, const int32_t* meta,
+                     const uint64_t* keys, const int32_t* nkeys, int search_id, cudaStream_t s) {
   count_launches(1);
-  k_begin_go<<<v.R, 256, 0, s>>>(v, history, meta, search_id);
+  k_begin_go<<<v.R, 256, 0, s>>>(v, history, meta, keys, nkeys, search_id);
 }
 
 void launch_select(const EngineView& v, int wave, cudaStream_t s) {
@@ -854,9 +879,11 @@ void launch_expand(const EngineView& v, int root_mode, cudaStream_t s) {
   count_launches(1);
   const size_t extra = v.game == OMQ_GAME_GO ? sizeof(GoPos)
                        : v.game == OMQ_GAME_CHESS ? sizeof(ChessWarpSmem) : 0;
-  const int sm = (int)((tree_threads(v) / 32) * (sizeof(ExpandWarpSmem) + extra));
+  // Go's per-warp scratch (board analysis with group keys) allows 16 warps per tree
+  const int threads = v.game == OMQ_GAME_GO ? min(tree_threads(v), 512) : tree_threads(v);
+  const int sm = (int)((threads / 32) * (sizeof(ExpandWarpSmem) + extra));
   cudaFuncSetAttribute(k_expand, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-  k_expand<<<v.R, tree_threads(v), sm, s>>>(v, root_mode);
+  k_expand<<<v.R, threads, sm, s>>>(v, root_mode);
 }
 
 void launch_backup(const EngineView& v, cudaStream_t s) {

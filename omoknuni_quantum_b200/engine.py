@@ -53,7 +53,7 @@ class WaveEngine:
                  max_wave_size: int = 256, c_puct: float = 1.4, virtual_loss: float = 1.0,
                  enable_virtual_loss: bool = True, max_depth: int = 100, device=None,
                  dirichlet_alpha: float = 0.3, dirichlet_epsilon: float = 0.0, noise_seed: int = 0,
-                 game: str = "gomoku"):
+                 game: str = "gomoku", go_superko: bool = True):
         if not torch.cuda.is_available():
             raise RuntimeError("WaveEngine needs a CUDA device (B200); there is no CPU fallback")
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -77,7 +77,8 @@ class WaveEngine:
                                 int(max_depth), float(c_puct), float(virtual_loss),
                                 int(bool(enable_virtual_loss)), dev.index or 0,
                                 float(dirichlet_alpha), float(dirichlet_epsilon),
-                                int(noise_seed) & 0xFFFFFFFFFFFFFFFF, _lib.GAMES[game])
+                                int(noise_seed) & 0xFFFFFFFFFFFFFFFF, _lib.GAMES[game],
+                                int(bool(go_superko)))
         self.cfg = cfg
         h = ctypes.c_void_p()
         with torch.cuda.device(dev):
@@ -159,6 +160,19 @@ class WaveEngine:
                      .reshape(n).to(self.device, torch.float32))
 
     # -- search phases -------------------------------------------------------------------------
+    def _go_keys(self, keys):
+        """Per-root superko keys (a list of uint64 arrays, or None) -> device [R, 512] + counts;
+        a game with more keys keeps its most recent 512."""
+        R = self.num_trees
+        k = torch.zeros(R, _lib.GO_MAX_KEYS, dtype=torch.int64)
+        cnt = torch.zeros(R, dtype=torch.int32)
+        if keys is not None:
+            for r, kr in enumerate(keys):
+                a = np.asarray(kr, dtype=np.uint64).reshape(-1)[-_lib.GO_MAX_KEYS:]
+                k[r, : a.size] = torch.from_numpy(a.view(np.int64))
+                cnt[r] = a.size
+        return k.to(self.device), cnt.to(self.device)
+
     def _go_roots(self, boards, meta):
         n, R = self.board_size, self.num_trees
         b = torch.as_tensor(boards).to(self.device, torch.int8)
@@ -186,7 +200,7 @@ class WaveEngine:
         m = m.to(self.device, torch.int32).reshape(R).contiguous()
         return b, m
 
-    def begin(self, boards: torch.Tensor, meta=None) -> None:
+    def begin(self, boards: torch.Tensor, meta=None, keys=None) -> None:
         if self.is_chess:
             b, m = self._chess_roots(boards, meta)
             self._boards, self._meta = b, m
@@ -195,9 +209,11 @@ class WaveEngine:
             return
         if self.is_go:
             b, m = self._go_roots(boards, meta)
-            self._boards, self._meta = b, m
+            k, kc = self._go_keys(keys)
+            self._boards, self._meta, self._keys = b, m, (k, kc)
             _lib.check(self.L.omq_begin_go(self._h, ctypes.c_void_p(b.data_ptr()),
-                                           ctypes.c_void_p(m.data_ptr()), _stream_ptr()), "omq_begin_go")
+                                           ctypes.c_void_p(m.data_ptr()), ctypes.c_void_p(k.data_ptr()),
+                                           ctypes.c_void_p(kc.data_ptr()), _stream_ptr()), "omq_begin_go")
             return
         b = boards.to(self.device, torch.int8).contiguous()
         if b.shape != (self.num_trees, self.board_size, self.board_size):
@@ -218,7 +234,7 @@ class WaveEngine:
         _lib.check(self.L.omq_wave_backup(self._h, s), "omq_wave_backup")
 
     def search(self, boards: torch.Tensor, num_simulations: int, evaluator="synthetic",
-               meta=None) -> None:
+               meta=None, keys=None) -> None:
         """begin + forced root expansion + ceil(sims / max_wave_size) waves
         (python/mcts/core/mcts.py:1020-1063). Raises on a device status (e.g. TreeFullError).
         Go engines take history boards and ``meta`` (see ``begin``)."""
@@ -232,9 +248,12 @@ class WaveEngine:
             return
         if isinstance(evaluator, str) and evaluator == "synthetic" and self.is_go:
             b, m = self._go_roots(boards, meta)
-            self._boards, self._meta = b, m
+            k, kc = self._go_keys(keys)
+            self._boards, self._meta, self._keys = b, m, (k, kc)
             _lib.check(self.L.omq_search_synthetic_go(self._h, ctypes.c_void_p(b.data_ptr()),
                                                       ctypes.c_void_p(m.data_ptr()),
+                                                      ctypes.c_void_p(k.data_ptr()),
+                                                      ctypes.c_void_p(kc.data_ptr()),
                                                       int(num_simulations), _stream_ptr()),
                        "omq_search_synthetic_go")
             return
@@ -245,7 +264,7 @@ class WaveEngine:
                                                    int(num_simulations), _stream_ptr()),
                        "omq_search_synthetic")
             return
-        self.begin(boards, meta)
+        self.begin(boards, meta, keys)
         self.root_expand(evaluator)
         done = 0
         while done < num_simulations:

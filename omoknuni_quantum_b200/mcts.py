@@ -115,25 +115,25 @@ class MCTS:
         raise TypeError("state must be a numpy/torch board [n, n] with 0 empty, 1 black, 2 white")
 
     def _go_root(self, state):
-        """(history int8 [8, n, n], meta int32 [3]) of a Go root: a GoPosition of this package,
+        """(history int8 [8, n, n], meta int32 [3], superko keys) of a Go root: a GoPosition of this package,
         an object with the reference IGameState interface (rebuilt by replaying
         get_move_history(), pass = -1, from the empty board), or a bare board (side to move by
         stone parity as mcts.py:1509-1519, no ko, no earlier positions)."""
         from .go import GoPosition
         n = self.config.board_size
         if isinstance(state, GoPosition):
-            return state.history_planes(), state.meta()
+            return state.history_planes(), state.meta(), state.root_keys()
         if hasattr(state, "get_move_history"):
             g = GoPosition(n)
             for m in state.get_move_history():
                 g.play(g.pass_action if int(m) < 0 else int(m))
-            return g.history_planes(), g.meta()
+            return g.history_planes(), g.meta(), g.root_keys()
         b = self._boards(state)
         b = b.cpu().numpy() if torch.is_tensor(b) else np.asarray(b)
         h = np.zeros((8, n, n), np.int8)
         h[0] = b
         stones = int((b != 0).sum())
-        return h, np.array([1 if stones % 2 == 0 else 2, -1, 0], np.int32)
+        return h, np.array([1 if stones % 2 == 0 else 2, -1, 0], np.int32), np.zeros(0, np.uint64)
 
     def _chess_root(self, state):
         """(records POS_DTYPE [101], earlier positions) of a chess root: a ChessPosition of this
@@ -175,7 +175,7 @@ class MCTS:
         t0 = time.perf_counter()
         hist = torch.from_numpy(np.stack([r[0] for r in roots])).to(self.device)
         meta = torch.from_numpy(np.stack([r[1] for r in roots])).to(self.device)
-        eng.search(hist, sims, self._eval, meta=meta)
+        eng.search(hist, sims, self._eval, meta=meta, keys=[r[2] for r in roots])
         visits = eng.root_visits().cpu().numpy()
         self._last_tree = (eng, 0)
         self._update_statistics(sims * R, time.perf_counter() - t0)

@@ -114,7 +114,8 @@ class _GoGame:
 
     def engine_input(self, positions):
         return (np.stack([p.history_planes() for p in positions]),
-                np.stack([p.meta() for p in positions]))
+                {"meta": np.stack([p.meta() for p in positions]),
+                 "keys": [p.root_keys() for p in positions]})
 
     def player(self, pos):
         return pos.to_move
@@ -146,7 +147,7 @@ class _ChessGame:
 
     def engine_input(self, positions):
         return (np.stack([p.root_records() for p in positions]),
-                np.array([len(p.prior) for p in positions], np.int32))
+                {"meta": np.array([len(p.prior) for p in positions], np.int32)})
 
     def player(self, pos):
         return int(pos.side)
@@ -173,7 +174,7 @@ class BatchedSelfPlay:
     ``search(inputs) -> visits [G, A] int`` runs one move's searches; by default it is a
     ``WaveEngine`` search with ``evaluator`` ("synthetic", a ResNetEvaluator, or any
     evaluate_batch object). For Gomoku ``inputs`` is the boards array [G, n, n]; for Go and chess
-    it is the pair (root records, meta) that ``WaveEngine.search`` takes. Finished games keep
+    it is the pair (root records, keyword arguments of ``WaveEngine.search``). Finished games keep
     their final position and are not searched again.
     """
 
@@ -210,7 +211,7 @@ class BatchedSelfPlay:
     def _device_search(self, inputs) -> np.ndarray:
         import torch
         from .engine import WaveEngine
-        roots, meta = inputs if isinstance(inputs, tuple) else (inputs, None)
+        roots, kw = inputs if isinstance(inputs, tuple) else (inputs, {})
         R = roots.shape[0]
         eng = self._engines.get(R)
         if eng is None:
@@ -219,7 +220,7 @@ class BatchedSelfPlay:
         if self.game.name == "gomoku":
             eng.search(torch.from_numpy(np.ascontiguousarray(roots)).to(eng.device), self.sims, self._evaluator)
         else:
-            eng.search(roots, self.sims, self._evaluator, meta=meta)
+            eng.search(roots, self.sims, self._evaluator, **kw)
         return eng.root_visits().cpu().numpy()
 
     def live(self) -> np.ndarray:

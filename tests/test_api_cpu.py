@@ -104,9 +104,10 @@ def test_mcts_go_roots_from_positions_and_move_histories():
         def get_move_history(self):
             return list(moves)
 
-    h1, m1 = m._go_root(FakeGoState())
-    h2, m2 = m._go_root(g)
+    h1, m1, k1 = m._go_root(FakeGoState())
+    h2, m2, k2 = m._go_root(g)
     assert np.array_equal(h1, h2) and np.array_equal(m1, m2)
+    assert np.array_equal(k1, k2) and len(k1) == 20      # one superko key per non-pass move
     assert m1[2] == 1                                     # one pass made
 
 

@@ -222,3 +222,46 @@ def test_go_selfplay_moves_match_oracle(oracle_lib):
             o = oracle_lib.Oracle(30000, 7).search_go(g.history_planes(), g.to_move, 64, 16,
                                                      ko=g.ko, passes=g.passes)
             assert np.array_equal(ex["policy"], o.policy)
+
+
+def _superko_root(ply):
+    """The reference double-ko game (tests/golden/go_superko.npz, game 0) replayed to `ply`."""
+    import os
+    from omoknuni_quantum_b200.go import GoPosition
+    z = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "go_superko.npz"))
+    g = GoPosition(int(z["g0_n"]))
+    for a in z["g0_moves"][:ply]:
+        g.play(int(a))
+    return g, int(z["superko_ply"])
+
+
+def test_go_superko_refusal_on_device_matches_oracle(oracle_lib):
+    """At the double-ko position the reference refuses B's ko capture (1,2): the device root has
+    no such child when the game's keys are passed, has it without them or with superko off, and
+    every tree equals the oracle's."""
+    from omoknuni_quantum_b200.engine import WaveEngine
+    g, ply = _superko_root(20)
+    assert ply == 20 and not g.is_legal(11)
+    hist, meta, keys = g.history_planes(), g.meta(), g.root_keys()
+    for superko, ks, child in ((True, keys, False), (True, None, True), (False, keys, True)):
+        eng = WaveEngine(1, board_size=9, capacity=60000, max_wave_size=32, game="go", go_superko=superko)
+        eng.search(torch.from_numpy(hist[None]).cuda(), 128, meta=torch.from_numpy(meta[None]),
+                   keys=None if ks is None else [ks])
+        t = eng.export_tree(0)
+        assert bool(((t["parent"] == 0) & (t["action"] == 11)).any()) == child
+        o = oracle_lib.Oracle(60000, 9).search_go(hist, g.to_move, 128, 32, ko=g.ko, passes=g.passes,
+                                                 superko=superko, keys=() if ks is None else ks)
+        _compare(eng, 0, o)
+
+
+def test_go_superko_random_roots_with_game_keys(oracle_lib):
+    from omoknuni_quantum_b200.engine import WaveEngine
+    from omoknuni_quantum_b200.go import random_position
+    ps = [random_position(600 + i, moves=50, board_size=9) for i in range(3)]
+    eng = WaveEngine(3, board_size=9, capacity=80000, max_wave_size=64, game="go")
+    eng.search(torch.from_numpy(np.stack([p.history_planes() for p in ps])).cuda(), 256,
+               meta=torch.from_numpy(np.stack([p.meta() for p in ps])), keys=[p.root_keys() for p in ps])
+    for r, p in enumerate(ps):
+        o = oracle_lib.Oracle(80000, 9).search_go(p.history_planes(), p.to_move, 256, 64, ko=p.ko,
+                                                 passes=p.passes, keys=p.root_keys())
+        _compare(eng, r, o)
