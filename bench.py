@@ -35,7 +35,7 @@ sys.path.insert(0, REPO)
 
 METRIC = "MCTS simulations/sec (device-timed, whole box)"
 UNIT = "simulations/s"
-WORKLOAD_GO = ("config3: Go 19x19 (captures, no suicide, simple ko, pass), 3200 sims/root, wave 512, "
+WORKLOAD_GO = ("config3: Go 19x19 (captures, no suicide, simple ko, positional superko, pass), 3200 sims/root, wave 512, "
                "1M-node trees, ResNet 20x256 bf16 on 17 history planes, 362 actions; 256 roots sharded "
                "across GPUs, searched in lockstep")
 WORKLOAD_CHESS = ("config4: chess (the reference engine's rules), 1600 sims/root, wave 256, 500k-node "

@@ -87,6 +87,12 @@ typedef struct {
    * 64-bit Zobrist hashes: XOR over stones of mix64(0x6A09E667F3BCC909 ^ (cell * 4 + colour)),
    * ^ mix64(0xBB67AE8584CAA73B ^ ko) with a ko point (mix64 = the SplitMix64 finaliser). */
   int32_t go_superko;
+  /* Go: Japanese / Korean repetition rule (GoState::makeMove, go_state.cpp:342-356; isTerminal
+   * :502-513): a position - board, ko point and side to move, key ^ mix64(0x3C6EF372FE94F82B ^
+   * side) - reached for the third time (counting every move, passes included) ends the game.
+   * With go_cycle the root keys passed to omq_begin_go are those of every move of the game.
+   * The reference turns superko off under these rules; set go_superko = 0 with go_cycle = 1. */
+  int32_t go_cycle;
 } omq_engine_config;
 
 OMQ_API const char* omq_status_string(int status);

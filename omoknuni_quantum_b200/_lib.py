@@ -41,7 +41,7 @@ class EngineConfig(ctypes.Structure):
                 ("virtual_loss", ctypes.c_float), ("enable_virtual_loss", ctypes.c_int32),
                 ("device", ctypes.c_int32), ("dirichlet_alpha", ctypes.c_float),
                 ("dirichlet_epsilon", ctypes.c_float), ("noise_seed", ctypes.c_uint64),
-                ("game", ctypes.c_int32), ("go_superko", ctypes.c_int32)]
+                ("game", ctypes.c_int32), ("go_superko", ctypes.c_int32), ("go_cycle", ctypes.c_int32)]
 
 
 GO_MAX_KEYS = 512   # OMQ_GO_MAX_KEYS

@@ -67,6 +67,10 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   if (!cfg || !out) { set_error("null argument"); return OMQ_BAD_ARG; }
   *out = nullptr;
   const omq_engine_config c = *cfg;
+  if (c.game == OMQ_GAME_GO && c.go_superko && c.go_cycle) {
+    set_error("go_superko and go_cycle are exclusive (Chinese vs Japanese / Korean rules)");
+    return OMQ_BAD_ARG;
+  }
   if (c.dirichlet_epsilon > 0 && !(c.dirichlet_alpha > 0)) {
     set_error("dirichlet_alpha must be > 0 when dirichlet_epsilon > 0");
     return OMQ_BAD_ARG;
@@ -102,6 +106,7 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   v.noise_keep = (float)(1.0 - (double)v.noise_eps);
   v.noise_seed = c.noise_seed;
   v.go_superko = (c.game == OMQ_GAME_GO && c.go_superko) ? 1 : 0;
+  v.go_cycle = (c.game == OMQ_GAME_GO && c.go_cycle) ? 1 : 0;
   const size_t R = v.R, T = v.T, W = v.WCAP, QC = R * W;
   size_t off[40], n = 0, tot = 0;
   auto take = [&](size_t bytes) { off[n++] = tot; tot += align256(bytes); };
@@ -123,7 +128,7 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   take(QC * sizeof(float));                   // 14 value final
   take(2 * sizeof(int32_t));                  // 15 counts
   take(R * (size_t)v.A * sizeof(float));      // 16 root noise
-  take(c.game == OMQ_GAME_GO ? R * W * 16 * sizeof(uint32_t)
+  take(c.game == OMQ_GAME_GO ? R * W * 32 * sizeof(uint32_t)
        : chess ? R * W * 148 * sizeof(uint32_t) : 16);                    // 17 per-leaf legal masks
   take(chess ? R * 100 * sizeof(uint64_t) : 16);                          // 18 chess prior hashes
   take(c.game == OMQ_GAME_GO ? R * OMQ_GO_MAX_KEYS * sizeof(uint64_t) : 16);  // 19 Go superko keys

@@ -34,6 +34,8 @@ __device__ __forceinline__ uint64_t go_stone_key(int c, int colour) {
   return mix64(0x6A09E667F3BCC909ull ^ (uint64_t)(c * 4 + colour));
 }
 __device__ __forceinline__ uint64_t go_ko_key(int c) { return mix64(0xBB67AE8584CAA73Bull ^ (uint64_t)c); }
+// Side-to-move key of the repetition rule's keys (Japanese / Korean).
+__device__ __forceinline__ uint64_t go_side_key(int p) { return mix64(0x3C6EF372FE94F82Bull ^ (uint64_t)p); }
 
 // Key of the stones of board b (without a ko point). Warp-collective.
 __device__ inline uint64_t warp_go_board_key(const int8_t* b, int C) {
@@ -215,8 +217,10 @@ __device__ inline int warp_go_replay(const EngineView& v, int r, int node, GoPos
   for (int j = 0; j < d; ++j) {
     warp_go_play(pos.board, v.S, player, pos.acts[j], pos.g, ko, passes);
     player = 3 - player;
-    if (keys && pos.acts[j] < v.C) {
-      const uint64_t k = warp_go_board_key(pos.board, v.C) ^ (ko >= 0 ? go_ko_key(ko) : 0ull);
+    // superko: positions after non-pass moves; repetition rule: after every move, side included
+    if (keys && (v.go_cycle || pos.acts[j] < v.C)) {
+      uint64_t k = warp_go_board_key(pos.board, v.C) ^ (ko >= 0 ? go_ko_key(ko) : 0ull);
+      if (v.go_cycle) k ^= go_side_key(player);
       if ((threadIdx.x & 31) == 0) pos.pkeys[npk] = k;
       ++npk;
     }
@@ -232,6 +236,69 @@ __device__ inline int warp_go_replay(const EngineView& v, int r, int node, GoPos
   pos.depth = d;
   pos.npk = npk;
   return d;
+}
+
+// Key of the position that candidate c (C = pass) makes: board after captures, new ko point.
+// Needs warp_go_analyze(..., keys = true). Per lane.
+__device__ inline uint64_t go_child_key(const GoPos& pos, int S, uint64_t bkey, int c) {
+  const int C = S * S;
+  if (c >= C) return bkey;  // pass: same stones, no ko point
+  const int8_t* b = pos.board;
+  const GoScratch& g = pos.g;
+  const int me = pos.player, opp = 3 - me;
+  int nb[4];
+  go_neighbours(c, S, nb);
+  int cap[4];
+  int ncap = 0;
+  uint64_t k = bkey ^ go_stone_key(c, me);
+  for (int q = 0; q < 4; ++q) {
+    const int s = nb[q];
+    if (s < 0 || b[s] != opp) continue;
+    const int root = g.par[s];
+    if (g.libs[root] != 1) continue;
+    bool dup = false;
+    for (int j = 0; j < ncap; ++j) dup |= cap[j] == root;
+    if (!dup) { cap[ncap++] = root; k ^= g.gkey[root]; }
+  }
+  if (ncap == 1) {
+    int snb[4];
+    go_neighbours(cap[0], S, snb);
+    bool single = true;
+    for (int q = 0; q < 4; ++q) single &= snb[q] < 0 || b[snb[q]] != opp;
+    if (single) k ^= go_ko_key(cap[0]);
+  }
+  return k;
+}
+
+// Japanese / Korean repetition rule: tmask bit of a legal child is set when its position
+// (board, ko point, side to move) already occurred twice - in the root's game (sorted keys with
+// repeats) plus on the path - so that reaching it ends the game. Warp-collective.
+__device__ inline void warp_go_cycle(const EngineView& v, int r, const GoPos& pos, const uint32_t* mask,
+                                     uint32_t* tmask) {
+  const int lane = threadIdx.x & 31, C = v.C;
+  const uint64_t bkey = warp_go_board_key(pos.board, C);
+  const int nroot = v.hdr[r].root_nkeys;
+  const uint64_t* rk = v.go_keys + (size_t)r * OMQ_GO_MAX_KEYS;
+  const uint64_t side = go_side_key(3 - pos.player);
+  for (int w = 0; w * 32 <= C; ++w) {
+    const int c = w * 32 + lane;
+    bool term = false;
+    if ((mask[w] >> lane) & 1u) {
+      const uint64_t k = go_child_key(pos, v.S, bkey, c) ^ side;
+      int count = 0;
+      for (int i = 0; i < pos.npk; ++i) count += pos.pkeys[i] == k;
+      int lo = 0, hi = nroot;  // first root key >= k
+      for (int it = 0; it < 16 && lo < hi; ++it) {
+        const int mid = (lo + hi) >> 1;
+        if (rk[mid] < k) lo = mid + 1; else hi = mid;
+      }
+      for (int i = lo; i < nroot && rk[i] == k && count < 2; ++i) ++count;
+      term = count >= 2;
+    }
+    const uint32_t tm = __ballot_sync(0xFFFFFFFFu, term);
+    if (lane == 0) tmask[w] = tm;
+  }
+  __syncwarp();
 }
 
 // Positional superko (GoState::isLegalMove with enforce_superko, go_state.cpp:359-418): clears

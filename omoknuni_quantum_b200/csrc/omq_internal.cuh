@@ -86,10 +86,12 @@ struct EngineView {
   NodeTopo* topo;        // [R*T]
   int8_t* root_board;    // Gomoku [R][C]; Go [R][8][C] (root position and 7 earlier ones);
                          // chess [R][1 + 100] position records (root, then earlier positions)
-  uint32_t* go_mask;     // per-leaf legal bits: Go [R][WCAP][16] (12 words + the leaf's passes),
+  uint32_t* go_mask;     // per-leaf legal bits: Go [R][WCAP][32] (12 words, the leaf's passes at 12,
+                         // 12 words of repetition-terminal child bits from 16),
                          // chess [R][WCAP][148]
   uint64_t* chess_prior_hash;  // chess: [R][100] placement hashes of the earlier positions
   int go_superko;              // Go: positional superko on
+  int go_cycle;                // Go: third repetition (board, ko, side to move) ends the game
   uint64_t* go_keys;           // Go: [R][OMQ_GO_MAX_KEYS] the root game's position keys, sorted
   uint32_t* go_bloom;          // Go: [R][128] 4096-bit filter of those keys (key & 4095)
   int max_children;      // most children a node can have (sizes the selection sort)

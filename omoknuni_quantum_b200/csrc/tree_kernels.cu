@@ -566,13 +566,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
     for (int i = warp; i < nleaf; i += (int)(blockDim.x >> 5)) {
       int n = 0;
       if (lf[i].y >= 0 && !(topo_flags(v.topo[base + leaves[i].node]) & kFlagTerminal)) {
-        const int d = warp_go_replay(v, r, leaves[i].node, gp, nullptr, v.go_superko != 0);
+        const bool keyed = v.go_superko || v.go_cycle;
+        const int d = warp_go_replay(v, r, leaves[i].node, gp, nullptr, keyed);
         if (d < 0) { if (lane == 0) H->status = OMQ_BAD_ARG; n = 0; }
         else {
-          uint32_t* m = v.go_mask + ((size_t)r * v.WCAP + i) * 16;
-          warp_go_analyze(gp.board, v.S, gp.g, v.go_superko != 0);
+          uint32_t* m = v.go_mask + ((size_t)r * v.WCAP + i) * 32;
+          warp_go_analyze(gp.board, v.S, gp.g, keyed);
           n = warp_go_legal(gp.board, v.S, gp.player, gp.ko, gp.g, m);
           if (v.go_superko) n = warp_go_superko(v, r, gp, m);
+          if (v.go_cycle) warp_go_cycle(v, r, gp, m, m + 16);
           if (lane == 0) m[12] = (uint32_t)gp.passes;
         }
       }
@@ -596,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
     const int q = lf[i].y;
     int final_node = e.node, ext = 0;
     if (q >= 0 && (go || chs)) {
-      const uint32_t* m = v.go_mask + ((size_t)r * v.WCAP + i) * (chs ? kChessMaskWords : 16);
+      const uint32_t* m = v.go_mask + ((size_t)r * v.WCAP + i) * (chs ? kChessMaskWords : 32);
       const int leaf_passes = go ? (int)m[12] : 0;
       int n = 0;
       if (!(topo_flags(v.topo[base + e.node]) & kFlagTerminal)) {
@@ -621,7 +623,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
       for (int j = lane; j < n; j += 32) {
         const int a = W.legal[j];
         const float P = __fdiv_rn(W.pv[j], denom);
-        const bool term = go && a == v.C && leaf_passes >= 1;  // second consecutive pass
+        // second consecutive pass, or (Japanese / Korean) a third repetition
+        const bool term = go && ((a == v.C && leaf_passes >= 1) ||
+                                 (v.go_cycle && ((m[16 + (a >> 5)] >> (a & 31)) & 1u)));
         const int c = start + j;
         const NodeStats st{0, 0.0f, P, 0};
         v.stats[base + c] = st;

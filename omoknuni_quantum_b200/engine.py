@@ -53,7 +53,7 @@ class WaveEngine:
                  max_wave_size: int = 256, c_puct: float = 1.4, virtual_loss: float = 1.0,
                  enable_virtual_loss: bool = True, max_depth: int = 100, device=None,
                  dirichlet_alpha: float = 0.3, dirichlet_epsilon: float = 0.0, noise_seed: int = 0,
-                 game: str = "gomoku", go_superko: bool = True):
+                 game: str = "gomoku", go_superko: bool = True, go_rules: str = "chinese"):
         if not torch.cuda.is_available():
             raise RuntimeError("WaveEngine needs a CUDA device (B200); there is no CPU fallback")
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -63,7 +63,9 @@ class WaveEngine:
         self.board_size = int(board_size)
         self.cells = self.board_size ** 2
         if game not in _lib.GAMES:
-            raise ValueError(f"unknown game {game!r} (gomoku, go)")
+            raise ValueError(f"unknown game {game!r} (gomoku, go, chess)")
+        if go_rules not in ("chinese", "japanese", "korean"):
+            raise ValueError(f"unknown Go rules {go_rules!r}")
         self.game = game
         self.is_go = game == "go"
         self.is_chess = game == "chess"
@@ -78,7 +80,8 @@ class WaveEngine:
                                 int(bool(enable_virtual_loss)), dev.index or 0,
                                 float(dirichlet_alpha), float(dirichlet_epsilon),
                                 int(noise_seed) & 0xFFFFFFFFFFFFFFFF, _lib.GAMES[game],
-                                int(bool(go_superko)))
+                                int(bool(go_superko) and go_rules == "chinese"),
+                                int(go_rules in ("japanese", "korean")))
         self.cfg = cfg
         h = ctypes.c_void_p()
         with torch.cuda.device(dev):

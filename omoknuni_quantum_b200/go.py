@@ -47,6 +47,11 @@ def _key_tables(n: int):
     return t
 
 
+def side_key(player: int) -> int:
+    """Side-to-move key of the repetition rule (Japanese / Korean): mix64(0x3C6EF372FE94F82B ^ p)."""
+    return _mix64(0x3C6EF372FE94F82B ^ int(player))
+
+
 def position_key(board: np.ndarray, ko: int = -1) -> int:
     """64-bit key of (stones, ko point): XOR of mix64(0x6A09E667F3BCC909 ^ (cell * 4 + colour))
     over the stones, and mix64(0xBB67AE8584CAA73B ^ ko) when there is a ko point."""
@@ -60,11 +65,24 @@ def position_key(board: np.ndarray, ko: int = -1) -> int:
 
 
 class GoPosition:
-    def __init__(self, board_size: int = 19, komi: float = 7.5, superko: bool = True):
+    def __init__(self, board_size: int = 19, komi: float = None, superko: bool = True,
+                 rules: str = "chinese"):
+        """``rules``: "chinese" (positional superko unless ``superko=False``, area scoring, komi
+        7.5), "japanese" or "korean" (no superko; a third repetition of (board, ko point, side to
+        move) ends the game - no result / draw; territory + prisoners scoring, komi 6.5),
+        as GoState(board_size, RuleSet) sets them (go_state.cpp:15-66, 342-356, 516-544)."""
+        if rules not in ("chinese", "japanese", "korean"):
+            raise ValueError(f"unknown Go rules {rules!r}")
         self.n = int(board_size)
-        self.komi = float(komi)
-        self.superko = bool(superko)
-        self.keys = []  # position keys after each non-pass move (GoState::position_history_)
+        self.rules = rules
+        self.komi = float(komi) if komi is not None else (7.5 if rules == "chinese" else 6.5)
+        self.superko = bool(superko) and rules == "chinese"
+        self.cycle = rules != "chinese"
+        self.repeated = False     # a third repetition happened (Japanese / Korean)
+        self.prisoners = [0, 0, 0]  # stones captured by black [1] and by white [2]
+        # superko: keys after each non-pass move (GoState::position_history_); repetition rule:
+        # keys with the side to move after every move (position_frequency_)
+        self.keys = []
         self.board = np.zeros((self.n, self.n), np.int8)
         self.to_move = 1
         self.ko = -1
@@ -76,7 +94,9 @@ class GoPosition:
         return self.n * self.n
 
     def copy(self) -> "GoPosition":
-        g = GoPosition(self.n, self.komi, self.superko)
+        g = GoPosition.__new__(GoPosition)
+        g.n, g.rules, g.komi, g.superko, g.cycle = self.n, self.rules, self.komi, self.superko, self.cycle
+        g.repeated, g.prisoners = self.repeated, list(self.prisoners)
         g.keys = list(self.keys)
         g.board = self.board.copy()
         g.to_move, g.ko, g.passes = self.to_move, self.ko, self.passes
@@ -84,7 +104,7 @@ class GoPosition:
         return g
 
     def is_terminal(self) -> bool:
-        return self.passes >= 2
+        return self.passes >= 2 or self.repeated
 
     def _group(self, b, y, x):
         """Stones of the group at (y, x) and whether it has a liberty."""
@@ -145,11 +165,17 @@ class GoPosition:
         res = self._try(int(action))
         if res is None:
             raise ValueError(f"illegal Go move {action} for player {self.to_move}")
+        before = int((self.board == 3 - self.to_move).sum())
         self.board, self.ko = res
-        if action != self.pass_action:
+        self.prisoners[self.to_move] += before - int((self.board == 3 - self.to_move).sum())
+        if action != self.pass_action and not self.cycle:
             self.keys.append(position_key(self.board, self.ko))
         self.passes = self.passes + 1 if action == self.pass_action else 0
         self.to_move = 3 - self.to_move
+        if self.cycle and not self.repeated:
+            k = position_key(self.board, self.ko) ^ side_key(self.to_move)
+            self.keys.append(k)
+            self.repeated = self.keys.count(k) >= 3
         self.history.append(self.board.copy())
         del self.history[:-HISTORY]
 
@@ -161,13 +187,17 @@ class GoPosition:
         return h
 
     def score(self):
-        """(black, white) area scores with Chinese rules (GoRules::calculateScores /
-        getTerritoryOwnership, go_rules.cpp:211-260, 343-380): each stone counts for its colour,
-        each empty region bordered by one colour only counts for that colour, komi goes to
-        white. No stones are marked dead."""
+        """(black, white) scores (GoRules::calculateScores / getTerritoryOwnership,
+        go_rules.cpp:211-260, 343-380): each empty region bordered by one colour only counts for
+        that colour; Chinese rules add the stones on the board, Japanese / Korean the prisoners;
+        komi goes to white. No stones are marked dead."""
         b = self.board
-        black = float((b == 1).sum())
-        white = float((b == 2).sum()) + self.komi
+        if self.rules == "chinese":
+            black = float((b == 1).sum())
+            white = float((b == 2).sum()) + self.komi
+        else:
+            black = float(self.prisoners[1])
+            white = float(self.prisoners[2]) + self.komi
         seen = np.zeros_like(b, dtype=bool)
         for y in range(self.n):
             for x in range(self.n):
@@ -192,14 +222,18 @@ class GoPosition:
         return black, white
 
     def result(self) -> int:
-        """The reference's GameResult: 0 ongoing, 1 black wins, 2 white wins, 3 draw."""
+        """The reference's GameResult: 0 ongoing, 1 black wins, 2 white wins, 3 draw, 4 no result
+        (a Japanese repetition)."""
         if not self.is_terminal():
             return 0
+        if self.repeated:
+            return 4 if self.rules == "japanese" else 3
         black, white = self.score()
         return 1 if black > white else 2 if white > black else 3
 
     def root_keys(self) -> np.ndarray:
-        """uint64 [k]: the game's position keys so far (the engine's root history for superko)."""
+        """uint64 [k]: the game's position keys so far - the engine's root history for superko
+        (Chinese) or for the repetition rule (Japanese / Korean)."""
         return np.array(self.keys, np.uint64)
 
     def meta(self) -> np.ndarray:

@@ -38,7 +38,7 @@ struct Tree {
   std::vector<int32_t> ko, passes;
   std::vector<int8_t> root_hist;
   // Go positional superko: the game's keys before the root, and each node's key (board + ko)
-  int superko = 0;
+  int superko = 0, cycle = 0;
   std::vector<uint64_t> root_keys, node_key;
   // Chess (game == 2): a position record per node, the game's positions before the root (most
   // recent first) for the history planes and the repetition count.
@@ -185,6 +185,22 @@ struct Tree {
         parent[c] = n; action[c] = a; child_count[c] = 0;
         player[c] = (int8_t)(3 - player[n]);
         mc[c] = mc[n] + 1;
+        if (game == 1 && cycle) {
+          // Japanese / Korean repetition rule (go_state.cpp:342-356): the child's position
+          // (board, ko point, side to move) occurring for the third time ends the game
+          int k2 = -1;
+          oracle::go_play(b, size, player[n], a, ko[n], &boards[(size_t)c * cells], &k2);
+          const uint64_t key = oracle::go_key(&boards[(size_t)c * cells], size, k2) ^
+                               oracle::mix64(0x3C6EF372FE94F82Bull ^ (uint64_t)(3 - player[n]));
+          node_key[c] = key;
+          int count = 0;
+          for (uint64_t rk : root_keys) count += rk == key;
+          for (int p2 = n; p2 > 0; p2 = parent[p2]) count += node_key[p2] == key;
+          ko[c] = k2;
+          passes[c] = a == cells ? passes[n] + 1 : 0;
+          terminal[c] = (passes[c] >= 2 || count >= 2) ? 1 : 0;
+          continue;
+        }
         if (game == 2) {
           oracle_chess_pos q = cpos[n];
           oracle_chess_play(&q, chess_moves[j]);
@@ -214,11 +230,12 @@ struct Tree {
   // the game had not started), side to move, ko point (-1 none), consecutive passes.
   int begin_go(const oracle_config* c, const int8_t* hist, int to_move, int root_ko,
                int root_passes, oracle_eval_fn e, void* x, const uint64_t* keys = nullptr,
-               int nkeys = 0, int sk = 0) {
+               int nkeys = 0, int sk = 0, int cy = 0) {
     game = 1;
     superko = sk;
+    cycle = cy;
     root_keys.assign(keys, keys + (keys && nkeys > 0 ? nkeys : 0));
-    if (superko) node_key.assign(cap, 0);
+    if (superko || cycle) node_key.assign(cap, 0);
     planes = oracle::kGoPlanes;
     actions = cells + 1;
     root_hist.assign(hist, hist + (size_t)8 * cells);
@@ -453,6 +470,13 @@ int oracle_begin_go_sk(void* t, const oracle_config* cfg, const int8_t* hist, in
                        int passes, const uint64_t* keys, int nkeys, int superko, oracle_eval_fn e,
                        void* x) {
   return static_cast<Tree*>(t)->begin_go(cfg, hist, to_move, ko, passes, e, x, keys, nkeys, superko);
+}
+
+int oracle_begin_go_rules(void* t, const oracle_config* cfg, const int8_t* hist, int to_move, int ko,
+                          int passes, const uint64_t* keys, int nkeys, int superko, int cycle,
+                          oracle_eval_fn e, void* x) {
+  return static_cast<Tree*>(t)->begin_go(cfg, hist, to_move, ko, passes, e, x, keys, nkeys, superko,
+                                         cycle);
 }
 
 int oracle_search_go(void* t, const oracle_config* cfg, const int8_t* hist, int to_move, int ko,

@@ -72,6 +72,12 @@ int oracle_begin_go(void* tree, const oracle_config* cfg, const int8_t* hist, in
 int oracle_begin_go_sk(void* tree, const oracle_config* cfg, const int8_t* hist, int to_move, int ko,
                        int passes, const uint64_t* keys, int nkeys, int superko,
                        oracle_eval_fn eval, void* ctx);
+// With the Japanese / Korean repetition rule (cycle != 0): keys are those of every move of the
+// game (board, ko point, side to move: go_key ^ mix64(0x3C6EF372FE94F82B ^ side)); a child whose
+// position occurs for the third time (root keys + path) is terminal.
+int oracle_begin_go_rules(void* tree, const oracle_config* cfg, const int8_t* hist, int to_move,
+                          int ko, int passes, const uint64_t* keys, int nkeys, int superko,
+                          int cycle, oracle_eval_fn eval, void* ctx);
 int oracle_search_go(void* tree, const oracle_config* cfg, const int8_t* hist, int to_move, int ko,
                      int passes, oracle_eval_fn eval, void* ctx, oracle_result* out);
 // Chess root (chess_rules.h): the root record (reps = occurrences so far, itself included) and

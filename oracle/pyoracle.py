@@ -194,6 +194,9 @@ def lib():
         L.oracle_begin_go_sk.argtypes = [ctypes.c_void_p, ctypes.POINTER(OracleConfig), ctypes.c_void_p,
                                          ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                          ctypes.c_int, ctypes.c_int, EVAL_FN, ctypes.c_void_p]
+        L.oracle_begin_go_rules.argtypes = [ctypes.c_void_p, ctypes.POINTER(OracleConfig), ctypes.c_void_p,
+                                            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                            ctypes.c_int, ctypes.c_int, ctypes.c_int, EVAL_FN, ctypes.c_void_p]
         L.oracle_go_play.restype = ctypes.c_int
         L.oracle_go_play.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                      ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]
@@ -398,7 +401,7 @@ class Oracle:
                             self.max_nodes, max_depth)
 
     def begin_go(self, hist, to_move, cfg: OracleConfig, ko=-1, passes=0, evaluator=None,
-                 superko=True, keys=()) -> int:
+                 superko=True, keys=(), cycle=False) -> int:
         """Go root: ``hist`` int8 [8, n, n] (hist[0] = the root position, hist[k] k plies
         earlier); a single [n, n] board means no earlier positions. With ``superko`` the moves that
         recreate a position key of ``keys`` (the game before the root) or of the path are
@@ -408,14 +411,15 @@ class Oracle:
         self._cb = self._make_cb(evaluator)
         k = np.ascontiguousarray(np.asarray(list(keys), dtype=np.uint64).reshape(-1))
         self._board = (h, k)
-        return self._L.oracle_begin_go_sk(self._t, ctypes.byref(cfg), h.ctypes.data, int(to_move),
-                                          int(ko), int(passes), k.ctypes.data if k.size else None,
-                                          int(k.size), int(bool(superko)), self._cb, None)
+        return self._L.oracle_begin_go_rules(self._t, ctypes.byref(cfg), h.ctypes.data, int(to_move),
+                                             int(ko), int(passes), k.ctypes.data if k.size else None,
+                                             int(k.size), int(bool(superko)), int(bool(cycle)),
+                                             self._cb, None)
 
     def search_go(self, hist, to_move, sims, wave, ko=-1, passes=0, evaluator=None, superko=True,
-                  keys=(), **kw) -> OracleTree:
+                  keys=(), cycle=False, **kw) -> OracleTree:
         cfg = self.config(sims, wave, **kw)
-        st = self.begin_go(hist, to_move, cfg, ko, passes, evaluator, superko, keys)
+        st = self.begin_go(hist, to_move, cfg, ko, passes, evaluator, superko, keys, cycle)
         done = 0
         while st == 0 and done < sims:
             w = min(wave, sims - done)

@@ -144,3 +144,30 @@ def test_go_superko_host_position_replays_reference_games(oracle_lib):
     # the host keys are the oracle's keys
     b = boards[-1]
     assert position_key(b, 5) == oracle_lib.go_key(b, 5) and position_key(b) == oracle_lib.go_key(b, -1)
+
+
+RULESETS = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "go_rulesets.npz")
+
+
+def test_go_rulesets_host_position_replays_reference_games():
+    """Chinese / Japanese / Korean GoState games: legality (superko only under Chinese rules),
+    the Japanese / Korean third-repetition terminal (no result / draw) and the scored results of
+    games ended by two passes, ply by ply."""
+    from omoknuni_quantum_b200.go import GoPosition
+    z = np.load(RULESETS)
+    seen = set()
+    for i in range(int(z["games"])):
+        rules, n = str(z[f"g{i}_rules"]), int(z[f"g{i}_n"])
+        legal = np.unpackbits(z[f"g{i}_legal"], axis=1)[:, : n * n + 1].astype(bool)
+        g = GoPosition(n, rules=rules)
+        for t, mv in enumerate(z[f"g{i}_moves"]):
+            assert np.array_equal(g.board, z[f"g{i}_boards"][t]) and g.to_move == z[f"g{i}_players"][t]
+            assert g.is_terminal() == bool(z[f"g{i}_terminal"][t]), (rules, i, t)
+            assert g.result() == int(z[f"g{i}_result"][t]), (rules, i, t)
+            if t % 4 == 0 or t >= 18:
+                assert np.array_equal(g.legal_mask(), legal[t]), (rules, i, t)
+            if mv == -2:
+                seen.add((rules, g.result()))
+                break
+            g.play(int(mv))
+    assert ("japanese", 4) in seen and ("korean", 3) in seen

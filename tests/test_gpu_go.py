@@ -265,3 +265,32 @@ def test_go_superko_random_roots_with_game_keys(oracle_lib):
         o = oracle_lib.Oracle(80000, 9).search_go(p.history_planes(), p.to_move, 256, 64, ko=p.ko,
                                                  passes=p.passes, keys=p.root_keys())
         _compare(eng, r, o)
+
+
+@pytest.mark.parametrize("rules", ["japanese", "korean"])
+def test_go_repetition_terminal_on_device_matches_oracle(oracle_lib, rules):
+    """Japanese / Korean rules: one move before the cycle's third repetition, that move's child is
+    terminal on the device (root keys of every move, side to move included) and the trees equal
+    the oracle's; a root three moves earlier must find it inside the tree the same way."""
+    import os
+    from omoknuni_quantum_b200.engine import WaveEngine
+    from omoknuni_quantum_b200.go import GoPosition
+    z = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "go_rulesets.npz"))
+    gi = [i for i in range(int(z["games"])) if str(z[f"g{i}_rules"]) == rules][0]
+    moves = z[f"g{gi}_moves"]
+    last = len(moves) - 1                       # the ply where the reference reports terminal
+    for ply in (last - 1, last - 3):
+        g = GoPosition(9, rules=rules)
+        for a in moves[:ply]:
+            g.play(int(a))
+        eng = WaveEngine(1, board_size=9, capacity=60000, max_wave_size=32, game="go", go_rules=rules)
+        eng.search(torch.from_numpy(g.history_planes()[None]).cuda(), 256,
+                   meta=torch.from_numpy(g.meta()[None]), keys=[g.root_keys()])
+        o = oracle_lib.Oracle(60000, 9).search_go(g.history_planes(), g.to_move, 256, 32, ko=g.ko,
+                                                 passes=g.passes, superko=False, cycle=True,
+                                                 keys=g.root_keys())
+        _compare(eng, 0, o)
+        if ply == last - 1:
+            t = eng.export_tree(0)
+            child = np.flatnonzero((t["parent"] == 0) & (t["action"] == int(moves[ply])))
+            assert len(child) == 1 and t["terminal"][child[0]] == 1
