@@ -83,8 +83,11 @@ class MCTS:
             return 4672
         return self.config.board_size ** 2 + (1 if self.is_go else 0)
 
-    def _engine(self, num_trees: int) -> WaveEngine:
+    def _engine(self, num_trees: int, go_rules: str = "chinese") -> WaveEngine:
         eng = self._engines.get(num_trees)
+        if eng is not None and self.is_go and getattr(eng, "go_rules", "chinese") != go_rules:
+            eng.close()
+            eng = None
         if eng is None:
             if not torch.cuda.is_available():
                 raise RuntimeError("MCTS search needs a CUDA device (B200); there is no CPU fallback")
@@ -97,7 +100,9 @@ class MCTS:
                              max_depth=c.max_depth, device=self.device,
                              dirichlet_alpha=c.dirichlet_alpha, dirichlet_epsilon=c.dirichlet_epsilon,
                              noise_seed=self._noise_seed,
-                             game="go" if self.is_go else "chess" if self.is_chess else "gomoku")
+                             game="go" if self.is_go else "chess" if self.is_chess else "gomoku",
+                             go_rules=go_rules)
+            eng.go_rules = go_rules
             self._engines[num_trees] = eng
         return eng
 
@@ -171,7 +176,10 @@ class MCTS:
         R = len(roots)
         if sims == 0:
             return np.full((R, self.action_size), 1.0 / self.action_size)
-        eng = self._engine(R)
+        rules = {getattr(s, "rules", "chinese") for s in states}
+        if len(rules) != 1:
+            raise ValueError("one search batch must use one Go rule set")
+        eng = self._engine(R, rules.pop())
         t0 = time.perf_counter()
         hist = torch.from_numpy(np.stack([r[0] for r in roots])).to(self.device)
         meta = torch.from_numpy(np.stack([r[1] for r in roots])).to(self.device)
