@@ -112,12 +112,14 @@ OMQ_API int omq_engine_memory(const omq_engine* e, uint64_t* h_bytes);
  * forced expansion (mcts.py:1659-1691): evaluate OMQ_QUEUE_EXPAND, then call
  * omq_root_expand. */
 OMQ_API int omq_begin(omq_engine* e, const int8_t* d_boards, void* stream);
-/* Chess engines: reset every tree and set its root from d_records, 72-byte position records
+/* Chess engines: reset every tree and set its root from d_records, 80-byte position records
  * [num_trees][101] (record 0 = the root, records 1..100 = the game's earlier positions, most
  * recent first; layout: int8 squares[64] (rank 0 = the eighth rank; 0 empty, piece type 1..6 =
  * P N B R Q K, +8 for black), int8 side (1 white, 2 black), int8 castling bits (1 K, 2 Q, 4 k,
  * 8 q), int8 en-passant square (-1 none), int8 occurrences of the position so far, int16 halfmove
- * clock, int16 fullmove number) and d_nprior int32 [num_trees] (earlier positions present).
+ * clock, int16 fullmove number, int8 Chess960 flag, int8 original rook files [4] (white kingside,
+ * white queenside, black kingside, black queenside; 7 0 7 0 in standard chess), 3 pad bytes) and
+ * d_nprior int32 [num_trees] (earlier positions present).
  * Replaces MCTS._initialize_root for GameType.CHESS (mcts.py:1495-1519) with the rules of the
  * reference's ChessState (chess_state.cpp, chess_rules.cpp) in place of the placeholder
  * gpu_game_states.py:397-405. A node's terminal status is found when it is first expanded. */

@@ -25,9 +25,11 @@ WHITE, BLACK = 1, 2
 START_FEN = "rnbqkbnr/pppppppp/8/8/8/8/PPPPPPPP/RNBQKBNR w KQkq - 0 1"
 PRIOR = 100  # earlier positions kept for the repetition count and the history planes
 
-# position record shared with the engine (72 bytes, the layout of the engine's root records)
+# position record shared with the engine (80 bytes, the layout of the engine's root records)
 POS_DTYPE = np.dtype([("sq", np.int8, 64), ("side", np.int8), ("castle", np.int8), ("ep", np.int8),
-                      ("reps", np.int8), ("halfmove", np.int16), ("fullmove", np.int16)])
+                      ("reps", np.int8), ("halfmove", np.int16), ("fullmove", np.int16),
+                      ("c960", np.int8), ("rook_file", np.int8, 4), ("pad", np.int8, 3)])
+_KRN = ((0, 1), (0, 2), (0, 3), (0, 4), (1, 2), (1, 3), (1, 4), (2, 3), (2, 4), (3, 4))
 
 _KNIGHT = ((-2, -1), (-2, 1), (-1, -2), (-1, 2), (1, -2), (1, 2), (2, -1), (2, 1))
 _KING = ((-1, -1), (-1, 0), (-1, 1), (0, -1), (0, 1), (1, -1), (1, 0), (1, 1))
@@ -44,10 +46,42 @@ def _piece(t: int, c: int) -> int:
     return t | (8 if c == BLACK else 0)
 
 
+def chess960_fen(number: int) -> str:
+    """Start FEN of Chess960 position ``number`` (0..959) in the reference's numbering
+    (Chess960::getPermutation, src/games/chess/chess960.cpp:454-530: n % 4 picks the bishop on
+    files a/c/e/g, n / 4 % 4 the one on b/d/f/h, n / 16 % 6 the queen among the free files,
+    n / 96 the knight pair in lexicographic order, then rook, king, rook on what is left; 518 is special-cased to
+    the classical setup), the
+    castling field naming the rook files as the reference prints it."""
+    n = int(number)
+    if not 0 <= n < 960:
+        raise ValueError("Chess960 position numbers are 0..959")
+    if n == 518:   # hard-coded to the classical setup (chess960.cpp:449-453); 521 decodes to it too
+        n = 521
+    row = [""] * 8
+    row[2 * (n % 4)] = "b"        # files a, c, e, g
+    n //= 4
+    row[2 * (n % 4) + 1] = "b"    # files b, d, f, h
+    n //= 4
+    free = [f for f in range(8) if not row[f]]
+    row[free[n % 6]] = "q"
+    n //= 6
+    free = [f for f in range(8) if not row[f]]
+    for i in _KRN[n]:
+        row[free[i]] = "n"
+    free = [f for f in range(8) if not row[f]]
+    row[free[0]], row[free[1]], row[free[2]] = "r", "k", "r"
+    back = "".join(row)
+    cast = "ABCDEFGH"[free[2]] + "ABCDEFGH"[free[0]] + "abcdefgh"[free[2]] + "abcdefgh"[free[0]]
+    return f"{back}/pppppppp/8/8/8/8/PPPPPPPP/{back.upper()} w {cast} - 0 1"
+
+
 class ChessPosition:
-    def __init__(self, fen: str = START_FEN):
+    def __init__(self, fen: str = START_FEN, chess960: bool = False):
         self.sq = [0] * 64
         self.side, self.castle, self.ep, self.halfmove, self.fullmove = WHITE, 0, -1, 0, 1
+        self.c960 = bool(chess960)
+        self.rook_file = [7, 0, 7, 0]  # original rook files: white k, white q, black k, black q
         self._parse(fen)
         self.prior: list = []   # earlier positions (records), most recent first
         self.reps = 1
@@ -68,6 +102,14 @@ class ChessPosition:
             raise ValueError(f"bad FEN {fen!r}")
         self.side = BLACK if f[1] == "b" else WHITE
         self.castle = sum(b for c, b in (("K", 1), ("Q", 2), ("k", 4), ("q", 8)) if c in f[2])
+        for ch in f[2]:  # rook files (ChessState::setFromFEN, chess_state.cpp:460-487)
+            if ch.upper() in "ABCDEFGH" and ch not in "-":
+                white = ch.isupper()
+                file = "ABCDEFGH".index(ch.upper())
+                k = self._king(WHITE if white else BLACK)
+                kside = k >= 0 and file > (k & 7)
+                self.castle |= (1 if kside else 2) if white else (4 if kside else 8)
+                self.rook_file[(0 if white else 2) + (0 if kside else 1)] = file
         self.ep = -1 if f[3] == "-" else (8 - int(f[3][1])) * 8 + "abcdefgh".index(f[3][0])
         self.halfmove = int(f[4]) if len(f) > 4 else 0
         self.fullmove = int(f[5]) if len(f) > 5 else 1
@@ -87,7 +129,11 @@ class ChessPosition:
                 ch = "pnbrqk"[(p & 7) - 1]
                 row += ch if p & 8 else ch.upper()
             rows.append(row + (str(empty) if empty else ""))
-        cs = "".join(c for c, b in (("K", 1), ("Q", 2), ("k", 4), ("q", 8)) if self.castle & b) or "-"
+        if self.c960:  # the reference prints rook files in Chess960 mode
+            cs = "".join(("ABCDEFGH" if b < 4 else "abcdefgh")[self.rook_file[i]]
+                         for i, b in enumerate((1, 2, 4, 8)) if self.castle & b) or "-"
+        else:
+            cs = "".join(c for c, b in (("K", 1), ("Q", 2), ("k", 4), ("q", 8)) if self.castle & b) or "-"
         ep = "-" if self.ep < 0 else "abcdefgh"[self.ep % 8] + str(8 - self.ep // 8)
         return f"{'/'.join(rows)} {'w' if self.side == WHITE else 'b'} {cs} {ep} {self.halfmove} {self.fullmove}"
 
@@ -187,9 +233,12 @@ class ChessPosition:
                 for kingside, right in ((True, ks), (False, qs)):
                     if not right:
                         continue
-                    target = home * 8 + (6 if kingside else 2)
+                    tfile = ((k & 7) if self.c960 else 4) + (2 if kingside else -2)
+                    if not 0 <= tfile <= 7:
+                        continue  # the reference's target leaves the board here
+                    target = home * 8 + tfile
                     fr, ff, tf = k >> 3, k & 7, target & 7
-                    rook_file = 7 if kingside else 0
+                    rook_file = self.rook_file[(0 if me == WHITE else 2) + (0 if kingside else 1)]
                     rook_sq = fr * 8 + rook_file
                     if sq[rook_sq] != _piece(ROOK, me):
                         continue
@@ -226,21 +275,27 @@ class ChessPosition:
         if (piece & 7) == KING and abs((frm & 7) - (to & 7)) == 2:
             r = frm >> 3
             kingside = (to & 7) > (frm & 7)
-            rf, rt = r * 8 + (7 if kingside else 0), r * 8 + (5 if kingside else 3)
-            sq[rt], sq[rf] = sq[rf], 0
+            rfile = self.rook_file[(0 if me == WHITE else 2) + (0 if kingside else 1)]
+            tfile = ((to & 7) - 1 if kingside else (to & 7) + 1) if self.c960 else (5 if kingside else 3)
+            rf, rt = r * 8 + rfile, r * 8 + tfile
+            rook = sq[rf]
+            sq[rf] = 0
+            sq[rt] = rook
         if (piece & 7) == KING:
             self.castle &= ~(3 if me == WHITE else 12)
         if (piece & 7) == ROOK and (frm >> 3) == (7 if me == WHITE else 0):
-            if (frm & 7) == 7:
+            base = 0 if me == WHITE else 2
+            if (frm & 7) == self.rook_file[base]:
                 self.castle &= ~(1 if me == WHITE else 4)
-            elif (frm & 7) == 0:
+            elif (frm & 7) == self.rook_file[base + 1]:
                 self.castle &= ~(2 if me == WHITE else 8)
         if captured and (captured & 7) == ROOK:
             c = _color(captured)
+            base = 0 if c == WHITE else 2
             if (to >> 3) == (7 if c == WHITE else 0):
-                if (to & 7) == 7:
+                if (to & 7) == self.rook_file[base]:
                     self.castle &= ~(1 if c == WHITE else 4)
-                elif (to & 7) == 0:
+                elif (to & 7) == self.rook_file[base + 1]:
                     self.castle &= ~(2 if c == WHITE else 8)
         sq[frm], sq[to] = 0, piece
         self.side = 3 - self.side
@@ -251,6 +306,7 @@ class ChessPosition:
         c = ChessPosition.__new__(ChessPosition)
         c.sq = list(self.sq)
         c.side, c.castle, c.ep, c.halfmove, c.fullmove = self.side, self.castle, self.ep, self.halfmove, self.fullmove
+        c.c960, c.rook_file = self.c960, list(self.rook_file)
         c.prior, c.reps = self.prior, self.reps
         return c
 
@@ -303,6 +359,8 @@ class ChessPosition:
         r["sq"] = self.sq
         r["side"], r["castle"], r["ep"], r["reps"] = self.side, self.castle, self.ep, min(self.reps, 127)
         r["halfmove"], r["fullmove"] = self.halfmove, self.fullmove
+        r["c960"] = int(self.c960)
+        r["rook_file"] = self.rook_file
         return r
 
     def play(self, move: int) -> None:

@@ -113,7 +113,7 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   take(R * T * sizeof(NodeStats));            // 0 stats
   take(R * T * sizeof(NodeTopo));             // 1 topo
   const bool chess = c.game == OMQ_GAME_CHESS;
-  take(chess ? R * 101 * 72 : R * v.C * (c.game == OMQ_GAME_GO ? 8 : 1));  // 2 roots (+ history)
+  take(chess ? R * 101 * 80 : R * v.C * (c.game == OMQ_GAME_GO ? 8 : 1));  // 2 roots (+ history)
   take(R * sizeof(TreeHeader));               // 3 headers
   take(R * 2 * W * sizeof(Visit));            // 4 frontier
   take(R * (size_t)v.LOGCAP * sizeof(Visit)); // 5 visit log

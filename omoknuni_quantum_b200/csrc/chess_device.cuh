@@ -37,8 +37,11 @@ struct __align__(8) ChessRec {
   int8_t reps;     // occurrences so far, itself included
   int16_t halfmove;
   int16_t fullmove;
+  int8_t c960;          // Chess960 castling (king file +- 2, rook beside the king's target)
+  int8_t rook_file[4];  // original rook files: white kingside, white queenside, black k, black q
+  int8_t pad[3];
 };
-static_assert(sizeof(ChessRec) == 72, "chess record layout");
+static_assert(sizeof(ChessRec) == 80, "chess record layout");
 
 namespace chess {
 constexpr int P = 1, N = 2, B = 3, R = 4, Q = 5, K = 6;
@@ -115,21 +118,25 @@ __device__ inline void ch_play(ChessRec& p, int m) {
   if ((pc & 7) == K && ((from & 7) - (to & 7) == 2 || (to & 7) - (from & 7) == 2)) {
     const int r = from >> 3;
     const bool ks = (to & 7) > (from & 7);
-    const int rf = r * 8 + (ks ? 7 : 0), rt = r * 8 + (ks ? 5 : 3);
+    // chess_state.cpp:1296-1312: the rook ends beside the king's target in Chess960
+    const int rook_to = p.c960 ? (ks ? (to & 7) - 1 : (to & 7) + 1) : (ks ? 5 : 3);
+    const int rf = r * 8 + p.rook_file[(me == WHITE ? 0 : 2) + (ks ? 0 : 1)], rt = r * 8 + rook_to;
     const int8_t rook = p.sq[rf];
     p.sq[rf] = 0;
     p.sq[rt] = rook;
   }
   if ((pc & 7) == K) p.castle &= (int8_t)(me == WHITE ? ~3 : ~12);
   if ((pc & 7) == R && (from >> 3) == (me == WHITE ? 7 : 0)) {
-    if ((from & 7) == 7) p.castle &= (int8_t)~(me == WHITE ? 1 : 4);
-    else if ((from & 7) == 0) p.castle &= (int8_t)~(me == WHITE ? 2 : 8);
+    const int base = me == WHITE ? 0 : 2;
+    if ((from & 7) == p.rook_file[base]) p.castle &= (int8_t)~(me == WHITE ? 1 : 4);
+    else if ((from & 7) == p.rook_file[base + 1]) p.castle &= (int8_t)~(me == WHITE ? 2 : 8);
   }
   if (captured != 0 && (captured & 7) == R) {
     const int c = color_of(captured);
     if ((to >> 3) == (c == WHITE ? 7 : 0)) {
-      if ((to & 7) == 7) p.castle &= (int8_t)~(c == WHITE ? 1 : 4);
-      else if ((to & 7) == 0) p.castle &= (int8_t)~(c == WHITE ? 2 : 8);
+      const int base = c == WHITE ? 0 : 2;
+      if ((to & 7) == p.rook_file[base]) p.castle &= (int8_t)~(c == WHITE ? 1 : 4);
+      else if ((to & 7) == p.rook_file[base + 1]) p.castle &= (int8_t)~(c == WHITE ? 2 : 8);
     }
   }
   p.sq[from] = 0;
@@ -301,9 +308,14 @@ __device__ inline void ch_castling(const ChessRec& p, uint32_t* mask) {
   for (int side = 0; side < 2; ++side) {
     if (side == 0 ? !ks : !qs) continue;
     const bool kingside = side == 0;
-    const int target = home * 8 + (kingside ? 6 : 2);
-    const int fr = k >> 3, ff = k & 7, tf = target & 7;
-    const int rook_file = kingside ? 7 : 0, rook_sq = fr * 8 + rook_file;
+    // getCastlingSquares: king file +- 2 (e-file based in standard chess); a Chess960 king on the
+    // b- or g-file would get an off-board target in the reference and castles nowhere here
+    const int tfile = (p.c960 ? (k & 7) : 4) + (kingside ? 2 : -2);
+    if (tfile < 0 || tfile > 7) continue;
+    const int target = home * 8 + tfile;
+    const int fr = k >> 3, ff = k & 7, tf = tfile;
+    const int rook_file = p.rook_file[(me == WHITE ? 0 : 2) + (kingside ? 0 : 1)];
+    const int rook_sq = fr * 8 + rook_file;
     if (p.sq[rook_sq] != piece(R, me)) continue;
     bool ok = true;
     const int lo = ff < rook_file ? ff : rook_file, hi = ff < rook_file ? rook_file : ff;

@@ -190,13 +190,13 @@ class WaveEngine:
         return b.contiguous(), m
 
     def _chess_roots(self, records, nprior):
-        """records: POS_DTYPE [R, 101] (numpy) or uint8 [R, 101*72]; nprior int32 [R]."""
+        """records: POS_DTYPE [R, 101] (numpy) or uint8 [R, 101*80]; nprior int32 [R]."""
         R = self.num_trees
         if isinstance(records, np.ndarray) and records.dtype.names:
             records = np.ascontiguousarray(records).view(np.uint8).reshape(R, -1)
         b = torch.as_tensor(records).to(self.device, torch.uint8).reshape(R, -1).contiguous()
-        if b.shape[1] != 101 * 72:
-            raise ValueError("chess roots must be 101 position records of 72 bytes per tree")
+        if b.shape[1] != 101 * 80:
+            raise ValueError("chess roots must be 101 position records of 80 bytes per tree")
         if nprior is None:
             raise ValueError("chess roots need meta = the number of earlier positions per tree")
         m = torch.as_tensor(np.asarray(nprior, np.int32) if not torch.is_tensor(nprior) else nprior)

@@ -130,9 +130,13 @@ int pseudo_moves(const oracle_chess_pos& p, int32_t* out) {
       for (int side = 0; side < 2; ++side) {
         if (side == 0 ? !ks : !qs) continue;
         const bool kingside = side == 0;
-        const int target = home * 8 + (kingside ? 6 : 2);
-        const int fr = rank_of(k), ff = file_of(k), tf = file_of(target);
-        const int rook_file = kingside ? 7 : 0, rook_sq = fr * 8 + rook_file;
+        const int kf = p.c960 ? file_of(k) : 4;  // getCastlingSquares
+        const int tfile = kf + (kingside ? 2 : -2);
+        if (tfile < 0 || tfile > 7) continue;     // off-board target in the reference
+        const int target = home * 8 + tfile;
+        const int fr = rank_of(k), ff = file_of(k), tf = tfile;
+        const int rook_file = p.rook_file[(me == kWhite ? 0 : 2) + (kingside ? 0 : 1)];
+        const int rook_sq = fr * 8 + rook_file;
         if (p.sq[rook_sq] != make_piece(kRook, me)) continue;
         bool ok = true;
         const int lo = ff < rook_file ? ff : rook_file, hi = ff < rook_file ? rook_file : ff;
@@ -187,10 +191,12 @@ const int kQueenD[8][2] = {{-1, 0}, {-1, 1}, {0, 1}, {1, 1}, {1, 0}, {1, -1}, {0
 
 extern "C" {
 
-int oracle_chess_from_fen(const char* fen, oracle_chess_pos* out) {
+static int parse_fen(const char* fen, oracle_chess_pos* out, int c960) {
   oracle_chess_pos p;
   std::memset(&p, 0, sizeof(p));
   p.ep = -1;
+  p.c960 = (int8_t)c960;
+  p.rook_file[0] = 7; p.rook_file[1] = 0; p.rook_file[2] = 7; p.rook_file[3] = 0;
   const char* c = fen;
   int s = 0;
   for (; *c && *c != ' '; ++c) {
@@ -211,6 +217,15 @@ int oracle_chess_from_fen(const char* fen, oracle_chess_pos* out) {
     else if (*c == 'Q') p.castle |= 2;
     else if (*c == 'k') p.castle |= 4;
     else if (*c == 'q') p.castle |= 8;
+    else if ((*c >= 'A' && *c <= 'H') || (*c >= 'a' && *c <= 'h')) {
+      // a rook file (ChessState::setFromFEN, chess_state.cpp:460-487): king side if right of the king
+      const bool white = *c <= 'H';
+      const int f = white ? *c - 'A' : *c - 'a';
+      const int ksq = king_square(p, white ? kWhite : kBlack);
+      const bool kside = ksq >= 0 && f > file_of(ksq);
+      p.castle |= (int8_t)(white ? (kside ? 1 : 2) : (kside ? 4 : 8));
+      p.rook_file[(white ? 0 : 2) + (kside ? 0 : 1)] = (int8_t)f;
+    }
   }
   if (*c) ++c;
   if (*c && *c != '-') {
@@ -228,6 +243,9 @@ int oracle_chess_from_fen(const char* fen, oracle_chess_pos* out) {
   *out = p;
   return 0;
 }
+
+int oracle_chess_from_fen(const char* fen, oracle_chess_pos* out) { return parse_fen(fen, out, 0); }
+int oracle_chess_from_fen960(const char* fen, oracle_chess_pos* out) { return parse_fen(fen, out, 1); }
 
 void oracle_chess_play(oracle_chess_pos* pp, int32_t m) {
   oracle_chess_pos& p = *pp;
@@ -251,7 +269,9 @@ void oracle_chess_play(oracle_chess_pos* pp, int32_t m) {
   if (type_of(piece) == kKing && std::abs(file_of(from) - file_of(to)) == 2) {
     const int r = rank_of(from);
     const bool kingside = file_of(to) > file_of(from);
-    const int rf = r * 8 + (kingside ? 7 : 0), rt = r * 8 + (kingside ? 5 : 3);
+    const int rook_file = p.rook_file[(me == kWhite ? 0 : 2) + (kingside ? 0 : 1)];
+    const int rook_to = p.c960 ? (kingside ? file_of(to) - 1 : file_of(to) + 1) : (kingside ? 5 : 3);
+    const int rf = r * 8 + rook_file, rt = r * 8 + rook_to;
     const int8_t rook = p.sq[rf];
     p.sq[rf] = 0;
     p.sq[rt] = rook;
@@ -259,17 +279,17 @@ void oracle_chess_play(oracle_chess_pos* pp, int32_t m) {
   // ChessRules::getUpdatedCastlingRights (chess_rules.cpp:400-474)
   if (type_of(piece) == kKing) p.castle &= (int8_t)(me == kWhite ? ~3 : ~12);
   if (type_of(piece) == kRook) {
-    const int home = me == kWhite ? 7 : 0;
+    const int home = me == kWhite ? 7 : 0, base = me == kWhite ? 0 : 2;
     if (rank_of(from) == home) {
-      if (file_of(from) == 7) p.castle &= (int8_t)~(me == kWhite ? 1 : 4);
-      else if (file_of(from) == 0) p.castle &= (int8_t)~(me == kWhite ? 2 : 8);
+      if (file_of(from) == p.rook_file[base]) p.castle &= (int8_t)~(me == kWhite ? 1 : 4);
+      else if (file_of(from) == p.rook_file[base + 1]) p.castle &= (int8_t)~(me == kWhite ? 2 : 8);
     }
   }
   if (captured != 0 && type_of(captured) == kRook) {
-    const int c = color_of(captured), home = c == kWhite ? 7 : 0;
+    const int c = color_of(captured), home = c == kWhite ? 7 : 0, base = c == kWhite ? 0 : 2;
     if (rank_of(to) == home) {
-      if (file_of(to) == 7) p.castle &= (int8_t)~(c == kWhite ? 1 : 4);
-      else if (file_of(to) == 0) p.castle &= (int8_t)~(c == kWhite ? 2 : 8);
+      if (file_of(to) == p.rook_file[base]) p.castle &= (int8_t)~(c == kWhite ? 1 : 4);
+      else if (file_of(to) == p.rook_file[base + 1]) p.castle &= (int8_t)~(c == kWhite ? 2 : 8);
     }
   }
   p.sq[from] = 0;

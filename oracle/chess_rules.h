@@ -13,6 +13,11 @@
 //   * terminal (ChessState::isTerminal, :623-676): no legal move (draw unless in check), then the
 //     insufficient-material table of chess_rules.cpp:236-394, then halfmove clock >= 100, then
 //     the position's third occurrence.
+// Chess960 (the reference's chess960_ mode): castling takes the king two files towards the rook
+// (king file +- 2, chess_rules.cpp:619-680, 735-749) and puts the rook on the king's other side
+// (chess_state.cpp:1296-1312); the original rook files come from the start position. Where
+// king file +- 2 leaves the board (king on the b- or g-file) the reference computes an off-board
+// target; no such castling move is generated here.
 // Squares are rank * 8 + file with rank 0 = the eighth rank (black's back rank); white pawns move
 // towards rank 0. Moves use the reference encoding (promotion << 12) | (from << 6) | to with
 // promotion 1 queen, 2 rook, 3 bishop, 4 knight (chess_state.cpp:1474-1507).
@@ -20,7 +25,7 @@
 #include <cstdint>
 
 extern "C" {
-// Position record shared with the device engine (72 bytes).
+// Position record shared with the device engine (80 bytes).
 typedef struct {
   int8_t sq[64];     // 0 empty; piece type 1..6 (P N B R Q K), +8 for black
   int8_t side;       // 1 white, 2 black
@@ -29,9 +34,14 @@ typedef struct {
   int8_t reps;       // occurrences of this position so far, itself included (repetition planes)
   int16_t halfmove;
   int16_t fullmove;
+  int8_t c960;       // Chess960 castling (the reference's chess960_ flag)
+  int8_t rook_file[4];  // original rook files: white kingside, white queenside, black k, black q
+  int8_t pad[3];
 } oracle_chess_pos;
 
 int oracle_chess_from_fen(const char* fen, oracle_chess_pos* out);  // 0 ok
+// The same for a Chess960 game: castling letters may name rook files (Shredder FEN).
+int oracle_chess_from_fen960(const char* fen, oracle_chess_pos* out);
 // Legal moves (reference encoding) into moves[256]; returns the count.
 int oracle_chess_legal(const oracle_chess_pos* p, int32_t* moves);
 // ChessState::makeMove (chess_state.cpp:1232-1346) for a move of the reference encoding.

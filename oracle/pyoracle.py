@@ -180,6 +180,7 @@ def lib():
         L.oracle_synth_eval_go.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                            ctypes.c_void_p, ctypes.c_void_p]
         L.oracle_chess_from_fen.argtypes = [ctypes.c_char_p, ctypes.c_void_p]
+        L.oracle_chess_from_fen960.argtypes = [ctypes.c_char_p, ctypes.c_void_p]
         L.oracle_chess_legal.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         L.oracle_chess_play.argtypes = [ctypes.c_void_p, ctypes.c_int32]
         L.oracle_chess_terminal.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
@@ -207,13 +208,15 @@ def lib():
 
 
 CHESS_POS = np.dtype([("sq", np.int8, 64), ("side", np.int8), ("castle", np.int8), ("ep", np.int8),
-                      ("reps", np.int8), ("halfmove", np.int16), ("fullmove", np.int16)])
+                      ("reps", np.int8), ("halfmove", np.int16), ("fullmove", np.int16),
+                      ("c960", np.int8), ("rook_file", np.int8, 4), ("pad", np.int8, 3)])
 
 
-def chess_from_fen(fen: str) -> np.ndarray:
+def chess_from_fen(fen: str, chess960: bool = False) -> np.ndarray:
     """Oracle chess position record (chess_rules.h) from a FEN string."""
     p = np.zeros(1, CHESS_POS)
-    if lib().oracle_chess_from_fen(fen.encode(), p.ctypes.data) != 0:
+    fn = lib().oracle_chess_from_fen960 if chess960 else lib().oracle_chess_from_fen
+    if fn(fen.encode(), p.ctypes.data) != 0:
         raise ValueError(f"bad FEN {fen!r}")
     return p[0]
 

@@ -81,3 +81,50 @@ def test_chess_roots_are_seeded_and_records_match_oracle(oracle_lib):
     # the prior positions are the game's, most recent first
     q = p.copy()
     assert np.array_equal(np.asarray(r1[1, 1]["sq"]), np.asarray(q.prior[0]["sq"]))
+
+
+C960 = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "chess960.npz")
+
+
+def _games960():
+    z = np.load(C960)
+    go, off = z["game_off"], z["legal_off"]
+    for g in range(len(go) - 1):
+        yield int(z["numbers"][g]), [(str(z["fens"][i]), z["legal"][off[i]:off[i + 1]], bool(z["terminal"][i]),
+                                      int(z["result"][i]), int(z["moves"][i])) for i in range(go[g], go[g + 1])]
+
+
+def test_chess960_start_positions_follow_the_reference_numbering():
+    from omoknuni_quantum_b200.chess import chess960_fen
+    starts = np.load(C960)["starts"]
+    assert len(starts) == 960
+    for k in range(960):
+        assert chess960_fen(k) == str(starts[k]), k
+
+
+def test_chess960_oracle_and_host_replay_reference_games(oracle_lib):
+    """Chess960 games of the reference engine (kings starting on files c-f): legal moves incl.
+    castling with arbitrary rook files, rights, terminal flags and resulting FENs, ply by ply."""
+    from omoknuni_quantum_b200.chess import ChessPosition, chess960_fen
+    castles = 0
+    for number, game in _games960():
+        pos = oracle_lib.chess_from_fen(game[0][0], chess960=True)
+        host = ChessPosition(chess960_fen(number), chess960=True)
+        seen = [pos]
+        for t, (fen, legal, term, res, move) in enumerate(game):
+            assert host.fen() == fen, (number, t)
+            want = oracle_lib.chess_from_fen(fen, chess960=True)
+            assert oracle_lib.chess_same(pos, want) and pos["castle"] == want["castle"], (number, t)
+            assert np.array_equal(oracle_lib.chess_legal(pos), legal), (number, fen)
+            if t % 3 == 0 or term:
+                assert host.legal_moves() == [int(m) for m in legal], (number, fen)
+            reps = sum(oracle_lib.chess_same(pos, q) for q in seen)
+            assert oracle_lib.chess_terminal(pos, reps) == (term, res if term else 0), fen
+            if move < 0:
+                break
+            frm, to = (move >> 6) & 63, move & 63
+            castles += int((pos["sq"][frm] & 7) == 6 and abs(frm % 8 - to % 8) == 2)
+            pos = oracle_lib.chess_play(pos, move)
+            host.play(move)
+            seen.append(pos)
+    assert castles >= 10

@@ -206,3 +206,45 @@ def test_chess_selfplay_moves_match_oracle(oracle_lib):
             o = oracle_lib.Oracle(30000, 8).search_chess(p.record(), 64, 16, prior=p.prior)
             assert np.array_equal(ex["policy"], o.policy)
             p.play(p.action_to_move(r.moves[i]))
+
+
+def _castles(p):
+    return [m for m in p.legal_moves()
+            if (p.sq[(m >> 6) & 63] & 7) == 6 and abs(((m >> 6) & 7) - (m & 7)) == 2]
+
+
+def _chess960_roots(count=6):
+    """Positions of the reference's Chess960 games (tests/golden/chess960.npz) at the first ply
+    where the side to move can castle, plus two start positions; games replayed on the host."""
+    import os
+    from omoknuni_quantum_b200.chess import ChessPosition, chess960_fen
+    z = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "chess960.npz"))
+    out = [ChessPosition(chess960_fen(int(z["numbers"][0])), chess960=True),
+           ChessPosition(chess960_fen(int(z["numbers"][1])), chess960=True)]
+    go = z["game_off"]
+    for g in range(len(go) - 1):
+        p = ChessPosition(chess960_fen(int(z["numbers"][g])), chess960=True)
+        for i in range(go[g], go[g + 1]):
+            if _castles(p):
+                out.append(p.copy())
+                break
+            if int(z["moves"][i]) < 0:
+                break
+            p.play(int(z["moves"][i]))
+        if len(out) >= count:
+            break
+    return out
+
+
+def test_chess960_roots_match_oracle(oracle_lib):
+    """Chess960 castling (arbitrary king and rook files) on the device matches the oracle, which
+    replays the reference engine's Chess960 games; the castling moves are root children."""
+    ps = _chess960_roots()
+    assert len(ps) >= 5
+    eng = _run(ps, 384, 48)
+    for r, p in enumerate(ps):
+        _compare(eng, r, _oracle(oracle_lib, p, 384, 48))
+        t = eng.export_tree(r)
+        kids = set(int(a) for a, par in zip(t["action"], t["parent"]) if par == 0)
+        assert all(p.move_to_action(m) in kids for m in _castles(p))
+        assert len(kids) == len(p.legal_moves())
