@@ -52,8 +52,9 @@ typedef enum {
 
 /* Game of an engine. Gomoku: actions = n*n, 19 feature planes (the reference's basic
  * representation). Go: actions = n*n + 1 (pass last, the reference's NN action space for Go),
- * 17 feature planes; rules of GoState with Chinese rules and superko off
- * (src/games/go/go_state.cpp:227-420, 502-506). */
+ * 17 feature planes; rules of GoState (src/games/go/go_state.cpp:227-420, 502-506): Chinese
+ * rules with positional superko (go_superko), or Japanese / Korean rules (go_cycle). Chess:
+ * the rules of the reference's ChessState, standard or Chess960. */
 typedef enum {
   OMQ_GAME_GOMOKU = 0,
   OMQ_GAME_GO = 1,
@@ -61,6 +62,10 @@ typedef enum {
 } omq_game;
 
 typedef struct omq_engine omq_engine;
+
+/* omq_reroot modes. */
+#define OMQ_REROOT_CARRY 1  /* next root starts with the chosen child's visit count and value sum */
+#define OMQ_REROOT_KEEP 2   /* keep the chosen child's whole subtree */
 
 typedef struct {
   int32_t num_trees;        /* independent trees searched in lockstep (one root each) */
@@ -106,6 +111,19 @@ OMQ_API int omq_engine_create(const omq_engine_config* cfg, omq_engine** out);
 OMQ_API int omq_engine_destroy(omq_engine* e);
 /* Bytes of device memory held by the engine. */
 OMQ_API int omq_engine_memory(const omq_engine* e, uint64_t* h_bytes);
+
+/* Between searches: tree r's root child reached by the move d_actions[r] (int32 [num_trees], the
+ * engine's action space; -1 = none) becomes the root of the next search, which must begin from
+ * the position that move leads to. Replaces MCTS.update_root with subtree reuse
+ * (mcts.py:1205-1246). OMQ_REROOT_CARRY restates what the reference's use_gpu_tree_reuse path
+ * (mcts.py:1929-2005, compact_subtree.py:195-313) leaves behind: a fresh tree whose root starts
+ * with the child's visit count and value sum. OMQ_REROOT_KEEP keeps the child's subtree,
+ * renumbered breadth-first with children in action order - what CSRTree.shift_root
+ * (csr_tree.py:1020-1229) describes, which the reference never reaches (its call raises and the
+ * tree is reset); a kept root that is already expanded is not expanded again. A move that is not
+ * a root child, or a tree with an error status, gives a fresh tree. Mode KEEP allocates (once)
+ * node copies for a chunk of trees, about 1 GiB at most. */
+OMQ_API int omq_reroot(omq_engine* e, const int32_t* d_actions, int mode, void* stream);
 
 /* Reset every tree and set its root from d_boards[num_trees][n][n] (int8, 0/1/2); the side to
  * move is black when the stone count is even (mcts.py:1509-1519). Queues the roots for their

@@ -49,6 +49,8 @@ GAME_GOMOKU = 0
 GAME_GO = 1
 GAME_CHESS = 2
 GAMES = {"gomoku": GAME_GOMOKU, "go": GAME_GO, "chess": GAME_CHESS}
+REROOT_CARRY = 1    # OMQ_REROOT_CARRY
+REROOT_KEEP = 2     # OMQ_REROOT_KEEP
 
 
 class ResNetConfig(ctypes.Structure):
@@ -73,6 +75,7 @@ SIGNATURES = {
     "omq_begin_go": [_P, _P, _P, _P, _P, _P],
     "omq_begin_chess": [_P, _P, _P, _P],
     "omq_root_expand": [_P, _P],
+    "omq_reroot": [_P, _P, _I, _P],
     "omq_wave_select": [_P, _I, _P],
     "omq_wave_expand": [_P, _P],
     "omq_wave_backup": [_P, _P],

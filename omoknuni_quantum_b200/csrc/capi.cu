@@ -1,4 +1,5 @@
 // C ABI of the wave-MCTS engine (declarations and reference map in include/omq_b200.h).
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -180,6 +181,10 @@ int omq_engine_destroy(omq_engine* e) {
   if (!e) return OMQ_OK;
   DeviceGuard g(e->cfg.device);
   cudaError_t err = cudaFree(e->arena);
+  if (e->reroot_scratch) {
+    const cudaError_t e2 = cudaFree(e->reroot_scratch);
+    if (err == cudaSuccess) err = e2;
+  }
   delete e;
   return cuda_status(err, "cudaFree(engine arena)");
 }
@@ -187,6 +192,42 @@ int omq_engine_destroy(omq_engine* e) {
 int omq_engine_memory(const omq_engine* e, uint64_t* bytes) {
   if (!e || !bytes) { set_error("null argument"); return OMQ_BAD_ARG; }
   *bytes = e->bytes;
+  return OMQ_OK;
+}
+
+int omq_reroot(omq_engine* e, const int32_t* d_actions, int mode, void* stream) {
+  if (!e || !d_actions) { set_error("null argument"); return OMQ_BAD_ARG; }
+  if (mode != OMQ_REROOT_CARRY && mode != OMQ_REROOT_KEEP) {
+    set_error("omq_reroot mode %d (OMQ_REROOT_CARRY or OMQ_REROOT_KEEP)", mode);
+    return OMQ_BAD_ARG;
+  }
+  if (e->phase == 1 || e->phase == 3 || e->phase == 4) {
+    set_error("omq_reroot between searches only (a search is in progress)");
+    return OMQ_NOT_READY;
+  }
+  DeviceGuard g(e->cfg.device);
+  NodeStats* ss = nullptr;
+  NodeTopo* st = nullptr;
+  if (mode == OMQ_REROOT_KEEP) {
+    const size_t per_tree = (size_t)e->v.T * (sizeof(NodeStats) + sizeof(NodeTopo));
+    if (!e->reroot_scratch) {
+      // node copies for a chunk of trees, about 1 GiB at most (at least one tree)
+      const size_t chunk = std::max<size_t>(1, std::min<size_t>(e->v.R, (size_t(1) << 30) / per_tree));
+      void* p = nullptr;
+      const cudaError_t err = cudaMalloc(&p, chunk * per_tree);
+      if (err != cudaSuccess) return cuda_status(err, "cudaMalloc(reroot scratch)");
+      e->reroot_scratch = p;
+      e->reroot_chunk = (int32_t)chunk;
+      e->bytes += chunk * per_tree;
+    }
+    ss = static_cast<NodeStats*>(e->reroot_scratch);
+    st = reinterpret_cast<NodeTopo*>(static_cast<char*>(e->reroot_scratch) +
+                                     (size_t)e->reroot_chunk * e->v.T * sizeof(NodeStats));
+  }
+  launch_reroot(e->v, d_actions, mode, ss, st, e->reroot_chunk > 0 ? e->reroot_chunk : e->v.R,
+                (cudaStream_t)stream);
+  OMQ_CHECK_LAUNCH("omq_reroot");
+  e->phase = 0;
   return OMQ_OK;
 }
 

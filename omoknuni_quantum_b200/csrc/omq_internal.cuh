@@ -66,7 +66,12 @@ struct TreeHeader {
   int32_t root_passes;   // Go: consecutive passes that led to the root position
   int32_t root_prior;    // chess: earlier game positions stored with the root
   int32_t root_nkeys;    // Go: superko keys of the root's game (sorted in go_keys)
-  int32_t pad[2];
+  // set by omq_reroot, consumed by the next begin: 0 fresh tree; 1 fresh tree whose root starts
+  // with (carry_n, carry_w); 2 nodes [0, num_nodes) are the kept subtree of the new root
+  int32_t kept;
+  int32_t carry_n;
+  float carry_w;
+  int32_t pad;
 };
 
 constexpr int kPlanes = 19;
@@ -173,6 +178,8 @@ struct omq_engine {
   int32_t searches;      // omq_begin calls so far
   uint64_t bytes;
   void* arena;           // single device allocation backing every buffer
+  void* reroot_scratch;  // omq_reroot mode 2: node copies for reroot_chunk trees (lazy)
+  int32_t reroot_chunk;
 };
 
 namespace omq {
@@ -201,6 +208,8 @@ void launch_begin_chess(const EngineView& v, const void* records, const int32_t*
 void launch_begin_go(const EngineView& v, const int8_t* history, const int32_t* meta,
                      const uint64_t* keys, const int32_t* nkeys, int search_id, cudaStream_t s);
 void launch_select(const EngineView& v, int wave, cudaStream_t s);
+void launch_reroot(const EngineView& v, const int32_t* actions, int mode, NodeStats* scratch_stats,
+                   NodeTopo* scratch_topo, int chunk, cudaStream_t s);
 void launch_expand(const EngineView& v, int root_mode, cudaStream_t s);
 void launch_backup(const EngineView& v, cudaStream_t s);
 void launch_root_visits(const EngineView& v, int32_t* visits, float* nw, cudaStream_t s);

@@ -132,6 +132,31 @@ __device__ void warp_sort_desc(unsigned long long* keys, int p2) {
 // ---------------------------------------------------------------------------------------------
 // begin: reset trees, install roots, queue the roots for the forced root expansion
 // ---------------------------------------------------------------------------------------------
+// Header + node 0 of tree r for a new search (one thread). After omq_reroot the tree may be kept:
+// mode 2 keeps nodes [0, num_nodes) and, with the root already expanded, skips the forced root
+// expansion (the root stays queued, its evaluation unused); mode 1 starts a fresh tree whose root
+// begins with the chosen child's visit count and value sum.
+__device__ void install_root(const EngineView& v, int r, TreeHeader h, int root_flags) {
+  const TreeHeader old = v.hdr[r];
+  const size_t base = (size_t)r * v.T;
+  h.kept = 0;
+  if (old.kept == 2 && h.status == OMQ_OK) {
+    h.num_nodes = old.num_nodes;
+    h.nleaves = 0;
+    h.exp_cnt = 0;
+  } else {
+    h.num_nodes = 1;
+    const bool carry = old.kept == 1 && h.status == OMQ_OK;
+    v.stats[base] = NodeStats{carry ? old.carry_n : 0, carry ? old.carry_w : 0.0f, 1.0f, 0};
+    v.topo[base] = NodeTopo{-1, pack_act_depth(-1, 0), 0, pack_cnt_flags(0, root_flags)};
+    v.leaves[(size_t)r * v.WCAP] = Visit{0, 0, 0, 0};
+    v.leaf_final[(size_t)r * v.WCAP] = make_int2(0, r);
+  }
+  v.hdr[r] = h;
+  v.q_entries[0][r] = make_int2(r, 0);
+  if (r == 0) { v.q_count[0] = v.R; v.q_count[1] = 0; }
+}
+
 __global__ void __launch_bounds__(kThreads) k_begin(EngineView v, const int8_t* boards, int search_id) {
   const int r = blockIdx.x, tid = threadIdx.x;
   __shared__ int8_t sb[kMaxCells];
@@ -153,7 +178,6 @@ __global__ void __launch_bounds__(kThreads) k_begin(EngineView v, const int8_t* 
   __syncthreads();
   if (tid == 0) {
     TreeHeader h{};
-    h.num_nodes = 1;
     h.status = OMQ_OK;
     h.root_player = (s_stones % 2 == 0) ? 1 : 2;
     h.root_mc = s_stones;
@@ -163,14 +187,7 @@ __global__ void __launch_bounds__(kThreads) k_begin(EngineView v, const int8_t* 
     h.exp_cnt = 1;
     h.wave_idx = 0;
     h.search_idx = search_id;
-    v.hdr[r] = h;
-    const size_t base = (size_t)r * v.T;
-    v.stats[base] = NodeStats{0, 0.0f, 1.0f, 0};
-    v.topo[base] = NodeTopo{-1, pack_act_depth(-1, 0), 0, pack_cnt_flags(0, 0)};
-    v.leaves[(size_t)r * v.WCAP] = Visit{0, 0, 0, 0};
-    v.leaf_final[(size_t)r * v.WCAP] = make_int2(0, r);
-    v.q_entries[0][r] = make_int2(r, 0);
-    if (r == 0) { v.q_count[0] = v.R; v.q_count[1] = 0; }
+    install_root(v, r, h, 0);
   }
 }
 
@@ -217,15 +234,7 @@ __global__ void k_begin_go(EngineView v, const int8_t* hist, const int32_t* meta
     h.exp_off = r;
     h.exp_cnt = 1;
     h.search_idx = search_id;
-    v.hdr[r] = h;
-    const size_t base = (size_t)r * v.T;
-    v.stats[base] = NodeStats{0, 0.0f, 1.0f, 0};
-    v.topo[base] = NodeTopo{-1, pack_act_depth(-1, 0), 0,
-                            pack_cnt_flags(0, passes >= 2 ? kFlagTerminal : 0)};
-    v.leaves[(size_t)r * v.WCAP] = Visit{0, 0, 0, 0};
-    v.leaf_final[(size_t)r * v.WCAP] = make_int2(0, r);
-    v.q_entries[0][r] = make_int2(r, 0);
-    if (r == 0) { v.q_count[0] = v.R; v.q_count[1] = 0; }
+    install_root(v, r, h, passes >= 2 ? kFlagTerminal : 0);
   }
 }
 
@@ -253,14 +262,121 @@ __global__ void k_begin_chess(EngineView v, const ChessRec* rec, const int32_t* 
     h.exp_off = r;
     h.exp_cnt = 1;
     h.search_idx = search_id;
-    v.hdr[r] = h;
-    const size_t base = (size_t)r * v.T;
-    v.stats[base] = NodeStats{0, 0.0f, 1.0f, 0};
-    v.topo[base] = NodeTopo{-1, pack_act_depth(-1, 0), 0, pack_cnt_flags(0, 0)};
-    v.leaves[(size_t)r * v.WCAP] = Visit{0, 0, 0, 0};
-    v.leaf_final[(size_t)r * v.WCAP] = make_int2(0, r);
-    v.q_entries[0][r] = make_int2(r, 0);
-    if (r == 0) { v.q_count[0] = v.R; v.q_count[1] = 0; }
+    install_root(v, r, h, 0);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// reroot: after a move, keep the chosen child's subtree (or its statistics) for the next search
+// ---------------------------------------------------------------------------------------------
+// One CTA per tree, trees [r0, r0 + gridDim.x). actions[r] is the move played (-1: fresh tree).
+// Mode 1 records the child's visit count and value sum for the next root (the reference's
+// use_gpu_tree_reuse path, mcts.py:1929-2005, observably keeps only those). Mode 2 keeps the
+// whole subtree, renumbered in breadth-first order with children in action order (the layout
+// CSRTree.shift_root describes, csr_tree.py:1020-1229): level by level, a block-wide scan of
+// the child counts gives each node's new child_start, and nodes are written to a scratch copy
+// (the old id parked in child_start until the node's level is processed), then copied back.
+// A chosen child without children falls back to mode 1.
+__global__ void __launch_bounds__(1024) k_reroot(EngineView v, const int32_t* actions, int mode,
+                                                 NodeStats* sst, NodeTopo* stp, int r0) {
+  const int r = r0 + blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ int s_child, s_wsum[32], s_total;
+  TreeHeader* H = &v.hdr[r];
+  const size_t base = (size_t)r * v.T;
+  if (tid == 0) s_child = -1;
+  __syncthreads();
+  const int a = actions[r];
+  const NodeTopo rt = v.topo[base];
+  if (H->status != OMQ_OK || H->num_nodes < 1 || a < 0) {
+    if (tid == 0) H->kept = 0;
+    return;
+  }
+  for (int j = tid; j < topo_count(rt); j += blockDim.x)
+    if (topo_action(v.topo[base + rt.child_start + j]) == a) s_child = rt.child_start + j;
+  __syncthreads();
+  const int c = s_child;
+  if (c < 0) {                         // the move is not in the tree: fresh tree
+    if (tid == 0) H->kept = 0;
+    return;
+  }
+  const NodeTopo ct = v.topo[base + c];
+  if (mode == 1 || topo_count(ct) == 0) {
+    if (tid == 0) {
+      const NodeStats cs = v.stats[base + c];
+      H->kept = 1;
+      H->carry_n = cs.N;
+      H->carry_w = cs.W;
+    }
+    return;
+  }
+  NodeStats* S = sst + (size_t)blockIdx.x * v.T;
+  NodeTopo* P = stp + (size_t)blockIdx.x * v.T;
+  if (tid == 0) {
+    S[0] = v.stats[base + c];
+    P[0] = NodeTopo{-1, pack_act_depth(-1, 0), c, ct.cnt_flags};
+  }
+  __syncthreads();
+  int lo = 0, hi = 1;
+  for (int level = 0; lo < hi && level <= v.max_depth + 1; ++level) {
+    int carry = 0;
+    for (int start = lo; start < hi; start += blockDim.x) {
+      const int i = start + tid;
+      int cnt = 0, ocs = 0;
+      if (i < hi) {
+        const NodeTopo ot = v.topo[base + P[i].child_start];
+        cnt = topo_count(ot);
+        ocs = ot.child_start;
+      }
+      // block-wide exclusive scan of cnt
+      int x = cnt;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      if (lane == 31) s_wsum[warp] = x;
+      __syncthreads();
+      if (warp == 0) {
+        int w = lane < (int)(blockDim.x >> 5) ? s_wsum[lane] : 0;
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, w, o);
+          if (lane >= o) w += y;
+        }
+        s_wsum[lane] = w;                 // inclusive warp totals
+        if (lane == 31) s_total = w;
+      }
+      __syncthreads();
+      const int excl = x - cnt + (warp ? s_wsum[warp - 1] : 0);
+      if (i < hi) {
+        const int ns = hi + carry + excl;
+        const int d = topo_depth(P[i]);
+        for (int j = 0; j < cnt; ++j) {
+          const NodeTopo ot = v.topo[base + ocs + j];
+          S[ns + j] = v.stats[base + ocs + j];
+          P[ns + j] = NodeTopo{i, pack_act_depth(topo_action(ot), d + 1), ocs + j, ot.cnt_flags};
+        }
+        P[i].child_start = cnt ? ns : 0;
+      }
+      carry += s_total;
+      __syncthreads();
+    }
+    lo = hi;
+    hi += carry;
+  }
+  for (int i = tid; i < hi; i += blockDim.x) {
+    v.stats[base + i] = S[i];
+    v.topo[base + i] = P[i];
+  }
+  if (tid == 0) {
+    H->num_nodes = hi;
+    H->kept = 2;
+  }
+}
+
+void launch_reroot(const EngineView& v, const int32_t* actions, int mode, NodeStats* scratch_stats,
+                   NodeTopo* scratch_topo, int chunk, cudaStream_t s) {
+  for (int r0 = 0; r0 < v.R; r0 += chunk) {
+    k_reroot<<<min(chunk, v.R - r0), 1024, 0, s>>>(v, actions, mode, scratch_stats, scratch_topo, r0);
+    count_launches(1);
   }
 }
 

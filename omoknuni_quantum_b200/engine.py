@@ -224,6 +224,19 @@ class WaveEngine:
         self._boards = b
         _lib.check(self.L.omq_begin(self._h, ctypes.c_void_p(b.data_ptr()), _stream_ptr()), "omq_begin")
 
+    def reroot(self, actions, keep: bool = False) -> None:
+        """Between searches: make each tree's root child reached by ``actions[r]`` (-1: none) the
+        next search's root; the next ``begin`` / ``search`` must start from the positions those
+        moves lead to. ``keep=False`` starts a fresh tree whose root has the child's visit count
+        and value sum (the reference's use_gpu_tree_reuse behaviour); ``keep=True`` keeps the
+        child's whole subtree (omq_reroot, OMQ_REROOT_KEEP)."""
+        a = torch.as_tensor(np.asarray(actions, np.int32) if not torch.is_tensor(actions) else actions)
+        a = a.to(self.device, torch.int32).reshape(self.num_trees).contiguous()
+        self._reroot_actions = a
+        _lib.check(self.L.omq_reroot(self._h, ctypes.c_void_p(a.data_ptr()),
+                                     _lib.REROOT_KEEP if keep else _lib.REROOT_CARRY, _stream_ptr()),
+                   "omq_reroot")
+
     def root_expand(self, evaluator="synthetic") -> None:
         self.evaluate_queue(_lib.QUEUE_EXPAND, evaluator)
         _lib.check(self.L.omq_root_expand(self._h, _stream_ptr()), "omq_root_expand")

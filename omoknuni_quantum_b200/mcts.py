@@ -71,6 +71,7 @@ class MCTS:
         # itself from torch's global RNG)
         self._noise_seed = int(np.random.randint(0, 2 ** 62))
         self._last_tree = None          # (engine, index) of the last single search
+        self._pending = None            # engine holding a reroot for its next search
         self._root_state = None
         self.stats = dict(total_searches=0, total_simulations=0, total_time=0.0,
                           last_search_sims_per_second=0.0, peak_sims_per_second=0.0,
@@ -83,8 +84,16 @@ class MCTS:
             return 4672
         return self.config.board_size ** 2 + (1 if self.is_go else 0)
 
+    def _drop_pending(self, keep_engine=None) -> None:
+        """A reroot applies only to the next search on the same engine; clear it otherwise."""
+        p, self._pending = self._pending, None
+        if p is not None and p is not keep_engine and p._h.value:
+            p.reroot(np.full(p.num_trees, -1, np.int32))
+
     def _engine(self, num_trees: int, go_rules: str = "chinese") -> WaveEngine:
         eng = self._engines.get(num_trees)
+        if eng is not None and self._pending is eng and self.is_go and getattr(eng, "go_rules", "chinese") != go_rules:
+            self._pending = None
         if eng is not None and self.is_go and getattr(eng, "go_rules", "chinese") != go_rules:
             eng.close()
             eng = None
@@ -162,6 +171,7 @@ class MCTS:
         if sims == 0:
             return np.full((R, self.action_size), 1.0 / self.action_size)
         eng = self._engine(R)
+        self._drop_pending(eng)
         t0 = time.perf_counter()
         rec = np.stack([r[0] for r in roots])
         npr = np.array([r[1] for r in roots], np.int32)
@@ -180,6 +190,7 @@ class MCTS:
         if len(rules) != 1:
             raise ValueError("one search batch must use one Go rule set")
         eng = self._engine(R, rules.pop())
+        self._drop_pending(eng)
         t0 = time.perf_counter()
         hist = torch.from_numpy(np.stack([r[0] for r in roots])).to(self.device)
         meta = torch.from_numpy(np.stack([r[1] for r in roots])).to(self.device)
@@ -216,6 +227,7 @@ class MCTS:
         if sims == 0:                                        # mcts.py:1023-1031
             return np.full((R, self.action_size), 1.0 / self.action_size)
         eng = self._engine(R)
+        self._drop_pending(eng)
         t0 = time.perf_counter()
         if torch.is_tensor(boards):   # host tensor (pinned for an asynchronous copy) or device
             dev_boards = boards.to(self.device, torch.int8, non_blocking=True)
@@ -253,15 +265,37 @@ class MCTS:
         return int(np.random.choice(len(policy), p=p))
 
     def update_root(self, action: int, new_state: Any = None) -> None:
-        """mcts.py:1205-1246. Subtree reuse is not implemented: the next search starts a fresh
-        tree from ``new_state`` (the reference's fallback path, mcts.py:1242-1246)."""
+        """mcts.py:1205-1246. With subtree reuse on, the root child reached by ``action`` seeds the
+        next search (omq_reroot on the last search's tree):
+          * ``keep_subtree=True`` (extension): its whole subtree is kept, renumbered breadth-first
+            as CSRTree.shift_root describes (csr_tree.py:1020-1229);
+          * ``use_gpu_tree_reuse=True``: the next tree is fresh but its root starts with the
+            child's visit count and value sum, which is what the reference's
+            _gpu_friendly_tree_reuse (mcts.py:1929-2005) leaves behind;
+          * otherwise a fresh tree: the reference's default reuse path raises inside
+            apply_subtree_reuse (tree_operations.py:120) and falls back to a reset
+            (mcts.py:1242-1246).
+        The next search must start from the position ``action`` leads to."""
         if action < 0 or action >= self.action_size:
             raise ValueError(f"Invalid action {action}. Must be in range [0, {self.action_size})")
-        self._last_tree = None
+        c = self.config
+        keep = bool(c.enable_subtree_reuse and getattr(c, "keep_subtree", False))
+        carry = bool(c.enable_subtree_reuse and getattr(c, "use_gpu_tree_reuse", False))
+        if self._last_tree is not None:
+            eng, r = self._last_tree
+            acts = np.full(eng.num_trees, -1, np.int32)
+            if keep or carry:
+                acts[r] = int(action)
+                self.stats["tree_reuse_count"] = self.stats.get("tree_reuse_count", 0) + 1
+            eng.reroot(acts, keep=keep)      # -1 everywhere: clears an earlier pending reroot
+            self._pending = eng if (keep or carry) else None
+            if not (keep or carry):
+                self._last_tree = None
         if new_state is not None:
             self._root_state = new_state if (self.is_go or self.is_chess) else self._boards(new_state)
 
     def clear(self) -> None:
+        self._drop_pending()
         self._last_tree = None
         self._root_state = None
 

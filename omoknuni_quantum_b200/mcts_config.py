@@ -166,6 +166,10 @@ class MCTSConfig:
     initial_tree_nodes: int = 100000
     enable_dynamic_allocation: bool = True
     enable_subtree_reuse: bool = True
+    # B200 extension (not a reference field): with subtree reuse on, update_root keeps the chosen
+    # child's whole subtree for the next search, as CSRTree.shift_root describes
+    # (csr_tree.py:1020-1229) but the reference never reaches.
+    keep_subtree: bool = False
     use_mixed_precision: bool = True
     use_cuda_graphs: bool = True
     # -- every other reference field ------------------------------------------------------------

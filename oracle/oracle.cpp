@@ -43,6 +43,68 @@ struct Tree {
   // Chess (game == 2): a position record per node, the game's positions before the root (most
   // recent first) for the history planes and the repetition count.
   std::vector<oracle_chess_pos> cpos, prior;
+  // Subtree reuse between searches (reroot): 0 fresh tree, 1 fresh tree whose root starts with
+  // (carry_n, carry_w), 2 nodes [0, num_nodes) are the kept subtree of the next root.
+  int kept = 0;
+  int32_t carry_n = 0;
+  float carry_w = 0.f;
+
+  // Root child reached by move a becomes the next search's root. Mode 1: the reference's
+  // use_gpu_tree_reuse path (mcts.py:1929-2005) observably keeps the child's visit count and value
+  // sum on a fresh root. Mode 2: the child's subtree as CSRTree.shift_root describes it
+  // (csr_tree.py:1020-1229): breadth-first order, children in action order, per-node data moved
+  // with the nodes. A child without children falls back to mode 1.
+  int reroot(int a, int mode) {
+    kept = 0;
+    if (num_nodes < 1 || res.status != 0 || a < 0) return 0;
+    int c = -1;
+    for (int j = 0; j < child_count[0]; ++j)
+      if (action[child_start[0] + j] == a) c = child_start[0] + j;
+    if (c < 0) return 0;
+    if (mode == 1 || child_count[c] == 0) {
+      kept = 1; carry_n = N[c]; carry_w = W[c];
+      return 1;
+    }
+    std::vector<int> order{c}, ncs{0}, npar{-1};
+    for (size_t i = 0; i < order.size(); ++i) {
+      const int o = order[i];
+      ncs[i] = child_count[o] ? (int)order.size() : 0;
+      for (int j = 0; j < child_count[o]; ++j) {
+        order.push_back(child_start[o] + j);
+        ncs.push_back(0);
+        npar.push_back((int)i);
+      }
+    }
+    const int k = (int)order.size();
+    auto perm = [&](auto& vec, size_t width) {
+      if (vec.size() < (size_t)k * width) return;
+      auto old = vec;
+      for (int i = 0; i < k; ++i)
+        for (size_t w = 0; w < width; ++w) vec[(size_t)i * width + w] = old[(size_t)order[i] * width + w];
+    };
+    perm(N, 1); perm(VL, 1); perm(W, 1); perm(P, 1); perm(terminal, 1); perm(player, 1); perm(mc, 1);
+    perm(ko, 1); perm(passes, 1); perm(boards, (size_t)cells); perm(action, 1); perm(child_count, 1);
+    if (!node_key.empty()) perm(node_key, 1);
+    if (!cpos.empty()) perm(cpos, 1);
+    for (int i = 0; i < k; ++i) { child_start[i] = ncs[i]; parent[i] = npar[i]; }
+    action[0] = -1;
+    num_nodes = k;
+    kept = 2;
+    return 2;
+  }
+
+  // Node 0 and the node count for a new search; returns true when the kept subtree stays (its
+  // root is already expanded: no forced root expansion).
+  bool install_root() {
+    const int k = kept;
+    kept = 0;
+    if (k == 2) return true;
+    num_nodes = 1;
+    N[0] = k == 1 ? carry_n : 0; W[0] = k == 1 ? carry_w : 0.f;
+    VL[0] = 0; P[0] = 1.0f; parent[0] = -1; action[0] = -1;
+    child_count[0] = 0;
+    return false;
+  }
 
   Tree(int cap_, int size_) : cap(cap_), size(size_), cells(size_ * size_), actions(size_ * size_) {
     ko.assign(cap, -1); passes.assign(cap, 0);
@@ -235,7 +297,7 @@ struct Tree {
     superko = sk;
     cycle = cy;
     root_keys.assign(keys, keys + (keys && nkeys > 0 ? nkeys : 0));
-    if (superko || cycle) node_key.assign(cap, 0);
+    if ((superko || cycle) && !(kept == 2 && node_key.size() == (size_t)cap)) node_key.assign(cap, 0);
     planes = oracle::kGoPlanes;
     actions = cells + 1;
     root_hist.assign(hist, hist + (size_t)8 * cells);
@@ -243,9 +305,7 @@ struct Tree {
     if (cfg.board_size != size || cfg.max_nodes > cap || cfg.max_wave_size <= 0) return 2;
     eval = e; ctx = x;
     res = oracle_result{};
-    num_nodes = 1;
-    N[0] = 0; W[0] = 0.f; VL[0] = 0; P[0] = 1.0f; parent[0] = -1; action[0] = -1;
-    child_count[0] = 0;
+    if (install_root()) return 0;
     std::memcpy(boards.data(), hist, cells);
     player[0] = (int8_t)to_move;
     ko[0] = root_ko;
@@ -266,13 +326,11 @@ struct Tree {
     actions = oracle::kChessActions;
     cfg = *c;
     if (cfg.board_size != 8 || size != 8 || cfg.max_nodes > cap || cfg.max_wave_size <= 0) return 2;
-    cpos.assign(cap, oracle_chess_pos{});
+    if (!(kept == 2 && cpos.size() == (size_t)cap)) cpos.assign(cap, oracle_chess_pos{});
     prior.assign(pr, pr + (nprior > 0 ? nprior : 0));
     eval = e; ctx = x;
     res = oracle_result{};
-    num_nodes = 1;
-    N[0] = 0; W[0] = 0.f; VL[0] = 0; P[0] = 1.0f; parent[0] = -1; action[0] = -1;
-    child_count[0] = 0;
+    if (install_root()) return 0;
     terminal[0] = 0;
     cpos[0] = *root;
     player[0] = root->side;
@@ -290,9 +348,8 @@ struct Tree {
     if (cfg.board_size != size || cfg.max_nodes > cap || cfg.max_wave_size <= 0) return 2;
     eval = e; ctx = x;
     res = oracle_result{};
-    num_nodes = 1;
-    N[0] = 0; W[0] = 0.f; VL[0] = 0; P[0] = 1.0f; parent[0] = -1; action[0] = -1;
-    child_count[0] = 0; terminal[0] = 0;
+    if (install_root()) return 0;
+    terminal[0] = 0;
     int stones = 0;
     for (int i = 0; i < cells; ++i) { boards[i] = root[i]; stones += root[i] != 0; }
     player[0] = (stones % 2 == 0) ? 1 : 2;
@@ -518,6 +575,7 @@ int oracle_export(void* t, int32_t* visits, float* wsum, float* priors, int32_t*
 }
 
 int oracle_actions(void* t) { return static_cast<Tree*>(t)->actions; }
+int oracle_reroot(void* t, int action, int mode) { return static_cast<Tree*>(t)->reroot(action, mode); }
 
 int oracle_root_policy(void* t, double* policy) {
   Tree* tr = static_cast<Tree*>(t);

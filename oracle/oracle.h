@@ -88,6 +88,11 @@ int oracle_begin_chess(void* tree, const oracle_config* cfg, const oracle_chess_
                        const oracle_chess_pos* prior, int nprior, oracle_eval_fn eval, void* ctx);
 // Action count of the last begun game (cells for Gomoku, cells + 1 for Go).
 int oracle_actions(void* tree);
+// Between searches: the root child reached by `action` becomes the next begin's root (which must
+// be the position that move leads to). mode 1 keeps the child's visit count and value sum on a
+// fresh root; mode 2 keeps its subtree in breadth-first order. Returns the mode applied (0: the
+// move is not a root child, fresh tree).
+int oracle_reroot(void* tree, int action, int mode);
 // Full search = begin + ceil(sims / max_wave_size) waves.
 int oracle_search(void* tree, const oracle_config* cfg, const int8_t* root_board,
                   oracle_eval_fn eval, void* ctx, oracle_result* out);

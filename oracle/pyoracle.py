@@ -170,6 +170,7 @@ def lib():
                                        ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                        EVAL_FN, ctypes.c_void_p, ctypes.POINTER(OracleResult)]
         L.oracle_actions.argtypes = [ctypes.c_void_p]
+        L.oracle_reroot.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
         L.oracle_begin_chess.argtypes = [ctypes.c_void_p, ctypes.POINTER(OracleConfig), ctypes.c_void_p,
                                          ctypes.c_void_p, ctypes.c_int, EVAL_FN, ctypes.c_void_p]
         L.oracle_feature_hash_chess.restype = ctypes.c_uint64
@@ -455,6 +456,12 @@ class Oracle:
             st = self._L.oracle_wave(self._t, w)
             done += w
         return self.export()
+
+    def reroot(self, action: int, keep: bool = False) -> int:
+        """Between searches: the root child reached by ``action`` becomes the next search's root
+        (carrying its visit count and value sum, or with ``keep`` its whole subtree). Returns the
+        mode applied: 0 fresh, 1 carry, 2 kept subtree."""
+        return self._L.oracle_reroot(self._t, int(action), 2 if keep else 1)
 
     def begin(self, board, cfg: OracleConfig, evaluator=None) -> int:
         self.game = "gomoku"

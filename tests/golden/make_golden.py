@@ -179,6 +179,66 @@ def run_reference_reuse(board, sims, wave, min_visits, cap=200000):
     return pol1, action, child_visits, kept, b2, pol2, arr, ev
 
 
+def gpu_reuse_cases():
+    from omoknuni_quantum_b200.roots import random_root
+    return [
+        # name, board, sims, wave, searches
+        ("seed20", random_root(20), 256, 64, 3),
+        ("seed21_w32", random_root(21), 400, 32, 3),
+        ("empty", np.zeros((15, 15), np.int8), 512, 128, 3),
+        ("seed22", random_root(22), 192, 64, 4),
+        ("seed23_w16", random_root(23), 160, 16, 3),
+    ]
+
+
+def run_reference_gpu_reuse(board, sims, wave, searches, cap=200000):
+    """The reference's `use_gpu_tree_reuse=True` path: search -> update_root(arg-max, new board)
+    -> search ..., which goes through _gpu_friendly_tree_reuse (mcts.py:1929-2005):
+    extract_subtree_gpu_optimized + rebuild_tree_from_compact (compact_subtree.py:195-313). The
+    rebuild writes visit counts and value sums of the kept nodes but leaves the children table
+    and the node counter reset, so the next search re-expands the root and allocates its nodes
+    from id 1 again: what stays is node 0's visit count and value sum, those of the chosen child.
+    The new root's game-state slot comes from a LazyStateManager (index capacity - 1) that the
+    state pool does not know about; when the pool hands that slot to another node during a search
+    (recorded as `aliased`), the root's state is overwritten mid-search and evaluations below it
+    change. Each search's policy, tree digests and root statistics are recorded."""
+    from mcts.core.mcts import MCTS
+    from mcts.core.mcts_config import MCTSConfig
+    from mcts.gpu.gpu_game_states import GameType
+    cfg = MCTSConfig(backend="gpu", device="cpu", wave_async_expansion=False,
+                     dirichlet_epsilon=0.0, enable_subtree_reuse=True, use_gpu_tree_reuse=True,
+                     max_wave_size=wave, c_puct=1.4, virtual_loss=1.0, num_simulations=sims,
+                     max_tree_nodes=cap, initial_tree_nodes=cap, game_type=GameType.GOMOKU,
+                     board_size=15)
+    m = MCTS(cfg, TracingSynthEvaluator())
+    b = board.copy()
+    out = []
+    for i in range(searches):
+        pol = np.asarray(m.search(b.copy()), np.float64)
+        tree, nd = m.tree, m.tree.node_data
+        n = int(tree.num_nodes)
+        nts = m.node_to_state[:n].numpy()
+        aliased = int(nts[0] >= 0 and bool((nts[1:] == nts[0]).any()))
+        rec = dict(board=b.astype(np.int8).copy(), policy=pol, num_nodes=n, aliased=aliased,
+                   root_n=int(nd.visit_counts[0]), root_w=np.float32(nd.value_sums[0]))
+        for k, arr in (("visits", nd.visit_counts), ("value_sums", nd.value_sums),
+                       ("priors", nd.node_priors), ("parent", nd.parent_indices),
+                       ("action", nd.parent_actions)):
+            rec["sha_" + k] = digest(arr[:n].numpy().astype(np.float32 if k in ("value_sums", "priors") else np.int32))
+        action = int(np.argmax(pol))
+        rec["action"] = action
+        child = int(tree.children[0, action])
+        rec["child_n"], rec["child_w"] = int(nd.visit_counts[child]), np.float32(nd.value_sums[child])
+        out.append(rec)
+        if i + 1 < searches:
+            b2 = b.copy()
+            b2.reshape(-1)[action] = 1 if int((b != 0).sum()) % 2 == 0 else 2
+            m.update_root(action, b2)
+            assert m.stats["tree_reuse_count"] == i + 1, "the reference's GPU reuse path did not run"
+            b = b2
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("OMQ_REFERENCE", "/root/reference"))
@@ -192,6 +252,19 @@ def main():
     logging.disable(logging.WARNING)
     import torch
     torch.set_num_threads(os.cpu_count() or 1)
+
+    for name, board, sims, wave, searches in gpu_reuse_cases():
+        if args.only and name not in args.only:
+            continue
+        recs = run_reference_gpu_reuse(board, sims, wave, searches)
+        flat = dict(sims=sims, wave=wave, searches=searches)
+        for i, r in enumerate(recs):
+            for k, x in r.items():
+                flat[f"s{i}_{k}"] = x
+        path = os.path.join(HERE, f"gpureuse_{name}.npz")
+        np.savez_compressed(path, **flat)
+        print(f"gpureuse {name}: " + ", ".join(f"root N {r['root_n']} nodes {r['num_nodes']} "
+                                               f"aliased {r['aliased']}" for r in recs))
 
     for name, board, sims, wave, minv in reuse_cases():
         if args.only and name not in args.only:
