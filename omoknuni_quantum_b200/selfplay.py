@@ -6,7 +6,8 @@ Per move it follows the reference's ``SelfPlayGame.play_single_move``
 (python/mcts/neural_networks/self_play_manager.py:218-370): search the current position, record
 ``(state, policy, player, move_number)``, choose the move (sampled from the policy while
 ``move_number < temperature_threshold``, arg-max afterwards; ``_get_temperature`` :466-470), play
-it, and restart the tree from the new position (``update_root`` without subtree reuse). At the end
+it, and restart the tree from the new position (``update_root`` without subtree reuse, or with
+``subtree_reuse`` "carry" / "keep" as ``MCTS.update_root`` has them). At the end
 each example gets the game outcome from its player's perspective (:388-420), and the examples use
 the reference's ``GameExample`` fields (python/mcts/neural_networks/replay_buffer.py:18-37).
 
@@ -182,9 +183,19 @@ class BatchedSelfPlay:
                  evaluator="synthetic", capacity: int = 200000, c_puct: float = 1.4,
                  temperature: float = 1.0, temperature_threshold: int = 30, seed: int = 0,
                  roots=None, board_size: int = 15,
-                 search: Optional[Callable] = None, device=None, game: str = "gomoku"):
+                 search: Optional[Callable] = None, device=None, game: str = "gomoku",
+                 subtree_reuse: str = "none"):
         if game not in _GAMES:
             raise ValueError(f"unknown game {game!r}")
+        if subtree_reuse not in ("none", "carry", "keep"):
+            raise ValueError("subtree_reuse must be 'none', 'carry' or 'keep'")
+        # between moves the played child seeds the next search of its game (omq_reroot): "keep"
+        # keeps its subtree, "carry" its visit count and value sum (the reference's
+        # use_gpu_tree_reuse behaviour); only while the set of live games is unchanged, so that
+        # tree r still belongs to the same game
+        self.subtree_reuse = subtree_reuse
+        self._last_move = None          # (live games, their moves) of the previous step
+        self._live_now = None
         self.game = _GAMES[game](board_size)
         self.G = int(num_games)
         self.sims = int(num_simulations)
@@ -217,6 +228,9 @@ class BatchedSelfPlay:
         if eng is None:
             eng = WaveEngine(R, **self._engine_args)
             self._engines[R] = eng
+        elif (self.subtree_reuse != "none" and self._last_move is not None
+              and self._last_move[0] == self._live_now):
+            eng.reroot(np.asarray(self._last_move[1], np.int32), keep=self.subtree_reuse == "keep")
         if self.game.name == "gomoku":
             eng.search(torch.from_numpy(np.ascontiguousarray(roots)).to(eng.device), self.sims, self._evaluator)
         else:
@@ -233,6 +247,8 @@ class BatchedSelfPlay:
         if len(live) == 0:
             return 0
         search = self._search or self._device_search
+        self._live_now = tuple(int(g) for g in live)
+        moves = []
         roots, meta = self.game.engine_input([self.positions[g] for g in live])
         visits = np.asarray(search(roots if meta is None else (roots, meta)))
         for i, g in enumerate(live):
@@ -252,10 +268,12 @@ class BatchedSelfPlay:
                 action = int(np.argmax(policy))
             self.positions[g] = self.game.apply(pos, action)
             rec.moves.append(action)
+            moves.append(action)
             res = self.game.outcome(self.positions[g])
             if res is not None:
                 rec.finished = True
                 rec.winner = res
+        self._last_move = (self._live_now, moves)
         self.move_number += 1
         return len(live)
 

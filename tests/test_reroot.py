@@ -187,3 +187,21 @@ def test_dropin_keep_subtree_and_carry(oracle_lib):
         m.search_batch(np.stack([b, b]))          # another engine: the pending reroot is dropped
         p = m.search(b)
         assert np.array_equal(p, oracle_lib.Oracle(100000).search(b, 256, 64).policy)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", ["keep", "carry"])
+def test_selfplay_with_subtree_reuse_matches_oracle(oracle_lib, mode):
+    """Batched self-play with reuse: every move's policy equals the oracle's search of that game
+    continued on its rerooted tree (fresh again whenever the set of live games changed)."""
+    from omoknuni_quantum_b200.selfplay import BatchedSelfPlay
+    sp = BatchedSelfPlay(3, num_simulations=128, wave_size=32, capacity=60000, seed=5,
+                         subtree_reuse=mode)
+    recs = sp.play(4)
+    for r in recs:
+        o = oracle_lib.Oracle(60000)
+        for i, ex in enumerate(r.examples):
+            t = o.search(ex["state"], 128, 32)
+            assert np.array_equal(ex["policy"], t.policy), (r.game_id, i)
+            o.reroot(r.moves[i], keep=mode == "keep")
+    assert all(not r.finished for r in recs)      # the live set stayed the same: reuse every move
