@@ -55,28 +55,30 @@ __constant__ int8_t kKingD[8][2] = {{-1, -1}, {-1, 0}, {-1, 1}, {0, -1}, {0, 1},
 __constant__ int8_t kQueenD[8][2] = {{-1, 0}, {-1, 1}, {0, 1}, {1, 1}, {1, 0}, {1, -1}, {0, -1}, {-1, -1}};
 }  // namespace chess
 
-// ChessRules::isSquareAttacked with the reference's pawn direction.
-__device__ inline bool ch_attacked(const ChessRec& p, int s, int by) {
+// ChessRules::isSquareAttacked with the reference's pawn direction, on the board that `at(sq)`
+// reads (the position itself, or a position after a move, see ChessAfter).
+template <class At>
+__device__ inline bool ch_attacked_on(const At& at, int s, int by) {
   using namespace chess;
   const int r = s >> 3, f = s & 7;
   const int pr = r + (by == WHITE ? -1 : 1);
   const int8_t pawn = (int8_t)piece(P, by), knight = (int8_t)piece(N, by), king = (int8_t)piece(K, by);
-  if (on(pr, f - 1) && p.sq[pr * 8 + f - 1] == pawn) return true;
-  if (on(pr, f + 1) && p.sq[pr * 8 + f + 1] == pawn) return true;
+  if (on(pr, f - 1) && at(pr * 8 + f - 1) == pawn) return true;
+  if (on(pr, f + 1) && at(pr * 8 + f + 1) == pawn) return true;
   for (int k = 0; k < 8; ++k) {
     const int rr = r + kKnightD[k][0], ff = f + kKnightD[k][1];
-    if (on(rr, ff) && p.sq[rr * 8 + ff] == knight) return true;
+    if (on(rr, ff) && at(rr * 8 + ff) == knight) return true;
   }
   for (int k = 0; k < 8; ++k) {
     const int rr = r + kKingD[k][0], ff = f + kKingD[k][1];
-    if (on(rr, ff) && p.sq[rr * 8 + ff] == king) return true;
+    if (on(rr, ff) && at(rr * 8 + ff) == king) return true;
   }
   for (int k = 0; k < 8; ++k) {
     const int dr = kKingD[k][0], df = kKingD[k][1];
     const bool diag = dr != 0 && df != 0;
     int rr = r + dr, ff = f + df;
     for (int st = 0; st < 7 && on(rr, ff); ++st, rr += dr, ff += df) {
-      const int q = p.sq[rr * 8 + ff];
+      const int q = at(rr * 8 + ff);
       if (!q) continue;
       const int t = q & 7;
       if (color_of(q) == by && (t == Q || t == (diag ? B : R))) return true;
@@ -85,6 +87,46 @@ __device__ inline bool ch_attacked(const ChessRec& p, int s, int by) {
   }
   return false;
 }
+
+struct ChessAt {
+  const ChessRec& p;
+  __device__ int operator()(int s) const { return p.sq[s]; }
+};
+
+__device__ inline bool ch_attacked(const ChessRec& p, int s, int by) {
+  return ch_attacked_on(ChessAt{p}, s, by);
+}
+
+// The board after move m of p without copying it: the squares ch_play changes - origin emptied,
+// the moving (or promoted) piece on the target, a pawn taken en passant removed, the castling
+// rook moved beside the king - read through, everything else from p.
+struct ChessAfter {
+  const ChessRec& p;
+  int from, to, pc, ep_cap, rook_from, rook_to;
+  __device__ ChessAfter(const ChessRec& pos, int m) : p(pos) {
+    using namespace chess;
+    from = (m >> 6) & 63;
+    to = m & 63;
+    pc = p.sq[from];
+    ep_cap = -1;
+    rook_from = rook_to = -1;
+    if ((pc & 7) == P && to == p.ep) ep_cap = (from >> 3) * 8 + (to & 7);
+    if ((pc & 7) == K && ((from & 7) - (to & 7) == 2 || (to & 7) - (from & 7) == 2)) {
+      const int r = from >> 3, me = color_of(pc);
+      const bool ks = (to & 7) > (from & 7);
+      rook_to = r * 8 + (p.c960 ? (ks ? (to & 7) - 1 : (to & 7) + 1) : (ks ? 5 : 3));
+      rook_from = r * 8 + p.rook_file[(me == WHITE ? 0 : 2) + (ks ? 0 : 1)];
+    }
+  }
+  __device__ int operator()(int s) const {
+    // the target holds the mover's piece (a promotion changes only its type, and the mover's
+    // own pieces can only block attacks on its king)
+    if (s == to) return pc;
+    if (s == rook_to) return p.sq[rook_from];
+    if (s == from || s == rook_from || s == ep_cap) return 0;
+    return p.sq[s];
+  }
+};
 
 __device__ inline int ch_king(const ChessRec& p, int color) {
   const int8_t k = (int8_t)chess::piece(chess::K, color);
@@ -227,18 +269,27 @@ __device__ inline int ch_move(const ChessRec& p, int a) {
   return (promo << 12) | (from << 6) | (to & 63);
 }
 
-// Test move m of p on a private copy; on success set its action bit in mask.
-__device__ inline void ch_try(const ChessRec& p, int m, uint32_t* mask) {
-  ChessRec q = p;
-  ch_play(q, m);
-  if (!ch_in_check(q, p.side)) {
-    const int a = ch_action(p, m);
-    atomicOr(&mask[a >> 5], 1u << (a & 31));
-  }
+// Whether move m of p leaves the mover's king unattacked (ch_play, then ChessRules::isInCheck):
+// `king` is the mover's king square before the move (-1: no king, never in check).
+__device__ inline bool ch_legal_after(const ChessRec& p, int m, int king) {
+  const ChessAfter after(p, m);
+  const int k = (after.pc & 7) == chess::K ? after.to : king;
+  return k < 0 || !ch_attacked_on(after, k, 3 - p.side);
 }
 
+// Per-warp list of pseudo-legal moves (shared memory).
+constexpr int kChessMaxPseudo = 384;      // pseudo-legal moves per position (218 legal at most)
+struct ChessMoveList {
+  int32_t m[kChessMaxPseudo];
+  int n;
+  __device__ void push(int mv) {
+    const int i = atomicAdd(&n, 1);
+    if (i < kChessMaxPseudo) m[i] = mv;
+  }
+};
+
 // Pseudo-legal moves of the piece on square s (chess_rules.cpp:476-617), each tested.
-__device__ inline void ch_square_moves(const ChessRec& p, int s, uint32_t* mask) {
+__device__ inline void ch_square_moves(const ChessRec& p, int s, ChessMoveList& mask) {
   using namespace chess;
   const int pc = p.sq[s], me = p.side;
   if (color_of(pc) != me) return;
@@ -248,13 +299,13 @@ __device__ inline void ch_square_moves(const ChessRec& p, int s, uint32_t* mask)
     if (nr < 0 || nr > 7) return;
     if (p.sq[nr * 8 + f] == 0) {
       if (nr == 0 || nr == 7) {
-        for (int k = 1; k <= 4; ++k) ch_try(p, (k << 12) | (s << 6) | (nr * 8 + f), mask);
+        for (int k = 1; k <= 4; ++k) mask.push((k << 12) | (s << 6) | (nr * 8 + f));
       } else {
-        ch_try(p, (s << 6) | (nr * 8 + f), mask);
+        mask.push((s << 6) | (nr * 8 + f));
       }
       if ((me == WHITE && r == 6) || (me == BLACK && r == 1)) {
         const int n2 = (nr + dir) * 8 + f;
-        if (p.sq[n2] == 0) ch_try(p, (s << 6) | n2, mask);
+        if (p.sq[n2] == 0) mask.push((s << 6) | n2);
       }
     }
     for (int df = -1; df <= 1; df += 2) {
@@ -263,12 +314,12 @@ __device__ inline void ch_square_moves(const ChessRec& p, int s, uint32_t* mask)
       const int to = nr * 8 + nf;
       if (p.sq[to] != 0 && color_of(p.sq[to]) != me) {
         if (nr == 0 || nr == 7) {
-          for (int k = 1; k <= 4; ++k) ch_try(p, (k << 12) | (s << 6) | to, mask);
+          for (int k = 1; k <= 4; ++k) mask.push((k << 12) | (s << 6) | to);
         } else {
-          ch_try(p, (s << 6) | to, mask);
+          mask.push((s << 6) | to);
         }
       }
-      if (p.ep == to) ch_try(p, (s << 6) | to, mask);
+      if (p.ep == to) mask.push((s << 6) | to);
     }
     return;
   }
@@ -278,7 +329,7 @@ __device__ inline void ch_square_moves(const ChessRec& p, int s, uint32_t* mask)
       const int ff = f + (t == N ? kKnightD[k][1] : kKingD[k][1]);
       if (!on(rr, ff)) continue;
       const int q = p.sq[rr * 8 + ff];
-      if (q == 0 || color_of(q) != me) ch_try(p, (s << 6) | (rr * 8 + ff), mask);
+      if (q == 0 || color_of(q) != me) mask.push((s << 6) | (rr * 8 + ff));
     }
     return;
   }
@@ -289,15 +340,15 @@ __device__ inline void ch_square_moves(const ChessRec& p, int s, uint32_t* mask)
     int rr = r + dr, ff = f + df;
     for (int st = 0; st < 7 && on(rr, ff); ++st, rr += dr, ff += df) {
       const int q = p.sq[rr * 8 + ff];
-      if (q == 0) { ch_try(p, (s << 6) | (rr * 8 + ff), mask); continue; }
-      if (color_of(q) != me) ch_try(p, (s << 6) | (rr * 8 + ff), mask);
+      if (q == 0) { mask.push((s << 6) | (rr * 8 + ff)); continue; }
+      if (color_of(q) != me) mask.push((s << 6) | (rr * 8 + ff));
       break;
     }
   }
 }
 
 // Castling moves (ChessRules::addCastlingMoves / isValidCastle, chess_rules.cpp:619-733).
-__device__ inline void ch_castling(const ChessRec& p, uint32_t* mask) {
+__device__ inline void ch_castling(const ChessRec& p, ChessMoveList& mask) {
   using namespace chess;
   const int me = p.side;
   if (ch_in_check(p, me)) return;
@@ -327,24 +378,45 @@ __device__ inline void ch_castling(const ChessRec& p, uint32_t* mask) {
       if (ch_attacked(p, s, 3 - me)) ok = false;
       else if (s != rook_sq && p.sq[s] != 0) ok = false;
     }
-    if (ok) ch_try(p, (k << 6) | target, mask);
+    if (ok) mask.push((k << 6) | target);
   }
 }
 
-// Legal-action mask of p (warp-collective; mask[kChessMaskWords] in shared memory). Returns the
+// Legal-action mask of p (warp-collective; mask[kChessMaskWords] and the move list in shared
+// memory). Pseudo-legal moves are generated per square (chess_rules.cpp:476-733) into the list,
+// then each lane tests its share of the list against the board after the move. Returns the
 // number of legal moves.
-__device__ inline int warp_ch_legal(const ChessRec& p, uint32_t* mask) {
+__device__ inline int warp_ch_legal(const ChessRec& p, uint32_t* mask, ChessMoveList& list) {
   const int lane = threadIdx.x & 31;
   for (int w = lane; w < kChessMaskWords; w += 32) mask[w] = 0;
+  if (lane == 0) list.n = 0;
   __syncwarp();
-  ch_square_moves(p, lane, mask);
-  ch_square_moves(p, lane + 32, mask);
-  if (lane == 0) ch_castling(p, mask);
+  ch_square_moves(p, lane, list);
+  ch_square_moves(p, lane + 32, list);
+  if (lane == 0) ch_castling(p, list);
+  int king = -1;
+  const int8_t kp = (int8_t)chess::piece(chess::K, p.side);
+  for (int s = lane; s < 64; s += 32)
+    if (p.sq[s] == kp) king = king < 0 ? s : king;
+  // first king in square order (ChessState's king search)
+  for (int o = 16; o > 0; o >>= 1) {
+    const int x = __shfl_xor_sync(0xFFFFFFFFu, king, o);
+    if (x >= 0 && (king < 0 || x < king)) king = x;
+  }
   __syncwarp();
-  int n = 0;
-  for (int w = lane; w < kChessMaskWords; w += 32) n += __popc(mask[w]);
-  for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xFFFFFFFFu, n, o);
-  return n;
+  const int n = min(list.n, kChessMaxPseudo);
+  for (int i = lane; i < n; i += 32) {
+    const int m = list.m[i];
+    if (ch_legal_after(p, m, king)) {
+      const int a = ch_action(p, m);
+      atomicOr(&mask[a >> 5], 1u << (a & 31));
+    }
+  }
+  __syncwarp();
+  int c = 0;
+  for (int w = lane; w < kChessMaskWords; w += 32) c += __popc(mask[w]);
+  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
+  return c;
 }
 
 // 64-bit placement hash (Zobrist keys from SplitMix64), warp-collective.

@@ -609,6 +609,7 @@ constexpr int kMaxDepthCap = 128;
 struct ChessWarpSmem {
   ChessReplay rep;
   uint32_t mask[kChessMaskWords];
+  ChessMoveList list;
 };
 
 struct ExpandWarpSmem {
@@ -661,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
         const int d = warp_ch_replay(v, r, node, cw.rep, false);
         if (d < 0) { if (lane == 0) H->status = OMQ_BAD_ARG; }
         else {
-          n = warp_ch_legal(cw.rep.pos, cw.mask);
+          n = warp_ch_legal(cw.rep.pos, cw.mask, cw.list);
           if (lane == 0 && ch_terminal(cw.rep.pos, n)) {
             NodeTopo lt = v.topo[base + node];
             lt.cnt_flags = pack_cnt_flags(topo_count(lt), topo_flags(lt) | kFlagTerminal);
