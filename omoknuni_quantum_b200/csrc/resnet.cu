@@ -20,6 +20,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <new>
@@ -1688,6 +1689,21 @@ struct omq_resnet {
   int32_t* prof_host_counts;
 };
 
+// cudaFuncSetAttribute(kernel, MaxDynamicSharedMemorySize, bytes) once per device (bit dev of
+// `done`); safe when several host threads drive engines on different devices.
+template <class K>
+static cudaError_t set_smem_attr_once(std::atomic<uint32_t>& done, K kernel, cudaFuncAttribute attr,
+                                      int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint32_t bit = 1u << (dev & 31);
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, attr, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
 static PFN_encodeTiled_t get_encode() {
   static PFN_encodeTiled_t fn = nullptr;
   if (!fn) {
@@ -1953,14 +1969,11 @@ static int launch_conv(const omq_resnet* n, const CUtensorMap& tA, const CUtenso
                        const CUtensorMap& tO, const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
                        int kb_per_tap, const int32_t* d_count, int count, cudaStream_t s) {
   using Cfg = ConvCfg<BN, SUB>;
-  static int attr_dev = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (attr_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(k_conv3x3<BN, SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  static std::atomic<uint32_t> attr_set{0};
+  {
+    const cudaError_t e = set_smem_attr_once(attr_set, k_conv3x3<BN, SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::kSmem);
     if (e != cudaSuccess) return cuda_status(e, "conv smem attribute");
-    attr_dev = dev;
   }
   ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
   const int max_tiles = (int)((n->rows + Cfg::kRows - 1) / Cfg::kRows);
@@ -1974,14 +1987,11 @@ template <int BS, int SB, int EW>
 static int launch_conv_halo_t(const omq_resnet* n, const CUtensorMap& tH, const CUtensorMap& tB,
                               const CUtensorMap& tO, const ConvArgs& a, cudaStream_t s) {
   using Cfg = HaloCfgT<BS, SB, EW>;
-  static int attr_dev = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (attr_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(k_conv3x3_halo<BS, SB, EW>,
+  static std::atomic<uint32_t> attr_set{0};
+  {
+    const cudaError_t e = set_smem_attr_once(attr_set, k_conv3x3_halo<BS, SB, EW>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
     if (e != cudaSuccess) return cuda_status(e, "halo conv smem attribute");
-    attr_dev = dev;
   }
   const int max_tiles = (int)((n->rows + Cfg::kRows - 1) / Cfg::kRows);
   const int grid = max(1, min(max_tiles, n->sm_count));
@@ -2023,14 +2033,11 @@ static int launch_conv_halo_tr(const omq_resnet* n, const CUtensorMap& tH, const
                                const CUtensorMap& tO, const float* bias, const __nv_bfloat16* res,
                                __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count, int count,
                                cudaStream_t s) {
-  static int attr_dev = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (attr_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(k_conv3x3_halo_t, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  static std::atomic<uint32_t> attr_set{0};
+  {
+    const cudaError_t e = set_smem_attr_once(attr_set, k_conv3x3_halo_t, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          HaloTCfg::kSmem);
     if (e != cudaSuccess) return cuda_status(e, "transposed halo conv smem attribute");
-    attr_dev = dev;
   }
   ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
   const int max_tiles = (int)((n->rows + HaloTCfg::kRows - 1) / HaloTCfg::kRows);
@@ -2043,14 +2050,11 @@ static int launch_conv_halo_tr(const omq_resnet* n, const CUtensorMap& tH, const
 static int launch_conv_t(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB,
                          const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
                          int kb_per_tap, const int32_t* d_count, int count, cudaStream_t s) {
-  static int attr_dev = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (attr_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(k_conv3x3_t, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  static std::atomic<uint32_t> attr_set{0};
+  {
+    const cudaError_t e = set_smem_attr_once(attr_set, k_conv3x3_t, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          TCfg::kSmem);
     if (e != cudaSuccess) return cuda_status(e, "transposed conv smem attribute");
-    attr_dev = dev;
   }
   ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
   const int max_tiles = (int)((n->rows + TCfg::kPix - 1) / TCfg::kPix);
@@ -2065,14 +2069,11 @@ static int launch_conv_pair(const omq_resnet* n, const CUtensorMap& tA, const CU
                             const CUtensorMap& tO, const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
                             int kb_per_tap, const int32_t* d_count, int count, cudaStream_t s) {
   using Cfg = PairCfg<BN>;
-  static int attr_dev = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (attr_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(k_conv3x3_pair<BN>,
+  static std::atomic<uint32_t> attr_set{0};
+  {
+    const cudaError_t e = set_smem_attr_once(attr_set, k_conv3x3_pair<BN>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
     if (e != cudaSuccess) return cuda_status(e, "pair conv smem attribute");
-    attr_dev = dev;
   }
   ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
   const int max_tiles = (int)((n->rows + 2 * kTileM - 1) / (2 * kTileM));
@@ -2100,13 +2101,10 @@ static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& t
 template <int NT, int MODE>
 static int launch_dense(const CUtensorMap& tA, const CUtensorMap& tW, const DenseArgs& a, int rows_cap,
                         int ntiles, cudaStream_t s) {
-  static int attr_dev = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (attr_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(k_dense<NT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDenseSmem);
+  static std::atomic<uint32_t> attr_set{0};
+  {
+    const cudaError_t e = set_smem_attr_once(attr_set, k_dense<NT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDenseSmem);
     if (e != cudaSuccess) return cuda_status(e, "dense smem attribute");
-    attr_dev = dev;
   }
   count_launches(1);
   k_dense<NT, MODE><<<dim3((rows_cap + 127) / 128, ntiles), kDenseThreads, kDenseSmem, s>>>(tA, tW, a);

@@ -79,3 +79,35 @@ def test_queue_path_equals_protocol_path():
         a, b = e1.export_tree(r), e2.export_tree(r)
         for k in a:
             assert np.array_equal(a[k], b[k]), (r, k)
+
+
+def test_distinct_handles_from_concurrent_host_threads():
+    """Engines and networks are thread-safe across distinct handles: two host threads, each with
+    its own ResNet and search engine on its own stream, give the results of a sequential run."""
+    import threading
+    from omoknuni_quantum_b200.engine import WaveEngine
+    from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec
+    from omoknuni_quantum_b200.roots import random_root
+    spec = ResNetSpec(num_blocks=2, filters=128)
+    boards = [np.stack([random_root(90 + 4 * t + i) for i in range(4)]) for t in range(2)]
+
+    def run(t, out):
+        with torch.cuda.stream(torch.cuda.Stream()):
+            ev = ResNetEvaluator.random(spec, seed=11, max_batch=1024)
+            eng = WaveEngine(4, capacity=60000, max_wave_size=64)
+            for _ in range(3):
+                eng.search(torch.from_numpy(boards[t]).cuda(), 192, evaluator=ev)
+            out[t] = eng.root_visits().cpu().numpy()
+            torch.cuda.current_stream().synchronize()
+
+    seq = {}
+    for t in range(2):
+        run(t, seq)
+    par = {}
+    th = [threading.Thread(target=run, args=(t, par)) for t in range(2)]
+    for x in th:
+        x.start()
+    for x in th:
+        x.join()
+    for t in range(2):
+        assert np.array_equal(seq[t], par[t]), t
