@@ -134,6 +134,7 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   take(chess ? R * 100 * sizeof(uint64_t) : 16);                          // 18 chess prior hashes
   take(c.game == OMQ_GAME_GO ? R * OMQ_GO_MAX_KEYS * sizeof(uint64_t) : 16);  // 19 Go superko keys
   take(c.game == OMQ_GAME_GO ? R * 128 * sizeof(uint32_t) : 16);              // 20 Go key filter
+  take(c.game == OMQ_GAME_GOMOKU ? R * W * 128 * sizeof(int16_t) : 16);       // 21 leaf paths
   void* arena = nullptr;
   cudaError_t err = cudaMalloc(&arena, tot);
   if (err != cudaSuccess) {
@@ -162,6 +163,7 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   v.chess_prior_hash = reinterpret_cast<uint64_t*>(b + off[18]);
   v.go_keys = reinterpret_cast<uint64_t*>(b + off[19]);
   v.go_bloom = reinterpret_cast<uint32_t*>(b + off[20]);
+  v.leaf_paths = reinterpret_cast<int16_t*>(b + off[21]);
   err = cudaMemset(v.hdr, 0, R * sizeof(TreeHeader));
   if (err == cudaSuccess) err = cudaMemset(v.q_count, 0, 2 * sizeof(int32_t));
   if (err == cudaSuccess) err = cudaMemset(v.root_noise, 0, R * (size_t)v.A * sizeof(float));

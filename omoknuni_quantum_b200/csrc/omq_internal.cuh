@@ -100,6 +100,8 @@ struct EngineView {
   uint64_t* go_keys;           // Go: [R][OMQ_GO_MAX_KEYS] the root game's position keys, sorted
   uint32_t* go_bloom;          // Go: [R][128] 4096-bit filter of those keys (key & 4095)
   int max_children;      // most children a node can have (sizes the selection sort)
+  int16_t* leaf_paths;   // Gomoku: [R][WCAP][128] actions root -> leaf of each expandable leaf
+                         // (slot 127: its depth), written and read by k_expand
   TreeHeader* hdr;       // [R]
   Visit* frontier;       // [R][2][WCAP]
   Visit* vlog;           // [R][LOGCAP]

@@ -26,28 +26,46 @@ constexpr int kWarps = kThreads / 32;
 // ---------------------------------------------------------------------------------------------
 // Gomoku rules on a shared-memory board
 // ---------------------------------------------------------------------------------------------
-// True when placing `p` at cell `a` of board `b` (which does not yet hold that stone) makes five
-// or more in a row through `a`. For a non-terminal parent this equals the reference's
-// full-board scan (python/mcts/utils/fast_terminal_check.py:233-332): any new five must
-// contain the new stone.
-__device__ bool five_through(const int8_t* b, int S, int a, int p) {
-  const int r0 = a / S, c0 = a % S;
-  const int dr[4] = {0, 1, 1, 1}, dc[4] = {1, 0, 1, -1};
+// Warp-collective: for each row y < S, fm[y] gets bit x set when placing `p` on the empty cell
+// (y, x) of board b makes five or more in a row through it. For a non-terminal parent this equals
+// the reference's full-board scan (python/mcts/utils/fast_terminal_check.py:233-332): any new
+// five must contain the new stone. Lane y holds row y's stone mask; a cell completes a five in direction (dr, dc) when one
+// of the five windows of 5 cells containing it has its other 4 cells occupied by `p`. Row j of
+// a window comes from lane y + j*dr by shuffle, its column offset is a shift by j*dc.
+__device__ void warp_five_masks(const int8_t* b, int S, int p, uint32_t* fm) {
+  const int lane = threadIdx.x & 31;
+  uint32_t row = 0, occ = 0;
+  if (lane < S)
+    for (int x = 0; x < S; ++x) {
+      const int q = b[lane * S + x];
+      row |= (q == p ? 1u : 0u) << x;
+      occ |= (q != 0 ? 1u : 0u) << x;
+    }
+  const uint32_t full = (1u << S) - 1u;
+  uint32_t five = 0;
+#pragma unroll
   for (int d = 0; d < 4; ++d) {
-    int run = 1;
-    for (int s = 1; s < 5; ++s) {
-      int r = r0 + dr[d] * s, c = c0 + dc[d] * s;
-      if (r < 0 || r >= S || c < 0 || c >= S || b[r * S + c] != p) break;
-      ++run;
+    const int dr = d == 0 ? 0 : 1, dc = d == 1 ? 0 : (d == 3 ? -1 : 1);
+    uint32_t t[9];                                  // t[j + 4]: bit x = stone at (y + j*dr, x + j*dc)
+#pragma unroll
+    for (int j = -4; j <= 4; ++j) {
+      const int src = lane + j * dr;
+      uint32_t m = __shfl_sync(0xFFFFFFFFu, row, src & 31);
+      if (src < 0 || src >= S) m = 0;
+      const int sh = j * dc;
+      t[j + 4] = sh >= 0 ? (m >> sh) : ((m << -sh) & full);
     }
-    for (int s = 1; s < 5; ++s) {
-      int r = r0 - dr[d] * s, c = c0 - dc[d] * s;
-      if (r < 0 || r >= S || c < 0 || c >= S || b[r * S + c] != p) break;
-      ++run;
+#pragma unroll
+    for (int k = 0; k <= 4; ++k) {                  // window covering offsets -k .. 4-k
+      uint32_t w = full;
+#pragma unroll
+      for (int j = -4; j <= 4; ++j)
+        if (j != 0 && j >= -k && j <= 4 - k) w &= t[j + 4];
+      five |= w;
     }
-    if (run >= 5) return true;
   }
-  return false;
+  if (lane < S) fm[lane] = five & ~occ & full;
+  __syncwarp();
 }
 
 // Five in a row starting at cell i in any of the 4 forward directions.
@@ -464,10 +482,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
   for (int depth = 1; depth < v.max_depth; ++depth) {
     const int n_cur = sh.cnt[cur];
     if (n_cur == 0) break;
-    for (int i = warp; i < n_cur; i += (int)(blockDim.x >> 5)) {
-      const Visit e = F[cur][i];
-      const NodeTopo tp = v.topo[base + e.node];
-      const int n = topo_count(tp);
+    const int nwarps = (int)(blockDim.x >> 5);
+    // this warp's parents are i = warp + nwarps * t; lane t prefetches parent t of each group of
+    // 32 (frontier entry, topology, visit count), so the dependent loads of 32 parents overlap
+    for (int g0 = warp; g0 < n_cur; g0 += 32 * nwarps) {
+      const int mine = g0 + nwarps * lane;
+      Visit pe{0, 0, 0, 0};
+      NodeTopo ptp{0, 0, 0, 0};
+      int32_t pn = 0;
+      if (mine < n_cur) {
+        pe = F[cur][mine];
+        ptp = v.topo[base + pe.node];
+        if (topo_count(ptp) > 0) pn = v.stats[base + pe.node].N;
+      }
+      const int ng = min(32, (n_cur - g0 + nwarps - 1) / nwarps);
+    for (int t = 0; t < ng; ++t) {
+      const Visit e{__shfl_sync(0xFFFFFFFFu, pe.node, t), __shfl_sync(0xFFFFFFFFu, pe.lo, t),
+                    __shfl_sync(0xFFFFFFFFu, pe.k, t), __shfl_sync(0xFFFFFFFFu, pe.depth, t)};
+      const int n = topo_count(NodeTopo{0, 0, 0, __shfl_sync(0xFFFFFFFFu, ptp.cnt_flags, t)});
       if (n == 0) {  // no children: the simulation stops here (wave_search.py:762-768)
         if (lane == 0) {
           int li = atomicAdd(&sh.nleaf, 1);
@@ -475,8 +507,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
         }
         continue;
       }
-      const int cs = tp.child_start;
-      const int32_t np = v.stats[base + e.node].N;
+      const int cs = __shfl_sync(0xFFFFFFFFu, ptp.child_start, t);
+      const int32_t np = __shfl_sync(0xFFFFFFFFu, pn, t);
       if (e.node == 0 && v.noise_eps > 0.0f) {
         // One Dirichlet(alpha) vector per wave at the root (wave_search.py:1160-1170): gamma draws
         // normalised in the engine's fixed summation order (lane-strided partials, butterfly).
@@ -505,8 +537,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
           out[topo_action(v.topo[base + cs + j])] = noise;
         }
       } else {
-        for (int j = lane; j < n; j += 32) {
-          const NodeStats st = v.stats[base + cs + j];
+        // children statistics, four independent 16-byte loads in flight per lane
+        const NodeStats* cst = v.stats + base + cs;
+        int j = lane;
+        for (; j + 96 < n; j += 128) {
+          const NodeStats s0 = cst[j], s1 = cst[j + 32], s2 = cst[j + 64], s3 = cst[j + 96];
+          keys[j] = rank_key(ucb_score(s0, np, v.c_puct, v.vl_value, v.enable_vl), j);
+          keys[j + 32] = rank_key(ucb_score(s1, np, v.c_puct, v.vl_value, v.enable_vl), j + 32);
+          keys[j + 64] = rank_key(ucb_score(s2, np, v.c_puct, v.vl_value, v.enable_vl), j + 64);
+          keys[j + 96] = rank_key(ucb_score(s3, np, v.c_puct, v.vl_value, v.enable_vl), j + 96);
+        }
+        for (; j < n; j += 32) {
+          const NodeStats st = cst[j];
           keys[j] = rank_key(ucb_score(st, np, v.c_puct, v.vl_value, v.enable_vl), j);
         }
       }
@@ -544,6 +586,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
         }
       }
       __syncwarp();
+    }
     }
     __syncthreads();
     if (tid == 0) sh.cnt[cur] = 0;
@@ -613,6 +656,7 @@ struct ChessWarpSmem {
 };
 
 struct ExpandWarpSmem {
+  uint32_t five[32];    // Gomoku: cells where the mover completes five (warp_five_masks)
   int16_t acts[kMaxDepthCap];
   int16_t legal[kMaxCells + 1];
   float pv[kMaxCells + 1];
@@ -710,6 +754,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
     return;
   }
   ExpandWarpSmem& W = ws[warp];
+  // Gomoku: every thread walks one expandable leaf's parent chain into the path scratch (slot
+  // kMaxDepthCap - 1 holds the depth), so the chains' dependent loads overlap across leaves
+  int16_t* gpath = v.leaf_paths + (size_t)r * v.WCAP * kMaxDepthCap;
+  if (!go && !chs) {
+    for (int i = tid; i < nleaf; i += blockDim.x)
+      if (lf[i].y >= 0) {
+        int16_t* P = gpath + (size_t)i * kMaxDepthCap;
+        P[kMaxDepthCap - 1] = (int16_t)path_actions(v.topo + base, leaves[i].node, kMaxDepthCap - 2, P);
+      }
+    __syncthreads();
+  }
   for (int i = warp; i < nleaf; i += (int)(blockDim.x >> 5)) {
     const Visit e = leaves[i];
     const int q = lf[i].y;
@@ -765,28 +820,37 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
         if (lane == 0 && v.enable_vl) v.stats[base + final_node].VL += 1;
       }
     } else if (q >= 0) {
-      // reconstruct the leaf's board: root board + the stones along its path
-      int d = 0;
-      if (lane == 0) d = path_actions(v.topo + base, e.node, kMaxDepthCap - 1, W.acts);
-      d = __shfl_sync(0xFFFFFFFFu, d, 0);
+      // reconstruct the leaf's board: root board + the stones along its path (walked above)
+      constexpr int kChunks = (kMaxCells + 31) / 32;
+      float pq[kChunks];
+      const float* prow = pol + (size_t)q * v.A;
+#pragma unroll
+      for (int t = 0; t < kChunks; ++t) {         // the leaf's policy row: independent loads
+        const int c = lane + 32 * t;
+        pq[t] = c < v.C ? prow[c] : 0.0f;
+      }
+      const int16_t* P = gpath + (size_t)i * kMaxDepthCap;
+      const int d = P[kMaxDepthCap - 1];
       if (d < 0) { if (lane == 0) H->status = OMQ_BAD_ARG; continue; }
       for (int c = lane; c < v.C; c += 32) W.board[c] = v.root_board[(size_t)r * v.C + c];
       __syncwarp();
       for (int j = lane; j < d; j += 32)
-        W.board[W.acts[j]] = (int8_t)((j % 2 == 0) ? H->root_player : 3 - H->root_player);
+        W.board[P[j]] = (int8_t)((j % 2 == 0) ? H->root_player : 3 - H->root_player);
       __syncwarp();
       const int player = (d % 2 == 0) ? H->root_player : 3 - H->root_player;
       const int mc = H->root_mc + d;
+      warp_five_masks(W.board, v.S, player, W.five);
       // legal actions in ascending order and their policy values
       int n = 0;
-      for (int c0 = 0; c0 < v.C; c0 += 32) {
-        const int c = c0 + lane;
+#pragma unroll
+      for (int t = 0; t < kChunks; ++t) {
+        const int c = lane + 32 * t;
         const bool legal = c < v.C && W.board[c] == 0;
         const unsigned m = __ballot_sync(0xFFFFFFFFu, legal);
         if (legal) {
           const int j = n + __popc(m & ((1u << lane) - 1));
           W.legal[j] = (int16_t)c;
-          W.pv[j] = pol[(size_t)q * v.A + c];
+          W.pv[j] = pq[t];
         }
         n += __popc(m);
       }
@@ -798,7 +862,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
       for (int j = lane; j < n; j += 32) {
         const int a = W.legal[j];
         const float P = __fdiv_rn(W.pv[j], denom);
-        const bool term = H->root_five || five_through(W.board, v.S, a, player) || (mc + 1 >= v.C);
+        const bool term = H->root_five || ((W.five[a / v.S] >> (a % v.S)) & 1u) || (mc + 1 >= v.C);
         const int c = start + j;
         const NodeStats st{0, 0.0f, P, 0};
         v.stats[base + c] = st;
