@@ -68,6 +68,16 @@ __constant__ uint32_t c_exp2[64] = {
     1802103u,1821727u,1841564u,1861617u,1881889u,1902381u,1923097u,1944038u,1965207u,1986607u,
     2008240u,2030108u,2052214u,2074562u};
 
+// floor(n / d) for 0 < d and n < 2^53: an fp64 estimate from rd = 1.0 / d (relative error a few
+// ulps, so at most one off for quotients below 2^20), corrected by integer products - the same
+// quotient as the integer division, without a 64-bit divide per action.
+__device__ __forceinline__ uint64_t div_floor53(uint64_t n, uint64_t d, double rd) {
+  uint64_t q = (uint64_t)__dmul_rn((double)n, rd);
+  if (q * d > n) --q;
+  else if ((q + 1) * d <= n) ++q;
+  return q;
+}
+
 __device__ __forceinline__ uint64_t exp2_fixed(int64_t t) {
   return (uint64_t)c_exp2[t & 63] << ((t >> 6) + 6);
 }
@@ -95,6 +105,7 @@ __device__ void synth_emit(const EngineView& v, int queue, int q, uint64_t h, co
       }
     }
     for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xFFFFFFFFu, tot, o);
+    const double rtot = tot ? 1.0 / (double)tot : 0.0;
     int idx_base = 0;
     float* out = v.q_policy[0] + (size_t)q * v.A;
 #pragma unroll
@@ -106,7 +117,7 @@ __device__ void synth_emit(const EngineView& v, int queue, int q, uint64_t h, co
         float p = 0.0f;
         if (legal) {
           const uint64_t idx = (uint64_t)(idx_base + __popc(m & ((1u << lane) - 1)));
-          const uint64_t qa = 512ull * ((wv[t] * 32640ull) / tot) + idx;
+          const uint64_t qa = 512ull * div_floor53(wv[t] * 32640ull, tot, rtot) + idx;
           p = __fmul_rn(__ull2float_rn(qa), 1.0f / 16777216.0f);
         }
         out[a] = p;
@@ -370,10 +381,11 @@ __global__ void __launch_bounds__(kChessWarps * 32) k_synth_chess(EngineView v, 
     for (int a = lane; a < kChessActions; a += 32)
       tot += exp2_fixed(exp_step(mix64(h + 0x9E3779B97F4A7C15ull * (uint64_t)(a + 1))));
     for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xFFFFFFFFu, tot, o);
+    const double rtot = 1.0 / (double)tot;
     float* out = v.q_policy[0] + (size_t)q * v.A;
     for (int a = lane; a < kChessActions; a += 32) {
       const uint64_t wa = exp2_fixed(exp_step(mix64(h + 0x9E3779B97F4A7C15ull * (uint64_t)(a + 1))));
-      const uint64_t qa = 512ull * ((wa * 32640ull) / tot) + (uint64_t)a;
+      const uint64_t qa = 512ull * div_floor53(wa * 32640ull, tot, rtot) + (uint64_t)a;
       out[a] = __fmul_rn(__ull2float_rn(qa), 1.0f / 16777216.0f);
     }
   }
