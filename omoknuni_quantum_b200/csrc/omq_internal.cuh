@@ -119,15 +119,28 @@ struct EngineView {
 //   Ne = float(N + VL); We = W + float(VL) * (-|vl|); Q = We / Ne if Ne > 0 else 0;
 //   U = ((c * P) * sqrt(max(float(N_parent), 1))) / (1 + Ne); score = Q + U
 // Every operation is an explicitly rounded intrinsic so no contraction can change the result.
-__device__ __forceinline__ float ucb_score(const NodeStats& s, int32_t n_parent, float c_puct,
-                                           float vl_value, int enable_vl) {
+// The same with sq = sqrt(max(N_parent, 1)) computed once per parent. A child with N + VL = 0
+// has Q = 0 and U = c*P*sq / 1, and the IEEE division by 1 is exact, so its score is c*P*sq
+// without a divide.
+__device__ __forceinline__ float ucb_score_sq(const NodeStats& s, float sq, float c_puct,
+                                              float vl_value, int enable_vl) {
   const int32_t vl = enable_vl ? s.VL : 0;
+  const float cps = __fmul_rn(__fmul_rn(c_puct, s.P), sq);
+  if (s.N + vl == 0) return __fadd_rn(0.0f, cps);
   const float ne = __int2float_rn(s.N + vl);
   const float we = enable_vl ? __fadd_rn(s.W, __fmul_rn(__int2float_rn(s.VL), vl_value)) : s.W;
   const float q = ne > 0.0f ? __fdiv_rn(we, ne) : 0.0f;
-  const float sq = __fsqrt_rn(fmaxf(__int2float_rn(n_parent), 1.0f));
-  const float u = __fdiv_rn(__fmul_rn(__fmul_rn(c_puct, s.P), sq), __fadd_rn(1.0f, ne));
+  const float u = __fdiv_rn(cps, __fadd_rn(1.0f, ne));
   return __fadd_rn(q, u);
+}
+
+__device__ __forceinline__ float parent_sqrt(int32_t n_parent) {
+  return __fsqrt_rn(fmaxf(__int2float_rn(n_parent), 1.0f));
+}
+
+__device__ __forceinline__ float ucb_score(const NodeStats& s, int32_t n_parent, float c_puct,
+                                           float vl_value, int enable_vl) {
+  return ucb_score_sq(s, parent_sqrt(n_parent), c_puct, vl_value, enable_vl);
 }
 
 // Order-preserving 32-bit image of a float (total order; +0 and -0 mapped together).

@@ -539,17 +539,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
       } else {
         // children statistics, four independent 16-byte loads in flight per lane
         const NodeStats* cst = v.stats + base + cs;
+        const float sq = parent_sqrt(np);
         int j = lane;
         for (; j + 96 < n; j += 128) {
           const NodeStats s0 = cst[j], s1 = cst[j + 32], s2 = cst[j + 64], s3 = cst[j + 96];
-          keys[j] = rank_key(ucb_score(s0, np, v.c_puct, v.vl_value, v.enable_vl), j);
-          keys[j + 32] = rank_key(ucb_score(s1, np, v.c_puct, v.vl_value, v.enable_vl), j + 32);
-          keys[j + 64] = rank_key(ucb_score(s2, np, v.c_puct, v.vl_value, v.enable_vl), j + 64);
-          keys[j + 96] = rank_key(ucb_score(s3, np, v.c_puct, v.vl_value, v.enable_vl), j + 96);
+          keys[j] = rank_key(ucb_score_sq(s0, sq, v.c_puct, v.vl_value, v.enable_vl), j);
+          keys[j + 32] = rank_key(ucb_score_sq(s1, sq, v.c_puct, v.vl_value, v.enable_vl), j + 32);
+          keys[j + 64] = rank_key(ucb_score_sq(s2, sq, v.c_puct, v.vl_value, v.enable_vl), j + 64);
+          keys[j + 96] = rank_key(ucb_score_sq(s3, sq, v.c_puct, v.vl_value, v.enable_vl), j + 96);
         }
         for (; j < n; j += 32) {
           const NodeStats st = cst[j];
-          keys[j] = rank_key(ucb_score(st, np, v.c_puct, v.vl_value, v.enable_vl), j);
+          keys[j] = rank_key(ucb_score_sq(st, sq, v.c_puct, v.vl_value, v.enable_vl), j);
         }
       }
       __syncwarp();
@@ -791,7 +792,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
       const int start = num_nodes + s_cnt[i];
       const int d = e.depth;
       unsigned long long best = 0;
-      const int32_t nleafN = v.stats[base + e.node].N;
+      const float sq_leaf = parent_sqrt(v.stats[base + e.node].N);
       for (int j = lane; j < n; j += 32) {
         const int a = W.legal[j];
         const float P = __fdiv_rn(W.pv[j], denom);
@@ -804,7 +805,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
         v.topo[base + c] = NodeTopo{e.node, pack_act_depth(a, d + 1), 0,
                                     pack_cnt_flags(0, term ? kFlagTerminal : 0)};
         const unsigned long long key =
-            rank_key(ucb_score(st, nleafN, v.c_puct, v.vl_value, v.enable_vl), j);
+            rank_key(ucb_score_sq(st, sq_leaf, v.c_puct, v.vl_value, v.enable_vl), j);
         best = key > best ? key : best;
       }
       best = warp_max_u64(best);
@@ -858,7 +859,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
       const float denom = __fadd_rn(warp_fixed_order_sum(W.pv, n), 1e-8f);
       const int start = num_nodes + s_cnt[i];
       unsigned long long best = 0;
-      const int32_t nleafN = v.stats[base + e.node].N;
+      const float sq_leaf = parent_sqrt(v.stats[base + e.node].N);
       for (int j = lane; j < n; j += 32) {
         const int a = W.legal[j];
         const float P = __fdiv_rn(W.pv[j], denom);
@@ -869,7 +870,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
         v.topo[base + c] = NodeTopo{e.node, pack_act_depth(a, d + 1), 0,
                                     pack_cnt_flags(0, term ? kFlagTerminal : 0)};
         const unsigned long long key =
-            rank_key(ucb_score(st, nleafN, v.c_puct, v.vl_value, v.enable_vl), j);
+            rank_key(ucb_score_sq(st, sq_leaf, v.c_puct, v.vl_value, v.enable_vl), j);
         best = key > best ? key : best;
       }
       best = warp_max_u64(best);
