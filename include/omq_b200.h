@@ -104,6 +104,9 @@ OMQ_API const char* omq_status_string(int status);
 OMQ_API const char* omq_last_error(void); /* thread-local detail for the last non-OK status */
 /* Number of kernels this library has launched in the calling process so far. */
 OMQ_API int omq_kernel_launches(uint64_t* h_count);
+/* Adjust that count by delta: a CUDA graph capture records launches without running them (-n),
+ * each replay of the graph runs them (+n). */
+OMQ_API int omq_kernel_launches_add(int64_t delta);
 
 /* Allocates all device memory of the engine (trees + per-wave scratch + queues).
  * Replaces CSRTree(CSRTreeConfig) (csr_tree.py:86) and WaveSearch.allocate_buffers (:414). */

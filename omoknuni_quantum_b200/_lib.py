@@ -105,6 +105,7 @@ SIGNATURES = {
     "omq_resnet_profile": [_P, _I],
     "omq_resnet_profile_read": [_P, ctypes.POINTER(_I), _P, _P, _I],
     "omq_kernel_launches": [ctypes.POINTER(ctypes.c_uint64)],
+    "omq_kernel_launches_add": [ctypes.c_int64],
     "omq_resnet_forward_noalloc": [ctypes.POINTER(ResNetConfig), _P, _P, _P, _P, _I, _P, _P, _P],
 }
 _RESTYPES = {"omq_status_string": ctypes.c_char_p, "omq_last_error": ctypes.c_char_p}
@@ -134,6 +135,10 @@ def load(build_if_missing: bool = True):
         fn.restype = _RESTYPES.get(name, ctypes.c_int)
     _lib = L
     return L
+
+
+def add_kernel_launches(delta: int) -> None:
+    check(load().omq_kernel_launches_add(int(delta)), "omq_kernel_launches_add")
 
 
 def kernel_launches() -> int:

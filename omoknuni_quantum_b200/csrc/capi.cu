@@ -58,6 +58,11 @@ const char* omq_status_string(int s) {
 
 const char* omq_last_error(void) { return g_err; }
 
+int omq_kernel_launches_add(int64_t delta) {
+  g_launches.fetch_add((unsigned long long)delta, std::memory_order_relaxed);
+  return OMQ_OK;
+}
+
 int omq_kernel_launches(uint64_t* h_count) {
   if (!h_count) { set_error("null argument"); return OMQ_BAD_ARG; }
   *h_count = g_launches.load();

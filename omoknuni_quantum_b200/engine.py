@@ -88,6 +88,7 @@ class WaveEngine:
             _lib.check(self.L.omq_engine_create(ctypes.byref(cfg), ctypes.byref(h)), "omq_engine_create")
         self._h = h
         self.queue_capacity = self.num_trees * self.max_wave_size
+        self._graphs = {}
         self._features = None
         self._visits = torch.zeros(self.num_trees, self.actions, dtype=torch.int32, device=dev)
         self._root_nw = torch.zeros(self.num_trees, 2, dtype=torch.float32, device=dev)
@@ -96,6 +97,7 @@ class WaveEngine:
 
     # -- lifetime ------------------------------------------------------------------------------
     def close(self):
+        getattr(self, "_graphs", {}).clear()     # graphs point into the engine's memory
         if getattr(self, "_h", None) and self._h.value:
             self.L.omq_engine_destroy(self._h)
             self._h = ctypes.c_void_p()
@@ -249,8 +251,25 @@ class WaveEngine:
         self.evaluate_queue(_lib.QUEUE_FINAL, evaluator)
         _lib.check(self.L.omq_wave_backup(self._h, s), "omq_wave_backup")
 
+    def _wave_graph(self, w: int, evaluator):
+        """CUDA graph of one wave of size w with an on-device evaluator (captured on first use;
+        keyed by the evaluator and its buffer generation, so a re-created net is recaptured)."""
+        key = (w, id(evaluator), getattr(evaluator, "generation", 0))
+        ent = self._graphs.get(key)
+        if ent is None:
+            for k in [k for k in self._graphs if k[:2] == key[:2]]:
+                del self._graphs[k]                # captured against an earlier net
+            n0 = _lib.kernel_launches()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.wave(w, evaluator)
+            n = _lib.kernel_launches() - n0
+            _lib.add_kernel_launches(-n)          # recorded, not run
+            ent = self._graphs[key] = (g, n, evaluator)
+        return ent
+
     def search(self, boards: torch.Tensor, num_simulations: int, evaluator="synthetic",
-               meta=None, keys=None) -> None:
+               meta=None, keys=None, graphs: bool = False) -> None:
         """begin + forced root expansion + ceil(sims / max_wave_size) waves
         (python/mcts/core/mcts.py:1020-1063). Raises on a device status (e.g. TreeFullError).
         Go engines take history boards and ``meta`` (see ``begin``)."""
@@ -282,10 +301,20 @@ class WaveEngine:
             return
         self.begin(boards, meta, keys)
         self.root_expand(evaluator)
+        # full-size waves replay a CUDA graph when asked (MCTSConfig.use_cuda_graphs) and the
+        # evaluator runs on the device queue (no host round trip inside a wave)
+        graphed = graphs and hasattr(evaluator, "forward_queue")
         done = 0
         while done < num_simulations:
             w = min(self.max_wave_size, num_simulations - done)
-            self.wave(w, evaluator)
+            if graphed and w == self.max_wave_size:
+                if hasattr(evaluator, "_ensure"):
+                    evaluator._ensure(self.queue_capacity)
+                g, n, _ = self._wave_graph(w, evaluator)
+                g.replay()
+                _lib.add_kernel_launches(n)
+            else:
+                self.wave(w, evaluator)
             done += w
         self.check_status()
 

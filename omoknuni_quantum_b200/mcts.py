@@ -77,6 +77,12 @@ class MCTS:
                           last_search_sims_per_second=0.0, peak_sims_per_second=0.0,
                           avg_sims_per_second=0.0)
 
+    @property
+    def _graphs_on(self) -> bool:
+        """MCTSConfig.use_cuda_graphs (reference default True): full-size waves replay a captured
+        CUDA graph when the evaluator runs on the device queue."""
+        return bool(getattr(self.config, "use_cuda_graphs", True))
+
     # -- engines -------------------------------------------------------------------------------
     @property
     def action_size(self) -> int:
@@ -175,7 +181,7 @@ class MCTS:
         t0 = time.perf_counter()
         rec = np.stack([r[0] for r in roots])
         npr = np.array([r[1] for r in roots], np.int32)
-        eng.search(rec, sims, self._eval, meta=npr)
+        eng.search(rec, sims, self._eval, meta=npr, graphs=self._graphs_on)
         visits = eng.root_visits().cpu().numpy()
         self._last_tree = (eng, 0)
         self._update_statistics(sims * R, time.perf_counter() - t0)
@@ -194,7 +200,8 @@ class MCTS:
         t0 = time.perf_counter()
         hist = torch.from_numpy(np.stack([r[0] for r in roots])).to(self.device)
         meta = torch.from_numpy(np.stack([r[1] for r in roots])).to(self.device)
-        eng.search(hist, sims, self._eval, meta=meta, keys=[r[2] for r in roots])
+        eng.search(hist, sims, self._eval, meta=meta, keys=[r[2] for r in roots],
+                   graphs=self._graphs_on)
         visits = eng.root_visits().cpu().numpy()
         self._last_tree = (eng, 0)
         self._update_statistics(sims * R, time.perf_counter() - t0)
@@ -233,7 +240,7 @@ class MCTS:
             dev_boards = boards.to(self.device, torch.int8, non_blocking=True)
         else:
             dev_boards = torch.from_numpy(np.ascontiguousarray(boards)).to(self.device)
-        eng.search(dev_boards, sims, self._eval)
+        eng.search(dev_boards, sims, self._eval, graphs=self._graphs_on)
         visits = eng.root_visits().cpu().numpy()
         dt = time.perf_counter() - t0
         self._last_tree = (eng, 0)

@@ -189,6 +189,7 @@ class ResNetEvaluator:
         self.L = _lib.load()
         self._net = None
         self._max_batch = 0
+        self.generation = 0     # bumped whenever the device net (and its buffers) is re-created
         self._ensure(max_batch)
         self._return_torch_tensors = True
 
@@ -213,6 +214,7 @@ class ResNetEvaluator:
             _lib.check(self.L.omq_resnet_create(ctypes.byref(cfg), ctypes.byref(h)), "omq_resnet_create")
             self._net = h
             self._max_batch = int(max_batch)
+            self.generation += 1
             conv_w, conv_b, head = pack_parameters(self.state_dict, s)
             a, b, c = (ctypes.c_uint64() for _ in range(3))
             _lib.check(self.L.omq_resnet_param_sizes(h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c)),

@@ -203,3 +203,29 @@ def test_root_dirichlet_noise_replays_bit_exact_in_oracle(oracle_lib):
     e0.search(torch.from_numpy(board[None]).cuda(), waves * wave)
     o0 = oracle_lib.Oracle(60000).search(board, waves * wave, wave)
     assert np.array_equal(e0.export_tree(0)["visits"], o0.visits)
+
+
+def test_cuda_graph_waves_equal_plain_waves():
+    """WaveEngine.search(graphs=True) replays a captured wave: identical trees to the plain
+    launches, for several searches in a row and a partial last wave; the launch counter counts
+    each replay's kernels once."""
+    from omoknuni_quantum_b200 import _lib
+    from omoknuni_quantum_b200.engine import WaveEngine
+    from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec
+    from omoknuni_quantum_b200.roots import random_root
+    ev = ResNetEvaluator.random(ResNetSpec(num_blocks=2, filters=128), seed=5, max_batch=512)
+    b = torch.from_numpy(np.stack([random_root(70 + i) for i in range(2)])).cuda()
+    plain, graph = WaveEngine(2, capacity=80000, max_wave_size=64), WaveEngine(2, capacity=80000, max_wave_size=64)
+    for sims in (200, 256, 200):
+        n0 = _lib.kernel_launches()
+        plain.search(b, sims, ev)
+        n_plain = _lib.kernel_launches() - n0
+        n0 = _lib.kernel_launches()
+        graph.search(b, sims, ev, graphs=True)
+        n_graph = _lib.kernel_launches() - n0
+        for r in range(2):
+            a, c = plain.export_tree(r), graph.export_tree(r)
+            for k in ("parent", "action", "priors", "visits", "value_sums", "terminal"):
+                assert np.array_equal(a[k], c[k]), (sims, k)
+        assert n_graph == n_plain, (n_graph, n_plain)
+    assert len(graph._graphs) == 1
