@@ -603,10 +603,14 @@ def run_b200_go(args, game="go"):
     avg_launch_s = float(trunk_ms.sum()) / 1000.0 / max(1, conv_launches)
     achieved = (flops / max(1, conv_launches)) / avg_launch_s / 1e12 if avg_launch_s > 0 else 0.0
     peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    # DRAM bytes per launch: the committed ncu capture of this kernel on the same board shape
+    # (profiles/conv3x3_pair256_go_chess.md), scaled by the positions a launch processes
+    per_pos = profile_value("conv3x3_pair256_go_chess.md", f"dram_bytes_per_position_per_launch_{game}")
+    traffic = per_pos * positions / len(trunk_ms) if per_pos is not None and len(trunk_ms) else None
     roofline = {"kernel": f"k_conv3x3_pair<256> (tcgen05 cta_group::2 implicit-GEMM 3x3 conv, "
                           f"{n_board + 1}x{n_board + 1} padded pixel grid)", "bound": "tensor", "achieved": achieved, "peak": peak,
                 "unit": "TFLOP/s", "frac": achieved / peak,
-                "peak_kind": f"bf16_tflops_sustained of {peak_kind}", "traffic": None,
+                "peak_kind": f"bf16_tflops_sustained of {peak_kind}", "traffic": traffic,
                 "algorithmic_flops_per_launch": flops / max(1, conv_launches),
                 "avg_launch_ms": avg_launch_s * 1e3, "launches": conv_launches}
 
