@@ -1076,7 +1076,12 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
       }
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer: A = weights (M = 128 channels), B = pixel window (N = 256) ----
-    constexpr uint32_t idesc = ptx::idesc_bf16_f32(BN, Cfg::kRows);
+    // When a tile is exactly one position (P = 256: the 16x16 grid of a 15x15 board) its last grid
+    // row is the zero pad row: no real output reads past pixel 255 of the tile (largest tap shift
+    // S + 2 from pixel 14*16 + 14), and the pad row's outputs are written as zeros by the
+    // epilogue, so the UMMAs cover only the first 256 - 16 = 240 pixel columns.
+    const uint32_t idesc =
+        ptx::idesc_bf16_f32(BN, args.P == Cfg::kRows ? Cfg::kRows - rowstride : Cfg::kRows);
     const uint64_t w_desc0 = ptx::smem_desc_sw128(ptx::smem_u32(w_ring));
     int sx = 0, sw = 0;
     uint32_t px = 0, pw = 0;
