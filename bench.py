@@ -504,6 +504,9 @@ def run_b200_selfplay(args):
     peaks, kind = measured_peaks()
     launches = len(trunk_ms) * ev.conv_launches_per_call
     flops = int(counts.sum()) * ev.trunk_flops_per_position()
+    # DRAM bytes per launch from the committed capture of this kernel on 15x15 boards
+    per_pos = profile_value("conv3x3_pair256_go_chess.md", "dram_bytes_per_position_per_launch_gomoku")
+    traffic = per_pos * int(counts.sum()) / len(trunk_ms) if per_pos is not None and len(trunk_ms) else None
     avg_s = float(trunk_ms.sum()) / 1000.0 / max(1, launches)
     achieved = flops / max(1, launches) / avg_s / 1e12 if avg_s > 0 else 0.0
     peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
@@ -519,7 +522,7 @@ def run_b200_selfplay(args):
             "leaf_evals_per_s": int(counts.sum()) * ws / (ms / 1000.0),
             "roofline": {"kernel": "k_conv3x3_pair<256> (cta_group::2 tcgen05 conv)", "bound": "tensor",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                         "peak_kind": f"bf16_tflops_sustained of {kind}", "traffic": None},
+                         "peak_kind": f"bf16_tflops_sustained of {kind}", "traffic": traffic},
             "cpu_baseline": None, "e2e": None, "clocks": clk.summary(),
             "gpu_launches": _lib.kernel_launches() - n0}), flush=True)
     if ws > 1:

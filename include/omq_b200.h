@@ -304,6 +304,9 @@ OMQ_API int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const uint1
                                        const float* d_conv_b, const float* d_head,
                                        const float* d_features, int32_t batch, float* d_policy,
                                        float* d_value, void* stream);
+/* Self-test of the bounded device waits: launches a kernel whose mbarrier wait can never complete;
+ * after limit_ns (at most 1 s) it gives up and writes OMQ_TIMEOUT to d_status (int32, device). */
+OMQ_API int omq_selftest_wait_timeout(uint64_t limit_ns, int32_t* d_status, void* stream);
 /* Device error word of the net (OMQ_TIMEOUT after a bounded wait gave up); synchronizes. */
 OMQ_API int omq_resnet_error(omq_resnet* net, int32_t* h_error, void* stream);
 

@@ -1807,6 +1807,24 @@ static int head_pos(const omq_resnet* n) {
   return 8;
 }
 
+// Self-test of the bounded wait every pipelined kernel here uses: one thread waits on an mbarrier
+// that nothing arrives on. After limit_ns the wait gives up and raises the abort flag, and the
+// kernel stores OMQ_TIMEOUT in *status and returns, leaving the context usable.
+__global__ void k_selftest_wait(uint64_t limit_ns, int32_t* status) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(&bar, 1);
+    abort_flag = 0;
+    ptx::fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool ok = ptx::mbar_wait(&bar, 0, &abort_flag, limit_ns);
+    *status = ok ? OMQ_OK : (abort_flag ? OMQ_TIMEOUT : OMQ_CUDA_ERROR);
+  }
+}
+
 extern "C" {
 
 int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
@@ -2316,6 +2334,16 @@ int omq_resnet_profile_read(omq_resnet* n, int32_t* h_calls, float* h_trunk_ms, 
       if (n->prof_host_counts[i] >= 0) h_counts[i] = n->prof_host_counts[i];
   }
   return cuda_status(e, "omq_resnet_profile_read");
+}
+
+int omq_selftest_wait_timeout(uint64_t limit_ns, int32_t* d_status, void* stream) {
+  if (!d_status || limit_ns == 0 || limit_ns > 1000000000ull) {
+    set_error("omq_selftest_wait_timeout: d_status null or limit outside (0, 1 s]");
+    return OMQ_BAD_ARG;
+  }
+  count_launches(1);
+  k_selftest_wait<<<1, 32, 0, (cudaStream_t)stream>>>(limit_ns, d_status);
+  return cuda_status(cudaGetLastError(), "k_selftest_wait");
 }
 
 int omq_resnet_error(omq_resnet* n, int32_t* h_error, void* stream) {

@@ -229,3 +229,26 @@ def test_cuda_graph_waves_equal_plain_waves():
                 assert np.array_equal(a[k], c[k]), (sims, k)
         assert n_graph == n_plain, (n_graph, n_plain)
     assert len(graph._graphs) == 1
+
+
+def test_bounded_wait_times_out_and_context_stays_usable(oracle_lib):
+    """A device wait that can never complete (an mbarrier nothing arrives on) gives up after its
+    limit and reports OMQ_TIMEOUT through device memory; the context then runs a normal search."""
+    import ctypes
+    import time
+    from omoknuni_quantum_b200 import _lib
+    from omoknuni_quantum_b200.engine import WaveEngine, _stream_ptr
+    from omoknuni_quantum_b200.roots import random_root
+    status = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    t0 = time.perf_counter()
+    _lib.check(_lib.load().omq_selftest_wait_timeout(20_000_000, ctypes.c_void_p(status.data_ptr()),
+                                                     _stream_ptr()), "omq_selftest_wait_timeout")
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    assert int(status.item()) == 3            # OMQ_TIMEOUT
+    assert 0.015 < dt < 5.0
+    board = random_root(77)
+    eng = WaveEngine(1, capacity=40000, max_wave_size=64)
+    eng.search(torch.from_numpy(board[None]).cuda(), 128)
+    o = oracle_lib.Oracle(40000).search(board, 128, 64)
+    assert np.array_equal(eng.export_tree(0)["visits"], o.visits)
