@@ -98,9 +98,9 @@ class MCTS:
 
     def _engine(self, num_trees: int, go_rules: str = "chinese") -> WaveEngine:
         eng = self._engines.get(num_trees)
-        if eng is not None and self._pending is eng and self.is_go and getattr(eng, "go_rules", "chinese") != go_rules:
-            self._pending = None
         if eng is not None and self.is_go and getattr(eng, "go_rules", "chinese") != go_rules:
+            if self._pending is eng:          # its tree goes with it
+                self._pending = None
             eng.close()
             eng = None
         if eng is None:
