@@ -42,14 +42,35 @@ class GameRecord:
     examples: List[dict] = field(default_factory=list)
     winner: int = 0          # +1 black (player 1) won, -1 white won, 0 draw / unfinished
     finished: bool = False
+    resigned: bool = False
 
-    def training_examples(self) -> List[GameExample]:
+    def training_examples(self, use_mcts_q_values: bool = False,
+                          q_value_weight: float = 0.8) -> List[GameExample]:
+        """The game outcome from each example's player's perspective (self_play_manager.py:
+        400-431); with ``use_mcts_q_values`` mixed as q_value_weight * root value of that move's
+        search + (1 - q_value_weight) * outcome."""
         out = []
         for ex in self.examples:
             v = self.winner if ex["player"] == 1 else -self.winner
+            if use_mcts_q_values:
+                v = q_value_weight * ex.get("value_pred", 0.0) + (1 - q_value_weight) * v
             out.append(GameExample(state=ex["state"], policy=ex["policy"], value=float(v),
                                    game_id=self.game_id, move_number=ex["move_number"]))
         return out
+
+    def metrics(self) -> Dict[str, object]:
+        """Per-game metrics of the reference's play_game (self_play_manager.py:263-270, 433-462):
+        policy entropies, sign accuracy of the root values against the outcome (|v| < 0.1 for a
+        draw), game length, winner, resignation."""
+        ent, acc = [], []
+        for ex in self.examples:
+            p = ex["policy"][ex["policy"] > 1e-10]
+            ent.append(float(-(p * np.log(p)).sum()) if len(p) else 0.0)
+            actual = self.winner if ex["player"] == 1 else -self.winner
+            vp = ex.get("value_pred", 0.0)
+            acc.append((1.0 if abs(vp) < 0.1 else 0.0) if actual == 0 else (1.0 if vp * actual > 0 else 0.0))
+        return {"resigned": self.resigned, "policy_entropies": ent, "value_accuracies": acc,
+                "game_length": len(self.examples), "winner": self.winner}
 
 
 def board_after(board: np.ndarray, action: int) -> np.ndarray:
@@ -184,7 +205,8 @@ class BatchedSelfPlay:
                  temperature: float = 1.0, temperature_threshold: int = 30, seed: int = 0,
                  roots=None, board_size: int = 15,
                  search: Optional[Callable] = None, device=None, game: str = "gomoku",
-                 subtree_reuse: str = "none"):
+                 subtree_reuse: str = "none", enable_resign: bool = True,
+                 resign_threshold: float = -0.98, resign_min_move: int = 10):
         if game not in _GAMES:
             raise ValueError(f"unknown game {game!r}")
         if subtree_reuse not in ("none", "carry", "keep"):
@@ -194,6 +216,10 @@ class BatchedSelfPlay:
         # use_gpu_tree_reuse behaviour); only while the set of live games is unchanged, so that
         # tree r still belongs to the same game
         self.subtree_reuse = subtree_reuse
+        # resignation as SelfPlayGame (self_play_manager.py:350-365; SelfPlayConfig defaults)
+        self.enable_resign = bool(enable_resign)
+        self.resign_threshold = float(resign_threshold)
+        self.resign_min_move = int(resign_min_move)
         self._last_move = None          # (live games, their moves) of the previous step
         self._live_now = None
         self.game = _GAMES[game](board_size)
@@ -235,7 +261,9 @@ class BatchedSelfPlay:
             eng.search(torch.from_numpy(np.ascontiguousarray(roots)).to(eng.device), self.sims, self._evaluator)
         else:
             eng.search(roots, self.sims, self._evaluator, **kw)
-        return eng.root_visits().cpu().numpy()
+        nw = eng.root_nw().cpu().numpy()
+        values = np.where(nw[:, 0] > 0, nw[:, 1] / np.maximum(nw[:, 0], 1), 0.0)
+        return eng.root_visits().cpu().numpy(), values
 
     def live(self) -> np.ndarray:
         return np.array([not r.finished for r in self.records])
@@ -250,7 +278,13 @@ class BatchedSelfPlay:
         self._live_now = tuple(int(g) for g in live)
         moves = []
         roots, meta = self.game.engine_input([self.positions[g] for g in live])
-        visits = np.asarray(search(roots if meta is None else (roots, meta)))
+        res = search(roots if meta is None else (roots, meta))
+        # a search returns the root visits, or (visits, root values) - the root value W / N is
+        # MCTS.get_root_value(), from the side to move's perspective
+        if isinstance(res, tuple):
+            visits, values = np.asarray(res[0]), np.asarray(res[1], np.float64)
+        else:
+            visits, values = np.asarray(res), np.zeros(len(live))
         for i, g in enumerate(live):
             v = visits[i].astype(np.float64)
             tot = v.sum()
@@ -259,7 +293,8 @@ class BatchedSelfPlay:
             player = self.game.player(pos)
             rec = self.records[g]
             rec.examples.append({"state": self.game.state(pos), "policy": policy, "player": player,
-                                 "move_number": self.move_number})
+                                 "move_number": self.move_number,
+                                 "value_pred": float(values[i])})
             if self.move_number < self.temperature_threshold and self.temperature > 0:
                 p = policy if self.temperature == 1.0 else np.power(policy, 1.0 / self.temperature)
                 p = p / p.sum()
@@ -273,6 +308,13 @@ class BatchedSelfPlay:
             if res is not None:
                 rec.finished = True
                 rec.winner = res
+            # resignation after the move (the reference checks it even when the move ended the
+            # game, and the resignation then decides the winner): the player who moved resigns
+            if (self.enable_resign and self.move_number + 1 > self.resign_min_move
+                    and values[i] < self.resign_threshold):
+                rec.finished = True
+                rec.resigned = True
+                rec.winner = -1 if player == 1 else 1
         self._last_move = (self._live_now, moves)
         self.move_number += 1
         return len(live)

@@ -111,3 +111,29 @@ def test_chess_selfplay_plays_legal_games():
         for a in r.moves:
             p.play(p.action_to_move(a))
         assert p.fen() == sp.positions[g].fen()
+
+
+def test_resignation_q_values_and_metrics():
+    """SelfPlayGame's resignation (self_play_manager.py:350-393): after move resign_min_move + 1
+    a root value below the threshold makes the player who just moved resign and lose; training
+    values mix the root values with use_mcts_q_values; metrics as the reference's play_game."""
+    def losing(boards):
+        # black's root values are fine, white's are lost (< -0.98) from its own perspective
+        vals = np.array([0.5 if int((b != 0).sum()) % 2 == 0 else -0.99 for b in boards])
+        return _fake_search(boards), vals
+    sp = BatchedSelfPlay(2, search=losing, temperature_threshold=0, seed=1, resign_min_move=4)
+    recs = sp.play(20)
+    for r in recs:
+        assert r.finished and r.resigned
+        # white moves at move numbers 1, 3, 5 ...: the first white move with move_count > 4
+        assert len(r.moves) == 6 and r.winner == 1
+        ex = r.training_examples()
+        assert [e.value for e in ex] == [1.0, -1.0] * 3
+        mixed = r.training_examples(use_mcts_q_values=True, q_value_weight=0.8)
+        assert abs(mixed[0].value - (0.8 * 0.5 + 0.2 * 1.0)) < 1e-12
+        assert abs(mixed[1].value - (0.8 * -0.99 + 0.2 * -1.0)) < 1e-12
+        m = r.metrics()
+        assert m["resigned"] and m["game_length"] == 6 and m["winner"] == 1
+        assert m["value_accuracies"] == [1.0] * 6 and len(m["policy_entropies"]) == 6
+    off = BatchedSelfPlay(2, search=losing, temperature_threshold=0, seed=1, enable_resign=False)
+    assert not any(r.resigned for r in off.play(8))
