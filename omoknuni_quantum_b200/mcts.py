@@ -301,6 +301,27 @@ class MCTS:
         if new_state is not None:
             self._root_state = new_state if (self.is_go or self.is_chess) else self._boards(new_state)
 
+    def update_with_move(self, move: int) -> None:
+        """mcts.py update_with_move: update_root(move, None)."""
+        self.update_root(move, None)
+
+    def warmup(self, num_searches: int = 3, simulations_per_search: int = 100) -> None:
+        """mcts.py warmup: a few searches of the initial position before timed use (engine
+        allocation, kernel attributes, the wave graph); the tree and statistics are reset after."""
+        if self.is_go:
+            from .go import GoPosition
+            state = GoPosition(self.config.board_size)
+        elif self.is_chess:
+            from .chess import ChessPosition
+            state = ChessPosition()
+        else:
+            state = np.zeros((self.config.board_size, self.config.board_size), np.int8)
+        saved = dict(self.stats)
+        for _ in range(max(0, int(num_searches))):
+            self.search(state, num_simulations=int(simulations_per_search))
+        self.clear()
+        self.stats = saved
+
     def clear(self) -> None:
         self._drop_pending()
         self._last_tree = None

@@ -136,3 +136,11 @@ def test_mcts_chess_roots_from_positions_fens_and_move_histories():
     r3, n3 = m._chess_root(p.fen())
     assert np.array_equal(r3[0], r2[0]) and n3 == 0      # a FEN carries no earlier positions
     assert random_position(3).record()["side"] in (1, 2)
+
+
+def test_reference_method_surface():
+    """Every public method of the reference MCTS class (python/mcts/core/mcts.py) exists here."""
+    from omoknuni_quantum_b200 import MCTS
+    for name in ("search", "search_batch", "select_action", "update_root", "update_with_move",
+                 "get_root_value", "get_statistics", "clear", "reset_tree", "warmup", "shutdown"):
+        assert callable(getattr(MCTS, name, None)), name
