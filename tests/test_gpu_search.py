@@ -252,3 +252,16 @@ def test_bounded_wait_times_out_and_context_stays_usable(oracle_lib):
     eng.search(torch.from_numpy(board[None]).cuda(), 128)
     o = oracle_lib.Oracle(40000).search(board, 128, 64)
     assert np.array_equal(eng.export_tree(0)["visits"], o.visits)
+
+
+def test_warmup_and_update_with_move(oracle_lib):
+    from omoknuni_quantum_b200 import MCTS, MCTSConfig, SyntheticEvaluator
+    from omoknuni_quantum_b200.roots import random_root
+    m = MCTS(MCTSConfig(num_simulations=192, max_wave_size=64, dirichlet_epsilon=0.0,
+                        initial_tree_nodes=60000), SyntheticEvaluator())
+    m.warmup(2, 64)
+    assert m.get_statistics()["total_searches"] == 0
+    b = random_root(88)
+    p = m.search(b)
+    assert np.array_equal(p, oracle_lib.Oracle(60000).search(b, 192, 64).policy)
+    m.update_with_move(int(np.argmax(p)))
