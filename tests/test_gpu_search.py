@@ -265,3 +265,30 @@ def test_warmup_and_update_with_move(oracle_lib):
     p = m.search(b)
     assert np.array_equal(p, oracle_lib.Oracle(60000).search(b, 192, 64).policy)
     m.update_with_move(int(np.argmax(p)))
+
+
+@pytest.mark.parametrize("n", [9, 19])
+def test_gomoku_other_board_sizes_match_oracle(oracle_lib, n):
+    """Gomoku on 9x9 and 19x19 (MCTSConfig.board_size): device trees equal the oracle's, and the
+    ResNet on the (n+1)^2 padded grid matches the fp32 reference forward."""
+    from omoknuni_quantum_b200.engine import WaveEngine
+    from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec, init_state_dict, reference_forward_fp32
+    from omoknuni_quantum_b200.roots import random_root
+    boards = np.stack([random_root(300 + i, stones=10, board_size=n) for i in range(3)])
+    eng = WaveEngine(3, board_size=n, capacity=100000, max_wave_size=64)
+    eng.search(torch.from_numpy(boards).cuda(), 256)
+    for r in range(3):
+        o = oracle_lib.Oracle(100000, n).search(boards[r], 256, 64)
+        t = eng.export_tree(r)
+        for k in ("parent", "action", "priors", "visits", "value_sums", "terminal"):
+            assert np.array_equal(t[k], getattr(o, k)), (n, r, k)
+    spec = ResNetSpec(board_size=n, num_blocks=2, filters=128, num_actions=n * n)
+    sd = init_state_dict(spec, seed=4)
+    ev = ResNetEvaluator(sd, board_size=n, max_batch=256)
+    g = np.random.default_rng(n)
+    x = torch.zeros(100, 19, n, n)
+    x[:, 0] = torch.from_numpy((g.random((100, n, n)) < 0.3).astype(np.float32))
+    x[:, 1] = 1.0
+    p, v = ev.evaluate_batch(x.cuda())
+    pr, vr = reference_forward_fp32({k: t.cuda() for k, t in sd.items()}, x.cuda())
+    assert (p - pr).abs().max().item() < 2e-2 and (v - vr).abs().max().item() < 2e-2
