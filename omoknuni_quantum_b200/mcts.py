@@ -132,7 +132,18 @@ class MCTS:
             if state.shape[-2:] != (n, n):
                 raise ValueError(f"Invalid state shape: {state.shape}, expected {(n, n)}")
             return state.astype(np.int8, copy=False)
-        raise TypeError("state must be a numpy/torch board [n, n] with 0 empty, 1 black, 2 white")
+        if hasattr(state, "get_move_history"):
+            # a reference IGameState (mcts.py:1520-1580 rebuilds its board from the tensor
+            # planes): replay its moves on the empty board, black first
+            b = np.zeros((n, n), np.int8)
+            for i, m in enumerate(state.get_move_history()):
+                m = int(m)
+                if not 0 <= m < n * n or b.reshape(-1)[m] != 0:
+                    raise ValueError(f"move {m} of the state's history is not playable")
+                b.reshape(-1)[m] = 1 if i % 2 == 0 else 2
+            return b
+        raise TypeError("state must be a numpy/torch board [n, n] with 0 empty, 1 black, 2 white, "
+                        "or a game state with get_move_history()")
 
     def _go_root(self, state):
         """(history int8 [8, n, n], meta int32 [3], superko keys) of a Go root: a GoPosition of this package,

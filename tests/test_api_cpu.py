@@ -144,3 +144,16 @@ def test_reference_method_surface():
     for name in ("search", "search_batch", "select_action", "update_root", "update_with_move",
                  "get_root_value", "get_statistics", "clear", "reset_tree", "warmup", "shutdown"):
         assert callable(getattr(MCTS, name, None)), name
+
+
+def test_gomoku_state_objects_are_replayed():
+    from omoknuni_quantum_b200 import MCTS, MCTSConfig, SyntheticEvaluator
+
+    class State:                      # the IGameState surface the drop-in uses
+        def get_move_history(self):
+            return [112, 113, 97]
+
+    m = MCTS(MCTSConfig(num_simulations=8), SyntheticEvaluator())
+    b = m._boards(State())
+    assert b.reshape(-1)[112] == 1 and b.reshape(-1)[113] == 2 and b.reshape(-1)[97] == 1
+    assert int((b != 0).sum()) == 3
