@@ -59,7 +59,9 @@ __device__ __forceinline__ int64_t exp_step(uint64_t r) {
   return (s * 160) >> 16;
 }
 
-__constant__ uint32_t c_exp2[64] = {
+// In global memory, read through the read-only cache: lanes index it with different values,
+// which the constant cache would serialise.
+__device__ const uint32_t c_exp2[64] = {
     1048576u,1059994u,1071537u,1083205u,1095000u,1106924u,1118978u,1131163u,1143480u,1155932u,
     1168519u,1181244u,1194106u,1207109u,1220254u,1233542u,1246974u,1260553u,1274279u,1288155u,
     1302182u,1316362u,1330696u,1345187u,1359835u,1374642u,1389611u,1404743u,1420040u,1435503u,
@@ -79,7 +81,7 @@ __device__ __forceinline__ uint64_t div_floor53(uint64_t n, uint64_t d, double r
 }
 
 __device__ __forceinline__ uint64_t exp2_fixed(int64_t t) {
-  return (uint64_t)c_exp2[t & 63] << ((t >> 6) + 6);
+  return (uint64_t)__ldg(&c_exp2[t & 63]) << ((t >> 6) + 6);
 }
 
 // Built-in synthetic evaluator (integer-exact definition: policy on a 2^-24 grid with distinct
