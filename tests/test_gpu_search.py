@@ -292,3 +292,21 @@ def test_gomoku_other_board_sizes_match_oracle(oracle_lib, n):
     p, v = ev.evaluate_batch(x.cuda())
     pr, vr = reference_forward_fp32({k: t.cuda() for k, t in sd.items()}, x.cuda())
     assert (p - pr).abs().max().item() < 2e-2 and (v - vr).abs().max().item() < 2e-2
+
+
+def test_backup_sign_convention_on_device():
+    """test_mcts_phases_detailed.py:578-616 on the device through the evaluator protocol."""
+    from omoknuni_quantum_b200.engine import WaveEngine
+
+    class Const:
+        def evaluate_batch(self, x):
+            n = x.shape[0]
+            return torch.full((n, 225), 1.0 / 225, device=x.device), torch.full((n,), 0.5, device=x.device)
+
+    eng = WaveEngine(1, capacity=20000, max_wave_size=1)
+    eng.search(torch.zeros(1, 15, 15, dtype=torch.int8).cuda(), 1, evaluator=Const())
+    t = eng.export_tree(0)
+    leaf = int(np.nonzero(t["visits"][1:])[0].max()) + 1
+    child = int(t["parent"][leaf])
+    assert t["parent"][child] == 0
+    assert (t["value_sums"][0], t["value_sums"][child], t["value_sums"][leaf]) == (0.5, -0.5, 0.5)

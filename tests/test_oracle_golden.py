@@ -67,3 +67,24 @@ def test_synthetic_evaluator_numpy_equals_c(oracle_lib):
         assert len(np.unique(vals)) == len(vals)
         assert vals.sum() <= 2 ** 24
     assert np.array_equal(v1 * 4096, np.round(v1 * 4096)) and np.all(np.abs(v1) < 1)
+
+
+def _const_eval(v):
+    def ev(features):
+        n = features.shape[0]
+        return np.full((n, 225), 1.0 / 225, np.float32), np.full(n, v, np.float32)
+    return ev
+
+
+def test_backup_sign_convention_three_node_path(oracle_lib):
+    """The reference's own anchor (python/tests/test_mcts_phases_detailed.py:578-616): after one
+    simulation the path root -> child -> leaf holds leaf +v, parent -v, root +v; the policy has
+    225 entries and sums to 1."""
+    board = np.zeros((15, 15), np.int8)
+    t = oracle_lib.Oracle(20000).search(board, 1, 1, evaluator=_const_eval(0.5))
+    leaf = int(np.nonzero(t.visits[1:])[0].max()) + 1
+    child = int(t.parent[leaf])
+    assert t.parent[child] == 0
+    assert (t.visits[0], t.visits[child], t.visits[leaf]) == (1, 1, 1)
+    assert (t.value_sums[0], t.value_sums[child], t.value_sums[leaf]) == (0.5, -0.5, 0.5)
+    assert t.policy.shape == (225,) and abs(t.policy.sum() - 1.0) < 1e-12
