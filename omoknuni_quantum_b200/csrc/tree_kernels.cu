@@ -478,8 +478,54 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
     sh.nleaf = 0; sh.nlog = 1; sh.overflow = 0;
   }
   __syncthreads();
-  int cur = 0;
-  for (int depth = 1; depth < v.max_depth; ++depth) {
+  int cur = 0, depth0 = 1;
+  {
+    // Depth 1 is the root alone. When its simulations take the sorted-children path (more than 8
+    // of them, or more than it has children) and no root noise is mixed in, the whole block
+    // scores, sorts and distributes them instead of one warp; the keys are unique, so the order
+    // - and every result - is the one the warp path gives.
+    const NodeTopo rt = v.topo[base];
+    const int n = topo_count(rt);
+    if (n > 0 && !(v.noise_eps > 0.0f) && !(wave <= n && wave <= 8)) {
+      const int cs = rt.child_start;
+      const float sq = parent_sqrt(v.stats[base].N);
+      unsigned long long* bk = keys_all;                  // p2 >= n entries
+      for (int j = tid; j < p2; j += blockDim.x)
+        bk[j] = j < n ? rank_key(ucb_score_sq(v.stats[base + cs + j], sq, v.c_puct, v.vl_value,
+                                              v.enable_vl), j)
+                      : 0ull;
+      __syncthreads();
+      for (int size = 2; size <= p2; size <<= 1)
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+          for (int i = tid; i < (p2 >> 1); i += blockDim.x) {
+            const int j = 2 * i - (i & (stride - 1)), l = j + stride;
+            const bool desc = (j & size) == 0;
+            const unsigned long long x = bk[j], y = bk[l];
+            if ((x < y) == desc) { bk[j] = y; bk[l] = x; }
+          }
+          __syncthreads();
+        }
+      if (wave <= n) {
+        for (int rr = tid; rr < wave; rr += blockDim.x)
+          emit_child(v, r, F[1], &sh.cnt[1], log, &sh.nlog, &sh.overflow, cs + key_slot(bk[rr]),
+                     rr, 1, 1);
+      } else {
+        const int basek = wave / n, extra = wave % n;
+        for (int rr = tid; rr < n; rr += blockDim.x) {
+          const int c = basek + (rr < extra ? 1 : 0);
+          const int off = rr * basek + (rr < extra ? rr : extra);
+          emit_child(v, r, F[1], &sh.cnt[1], log, &sh.nlog, &sh.overflow, cs + key_slot(bk[rr]),
+                     off, c, 1);
+        }
+      }
+      __syncthreads();
+      if (tid == 0) sh.cnt[0] = 0;
+      cur = 1;
+      depth0 = 2;
+      __syncthreads();
+    }
+  }
+  for (int depth = depth0; depth < v.max_depth; ++depth) {
     const int n_cur = sh.cnt[cur];
     if (n_cur == 0) break;
     const int nwarps = (int)(blockDim.x >> 5);
