@@ -542,7 +542,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
         if (topo_count(ptp) > 0) pn = v.stats[base + pe.node].N;
       }
       const int ng = min(32, (n_cur - g0 + nwarps - 1) / nwarps);
+      // children lane and lane + 32 of the next parent, loaded while this one is scored
+      NodeStats pre0{0, 0.0f, 0.0f, 0}, pre1{0, 0.0f, 0.0f, 0};
+      auto prefetch = [&](int tt) {
+        const int pcs = __shfl_sync(0xFFFFFFFFu, ptp.child_start, tt);
+        const int pnn = topo_count(NodeTopo{0, 0, 0, __shfl_sync(0xFFFFFFFFu, ptp.cnt_flags, tt)});
+        if (lane < pnn) pre0 = v.stats[base + pcs + lane];
+        if (lane + 32 < pnn) pre1 = v.stats[base + pcs + lane + 32];
+      };
+      prefetch(0);
     for (int t = 0; t < ng; ++t) {
+      const NodeStats cur0 = pre0, cur1 = pre1;
+      if (t + 1 < ng) prefetch(t + 1);
       const Visit e{__shfl_sync(0xFFFFFFFFu, pe.node, t), __shfl_sync(0xFFFFFFFFu, pe.lo, t),
                     __shfl_sync(0xFFFFFFFFu, pe.k, t), __shfl_sync(0xFFFFFFFFu, pe.depth, t)};
       const int n = topo_count(NodeTopo{0, 0, 0, __shfl_sync(0xFFFFFFFFu, ptp.cnt_flags, t)});
@@ -583,10 +594,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
           out[topo_action(v.topo[base + cs + j])] = noise;
         }
       } else {
-        // children statistics, four independent 16-byte loads in flight per lane
+        // children statistics: the first two per lane came with the prefetch, the rest four
+        // independent 16-byte loads in flight per lane
         const NodeStats* cst = v.stats + base + cs;
         const float sq = parent_sqrt(np);
-        int j = lane;
+        if (lane < n) keys[lane] = rank_key(ucb_score_sq(cur0, sq, v.c_puct, v.vl_value, v.enable_vl), lane);
+        if (lane + 32 < n)
+          keys[lane + 32] = rank_key(ucb_score_sq(cur1, sq, v.c_puct, v.vl_value, v.enable_vl), lane + 32);
+        int j = lane + 64;
         for (; j + 96 < n; j += 128) {
           const NodeStats s0 = cst[j], s1 = cst[j + 32], s2 = cst[j + 64], s3 = cst[j + 96];
           keys[j] = rank_key(ucb_score_sq(s0, sq, v.c_puct, v.vl_value, v.enable_vl), j);
