@@ -92,7 +92,8 @@ constexpr int kMaxActionsPerLane = 12;  // ceil(362 / 32)
 
 // Policy (queue 0) and value of queue entry q from the position hash h; legal = empty points of
 // `board` plus any action past the board (Go pass). Warp-collective.
-__device__ void synth_emit(const EngineView& v, int queue, int q, uint64_t h, const int8_t* board) {
+template <class Occupied>
+__device__ void synth_emit(const EngineView& v, int queue, int q, uint64_t h, const Occupied& occupied) {
   const int lane = threadIdx.x & 31;
   if (queue == 0) {
     uint64_t wv[kMaxActionsPerLane];
@@ -101,7 +102,7 @@ __device__ void synth_emit(const EngineView& v, int queue, int q, uint64_t h, co
     for (int t = 0; t < kMaxActionsPerLane; ++t) {
       const int a = t * 32 + lane;
       wv[t] = 0;
-      if (a < v.A && (a >= v.C || board[a] == 0)) {
+      if (a < v.A && (a >= v.C || !occupied(a))) {
         wv[t] = exp2_fixed(exp_step(mix64(h + 0x9E3779B97F4A7C15ull * (uint64_t)(a + 1))));
         tot += wv[t];
       }
@@ -113,7 +114,7 @@ __device__ void synth_emit(const EngineView& v, int queue, int q, uint64_t h, co
 #pragma unroll
     for (int t = 0; t < kMaxActionsPerLane; ++t) {
       const int a = t * 32 + lane;
-      const bool legal = a < v.A && (a >= v.C || board[a] == 0);
+      const bool legal = a < v.A && (a >= v.C || !occupied(a));
       const unsigned m = __ballot_sync(0xFFFFFFFFu, legal);
       if (a < v.A) {
         float p = 0.0f;
@@ -135,37 +136,58 @@ __device__ void synth_emit(const EngineView& v, int queue, int q, uint64_t h, co
   }
 }
 
+// Positions per warp in k_synth: the boards are rebuilt one after another by the whole warp, then
+// lane i runs position i's hash chain (a serial chain per position), then the policies are
+// emitted one position at a time.
+constexpr int kSynthGroup = 8;
+
 __global__ void __launch_bounds__(kSynthWarps * 32) k_synth(EngineView v, int queue) {
   __shared__ WarpPos wps[kSynthWarps];
+  __shared__ uint64_t gwords[kSynthWarps][kSynthGroup][kMaxWords];  // occupancy bit boards
+  __shared__ int gmeta[kSynthWarps][kSynthGroup][4];                 // player, move count, depth, last
+  __shared__ uint64_t ghash[kSynthWarps][kSynthGroup];
   const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
-  const int q = blockIdx.x * kSynthWarps + wl;
+  const int q0 = (blockIdx.x * kSynthWarps + wl) * kSynthGroup;
   const int count = v.q_count[queue];
-  if (q >= count) return;
+  if (q0 >= count) return;
+  const int ng = min(kSynthGroup, count - q0);
   WarpPos& wp = wps[wl];
-  const int2 ent = v.q_entries[queue][q];
-  const int r = ent.x, node = ent.y;
-  const int d = warp_rebuild(v, r, node, wp);
-  if (d < 0) { if (lane == 0) v.hdr[r].status = OMQ_BAD_ARG; return; }
-  const TreeHeader& H = v.hdr[r];
-  const int player = (d % 2 == 0) ? H.root_player : 3 - H.root_player;
-  const int mc = H.root_mc + d;
   const int nwords = (v.C + 63) / 64;
-  if (lane < nwords) {
-    uint64_t w = 0;
-    for (int b = 0; b < 64; ++b) {
-      const int c = lane * 64 + b;
-      if (c < v.C && wp.board[c] != 0) w |= 1ull << b;
+  for (int i = 0; i < ng; ++i) {
+    const int2 ent = v.q_entries[queue][q0 + i];
+    const int r = ent.x;
+    const int d = warp_rebuild(v, r, ent.y, wp);
+    if (d < 0) {
+      if (lane == 0) { v.hdr[r].status = OMQ_BAD_ARG; gmeta[wl][i][2] = -1; }
+      __syncwarp();
+      continue;
     }
-    wp.words[lane] = w;
+    // occupancy words: bit b of word j is cell 64 j + b
+    for (int c0 = 0, k = 0; c0 < v.C; c0 += 32, ++k) {
+      const unsigned m = __ballot_sync(0xFFFFFFFFu, c0 + lane < v.C && wp.board[c0 + lane] != 0);
+      if (lane == 0) {
+        if (k & 1) gwords[wl][i][k >> 1] |= (uint64_t)m << 32;
+        else gwords[wl][i][k >> 1] = m;
+      }
+    }
+    if (lane == 0) {
+      const TreeHeader& H = v.hdr[r];
+      gmeta[wl][i][0] = (d % 2 == 0) ? H.root_player : 3 - H.root_player;
+      gmeta[wl][i][1] = H.root_mc + d;
+      gmeta[wl][i][2] = d;
+      gmeta[wl][i][3] = d >= 1 ? wp.acts[d - 1] : -1;
+    }
+    __syncwarp();
   }
-  __syncwarp();
-  uint64_t h = 0;
-  if (lane == 0) {
-    h = 0x243F6A8885A308D3ull;
-    for (int j = 0; j < nwords; ++j) h = mix64(h ^ wp.words[j]);
+  // the hash of the reference feature planes, one chain per lane
+  if (lane < ng && gmeta[wl][lane][2] >= 0) {
+    const uint64_t* w = gwords[wl][lane];
+    const int player = gmeta[wl][lane][0], mc = gmeta[wl][lane][1], d = gmeta[wl][lane][2];
+    const int last = gmeta[wl][lane][3];
+    uint64_t h = 0x243F6A8885A308D3ull;
+    for (int j = 0; j < nwords; ++j) h = mix64(h ^ w[j]);
     h = mix64(h ^ (uint64_t)player);
     const uint32_t hp = history_planes(mc, d, kFullHistoryGomoku);
-    const int last = d >= 1 ? wp.acts[d - 1] : -1;
     for (int c = 2; c < kPlanes; ++c)
       for (int j = 0; j < nwords; ++j) {
         uint64_t word = 0;
@@ -174,9 +196,15 @@ __global__ void __launch_bounds__(kSynthWarps * 32) k_synth(EngineView v, int qu
         }
         h = mix64(h ^ word);
       }
+    ghash[wl][lane] = h;
   }
-  h = __shfl_sync(0xFFFFFFFFu, h, 0);
-  synth_emit(v, queue, q, h, wp.board);
+  __syncwarp();
+  for (int i = 0; i < ng; ++i) {
+    if (gmeta[wl][i][2] < 0) continue;
+    const uint64_t* w = gwords[wl][i];
+    synth_emit(v, queue, q0 + i, ghash[wl][i],
+               [w](int a) { return ((w[a >> 6] >> (a & 63)) & 1ull) != 0; });
+  }
 }
 
 // Reference feature tensor, fp32 [count][19][C]. One warp per queued position.
@@ -297,7 +325,8 @@ __global__ void __launch_bounds__(kGoWarps * 32) k_synth_go(EngineView v, int qu
     for (int i = 0; i < kGoPlanes * nwords; ++i) h = mix64(h ^ w.words[i]);
   }
   h = __shfl_sync(0xFFFFFFFFu, h, 0);
-  synth_emit(v, queue, q, h, w.pos.board);
+  const int8_t* board = w.pos.board;
+  synth_emit(v, queue, q, h, [board](int a) { return board[a] != 0; });
 }
 
 __global__ void __launch_bounds__(kGoWarps * 32) k_features_go(EngineView v, int queue, float* out) {
@@ -468,7 +497,8 @@ void launch_synth_eval(const EngineView& v, int queue, cudaStream_t s) {
     k_synth_chess<<<(cap + kChessWarps - 1) / kChessWarps, kChessWarps * 32, 0, s>>>(v, queue);
     return;
   }
-  k_synth<<<(cap + kSynthWarps - 1) / kSynthWarps, kSynthWarps * 32, 0, s>>>(v, queue);
+  const int per_block = kSynthWarps * kSynthGroup;
+  k_synth<<<(cap + per_block - 1) / per_block, kSynthWarps * 32, 0, s>>>(v, queue);
 }
 
 void launch_features(const EngineView& v, int queue, float* out, cudaStream_t s) {
