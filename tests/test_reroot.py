@@ -205,3 +205,40 @@ def test_selfplay_with_subtree_reuse_matches_oracle(oracle_lib, mode):
             assert np.array_equal(ex["policy"], t.policy), (r.game_id, i)
             o.reroot(r.moves[i], keep=mode == "keep")
     assert all(not r.finished for r in recs)      # the live set stayed the same: reuse every move
+
+
+def _check_bfs(t, k, c):
+    order = _bfs(t.parent, c)
+    assert k.visits.shape[0] == len(order)
+    for f in ("visits", "value_sums", "priors", "virtual_loss", "terminal"):
+        assert np.array_equal(getattr(k, f), getattr(t, f)[order]), f
+    new_of = {int(old): i for i, old in enumerate(order)}
+    assert all(k.parent[i] == new_of[int(t.parent[order[i]])] for i in range(1, len(order)))
+
+
+def test_oracle_keep_reroot_go_and_chess(oracle_lib):
+    """The keep relabelling for Go (superko keys move with the nodes) and chess (position records
+    move with the nodes); a search continued on the kept tree keeps the root's visits."""
+    from omoknuni_quantum_b200.chess import random_position as chess_position
+    from omoknuni_quantum_b200.go import random_position as go_position
+    p = go_position(61, moves=24, board_size=9)
+    o = oracle_lib.Oracle(100000, 9)
+    t = o.search_go(p.history_planes(), p.to_move, 384, 64, ko=p.ko, passes=p.passes, keys=p.root_keys())
+    a = int(np.argmax(t.policy))
+    c = int(np.nonzero((t.parent == 0) & (t.action == a))[0][0])
+    assert o.reroot(a, keep=True) == 2
+    _check_bfs(t, o.export(), c)
+    p.play(a)
+    t2 = o.search_go(p.history_planes(), p.to_move, 128, 64, ko=p.ko, passes=p.passes, keys=p.root_keys())
+    assert int(t2.visits[0]) == int(t.visits[c]) + 128
+
+    q = chess_position(71)
+    o = oracle_lib.Oracle(100000, 8)
+    t = o.search_chess(q.record(), 288, 48, prior=q.prior)
+    a = int(np.argmax(t.policy))
+    c = int(np.nonzero((t.parent == 0) & (t.action == a))[0][0])
+    assert o.reroot(a, keep=True) == 2
+    _check_bfs(t, o.export(), c)
+    q.play(q.action_to_move(a))
+    t2 = o.search_chess(q.record(), 96, 48, prior=q.prior)
+    assert int(t2.visits[0]) == int(t.visits[c]) + 96
