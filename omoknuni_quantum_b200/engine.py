@@ -303,7 +303,8 @@ class WaveEngine:
         self.root_expand(evaluator)
         # full-size waves replay a CUDA graph when asked (MCTSConfig.use_cuda_graphs) and the
         # evaluator runs on the device queue (no host round trip inside a wave)
-        graphed = graphs and hasattr(evaluator, "forward_queue")
+        graphed = (graphs and hasattr(evaluator, "forward_queue")
+                   and not getattr(evaluator, "profiling", False))
         done = 0
         while done < num_simulations:
             w = min(self.max_wave_size, num_simulations - done)

@@ -190,6 +190,7 @@ class ResNetEvaluator:
         self._net = None
         self._max_batch = 0
         self.generation = 0     # bumped whenever the device net (and its buffers) is re-created
+        self.profiling = False  # CUDA-event timing of forward calls on (no graph capture then)
         self._ensure(max_batch)
         self._return_torch_tensors = True
 
@@ -263,6 +264,7 @@ class ResNetEvaluator:
     def profile(self, capacity: int) -> None:
         """Time the convolution trunk of the next ``capacity`` forward calls with CUDA events."""
         _lib.check(self.L.omq_resnet_profile(self._net, int(capacity)), "omq_resnet_profile")
+        self.profiling = int(capacity) > 0
 
     def profile_read(self, max_calls: int = 1 << 16):
         """(trunk_ms [calls], positions [calls]) of the profiled calls (synchronizes)."""
