@@ -27,7 +27,8 @@ constexpr int kWarps = kThreads / 32;
 // Gomoku rules on a shared-memory board
 // ---------------------------------------------------------------------------------------------
 // Warp-collective: for each row y < S, fm[y] gets bit x set when placing `p` on the empty cell
-// (y, x) of board b makes five or more in a row through it. For a non-terminal parent this equals
+// (y, x) of board b makes five or more in a row through it; fm[32 ..] holds the same cells as a
+// flat bit set indexed by cell. For a non-terminal parent this equals
 // the reference's full-board scan (python/mcts/utils/fast_terminal_check.py:233-332): any new
 // five must contain the new stone. Lane y holds row y's stone mask; a cell completes a five in direction (dr, dc) when one
 // of the five windows of 5 cells containing it has its other 4 cells occupied by `p`. Row j of
@@ -64,7 +65,18 @@ __device__ void warp_five_masks(const int8_t* b, int S, int p, uint32_t* fm) {
       five |= w;
     }
   }
-  if (lane < S) fm[lane] = five & ~occ & full;
+  // flat form: bit (y * S + x) % 32 of word (y * S + x) / 32, so a child's action indexes it
+  // without a division by S
+  for (int w = lane; w < (kMaxCells + 31) / 32; w += 32) fm[32 + w] = 0u;
+  __syncwarp();
+  if (lane < S) {
+    const uint32_t m = five & ~occ & full;
+    const int bit = lane * S, w = bit >> 5, o = bit & 31;
+    if (m) {
+      atomicOr(&fm[32 + w], m << o);
+      if (o + S > 32) atomicOr(&fm[32 + w + 1], m >> (32 - o));
+    }
+  }
   __syncwarp();
 }
 
@@ -718,7 +730,8 @@ struct ChessWarpSmem {
 };
 
 struct ExpandWarpSmem {
-  uint32_t five[32];    // Gomoku: cells where the mover completes five (warp_five_masks)
+  uint32_t five[32 + (kMaxCells + 31) / 32];  // Gomoku: cells where the mover completes five
+                                              // (warp_five_masks): rows, then flat by cell
   int16_t acts[kMaxDepthCap];
   int16_t legal[kMaxCells + 1];
   float pv[kMaxCells + 1];
@@ -902,6 +915,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
       const int player = (d % 2 == 0) ? H->root_player : 3 - H->root_player;
       const int mc = H->root_mc + d;
       warp_five_masks(W.board, v.S, player, W.five);
+      const bool root_five = H->root_five != 0;
       // legal actions in ascending order and their policy values
       int n = 0;
 #pragma unroll
@@ -924,7 +938,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
       for (int j = lane; j < n; j += 32) {
         const int a = W.legal[j];
         const float P = __fdiv_rn(W.pv[j], denom);
-        const bool term = H->root_five || ((W.five[a / v.S] >> (a % v.S)) & 1u) || (mc + 1 >= v.C);
+        const bool term = root_five || ((W.five[32 + (a >> 5)] >> (a & 31)) & 1u) || (mc + 1 >= v.C);
         const int c = start + j;
         const NodeStats st{0, 0.0f, P, 0};
         v.stats[base + c] = st;
