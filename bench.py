@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the wave-MCTS hot path: MCTS simulations/s on B200 (device-timed, whole box).
 
-Workload (one GPU): Gomoku 15x15 single-tree searches, 1600 simulations per
+Workload (benchmark config 1, one GPU): Gomoku 15x15 single-tree searches, 1600 simulations per
 root, max_wave_size 256, c_puct 1.4, virtual loss 1.0, ResNet evaluator 10 blocks x 128 filters
 (value head FC 225 -> 128 -> 1), bf16 weights/activations with fp32 accumulation, seeded He-init
 weights. Roots: 20 stones placed uniformly at random, colours alternating, from a seed. Each GPU
@@ -67,7 +67,7 @@ def parse():
                          "config3 = Go 19x19: 256 roots (sharded), 3200 sims, wave 512, 1M nodes, 20x256; "
                          "config4 = chess: 1024 roots (sharded), 1600 sims, wave 256, 500k nodes, 20x256")
     ap.add_argument("--evaluator", choices=["resnet", "synthetic"], default="resnet",
-                    help="synthetic = BASELINE config 0 (tree kernels only; 800 sims, 200k nodes)")
+                    help="synthetic = benchmark config 0 (tree kernels only; 800 sims, 200k nodes)")
     return ap.parse_args()
 
 
@@ -180,7 +180,7 @@ def make_spec(args):
 
 
 def apply_config4(args):
-    """chess, 1600 sims per root, wave 256, 500k-node trees, ResNet 20x256 on
+    """benchmark config 4: chess, 1600 sims per root, wave 256, 500k-node trees, ResNet 20x256 on
     119 planes with a 4672-way policy; 1024 roots (10-40 random plies) sharded across the GPUs."""
     args.sims, args.wave, args.capacity = 1600, 256, 500_000
     args.blocks, args.filters, args.value_hidden = 20, 256, 256
@@ -189,7 +189,7 @@ def apply_config4(args):
 
 
 def apply_config3(args):
-    """Go 19x19, 3200 sims per root, wave 512, 1M-node trees, ResNet 20x256
+    """benchmark config 3: Go 19x19, 3200 sims per root, wave 512, 1M-node trees, ResNet 20x256
     (value FC 361 -> 256 -> 1); 256 roots sharded across the GPUs."""
     args.sims, args.wave, args.capacity = 3200, 512, 1_000_000
     args.blocks, args.filters, args.value_hidden = 20, 256, 256
@@ -418,7 +418,7 @@ def run_b200(args):
 
 
 def run_b200_synthetic(args):
-    """BASELINE config 0 on the device: the integer-exact synthetic evaluator, so the step is the
+    """benchmark config 0 on the device: the integer-exact synthetic evaluator, so the step is the
     tree kernels alone (select, expand, backup, evaluation kernel)."""
     from omoknuni_quantum_b200 import _lib, parallel
     from omoknuni_quantum_b200.engine import WaveEngine
@@ -461,7 +461,7 @@ def run_b200_synthetic(args):
 
 
 def run_b200_selfplay(args):
-    """512 concurrent self-play games sharded over the ranks (total fixed),
+    """benchmark config 2: 512 concurrent self-play games sharded over the ranks (total fixed),
     800 simulations per move, max_wave_size 64 (leaf batches up to games x 64), ResNet 20 x 256
     bf16; one step = one move of every game (temperature-1 sampling from the visit policy)."""
     from omoknuni_quantum_b200 import _lib, parallel

@@ -243,7 +243,7 @@ class GoPosition:
 
 def random_position(seed: int, moves: int = 60, board_size: int = 19) -> GoPosition:
     """``moves`` uniformly random legal non-pass moves from the empty board, colours alternating
-    from black, captures resolved by the rules (BASELINE config 3's "60 stones placed at random
+    from black, captures resolved by the rules (benchmark config 3's "60 stones placed at random
     under the legality rules"); numpy.random.default_rng(seed)."""
     rng = np.random.default_rng(seed)
     g = GoPosition(board_size)

@@ -1,5 +1,5 @@
 """Batched self-play driver: many games advanced move by move, all searches of a move in one device
-wave loop (512 Gomoku games, 800 simulations, wave 64, 30 moves). Gomoku, Go
+wave loop (benchmark config 2: 512 Gomoku games, 800 simulations, wave 64, 30 moves). Gomoku, Go
 and chess games are supported (``game=``).
 
 Per move it follows the reference's ``SelfPlayGame.play_single_move``

@@ -1,6 +1,6 @@
 // Parity oracle (TEST INFRASTRUCTURE ONLY - never linked into the product library).
 //
-// Deterministic synthetic evaluator used by the parity gate:
+// Deterministic synthetic evaluator used by the parity gate (benchmark config 0):
 // "policy logits ~N(0,1) over the actions, seeded by a 64-bit hash of the position, masked to
 // legal moves and softmaxed; value = tanh of a hash-seeded N(0,0.5) draw".
 //

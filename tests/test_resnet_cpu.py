@@ -117,5 +117,5 @@ def _pack_fp32(sd, spec):
 def test_flops_per_position_config1():
     from omoknuni_quantum_b200.resnet import ResNetSpec
     s = ResNetSpec(num_blocks=10, filters=128, fc_value_hidden=128)
-    # trunk of BASELINE config 1 (10 x 128, 15x15): ~1.34 GFLOP per position
+    # trunk of benchmark config 1 (10 x 128, 15x15): ~1.34 GFLOP per position
     assert 1.30e9 < s.flops_per_position() < 1.36e9
