@@ -426,7 +426,7 @@ class ChessPosition:
 
 
 def random_position(seed: int, min_plies: int = 10, max_plies: int = 40) -> ChessPosition:
-    """Seeded uniformly random legal playout of min..max plies from the start position (BASELINE
+    """Seeded uniformly random legal playout of min..max plies from the start position (benchmark
     config 4's roots); stops early at a terminal position."""
     rng = np.random.default_rng(seed)
     plies = int(rng.integers(min_plies, max_plies + 1))
