@@ -104,6 +104,9 @@ OMQ_API const char* omq_status_string(int status);
 OMQ_API const char* omq_last_error(void); /* thread-local detail for the last non-OK status */
 /* Number of kernels this library has launched in the calling process so far. */
 OMQ_API int omq_kernel_launches(uint64_t* h_count);
+/* sizeof(omq_engine_config) and sizeof(omq_resnet_config) as this library was compiled: a binding
+ * checks its own struct declarations against them (host only, no device needed). */
+OMQ_API int omq_abi_struct_sizes(uint32_t* h_engine_config, uint32_t* h_resnet_config);
 /* Adjust that count by delta: a CUDA graph capture records launches without running them (-n),
  * each replay of the graph runs them (+n). */
 OMQ_API int omq_kernel_launches_add(int64_t delta);

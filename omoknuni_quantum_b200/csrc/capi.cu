@@ -58,6 +58,13 @@ const char* omq_status_string(int s) {
 
 const char* omq_last_error(void) { return g_err; }
 
+int omq_abi_struct_sizes(uint32_t* h_engine_config, uint32_t* h_resnet_config) {
+  if (!h_engine_config || !h_resnet_config) { set_error("null argument"); return OMQ_BAD_ARG; }
+  *h_engine_config = (uint32_t)sizeof(omq_engine_config);
+  *h_resnet_config = (uint32_t)sizeof(omq_resnet_config);
+  return OMQ_OK;
+}
+
 int omq_kernel_launches_add(int64_t delta) {
   g_launches.fetch_add((unsigned long long)delta, std::memory_order_relaxed);
   return OMQ_OK;

@@ -46,3 +46,13 @@ def test_integration_stub_matches_engine_config():
     block = doc[doc.index("class EngineConfig"):doc.index("lib.omq_engine_create.argtypes")]
     names = re.findall(r'\("([a-z_]+)", ctypes\.c_', block)
     assert names == [f[0] for f in EngineConfig._fields_]
+
+
+def test_struct_layouts_match_the_library():
+    """The Python ctypes structures have the sizes the library was compiled with (host call)."""
+    import ctypes
+    from omoknuni_quantum_b200 import _lib
+    e, r = ctypes.c_uint32(), ctypes.c_uint32()
+    assert _lib.load().omq_abi_struct_sizes(ctypes.byref(e), ctypes.byref(r)) == 0
+    assert e.value == ctypes.sizeof(_lib.EngineConfig)
+    assert r.value == ctypes.sizeof(_lib.ResNetConfig)
