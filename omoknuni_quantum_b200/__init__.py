@@ -5,10 +5,10 @@ Drop-in for the reference's ``MCTS(config, evaluator, game_interface).search()``
 ordered backup, an on-device leaf queue, and a tcgen05 bf16 ResNet evaluator, all in
 ``libomq_b200.so`` (C ABI: include/omq_b200.h).
 """
-from .mcts_config import GameType, MCTSConfig, create_optimized_config  # noqa: F401
+from .mcts_config import GameType, MCTSConfig, create_optimized_config, create_performance_config  # noqa: F401
 
 __all__ = ["MCTS", "MCTSConfig", "GameType", "SyntheticEvaluator", "ResNetEvaluator", "WaveEngine",
-           "create_optimized_config"]
+           "create_optimized_config", "create_performance_config"]
 
 
 def __getattr__(name):  # torch-importing modules load lazily

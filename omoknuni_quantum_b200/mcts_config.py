@@ -223,3 +223,11 @@ def create_optimized_config(game_type=GameType.GOMOKU, num_simulations: int = 10
     """mcts_config.py:287-310."""
     return MCTSConfig(game_type=game_type, num_simulations=num_simulations, device=device,
                       enable_quantum=enable_quantum, **kwargs)
+
+
+def create_performance_config(wave_size: int = 3072, memory_pool_mb: int = 2048, **kwargs) -> MCTSConfig:
+    """mcts_config.py:315-339: the reference's performance preset (its wave_size and pool size are
+    reference tuning fields; the engine's wave is max_wave_size)."""
+    return MCTSConfig(wave_size=wave_size, memory_pool_size_mb=memory_pool_mb, classical_only_mode=True,
+                      enable_fast_ucb=True, use_mixed_precision=True, use_cuda_graphs=True,
+                      use_tensor_cores=True, **kwargs)

@@ -157,3 +157,12 @@ def test_gomoku_state_objects_are_replayed():
     b = m._boards(State())
     assert b.reshape(-1)[112] == 1 and b.reshape(-1)[113] == 2 and b.reshape(-1)[97] == 1
     assert int((b != 0).sum()) == 3
+
+
+def test_config_presets():
+    from omoknuni_quantum_b200 import create_optimized_config, create_performance_config
+    c = create_performance_config(num_simulations=64)
+    assert c.wave_size == 3072 and c.memory_pool_size_mb == 2048 and c.use_cuda_graphs
+    assert c.num_simulations == 64
+    o = create_optimized_config(num_simulations=128)
+    assert o.num_simulations == 128 and o.device == "cuda"
