@@ -41,12 +41,17 @@ class SyntheticEvaluator:
         raise NotImplementedError("SyntheticEvaluator runs inside the device engine")
 
 
-def _resolve_evaluator(evaluator):
-    if isinstance(evaluator, SyntheticEvaluator) or evaluator == "synthetic":
+def _resolve_evaluator(evaluator, board_size: int = 15):
+    """The evaluator the engine runs. A reference ResNetModel - passed directly, or inside a
+    reference ResNetEvaluator as its ``model`` (resnet_evaluator.py:80-265, possibly TorchScript-
+    compiled) - becomes this package's bf16 tensor-core ResNetEvaluator with the same weights;
+    the synthetic evaluator runs on the device; anything else is called through evaluate_batch."""
+    if isinstance(evaluator, SyntheticEvaluator) or (isinstance(evaluator, str) and evaluator == "synthetic"):
         return "synthetic"
-    if isinstance(evaluator, torch.nn.Module) and hasattr(evaluator, "residual_blocks"):
-        from .resnet import ResNetEvaluator
-        return ResNetEvaluator.from_module(evaluator)
+    module = evaluator if hasattr(evaluator, "residual_blocks") else getattr(evaluator, "model", None)
+    if module is not None and hasattr(module, "residual_blocks") and hasattr(module, "state_dict"):
+        from . import resnet
+        return resnet.ResNetEvaluator(module.state_dict(), board_size=getattr(module, "board_size", board_size))
     return evaluator
 
 
@@ -61,7 +66,7 @@ class MCTS:
         if self.is_chess and config.board_size != 8:
             config.board_size = 8
         self.evaluator = evaluator
-        self._eval = _resolve_evaluator(evaluator)
+        self._eval = _resolve_evaluator(evaluator, config.board_size)
         if hasattr(evaluator, "_return_torch_tensors"):
             evaluator._return_torch_tensors = True          # mcts.py:120-121
         dev = config.device if config.device != "cpu" else "cuda"

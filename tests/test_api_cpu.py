@@ -166,3 +166,37 @@ def test_config_presets():
     assert c.num_simulations == 64
     o = create_optimized_config(num_simulations=128)
     assert o.num_simulations == 128 and o.device == "cuda"
+
+
+def test_reference_models_and_evaluators_become_the_device_resnet(monkeypatch):
+    """A reference ResNetModel, or a reference ResNetEvaluator holding one as ``model``, is run by
+    the tensor-core ResNet with its state_dict; the board size comes from the MCTS config."""
+    from omoknuni_quantum_b200 import mcts, resnet
+
+    made = []
+
+    class Stub:
+        def __init__(self, sd, board_size):
+            made.append((sd, board_size))
+
+    monkeypatch.setattr(resnet, "ResNetEvaluator", Stub)
+
+    class Model:                           # the attributes of the reference ResNetModel used here
+        residual_blocks = []
+
+        def state_dict(self):
+            return {"w": 1}
+
+    class RefEvaluator:
+        def __init__(self):
+            self.model = Model()
+
+        def evaluate_batch(self, x):
+            raise AssertionError("the reference evaluator itself must not be called")
+
+    assert isinstance(mcts._resolve_evaluator(Model(), 19), Stub)
+    assert isinstance(mcts._resolve_evaluator(RefEvaluator(), 8), Stub)
+    assert made == [({"w": 1}, 19), ({"w": 1}, 8)]
+    other = object()
+    assert mcts._resolve_evaluator(other) is other
+    assert mcts._resolve_evaluator("synthetic") == "synthetic"
