@@ -142,6 +142,13 @@ class _GoGame:
     def player(self, pos):
         return pos.to_move
 
+    def rules(self, positions):
+        """The rule set of a batch (GoPosition.rules); one search batch uses one rule set."""
+        rules = {getattr(p, "rules", "chinese") for p in positions}
+        if len(rules) != 1:
+            raise ValueError("one self-play batch must use one Go rule set")
+        return rules.pop()
+
     def state(self, pos):
         return pos.history_planes()
 
@@ -222,6 +229,7 @@ class BatchedSelfPlay:
         self.resign_min_move = int(resign_min_move)
         self._last_move = None          # (live games, their moves) of the previous step
         self._live_now = None
+        self._rules_now = None
         self.game = _GAMES[game](board_size)
         self.G = int(num_games)
         self.sims = int(num_simulations)
@@ -250,10 +258,14 @@ class BatchedSelfPlay:
         from .engine import WaveEngine
         roots, kw = inputs if isinstance(inputs, tuple) else (inputs, {})
         R = roots.shape[0]
-        eng = self._engines.get(R)
+        key = (R, self._rules_now)
+        eng = self._engines.get(key)
         if eng is None:
-            eng = WaveEngine(R, **self._engine_args)
-            self._engines[R] = eng
+            args = dict(self._engine_args)
+            if self._rules_now is not None:
+                args["go_rules"] = self._rules_now      # the device engine follows the positions
+            eng = WaveEngine(R, **args)
+            self._engines[key] = eng
         elif (self.subtree_reuse != "none" and self._last_move is not None
               and self._last_move[0] == self._live_now):
             eng.reroot(np.asarray(self._last_move[1], np.int32), keep=self.subtree_reuse == "keep")
@@ -276,6 +288,8 @@ class BatchedSelfPlay:
             return 0
         search = self._search or self._device_search
         self._live_now = tuple(int(g) for g in live)
+        self._rules_now = (self.game.rules([self.positions[g] for g in live])
+                           if hasattr(self.game, "rules") else None)
         moves = []
         roots, meta = self.game.engine_input([self.positions[g] for g in live])
         res = search(roots if meta is None else (roots, meta))

@@ -1,3 +1,4 @@
+import pytest
 """Self-play bookkeeping on CPU with a fake searcher: temperature sampling then arg-max,
 legal moves, five detection, outcome values from each player's perspective, reproducibility."""
 import numpy as np
@@ -137,3 +138,43 @@ def test_resignation_q_values_and_metrics():
         assert m["value_accuracies"] == [1.0] * 6 and len(m["policy_entropies"]) == 6
     off = BatchedSelfPlay(2, search=losing, temperature_threshold=0, seed=1, enable_resign=False)
     assert not any(r.resigned for r in off.play(8))
+
+
+def test_go_selfplay_engine_follows_the_rule_set(monkeypatch):
+    """Japanese / Korean roots are searched by an engine built with that rule set (the device's
+    repetition rule instead of superko), one engine per rule set; mixed batches are refused."""
+    import torch
+    from omoknuni_quantum_b200 import engine as engine_mod
+    from omoknuni_quantum_b200.go import GoPosition
+    built = []
+
+    class FakeEngine:
+        def __init__(self, R, **kw):
+            built.append(kw.get("go_rules", "chinese"))
+            self.R, self.n = R, kw["board_size"]
+
+        def search(self, roots, sims, evaluator, **kw):
+            self.masks = [np.ones(self.n * self.n + 1, bool) for _ in range(self.R)]
+            self.meta = kw["meta"]
+
+        def root_visits(self):
+            v = np.zeros((self.R, self.n * self.n + 1), np.int64)
+            v[:, 0] = 1                       # every game plays its first cell, then passes
+            return torch.from_numpy(v)
+
+        def root_nw(self):
+            return torch.zeros(self.R, 2)
+
+        def reroot(self, actions, keep=False):
+            pass
+
+    monkeypatch.setattr(engine_mod, "WaveEngine", FakeEngine)
+    roots = [GoPosition(9, rules="japanese") for _ in range(2)]
+    sp = BatchedSelfPlay(2, num_simulations=8, game="go", board_size=9, roots=roots,
+                         enable_resign=False)
+    sp.step()
+    assert built == ["japanese"]
+    mixed = [GoPosition(9, rules="japanese"), GoPosition(9)]
+    sp2 = BatchedSelfPlay(2, num_simulations=8, game="go", board_size=9, roots=mixed)
+    with pytest.raises(ValueError):
+        sp2.step()
