@@ -1,7 +1,7 @@
-import pytest
 """Self-play bookkeeping on CPU with a fake searcher: temperature sampling then arg-max,
 legal moves, five detection, outcome values from each player's perspective, reproducibility."""
 import numpy as np
+import pytest
 
 from omoknuni_quantum_b200.selfplay import BatchedSelfPlay, board_after, game_result
 
