@@ -310,15 +310,18 @@ class ChessPosition:
         c.prior, c.reps = self.prior, self.reps
         return c
 
+    def _legal(self, m: int) -> bool:
+        """A pseudo-legal move that does not leave the mover's king attacked."""
+        c = self._copy_board()
+        c._apply(m)
+        return not c.in_check(self.side)
+
     def legal_moves(self) -> list:
         """Legal moves (reference encoding), sorted."""
-        out = []
-        for m in self._pseudo():
-            c = self._copy_board()
-            c._apply(m)
-            if not c.in_check(self.side):
-                out.append(m)
-        return sorted(out)
+        return sorted(m for m in self._pseudo() if self._legal(m))
+
+    def has_legal_move(self) -> bool:
+        return any(self._legal(m) for m in self._pseudo())
 
     def _insufficient(self) -> bool:
         cnt = {(c, t): 0 for c in (WHITE, BLACK) for t in range(1, 7)}
@@ -345,7 +348,7 @@ class ChessPosition:
 
     def result(self) -> int:
         """The reference's GameResult: 0 ongoing, 1 white wins, 2 black wins, 3 draw."""
-        if not self.legal_moves():
+        if not self.has_legal_move():
             return (2 if self.side == WHITE else 1) if self.in_check() else 3
         if self._insufficient() or self.halfmove >= 100 or self.reps >= 3:
             return 3
@@ -365,7 +368,7 @@ class ChessPosition:
 
     def play(self, move: int) -> None:
         """Play a legal move (reference encoding); keeps the earlier positions for repetitions."""
-        if move not in self.legal_moves():
+        if move not in self._pseudo() or not self._legal(move):
             raise ValueError(f"illegal chess move {move}")
         rec = self.record()
         self._apply(int(move))
