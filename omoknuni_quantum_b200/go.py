@@ -153,11 +153,57 @@ class GoPosition:
     def is_legal(self, action: int) -> bool:
         return self._try(int(action)) is not None
 
+    def _group_liberties(self):
+        """Per cell: the liberty count of its group (0 on empty cells)."""
+        n, b = self.n, self.board
+        libs = np.zeros((n, n), np.int32)
+        seen = np.zeros((n, n), bool)
+        for y in range(n):
+            for x in range(n):
+                if b[y, x] == 0 or seen[y, x]:
+                    continue
+                stones, empties, stack = [], set(), [(y, x)]
+                seen[y, x] = True
+                while stack:
+                    cy, cx = stack.pop()
+                    stones.append((cy, cx))
+                    for ny, nx in ((cy - 1, cx), (cy + 1, cx), (cy, cx - 1), (cy, cx + 1)):
+                        if 0 <= ny < n and 0 <= nx < n:
+                            if b[ny, nx] == 0:
+                                empties.add((ny, nx))
+                            elif b[ny, nx] == b[y, x] and not seen[ny, nx]:
+                                seen[ny, nx] = True
+                                stack.append((ny, nx))
+                for cy, cx in stones:
+                    libs[cy, cx] = len(empties)
+        return libs
+
     def legal_mask(self) -> np.ndarray:
-        """bool [n*n + 1], pass last."""
+        """bool [n*n + 1], pass last. A cell with an empty neighbour that captures nothing and is
+        not the ko point is a legal placement whose new position key is one XOR away (no ko
+        point arises without a capture), so only the other cells need the full trial move."""
+        n = self.n
         m = np.zeros(self.pass_action + 1, bool)
-        for a in np.flatnonzero(self.board.reshape(-1) == 0):
-            m[a] = self._try(int(a)) is not None
+        libs = self._group_liberties()
+        b = self.board
+        opp = 3 - self.to_move
+        stones, _ = _key_tables(n)
+        base = position_key(b, -1) if self.superko and self.keys else 0
+        keys = set(self.keys) if self.superko else ()
+        for a in np.flatnonzero(b.reshape(-1) == 0):
+            a = int(a)
+            y, x = divmod(a, n)
+            empty_nb = capture = False
+            for ny, nx in ((y - 1, x), (y + 1, x), (y, x - 1), (y, x + 1)):
+                if 0 <= ny < n and 0 <= nx < n:
+                    if b[ny, nx] == 0:
+                        empty_nb = True
+                    elif b[ny, nx] == opp and libs[ny, nx] == 1:
+                        capture = True
+            if empty_nb and not capture and a != self.ko:
+                m[a] = not (keys and (base ^ int(stones[a, self.to_move])) in keys)
+            else:
+                m[a] = self._try(a) is not None
         m[self.pass_action] = True
         return m
 

@@ -52,3 +52,20 @@ def test_chess_host_position_matches_oracle_on_random_games(oracle_lib):
             o = oracle_lib.chess_play(o, m)
             want = oracle_lib.chess_from_fen(p.fen(), chess960=c960)
             assert oracle_lib.chess_same(o, want) and o["castle"] == want["castle"] and o["ep"] == want["ep"], (i, ply)
+
+
+def test_go_fast_legal_mask_equals_trial_moves():
+    """GoPosition.legal_mask's shortcut (empty neighbour, no capture, not ko) agrees with the full
+    trial move on every cell of random positions, with and without superko keys."""
+    from omoknuni_quantum_b200.go import GoPosition
+    for n, seed in [(9, 1), (9, 2), (13, 3), (19, 4)]:
+        rng = np.random.default_rng(seed)
+        for superko in (True, False):
+            g = GoPosition(n, superko=superko)
+            for _ in range(3 * n * n // 2):
+                slow = np.array([g._try(a) is not None for a in range(n * n)] + [True])
+                assert np.array_equal(g.legal_mask(), slow)
+                cand = np.flatnonzero(slow[:-1])
+                if len(cand) == 0:
+                    break
+                g.play(int(cand[rng.integers(len(cand))]))
