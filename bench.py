@@ -62,10 +62,14 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", choices=["config1", "config2", "config3", "config4"], default="config1",
-                    help="config2 = batched self-play: 512 games (sharded), 800 sims, wave 64, 20x256; "
+    ap.add_argument("--workload", choices=["config1", "config2", "config3", "config4", "forward"], default="config1",
+                    help="forward = ResNet leaf evaluations/s alone (--game, --batch, --blocks, --filters); "
+                         "config2 = batched self-play: 512 games (sharded), 800 sims, wave 64, 20x256; "
                          "config3 = Go 19x19: 256 roots (sharded), 3200 sims, wave 512, 1M nodes, 20x256; "
                          "config4 = chess: 1024 roots (sharded), 1600 sims, wave 256, 500k nodes, 20x256")
+    ap.add_argument("--game", choices=["gomoku", "go", "chess"], default="gomoku",
+                    help="board shape of --workload forward")
+    ap.add_argument("--batch", type=int, default=4096, help="positions per call of --workload forward")
     ap.add_argument("--evaluator", choices=["resnet", "synthetic"], default="resnet",
                     help="synthetic = benchmark config 0 (tree kernels only; 800 sims, 200k nodes)")
     return ap.parse_args()
@@ -672,8 +676,55 @@ def run_b200_go(args, game="go"):
         dist.destroy_process_group()
 
 
+def run_b200_forward(args):
+    """ResNet leaf evaluations/s alone: seeded random weights and features of one game's shape,
+    `--batch` positions per call, one step = one forward call; also the target of the committed
+    conv ncu captures. ``--game go`` is 19x19 / 17 planes / 362 actions, ``--game chess`` 8x8 /
+    119 planes / 4672 actions."""
+    from omoknuni_quantum_b200 import _lib
+    from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    n, planes, acts = {"gomoku": (15, 19, 225), "go": (19, 17, 362), "chess": (8, 119, 4672)}[args.game]
+    spec = ResNetSpec(board_size=n, input_channels=planes, num_blocks=args.blocks, filters=args.filters,
+                      num_actions=acts, fc_value_hidden=args.value_hidden)
+    ev = ResNetEvaluator.random(spec, seed=args.seed, max_batch=args.batch)
+    g = torch.Generator().manual_seed(args.seed)
+    x = torch.zeros(args.batch, planes, n, n)
+    x[:, 0] = (torch.rand(args.batch, n, n, generator=g) < 0.2).float()
+    x[:, 1] = (torch.rand(args.batch, n, n, generator=g) < 0.2).float()
+    x = x.to(ev.device)
+    for _ in range(args.warmup):
+        ev.evaluate_batch(x)
+    torch.cuda.synchronize()
+    n0 = _lib.kernel_launches()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        s0.record()
+        for _ in range(args.steps):
+            ev.evaluate_batch(x)
+        s1.record()
+        torch.cuda.synchronize()
+    ms = s0.elapsed_time(s1)
+    if ev.error() != 0:
+        raise SystemExit("ResNet forward reported a device error")
+    if rank == 0:
+        print(json.dumps({
+            "metric": "ResNet leaf evaluations/sec", "value": args.batch * args.steps / (ms / 1000.0),
+            "unit": "positions/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded features and weights)",
+            "config": {"workload": f"forward: {args.game} {n}x{n}, {planes} planes, {acts} actions",
+                       "model": f"resnet{args.blocks}x{args.filters}", "batch": args.batch},
+            "trunk_tflops": args.batch * args.steps * ev.trunk_flops_per_position() / (ms / 1000.0) / 1e12,
+            "clocks": clk.summary(), "gpu_launches": _lib.kernel_launches() - n0}), flush=True)
+
+
 def main():
     args = parse()
+    if args.workload == "forward" and args.impl == "b200":
+        run_b200_forward(args)
+        return
     if args.workload in ("config3", "config4") and args.impl == "b200":
         run_b200_go(args, "go" if args.workload == "config3" else "chess")
         return

@@ -307,6 +307,11 @@ OMQ_API int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const uint1
                                        const float* d_conv_b, const float* d_head,
                                        const float* d_features, int32_t batch, float* d_policy,
                                        float* d_value, void* stream);
+/* Error word of the last omq_resnet_forward_noalloc call on `device`: OMQ_OK, or OMQ_TIMEOUT when
+ * a kernel's bounded wait gave up (the outputs of that call are then incomplete). Waits for the
+ * work queued on `stream` and allocates nothing (no counterpart in the reference; the companion
+ * of omq_resnet_forward_noalloc). The next forward clears the word. */
+OMQ_API int omq_resnet_noalloc_error(int32_t device, int32_t* h_error, void* stream);
 /* Self-test of the bounded device waits: launches a kernel whose mbarrier wait can never complete;
  * after limit_ns (at most 1 s) it gives up and writes OMQ_TIMEOUT to d_status (int32, device). */
 OMQ_API int omq_selftest_wait_timeout(uint64_t limit_ns, int32_t* d_status, void* stream);

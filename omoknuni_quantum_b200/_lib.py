@@ -109,6 +109,7 @@ SIGNATURES = {
     "omq_abi_struct_sizes": [ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)],
     "omq_selftest_wait_timeout": [ctypes.c_uint64, _P, _P],
     "omq_resnet_forward_noalloc": [ctypes.POINTER(ResNetConfig), _P, _P, _P, _P, _I, _P, _P, _P],
+    "omq_resnet_noalloc_error": [_I, ctypes.POINTER(_I), _P],
 }
 _RESTYPES = {"omq_status_string": ctypes.c_char_p, "omq_last_error": ctypes.c_char_p}
 

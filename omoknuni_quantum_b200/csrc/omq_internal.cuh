@@ -203,7 +203,9 @@ struct DeviceGuard {
   int prev = -1;
   explicit DeviceGuard(int dev) {
     cudaGetDevice(&prev);
-    if (prev != dev) cudaSetDevice(dev);
+    // an invalid ordinal leaves the device unchanged; the caller's own checks report it, and the
+    // failed call's error is cleared so that a later cudaGetLastError does not pick it up
+    if (prev != dev && cudaSetDevice(dev) != cudaSuccess) cudaGetLastError();
   }
   ~DeviceGuard() {
     int cur = -1;

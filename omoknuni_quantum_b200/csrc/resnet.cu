@@ -51,226 +51,6 @@ struct ConvArgs {
   int32_t* error;
 };
 
-// BN = output channels per tile (all of them); SUB = 128-row UMMA sub-tiles per CTA tile that
-// share each B (weight) stage. SUB = 2 halves the shared-memory bytes per FLOP of the N = 128
-// net; TMEM holds 2 (double buffer) x SUB x BN fp32 columns <= 512.
-template <int BN, int SUB>
-struct ConvCfg {
-  static constexpr int kRows = kTileM * SUB;
-  static constexpr int kA = kRows * kBlockK * 2;
-  static constexpr int kB = BN * kBlockK * 2;
-  static constexpr int kStage = kA + kB;
-  static constexpr int kStages = (196608 / kStage) < 8 ? (196608 / kStage) : 8;
-  static constexpr int kEpiWarps = 4 * SUB;
-  static constexpr int kThreads = 64 + 32 * kEpiWarps;
-  static constexpr int kTmemCols = 2 * SUB * BN;
-  static constexpr int kStaging = kEpiWarps * 2 * 2048;  // per epilogue warp: 2 x (32 rows x 64 B)
-  static constexpr int kStageBufs = 2;                       // epilogue staging buffers per warp
-  static constexpr int kSmem = kStages * kStage + kStaging + 1024 /*align*/ + 256 /*barriers*/ + BN * 4;
-  static_assert(kTmemCols <= 512, "TMEM holds 512 fp32 columns");
-  static_assert(kSmem <= 232448, "227 KB of shared memory per CTA");
-};
-
-template <int BN, int SUB>
-__global__ void __launch_bounds__(ConvCfg<BN, SUB>::kThreads, 1)
-    k_conv3x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-              const __grid_constant__ CUtensorMap tmO, ConvArgs args) {
-  using Cfg = ConvCfg<BN, SUB>;
-  constexpr int kStages = Cfg::kStages;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  uint8_t* staging = smem + kStages * Cfg::kStage;  // 1024-aligned (64B-swizzle atoms need 512)
-  uint64_t* full = reinterpret_cast<uint64_t*>(staging + Cfg::kStaging);
-  uint64_t* empty = full + kStages;
-  uint64_t* tfull = empty + kStages;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* s_bias = reinterpret_cast<float*>(staging + Cfg::kStaging + 256);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_pos = args.d_count ? min(*args.d_count, args.count) : args.count;
-  const int rows = n_pos * args.P;
-  const int tiles = (rows + Cfg::kRows - 1) / Cfg::kRows;
-  const int KB = 9 * args.kb_per_tap;
-  const int rowstride = args.S + 1;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) { ptx::mbar_init(&full[s], 1); ptx::mbar_init(&empty[s], 1); }
-    for (int i = 0; i < 2; ++i) { ptx::mbar_init(&tfull[i], 1); ptx::mbar_init(&tempty[i], Cfg::kEpiWarps); }
-    ptx::mbar_init(drain, 1);
-    *abort_flag = 0;
-    ptx::fence_barrier_init();
-    ptx::prefetch_tmap(&tmA);
-    ptx::prefetch_tmap(&tmB);
-    ptx::prefetch_tmap(&tmO);
-  }
-  for (int i = threadIdx.x; i < BN; i += blockDim.x) s_bias[i] = args.bias[i];
-  if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, Cfg::kTmemCols);
-    ptx::tmem_relinquish();
-  }
-  ptx::tc_fence_before();
-  __syncthreads();
-  ptx::tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer ----------------
-    int s = 0;
-    uint32_t ph = 0;
-    int issued[kStages];
-    for (int i = 0; i < kStages; ++i) issued[i] = -1;
-    for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
-      const int m0 = tile * Cfg::kRows;
-      for (int kb = 0; kb < KB; ++kb) {
-        if (!ptx::mbar_wait(&empty[s], ph ^ 1, abort_flag, kWaitLimitNs)) goto producer_done;
-        const int tap = kb / args.kb_per_tap, cb = kb - tap * args.kb_per_tap;
-        const int dy = tap / 3 - 1, dx = tap % 3 - 1;
-        ptx::mbar_arrive_expect_tx(&full[s], Cfg::kStage);
-        ptx::tma_load_2d(smem + s * Cfg::kStage, &tmA, &full[s], cb * kBlockK,
-                         m0 + dy * rowstride + dx);
-        ptx::tma_load_2d(smem + s * Cfg::kStage + Cfg::kA, &tmB, &full[s], kb * kBlockK, 0);
-        issued[s] = (int)ph;
-        if (++s == kStages) { s = 0; ph ^= 1; }
-      }
-    }
-  producer_done:
-    // never leave with copies in flight: wait (bounded) for every issued stage to land
-    for (int i = 0; i < kStages; ++i)
-      if (issued[i] >= 0) {
-        volatile int dummy = 0;
-        ptx::mbar_wait(&full[i], (uint32_t)issued[i], &dummy, kWaitLimitNs);
-      }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer ----------------
-    constexpr uint32_t idesc = ptx::idesc_bf16_f32(kTileM, BN);
-    int s = 0;
-    uint32_t ph = 0;
-    bool any = false;
-    int t = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
-      const int ab = t & 1;
-      const uint32_t aph = (t >> 1) & 1;
-      if (!ptx::mbar_wait(&tempty[ab], aph ^ 1, abort_flag, kWaitLimitNs)) break;
-      ptx::tc_fence_after();
-      const uint32_t d = tmem + ab * SUB * BN;
-      bool ok = true;
-      for (int kb = 0; kb < KB; ++kb) {
-        if (!ptx::mbar_wait(&full[s], ph, abort_flag, kWaitLimitNs)) { ok = false; break; }
-        ptx::tc_fence_after();
-        const uint32_t a_addr = ptx::smem_u32(smem + s * Cfg::kStage);
-        const uint32_t b_addr = a_addr + Cfg::kA;
-#pragma unroll
-        for (int k = 0; k < kBlockK / 16; ++k) {
-          const uint64_t bdesc = ptx::smem_desc_sw128(b_addr + k * 32);
-#pragma unroll
-          for (int sub = 0; sub < SUB; ++sub)
-            ptx::mma_bf16(d + sub * BN, ptx::smem_desc_sw128(a_addr + sub * (kTileM * 128) + k * 32),
-                          bdesc, idesc, (kb | k) != 0);
-        }
-        any = true;
-        ptx::mma_commit(&empty[s]);
-        if (++s == kStages) { s = 0; ph ^= 1; }
-      }
-      if (!ok) break;
-      ptx::mma_commit(&tfull[ab]);
-    }
-    if (any) {  // drain outstanding MMAs before TMEM is released
-      ptx::mma_commit(drain);
-      volatile int dummy = 0;
-      ptx::mbar_wait(drain, 0, &dummy, kWaitLimitNs);
-    }
-  } else if (warp >= 2) {
-    // ---------------- epilogue: warp 2 + 4*sub + q handles rows sub*128 + 32q .. +31 ----------
-    // Each 32 rows x 32 channels chunk is staged in shared memory (64-byte swizzle, two buffers
-    // per warp) and written by one TMA store, instead of 32 scattered 16-byte row stores.
-    const int sub = (warp - 2) >> 2;
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    uint8_t* my_stage = staging + (warp - 2) * Cfg::kStageBufs * 2048;
-    int buf = 0;
-    int t = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
-      const int ab = t & 1;
-      const uint32_t aph = (t >> 1) & 1;
-      if (!ptx::mbar_wait(&tfull[ab], aph, abort_flag, kWaitLimitNs)) break;
-      ptx::tc_fence_after();
-      const int row0 = tile * Cfg::kRows + sub * kTileM + q * 32;
-      const int m = row0 + lane;
-      const bool valid = m < rows;
-      const int pix = m % args.P;
-      const int y = pix / rowstride, x = pix - y * rowstride;
-      const bool pad = !valid || (y == args.S) || (x == args.S);
-      const __nv_bfloat16* rrow = args.residual ? args.residual + (size_t)m * BN : nullptr;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + ab * SUB * BN + sub * BN + c0, r);
-        ptx::tmem_ld_wait();
-        uint4 packed[4];
-        uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
-        if (pad) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) pw[j] = 0u;
-        } else {
-          float res[32];
-          if (rrow) {
-            const uint4* rp = reinterpret_cast<const uint4*>(rrow + c0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint4 u = rp[j];
-              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                float2 f = __bfloat1622float2(h[e]);
-                res[8 * j + 2 * e] = f.x;
-                res[8 * j + 2 * e + 1] = f.y;
-              }
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) res[j] = 0.0f;
-          }
-#pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            float v0 = __uint_as_float(r[j]) + s_bias[c0 + j] + res[j];
-            float v1 = __uint_as_float(r[j + 1]) + s_bias[c0 + j + 1] + res[j + 1];
-            if (args.relu) { v0 = fmaxf(v0, 0.0f); v1 = fmaxf(v1, 0.0f); }
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
-            pw[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
-          }
-        }
-        // the buffer about to be written must no longer be read by an earlier store
-        if (lane == 0) ptx::bulk_wait_read<1>();
-        __syncwarp();
-        uint8_t* sb = my_stage + buf * 2048;
-        const int sw = (lane >> 1) & 3;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(sb + lane * 64 + ((j ^ sw) * 16)) = packed[j];
-        ptx::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          ptx::tma_store_2d(&tmO, sb, c0, row0);
-          ptx::bulk_commit();
-        }
-        buf ^= 1;
-      }
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&tempty[ab]);
-    }
-    if (lane == 0) ptx::bulk_wait<0>();
-  }
-  __syncthreads();
-  if (warp == 1) {
-    ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem, Cfg::kTmemCols);
-  }
-  if (threadIdx.x == 0 && *abort_flag) atomicExch(args.error, OMQ_TIMEOUT);
-}
-
 // CTA-pair variant (cta_group::2). A cluster of 2 CTAs computes 256-row tiles with one UMMA of
 // M = 256: each CTA stages its own 128 rows of A and half (BN/2 rows) of the weight tile, so a
 // K=16 step reads 4 KB + BN/2 * 32 B of shared memory per SM instead of 4 KB + BN * 32 B - the
@@ -495,469 +275,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::kThread
   }
   if (threadIdx.x == 0 && *abort_flag) atomicExch(args.error, OMQ_TIMEOUT);
 }
-
-// Transposed variant for 128 filters: D^T = W * A^T. Output channels are the UMMA's M (128 TMEM
-// lanes) and the tile's 256 pixel rows are its N, so every MMA is 128 x 256 x 16 - the shape
-// that keeps the tensor pipe fed - while a K step still reads only 4 KB of weights plus 8 KB of
-// activations from shared memory. The epilogue turns each warp's 32 channels x 32 pixels block
-// around through a padded shared-memory tile so that stores stay row-contiguous.
-struct TCfg {
-  static constexpr int kPix = 256;                         // pixel rows per tile (UMMA N)
-  static constexpr int kW = 128 * kBlockK * 2;             // weights, 16 KB (UMMA A)
-  static constexpr int kX = kPix * kBlockK * 2;            // activations, 32 KB (UMMA B)
-  static constexpr int kStage = kW + kX;
-  static constexpr int kStages = 4;
-  static constexpr int kThreads = 192;
-  static constexpr int kTmemCols = 2 * kPix;
-  static constexpr int kTransposeFloats = 32 * 33;         // per epilogue warp
-  static constexpr int kSmem = kStages * kStage + 1024 + 256 + 128 * 4 + 4 * kTransposeFloats * 4;
-};
-
-__global__ void __launch_bounds__(TCfg::kThreads, 1)
-    k_conv3x3_t(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                ConvArgs args) {
-  constexpr int BN = 128;
-  constexpr int kStages = TCfg::kStages;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * TCfg::kStage);
-  uint64_t* empty = full + kStages;
-  uint64_t* tfull = empty + kStages;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* s_bias = reinterpret_cast<float*>(smem + kStages * TCfg::kStage + 256);
-  float* s_tr = s_bias + BN;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_pos = args.d_count ? min(*args.d_count, args.count) : args.count;
-  const int rows = n_pos * args.P;
-  const int tiles = (rows + TCfg::kPix - 1) / TCfg::kPix;
-  const int KB = 9 * args.kb_per_tap;
-  const int rowstride = args.S + 1;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) { ptx::mbar_init(&full[s], 1); ptx::mbar_init(&empty[s], 1); }
-    for (int i = 0; i < 2; ++i) { ptx::mbar_init(&tfull[i], 1); ptx::mbar_init(&tempty[i], 4); }
-    ptx::mbar_init(drain, 1);
-    *abort_flag = 0;
-    ptx::fence_barrier_init();
-    ptx::prefetch_tmap(&tmA);
-    ptx::prefetch_tmap(&tmB);
-  }
-  for (int i = threadIdx.x; i < BN; i += blockDim.x) s_bias[i] = args.bias[i];
-  if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, TCfg::kTmemCols);
-    ptx::tmem_relinquish();
-  }
-  ptx::tc_fence_before();
-  __syncthreads();
-  ptx::tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0 && lane == 0) {
-    int s = 0;
-    uint32_t ph = 0;
-    int issued[kStages];
-    for (int i = 0; i < kStages; ++i) issued[i] = -1;
-    for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
-      const int m0 = tile * TCfg::kPix;
-      for (int kb = 0; kb < KB; ++kb) {
-        if (!ptx::mbar_wait(&empty[s], ph ^ 1, abort_flag, kWaitLimitNs)) goto producer_done;
-        const int tap = kb / args.kb_per_tap, cb = kb - tap * args.kb_per_tap;
-        const int dy = tap / 3 - 1, dx = tap % 3 - 1;
-        ptx::mbar_arrive_expect_tx(&full[s], TCfg::kStage);
-        ptx::tma_load_2d(smem + s * TCfg::kStage, &tmB, &full[s], kb * kBlockK, 0);
-        ptx::tma_load_2d(smem + s * TCfg::kStage + TCfg::kW, &tmA, &full[s], cb * kBlockK,
-                         m0 + dy * rowstride + dx);
-        issued[s] = (int)ph;
-        if (++s == kStages) { s = 0; ph ^= 1; }
-      }
-    }
-  producer_done:
-    for (int i = 0; i < kStages; ++i)
-      if (issued[i] >= 0) {
-        volatile int dummy = 0;
-        ptx::mbar_wait(&full[i], (uint32_t)issued[i], &dummy, kWaitLimitNs);
-      }
-  } else if (warp == 1 && lane == 0) {
-    constexpr uint32_t idesc = ptx::idesc_bf16_f32(128, TCfg::kPix);
-    int s = 0;
-    uint32_t ph = 0;
-    bool any = false;
-    int t = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
-      const int ab = t & 1;
-      const uint32_t aph = (t >> 1) & 1;
-      if (!ptx::mbar_wait(&tempty[ab], aph ^ 1, abort_flag, kWaitLimitNs)) break;
-      ptx::tc_fence_after();
-      const uint32_t d = tmem + ab * TCfg::kPix;
-      bool ok = true;
-      for (int kb = 0; kb < KB; ++kb) {
-        if (!ptx::mbar_wait(&full[s], ph, abort_flag, kWaitLimitNs)) { ok = false; break; }
-        ptx::tc_fence_after();
-        const uint32_t w_addr = ptx::smem_u32(smem + s * TCfg::kStage);
-        const uint32_t x_addr = w_addr + TCfg::kW;
-#pragma unroll
-        for (int k = 0; k < kBlockK / 16; ++k)
-          ptx::mma_bf16(d, ptx::smem_desc_sw128(w_addr + k * 32), ptx::smem_desc_sw128(x_addr + k * 32),
-                        idesc, (kb | k) != 0);
-        any = true;
-        ptx::mma_commit(&empty[s]);
-        if (++s == kStages) { s = 0; ph ^= 1; }
-      }
-      if (!ok) break;
-      ptx::mma_commit(&tfull[ab]);
-    }
-    if (any) {
-      ptx::mma_commit(drain);
-      volatile int dummy = 0;
-      ptx::mbar_wait(drain, 0, &dummy, kWaitLimitNs);
-    }
-  } else if (warp >= 2) {
-    // warp q owns output channels 32q..32q+31 (its TMEM lane quarter) for all 256 pixels
-    const int q = warp & 3;
-    float* tr = s_tr + (warp - 2) * TCfg::kTransposeFloats;
-    int t = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
-      const int ab = t & 1;
-      const uint32_t aph = (t >> 1) & 1;
-      if (!ptx::mbar_wait(&tfull[ab], aph, abort_flag, kWaitLimitNs)) break;
-      ptx::tc_fence_after();
-#pragma unroll 1
-      for (int j0 = 0; j0 < TCfg::kPix; j0 += 32) {
-        uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + ab * TCfg::kPix + j0, r);
-        ptx::tmem_ld_wait();
-        // r[jj] = channel (32q + lane) of pixel j0 + jj  ->  tr[jj][lane]
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) tr[jj * 33 + lane] = __uint_as_float(r[jj]);
-        __syncwarp();
-        const int m = tile * TCfg::kPix + j0 + lane;  // this lane's pixel row
-        if (m < rows) {
-          const int pix = m % args.P;
-          const int y = pix / rowstride, x = pix - y * rowstride;
-          const bool pad = (y == args.S) || (x == args.S);
-          uint4 packed[4];
-          uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
-          if (pad) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) pw[j] = 0u;
-          } else {
-            float res[32];
-            if (args.residual) {
-              const uint4* rp = reinterpret_cast<const uint4*>(args.residual + (size_t)m * BN + q * 32);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                uint4 u = rp[j];
-                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  float2 f = __bfloat1622float2(h[e]);
-                  res[8 * j + 2 * e] = f.x;
-                  res[8 * j + 2 * e + 1] = f.y;
-                }
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) res[j] = 0.0f;
-            }
-#pragma unroll
-            for (int c = 0; c < 32; c += 2) {
-              float v0 = tr[lane * 33 + c] + s_bias[q * 32 + c] + res[c];
-              float v1 = tr[lane * 33 + c + 1] + s_bias[q * 32 + c + 1] + res[c + 1];
-              if (args.relu) { v0 = fmaxf(v0, 0.0f); v1 = fmaxf(v1, 0.0f); }
-              __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
-              pw[c / 2] = *reinterpret_cast<uint32_t*>(&h2);
-            }
-          }
-          uint4* op = reinterpret_cast<uint4*>(args.out + (size_t)m * BN + q * 32);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) op[j] = packed[j];
-        }
-        __syncwarp();
-      }
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&tempty[ab]);
-    }
-  }
-  __syncthreads();
-  if (warp == 1) {
-    ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem, TCfg::kTmemCols);
-  }
-  if (threadIdx.x == 0 && *abort_flag) atomicExch(args.error, OMQ_TIMEOUT);
-}
-
-// Halo variant for 128 filters: the 9 taps of a 3x3 conv read 9 row-shifted copies of the same
-// activation rows. Here one TMA load per 64-channel block brings the union of those rows (the
-// tile's 256 rows plus a (S+2)-row halo on each side, 304 rows) into shared memory once, and each
-// tap's UMMA reads a row-shifted window of it (the descriptor simply starts `off` rows in). The
-// weights still stream per tap.
-// L2 -> SM traffic per 256-row tile drops from 18 x (32 + 16) KB to 2 x 38 KB + 18 x 16 KB.
-template <int BS, int SB, int EW = 8>
-struct HaloCfgT {
-  static constexpr int kRows = 256;                          // output rows per tile
-  static constexpr int kLead = 24;                           // halo rows before the tile (>= S+2, multiple of 8)
-  static constexpr int kHaloRows = 304;                      // kLead + 256 + 24
-  static constexpr int kHaloBox = 152;                       // two TMA boxes of 152 rows
-  static constexpr int kA = kHaloRows * 128;                 // 38,912 B
-  static constexpr int kAStages = 2;
-  static constexpr int kB = 128 * 128;                       // one tap's weights, 16 KB
-  static constexpr int kBStages = BS;                         // weight stages in flight
-  static constexpr int kEpiWarps = EW;                         // a multiple of 4 (TMEM lane quarters)
-  static constexpr int kThreads = 64 + 32 * kEpiWarps;
-  static constexpr int kTmemCols = 512;                      // 2 buffers x 2 sub-tiles x 128
-  static constexpr int kStageBufs = SB;                      // epilogue staging buffers per warp
-  static constexpr int kStaging = kEpiWarps * SB * 2048;
-  static constexpr int kSmem = kAStages * kA + kBStages * kB + kStaging + 1024 + 512 + 128 * 4;
-  static_assert(kSmem <= 232448, "227 KB of shared memory per CTA");
-};
-using HaloCfg = HaloCfgT<6, 2>;
-
-template <int BS, int SB, int EW>
-__global__ void __launch_bounds__(HaloCfgT<BS, SB, EW>::kThreads, 1)
-    k_conv3x3_halo(const __grid_constant__ CUtensorMap tmH, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmO, ConvArgs args) {
-  using Cfg = HaloCfgT<BS, SB, EW>;
-  constexpr int BN = 128;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  uint8_t* a_ring = smem;                                     // 2 x 38,912 (38 x 1024)
-  uint8_t* b_ring = smem + Cfg::kAStages * Cfg::kA;           // 6 x 16 KB
-  uint8_t* staging = b_ring + Cfg::kBStages * Cfg::kB;
-  uint64_t* afull = reinterpret_cast<uint64_t*>(staging + Cfg::kStaging);
-  uint64_t* aempty = afull + Cfg::kAStages;
-  uint64_t* bfull = aempty + Cfg::kAStages;
-  uint64_t* bempty = bfull + Cfg::kBStages;
-  uint64_t* tfull = bempty + Cfg::kBStages;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* s_bias = reinterpret_cast<float*>(staging + Cfg::kStaging + 512);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_pos = args.d_count ? min(*args.d_count, args.count) : args.count;
-  const int rows = n_pos * args.P;
-  const int tiles = (rows + Cfg::kRows - 1) / Cfg::kRows;
-  const int CB = args.kb_per_tap;
-  const int rowstride = args.S + 1;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < Cfg::kAStages; ++s) { ptx::mbar_init(&afull[s], 1); ptx::mbar_init(&aempty[s], 1); }
-    for (int s = 0; s < Cfg::kBStages; ++s) { ptx::mbar_init(&bfull[s], 1); ptx::mbar_init(&bempty[s], 1); }
-    for (int i = 0; i < 2; ++i) { ptx::mbar_init(&tfull[i], 1); ptx::mbar_init(&tempty[i], Cfg::kEpiWarps); }
-    ptx::mbar_init(drain, 1);
-    *abort_flag = 0;
-    ptx::fence_barrier_init();
-    ptx::prefetch_tmap(&tmH);
-    ptx::prefetch_tmap(&tmB);
-    ptx::prefetch_tmap(&tmO);
-  }
-  for (int i = threadIdx.x; i < BN; i += blockDim.x) s_bias[i] = args.bias[i];
-  if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, Cfg::kTmemCols);
-    ptx::tmem_relinquish();
-  }
-  ptx::tc_fence_before();
-  __syncthreads();
-  ptx::tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer: per 64-channel block one halo, then 9 weight taps -------
-    int sa = 0, sb = 0;
-    uint32_t pa = 0, pb = 0;
-    int a_issued[Cfg::kAStages], b_issued[Cfg::kBStages];
-    for (int i = 0; i < Cfg::kAStages; ++i) a_issued[i] = -1;
-    for (int i = 0; i < Cfg::kBStages; ++i) b_issued[i] = -1;
-    for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
-      const int h0 = tile * Cfg::kRows - Cfg::kLead;
-      for (int cb = 0; cb < CB; ++cb) {
-        if (!ptx::mbar_wait(&aempty[sa], pa ^ 1, abort_flag, kWaitLimitNs)) goto producer_done;
-        ptx::mbar_arrive_expect_tx(&afull[sa], Cfg::kA);
-        uint8_t* dst = a_ring + sa * Cfg::kA;
-        ptx::tma_load_2d(dst, &tmH, &afull[sa], cb * kBlockK, h0);
-        ptx::tma_load_2d(dst + Cfg::kHaloBox * 128, &tmH, &afull[sa], cb * kBlockK, h0 + Cfg::kHaloBox);
-        a_issued[sa] = (int)pa;
-        if (++sa == Cfg::kAStages) { sa = 0; pa ^= 1; }
-        for (int tap = 0; tap < 9; ++tap) {
-          if (!ptx::mbar_wait(&bempty[sb], pb ^ 1, abort_flag, kWaitLimitNs)) goto producer_done;
-          ptx::mbar_arrive_expect_tx(&bfull[sb], Cfg::kB);
-          ptx::tma_load_2d(b_ring + sb * Cfg::kB, &tmB, &bfull[sb], (tap * CB + cb) * kBlockK, 0);
-          b_issued[sb] = (int)pb;
-          if (++sb == Cfg::kBStages) { sb = 0; pb ^= 1; }
-        }
-      }
-    }
-  producer_done:
-    for (int i = 0; i < Cfg::kAStages; ++i)
-      if (a_issued[i] >= 0) {
-        volatile int dummy = 0;
-        ptx::mbar_wait(&afull[i], (uint32_t)a_issued[i], &dummy, kWaitLimitNs);
-      }
-    for (int i = 0; i < Cfg::kBStages; ++i)
-      if (b_issued[i] >= 0) {
-        volatile int dummy = 0;
-        ptx::mbar_wait(&bfull[i], (uint32_t)b_issued[i], &dummy, kWaitLimitNs);
-      }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer ----------------
-    constexpr uint32_t idesc = ptx::idesc_bf16_f32(kTileM, BN);
-    const uint64_t b_desc0 = ptx::smem_desc_sw128(ptx::smem_u32(b_ring));
-    int tap_row[9];
-#pragma unroll
-    for (int tap = 0; tap < 9; ++tap) tap_row[tap] = (tap / 3 - 1) * rowstride + (tap % 3 - 1);
-    int sa = 0, sb = 0;
-    uint32_t pa = 0, pb = 0;
-    bool any = false;
-    int t = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
-      const int ab = t & 1;
-      const uint32_t aph = (t >> 1) & 1;
-      if (!ptx::mbar_wait(&tempty[ab], aph ^ 1, abort_flag, kWaitLimitNs)) break;
-      ptx::tc_fence_after();
-      const uint32_t d = tmem + ab * 2 * BN;
-      bool ok = true;
-      for (int cb = 0; cb < CB && ok; ++cb) {
-        if (!ptx::mbar_wait(&afull[sa], pa, abort_flag, kWaitLimitNs)) { ok = false; break; }
-        ptx::tc_fence_after();
-        // Descriptors are advanced by adding (byte offset >> 4) to the start-address field: the
-        // single issuing thread must spend as few instructions per MMA as possible (measured: a
-        // few extra integer instructions per MMA leave the tensor pipe idle a third of the time).
-        const uint64_t a_desc0 = ptx::smem_desc_sw128(ptx::smem_u32(a_ring + sa * Cfg::kA));
-#pragma unroll
-        for (int tap = 0; tap < 9; ++tap) {
-          if (!ptx::mbar_wait(&bfull[sb], pb, abort_flag, kWaitLimitNs)) { ok = false; break; }
-          ptx::tc_fence_after();
-          const int off = Cfg::kLead + tap_row[tap];
-          const uint64_t ad = a_desc0 + (uint64_t)(off * 8);           // off rows of 128 B
-          const uint64_t bd = b_desc0 + (uint64_t)(sb * (Cfg::kB >> 4));
-          const uint32_t acc0 = (cb | tap) != 0;
-          ptx::mma_bf16(d, ad, bd, idesc, acc0);
-          ptx::mma_bf16(d + BN, ad + 1024, bd, idesc, acc0);             // + 128 rows
-#pragma unroll
-          for (int k = 1; k < kBlockK / 16; ++k) {
-            ptx::mma_bf16(d, ad + 2 * k, bd + 2 * k, idesc, 1u);         // + 32 B along K
-            ptx::mma_bf16(d + BN, ad + 1024 + 2 * k, bd + 2 * k, idesc, 1u);
-          }
-          any = true;
-          ptx::mma_commit(&bempty[sb]);
-          if (++sb == Cfg::kBStages) { sb = 0; pb ^= 1; }
-        }
-        if (!ok) break;
-        ptx::mma_commit(&aempty[sa]);
-        if (++sa == Cfg::kAStages) { sa = 0; pa ^= 1; }
-      }
-      if (!ok) break;
-      ptx::mma_commit(&tfull[ab]);
-    }
-    if (any) {
-      ptx::mma_commit(drain);
-      volatile int dummy = 0;
-      ptx::mbar_wait(drain, 0, &dummy, kWaitLimitNs);
-    }
-  } else if (warp >= 2) {
-    // ---------------- epilogue ----------------
-    // Warp w may read TMEM lanes 32q..32q+31 with q = w % 4 (rows 32q.. of each 128-row sub-tile).
-    // The kEpiWarps / 4 warps of a lane quarter split its 8 units (2 sub-tiles x 4 chunks of 32
-    // channels). Each 32 rows x 32 channels chunk is staged in shared memory (64-byte swizzle)
-    // and written by one TMA store, instead of 32 scattered 16-byte row stores.
-    constexpr int kPerQ = Cfg::kEpiWarps / 4;
-    const int q = warp & 3;
-    const int wq = (warp - 2) >> 2;
-    uint8_t* my_stage = staging + (warp - 2) * Cfg::kStageBufs * 2048;
-    int buf = 0;
-    int t = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
-      const int ab = t & 1;
-      const uint32_t aph = (t >> 1) & 1;
-      if (!ptx::mbar_wait(&tfull[ab], aph, abort_flag, kWaitLimitNs)) break;
-      ptx::tc_fence_after();
-#pragma unroll 1
-      for (int u = wq; u < 8; u += kPerQ) {
-      const int sub = u >> 2, c0 = (u & 3) * 32;
-      const int row0 = tile * Cfg::kRows + sub * kTileM + q * 32;
-      const int m = row0 + lane;
-      const bool valid = m < rows;
-      const int pix = m % args.P;
-      const int y = pix / rowstride, x = pix - y * rowstride;
-      const bool pad = !valid || (y == args.S) || (x == args.S);
-      const __nv_bfloat16* rrow = args.residual ? args.residual + (size_t)m * BN : nullptr;
-      {
-        uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + ab * 2 * BN + sub * BN + c0, r);
-        ptx::tmem_ld_wait();
-        uint4 packed[4];
-        uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
-        if (pad) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) pw[j] = 0u;
-        } else {
-          float res[32];
-          if (rrow) {
-            const uint4* rp = reinterpret_cast<const uint4*>(rrow + c0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint4 u = rp[j];
-              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                float2 f = __bfloat1622float2(h[e]);
-                res[8 * j + 2 * e] = f.x;
-                res[8 * j + 2 * e + 1] = f.y;
-              }
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) res[j] = 0.0f;
-          }
-#pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            float v0 = __uint_as_float(r[j]) + s_bias[c0 + j] + res[j];
-            float v1 = __uint_as_float(r[j + 1]) + s_bias[c0 + j + 1] + res[j + 1];
-            if (args.relu) { v0 = fmaxf(v0, 0.0f); v1 = fmaxf(v1, 0.0f); }
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
-            pw[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
-          }
-        }
-        // the buffer about to be written must no longer be read by an earlier store
-        if (lane == 0) ptx::bulk_wait_read<Cfg::kStageBufs - 1>();
-        __syncwarp();
-        uint8_t* sb = my_stage + buf * 2048;
-        const int sw = (lane >> 1) & 3;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(sb + lane * 64 + ((j ^ sw) * 16)) = packed[j];
-        ptx::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          ptx::tma_store_2d(&tmO, sb, c0, row0);
-          ptx::bulk_commit();
-        }
-        buf = buf + 1 == Cfg::kStageBufs ? 0 : buf + 1;
-      }
-      }
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&tempty[ab]);
-    }
-    if (lane == 0) ptx::bulk_wait<0>();
-  }
-  __syncthreads();
-  if (warp == 1) {
-    ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem, Cfg::kTmemCols);
-  }
-  if (threadIdx.x == 0 && *abort_flag) atomicExch(args.error, OMQ_TIMEOUT);
-}
-
-// Sub-tiles per CTA tile for a given filter count (must match the A tensor maps' box height).
-__host__ __device__ constexpr int conv_sub(int filters) { return filters == 128 ? 2 : 1; }
 
 
 // Transposed halo variant for 128 filters: D[channel][pixel] = W[channel][K] . X[pixel][K]^T, so
@@ -1695,14 +1012,15 @@ struct omq_resnet {
 };
 
 // cudaFuncSetAttribute(kernel, MaxDynamicSharedMemorySize, bytes) once per device (bit dev of
-// `done`); safe when several host threads drive engines on different devices.
+// `done`, so ordinals 0..63); safe when several host threads drive engines on different devices.
+// An ordinal of 64 or more sets the attribute on every call.
 template <class K>
-static cudaError_t set_smem_attr_once(std::atomic<uint32_t>& done, K kernel, cudaFuncAttribute attr,
+static cudaError_t set_smem_attr_once(std::atomic<uint64_t>& done, K kernel, cudaFuncAttribute attr,
                                       int bytes) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  const uint32_t bit = 1u << (dev & 31);
+  const uint64_t bit = dev < 64 ? (uint64_t)1 << dev : 0;
   if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
   e = cudaFuncSetAttribute(kernel, attr, bytes);
   if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
@@ -1751,26 +1069,14 @@ static int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t o
   return OMQ_OK;
 }
 
-// Conv kernel variant per filter count (OMQ_CONV_KERNEL=single|pair|transposed|halo|halot forces one,
-// for measurements): 0 = single CTA, 1 = CTA pair (default for 256 filters: 1.16 vs 1.07 PFLOP/s),
-// 2 = transposed, 3 = halo, 4 = transposed halo (default for 128 filters: 1.12 vs 0.94 PFLOP/s for
-// the halo kernel at batch 65,536, power-capped).
-static int conv_variant(int filters) {
-  const char* v = getenv("OMQ_CONV_KERNEL");
-  if (v && strcmp(v, "single") == 0) return 0;
-  if (v && strcmp(v, "pair") == 0) return 1;
-  if (v && strcmp(v, "transposed") == 0 && filters == 128) return 2;
-  if (v && strcmp(v, "halo") == 0 && filters == 128) return 3;
-  if (v && strcmp(v, "halot") == 0 && filters == 128) return 4;
-  return filters == 256 ? 1 : 4;
-}
+// Conv kernel per filter count: 1 = CTA pair (256 filters), 4 = transposed halo (128 filters).
+static int conv_variant(int filters) { return filters == 256 ? 1 : 4; }
 
 // Tensor maps of a net's activation buffers and weights. Box heights follow the kernel variant:
-// A boxes are 128 rows (pair) or 128 * conv_sub(C) rows (single CTA); weight boxes are the CTA's
-// half of the output channels (pair) or all of them.
+// A boxes are 128 rows (pair) or two 152-row halo boxes (transposed halo); weight boxes are the
+// CTA's half of the output channels (pair) or all of them.
 static int build_maps(omq_resnet* n) {
-  const uint32_t a_rows = n->pair == 1 ? kTileM : (n->pair == 3 || n->pair == 4) ? HaloCfg::kHaloBox
-                                                                                : kTileM * conv_sub(n->C);
+  const uint32_t a_rows = n->pair == 1 ? kTileM : HaloTCfg::kHaloBox;
   const uint32_t b_rows = n->pair == 1 ? n->C / 2 : n->C;
   int st = make_map(&n->tmA_in, n->x_in, n->in_pad, n->rows, a_rows);
   for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n->tmA[i], n->act[i], n->C, n->rows, a_rows);
@@ -1799,14 +1105,6 @@ static size_t head_smem_for(const omq_resnet* n, int hp) {
   return sizeof(float) * ((size_t)hp * (3 * n->HW + n->Hp + n->A + n->Hv) + 3 * n->C);
 }
 static size_t head_smem(const omq_resnet* n) { return head_smem_for(n, kHeadPos); }
-// Positions per heads block: 8 (measured on B200 for ResNet 10x128 at 16,384 positions: 1.00 ms
-// with 8, 1.09 ms with 16; OMQ_HEAD_POS=16 selects 16 where it fits).
-static int head_pos(const omq_resnet* n) {
-  const char* e = getenv("OMQ_HEAD_POS");
-  if (e && strcmp(e, "16") == 0 && head_smem_for(n, 16) <= 227 * 1024) return 16;
-  return 8;
-}
-
 // Self-test of the bounded wait every pipelined kernel here uses: one thread waits on an mbarrier
 // that nothing arrives on. After limit_ns the wait gives up and raises the abort flag, and the
 // kernel stores OMQ_TIMEOUT in *status and returns, leaving the context usable.
@@ -1871,8 +1169,7 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
   for (int i = 0; i < 3; ++i) take(n->rows * n->C * 2);
   take(16);
   // tensor-core heads: fc1 width a multiple of 64 (it is the next layer's K), value width <= 256
-  n->tc_heads = (n->Hp % 64 == 0 && n->Hp <= 1024 && n->Hv % 16 == 0 && n->Hv <= 256 &&
-                 !(getenv("OMQ_SIMT_HEADS") && strcmp(getenv("OMQ_SIMT_HEADS"), "1") == 0)) ? 1 : 0;
+  n->tc_heads = (n->Hp % 64 == 0 && n->Hp <= 1024 && n->Hv % 16 == 0 && n->Hv <= 256) ? 1 : 0;
   n->k1p = (2 * n->HW + 63) / 64 * 64;
   n->k3p = (n->HW + 63) / 64 * 64;
   n->n1pad = (n->Hp + 255) / 256 * 256;
@@ -1987,76 +1284,11 @@ int omq_resnet_memory(const omq_resnet* n, uint64_t* bytes) {
 
 namespace omq {
 
-template <int BN, int SUB>
-static int launch_conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB,
-                       const CUtensorMap& tO, const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
-                       int kb_per_tap, const int32_t* d_count, int count, cudaStream_t s) {
-  using Cfg = ConvCfg<BN, SUB>;
-  static std::atomic<uint32_t> attr_set{0};
-  {
-    const cudaError_t e = set_smem_attr_once(attr_set, k_conv3x3<BN, SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg::kSmem);
-    if (e != cudaSuccess) return cuda_status(e, "conv smem attribute");
-  }
-  ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
-  const int max_tiles = (int)((n->rows + Cfg::kRows - 1) / Cfg::kRows);
-  const int grid = max(1, min(max_tiles, n->sm_count));
-  count_launches(1);
-  k_conv3x3<BN, SUB><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(tA, tB, tO, a);
-  return cuda_status(cudaGetLastError(), "k_conv3x3");
-}
-
-template <int BS, int SB, int EW>
-static int launch_conv_halo_t(const omq_resnet* n, const CUtensorMap& tH, const CUtensorMap& tB,
-                              const CUtensorMap& tO, const ConvArgs& a, cudaStream_t s) {
-  using Cfg = HaloCfgT<BS, SB, EW>;
-  static std::atomic<uint32_t> attr_set{0};
-  {
-    const cudaError_t e = set_smem_attr_once(attr_set, k_conv3x3_halo<BS, SB, EW>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
-    if (e != cudaSuccess) return cuda_status(e, "halo conv smem attribute");
-  }
-  const int max_tiles = (int)((n->rows + Cfg::kRows - 1) / Cfg::kRows);
-  const int grid = max(1, min(max_tiles, n->sm_count));
-  count_launches(1);
-  k_conv3x3_halo<BS, SB, EW><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(tH, tB, tO, a);
-  return cuda_status(cudaGetLastError(), "k_conv3x3_halo");
-}
-
-// Weight stages x staging buffers x epilogue warps of the halo kernel
-// (OMQ_HALO_PIPE=6x2|8x1|6x2e12|4x2e16|5x1e16).
-static int halo_pipe() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("OMQ_HALO_PIPE");
-    v = 0;
-    if (e && strcmp(e, "8x1") == 0) v = 2;
-    if (e && strcmp(e, "6x2e12") == 0) v = 3;
-    if (e && strcmp(e, "4x2e16") == 0) v = 4;
-    if (e && strcmp(e, "5x1e16") == 0) v = 5;
-  }
-  return v;
-}
-
-static int launch_conv_halo(const omq_resnet* n, const CUtensorMap& tH, const CUtensorMap& tB,
-                            const CUtensorMap& tO, const float* bias, const __nv_bfloat16* res,
-                            __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count, int count,
-                            cudaStream_t s) {
-  ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
-  switch (halo_pipe()) {
-    case 2: return launch_conv_halo_t<8, 1, 8>(n, tH, tB, tO, a, s);
-    case 3: return launch_conv_halo_t<6, 2, 12>(n, tH, tB, tO, a, s);
-    case 4: return launch_conv_halo_t<4, 2, 16>(n, tH, tB, tO, a, s);
-    case 5: return launch_conv_halo_t<5, 1, 16>(n, tH, tB, tO, a, s);
-    default: return launch_conv_halo_t<6, 2, 8>(n, tH, tB, tO, a, s);
-  }
-}
-
 static int launch_conv_halo_tr(const omq_resnet* n, const CUtensorMap& tH, const CUtensorMap& tB,
                                const CUtensorMap& tO, const float* bias, const __nv_bfloat16* res,
                                __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count, int count,
                                cudaStream_t s) {
-  static std::atomic<uint32_t> attr_set{0};
+  static std::atomic<uint64_t> attr_set{0};
   {
     const cudaError_t e = set_smem_attr_once(attr_set, k_conv3x3_halo_t, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          HaloTCfg::kSmem);
@@ -2070,29 +1302,12 @@ static int launch_conv_halo_tr(const omq_resnet* n, const CUtensorMap& tH, const
   return cuda_status(cudaGetLastError(), "k_conv3x3_halo_t");
 }
 
-static int launch_conv_t(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB,
-                         const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
-                         int kb_per_tap, const int32_t* d_count, int count, cudaStream_t s) {
-  static std::atomic<uint32_t> attr_set{0};
-  {
-    const cudaError_t e = set_smem_attr_once(attr_set, k_conv3x3_t, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         TCfg::kSmem);
-    if (e != cudaSuccess) return cuda_status(e, "transposed conv smem attribute");
-  }
-  ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
-  const int max_tiles = (int)((n->rows + TCfg::kPix - 1) / TCfg::kPix);
-  const int grid = max(1, min(max_tiles, n->sm_count));
-  count_launches(1);
-  k_conv3x3_t<<<grid, TCfg::kThreads, TCfg::kSmem, s>>>(tA, tB, a);
-  return cuda_status(cudaGetLastError(), "k_conv3x3_t");
-}
-
 template <int BN>
 static int launch_conv_pair(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB,
                             const CUtensorMap& tO, const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
                             int kb_per_tap, const int32_t* d_count, int count, cudaStream_t s) {
   using Cfg = PairCfg<BN>;
-  static std::atomic<uint32_t> attr_set{0};
+  static std::atomic<uint64_t> attr_set{0};
   {
     const cudaError_t e = set_smem_attr_once(attr_set, k_conv3x3_pair<BN>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
@@ -2110,21 +1325,14 @@ static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& t
                 const float* bias,
                 const __nv_bfloat16* res, __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count,
                 int count, cudaStream_t s) {
-  if (n->pair == 4) return launch_conv_halo_tr(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
-  if (n->pair == 3) return launch_conv_halo(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
-  if (n->pair == 2) return launch_conv_t(n, tA, tB, bias, res, out, kb_per_tap, d_count, count, s);
-  if (n->pair == 1) {
-    if (n->C == 128) return launch_conv_pair<128>(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
-    return launch_conv_pair<256>(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
-  }
-  if (n->C == 128) return launch_conv<128, conv_sub(128)>(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
-  return launch_conv<256, conv_sub(256)>(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
+  if (n->pair == 1) return launch_conv_pair<256>(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
+  return launch_conv_halo_tr(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
 }
 
 template <int NT, int MODE>
 static int launch_dense(const CUtensorMap& tA, const CUtensorMap& tW, const DenseArgs& a, int rows_cap,
                         int ntiles, cudaStream_t s) {
-  static std::atomic<uint32_t> attr_set{0};
+  static std::atomic<uint64_t> attr_set{0};
   {
     const cudaError_t e = set_smem_attr_once(attr_set, k_dense<NT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDenseSmem);
     if (e != cudaSuccess) return cuda_status(e, "dense smem attribute");
@@ -2227,15 +1435,12 @@ int resnet_run(omq_resnet* n, const int32_t* d_count, int count, float* policy, 
   h.count = count;
   h.policy = policy;
   h.value = value;
-  const int hpos = head_pos(n);
-  const size_t sm = head_smem_for(n, hpos);
-  cudaError_t e = cudaFuncSetAttribute(hpos == 16 ? k_heads<16> : k_heads<8>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  const size_t sm = head_smem_for(n, kHeadPos);
+  cudaError_t e = cudaFuncSetAttribute(k_heads<kHeadPos>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return cuda_status(e, "heads smem attribute");
-  const int blocks = (count + hpos - 1) / hpos;
+  const int blocks = (count + kHeadPos - 1) / kHeadPos;
   count_launches(1);
-  if (hpos == 16) k_heads<16><<<blocks, kHeadThreads, sm, s>>>(h);
-  else k_heads<8><<<blocks, kHeadThreads, sm, s>>>(h);
+  k_heads<kHeadPos><<<blocks, kHeadThreads, sm, s>>>(h);
   return cuda_status(cudaGetLastError(), "k_heads");
 }
 
@@ -2376,20 +1581,34 @@ namespace omq {
 constexpr int kMaxDevices = 64;
 // Device address of g_noalloc_scratch per device ordinal, looked up once per device with that
 // device current. In host code the array's name is only a host-side stand-in, never a usable
-// device address.
-static uint8_t* g_noalloc_ptr[kMaxDevices];
+// device address. Threads that race on a first lookup store the same address.
+static std::atomic<uint8_t*> g_noalloc_ptr[kMaxDevices];
 
+// Makes `dev` current (the caller's DeviceGuard restores the previous device) and returns the
+// scratch array's device address on it.
 static int noalloc_scratch(int dev, uint8_t** out) {
-  if (dev < 0 || dev >= kMaxDevices) { set_error("device ordinal %d out of range", dev); return OMQ_BAD_ARG; }
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(no-alloc scratch)");
-    g_noalloc_ptr[dev] = static_cast<uint8_t*>(p);
+  int ndev = 0;
+  cudaError_t e = cudaGetDeviceCount(&ndev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDeviceCount");
+  if (dev < 0 || dev >= ndev || dev >= kMaxDevices) {
+    set_error("device ordinal %d out of range (%d devices)", dev, ndev);
+    return OMQ_BAD_ARG;
   }
-  *out = g_noalloc_ptr[dev];
+  e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaSetDevice");
+  uint8_t* p = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (!p) {
+    void* q = nullptr;
+    e = cudaGetSymbolAddress(&q, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    p = static_cast<uint8_t*>(q);
+    g_noalloc_ptr[dev].store(p, std::memory_order_release);
+  }
+  *out = p;
   return OMQ_OK;
 }
+// The error word sits in the last 256 bytes of the scratch, clear of the activations.
+constexpr size_t kNoAllocErrorOffset = kNoAllocScratchBytes - 256;
 }  // namespace omq
 
 extern "C" int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const uint16_t* d_conv_w,
@@ -2450,7 +1669,7 @@ extern "C" int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const ui
     n.act[i] = reinterpret_cast<__nv_bfloat16*>(base + off);
     off += ((n.rows * n.C * 2) + 255) & ~(size_t)255;
   }
-  n.error = reinterpret_cast<int32_t*>(base + kNoAllocScratchBytes - 256);
+  n.error = reinterpret_cast<int32_t*>(base + kNoAllocErrorOffset);
   n.tmB = maps;
   n.loaded = 1;
   n.pair = conv_variant(n.C);
@@ -2466,4 +1685,20 @@ extern "C" int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const ui
   st = cuda_status(cudaGetLastError(), "k_pack_features");
   if (st) return st;
   return resnet_run(&n, nullptr, batch, d_policy, d_value, s);
+}
+
+// Reads the error word of the last omq_resnet_forward_noalloc call on `device` (OMQ_OK, or
+// OMQ_TIMEOUT when a pipelined kernel's bounded wait gave up) after the work queued on `stream`.
+// Like the forward itself, it allocates nothing: the word is copied into the caller's int.
+extern "C" int omq_resnet_noalloc_error(int32_t device, int32_t* h_error, void* stream) {
+  if (!h_error) { set_error("null argument"); return OMQ_BAD_ARG; }
+  DeviceGuard g(device);
+  uint8_t* base = nullptr;
+  int st = omq::noalloc_scratch(device, &base);
+  if (st) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemcpyAsync(h_error, base + omq::kNoAllocErrorOffset, sizeof(int32_t),
+                                  cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  return cuda_status(e, "omq_resnet_noalloc_error");
 }

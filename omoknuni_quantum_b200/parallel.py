@@ -40,18 +40,29 @@ def shard_range(total: int, world_size: int, rank: int) -> range:
 
 def broadcast_state_dict(sd: Optional[Dict[str, torch.Tensor]], device, src: int = 0,
                          keys: Optional[Sequence[str]] = None) -> Dict[str, torch.Tensor]:
-    """Broadcast every tensor of rank `src`'s state_dict to all ranks (one collective per
-    tensor, sorted key order). Non-source ranks may pass sd=None together with the key list and
-    shapes obtained from the same spec; here they pass a same-shaped template."""
+    """Broadcast rank `src`'s state_dict to all ranks in ONE collective: the tensors (sorted key
+    order) are packed byte for byte into a single uint8 buffer on `device`, broadcast, and cut
+    apart again, so every dtype arrives bit-exact. Every rank passes a state_dict of the
+    source's keys, shapes and dtypes (a template built from the same spec)."""
     if not initialized() or dist.get_world_size() == 1:
         return dict(sd)
     if sd is None:
         raise ValueError("every rank needs a template state_dict with the source's shapes")
-    out = {}
-    for k in sorted(sd if keys is None else keys):
-        t = sd[k].detach().to(device).contiguous()
-        dist.broadcast(t, src=src)
-        out[k] = t.cpu()
+    names = sorted(sd if keys is None else keys)
+    tensors = [sd[k].detach().contiguous() for k in names]
+    sizes = [t.numel() * t.element_size() for t in tensors]
+    buf = torch.empty(sum(sizes), dtype=torch.uint8, device=device)
+    if dist.get_rank() == src:
+        off = 0
+        for t, n in zip(tensors, sizes):
+            buf[off:off + n].copy_(t.reshape(-1).view(torch.uint8))
+            off += n
+    dist.broadcast(buf, src=src)
+    host = buf.cpu()
+    out, off = {}, 0
+    for k, t, n in zip(names, tensors, sizes):
+        out[k] = host[off:off + n].clone().view(t.dtype).reshape(t.shape)
+        off += n
     return out
 
 

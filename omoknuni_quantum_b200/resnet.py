@@ -288,35 +288,3 @@ class ResNetEvaluator:
         e = ctypes.c_int32()
         _lib.check(self.L.omq_resnet_error(self._net, ctypes.byref(e), _stream_ptr()), "omq_resnet_error")
         return int(e.value)
-
-
-def _main(argv=None) -> None:
-    """Standalone forward passes on seeded random weights and features, e.g. as a profiling
-    target: ``python -m omoknuni_quantum_b200.resnet --batch 4096 --blocks 10 --filters 128``;
-    ``--game go`` (19x19, 17 planes, 362 actions) or ``--game chess`` (8x8, 119 planes, 4672
-    actions) for the shapes of the Go and chess workloads."""
-    import argparse
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--batch", type=int, default=4096)
-    ap.add_argument("--blocks", type=int, default=10)
-    ap.add_argument("--filters", type=int, default=128)
-    ap.add_argument("--iters", type=int, default=3)
-    ap.add_argument("--game", choices=["gomoku", "go", "chess"], default="gomoku")
-    a = ap.parse_args(argv)
-    n, planes, acts = {"gomoku": (15, 19, 225), "go": (19, 17, 362), "chess": (8, 119, 4672)}[a.game]
-    spec = ResNetSpec(board_size=n, input_channels=planes, num_blocks=a.blocks, filters=a.filters,
-                      num_actions=acts, fc_value_hidden=128 if a.game == "gomoku" else 256)
-    ev = ResNetEvaluator.random(spec, seed=0, max_batch=a.batch)
-    g = torch.Generator().manual_seed(0)
-    x = torch.zeros(a.batch, planes, n, n)
-    x[:, 0] = (torch.rand(a.batch, n, n, generator=g) < 0.2).float()
-    x[:, 1] = (torch.rand(a.batch, n, n, generator=g) < 0.2).float()
-    x = x.to(ev.device)
-    for _ in range(a.iters):
-        ev.evaluate_batch(x)
-    torch.cuda.synchronize()
-    print(f"ok game={a.game} batch={a.batch} error={ev.error()}")
-
-
-if __name__ == "__main__":
-    _main()

@@ -14,7 +14,7 @@ Each case is written to tests/golden/search_<name>.npz with:
   * a digest of every feature tensor the reference passed to its evaluator, in call order.
 
 Usage (needs the reference tree and its C++ game engines built by `make -C oracle ref`):
-    python tests/golden/make_golden.py [--reference /root/reference] [--only NAME ...]
+    python tests/golden/make_golden.py --reference <reference source tree>  (or OMQ_REFERENCE) [--only NAME ...]
 This runs only in the build container; the GPU box never reads the reference.
 """
 from __future__ import annotations
@@ -241,7 +241,7 @@ def run_reference_gpu_reuse(board, sims, wave, searches, cap=200000):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("OMQ_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("OMQ_REFERENCE"), required="OMQ_REFERENCE" not in os.environ)
     ap.add_argument("--only", nargs="*")
     args = ap.parse_args()
     sys.dont_write_bytecode = True

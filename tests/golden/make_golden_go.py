@@ -30,7 +30,7 @@ def board_of(state, n):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("OMQ_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("OMQ_REFERENCE"), required="OMQ_REFERENCE" not in os.environ)
     ap.parse_args()
     sys.path.insert(0, os.path.join(REPO, "oracle", "_ref"))
     import alphazero_py as az

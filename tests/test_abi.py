@@ -35,19 +35,6 @@ def test_status_strings_without_gpu():
     assert L.omq_status_string(0) == b"ok"
 
 
-def test_integration_stub_matches_engine_config():
-    """The ctypes stub a reference maintainer would copy declares the engine config exactly as the
-    library lays it out (field names and order)."""
-    import os
-    import re
-    from omoknuni_quantum_b200._lib import EngineConfig
-    doc = open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
-                            "INTEGRATION.md")).read()
-    block = doc[doc.index("class EngineConfig"):doc.index("lib.omq_engine_create.argtypes")]
-    names = re.findall(r'\("([a-z_]+)", ctypes\.c_', block)
-    assert names == [f[0] for f in EngineConfig._fields_]
-
-
 def test_struct_layouts_match_the_library():
     """The Python ctypes structures have the sizes the library was compiled with (host call)."""
     import ctypes

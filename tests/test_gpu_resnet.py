@@ -9,6 +9,10 @@ pytestmark = pytest.mark.gpu
 
 TOL = 2e-2
 
+# the fp32 reference forward runs on the GPU: keep its convolutions and matmuls in true fp32
+torch.backends.cudnn.allow_tf32 = False
+torch.backends.cuda.matmul.allow_tf32 = False
+
 
 def _features(n, seed=0):
     """Reference-layout features of random legal-looking positions: occupancy, player plane,
@@ -44,6 +48,64 @@ def test_forward_matches_fp32_reference(blocks, filters, hv):
     assert dp < TOL and dv < TOL, (dp, dv)
     # the policy is a distribution
     assert torch.allclose(p.sum(1), torch.ones_like(p[:, 0]), atol=1e-4)
+
+
+def _calibrate_bn(sd, x):
+    """Running statistics of every BatchNorm set to the batch statistics of `x` as it flows
+    through the net (what a trained checkpoint carries). Without them a 20-block He-initialised
+    trunk grows its activations ~2x per block and every value saturates at +-1, which would make a
+    tolerance check vacuous."""
+    import torch.nn.functional as F
+    from omoknuni_quantum_b200.resnet import BN_EPS
+    sd = dict(sd)
+
+    def bn(t, p):
+        sd[p + ".running_mean"] = t.mean((0, 2, 3))
+        sd[p + ".running_var"] = t.var((0, 2, 3))
+        return F.batch_norm(t, sd[p + ".running_mean"], sd[p + ".running_var"], sd[p + ".weight"],
+                            sd[p + ".bias"], False, 0.0, BN_EPS)
+    h = F.relu(bn(F.conv2d(x, sd["conv_input.weight"], padding=1), "bn_input"))
+    i = 0
+    while f"residual_blocks.{i}.conv1.weight" in sd:
+        p = f"residual_blocks.{i}."
+        o = F.relu(bn(F.conv2d(h, sd[p + "conv1.weight"], padding=1), p + "bn1"))
+        h = F.relu(bn(F.conv2d(o, sd[p + "conv2.weight"], padding=1), p + "bn2") + h)
+        i += 1
+    bn(F.conv2d(h, sd["policy_head.conv.weight"]), "policy_head.bn")
+    bn(F.conv2d(h, sd["value_head.conv.weight"]), "value_head.bn")
+    return sd
+
+
+@pytest.mark.parametrize("game", ["gomoku", "go", "chess"])
+def test_deep_20x256_forward_matches_fp32_reference(game):
+    """The model of configs 2-4 at full depth (20 blocks x 256 filters, 41 bf16 convolutions)
+    against the fp32 forward, on a few hundred positions of each game's shape."""
+    from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec, init_state_dict, reference_forward_fp32
+    n, planes, acts = {"gomoku": (15, 19, 225), "go": (19, 17, 362), "chess": (8, 119, 4672)}[game]
+    hv = 128 if game == "gomoku" else 256
+    spec = ResNetSpec(board_size=n, input_channels=planes, num_blocks=20, filters=256, num_actions=acts,
+                      fc_value_hidden=hv)
+    g = np.random.default_rng(21)
+    x = torch.from_numpy((g.random((300, planes, n, n)) < 0.25).astype(np.float32)).cuda()
+    x[:, -1] = torch.from_numpy(g.integers(0, 2, (300, 1, 1)).astype(np.float32)).cuda()
+    sd = {k: t.cuda() for k, t in init_state_dict(spec, seed=9).items()}
+    with torch.no_grad():
+        sd = _calibrate_bn(sd, x[:128])
+    # a peaked policy: logits of a few units (the initialiser's fc2 gain of 0.1 gives ~0.01)
+    sd["policy_head.fc2.weight"] = sd["policy_head.fc2.weight"] * (30.0 * (acts / 225) ** 0.5)
+    ev = ResNetEvaluator({k: t.cpu() for k, t in sd.items()}, board_size=n, max_batch=300)
+    p, v = ev.evaluate_batch(x)
+    torch.cuda.synchronize()
+    assert ev.error() == 0
+    with torch.no_grad():
+        pr, vr = reference_forward_fp32(sd, x)
+    # the check means something: values spread inside (-1, 1), policies far from uniform
+    assert vr.std().item() > 0.1 and (vr.abs() < 0.99).float().mean().item() > 0.9
+    assert pr.max(1).values.median().item() > 5.0 / acts
+    dp = (p - pr).abs().max().item()
+    dv = (v - vr).abs().max().item()
+    assert torch.isfinite(p).all() and torch.isfinite(v).all()
+    assert dp < TOL and dv < TOL, (dp, dv)
 
 
 def test_forward_is_batch_invariant():

@@ -36,8 +36,16 @@ def _worker(rank, world, port, queue, fail_rank):
                                 timeout=datetime.timedelta(seconds=10))
         spec = ResNetSpec(num_blocks=1, filters=128, fc_value_hidden=16, fc_policy_hidden=16)
         sd = init_state_dict(spec, seed=100 + rank)       # ranks start with different weights
-        sd = parallel.broadcast_state_dict(sd, "cpu")
-        digest = float(sum(v.double().sum() for v in sd.values()))
+        calls = []
+        real = dist.broadcast
+        dist.broadcast = lambda *a, **k: (calls.append(1), real(*a, **k))[1]
+        try:
+            sd = parallel.broadcast_state_dict(sd, "cpu")
+        finally:
+            dist.broadcast = real
+        src = init_state_dict(spec, seed=100)
+        exact = all(torch.equal(sd[k], src[k]) and sd[k].dtype == src[k].dtype for k in src)
+        digest = (float(sum(v.double().sum() for v in sd.values())), len(calls), exact)
         shard = parallel.shard_range(10, world, rank)
         roots = random_roots(5, 10)[shard.start:shard.stop]
         ms = parallel.max_over_ranks(10.0 * (rank + 1), "cpu")
@@ -69,6 +77,7 @@ def test_two_rank_broadcast_shard_and_reduce():
     out = _run(2)
     (r0, d0, s0, _, ms0, tot0, g0), (r1, d1, s1, _, ms1, tot1, g1) = out
     assert d0 == d1                       # rank 1 received rank 0's weights
+    assert d0[1] == 1 and d0[2]           # in one collective, bit-exact in every dtype
     assert s0 == [0, 1, 2, 3, 4] and s1 == [5, 6, 7, 8, 9]
     assert ms0 == ms1 == 20.0             # max over ranks
     assert tot0 == tot1 == 10
