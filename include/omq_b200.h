@@ -315,6 +315,12 @@ OMQ_API int omq_resnet_noalloc_error(int32_t device, int32_t* h_error, void* str
 /* Self-test of the bounded device waits: launches a kernel whose mbarrier wait can never complete;
  * after limit_ns (at most 1 s) it gives up and writes OMQ_TIMEOUT to d_status (int32, device). */
 OMQ_API int omq_selftest_wait_timeout(uint64_t limit_ns, int32_t* d_status, void* stream);
+/* Self-test of the sum behind the prior normalisation p / (sum(p) + 1e-8) that expansion runs
+ * (wave_search.py:894-895, summed in torch's CPU order): writes the sum of each segment
+ * d_x[d_offsets[s] .. d_offsets[s+1]) to d_out[s] (device pointers; no counterpart in the
+ * reference, which has no device sum of its own). */
+OMQ_API int omq_selftest_prior_sum(const float* d_x, const int32_t* d_offsets, int32_t segments,
+                                   float* d_out, void* stream);
 /* Device error word of the net (OMQ_TIMEOUT after a bounded wait gave up); synchronizes. */
 OMQ_API int omq_resnet_error(omq_resnet* net, int32_t* h_error, void* stream);
 

@@ -108,6 +108,7 @@ SIGNATURES = {
     "omq_kernel_launches_add": [ctypes.c_int64],
     "omq_abi_struct_sizes": [ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)],
     "omq_selftest_wait_timeout": [ctypes.c_uint64, _P, _P],
+    "omq_selftest_prior_sum": [_P, _P, _I, _P, _P],
     "omq_resnet_forward_noalloc": [ctypes.POINTER(ResNetConfig), _P, _P, _P, _P, _I, _P, _P, _P],
     "omq_resnet_noalloc_error": [_I, ctypes.POINTER(_I), _P],
 }

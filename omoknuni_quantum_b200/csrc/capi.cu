@@ -442,6 +442,14 @@ int omq_root_visits(omq_engine* e, int32_t* d_visits, float* d_root_nw, void* st
   return OMQ_OK;
 }
 
+int omq_selftest_prior_sum(const float* d_x, const int32_t* d_offsets, int32_t segments, float* d_out,
+                           void* stream) {
+  if (!d_x || !d_offsets || !d_out || segments < 0) { set_error("bad argument"); return OMQ_BAD_ARG; }
+  if (segments == 0) return OMQ_OK;
+  launch_selftest_prior_sum(d_x, d_offsets, segments, d_out, (cudaStream_t)stream);
+  return cuda_status(cudaGetLastError(), "k_selftest_prior_sum");
+}
+
 int omq_export_tree(omq_engine* e, int32_t tree, int32_t count, int32_t* N, float* W, float* P,
                     int32_t* VL, int32_t* parent, int32_t* action, uint8_t* terminal,
                     void* stream) {

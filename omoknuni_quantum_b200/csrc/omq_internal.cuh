@@ -233,6 +233,8 @@ void launch_root_visits(const EngineView& v, int32_t* visits, float* nw, cudaStr
 void launch_export(const EngineView& v, int tree, int count, int32_t* N, float* W, float* P,
                    int32_t* VL, int32_t* parent, int32_t* action, uint8_t* terminal, cudaStream_t s);
 void launch_status(const EngineView& v, int32_t* status, int32_t* num_nodes, cudaStream_t s);
+void launch_selftest_prior_sum(const float* x, const int32_t* offsets, int segments, float* out,
+                               cudaStream_t s);
 void launch_features(const EngineView& v, int queue, float* out, cudaStream_t s);
 void launch_synth_eval(const EngineView& v, int queue, cudaStream_t s);
 // queue positions -> bf16 [count][P][in_pad] padded pixel layout (ResNet input)

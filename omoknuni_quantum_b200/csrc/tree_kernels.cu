@@ -738,16 +738,58 @@ struct ExpandWarpSmem {
   int8_t board[kMaxCells + 3];
 };
 
-// Sum of the legal-move policy in the engine's fixed order: lane L adds slots L, L+32, ...
-// sequentially, then a butterfly over the 32 partial sums. Exact for the synthetic evaluator
-// (all partial sums are exact fp32 integers times 2^-24); for a general evaluator the oracle
-// reproduces this order.
-__device__ float warp_fixed_order_sum(const float* pv, int n) {
+// Sum of the legal-move policy pv[0..n) in exactly the order in which torch's CPU sum kernel adds
+// a contiguous fp32 vector, which is what the reference's `priors.sum()` runs on its CPU path
+// (wave_search.py:894-895). That kernel (ATen's cascade sum for an inner reduction) views the
+// vector as 8-lane vectors: 4 interleaved vector accumulators take rows of 32 elements (lane L of
+// this warp holds accumulator L, i.e. elements L, L+32, L+64, ...); after every 16 rows the
+// accumulators are added into a second level and restarted (a third level after 256 rows, and so
+// on); the full vectors left after the last row go to the first vector accumulator; the four
+// vector accumulators are then added 0+1, +2, +3; finally a scalar starting at 0 adds the elements
+// after the last full vector, then the 8 lanes in order. Fewer than 8 elements: 4 scalar
+// accumulators instead of vectors, the same way. The order is pinned against torch.sum for every
+// length up to 5,000 (oracle/torch_sum.cpp holds the host twin) and is the same under the AVX2,
+// AVX-512 and default CPU kernels. Valid for n < 2^21 (16-row cascade blocks).
+__device__ float warp_torch_sum(const float* pv, int n) {
   const int lane = threadIdx.x & 31;
-  float s = 0.0f;
-  for (int j = lane; j < n; j += 32) s = __fadd_rn(s, pv[j]);
-  for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, o));
-  return s;
+  float r = 0.0f;
+  if (n < 8) {
+    if (lane == 0) {
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      const int rows = n >> 2;  // 0 or 1 row of 4 scalars
+      for (int k = 0; k < 4 * rows; ++k) acc[k] = __fadd_rn(acc[k], pv[k]);
+      for (int k = 4 * rows; k < n; ++k) acc[0] = __fadd_rn(acc[0], pv[k]);
+      r = __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), acc[2]), acc[3]);
+    }
+    return __shfl_sync(0xFFFFFFFFu, r, 0);
+  }
+  const int vecs = n >> 3, rows = vecs >> 2;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  int i = 0;
+  for (; i + 16 <= rows;) {
+    for (int j = 0; j < 16; ++j, ++i) acc[0] = __fadd_rn(acc[0], pv[32 * i + lane]);
+#pragma unroll
+    for (int l = 1; l < 4; ++l) {
+      acc[l] = __fadd_rn(acc[l], acc[l - 1]);
+      acc[l - 1] = 0.0f;
+      if (i & (15 << (4 * l))) break;
+    }
+  }
+  for (; i < rows; ++i) acc[0] = __fadd_rn(acc[0], pv[32 * i + lane]);
+  float a = __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), acc[2]), acc[3]);
+  // full vectors after the last row: into vector accumulator 0 (lanes 0..7)
+  if (lane < 8)
+    for (int t = 4 * rows; t < vecs; ++t) a = __fadd_rn(a, pv[8 * t + lane]);
+  // vector accumulators 0 + 1 + 2 + 3, lane by lane
+  const float a1 = __shfl_sync(0xFFFFFFFFu, a, (lane + 8) & 31);
+  const float a2 = __shfl_sync(0xFFFFFFFFu, a, (lane + 16) & 31);
+  const float a3 = __shfl_sync(0xFFFFFFFFu, a, (lane + 24) & 31);
+  const float v = __fadd_rn(__fadd_rn(__fadd_rn(a, a1), a2), a3);
+  float fin = 0.0f;
+  for (int k = 8 * vecs; k < n; ++k) fin = __fadd_rn(fin, pv[k]);
+#pragma unroll
+  for (int l = 0; l < 8; ++l) fin = __fadd_rn(fin, __shfl_sync(0xFFFFFFFFu, v, l));
+  return fin;
 }
 
 __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_mode) {
@@ -862,7 +904,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
         }
       }
       __syncwarp();
-      const float denom = __fadd_rn(warp_fixed_order_sum(W.pv, n), 1e-8f);
+      const float denom = __fadd_rn(warp_torch_sum(W.pv, n), 1e-8f);
       const int start = num_nodes + s_cnt[i];
       const int d = e.depth;
       unsigned long long best = 0;
@@ -931,7 +973,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
         n += __popc(m);
       }
       __syncwarp();
-      const float denom = __fadd_rn(warp_fixed_order_sum(W.pv, n), 1e-8f);
+      const float denom = __fadd_rn(warp_torch_sum(W.pv, n), 1e-8f);
       const int start = num_nodes + s_cnt[i];
       unsigned long long best = 0;
       const float sq_leaf = parent_sqrt(v.stats[base + e.node].N);
@@ -1168,6 +1210,21 @@ void launch_export(const EngineView& v, int tree, int count, int32_t* N, float* 
 void launch_status(const EngineView& v, int32_t* status, int32_t* num_nodes, cudaStream_t s) {
   count_launches(1);
   k_status<<<(v.R + 255) / 256, 256, 0, s>>>(v, status, num_nodes);
+}
+
+// Self-test of the prior-normalisation sum: one warp per segment [offsets[s], offsets[s+1]) of x.
+__global__ void k_selftest_prior_sum(const float* x, const int32_t* offsets, int segments, float* out) {
+  const int seg = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (seg >= segments) return;
+  const int lo = offsets[seg], n = offsets[seg + 1] - lo;
+  const float r = warp_torch_sum(x + lo, n);
+  if ((threadIdx.x & 31) == 0) out[seg] = r;
+}
+
+void launch_selftest_prior_sum(const float* x, const int32_t* offsets, int segments, float* out,
+                               cudaStream_t s) {
+  count_launches(1);
+  k_selftest_prior_sum<<<(segments + 7) / 8, 256, 0, s>>>(x, offsets, segments, out);
 }
 
 }  // namespace omq

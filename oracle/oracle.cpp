@@ -4,6 +4,7 @@
 // arithmetic is fp32 with one rounding per operation (built with -ffp-contract=off), in the
 // operand order the reference's torch expressions evaluate.
 #include "oracle.h"
+#include "torch_sum.h"
 #include "chess_rules.h"
 #include "go_rules.h"
 #include "gomoku_rules.h"
@@ -224,18 +225,11 @@ struct Tree {
           if (b[a] == 0) legal.push_back(a);
       }
       if (legal.empty()) continue;
-      // priors = p[legal] / (sum(p[legal]) + 1e-8) (wave_search.py:894-895). The reference sums
-      // with torch.sum; the summation order is fixed here as 32 strided partial sums (slot j
-      // goes to partial j % 32, added in ascending slot order) combined by a butterfly. For the
-      // synthetic evaluator every order gives the same exact sum.
-      float part[32] = {0};
-      for (size_t j = 0; j < legal.size(); ++j) part[j % 32] = part[j % 32] + p[legal[j]];
-      for (int m = 16; m > 0; m >>= 1) {
-        float nxt[32];
-        for (int L = 0; L < 32; ++L) nxt[L] = part[L] + part[L ^ m];
-        std::memcpy(part, nxt, sizeof(part));
-      }
-      const float denom = part[0] + 1e-8f;
+      // priors = p[legal] / (sum(p[legal]) + 1e-8) (wave_search.py:894-895), the sum in the order
+      // torch's CPU kernel adds the gathered fp32 vector (torch_sum.cpp)
+      std::vector<float> pl(legal.size());
+      for (size_t j = 0; j < legal.size(); ++j) pl[j] = p[legal[j]];
+      const float denom = torch_cpu_sum(pl.data(), (int)pl.size()) + 1e-8f;
       const int k = (int)legal.size();
       if (num_nodes + k > cap) return 1;  // "Tree full" (csr_tree.py:405-406)
       child_start[n] = num_nodes;

@@ -37,6 +37,12 @@ _GOLDEN = np.uint64(0x9E3779B97F4A7C15)
 _VALUE_SALT = np.uint64(0xD1B54A32D192ED03)
 
 
+def torch_sum(x: np.ndarray) -> np.float32:
+    """The oracle's restatement of torch's CPU summation order for a contiguous fp32 vector."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    return np.float32(lib().oracle_torch_sum(x.ctypes.data, int(x.size)))
+
+
 def build(quiet: bool = True) -> str:
     """Compile liboracle.so (g++, no GPU needed)."""
     out = subprocess.run(["make", "-C", _HERE, "all"], capture_output=True, text=True)
@@ -159,6 +165,8 @@ def lib():
         L.oracle_get_result.argtypes = [ctypes.c_void_p, ctypes.POINTER(OracleResult)]
         L.oracle_export.argtypes = [ctypes.c_void_p] + [ctypes.c_void_p] * 7
         L.oracle_root_policy.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        L.oracle_torch_sum.restype = ctypes.c_float
+        L.oracle_torch_sum.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.oracle_feature_hash.restype = ctypes.c_uint64
         L.oracle_feature_hash.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
         L.oracle_synth_eval.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,

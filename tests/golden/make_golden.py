@@ -101,6 +101,75 @@ class TracingSynthEvaluator:
         return self._h.hexdigest()
 
 
+def float_cases():
+    from omoknuni_quantum_b200.roots import random_root
+    return [
+        # name, board, sims, wave, capacity
+        ("seed30_w32", random_root(30), 160, 32, 100000),
+        ("seed31_w64", random_root(31), 192, 64, 100000),
+        ("dense6_w4", dense_board(10, 6), 40, 4, 100000),
+        ("dense12_w16", dense_board(8, 12), 64, 16, 100000),
+        ("dense40_w8", dense_board(9, 40), 96, 8, 100000),
+    ]
+
+
+class RecordingFloatEvaluator:
+    """Reference-facing float evaluator: an fp32 ResNet 2 x 128 (the architecture of the
+    reference's ResNetModel, seeded weights) evaluated one position at a time on the CPU, so that a
+    position's outputs never depend on the batch it came in. Every distinct position's outputs are
+    recorded under the SHA-256 of its fp32 feature bytes, so that the engine and the oracle can
+    replay exactly the reference's evaluator outputs. Its priors are generic fp32 values: their
+    sums are inexact, so the summation order of the prior normalisation shows."""
+
+    def __init__(self):
+        from omoknuni_quantum_b200.resnet import ResNetSpec, init_state_dict
+        self.sd = init_state_dict(ResNetSpec(num_blocks=2, filters=128, fc_value_hidden=64), seed=77)
+        self.table = {}
+        self.calls = 0
+
+    def evaluate_batch(self, features):
+        import torch
+        from omoknuni_quantum_b200.resnet import reference_forward_fp32
+        f = features.cpu().numpy() if hasattr(features, "cpu") else np.asarray(features)
+        f = np.ascontiguousarray(f, dtype=np.float32)
+        self.calls += 1
+        ps, vs = [], []
+        for x in f:
+            key = hashlib.sha256(x.tobytes()).hexdigest()
+            if key not in self.table:
+                with torch.no_grad():
+                    p, v = reference_forward_fp32(self.sd, torch.from_numpy(x[None]))
+                self.table[key] = (p[0].numpy().astype(np.float32), np.float32(v[0]))
+            ps.append(self.table[key][0])
+            vs.append(self.table[key][1])
+        return torch.from_numpy(np.stack(ps)), torch.from_numpy(np.array(vs, np.float32))
+
+
+def run_reference_float(board, sims, wave, cap):
+    from mcts.core.mcts import MCTS
+    from mcts.core.mcts_config import MCTSConfig
+    from mcts.gpu.gpu_game_states import GameType
+    cfg = MCTSConfig(backend="gpu", device="cpu", wave_async_expansion=False,
+                     dirichlet_epsilon=0.0, enable_subtree_reuse=False, max_wave_size=wave,
+                     c_puct=1.4, virtual_loss=1.0, num_simulations=sims, max_tree_nodes=cap,
+                     initial_tree_nodes=cap, game_type=GameType.GOMOKU, board_size=15)
+    ev = RecordingFloatEvaluator()
+    m = MCTS(cfg, ev)
+    policy = np.asarray(m.search(board.copy()), np.float64)
+    tree, nd = m.tree, m.tree.node_data
+    n = int(tree.num_nodes)
+    arr = dict(
+        visits=nd.visit_counts[:n].numpy().astype(np.int32),
+        value_sums=nd.value_sums[:n].numpy().astype(np.float32),
+        priors=nd.node_priors[:n].numpy().astype(np.float32),
+        virtual_loss=nd.virtual_loss_counts[:n].numpy().astype(np.int32),
+        parent=nd.parent_indices[:n].numpy().astype(np.int32),
+        action=nd.parent_actions[:n].numpy().astype(np.int32),
+        children=tree.children[:n].numpy().astype(np.int32),
+    )
+    return policy, arr, ev
+
+
 def run_reference(board, sims, wave, c_puct, vl, enable_vl, cap):
     from mcts.core.mcts import MCTS
     from mcts.core.mcts_config import MCTSConfig
@@ -252,6 +321,31 @@ def main():
     logging.disable(logging.WARNING)
     import torch
     torch.set_num_threads(os.cpu_count() or 1)
+
+    for name, board, sims, wave, cap in float_cases():
+        if args.only and name not in args.only:
+            continue
+        policy, arr, ev = run_reference_float(board, sims, wave, cap)
+        n = arr["visits"].shape[0]
+        keys = sorted(ev.table)
+        # legal-prior counts of the expanded nodes: which summation paths the case exercises
+        kids = np.bincount(arr["parent"][1:], minlength=n)
+        rec = dict(board=board.astype(np.int8), sims=sims, wave=wave, capacity=cap, num_nodes=n,
+                   policy=policy, final_move=int(np.argmax(policy)),
+                   table_keys=np.array(keys), table_policy=np.stack([ev.table[k][0] for k in keys]),
+                   table_value=np.array([ev.table[k][1] for k in keys], np.float32),
+                   expanded_child_counts=kids[kids > 0].astype(np.int32),
+                   torch_cpu_capability=str(__import__("torch").backends.cpu.get_cpu_capability()))
+        for k in ("visits", "value_sums", "priors", "virtual_loss", "parent", "action", "children"):
+            rec["sha_" + k] = digest(arr[k])
+        if n <= FULL_ARRAYS_MAX_NODES:
+            for k in ("visits", "value_sums", "priors", "parent", "action"):
+                rec["full_" + k] = arr[k]
+        path = os.path.join(HERE, f"floatsearch_{name}.npz")
+        np.savez_compressed(path, **rec)
+        print(f"float {name}: nodes={n} positions={len(keys)} move={rec['final_move']} "
+              f"child counts {sorted(set(rec['expanded_child_counts'].tolist()))[:6]}... "
+              f"-> {os.path.basename(path)} ({os.path.getsize(path)} B)")
 
     for name, board, sims, wave, searches in gpu_reuse_cases():
         if args.only and name not in args.only:

@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from golden_cases import children_table, digest, load, names
+from golden_cases import ReplayEvaluator, children_table, digest, float_names, load, load_float, names
 
 pytestmark = pytest.mark.gpu
 
@@ -310,3 +310,47 @@ def test_backup_sign_convention_on_device():
     child = int(t["parent"][leaf])
     assert t["parent"][child] == 0
     assert (t["value_sums"][0], t["value_sums"][child], t["value_sums"][leaf]) == (0.5, -0.5, 0.5)
+
+
+@pytest.mark.parametrize("name", float_names())
+def test_search_matches_reference_with_float_evaluator(name):
+    """The reference searched with a float evaluator (an fp32 ResNet, outputs recorded per
+    position); the engine fed the same outputs through the evaluator protocol builds the same tree
+    bit for bit: priors (normalised with torch's CPU summation order), visit counts, value sums,
+    the CSR layout, the root policy and the final move."""
+    from omoknuni_quantum_b200.engine import WaveEngine
+    g = load_float(name)
+    ev = ReplayEvaluator(g)
+    eng = WaveEngine(1, capacity=int(g["capacity"]), max_wave_size=int(g["wave"]))
+    eng.search(torch.from_numpy(g["board"][None]).cuda(), int(g["sims"]), evaluator=ev)
+    assert ev.misses == 0
+    t = eng.export_tree(0)
+    assert t["visits"].shape[0] == int(g["num_nodes"])
+    for k in ("visits", "value_sums", "priors", "virtual_loss", "parent", "action"):
+        assert digest(t[k]) == str(g["sha_" + k]), k
+    assert digest(children_table(t["parent"], t["action"])) == str(g["sha_children"])
+    pol = eng.policy_from_visits(eng.root_visits()[0].cpu().numpy())
+    assert np.array_equal(pol, g["policy"]) and int(np.argmax(pol)) == int(g["final_move"])
+
+
+def test_device_prior_sum_is_torchs_order():
+    """The warp sum behind the prior normalisation equals torch.sum on the CPU bit for bit at
+    every length up to 600 and at sampled lengths up to 5,000 (the 16-row cascade included)."""
+    import ctypes
+    from omoknuni_quantum_b200 import _lib
+    rng = np.random.default_rng(3)
+    lengths = list(range(0, 601)) + [int(n) for n in rng.integers(601, 5001, 200)]
+    vals = [(rng.random(n) ** 3 * rng.choice([1e-3, 1.0, 3e4])).astype(np.float32) for n in lengths]
+    offs = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    x = torch.from_numpy(np.concatenate(vals)).cuda()
+    o = torch.from_numpy(offs).cuda()
+    out = torch.full((len(lengths),), float("nan"), device="cuda")
+    L = _lib.load()
+    _lib.check(L.omq_selftest_prior_sum(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(o.data_ptr()),
+                                        len(lengths), ctypes.c_void_p(out.data_ptr()),
+                                        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
+               "omq_selftest_prior_sum")
+    got = out.cpu().numpy()
+    want = np.array([torch.from_numpy(v).sum().item() if len(v) else 0.0 for v in vals], np.float32)
+    bad = [n for n, a, b in zip(lengths, got, want) if a != b]
+    assert not bad, bad[:10]

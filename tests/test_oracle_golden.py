@@ -9,7 +9,7 @@ import hashlib
 import numpy as np
 import pytest
 
-from golden_cases import children_table, digest, load, names
+from golden_cases import ReplayEvaluator, children_table, digest, float_names, load, load_float, names
 
 
 def _run_oracle(pyoracle, g, trace=False):
@@ -88,3 +88,34 @@ def test_backup_sign_convention_three_node_path(oracle_lib):
     assert (t.visits[0], t.visits[child], t.visits[leaf]) == (1, 1, 1)
     assert (t.value_sums[0], t.value_sums[child], t.value_sums[leaf]) == (0.5, -0.5, 0.5)
     assert t.policy.shape == (225,) and abs(t.policy.sum() - 1.0) < 1e-12
+
+
+def test_torch_sum_order_is_torchs(oracle_lib):
+    """The oracle's summation order of the prior normalisation (`priors.sum()`,
+    wave_search.py:894-895) equals torch.sum on CPU bit for bit, at every length up to 600 and at
+    sampled lengths up to 5,000 (past the 16-row cascade of the kernel), on values whose sums are
+    far from exact in fp32."""
+    import torch
+    rng = np.random.default_rng(0)
+    lengths = list(range(1, 601)) + [int(n) for n in rng.integers(601, 5001, 300)]
+    for n in lengths:
+        for scale in (1.0, 1e-3, 3e4):
+            x = (rng.random(n) ** 3 * scale).astype(np.float32)
+            assert oracle_lib.torch_sum(x) == torch.from_numpy(x).sum().numpy(), n
+
+
+@pytest.mark.parametrize("name", float_names())
+def test_oracle_matches_reference_with_float_evaluator(oracle_lib, name):
+    """The reference searched with a float evaluator (fp32 ResNet outputs, recorded per position);
+    the oracle replaying the same outputs builds the same tree bit for bit: the priors' summation
+    order, and with it every prior, visit count and value sum, is the reference's."""
+    g = load_float(name)
+    ev = ReplayEvaluator(g)
+    t = oracle_lib.Oracle(int(g["capacity"])).search(g["board"], int(g["sims"]), int(g["wave"]), evaluator=ev)
+    assert ev.misses == 0
+    assert t.result["status"] == 0 and t.result["boundary_ties"] == 0
+    assert t.visits.shape[0] == int(g["num_nodes"])
+    for k in ("visits", "value_sums", "priors", "virtual_loss", "parent", "action"):
+        assert digest(getattr(t, k)) == str(g["sha_" + k]), k
+    assert digest(children_table(t.parent, t.action)) == str(g["sha_children"])
+    assert np.array_equal(t.policy, g["policy"])
