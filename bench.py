@@ -70,6 +70,8 @@ def parse():
     ap.add_argument("--game", choices=["gomoku", "go", "chess"], default="gomoku",
                     help="board shape of --workload forward")
     ap.add_argument("--batch", type=int, default=4096, help="positions per call of --workload forward")
+    ap.add_argument("--dtype", choices=["bf16", "fp16"], default="bf16",
+                    help="16-bit type of the ResNet (bf16: the benchmark configs' type)")
     ap.add_argument("--evaluator", choices=["resnet", "synthetic"], default="resnet",
                     help="synthetic = benchmark config 0 (tree kernels only; 800 sims, 200k nodes)")
     return ap.parse_args()
@@ -688,7 +690,7 @@ def run_b200_forward(args):
     n, planes, acts = {"gomoku": (15, 19, 225), "go": (19, 17, 362), "chess": (8, 119, 4672)}[args.game]
     spec = ResNetSpec(board_size=n, input_channels=planes, num_blocks=args.blocks, filters=args.filters,
                       num_actions=acts, fc_value_hidden=args.value_hidden)
-    ev = ResNetEvaluator.random(spec, seed=args.seed, max_batch=args.batch)
+    ev = ResNetEvaluator.random(spec, seed=args.seed, max_batch=args.batch, dtype=args.dtype)
     g = torch.Generator().manual_seed(args.seed)
     x = torch.zeros(args.batch, planes, n, n)
     x[:, 0] = (torch.rand(args.batch, n, n, generator=g) < 0.2).float()
@@ -713,7 +715,7 @@ def run_b200_forward(args):
             "metric": "ResNet leaf evaluations/sec", "value": args.batch * args.steps / (ms / 1000.0),
             "unit": "positions/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded features and weights)",
+            "vs_baseline": None, "dtype": args.dtype, "data": "synthetic (seeded features and weights)",
             "config": {"workload": f"forward: {args.game} {n}x{n}, {planes} planes, {acts} actions",
                        "model": f"resnet{args.blocks}x{args.filters}", "batch": args.batch},
             "trunk_tflops": args.batch * args.steps * ev.trunk_flops_per_position() / (ms / 1000.0) / 1e12,

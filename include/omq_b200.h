@@ -198,9 +198,9 @@ OMQ_API int omq_queue_features(omq_engine* e, int32_t queue, float* d_out, void*
  * for both). */
 OMQ_API int omq_queue_eval_synthetic(omq_engine* e, int32_t queue, void* stream);
 
-/* Whole search with the built-in synthetic evaluator: begin, forced root expansion and
- * ceil(num_simulations / max_wave_size) waves (mcts.py:1020-1063). Synchronizes the stream
- * once at the end to report device status. */
+/* Whole search with the built-in synthetic evaluator: omq_search with net == NULL (begin, forced
+ * root expansion and ceil(num_simulations / max_wave_size) waves, mcts.py:1020-1063).
+ * Synchronizes the stream once at the end to report device status. */
 OMQ_API int omq_search_synthetic(omq_engine* e, const int8_t* d_boards, int32_t num_simulations,
                          void* stream);
 /* The same for chess engines, with the roots of omq_begin_chess. */
@@ -250,13 +250,18 @@ typedef struct {
   int32_t fc_value_hidden;   /* ValueHead fc1 width (reference default 256) */
   int32_t max_batch;         /* positions per forward call (activation buffers are sized for it) */
   int32_t device;
+  int32_t dtype;             /* OMQ_DTYPE_BF16 (0, default) or OMQ_DTYPE_F16: the 16-bit type of the
+                                conv weights, activations and dense-layer operands (fp32 accumulate);
+                                F16 is the precision of the reference evaluator's fp16 autocast */
 } omq_resnet_config;
+
+enum { OMQ_DTYPE_BF16 = 0, OMQ_DTYPE_F16 = 1 };
 
 OMQ_API int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out);
 OMQ_API int omq_resnet_destroy(omq_resnet* net);
 OMQ_API int omq_resnet_memory(const omq_resnet* net, uint64_t* h_bytes);
 /* Element counts of the three packed parameter blobs omq_resnet_load expects:
- *  conv_w (bf16): input conv [F][9][Cin_pad] (input channels zero-padded to 64, or to 128 for
+ *  conv_w (16-bit, the config's dtype): input conv [F][9][Cin_pad] (input channels zero-padded to 64, or to 128 for
  *                 more than 64 planes), then per block
  *                 conv1 [F][9][F], conv2 [F][9][F]; K index = tap * Cin + channel, tap = 3*ky+kx;
  *                 BatchNorm scale folded in.
@@ -286,6 +291,21 @@ OMQ_API int omq_resnet_input_buffer(omq_resnet* net, uint16_t** d_input);
  * the queue's policy/value buffers are written; no host synchronisation. */
 OMQ_API int omq_resnet_forward_queue(omq_resnet* net, omq_engine* engine, int32_t queue,
                                      void* stream);
+/* Whole search in one call, the native counterpart of MCTS.search / _run_search
+ * (python/mcts/core/mcts.py:924-979, 1020-1063; mcts_search in the survey's C-ABI list): begin
+ * on the roots, forced root expansion, then ceil(num_simulations / max_wave_size) waves of
+ * select / evaluate / expand / evaluate / backup, every evaluation done by `net` on the engine's
+ * leaf queues in place (net == NULL: the built-in synthetic evaluator). The net's max_batch must
+ * cover the engine's queue capacity (num_trees x max_wave_size), and its board size, planes and
+ * actions must be the engine's. Synchronizes the stream once, at the end, to report the trees'
+ * status (OMQ_TREE_FULL, ...). Roots as for omq_begin / omq_begin_go / omq_begin_chess. */
+OMQ_API int omq_search(omq_engine* e, omq_resnet* net, const int8_t* d_boards, int32_t num_simulations,
+                       void* stream);
+OMQ_API int omq_search_go(omq_engine* e, omq_resnet* net, const int8_t* d_history, const int32_t* d_meta,
+                          const uint64_t* d_keys, const int32_t* d_nkeys, int32_t num_simulations,
+                          void* stream);
+OMQ_API int omq_search_chess(omq_engine* e, omq_resnet* net, const void* d_records,
+                             const int32_t* d_nprior, int32_t num_simulations, void* stream);
 /* Record CUDA events around the convolution trunk of the next `capacity` forward calls
  * (0 disables; re-arming resets). omq_resnet_profile_read synchronizes on the last event and
  * returns, per call, the trunk's device time in ms and the number of positions evaluated. */

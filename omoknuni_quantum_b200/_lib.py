@@ -58,7 +58,10 @@ class ResNetConfig(ctypes.Structure):
                 ("num_blocks", ctypes.c_int32), ("filters", ctypes.c_int32),
                 ("num_actions", ctypes.c_int32), ("fc_policy_hidden", ctypes.c_int32),
                 ("fc_value_hidden", ctypes.c_int32), ("max_batch", ctypes.c_int32),
-                ("device", ctypes.c_int32)]
+                ("device", ctypes.c_int32), ("dtype", ctypes.c_int32)]
+
+
+OMQ_DTYPE_BF16, OMQ_DTYPE_F16 = 0, 1
 
 
 _P = ctypes.c_void_p
@@ -85,6 +88,9 @@ SIGNATURES = {
     "omq_queue_features": [_P, _I, _P, _P],
     "omq_queue_eval_synthetic": [_P, _I, _P],
     "omq_search_synthetic": [_P, _P, _I, _P],
+    "omq_search": [_P, _P, _P, _I, _P],
+    "omq_search_go": [_P, _P, _P, _P, _P, _P, _I, _P],
+    "omq_search_chess": [_P, _P, _P, _P, _I, _P],
     "omq_search_synthetic_go": [_P, _P, _P, _P, _P, _I, _P],
     "omq_search_synthetic_chess": [_P, _P, _P, _I, _P],
     "omq_root_visits": [_P, _P, _P, _P],

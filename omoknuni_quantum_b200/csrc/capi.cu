@@ -391,47 +391,67 @@ static int first_tree_status(omq_engine* e, cudaStream_t s) {
   return st;
 }
 
-static int search_synthetic_waves(omq_engine* e, int32_t sims, void* stream);
-
-int omq_search_synthetic(omq_engine* e, const int8_t* d_boards, int32_t sims, void* stream) {
-  if (!e || !d_boards || sims < 0) { set_error("bad argument"); return OMQ_BAD_ARG; }
-  int st = omq_begin(e, d_boards, stream);
-  if (st) return st;
-  return search_synthetic_waves(e, sims, stream);
+// Leaf evaluator of a one-call search: the built-in synthetic evaluator (net == nullptr) or a
+// tensor-core ResNet reading the engine's leaf queue in place.
+static int eval_queue(omq_engine* e, omq_resnet* net, int queue, void* stream) {
+  return net ? omq_resnet_forward_queue(net, e, queue, stream) : omq_queue_eval_synthetic(e, queue, stream);
 }
 
-int omq_search_synthetic_chess(omq_engine* e, const void* d_records, const int32_t* d_nprior,
-                               int32_t sims, void* stream) {
-  if (!e || !d_records || !d_nprior || sims < 0) { set_error("bad argument"); return OMQ_BAD_ARG; }
-  int st = omq_begin_chess(e, d_records, d_nprior, stream);
-  if (st) return st;
-  return search_synthetic_waves(e, sims, stream);
-}
-
-int omq_search_synthetic_go(omq_engine* e, const int8_t* d_history, const int32_t* d_meta,
-                            const uint64_t* d_keys, const int32_t* d_nkeys, int32_t sims, void* stream) {
-  if (!e || !d_history || !d_meta || sims < 0) { set_error("bad argument"); return OMQ_BAD_ARG; }
-  int st = omq_begin_go(e, d_history, d_meta, d_keys, d_nkeys, stream);
-  if (st) return st;
-  return search_synthetic_waves(e, sims, stream);
-}
-
-static int search_synthetic_waves(omq_engine* e, int32_t sims, void* stream) {
+// Root expansion and ceil(sims / max_wave_size) waves (MCTS._run_search, mcts.py:1020-1063), every
+// evaluation through the on-device leaf queues; one host synchronisation at the end (tree status).
+static int search_waves(omq_engine* e, omq_resnet* net, int32_t sims, void* stream) {
   cudaStream_t s = (cudaStream_t)stream;
   int st;
-  if ((st = omq_queue_eval_synthetic(e, OMQ_QUEUE_EXPAND, stream))) return st;
+  if ((st = eval_queue(e, net, OMQ_QUEUE_EXPAND, stream))) return st;
   if ((st = omq_root_expand(e, stream))) return st;
   for (int done = 0; done < sims;) {
     const int w = sims - done < e->v.WCAP ? sims - done : e->v.WCAP;
     if ((st = omq_wave_select(e, w, stream))) return st;
-    if ((st = omq_queue_eval_synthetic(e, OMQ_QUEUE_EXPAND, stream))) return st;
+    if ((st = eval_queue(e, net, OMQ_QUEUE_EXPAND, stream))) return st;
     if ((st = omq_wave_expand(e, stream))) return st;
-    if ((st = omq_queue_eval_synthetic(e, OMQ_QUEUE_FINAL, stream))) return st;
+    if ((st = eval_queue(e, net, OMQ_QUEUE_FINAL, stream))) return st;
     if ((st = omq_wave_backup(e, stream))) return st;
     done += w;
   }
   DeviceGuard g(e->cfg.device);
   return first_tree_status(e, s);
+}
+
+int omq_search_synthetic(omq_engine* e, const int8_t* d_boards, int32_t sims, void* stream) {
+  return omq_search(e, nullptr, d_boards, sims, stream);
+}
+
+int omq_search_synthetic_chess(omq_engine* e, const void* d_records, const int32_t* d_nprior,
+                               int32_t sims, void* stream) {
+  return omq_search_chess(e, nullptr, d_records, d_nprior, sims, stream);
+}
+
+int omq_search_synthetic_go(omq_engine* e, const int8_t* d_history, const int32_t* d_meta,
+                            const uint64_t* d_keys, const int32_t* d_nkeys, int32_t sims, void* stream) {
+  return omq_search_go(e, nullptr, d_history, d_meta, d_keys, d_nkeys, sims, stream);
+}
+
+int omq_search(omq_engine* e, omq_resnet* net, const int8_t* d_boards, int32_t sims, void* stream) {
+  if (!e || !d_boards || sims < 0) { set_error("bad argument"); return OMQ_BAD_ARG; }
+  int st = omq_begin(e, d_boards, stream);
+  if (st) return st;
+  return search_waves(e, net, sims, stream);
+}
+
+int omq_search_go(omq_engine* e, omq_resnet* net, const int8_t* d_history, const int32_t* d_meta,
+                  const uint64_t* d_keys, const int32_t* d_nkeys, int32_t sims, void* stream) {
+  if (!e || !d_history || !d_meta || sims < 0) { set_error("bad argument"); return OMQ_BAD_ARG; }
+  int st = omq_begin_go(e, d_history, d_meta, d_keys, d_nkeys, stream);
+  if (st) return st;
+  return search_waves(e, net, sims, stream);
+}
+
+int omq_search_chess(omq_engine* e, omq_resnet* net, const void* d_records, const int32_t* d_nprior,
+                     int32_t sims, void* stream) {
+  if (!e || !d_records || !d_nprior || sims < 0) { set_error("bad argument"); return OMQ_BAD_ARG; }
+  int st = omq_begin_chess(e, d_records, d_nprior, stream);
+  if (st) return st;
+  return search_waves(e, net, sims, stream);
 }
 
 int omq_root_visits(omq_engine* e, int32_t* d_visits, float* d_root_nw, void* stream) {

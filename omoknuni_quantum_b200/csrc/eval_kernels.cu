@@ -232,9 +232,15 @@ __global__ void __launch_bounds__(kSynthWarps * 32) k_features(EngineView v, int
   }
 }
 
-// ResNet input: the same planes as k_features, bf16, channels padded to 64, in the padded pixel
-// space [(S+1) x (S+1)] whose last row and column stay zero. One warp per queued position.
-__global__ void __launch_bounds__(kSynthWarps * 32) k_pack_queue(EngineView v, int queue, int P, uint4* out) {
+// 16-bit encodings of 1.0 and 2.0 (the only feature values of Gomoku and Go planes)
+__device__ __forceinline__ uint16_t one_h16(bool f16) { return f16 ? 0x3C00 : 0x3F80; }
+constexpr uint16_t kTwoH16 = 0x4000;  // 2.0 in both bf16 and fp16
+
+// ResNet input: the same planes as k_features, bf16 or fp16 (the net's dtype), channels padded to
+// 64, in the padded pixel space [(S+1) x (S+1)] whose last row and column stay zero. One warp per
+// queued position.
+__global__ void __launch_bounds__(kSynthWarps * 32) k_pack_queue(EngineView v, int queue, int P, bool f16,
+                                                                 uint4* out) {
   __shared__ WarpPos wps[kSynthWarps];
   const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
   const int q = blockIdx.x * kSynthWarps + wl;
@@ -246,7 +252,8 @@ __global__ void __launch_bounds__(kSynthWarps * 32) k_pack_queue(EngineView v, i
   const int d = warp_rebuild(v, r, ent.y, wp);
   if (d < 0) { if (lane == 0) v.hdr[r].status = OMQ_BAD_ARG; return; }
   const TreeHeader& H = v.hdr[r];
-  const uint16_t player = ((d % 2 == 0) ? H.root_player : 3 - H.root_player) == 1 ? 0x3F80 : 0x4000;
+  const uint16_t one = one_h16(f16);
+  const uint16_t player = ((d % 2 == 0) ? H.root_player : 3 - H.root_player) == 1 ? one : kTwoH16;
   const uint32_t hp = history_planes(H.root_mc + d, d, kFullHistoryGomoku);
   const int last = d >= 1 ? wp.acts[d - 1] : -1;
   const int S = v.S;
@@ -260,9 +267,9 @@ __global__ void __launch_bounds__(kSynthWarps * 32) k_pack_queue(EngineView v, i
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int ch = chunk * 8 + e;
-        if (ch == 0) h[e] = wp.board[c] != 0 ? 0x3F80 : 0;
+        if (ch == 0) h[e] = wp.board[c] != 0 ? one : 0;
         else if (ch == 1) h[e] = player;
-        else if (ch < kPlanes) h[e] = (((hp >> ch) & 1u) && c == last) ? 0x3F80 : 0;
+        else if (ch < kPlanes) h[e] = (((hp >> ch) & 1u) && c == last) ? one : 0;
       }
     }
     o[i] = *reinterpret_cast<uint4*>(h);
@@ -342,8 +349,9 @@ __global__ void __launch_bounds__(kGoWarps * 32) k_features_go(EngineView v, int
     for (int c = lane; c < v.C; c += 32) o[(size_t)p * v.C + c] = go_plane_bit(v, r, w, p, c) ? 1.0f : 0.0f;
 }
 
-// ResNet input for Go: the 17 planes as bf16, channels padded to 64, padded pixel layout.
-__global__ void __launch_bounds__(kGoWarps * 32) k_pack_queue_go(EngineView v, int queue, int P, uint4* out) {
+// ResNet input for Go: the 17 planes as bf16 or fp16, channels padded to 64, padded pixel layout.
+__global__ void __launch_bounds__(kGoWarps * 32) k_pack_queue_go(EngineView v, int queue, int P, bool f16,
+                                                                 uint4* out) {
   __shared__ GoWarpPos wps[kGoWarps];
   const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
   const int q = blockIdx.x * kGoWarps + wl;
@@ -362,7 +370,7 @@ __global__ void __launch_bounds__(kGoWarps * 32) k_pack_queue_go(EngineView v, i
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int ch = chunk * 8 + e;
-        if (ch < kGoPlanes) h[e] = go_plane_bit(v, r, w, ch, c) ? 0x3F80 : 0;
+        if (ch < kGoPlanes) h[e] = go_plane_bit(v, r, w, ch, c) ? one_h16(f16) : 0;
       }
     }
     o[i] = *reinterpret_cast<uint4*>(h);
@@ -440,8 +448,9 @@ __global__ void __launch_bounds__(kChessWarps * 32) k_features_chess(EngineView 
   for (int i = lane; i < kChessPlanes * 64; i += 32) o[i] = ch_plane(v, r, w, i >> 6, i & 63);
 }
 
-// ResNet input for chess: 119 planes as bf16, channels padded to 128, padded 9x9 pixel grid.
-__global__ void __launch_bounds__(kChessWarps * 32) k_pack_queue_chess(EngineView v, int queue, int P, uint4* out) {
+// ResNet input for chess: 119 planes as bf16 or fp16, channels padded to 128, padded 9x9 pixel grid.
+__global__ void __launch_bounds__(kChessWarps * 32) k_pack_queue_chess(EngineView v, int queue, int P, bool f16,
+                                                                       uint4* out) {
   __shared__ ChessReplay wps[kChessWarps];
   const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
   const int q = blockIdx.x * kChessWarps + wl;
@@ -453,37 +462,37 @@ __global__ void __launch_bounds__(kChessWarps * 32) k_pack_queue_chess(EngineVie
   for (int i = lane; i < P * 16; i += 32) {
     const int pix = i >> 4, chunk = i & 15;
     const int y = pix / 9, x = pix - y * 9;
-    __nv_bfloat16 h[8];
+    uint16_t h[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const int ch = chunk * 8 + e;
       const float val = (y < 8 && x < 8 && ch < kChessPlanes) ? ch_plane(v, r, w, ch, y * 8 + x) : 0.0f;
-      h[e] = __float2bfloat16_rn(val);
+      h[e] = to_h16(val, f16);
     }
     o[i] = *reinterpret_cast<uint4*>(h);
   }
 }
 
-void launch_pack_queue(const EngineView& v, int queue, int P, int in_pad, void* out, cudaStream_t s) {
+void launch_pack_queue(const EngineView& v, int queue, int P, int in_pad, void* out, bool f16, cudaStream_t s) {
   if (v.game == OMQ_GAME_CHESS) {
     (void)in_pad;  // 128
     const int cap = v.R * v.WCAP;
     count_launches(1);
     k_pack_queue_chess<<<(cap + kChessWarps - 1) / kChessWarps, kChessWarps * 32, 0, s>>>(
-        v, queue, P, reinterpret_cast<uint4*>(out));
+        v, queue, P, f16, reinterpret_cast<uint4*>(out));
     return;
   }
   if (v.game == OMQ_GAME_GO) {
     const int cap = v.R * v.WCAP;
     count_launches(1);
     k_pack_queue_go<<<(cap + kGoWarps - 1) / kGoWarps, kGoWarps * 32, 0, s>>>(
-        v, queue, P, reinterpret_cast<uint4*>(out));
+        v, queue, P, f16, reinterpret_cast<uint4*>(out));
     return;
   }
   const int cap = v.R * v.WCAP;
   count_launches(1);
   k_pack_queue<<<(cap + kSynthWarps - 1) / kSynthWarps, kSynthWarps * 32, 0, s>>>(
-      v, queue, P, reinterpret_cast<uint4*>(out));
+      v, queue, P, f16, reinterpret_cast<uint4*>(out));
 }
 
 void launch_synth_eval(const EngineView& v, int queue, cudaStream_t s) {

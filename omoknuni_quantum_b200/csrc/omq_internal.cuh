@@ -1,11 +1,40 @@
 // Internal definitions shared by the engine's CUDA translation units.
 #pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include "omq_b200.h"
 
 namespace omq {
+
+// 16-bit storage of the ResNet's weights and activations: bf16 (OMQ_DTYPE_BF16) or fp16
+// (OMQ_DTYPE_F16, the reference evaluator's autocast precision); the same bits feed tcgen05
+// kind::f16. Conversions round to nearest even.
+using h16 = uint16_t;
+
+template <bool F16>
+__device__ __forceinline__ uint32_t pack2_h16(float a, float b) {
+  if constexpr (F16) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+template <bool F16>
+__device__ __forceinline__ float2 unpack2_h16(uint32_t u) {
+  if constexpr (F16) return __half22float2(*reinterpret_cast<const __half2*>(&u));
+  else return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+}
+__device__ __forceinline__ h16 to_h16(float a, bool f16) {
+  return f16 ? __half_as_ushort(__float2half_rn(a)) : __bfloat16_as_ushort(__float2bfloat16_rn(a));
+}
+__device__ __forceinline__ float from_h16(h16 a, bool f16) {
+  return f16 ? __half2float(__ushort_as_half(a)) : __bfloat162float(__ushort_as_bfloat16(a));
+}
 
 // Per-node statistics, one 16-byte vector load per child during selection.
 // Fields mirror NodeDataManager's SoA arrays (python/mcts/gpu/node_data_manager.py:88-113):
@@ -238,7 +267,7 @@ void launch_selftest_prior_sum(const float* x, const int32_t* offsets, int segme
 void launch_features(const EngineView& v, int queue, float* out, cudaStream_t s);
 void launch_synth_eval(const EngineView& v, int queue, cudaStream_t s);
 // queue positions -> bf16 [count][P][in_pad] padded pixel layout (ResNet input)
-void launch_pack_queue(const EngineView& v, int queue, int P, int in_pad, void* out, cudaStream_t s);
+void launch_pack_queue(const EngineView& v, int queue, int P, int in_pad, void* out, bool f16, cudaStream_t s);
 // feature planes of the engine's game (19 Gomoku, 17 Go)
 inline int engine_planes(const EngineView& v) {
   return v.game == OMQ_GAME_GO ? 17 : v.game == OMQ_GAME_CHESS ? 119 : 19;

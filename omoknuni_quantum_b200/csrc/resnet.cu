@@ -40,8 +40,8 @@ constexpr int kMaxActions = 5000;
 
 struct ConvArgs {
   const float* bias;
-  const __nv_bfloat16* residual;
-  __nv_bfloat16* out;
+  const h16* residual;
+  h16* out;
   const int32_t* d_count;
   int32_t count;
   int32_t P;
@@ -72,7 +72,7 @@ struct PairCfg {
   static_assert(kSmem <= 232448, "227 KB of shared memory per CTA");
 };
 
-template <int BN>
+template <int BN, bool F16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::kThreads, 1)
     k_conv3x3_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO, ConvArgs args) {
@@ -152,7 +152,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::kThread
         }
   } else if (warp == 1 && lane == 0 && rank == 0) {
     // ---------------- MMA issuer (leader only) ----------------
-    constexpr uint32_t idesc = ptx::idesc_bf16_f32(2 * kTileM, BN);
+    constexpr uint32_t idesc = ptx::idesc_f16_f32(2 * kTileM, BN, F16);
     int s = 0;
     uint32_t ph = 0;
     bool any = false;
@@ -208,7 +208,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::kThread
       const int pix = m % args.P;
       const int y = pix / rowstride, x = pix - y * rowstride;
       const bool pad = !valid || (y == args.S) || (x == args.S);
-      const __nv_bfloat16* rrow = args.residual ? args.residual + (size_t)m * BN : nullptr;
+      const h16* rrow = args.residual ? args.residual + (size_t)m * BN : nullptr;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
@@ -225,11 +225,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::kThread
             const uint4* rp = reinterpret_cast<const uint4*>(rrow + c0);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              uint4 u = rp[j];
-              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+              const uint4 u = rp[j];
+              const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                float2 f = __bfloat1622float2(h[e]);
+                const float2 f = unpack2_h16<F16>(uw[e]);
                 res[8 * j + 2 * e] = f.x;
                 res[8 * j + 2 * e + 1] = f.y;
               }
@@ -243,8 +243,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::kThread
             float v0 = __uint_as_float(r[j]) + s_bias[c0 + j] + res[j];
             float v1 = __uint_as_float(r[j + 1]) + s_bias[c0 + j + 1] + res[j + 1];
             if (args.relu) { v0 = fmaxf(v0, 0.0f); v1 = fmaxf(v1, 0.0f); }
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
-            pw[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
+            pw[j / 2] = pack2_h16<F16>(v0, v1);
           }
         }
         if (lane == 0) ptx::bulk_wait_read<1>();
@@ -304,6 +303,7 @@ struct HaloTCfg {
   static_assert(kSmem <= 232448, "227 KB of shared memory per CTA");
 };
 
+template <bool F16>
 __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
     k_conv3x3_halo_t(const __grid_constant__ CUtensorMap tmH, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmO, ConvArgs args) {
@@ -398,7 +398,7 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
     // S + 2 from pixel 14*16 + 14), and the pad row's outputs are written as zeros by the
     // epilogue, so the UMMAs cover only the first 256 - 16 = 240 pixel columns.
     const uint32_t idesc =
-        ptx::idesc_bf16_f32(BN, args.P == Cfg::kRows ? Cfg::kRows - rowstride : Cfg::kRows);
+        ptx::idesc_f16_f32(BN, args.P == Cfg::kRows ? Cfg::kRows - rowstride : Cfg::kRows, F16);
     const uint64_t w_desc0 = ptx::smem_desc_sw128(ptx::smem_u32(w_ring));
     int sx = 0, sw = 0;
     uint32_t px = 0, pw = 0;
@@ -491,11 +491,11 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
             const uint4* rp = reinterpret_cast<const uint4*>(args.residual + (size_t)m * BN + q * 32);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              uint4 u = rp[i];
-              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+              const uint4 u = rp[i];
+              const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                const float2 f = __bfloat1622float2(h[e]);
+                const float2 f = unpack2_h16<F16>(uw[e]);
                 v[8 * i + 2 * e] += f.x;
                 v[8 * i + 2 * e + 1] += f.y;
               }
@@ -505,8 +505,7 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
           for (int i = 0; i < 32; i += 2) {
             float v0 = v[i], v1 = v[i + 1];
             if (args.relu) { v0 = fmaxf(v0, 0.0f); v1 = fmaxf(v1, 0.0f); }
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
-            pwd[i / 2] = *reinterpret_cast<uint32_t*>(&h2);
+            pwd[i / 2] = pack2_h16<F16>(v0, v1);
           }
         }
         // the buffer about to be written must no longer be read by an earlier store
@@ -539,10 +538,11 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------------
-// input packing: reference fp32 features [n][planes][S][S] -> bf16 [n][P][in_pad] padded pixel space
+// input packing: reference fp32 features [n][planes][S][S] -> bf16 or fp16 [n][P][in_pad] padded
+// pixel space
 // ---------------------------------------------------------------------------------------------
 __global__ void k_pack_features(const float* feat, int planes, int S, int P, const int32_t* d_count,
-                                int count, __nv_bfloat16* out) {
+                                int count, bool f16, h16* out) {
   const int n = d_count ? min(*d_count, count) : count;
   const int total = n * P;
   const int C = S * S;
@@ -553,12 +553,12 @@ __global__ void k_pack_features(const float* feat, int planes, int S, int P, con
     const int y = pix / (S + 1), x = pix - y * (S + 1);
     uint4 u = make_uint4(0, 0, 0, 0);
     if (y < S && x < S) {
-      __nv_bfloat16 h[8];
+      h16 h[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int c = chunk * 8 + e;
         const float v = c < planes ? feat[((size_t)b * planes + c) * C + y * S + x] : 0.0f;
-        h[e] = __float2bfloat16_rn(v);
+        h[e] = to_h16(v, f16);
       }
       u = *reinterpret_cast<uint4*>(h);
     }
@@ -572,13 +572,13 @@ __global__ void k_pack_features(const float* feat, int planes, int S, int P, con
 // fully connected layer (M = 128 positions x N <= 256 outputs per UMMA, bf16 in, fp32 accumulate)
 // with the layer's epilogue fused (bias + ReLU -> bf16, softmax, or the value dot + tanh).
 // ---------------------------------------------------------------------------------------------
-enum DenseMode { kDenseReluBf16 = 0, kDenseSoftmax = 1, kDenseLogits = 2, kDenseValue = 3 };
+enum DenseMode { kDenseRelu16 = 0, kDenseSoftmax = 1, kDenseLogits = 2, kDenseValue = 3 };
 
 struct DenseArgs {
   const float* bias;       // [n_total]
   const float* w2;         // value mode: fc2 weights [n_total]
   const float* b2;         // value mode: fc2 bias [1]
-  void* out;               // bf16 [rows][ld] | fp32 [rows][ld] | value fp32 [rows]
+  void* out;               // 16-bit [rows][ld] | fp32 [rows][ld] | value fp32 [rows]
   int ld;                  // output row length (elements)
   int n_total;             // valid outputs
   int kblocks;             // K / 64
@@ -593,7 +593,7 @@ constexpr int kDenseThreads = 192;  // TMA warp, MMA warp, 4 epilogue warps
 // two CTAs (2 x 256 TMEM columns) share an SM.
 constexpr int kDenseSmem = kDenseStages * (128 * 128 + 256 * 128) + 1024 + 256;
 
-template <int NT, int MODE>
+template <int NT, int MODE, bool F16>
 __global__ void __launch_bounds__(kDenseThreads)
     k_dense(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, DenseArgs a) {
   constexpr int kA = 128 * 128, kW = NT * 128;            // bytes per 64-wide K block
@@ -644,7 +644,7 @@ __global__ void __launch_bounds__(kDenseThreads)
         ptx::mbar_wait(&full[s], (uint32_t)issued[s], &dummy, kWaitLimitNs);
       }
   } else if (warp == 1 && lane == 0) {
-    constexpr uint32_t idesc = ptx::idesc_bf16_f32(128, NT);
+    constexpr uint32_t idesc = ptx::idesc_f16_f32(128, NT, F16);
     const uint64_t d0 = ptx::smem_desc_sw128(ptx::smem_u32(ring));
     bool ok = true;
     for (int kb = 0; kb < a.kblocks && ok; ++kb) {
@@ -670,8 +670,8 @@ __global__ void __launch_bounds__(kDenseThreads)
     ptx::tc_fence_after();
     const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
     const int ncols = min(NT, a.n_total - col0);
-    if (ok && MODE == kDenseReluBf16) {
-      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (size_t)r * a.ld + col0;
+    if (ok && MODE == kDenseRelu16) {
+      h16* out = static_cast<h16*>(a.out) + (size_t)r * a.ld + col0;
       for (int c0 = 0; c0 < NT; c0 += 32) {
         uint32_t v[32];
         ptx::tmem_ld_32x32b_x32(taddr + c0, v);
@@ -682,8 +682,7 @@ __global__ void __launch_bounds__(kDenseThreads)
           for (int j = 0; j < 32; j += 2) {
             const float x0 = fmaxf(__uint_as_float(v[j]) + a.bias[col0 + c0 + j], 0.f);
             const float x1 = fmaxf(__uint_as_float(v[j + 1]) + a.bias[col0 + c0 + j + 1], 0.f);
-            __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-            pk[j / 2] = *reinterpret_cast<uint32_t*>(&h);
+            pk[j / 2] = pack2_h16<F16>(x0, x1);
           }
           uint4* o = reinterpret_cast<uint4*>(out + c0);
 #pragma unroll
@@ -773,11 +772,11 @@ __global__ void k_softmax_rows(float* x, int ld, int n_total, const int32_t* d_c
   }
 }
 
-// 1x1 convolutions (policy 2 channels, value 1) + folded BN + ReLU into the dense layers' bf16
+// 1x1 convolutions (policy 2 channels, value 1) + folded BN + ReLU into the dense layers' 16-bit
 // input rows: pin[pos][ch * HW + cell] (K padded, pad columns stay zero), vin[pos][cell].
-__global__ void k_head_in(const __nv_bfloat16* act, int C, int S, int P, const float* w1x1,
-                          const float* b1x1, const int32_t* d_count, int count,
-                          __nv_bfloat16* pin, int ld_p, __nv_bfloat16* vin, int ld_v) {
+__global__ void k_head_in(const h16* act, int C, int S, int P, const float* w1x1,
+                          const float* b1x1, const int32_t* d_count, int count, bool f16,
+                          h16* pin, int ld_p, h16* vin, int ld_v) {
   extern __shared__ float w1[];  // [3][C]
   for (int i = threadIdx.x; i < 3 * C; i += blockDim.x) w1[i] = w1x1[i];
   __syncthreads();
@@ -786,15 +785,15 @@ __global__ void k_head_in(const __nv_bfloat16* act, int C, int S, int P, const f
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n * HW; i += gridDim.x * blockDim.x) {
     const int pos = i / HW, cell = i - pos * HW;
     const int yy = cell / S, xx = cell - yy * S;
-    const __nv_bfloat16* row = act + ((size_t)pos * P + yy * (S + 1) + xx) * C;
+    const h16* row = act + ((size_t)pos * P + yy * (S + 1) + xx) * C;
     float s0 = 0.f, s1 = 0.f, s2 = 0.f;
     for (int c = 0; c < C; c += 8) {
-      uint4 u = *reinterpret_cast<const uint4*>(row + c);
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+      const uint4 u = *reinterpret_cast<const uint4*>(row + c);
+      const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
       float x[8];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(h[e]);
+        const float2 f = f16 ? unpack2_h16<true>(uw[e]) : unpack2_h16<false>(uw[e]);
         x[2 * e] = f.x;
         x[2 * e + 1] = f.y;
       }
@@ -808,18 +807,18 @@ __global__ void k_head_in(const __nv_bfloat16* act, int C, int S, int P, const f
         s2 += x[4 * e] * r.x + x[4 * e + 1] * r.y + x[4 * e + 2] * r.z + x[4 * e + 3] * r.w;
       }
     }
-    pin[(size_t)pos * ld_p + cell] = __float2bfloat16_rn(fmaxf(s0 + b1x1[0], 0.f));
-    pin[(size_t)pos * ld_p + HW + cell] = __float2bfloat16_rn(fmaxf(s1 + b1x1[1], 0.f));
-    vin[(size_t)pos * ld_v + cell] = __float2bfloat16_rn(fmaxf(s2 + b1x1[2], 0.f));
+    pin[(size_t)pos * ld_p + cell] = to_h16(fmaxf(s0 + b1x1[0], 0.f), f16);
+    pin[(size_t)pos * ld_p + HW + cell] = to_h16(fmaxf(s1 + b1x1[1], 0.f), f16);
+    vin[(size_t)pos * ld_v + cell] = to_h16(fmaxf(s2 + b1x1[2], 0.f), f16);
   }
 }
 
-// Dense-layer weights W[j][k] (bf16, K-major, zero padded to kpad columns and npad rows) from
+// Dense-layer weights W[j][k] (16-bit, K-major, zero padded to kpad columns and npad rows) from
 // the fp32 head blob's transposed layout src[k][j] (k < kin, j < nout).
-__global__ void k_pack_dense_w(const float* src, int kin, int nout, int kpad, int npad, __nv_bfloat16* dst) {
+__global__ void k_pack_dense_w(const float* src, int kin, int nout, int kpad, int npad, bool f16, h16* dst) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < npad * kpad; i += gridDim.x * blockDim.x) {
     const int j = i / kpad, k = i - j * kpad;
-    dst[i] = __float2bfloat16_rn((j < nout && k < kin) ? src[(size_t)k * nout + j] : 0.f);
+    dst[i] = to_h16((j < nout && k < kin) ? src[(size_t)k * nout + j] : 0.f, f16);
   }
 }
 
@@ -830,7 +829,7 @@ constexpr int kHeadPos = 8;       // positions per block
 constexpr int kHeadThreads = 256;
 
 struct HeadArgs {
-  const __nv_bfloat16* act;   // [rows][C]
+  const h16* act;   // [rows][C]
   int C, S, P, A, Hp, Hv;
   const float* w1x1;          // [3][C]
   const float* b1x1;          // [3]
@@ -846,6 +845,7 @@ struct HeadArgs {
   int count;
   float* policy;              // [n][A]
   float* value;               // [n]
+  bool f16;                   // activations are fp16 (else bf16)
 };
 
 // acc[p] += w * x[p] for p < HP, x 16-byte aligned in shared memory (HP / 4 broadcast loads).
@@ -883,15 +883,15 @@ __global__ void __launch_bounds__(kHeadThreads) k_heads(HeadArgs a) {
   for (int i = tid; i < np * HW; i += kHeadThreads) {
     const int pl = i / HW, cell = i - pl * HW;
     const int yy = cell / a.S, xx = cell - yy * a.S;
-    const __nv_bfloat16* row = a.act + ((size_t)(p0 + pl) * a.P + yy * (a.S + 1) + xx) * a.C;
+    const h16* row = a.act + ((size_t)(p0 + pl) * a.P + yy * (a.S + 1) + xx) * a.C;
     float s0 = 0.f, s1 = 0.f, s2 = 0.f;
     for (int c = 0; c < a.C; c += 8) {
-      uint4 u = *reinterpret_cast<const uint4*>(row + c);
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+      const uint4 u = *reinterpret_cast<const uint4*>(row + c);
+      const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
       float x[8];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(h[e]);
+        const float2 f = a.f16 ? unpack2_h16<true>(uw[e]) : unpack2_h16<false>(uw[e]);
         x[2 * e] = f.x;
         x[2 * e + 1] = f.y;
       }
@@ -987,23 +987,24 @@ struct omq_resnet {
   int sm_count;
   void* arena;
   size_t bytes;
-  __nv_bfloat16* conv_w;   // (1 + 2*NB) convs
+  h16* conv_w;   // (1 + 2*NB) convs
   float* conv_b;
   float* head;
-  __nv_bfloat16* x_in;     // [rows][in_pad]
+  h16* x_in;     // [rows][in_pad]
   int in_pad;              // input channels padded to 64 or 128
-  __nv_bfloat16* act[3];   // [rows][C]
+  h16* act[3];   // [rows][C]
   int32_t* error;
   CUtensorMap tmA_in, tmA[3], tmB_in;
   CUtensorMap tmO[3];      // output maps of the activation buffers (TMA-store epilogue)
   CUtensorMap* tmB;        // [2*NB]
   int loaded;
-  // tensor-core heads (dense layers): bf16 inputs / hidden rows, bf16 weights, their maps
+  // tensor-core heads (dense layers): 16-bit inputs / hidden rows / weights, their maps
   int tc_heads;
   int k1p, k3p, n1pad, n2pad, n3pad, nt3;  // padded K of fc1 policy / fc1 value, padded rows
-  __nv_bfloat16 *pin, *vin, *hid, *w1b, *w2b, *w3b;
+  h16 *pin, *vin, *hid, *w1b, *w2b, *w3b;
   CUtensorMap tm_pin, tm_vin, tm_hid, tm_w1, tm_w2, tm_w3;
-  int pair;                // conv variant: 0 single CTA, 1 CTA pair (cta_group::2), 2 transposed
+  int pair;                // conv variant: 1 CTA pair (cta_group::2), 4 transposed halo
+  bool f16;                // 16-bit storage is fp16 (OMQ_DTYPE_F16), else bf16
   // optional timing of the conv trunk of each forward call (CUDA events on the caller's stream)
   int prof_cap, prof_n;
   cudaEvent_t* prof_ev;    // [2 * prof_cap]
@@ -1039,30 +1040,35 @@ static PFN_encodeTiled_t get_encode() {
   return fn;
 }
 
-// 2D bf16 tensor map for the epilogue's TMA stores: box {32 channels, 32 rows}, 64B swizzle.
-static int make_out_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer) {
+static CUtensorMapDataType map_type(bool f16) {
+  return f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+}
+
+// 2D 16-bit tensor map for the epilogue's TMA stores: box {32 channels, 32 rows}, 64B swizzle.
+static int make_out_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, bool f16) {
   PFN_encodeTiled_t enc = get_encode();
   if (!enc) { set_error("cuTensorMapEncodeTiled unavailable"); return OMQ_CUDA_ERROR; }
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {inner * 2};
   cuuint32_t box[2] = {32, 32};
   cuuint32_t es[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+  CUresult r = enc(m, map_type(f16), 2, const_cast<void*>(base), dims, strides,
                    box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) { set_error("cuTensorMapEncodeTiled (output) failed (%d)", (int)r); return OMQ_CUDA_ERROR; }
   return OMQ_OK;
 }
 
-// 2D bf16 tensor map: inner dim `inner` elements, `outer` rows, box {64, box_rows}, 128B swizzle.
-static int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint32_t box_rows) {
+// 2D 16-bit tensor map: inner dim `inner` elements, `outer` rows, box {64, box_rows}, 128B swizzle.
+static int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint32_t box_rows,
+                    bool f16) {
   PFN_encodeTiled_t enc = get_encode();
   if (!enc) { set_error("cuTensorMapEncodeTiled unavailable"); return OMQ_CUDA_ERROR; }
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {inner * 2};
   cuuint32_t box[2] = {64, box_rows};
   cuuint32_t es[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+  CUresult r = enc(m, map_type(f16), 2, const_cast<void*>(base), dims, strides,
                    box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) { set_error("cuTensorMapEncodeTiled failed (%d)", (int)r); return OMQ_CUDA_ERROR; }
@@ -1078,20 +1084,20 @@ static int conv_variant(int filters) { return filters == 256 ? 1 : 4; }
 static int build_maps(omq_resnet* n) {
   const uint32_t a_rows = n->pair == 1 ? kTileM : HaloTCfg::kHaloBox;
   const uint32_t b_rows = n->pair == 1 ? n->C / 2 : n->C;
-  int st = make_map(&n->tmA_in, n->x_in, n->in_pad, n->rows, a_rows);
-  for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n->tmA[i], n->act[i], n->C, n->rows, a_rows);
-  for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_out_map(&n->tmO[i], n->act[i], n->C, n->rows);
-  if (st == OMQ_OK) st = make_map(&n->tmB_in, n->conv_w, 9 * n->in_pad, n->C, b_rows);
-  const __nv_bfloat16* wb = n->conv_w + (size_t)n->C * 9 * n->in_pad;
+  int st = make_map(&n->tmA_in, n->x_in, n->in_pad, n->rows, a_rows, n->f16);
+  for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n->tmA[i], n->act[i], n->C, n->rows, a_rows, n->f16);
+  for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_out_map(&n->tmO[i], n->act[i], n->C, n->rows, n->f16);
+  if (st == OMQ_OK) st = make_map(&n->tmB_in, n->conv_w, 9 * n->in_pad, n->C, b_rows, n->f16);
+  const h16* wb = n->conv_w + (size_t)n->C * 9 * n->in_pad;
   for (int i = 0; st == OMQ_OK && i < 2 * n->NB; ++i)
-    st = make_map(&n->tmB[i], wb + (size_t)i * n->C * 9 * n->C, 9 * n->C, n->C, b_rows);
+    st = make_map(&n->tmB[i], wb + (size_t)i * n->C * 9 * n->C, 9 * n->C, n->C, b_rows, n->f16);
   if (st == OMQ_OK && n->tc_heads) {
-    st = make_map(&n->tm_pin, n->pin, n->k1p, n->max_batch, 128);
-    if (st == OMQ_OK) st = make_map(&n->tm_vin, n->vin, n->k3p, n->max_batch, 128);
-    if (st == OMQ_OK) st = make_map(&n->tm_hid, n->hid, n->Hp, n->max_batch, 128);
-    if (st == OMQ_OK) st = make_map(&n->tm_w1, n->w1b, n->k1p, n->n1pad, 256);
-    if (st == OMQ_OK) st = make_map(&n->tm_w2, n->w2b, n->Hp, n->n2pad, 256);
-    if (st == OMQ_OK) st = make_map(&n->tm_w3, n->w3b, n->k3p, n->n3pad, n->nt3);
+    st = make_map(&n->tm_pin, n->pin, n->k1p, n->max_batch, 128, n->f16);
+    if (st == OMQ_OK) st = make_map(&n->tm_vin, n->vin, n->k3p, n->max_batch, 128, n->f16);
+    if (st == OMQ_OK) st = make_map(&n->tm_hid, n->hid, n->Hp, n->max_batch, 128, n->f16);
+    if (st == OMQ_OK) st = make_map(&n->tm_w1, n->w1b, n->k1p, n->n1pad, 256, n->f16);
+    if (st == OMQ_OK) st = make_map(&n->tm_w2, n->w2b, n->Hp, n->n2pad, 256, n->f16);
+    if (st == OMQ_OK) st = make_map(&n->tm_w3, n->w3b, n->k3p, n->n3pad, n->nt3, n->f16);
   }
   return st;
 }
@@ -1133,7 +1139,7 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
       (c.filters != 128 && c.filters != 256) || c.num_blocks < 0 || c.num_blocks > 64 ||
       c.num_actions < 1 || c.num_actions > kMaxActions || c.fc_policy_hidden < 1 ||
       c.fc_policy_hidden > 1024 || c.fc_value_hidden < 1 || c.fc_value_hidden > 1024 ||
-      c.max_batch < 1) {
+      c.max_batch < 1 || (c.dtype != OMQ_DTYPE_BF16 && c.dtype != OMQ_DTYPE_F16)) {
     set_error("bad resnet config");
     return OMQ_BAD_ARG;
   }
@@ -1152,6 +1158,7 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
   n->max_batch = c.max_batch;
   n->rows = (size_t)c.max_batch * n->P;
   n->in_pad = in_pad_of(c.input_channels);
+  n->f16 = c.dtype == OMQ_DTYPE_F16;
   if (head_smem(n) > 227 * 1024) {
     set_error("heads need %zu bytes of shared memory (policy size %d)", head_smem(n), n->A);
     delete n;
@@ -1189,18 +1196,18 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
   char* b = static_cast<char*>(arena);
   n->arena = arena;
   n->bytes = tot;
-  n->conv_w = reinterpret_cast<__nv_bfloat16*>(b + off[0]);
+  n->conv_w = reinterpret_cast<h16*>(b + off[0]);
   n->conv_b = reinterpret_cast<float*>(b + off[1]);
   n->head = reinterpret_cast<float*>(b + off[2]);
-  n->x_in = reinterpret_cast<__nv_bfloat16*>(b + off[3]);
-  for (int i = 0; i < 3; ++i) n->act[i] = reinterpret_cast<__nv_bfloat16*>(b + off[4 + i]);
+  n->x_in = reinterpret_cast<h16*>(b + off[3]);
+  for (int i = 0; i < 3; ++i) n->act[i] = reinterpret_cast<h16*>(b + off[4 + i]);
   n->error = reinterpret_cast<int32_t*>(b + off[7]);
-  n->pin = reinterpret_cast<__nv_bfloat16*>(b + off[8]);
-  n->vin = reinterpret_cast<__nv_bfloat16*>(b + off[9]);
-  n->hid = reinterpret_cast<__nv_bfloat16*>(b + off[10]);
-  n->w1b = reinterpret_cast<__nv_bfloat16*>(b + off[11]);
-  n->w2b = reinterpret_cast<__nv_bfloat16*>(b + off[12]);
-  n->w3b = reinterpret_cast<__nv_bfloat16*>(b + off[13]);
+  n->pin = reinterpret_cast<h16*>(b + off[8]);
+  n->vin = reinterpret_cast<h16*>(b + off[9]);
+  n->hid = reinterpret_cast<h16*>(b + off[10]);
+  n->w1b = reinterpret_cast<h16*>(b + off[11]);
+  n->w2b = reinterpret_cast<h16*>(b + off[12]);
+  n->w3b = reinterpret_cast<h16*>(b + off[13]);
   cudaMemset(n->error, 0, 16);
   // activations start zeroed so that never-written padding rows read as zeros
   cudaMemset(b + off[3], 0, tot - off[3]);
@@ -1264,9 +1271,9 @@ int omq_resnet_load(omq_resnet* n, const uint16_t* d_conv_w, const float* d_conv
     const float* fc2p = fc1p + (size_t)2 * n->HW * n->Hp + n->Hp;
     const float* fc1v = fc2p + (size_t)n->Hp * n->A + n->A;
     count_launches(3);
-    k_pack_dense_w<<<256, 256, 0, s>>>(fc1p, 2 * n->HW, n->Hp, n->k1p, n->n1pad, n->w1b);
-    k_pack_dense_w<<<256, 256, 0, s>>>(fc2p, n->Hp, n->A, n->Hp, n->n2pad, n->w2b);
-    k_pack_dense_w<<<256, 256, 0, s>>>(fc1v, n->HW, n->Hv, n->k3p, n->n3pad, n->w3b);
+    k_pack_dense_w<<<256, 256, 0, s>>>(fc1p, 2 * n->HW, n->Hp, n->k1p, n->n1pad, n->f16, n->w1b);
+    k_pack_dense_w<<<256, 256, 0, s>>>(fc2p, n->Hp, n->A, n->Hp, n->n2pad, n->f16, n->w2b);
+    k_pack_dense_w<<<256, 256, 0, s>>>(fc1v, n->HW, n->Hv, n->k3p, n->n3pad, n->f16, n->w3b);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "omq_resnet_load: dense weights");
   }
@@ -1284,68 +1291,74 @@ int omq_resnet_memory(const omq_resnet* n, uint64_t* bytes) {
 
 namespace omq {
 
+template <bool F16>
 static int launch_conv_halo_tr(const omq_resnet* n, const CUtensorMap& tH, const CUtensorMap& tB,
-                               const CUtensorMap& tO, const float* bias, const __nv_bfloat16* res,
-                               __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count, int count,
-                               cudaStream_t s) {
+                               const CUtensorMap& tO, const ConvArgs& a, cudaStream_t s) {
   static std::atomic<uint64_t> attr_set{0};
   {
-    const cudaError_t e = set_smem_attr_once(attr_set, k_conv3x3_halo_t, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         HaloTCfg::kSmem);
+    const cudaError_t e = set_smem_attr_once(attr_set, k_conv3x3_halo_t<F16>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, HaloTCfg::kSmem);
     if (e != cudaSuccess) return cuda_status(e, "transposed halo conv smem attribute");
   }
-  ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
   const int max_tiles = (int)((n->rows + HaloTCfg::kRows - 1) / HaloTCfg::kRows);
   const int grid = max(1, min(max_tiles, n->sm_count));
   count_launches(1);
-  k_conv3x3_halo_t<<<grid, HaloTCfg::kThreads, HaloTCfg::kSmem, s>>>(tH, tB, tO, a);
+  k_conv3x3_halo_t<F16><<<grid, HaloTCfg::kThreads, HaloTCfg::kSmem, s>>>(tH, tB, tO, a);
   return cuda_status(cudaGetLastError(), "k_conv3x3_halo_t");
 }
 
-template <int BN>
+template <int BN, bool F16>
 static int launch_conv_pair(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB,
-                            const CUtensorMap& tO, const float* bias, const __nv_bfloat16* res, __nv_bfloat16* out,
-                            int kb_per_tap, const int32_t* d_count, int count, cudaStream_t s) {
+                            const CUtensorMap& tO, const ConvArgs& a, cudaStream_t s) {
   using Cfg = PairCfg<BN>;
   static std::atomic<uint64_t> attr_set{0};
   {
-    const cudaError_t e = set_smem_attr_once(attr_set, k_conv3x3_pair<BN>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+    const cudaError_t e = set_smem_attr_once(attr_set, k_conv3x3_pair<BN, F16>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
     if (e != cudaSuccess) return cuda_status(e, "pair conv smem attribute");
   }
-  ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
   const int max_tiles = (int)((n->rows + 2 * kTileM - 1) / (2 * kTileM));
   const int pairs = max(1, min(max_tiles, n->sm_count / 2));
   count_launches(1);
-  k_conv3x3_pair<BN><<<2 * pairs, Cfg::kThreads, Cfg::kSmem, s>>>(tA, tB, tO, a);
+  k_conv3x3_pair<BN, F16><<<2 * pairs, Cfg::kThreads, Cfg::kSmem, s>>>(tA, tB, tO, a);
   return cuda_status(cudaGetLastError(), "k_conv3x3_pair");
 }
 
 static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tO,
                 const float* bias,
-                const __nv_bfloat16* res, __nv_bfloat16* out, int kb_per_tap, const int32_t* d_count,
+                const h16* res, h16* out, int kb_per_tap, const int32_t* d_count,
                 int count, cudaStream_t s) {
-  if (n->pair == 1) return launch_conv_pair<256>(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
-  return launch_conv_halo_tr(n, tA, tB, tO, bias, res, out, kb_per_tap, d_count, count, s);
+  const ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
+  if (n->pair == 1)
+    return n->f16 ? launch_conv_pair<256, true>(n, tA, tB, tO, a, s) : launch_conv_pair<256, false>(n, tA, tB, tO, a, s);
+  return n->f16 ? launch_conv_halo_tr<true>(n, tA, tB, tO, a, s) : launch_conv_halo_tr<false>(n, tA, tB, tO, a, s);
 }
 
-template <int NT, int MODE>
-static int launch_dense(const CUtensorMap& tA, const CUtensorMap& tW, const DenseArgs& a, int rows_cap,
-                        int ntiles, cudaStream_t s) {
+template <int NT, int MODE, bool F16>
+static int launch_dense_t(const CUtensorMap& tA, const CUtensorMap& tW, const DenseArgs& a, int rows_cap,
+                          int ntiles, cudaStream_t s) {
   static std::atomic<uint64_t> attr_set{0};
   {
-    const cudaError_t e = set_smem_attr_once(attr_set, k_dense<NT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDenseSmem);
+    const cudaError_t e = set_smem_attr_once(attr_set, k_dense<NT, MODE, F16>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kDenseSmem);
     if (e != cudaSuccess) return cuda_status(e, "dense smem attribute");
   }
   count_launches(1);
-  k_dense<NT, MODE><<<dim3((rows_cap + 127) / 128, ntiles), kDenseThreads, kDenseSmem, s>>>(tA, tW, a);
+  k_dense<NT, MODE, F16><<<dim3((rows_cap + 127) / 128, ntiles), kDenseThreads, kDenseSmem, s>>>(tA, tW, a);
   return cuda_status(cudaGetLastError(), "k_dense");
 }
 
-// Heads on the tensor cores: 1x1 convolutions -> bf16 rows, then fc1 (policy) with ReLU,
+template <int NT, int MODE>
+static int launch_dense(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tW, const DenseArgs& a,
+                        int rows_cap, int ntiles, cudaStream_t s) {
+  return n->f16 ? launch_dense_t<NT, MODE, true>(tA, tW, a, rows_cap, ntiles, s)
+                : launch_dense_t<NT, MODE, false>(tA, tW, a, rows_cap, ntiles, s);
+}
+
+// Heads on the tensor cores: 1x1 convolutions -> 16-bit rows, then fc1 (policy) with ReLU,
 // fc2 (policy) with the softmax fused when the policy fits one 256-wide tile, and the value
 // head's fc1 with the fc2 dot and tanh fused.
-static int run_tc_heads(omq_resnet* n, const __nv_bfloat16* act, const int32_t* d_count, int count,
+static int run_tc_heads(omq_resnet* n, const h16* act, const int32_t* d_count, int count,
                         float* policy, float* value, cudaStream_t s) {
   const float* p = n->head;
   const float* w1x1 = p; p += 3 * n->C;
@@ -1360,23 +1373,23 @@ static int run_tc_heads(omq_resnet* n, const __nv_bfloat16* act, const int32_t* 
   const float* b2v = p;
   count_launches(1);
   k_head_in<<<max(1, min((count * n->HW + 255) / 256, 4 * n->sm_count)), 256, 3 * n->C * sizeof(float), s>>>(
-      act, n->C, n->S, n->P, w1x1, b1x1, d_count, count, n->pin, n->k1p, n->vin, n->k3p);
+      act, n->C, n->S, n->P, w1x1, b1x1, d_count, count, n->f16, n->pin, n->k1p, n->vin, n->k3p);
   int st = cuda_status(cudaGetLastError(), "k_head_in");
   if (st) return st;
   DenseArgs a{};
   a.d_count = d_count;
   a.count = count;
   a.error = n->error;
-  // policy fc1 -> hidden (bf16, ReLU)
+  // policy fc1 -> hidden (16-bit, ReLU)
   a.bias = b1p; a.out = n->hid; a.ld = n->Hp; a.n_total = n->Hp; a.kblocks = n->k1p / 64;
-  st = launch_dense<256, kDenseReluBf16>(n->tm_pin, n->tm_w1, a, count, n->n1pad / 256, s);
+  st = launch_dense<256, kDenseRelu16>(n, n->tm_pin, n->tm_w1, a, count, n->n1pad / 256, s);
   if (st) return st;
   // policy fc2 -> probabilities
   a.bias = b2p; a.out = policy; a.ld = n->A; a.n_total = n->A; a.kblocks = n->Hp / 64;
   if (n->A <= 256) {
-    st = launch_dense<256, kDenseSoftmax>(n->tm_hid, n->tm_w2, a, count, 1, s);
+    st = launch_dense<256, kDenseSoftmax>(n, n->tm_hid, n->tm_w2, a, count, 1, s);
   } else {
-    st = launch_dense<256, kDenseLogits>(n->tm_hid, n->tm_w2, a, count, n->n2pad / 256, s);
+    st = launch_dense<256, kDenseLogits>(n, n->tm_hid, n->tm_w2, a, count, n->n2pad / 256, s);
     if (!st) {
       count_launches(1);
       k_softmax_rows<<<max(1, min((count + 7) / 8, 8 * n->sm_count)), 256, 0, s>>>(policy, n->A, n->A, d_count, count);
@@ -1386,8 +1399,8 @@ static int run_tc_heads(omq_resnet* n, const __nv_bfloat16* act, const int32_t* 
   if (st) return st;
   // value fc1 + ReLU, fc2, tanh
   a.bias = b1v; a.w2 = fc2v; a.b2 = b2v; a.out = value; a.ld = 1; a.n_total = n->Hv; a.kblocks = n->k3p / 64;
-  if (n->nt3 == 128) return launch_dense<128, kDenseValue>(n->tm_vin, n->tm_w3, a, count, 1, s);
-  return launch_dense<256, kDenseValue>(n->tm_vin, n->tm_w3, a, count, 1, s);
+  if (n->nt3 == 128) return launch_dense<128, kDenseValue>(n, n->tm_vin, n->tm_w3, a, count, 1, s);
+  return launch_dense<256, kDenseValue>(n, n->tm_vin, n->tm_w3, a, count, 1, s);
 }
 
 // trunk + heads on n->x_in (already packed), count from d_count (device) or `count`.
@@ -1435,6 +1448,7 @@ int resnet_run(omq_resnet* n, const int32_t* d_count, int count, float* policy, 
   h.count = count;
   h.policy = policy;
   h.value = value;
+  h.f16 = n->f16;
   const size_t sm = head_smem_for(n, kHeadPos);
   cudaError_t e = cudaFuncSetAttribute(k_heads<kHeadPos>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return cuda_status(e, "heads smem attribute");
@@ -1461,7 +1475,7 @@ int omq_resnet_forward_features(omq_resnet* n, const float* d_features, int32_t 
   const int total = batch * n->P * (n->in_pad / 8);
   count_launches(1);
   k_pack_features<<<min((total + 255) / 256, 8192), 256, 0, s>>>(
-      d_features, n->cfg.input_channels, n->S, n->P, nullptr, batch, n->x_in);
+      d_features, n->cfg.input_channels, n->S, n->P, nullptr, batch, n->f16, n->x_in);
   int st = cuda_status(cudaGetLastError(), "k_pack_features");
   if (st) return st;
   return resnet_run(n, nullptr, batch, d_policy, d_value, s);
@@ -1501,7 +1515,7 @@ int omq_resnet_forward_queue(omq_resnet* n, omq_engine* e, int32_t queue, void* 
   }
   DeviceGuard g(n->cfg.device);
   cudaStream_t s = (cudaStream_t)stream;
-  launch_pack_queue(e->v, queue, n->P, n->in_pad, n->x_in, s);
+  launch_pack_queue(e->v, queue, n->P, n->in_pad, n->x_in, n->f16, s);
   int st = cuda_status(cudaGetLastError(), "pack queue");
   if (st) return st;
   return resnet_run(n, e->v.q_count + queue, cap, e->v.q_policy[queue], e->v.q_value[queue], s);
@@ -1623,7 +1637,8 @@ extern "C" int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const ui
   if (c.board_size < 5 || c.board_size > 19 || c.input_channels < 1 || c.input_channels > kMaxInputPlanes ||
       (c.filters != 128 && c.filters != 256) || c.num_blocks < 0 || c.num_blocks > 64 ||
       c.num_actions < 1 || c.num_actions > kMaxActions || c.fc_policy_hidden < 1 ||
-      c.fc_policy_hidden > 1024 || c.fc_value_hidden < 1 || c.fc_value_hidden > 1024) {
+      c.fc_policy_hidden > 1024 || c.fc_value_hidden < 1 || c.fc_value_hidden > 1024 ||
+      (c.dtype != OMQ_DTYPE_BF16 && c.dtype != OMQ_DTYPE_F16)) {
     set_error("bad resnet config");
     return OMQ_BAD_ARG;
   }
@@ -1658,15 +1673,16 @@ extern "C" int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const ui
   n.max_batch = max_batch;
   n.rows = (size_t)max_batch * P;
   n.in_pad = in_pad;
+  n.f16 = c.dtype == OMQ_DTYPE_F16;
   if (head_smem(&n) > 227 * 1024) { set_error("heads need too much shared memory"); return OMQ_BAD_ARG; }
   cudaDeviceGetAttribute(&n.sm_count, cudaDevAttrMultiProcessorCount, c.device);
-  n.conv_w = reinterpret_cast<__nv_bfloat16*>(const_cast<uint16_t*>(d_conv_w));
+  n.conv_w = reinterpret_cast<h16*>(const_cast<uint16_t*>(d_conv_w));
   n.conv_b = const_cast<float*>(d_conv_b);
   n.head = const_cast<float*>(d_head);
-  n.x_in = reinterpret_cast<__nv_bfloat16*>(base);
+  n.x_in = reinterpret_cast<h16*>(base);
   size_t off = ((n.rows * in_pad * 2) + 255) & ~(size_t)255;
   for (int i = 0; i < 3; ++i) {
-    n.act[i] = reinterpret_cast<__nv_bfloat16*>(base + off);
+    n.act[i] = reinterpret_cast<h16*>(base + off);
     off += ((n.rows * n.C * 2) + 255) & ~(size_t)255;
   }
   n.error = reinterpret_cast<int32_t*>(base + kNoAllocErrorOffset);
@@ -1681,7 +1697,7 @@ extern "C" int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const ui
   const int total = batch * P * (in_pad / 8);
   count_launches(1);
   k_pack_features<<<min((total + 255) / 256, 8192), 256, 0, s>>>(
-      d_features, c.input_channels, n.S, P, nullptr, batch, n.x_in);
+      d_features, c.input_channels, n.S, P, nullptr, batch, n.f16, n.x_in);
   st = cuda_status(cudaGetLastError(), "k_pack_features");
   if (st) return st;
   return resnet_run(&n, nullptr, batch, d_policy, d_value, s);

@@ -184,11 +184,12 @@ __device__ __forceinline__ uint64_t smem_desc_sw128_rows(uint32_t aligned_base, 
   return smem_desc_sw128(aligned_base + (uint32_t)row * 128u + (uint32_t)kbytes);
 }
 
-// Instruction descriptor of kind::f16: D fp32, A/B bf16, both K-major, shape M x N.
-__host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
+// Instruction descriptor of kind::f16: D fp32, A and B both bf16 (f16 = false) or both fp16
+// (f16 = true), both K-major, shape M x N.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool f16) {
   return (1u << 4)                      // D format: f32
-         | (1u << 7)                    // A format: bf16
-         | (1u << 10)                   // B format: bf16
+         | ((f16 ? 0u : 1u) << 7)       // A format: fp16 = 0, bf16 = 1
+         | ((f16 ? 0u : 1u) << 10)      // B format: the same as A
          | ((uint32_t)(N >> 3) << 17)   // N / 8
          | ((uint32_t)(M >> 4) << 24);  // M / 16
 }

@@ -273,38 +273,40 @@ class WaveEngine:
         """begin + forced root expansion + ceil(sims / max_wave_size) waves
         (python/mcts/core/mcts.py:1020-1063). Raises on a device status (e.g. TreeFullError).
         Go engines take history boards and ``meta`` (see ``begin``)."""
-        if isinstance(evaluator, str) and evaluator == "synthetic" and self.is_chess:
-            b, m = self._chess_roots(boards, meta)
-            self._boards, self._meta = b, m
-            _lib.check(self.L.omq_search_synthetic_chess(self._h, ctypes.c_void_p(b.data_ptr()),
-                                                         ctypes.c_void_p(m.data_ptr()),
-                                                         int(num_simulations), _stream_ptr()),
-                       "omq_search_synthetic_chess")
-            return
-        if isinstance(evaluator, str) and evaluator == "synthetic" and self.is_go:
-            b, m = self._go_roots(boards, meta)
-            k, kc = self._go_keys(keys)
-            self._boards, self._meta, self._keys = b, m, (k, kc)
-            _lib.check(self.L.omq_search_synthetic_go(self._h, ctypes.c_void_p(b.data_ptr()),
-                                                      ctypes.c_void_p(m.data_ptr()),
-                                                      ctypes.c_void_p(k.data_ptr()),
-                                                      ctypes.c_void_p(kc.data_ptr()),
-                                                      int(num_simulations), _stream_ptr()),
-                       "omq_search_synthetic_go")
-            return
-        if isinstance(evaluator, str) and evaluator == "synthetic":
-            b = boards.to(self.device, torch.int8).contiguous()
-            self._boards = b
-            _lib.check(self.L.omq_search_synthetic(self._h, ctypes.c_void_p(b.data_ptr()),
-                                                   int(num_simulations), _stream_ptr()),
-                       "omq_search_synthetic")
+        synthetic = isinstance(evaluator, str) and evaluator == "synthetic"
+        native_net = getattr(evaluator, "_net", None) if hasattr(evaluator, "forward_queue") else None
+        graphed = (graphs and native_net is not None and not getattr(evaluator, "profiling", False))
+        if synthetic or (native_net is not None and not graphed):
+            # one native call: begin, root expansion and every wave, evaluations on the device
+            # leaf queues (omq_search*, the C-ABI counterpart of MCTS._run_search)
+            net = None
+            if not synthetic:
+                evaluator._ensure(self.queue_capacity)
+                net = evaluator._net
+            sims, st = int(num_simulations), _stream_ptr()
+            if self.is_chess:
+                b, m = self._chess_roots(boards, meta)
+                self._boards, self._meta = b, m
+                _lib.check(self.L.omq_search_chess(self._h, net, ctypes.c_void_p(b.data_ptr()),
+                                                   ctypes.c_void_p(m.data_ptr()), sims, st), "omq_search_chess")
+            elif self.is_go:
+                b, m = self._go_roots(boards, meta)
+                k, kc = self._go_keys(keys)
+                self._boards, self._meta, self._keys = b, m, (k, kc)
+                _lib.check(self.L.omq_search_go(self._h, net, ctypes.c_void_p(b.data_ptr()),
+                                                ctypes.c_void_p(m.data_ptr()), ctypes.c_void_p(k.data_ptr()),
+                                                ctypes.c_void_p(kc.data_ptr()), sims, st), "omq_search_go")
+            else:
+                b = boards.to(self.device, torch.int8).contiguous()
+                if b.shape != (self.num_trees, self.board_size, self.board_size):
+                    raise ValueError(f"boards must be [{self.num_trees}, {self.board_size}, {self.board_size}]")
+                self._boards = b
+                _lib.check(self.L.omq_search(self._h, net, ctypes.c_void_p(b.data_ptr()), sims, st), "omq_search")
             return
         self.begin(boards, meta, keys)
         self.root_expand(evaluator)
         # full-size waves replay a CUDA graph when asked (MCTSConfig.use_cuda_graphs) and the
         # evaluator runs on the device queue (no host round trip inside a wave)
-        graphed = (graphs and hasattr(evaluator, "forward_queue")
-                   and not getattr(evaluator, "profiling", False))
         done = 0
         while done < num_simulations:
             w = min(self.max_wave_size, num_simulations - done)

@@ -44,14 +44,17 @@ class SyntheticEvaluator:
 def _resolve_evaluator(evaluator, board_size: int = 15):
     """The evaluator the engine runs. A reference ResNetModel - passed directly, or inside a
     reference ResNetEvaluator as its ``model`` (resnet_evaluator.py:80-265, possibly TorchScript-
-    compiled) - becomes this package's bf16 tensor-core ResNetEvaluator with the same weights;
-    the synthetic evaluator runs on the device; anything else is called through evaluate_batch."""
+    compiled) - becomes this package's tensor-core ResNetEvaluator with the same weights (fp16 when
+    the reference evaluator runs under its fp16 autocast, `use_amp`, else bf16); the synthetic
+    evaluator runs on the device; anything else is called through evaluate_batch."""
     if isinstance(evaluator, SyntheticEvaluator) or (isinstance(evaluator, str) and evaluator == "synthetic"):
         return "synthetic"
     module = evaluator if hasattr(evaluator, "residual_blocks") else getattr(evaluator, "model", None)
     if module is not None and hasattr(module, "residual_blocks") and hasattr(module, "state_dict"):
         from . import resnet
-        return resnet.ResNetEvaluator(module.state_dict(), board_size=getattr(module, "board_size", board_size))
+        dtype = "fp16" if getattr(evaluator, "use_amp", False) is True else "bf16"
+        return resnet.ResNetEvaluator(module.state_dict(), board_size=getattr(module, "board_size", board_size),
+                                      dtype=dtype)
     return evaluator
 
 

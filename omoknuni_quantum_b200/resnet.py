@@ -140,9 +140,12 @@ def reference_forward_fp32(sd: Dict[str, torch.Tensor], x: torch.Tensor):
     return torch.exp(logp), v.reshape(B)
 
 
-def pack_parameters(sd: Dict[str, torch.Tensor], spec: ResNetSpec):
+DTYPES = {"bf16": (_lib.OMQ_DTYPE_BF16, torch.bfloat16), "fp16": (_lib.OMQ_DTYPE_F16, torch.float16)}
+
+
+def pack_parameters(sd: Dict[str, torch.Tensor], spec: ResNetSpec, dtype: str = "bf16"):
     """Fold BatchNorm and lay the parameters out as omq_resnet_load expects
-    (conv_w bf16, conv_b fp32, head fp32; see include/omq_b200.h)."""
+    (conv_w in the net's 16-bit dtype, conv_b fp32, head fp32; see include/omq_b200.h)."""
     C = spec.filters
     ws, bs = [], []
 
@@ -159,7 +162,7 @@ def pack_parameters(sd: Dict[str, torch.Tensor], spec: ResNetSpec):
         for c, n in (("conv1", "bn1"), ("conv2", "bn2")):
             w, b = _fold(sd, p + c, p + n)
             ws.append(pack_conv(w, C)); bs.append(b)
-    conv_w = torch.cat([x.reshape(-1) for x in ws]).to(torch.bfloat16)
+    conv_w = torch.cat([x.reshape(-1) for x in ws]).to(DTYPES[dtype][1])
     conv_b = torch.cat(bs).float()
     wp, bp = _fold(sd, "policy_head.conv", "policy_head.bn")
     wv, bv = _fold(sd, "value_head.conv", "value_head.bn")
@@ -174,15 +177,24 @@ def pack_parameters(sd: Dict[str, torch.Tensor], spec: ResNetSpec):
 
 
 class ResNetEvaluator:
-    """bf16 tcgen05 ResNet on one GPU. ``evaluate_batch(features)`` keeps the reference
+    """tcgen05 ResNet on one GPU. ``evaluate_batch(features)`` keeps the reference
     protocol (features [B, C, n, n] -> probabilities [B, A], values [B]); inside the device
     search the engine calls ``forward_queue`` instead, which packs the queued leaves on the
-    device and writes the queue's result buffers without a host round trip."""
+    device and writes the queue's result buffers without a host round trip.
+
+    ``dtype`` is the 16-bit type of the weights, activations and dense-layer operands (fp32
+    accumulation either way): "bf16" (default; the benchmark configs' type) or "fp16", the
+    precision of the reference evaluator's autocast (resnet_evaluator.py:247-249). fp16 keeps 3
+    more mantissa bits, which is what keeps a 20-block trunk within 2e-2 of an fp32 forward; like
+    the reference's autocast it overflows above 65504."""
 
     def __init__(self, state_dict: Dict[str, torch.Tensor], board_size: int = 15,
-                 max_batch: int = 4096, device=None):
+                 max_batch: int = 4096, device=None, dtype: str = "bf16"):
         if not torch.cuda.is_available():
             raise RuntimeError("ResNetEvaluator needs a CUDA device (B200); there is no CPU fallback")
+        if dtype not in DTYPES:
+            raise ValueError(f"dtype must be one of {sorted(DTYPES)}")
+        self.dtype = dtype
         self.spec = spec_from_state_dict(state_dict, board_size)
         self.state_dict = {k: v.detach().cpu() for k, v in state_dict.items()}
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -209,14 +221,15 @@ class ResNetEvaluator:
         self.close()
         s = self.spec
         cfg = _lib.ResNetConfig(s.board_size, s.input_channels, s.num_blocks, s.filters, s.num_actions,
-                                s.fc_policy_hidden, s.fc_value_hidden, int(max_batch), self.device.index or 0)
+                                s.fc_policy_hidden, s.fc_value_hidden, int(max_batch), self.device.index or 0,
+                                DTYPES[self.dtype][0])
         h = ctypes.c_void_p()
         with torch.cuda.device(self.device):
             _lib.check(self.L.omq_resnet_create(ctypes.byref(cfg), ctypes.byref(h)), "omq_resnet_create")
             self._net = h
             self._max_batch = int(max_batch)
             self.generation += 1
-            conv_w, conv_b, head = pack_parameters(self.state_dict, s)
+            conv_w, conv_b, head = pack_parameters(self.state_dict, s, self.dtype)
             a, b, c = (ctypes.c_uint64() for _ in range(3))
             _lib.check(self.L.omq_resnet_param_sizes(h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c)),
                        "omq_resnet_param_sizes")

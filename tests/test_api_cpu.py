@@ -170,14 +170,15 @@ def test_config_presets():
 
 def test_reference_models_and_evaluators_become_the_device_resnet(monkeypatch):
     """A reference ResNetModel, or a reference ResNetEvaluator holding one as ``model``, is run by
-    the tensor-core ResNet with its state_dict; the board size comes from the MCTS config."""
+    the tensor-core ResNet with its state_dict; the board size comes from the MCTS config, and an
+    evaluator under the reference's fp16 autocast (use_amp) keeps fp16."""
     from omoknuni_quantum_b200 import mcts, resnet
 
     made = []
 
     class Stub:
-        def __init__(self, sd, board_size):
-            made.append((sd, board_size))
+        def __init__(self, sd, board_size, dtype):
+            made.append((sd, board_size, dtype))
 
     monkeypatch.setattr(resnet, "ResNetEvaluator", Stub)
 
@@ -188,15 +189,17 @@ def test_reference_models_and_evaluators_become_the_device_resnet(monkeypatch):
             return {"w": 1}
 
     class RefEvaluator:
-        def __init__(self):
+        def __init__(self, use_amp=False):
             self.model = Model()
+            self.use_amp = use_amp
 
         def evaluate_batch(self, x):
             raise AssertionError("the reference evaluator itself must not be called")
 
     assert isinstance(mcts._resolve_evaluator(Model(), 19), Stub)
     assert isinstance(mcts._resolve_evaluator(RefEvaluator(), 8), Stub)
-    assert made == [({"w": 1}, 19), ({"w": 1}, 8)]
+    assert isinstance(mcts._resolve_evaluator(RefEvaluator(use_amp=True), 15), Stub)
+    assert made == [({"w": 1}, 19, "bf16"), ({"w": 1}, 8, "bf16"), ({"w": 1}, 15, "fp16")]
     other = object()
     assert mcts._resolve_evaluator(other) is other
     assert mcts._resolve_evaluator("synthetic") == "synthetic"

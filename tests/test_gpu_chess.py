@@ -151,10 +151,11 @@ def test_chess_resnet_matches_fp32_reference(oracle_lib, filters):
     assert dp < 2e-2 and dv < 2e-2, (dp, dv)
 
 
-def test_chess_resnet_queue_path_equals_protocol_path():
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_chess_resnet_queue_path_equals_protocol_path(dtype):
     from omoknuni_quantum_b200.chess import random_position
     from omoknuni_quantum_b200.resnet import ResNetEvaluator
-    ev = ResNetEvaluator.random(_chess_spec(), seed=3, max_batch=1024)
+    ev = ResNetEvaluator.random(_chess_spec(), seed=3, max_batch=1024, dtype=dtype)
 
     class Protocol:
         def evaluate_batch(self, f):

@@ -155,12 +155,13 @@ def test_go_resnet_matches_fp32_reference(filters):
     assert dp < 2e-2 and dv < 2e-2, (dp, dv)
 
 
-def test_go_resnet_queue_path_equals_protocol_path():
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_go_resnet_queue_path_equals_protocol_path(dtype):
     """forward_queue packs the 17 planes on the device straight from the tree; the result equals
     evaluate_batch on the engine's fp32 feature tensor (identical trees)."""
     from omoknuni_quantum_b200.engine import WaveEngine
     from omoknuni_quantum_b200.resnet import ResNetEvaluator
-    ev = ResNetEvaluator.random(_go_spec(), seed=2, max_batch=1024)
+    ev = ResNetEvaluator.random(_go_spec(), seed=2, max_batch=1024, dtype=dtype)
 
     class Protocol:
         def evaluate_batch(self, f):

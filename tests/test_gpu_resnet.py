@@ -30,12 +30,13 @@ def _features(n, seed=0):
     return torch.from_numpy(f)
 
 
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
 @pytest.mark.parametrize("blocks,filters,hv", [(10, 128, 128), (2, 256, 256)])
-def test_forward_matches_fp32_reference(blocks, filters, hv):
+def test_forward_matches_fp32_reference(blocks, filters, hv, dtype):
     from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec, init_state_dict, reference_forward_fp32
     spec = ResNetSpec(num_blocks=blocks, filters=filters, fc_value_hidden=hv)
     sd = init_state_dict(spec, seed=7)
-    ev = ResNetEvaluator(sd, max_batch=512)
+    ev = ResNetEvaluator(sd, max_batch=512, dtype=dtype)
     x = _features(333, seed=blocks)
     p, v = ev.evaluate_batch(x.cuda())
     torch.cuda.synchronize()
@@ -76,11 +77,37 @@ def _calibrate_bn(sd, x):
     return sd
 
 
-@pytest.mark.parametrize("game", ["gomoku", "go", "chess"])
-def test_deep_20x256_forward_matches_fp32_reference(game):
-    """The model of configs 2-4 at full depth (20 blocks x 256 filters, 41 bf16 convolutions)
-    against the fp32 forward, on a few hundred positions of each game's shape."""
-    from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec, init_state_dict, reference_forward_fp32
+def _rounded_forward(sd, x, dt):
+    """The fp32 forward with the trunk's weights (BatchNorm folded) and every activation the
+    kernels store rounded to the 16-bit type `dt`: the error that rounding alone causes, with no
+    kernel involved."""
+    import torch.nn.functional as F
+    from omoknuni_quantum_b200.resnet import _fold
+    q = lambda t: t.to(dt).float()
+    w, b = _fold(sd, "conv_input", "bn_input")
+    h = q(F.relu(F.conv2d(q(x), q(w), padding=1) + b.view(1, -1, 1, 1)))
+    i = 0
+    while f"residual_blocks.{i}.conv1.weight" in sd:
+        p = f"residual_blocks.{i}."
+        w1, b1 = _fold(sd, p + "conv1", p + "bn1")
+        w2, b2 = _fold(sd, p + "conv2", p + "bn2")
+        o = q(F.relu(F.conv2d(h, q(w1), padding=1) + b1.view(1, -1, 1, 1)))
+        h = q(F.relu(F.conv2d(o, q(w2), padding=1) + b2.view(1, -1, 1, 1) + h))
+        i += 1
+    B = h.shape[0]
+    wp, bp = _fold(sd, "policy_head.conv", "policy_head.bn")
+    wv, bv = _fold(sd, "value_head.conv", "value_head.bn")
+    pp = F.relu(F.conv2d(h, wp) + bp.view(1, -1, 1, 1)).reshape(B, -1)
+    pp = F.relu(F.linear(pp, sd["policy_head.fc1.weight"], sd["policy_head.fc1.bias"]))
+    lp = F.log_softmax(F.linear(pp, sd["policy_head.fc2.weight"], sd["policy_head.fc2.bias"]), 1)
+    vv = F.relu(F.conv2d(h, wv) + bv.view(1, -1, 1, 1)).reshape(B, -1)
+    vv = F.relu(F.linear(vv, sd["value_head.fc1.weight"], sd["value_head.fc1.bias"]))
+    v = torch.tanh(F.linear(vv, sd["value_head.fc2.weight"], sd["value_head.fc2.bias"]))
+    return lp.exp(), v.reshape(B)
+
+
+def _deep_case(game):
+    from omoknuni_quantum_b200.resnet import ResNetSpec, init_state_dict
     n, planes, acts = {"gomoku": (15, 19, 225), "go": (19, 17, 362), "chess": (8, 119, 4672)}[game]
     hv = 128 if game == "gomoku" else 256
     spec = ResNetSpec(board_size=n, input_channels=planes, num_blocks=20, filters=256, num_actions=acts,
@@ -93,7 +120,18 @@ def test_deep_20x256_forward_matches_fp32_reference(game):
         sd = _calibrate_bn(sd, x[:128])
     # a peaked policy: logits of a few units (the initialiser's fc2 gain of 0.1 gives ~0.01)
     sd["policy_head.fc2.weight"] = sd["policy_head.fc2.weight"] * (30.0 * (acts / 225) ** 0.5)
-    ev = ResNetEvaluator({k: t.cpu() for k, t in sd.items()}, board_size=n, max_batch=300)
+    return n, acts, sd, x
+
+
+@pytest.mark.parametrize("game", ["gomoku", "go", "chess"])
+def test_deep_20x256_fp16_forward_matches_fp32_reference(game):
+    """The model of configs 2-4 at full depth (20 blocks x 256 filters, 41 convolutions) in fp16,
+    the reference evaluator's autocast precision, against the fp32 forward within the 2e-2 gate,
+    on a few hundred positions of each game's shape, with BatchNorm statistics that keep the
+    values inside (-1, 1) and the policy far from uniform."""
+    from omoknuni_quantum_b200.resnet import ResNetEvaluator, reference_forward_fp32
+    n, acts, sd, x = _deep_case(game)
+    ev = ResNetEvaluator({k: t.cpu() for k, t in sd.items()}, board_size=n, max_batch=300, dtype="fp16")
     p, v = ev.evaluate_batch(x)
     torch.cuda.synchronize()
     assert ev.error() == 0
@@ -108,6 +146,28 @@ def test_deep_20x256_forward_matches_fp32_reference(game):
     assert dp < TOL and dv < TOL, (dp, dv)
 
 
+@pytest.mark.parametrize("game", ["gomoku", "go", "chess"])
+def test_deep_20x256_bf16_forward_error_is_the_rounding_error(game):
+    """The same model in bf16 (the benchmark configs' type). bf16 keeps 8 significant bits, and
+    over 41 convolutions the rounding of weights and stored activations alone moves the outputs
+    by several 1e-2 from fp32 (measured by `_rounded_forward`, no kernel involved). The kernels
+    must add no error of their own beyond that: their deviation from fp32 stays within 1.5x the
+    rounding-only deviation (plus 5e-3)."""
+    from omoknuni_quantum_b200.resnet import ResNetEvaluator, reference_forward_fp32
+    n, acts, sd, x = _deep_case(game)
+    ev = ResNetEvaluator({k: t.cpu() for k, t in sd.items()}, board_size=n, max_batch=300, dtype="bf16")
+    p, v = ev.evaluate_batch(x)
+    torch.cuda.synchronize()
+    assert ev.error() == 0
+    with torch.no_grad():
+        pr, vr = reference_forward_fp32(sd, x)
+        pq, vq = _rounded_forward(sd, x, torch.bfloat16)
+    ep, ev_ = (pq - pr).abs().max().item(), (vq - vr).abs().max().item()
+    dp, dv = (p - pr).abs().max().item(), (v - vr).abs().max().item()
+    assert torch.isfinite(p).all() and torch.isfinite(v).all()
+    assert dp <= 1.5 * ep + 5e-3 and dv <= 1.5 * ev_ + 5e-3, (dp, ep, dv, ev_)
+
+
 def test_forward_is_batch_invariant():
     from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec
     ev = ResNetEvaluator.random(ResNetSpec(num_blocks=3, filters=128), seed=3, max_batch=512)
@@ -120,13 +180,14 @@ def test_forward_is_batch_invariant():
     assert torch.equal(p1[:5], p3) and torch.equal(v1[:5], v3)
 
 
-def test_queue_path_equals_protocol_path():
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_queue_path_equals_protocol_path(dtype):
     """forward_queue (device packing from the tree) == evaluate_batch on the engine's reference
     feature tensor: identical trees."""
     from omoknuni_quantum_b200.engine import WaveEngine
     from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec
     from omoknuni_quantum_b200.roots import random_roots
-    ev = ResNetEvaluator.random(ResNetSpec(num_blocks=2, filters=128), seed=1, max_batch=1024)
+    ev = ResNetEvaluator.random(ResNetSpec(num_blocks=2, filters=128), seed=1, max_batch=1024, dtype=dtype)
 
     class Protocol:
         def evaluate_batch(self, f):

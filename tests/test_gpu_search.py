@@ -354,3 +354,65 @@ def test_device_prior_sum_is_torchs_order():
     want = np.array([torch.from_numpy(v).sum().item() if len(v) else 0.0 for v in vals], np.float32)
     bad = [n for n, a, b in zip(lengths, got, want) if a != b]
     assert not bad, bad[:10]
+
+
+@pytest.mark.parametrize("game", ["gomoku", "go", "chess"])
+def test_one_call_search_equals_stepwise_search(game):
+    """omq_search / omq_search_go / omq_search_chess (one C-ABI call: begin, root expansion and
+    every wave with the tensor-core ResNet on the leaf queues) build the same trees as the same
+    search sequenced step by step from the host (begin, root_expand, wave, ...)."""
+    import ctypes
+    from omoknuni_quantum_b200 import _lib
+    from omoknuni_quantum_b200.engine import WaveEngine, _stream_ptr
+    from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec
+    R, sims, wave = 3, 200, 64
+    if game == "go":
+        from omoknuni_quantum_b200.go import random_roots as go_roots
+        hist, meta = go_roots(4, R, moves=40, board_size=19)
+        boards, meta = torch.from_numpy(hist).cuda(), torch.from_numpy(meta)
+        spec = ResNetSpec(board_size=19, input_channels=17, num_blocks=2, filters=256, num_actions=362)
+        n = 19
+    elif game == "chess":
+        from omoknuni_quantum_b200.chess import random_position
+        ps = [random_position(40 + i) for i in range(R)]
+        boards = np.stack([p.root_records() for p in ps])
+        meta = np.array([len(p.prior) for p in ps], np.int32)
+        spec = ResNetSpec(board_size=8, input_channels=119, num_blocks=2, filters=128, num_actions=4672)
+        n = 8
+    else:
+        from omoknuni_quantum_b200.roots import random_roots
+        boards, meta = torch.from_numpy(random_roots(8, R)).cuda(), None
+        spec = ResNetSpec(num_blocks=2, filters=128)
+        n = 15
+    ev = ResNetEvaluator.random(spec, seed=4, max_batch=R * wave)
+    engines = [WaveEngine(R, board_size=n, capacity=80000, max_wave_size=wave, game=game)
+               for _ in range(2)]
+    a, b = engines
+    # one call through the C ABI
+    L = _lib.load()
+    if game == "chess":
+        rec, npr = a._chess_roots(boards, meta)
+        st = L.omq_search_chess(a._h, ev._net, ctypes.c_void_p(rec.data_ptr()), ctypes.c_void_p(npr.data_ptr()),
+                                sims, _stream_ptr())
+    elif game == "go":
+        h, m = a._go_roots(boards, meta)
+        k, kc = a._go_keys(None)
+        st = L.omq_search_go(a._h, ev._net, ctypes.c_void_p(h.data_ptr()), ctypes.c_void_p(m.data_ptr()),
+                             ctypes.c_void_p(k.data_ptr()), ctypes.c_void_p(kc.data_ptr()), sims, _stream_ptr())
+    else:
+        st = L.omq_search(a._h, ev._net, ctypes.c_void_p(boards.data_ptr()), sims, _stream_ptr())
+    _lib.check(st, "omq_search")
+    # the same search step by step
+    b.begin(boards, meta)
+    b.root_expand(ev)
+    done = 0
+    while done < sims:
+        w = min(wave, sims - done)
+        b.wave(w, ev)
+        done += w
+    b.check_status()
+    for r in range(R):
+        ta, tb = a.export_tree(r), b.export_tree(r)
+        assert ta["visits"].shape[0] > 1
+        for key in ta:
+            assert np.array_equal(ta[key], tb[key]), (r, key)
