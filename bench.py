@@ -171,6 +171,35 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def config1_config(args, ws):
+    """The `config` of config-1 lines: the same dict in the B200 arm and the reference arm."""
+    return {"workload": WORKLOAD, "roots_per_gpu": args.roots, "global_batch": args.roots * ws,
+            "sims": args.sims, "wave": args.wave, "capacity": args.capacity,
+            "model": f"resnet{args.blocks}x{args.filters} (value fc {args.value_hidden})",
+            "parallelism": f"dp{ws} (independent trees per GPU, weights NCCL-broadcast once)",
+            "l2": "inputs larger than L2 (multi-GB activations per ResNet call)"}
+
+
+def run_reference_script(args, mode, budget, timeout, extra=()):
+    """baseline/run_reference.py in a child process: the unmodified reference (staged under
+    baseline/_ref) through its own MCTS(config, evaluator).search, on the bench's seeded roots and
+    weights. Returns its JSON result, or {"unavailable": reason}."""
+    cmd = [sys.executable, os.path.join(REPO, "baseline", "run_reference.py"), "--mode", mode,
+           "--sims", str(args.sims), "--wave", str(args.wave), "--capacity", str(args.capacity),
+           "--blocks", str(args.blocks), "--filters", str(args.filters),
+           "--value-hidden", str(args.value_hidden), "--seed", str(args.seed), "--roots", str(args.roots),
+           "--budget", str(budget), *extra]
+    try:
+        out = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"reference {mode} run exceeded {timeout} s"}
+    for line in reversed(out.stdout.strip().splitlines()):
+        if line.startswith("{"):
+            return json.loads(line)
+    tail = (out.stderr or out.stdout).strip().splitlines()[-1:] or ["no output"]
+    return {"unavailable": f"reference {mode} run failed (rc {out.returncode}): {tail[0][:200]}"}
+
+
 def make_spec(args):
     from omoknuni_quantum_b200.resnet import ResNetSpec
     if args.workload == "config4":
@@ -204,14 +233,16 @@ def apply_config3(args):
 # ---------------------------------------------------------------------------------------------
 # CPU arms
 # ---------------------------------------------------------------------------------------------
-def cpu_search_rate(args, sd, budget_s: float, game: str = "gomoku"):
-    """Reference algorithm on the host: oracle tree search (C++ restatement of the reference's
-    torch WaveSearch) + fp32 torch ResNet forward on all host cores. Searches seeded roots of
-    the workload until `budget_s` of work is done; returns (sims/s, sims, seconds, threads)."""
+def cpu_search_rate(args, sd, budget_s: float, game: str = "gomoku", first_root: int = 0):
+    """The reference algorithm on the host as the oracle port runs it: the oracle's C++ tree
+    search (restatement of the reference's torch WaveSearch) + the fp32 torch ResNet forward on
+    all host cores. Whole searches of the bench's seeded roots (root first_root, first_root + 1,
+    ...) until `budget_s` has passed (at least one); returns (sims/s, sims, seconds, threads,
+    searches)."""
     from oracle import pyoracle
     from omoknuni_quantum_b200 import go as gomod
     from omoknuni_quantum_b200.resnet import reference_forward_fp32
-    from omoknuni_quantum_b200.roots import random_root
+    from omoknuni_quantum_b200.roots import random_roots
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     sd32 = {k: v.float() for k, v in sd.items()}
@@ -221,24 +252,25 @@ def cpu_search_rate(args, sd, budget_s: float, game: str = "gomoku"):
             p, v = reference_forward_fp32(sd32, torch.from_numpy(f))
         return p.numpy(), v.numpy()
 
-    sims_done, t0 = 0, time.perf_counter()
-    r = 0
+    gomoku_roots = random_roots(args.seed * 1000, max(args.roots, first_root + 1)) if game == "gomoku" else None
+    sims_done, searches, t0 = 0, 0, time.perf_counter()
+    r = first_root
     while True:
         if game == "chess":
             from omoknuni_quantum_b200 import chess as chessmod
             o = pyoracle.Oracle(args.capacity, 8)
             cfg = o.config(args.sims, args.wave)
-            cp = chessmod.random_position(args.seed * 7919 + r)
+            cp = chessmod.random_position(args.seed * 1_000_003 + r)
             st = o.begin_chess(cp.record(), cfg, prior=cp.prior, evaluator=ev)
         elif game == "go":
             o = pyoracle.Oracle(args.capacity, 19)
             cfg = o.config(args.sims, args.wave)
-            g = gomod.random_position(args.seed * 7919 + r, 60, 19)
+            g = gomod.random_position(args.seed * 1_000_003 + r, 60, 19)
             st = o.begin_go(g.history_planes(), g.to_move, cfg, ko=g.ko, passes=g.passes, evaluator=ev)
         else:
             o = pyoracle.Oracle(args.capacity)
             cfg = o.config(args.sims, args.wave)
-            st = o.begin(random_root(args.seed * 7919 + r), cfg, evaluator=ev)
+            st = o.begin(gomoku_roots[r % len(gomoku_roots)], cfg, evaluator=ev)
         if st != 0:
             raise RuntimeError("oracle begin failed")
         done = 0
@@ -247,17 +279,24 @@ def cpu_search_rate(args, sd, budget_s: float, game: str = "gomoku"):
             if o.wave(w) != 0:
                 raise RuntimeError("oracle wave failed")
             done += w
-            sims_done += w
-            if time.perf_counter() - t0 > budget_s:
-                break
+        sims_done += args.sims
+        searches += 1
         r += 1
         if time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
-    return sims_done / dt, sims_done, dt, threads
+    return sims_done / dt, sims_done, dt, threads, searches
 
 
 def run_reference_arm(args):
+    """`--impl reference`: the reference's own implementation of the path on this box's host
+    cores, on the B200 arm's workload and config. For config 1 that is the unmodified reference
+    (baseline/_ref) searching through its own MCTS.search with its deterministic torch
+    WaveSearch and its fp32 ResNet: whole searches of the bench's seeded roots within a bounded
+    time (the headline, kind "reference"); beside it the oracle port (the same algorithm as a C++
+    restatement) and the reference's Cython CPU backend. Configs 3-4 have no reference search
+    (the reference's Go and chess wave search use placeholder rules), so the port is their
+    reference arm (kind "port"). One step = 1/K of the timed sample."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return
@@ -268,29 +307,52 @@ def run_reference_arm(args):
     if game == "chess":
         apply_config4(args)
     sd = init_state_dict(make_spec(args), seed=args.seed)
-    budget = max(2.0, args.cpu_seconds / max(1, args.steps))
-    for _ in range(max(0, min(args.warmup, 1))):
-        cpu_search_rate(args, sd, 1.0, game)
-    rates, sims_total, secs_total = [], 0, 0.0
-    threads = 1
-    for _ in range(args.steps):
-        rate, sims, secs, threads = cpu_search_rate(args, sd, budget, game)
-        rates.append(rate)
-        sims_total += sims
-        secs_total += secs
-    value = sims_total / secs_total
-    sample = (f"{sims_total} simulations of {args.workload} searches (seeded roots, {args.sims} sims "
-              f"each, wave {args.wave}) in {secs_total:.1f} s, fp32 CPU ResNet {args.blocks}x{args.filters}")
+    budget = max(2.0, args.cpu_seconds)
+    ref = None
+    if game == "gomoku":
+        ref = run_reference_script(args, "cpu", budget, timeout=max(900, 20 * budget),
+                                   extra=("--warmup", str(max(1, min(args.warmup, 1)))))
+    baselines = {}
+    if ref is not None and "unavailable" not in ref:
+        value, secs, sims = ref["sims_per_s"], ref["seconds"], ref["sims"]
+        threads, kind = ref["threads"], "reference"
+        sample = (f"{ref['searches']} whole {args.sims}-simulation searches (wave {args.wave}) of the bench's seeded "
+                  f"roots by the unmodified reference ({ref['wave_search']}, device cpu, its fp32 ResNetModel "
+                  f"{args.blocks}x{args.filters} under its ResNetEvaluator) in {secs:.1f} s")
+        rate, psims, psecs, pthreads, psearch = cpu_search_rate(args, sd, max(2.0, args.cpu_seconds / 2), game)
+        baselines["oracle_port"] = {"value": rate, "unit": UNIT, "cores": pthreads, "kind": "port",
+                                    "sample": f"{psearch} whole searches ({psims} simulations) in {psecs:.1f} s: "
+                                              "oracle C++ tree + fp32 torch CPU ResNet"}
+        cy = run_reference_script(args, "cython", max(2.0, args.cpu_seconds / 2), timeout=900)
+        if "unavailable" in cy:
+            baselines["reference_cython"] = cy
+        else:
+            baselines["reference_cython"] = {
+                "value": cy["sims_per_s"], "unit": UNIT, "cores": cy["threads"], "kind": "reference",
+                "nondeterministic": True,
+                "sample": f"{cy['searches']} whole searches in {cy['seconds']:.1f} s by the reference's CPU backend "
+                          f"({cy['wave_search']} + Cython tree), fp32 ResNet on the host"}
+    else:
+        if ref is not None:
+            baselines["reference_torch_cpu"] = ref      # why the reference itself could not run
+        value, sims, secs, threads, searches = cpu_search_rate(args, sd, budget, game)
+        kind = "port"
+        sample = (f"{searches} whole searches ({sims} simulations) of {args.workload} in {secs:.1f} s: oracle C++ "
+                  f"tree{' with the ' + game + ' rules' if game != 'gomoku' else ''} + fp32 torch CPU ResNet "
+                  f"{args.blocks}x{args.filters}")
+    if game == "gomoku":
+        config = config1_config(args, ws)
+    else:
+        config = {"workload": {"go": WORKLOAD_GO, "chess": WORKLOAD_CHESS}[game], "sims": args.sims,
+                  "wave": args.wave, "model": f"resnet{args.blocks}x{args.filters}", "parallelism": "host threads"}
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 * secs_total / max(1, args.steps),
+            "warmup": args.warmup, "ms_per_step": 1000.0 * secs / max(1, args.steps),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded roots, seeded He-init weights)", "impl": "reference",
-            "config": {"workload": {"go": WORKLOAD_GO, "chess": WORKLOAD_CHESS}.get(game, WORKLOAD), "sims": args.sims,
-                       "wave": args.wave, "model": f"resnet{args.blocks}x{args.filters}",
-                       "parallelism": "host threads"},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": sample},
-            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "config": config,
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "baselines": baselines}
     print(json.dumps(line), flush=True)
 
 
@@ -393,12 +455,43 @@ def run_b200(args):
                "h2d_bytes_per_step": R * 225, "d2h_bytes_per_step": R * 225 * 4,
                "api": "MCTS(config, ResNetEvaluator).search_batch(pinned host boards) -> numpy policies"}
 
+    # single-tree latency through the public API (one root per MCTS.search call, as the
+    # reference's own users call it), and the reference's default CUDA search path on this GPU
+    single, ref_gpu = None, None
+    if rank == 0 and ws == 1 and not args.no_e2e:
+        cfg1 = MCTSConfig(num_simulations=args.sims, max_wave_size=args.wave, c_puct=1.4, virtual_loss=1.0,
+                          initial_tree_nodes=args.capacity, device=str(dev), enable_subtree_reuse=False,
+                          dirichlet_epsilon=0.0)
+        m1 = MCTS(cfg1, ev)
+        host_roots = roots.cpu().numpy()
+        for i in range(3):
+            m1.search(host_roots[i])
+        torch.cuda.synchronize()
+        n1 = min(R, 32)
+        s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s3.record()
+        for i in range(n1):
+            p1 = m1.search(host_roots[i])
+        e3.record()
+        torch.cuda.synchronize()
+        assert np.isclose(p1.sum(), 1.0)
+        ms1 = s3.elapsed_time(e3) / n1
+        single = {"ms_per_search": ms1, "value": args.sims / (ms1 / 1000.0), "unit": UNIT, "searches": n1,
+                  "api": "MCTS(config, ResNetEvaluator).search(host board), one root per call"}
+        r = run_reference_script(args, "gpu", 10.0, timeout=600, extra=("--warmup", "2"))
+        ref_gpu = r if "unavailable" in r else {
+            "ms_per_search": r["ms_per_search"], "value": r["sims_per_s"], "unit": UNIT, "searches": r["searches"],
+            "wave_search": r["wave_search"], "cuda_kernels": r["cuda_kernels"],
+            "api": "unmodified reference MCTS(MCTSConfig(backend='gpu', device='cuda', wave_async_expansion=True), "
+                   "its ResNetEvaluator under fp16 autocast).search(board), one root per call, mcts_kernels.cu "
+                   "built for sm_100"}
+
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        rate, sims, secs, threads = cpu_search_rate(args, sd, args.cpu_seconds)
+        rate, sims, secs, threads, searches = cpu_search_rate(args, sd, args.cpu_seconds)
         cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{sims} simulations of config-1 searches in {secs:.1f} s (oracle C++ tree "
-                         f"+ fp32 torch CPU ResNet 10x128)"}
+               "sample": f"{searches} whole config-1 searches ({sims} simulations) of the bench's roots in "
+                         f"{secs:.1f} s (oracle C++ tree + fp32 torch CPU ResNet 10x128)"}
 
     if rank == 0:
         line = {
@@ -406,15 +499,12 @@ def run_b200(args):
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded roots, seeded He-init weights)",
-            "config": {"workload": WORKLOAD, "roots_per_gpu": R, "global_batch": R * ws,
-                       "sims": args.sims, "wave": args.wave, "capacity": args.capacity,
-                       "model": f"resnet{args.blocks}x{args.filters} (value fc {args.value_hidden})",
-                       "parallelism": f"dp{ws} (independent trees per GPU, weights NCCL-broadcast once)",
-                       "l2": "inputs larger than L2 (multi-GB activations per ResNet call)"},
+            "config": config1_config(args, ws),
             "leaf_evals_per_s": positions * ws / (ms_max / 1000.0),
             "max_tree_nodes": nodes,
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
             "gpu_launches": launches,
+            "single_root_search": single, "reference_cuda_same_box": ref_gpu,
         }
         print(json.dumps(line), flush=True)
     if ws > 1:
@@ -650,9 +740,9 @@ def run_b200_go(args, game="go"):
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        rate, sims, secs, threads = cpu_search_rate(args, sd, args.cpu_seconds, game)
+        rate, sims, secs, threads, searches = cpu_search_rate(args, sd, args.cpu_seconds, game)
         cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{sims} simulations of {args.workload} {game} searches in {secs:.1f} s (oracle "
+               "sample": f"{searches} whole searches ({sims} simulations) of {args.workload} {game} in {secs:.1f} s (oracle "
                          f"C++ tree with the {game} rules + fp32 torch CPU ResNet 20x256)"}
     if rank == 0:
         line = {

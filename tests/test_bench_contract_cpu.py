@@ -1,6 +1,7 @@
-"""bench.py's reference arm (the reference algorithm on the host cores) prints the JSON line the
-driver parses: the contract's keys, impl "reference", a cpu_baseline describing the run, and an
-e2e object with no host<->device traffic. Runs on the CPU in about ten seconds."""
+"""bench.py's reference arm (the reference's own search on the host cores) prints the JSON line the
+driver parses: the contract's keys, impl "reference", the B200 arm's config, a cpu_baseline
+describing the run, an e2e object with no host<->device traffic, and the labelled extra CPU
+baselines. Runs on the CPU in under a minute (short searches)."""
 import json
 import os
 import subprocess
@@ -11,7 +12,7 @@ REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def test_reference_arm_json_line():
     out = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference",
-                          "--steps", "1", "--warmup", "1", "--cpu-seconds", "2"],
+                          "--steps", "1", "--warmup", "1", "--cpu-seconds", "2", "--sims", "128", "--wave", "64"],
                          capture_output=True, text=True, timeout=600, cwd=REPO)
     assert out.returncode == 0, out.stderr[-2000:]
     line = json.loads(out.stdout.strip().splitlines()[-1])
@@ -26,3 +27,9 @@ def test_reference_arm_json_line():
     e2e = line["e2e"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
     assert e2e["unit"] == line["unit"] and e2e["value"] == line["value"]
+    # same config keys as the B200 arm's line
+    for k in ("roots_per_gpu", "global_batch", "sims", "wave", "capacity", "model", "parallelism"):
+        assert k in line["config"], k
+    if cb["kind"] == "reference":        # the staged reference ran: the port and Cython numbers beside it
+        assert line["baselines"]["oracle_port"]["kind"] == "port"
+        assert "reference_cython" in line["baselines"]
