@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extra-configs", action="store_true",
+                    help="config 1 only (by default the line also carries configs 2-4, one timed step each)")
     ap.add_argument("--workload", choices=["config1", "config2", "config3", "config4", "forward"], default="config1",
                     help="forward = ResNet leaf evaluations/s alone (--game, --batch, --blocks, --filters); "
                          "config2 = batched self-play: 512 games (sharded), 800 sims, wave 64, 20x256; "
@@ -433,7 +435,7 @@ def run_b200(args):
                 "avg_launch_ms": avg_launch_s * 1e3, "launches": conv_launches}
 
     # end to end through the public API: host boards (pinned) in, host policies out
-    e2e = None
+    e2e, mcts, m1 = None, None, None
     if not args.no_e2e:
         cfg = MCTSConfig(num_simulations=args.sims, max_wave_size=args.wave, c_puct=1.4,
                          virtual_loss=1.0, initial_tree_nodes=args.capacity, device=str(dev),
@@ -478,7 +480,9 @@ def run_b200(args):
         ms1 = s3.elapsed_time(e3) / n1
         single = {"ms_per_search": ms1, "value": args.sims / (ms1 / 1000.0), "unit": UNIT, "searches": n1,
                   "api": "MCTS(config, ResNetEvaluator).search(host board), one root per call"}
-        r = run_reference_script(args, "gpu", 10.0, timeout=600, extra=("--warmup", "2"))
+        # AsyncWaveSearch sizes its own waves (at least 1024 simulations, async_wave_search.py:449-459)
+        # and so allocates more nodes than the requested simulations need: 1M-node trees
+        r = run_reference_script(args, "gpu", 10.0, timeout=600, extra=("--warmup", "2", "--capacity", "1000000"))
         ref_gpu = r if "unavailable" in r else {
             "ms_per_search": r["ms_per_search"], "value": r["sims_per_s"], "unit": UNIT, "searches": r["searches"],
             "wave_search": r["wave_search"], "cuda_kernels": r["cuda_kernels"],
@@ -493,6 +497,22 @@ def run_b200(args):
                "sample": f"{searches} whole config-1 searches ({sims} simulations) of the bench's roots in "
                          f"{secs:.1f} s (oracle C++ tree + fp32 torch CPU ResNet 10x128)"}
 
+    # configs 2-4 on the same GPUs: one warm-up and one timed step each, after config 1's
+    # buffers are freed (their own lines come from --workload config2|3|4)
+    extra = None
+    if not args.no_extra_configs:
+        for m in (mcts, m1):
+            if m is not None:
+                for e in m._engines.values():
+                    if e is not eng:
+                        e.close()
+                m._engines.clear()
+        ev.close()
+        eng.close()
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        extra = run_extra_configs(args)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
@@ -505,12 +525,39 @@ def run_b200(args):
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
             "gpu_launches": launches,
             "single_root_search": single, "reference_cuda_same_box": ref_gpu,
+            "other_configs": extra,
         }
         print(json.dumps(line), flush=True)
     if ws > 1:
         import torch.distributed as dist
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_extra_configs(args):
+    """Configs 2, 3 and 4 with one warm-up and one timed step each (the default bench line's
+    `other_configs`): the same code as --workload config2|config3|config4, without the e2e and
+    CPU legs. Runs on every rank (the timings are maxima over ranks)."""
+    import copy
+    out = {}
+    for name, fn in (("config2", lambda a: run_b200_selfplay(a, inner=True)),
+                     ("config3", lambda a: run_b200_go(a, "go", inner=True)),
+                     ("config4", lambda a: run_b200_go(a, "chess", inner=True))):
+        a = copy.copy(args)
+        a.workload, a.steps, a.warmup, a.no_e2e, a.no_cpu_baseline = name, 1, 1, True, True
+        a.roots = 256                       # the configs' own root counts are set by apply_config3/4
+        line = fn(a)
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        if line is None:
+            continue
+        rf = line.get("roofline") or {}
+        out[name] = {"value": line["value"], "unit": line["unit"], "ms_per_step": line["ms_per_step"],
+                     "steps": line["steps"], "warmup": line["warmup"], "scaling": line["scaling"],
+                     "config": line["config"], "leaf_evals_per_s": line.get("leaf_evals_per_s"),
+                     "roofline_frac": rf.get("frac"), "roofline_achieved_tflops": rf.get("achieved"),
+                     "clocks": line.get("clocks"), "gpu_launches": line.get("gpu_launches")}
+    return out
 
 
 def run_b200_synthetic(args):
@@ -556,7 +603,14 @@ def run_b200_synthetic(args):
         dist.destroy_process_group()
 
 
-def run_b200_selfplay(args):
+def init_dist(dev):
+    """One process group per run (NCCL over NVLink between the box's GPUs)."""
+    import torch.distributed as dist
+    if not dist.is_initialized():
+        dist.init_process_group("nccl", device_id=dev)
+
+
+def run_b200_selfplay(args, inner=False):
     """benchmark config 2: 512 concurrent self-play games sharded over the ranks (total fixed),
     800 simulations per move, max_wave_size 64 (leaf batches up to games x 64), ResNet 20 x 256
     bf16; one step = one move of every game (temperature-1 sampling from the visit policy)."""
@@ -567,8 +621,7 @@ def run_b200_selfplay(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if ws > 1:
-        import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=dev)
+        init_dist(dev)
     games_total, sims, wave = 512, 800, 64
     shard = parallel.shard_range(games_total, ws, rank)
     G = len(shard)
@@ -606,8 +659,7 @@ def run_b200_selfplay(args):
     avg_s = float(trunk_ms.sum()) / 1000.0 / max(1, launches)
     achieved = flops / max(1, launches) / avg_s / 1e12 if avg_s > 0 else 0.0
     peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
-    if rank == 0:
-        print(json.dumps({
+    line = {
             "metric": METRIC, "value": total_moves * sims / (ms / 1000.0), "unit": UNIT, "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
@@ -620,13 +672,19 @@ def run_b200_selfplay(args):
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_kind": f"bf16_tflops_sustained of {kind}", "traffic": traffic},
             "cpu_baseline": None, "e2e": None, "clocks": clk.summary(),
-            "gpu_launches": _lib.kernel_launches() - n0}), flush=True)
+            "gpu_launches": _lib.kernel_launches() - n0}
+    ev.close()
+    sp.close()
+    if inner:
+        return line
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if ws > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
 
 
-def run_b200_go(args, game="go"):
+def run_b200_go(args, game="go", inner=False):
     """Configs 3 and 4 on the device: Go roots (60 random legal moves each) or chess roots (10-40
     random plies), ResNet 20x256 evaluator."""
     ws, rank, local = dist_env()
@@ -635,8 +693,7 @@ def run_b200_go(args, game="go"):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if ws > 1:
-        import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=dev)
+        init_dist(dev)
     from omoknuni_quantum_b200 import _lib, parallel
     from omoknuni_quantum_b200 import go as gomod
     from omoknuni_quantum_b200.engine import WaveEngine
@@ -744,7 +801,8 @@ def run_b200_go(args, game="go"):
         cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
                "sample": f"{searches} whole searches ({sims} simulations) of {args.workload} {game} in {secs:.1f} s (oracle "
                          f"C++ tree with the {game} rules + fp32 torch CPU ResNet 20x256)"}
-    if rank == 0:
+    line = None
+    if rank == 0 or inner:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
@@ -761,6 +819,11 @@ def run_b200_go(args, game="go"):
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
             "gpu_launches": launches,
         }
+    ev.close()
+    eng.close()
+    if inner:
+        return line
+    if rank == 0:
         print(json.dumps(line), flush=True)
     if ws > 1:
         import torch.distributed as dist

@@ -247,6 +247,13 @@ class BatchedSelfPlay:
                                      c_puct=c_puct, device=device, game=game)
             self._engines: Dict[int, object] = {}
 
+    def close(self) -> None:
+        """Free the device engines (their trees); the evaluator belongs to the caller."""
+        for eng in getattr(self, "_engines", {}).values():
+            eng.close()
+        if hasattr(self, "_engines"):
+            self._engines.clear()
+
     # -- search ----------------------------------------------------------------------------
     @property
     def boards(self) -> np.ndarray:
