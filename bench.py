@@ -556,6 +556,7 @@ def run_extra_configs(args):
                      "steps": line["steps"], "warmup": line["warmup"], "scaling": line["scaling"],
                      "config": line["config"], "leaf_evals_per_s": line.get("leaf_evals_per_s"),
                      "roofline_frac": rf.get("frac"), "roofline_achieved_tflops": rf.get("achieved"),
+                     "moves_per_s": line.get("moves_per_s"),
                      "clocks": line.get("clocks"), "gpu_launches": line.get("gpu_launches")}
     return out
 
@@ -628,9 +629,10 @@ def run_b200_selfplay(args, inner=False):
     spec = ResNetSpec(num_blocks=20, filters=256, fc_value_hidden=128)
     sd = parallel.broadcast_state_dict(init_state_dict(spec, seed=args.seed), dev)
     ev = ResNetEvaluator(sd, max_batch=G * wave, device=dev)
+    # moves drawn and played on the device (omq_selfplay_move): no host round trip per move
     sp = BatchedSelfPlay(G, num_simulations=sims, wave_size=wave, evaluator=ev, capacity=200000,
                          temperature=1.0, temperature_threshold=30, seed=args.seed * 1000 + rank,
-                         device=dev)
+                         device=dev, sampling="device", max_moves=args.warmup + args.steps + 1)
     for _ in range(args.warmup):
         sp.step()
     torch.cuda.synchronize()
@@ -665,9 +667,11 @@ def run_b200_selfplay(args, inner=False):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (empty-board self-play, seeded sampling, seeded He-init weights)",
             "config": {"workload": "config2: batched Gomoku self-play, 512 games sharded across GPUs, "
-                                   "800 sims/move, wave 64, ResNet 20x256 bf16; step = one move of every game",
+                                   "800 sims/move, wave 64, ResNet 20x256 bf16; step = one move of every game, "
+                                   "drawn and played on the device",
                        "games_per_gpu": G, "global_batch": games_total, "parallelism": f"dp{ws}"},
             "leaf_evals_per_s": int(counts.sum()) * ws / (ms / 1000.0),
+            "moves_per_s": total_moves / (ms / 1000.0),
             "roofline": {"kernel": "k_conv3x3_pair<256> (cta_group::2 tcgen05 conv)", "bound": "tensor",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_kind": f"bf16_tflops_sustained of {kind}", "traffic": traffic},

@@ -232,6 +232,30 @@ OMQ_API int omq_export_tree(omq_engine* e, int32_t tree, int32_t count, int32_t*
                     float* d_value_sums, float* d_priors, int32_t* d_virtual_loss,
                     int32_t* d_parent, int32_t* d_action, uint8_t* d_terminal, void* stream);
 
+/* One self-play move of every game on the device (Gomoku), after a search of all the engine's
+ * trees, tree g = game g (SelfPlayGame.play_single_move, self_play_manager.py:218-370). */
+typedef struct {
+  int32_t move_number;            /* 0-based index of this move in every game */
+  int32_t max_moves;              /* history rows per game in the arrays below */
+  int32_t temperature_threshold;  /* sample while move_number < this, arg-max afterwards */
+  float temperature;              /* 1: sample in proportion to the visit counts; 0: arg-max */
+  int32_t enable_resign;
+  int32_t resign_min_move;        /* resignation only when move_number + 1 > this */
+  float resign_threshold;         /* the player who moved resigns when the root value < this */
+  uint64_t seed;                  /* draws: hash(seed, game, move), see selfplay.counter_draw */
+} omq_selfplay_step_config;
+/* For every live game g (d_game[8g] == 0): records the position (d_states_hist[g][move][C]),
+ * the root visit counts by action (d_visits_hist[g][move][A]) and the root value W/N
+ * (d_values_hist[g][move]); chooses the move (first action whose cumulative visit count exceeds
+ * floor(hash / 2^64 * total) while sampling; the first most-visited action otherwise), plays it on
+ * d_boards[g], writes it to d_moves_hist[g][move] and d_actions[g] (-1 for finished games, the
+ * input of omq_reroot for subtree reuse), and updates d_game[g][8] = {finished, winner (+1
+ * black, -1 white, 0 draw), resigned, error, moves played, 0, 0, 0}. No host synchronisation. */
+OMQ_API int omq_selfplay_move(omq_engine* e, const omq_selfplay_step_config* cfg, int8_t* d_boards,
+                              int32_t* d_game, int32_t* d_actions, int32_t* d_moves_hist,
+                              int32_t* d_visits_hist, float* d_values_hist, int8_t* d_states_hist,
+                              void* stream);
+
 
 /* ---------------------------------------------------------------------------------------------
  * ResNet policy/value evaluator (reference: ResNetModel, python/mcts/neural_networks/

@@ -64,6 +64,13 @@ class ResNetConfig(ctypes.Structure):
 OMQ_DTYPE_BF16, OMQ_DTYPE_F16 = 0, 1
 
 
+class SelfplayStepConfig(ctypes.Structure):
+    _fields_ = [("move_number", ctypes.c_int32), ("max_moves", ctypes.c_int32),
+                ("temperature_threshold", ctypes.c_int32), ("temperature", ctypes.c_float),
+                ("enable_resign", ctypes.c_int32), ("resign_min_move", ctypes.c_int32),
+                ("resign_threshold", ctypes.c_float), ("seed", ctypes.c_uint64)]
+
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int32
 
@@ -115,6 +122,7 @@ SIGNATURES = {
     "omq_abi_struct_sizes": [ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)],
     "omq_selftest_wait_timeout": [ctypes.c_uint64, _P, _P],
     "omq_selftest_prior_sum": [_P, _P, _I, _P, _P],
+    "omq_selfplay_move": [_P, ctypes.POINTER(SelfplayStepConfig), _P, _P, _P, _P, _P, _P, _P, _P],
     "omq_resnet_forward_noalloc": [ctypes.POINTER(ResNetConfig), _P, _P, _P, _P, _I, _P, _P, _P],
     "omq_resnet_noalloc_error": [_I, ctypes.POINTER(_I), _P],
 }

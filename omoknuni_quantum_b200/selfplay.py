@@ -12,8 +12,16 @@ each example gets the game outcome from its player's perspective (:388-420), and
 the reference's ``GameExample`` fields (python/mcts/neural_networks/replay_buffer.py:18-37).
 
 The searches of all live games run as one batch of independent trees in a ``WaveEngine``, so
-the leaf queue of every wave holds all games' leaves. Sampling and bookkeeping stay on the host
-with one seeded generator per game, so a run is reproducible.
+the leaf queue of every wave holds all games' leaves. Two ways to choose and play the moves:
+  * ``sampling="host"`` (every game type): bookkeeping on the host, one seeded numpy generator per
+    game (``rng="numpy"``), or the device's counter-based draws (``rng="counter"``, temperature 0
+    or 1) so that a host run replays a device run exactly;
+  * ``sampling="device"`` (Gomoku, temperature 0 or 1, the built-in engine): positions, histories
+    and game states stay in device memory, and one kernel per move (``omq_selfplay_move``)
+    records the examples, draws and plays the moves and applies the end and resignation rules,
+    so a move costs no host round trip beyond the search's status check. Tree g is game g for
+    the whole run (finished games get a one-node fresh tree each move); the trees are
+    independent, so results equal the host driver's, which searches only the live games.
 """
 from __future__ import annotations
 
@@ -23,6 +31,37 @@ from typing import Callable, Dict, List, Optional
 import numpy as np
 
 from .roots import has_five
+
+_MASK64 = (1 << 64) - 1
+
+
+def _mix64(x: int) -> int:
+    """SplitMix64 finaliser on Python ints (the device's mix64)."""
+    x &= _MASK64
+    x ^= x >> 30
+    x = (x * 0xBF58476D1CE4E5B9) & _MASK64
+    x ^= x >> 27
+    x = (x * 0x94D049BB133111EB) & _MASK64
+    x ^= x >> 31
+    return x
+
+
+def counter_draw(seed: int, game: int, move: int) -> int:
+    """The 64-bit draw of (seed, game, move) that omq_selfplay_move uses."""
+    return _mix64((_mix64((_mix64(seed) + game) & _MASK64) + move) & _MASK64)
+
+
+def counter_choice(visits: np.ndarray, draw: int) -> int:
+    """The action omq_selfplay_move samples from a visit-count row: the first action whose
+    cumulative count exceeds floor(draw / 2^64 * total) - visit-proportional sampling, i.e.
+    temperature 1 on policy = visits / total; uniform over all actions when total is 0 (the
+    uniform policy of an empty search)."""
+    v = np.asarray(visits, np.int64)
+    total = int(v.sum())
+    if total == 0:
+        return (draw * v.size) >> 64
+    target = (draw * total) >> 64
+    return int(np.searchsorted(np.cumsum(v), target, side="right"))
 
 
 @dataclass
@@ -213,9 +252,17 @@ class BatchedSelfPlay:
                  roots=None, board_size: int = 15,
                  search: Optional[Callable] = None, device=None, game: str = "gomoku",
                  subtree_reuse: str = "none", enable_resign: bool = True,
-                 resign_threshold: float = -0.98, resign_min_move: int = 10):
+                 resign_threshold: float = -0.98, resign_min_move: int = 10,
+                 sampling: str = "host", rng: str = "numpy", max_moves: int = 512):
         if game not in _GAMES:
             raise ValueError(f"unknown game {game!r}")
+        if sampling not in ("host", "device") or rng not in ("numpy", "counter"):
+            raise ValueError("sampling is 'host' or 'device', rng 'numpy' or 'counter'")
+        if (sampling == "device" or rng == "counter") and temperature not in (0.0, 1.0):
+            raise ValueError("counter-based draws take temperature 0 or 1")
+        if sampling == "device" and (game != "gomoku" or search is not None):
+            raise ValueError("device sampling runs Gomoku games on the built-in engine")
+        self.sampling, self.rng_kind, self.seed = sampling, rng, int(seed)
         if subtree_reuse not in ("none", "carry", "keep"):
             raise ValueError("subtree_reuse must be 'none', 'carry' or 'keep'")
         # between moves the played child seeds the next search of its game (omq_reroot): "keep"
@@ -246,6 +293,9 @@ class BatchedSelfPlay:
             self._engine_args = dict(board_size=self.n, capacity=capacity, max_wave_size=wave_size,
                                      c_puct=c_puct, device=device, game=game)
             self._engines: Dict[int, object] = {}
+        self._dev = None
+        if sampling == "device":
+            self._init_device(int(max_moves), device)
 
     def close(self) -> None:
         """Free the device engines (their trees); the evaluator belongs to the caller."""
@@ -253,6 +303,91 @@ class BatchedSelfPlay:
             eng.close()
         if hasattr(self, "_engines"):
             self._engines.clear()
+        self._dev = None
+
+    # -- device-resident games ---------------------------------------------------------------
+    def _init_device(self, max_moves: int, device) -> None:
+        import torch
+        from .engine import WaveEngine
+        eng = WaveEngine(self.G, **self._engine_args)
+        self._engines[("device", self.G)] = eng
+        dev = eng.device
+        G, C, A = self.G, self.n * self.n, self.n * self.n
+        self._dev = {
+            "engine": eng,
+            "boards": torch.from_numpy(np.stack(self.positions).astype(np.int8)).to(dev),
+            "game": torch.zeros(G, 8, dtype=torch.int32, device=dev),
+            "actions": torch.full((G,), -1, dtype=torch.int32, device=dev),
+            "moves": torch.full((G, max_moves), -1, dtype=torch.int32, device=dev),
+            "visits": torch.zeros(G, max_moves, A, dtype=torch.int32, device=dev),
+            "values": torch.zeros(G, max_moves, dtype=torch.float32, device=dev),
+            "states": torch.zeros(G, max_moves, C, dtype=torch.int8, device=dev),
+            "max_moves": max_moves, "synced": 0,
+        }
+        # games whose start position is already decided begin finished, as the host driver
+        # finds them when it checks the outcome (it never searches them)
+        for g, pos in enumerate(self.positions):
+            if self.game.outcome(pos) is not None:
+                res = self.game.outcome(pos)
+                self.records[g].finished, self.records[g].winner = True, res
+                self._dev["game"][g, 0] = 1
+                self._dev["game"][g, 1] = res
+
+    def _device_step(self) -> int:
+        import ctypes
+        from . import _lib
+        from .engine import _stream_ptr
+        d = self._dev
+        if self.move_number >= d["max_moves"]:
+            raise ValueError(f"max_moves ({d['max_moves']}) reached")
+        live = int((d["game"][:, 0] == 0).sum().item())
+        if live == 0:
+            return 0
+        eng = d["engine"]
+        # subtree reuse while the set of live games is unchanged, as the host driver has it
+        if self.subtree_reuse != "none" and self.move_number > 0 and live == d.get("live"):
+            eng.reroot(d["actions"], keep=self.subtree_reuse == "keep")
+        d["live"] = live
+        eng.search(d["boards"], self.sims, self._evaluator)
+        cfg = _lib.SelfplayStepConfig(self.move_number, d["max_moves"], self.temperature_threshold,
+                                      self.temperature, int(self.enable_resign), self.resign_min_move,
+                                      self.resign_threshold, self.seed & _MASK64)
+        p = lambda t: ctypes.c_void_p(t.data_ptr())
+        _lib.check(eng.L.omq_selfplay_move(eng._h, ctypes.byref(cfg), p(d["boards"]), p(d["game"]),
+                                           p(d["actions"]), p(d["moves"]), p(d["visits"]), p(d["values"]),
+                                           p(d["states"]), _stream_ptr()), "omq_selfplay_move")
+        self.move_number += 1
+        return live
+
+    def _sync_device(self) -> None:
+        """Copy the device histories of the moves played since the last sync into the records
+        and positions (examples as the host driver records them)."""
+        d = self._dev
+        if d is None or d["synced"] == self.move_number:
+            return
+        m0, m1 = d["synced"], self.move_number
+        game = d["game"].cpu().numpy()
+        if (game[:, 3] != 0).any():
+            raise RuntimeError("device self-play: an illegal move was drawn")
+        moves = d["moves"][:, m0:m1].cpu().numpy()
+        visits = d["visits"][:, m0:m1].cpu().numpy()
+        values = d["values"][:, m0:m1].cpu().numpy()
+        states = d["states"][:, m0:m1].cpu().numpy()
+        boards = d["boards"].cpu().numpy()
+        for g, rec in enumerate(self.records):
+            for m in range(m0, min(m1, int(game[g, 4]))):
+                k = m - m0
+                v = visits[g, k].astype(np.float64)
+                tot = v.sum()
+                st = states[g, k].reshape(self.n, self.n).copy()
+                rec.examples.append({"state": st, "policy": v / tot if tot > 0 else np.full(v.shape, 1.0 / v.size),
+                                     "player": self.game.player(st), "move_number": m,
+                                     "value_pred": float(values[g, k])})
+                rec.moves.append(int(moves[g, k]))
+            self.positions[g] = boards[g].reshape(self.n, self.n).copy()
+            if game[g, 0] and not rec.finished:
+                rec.finished, rec.winner, rec.resigned = True, int(game[g, 1]), bool(game[g, 2])
+        d["synced"] = m1
 
     # -- search ----------------------------------------------------------------------------
     @property
@@ -285,11 +420,14 @@ class BatchedSelfPlay:
         return eng.root_visits().cpu().numpy(), values
 
     def live(self) -> np.ndarray:
+        self._sync_device()
         return np.array([not r.finished for r in self.records])
 
     # -- one move of every live game ---------------------------------------------------------
     def step(self) -> int:
         """Play one move in every live game; returns the number of games that moved."""
+        if self._dev is not None:
+            return self._device_step()
         live = np.nonzero(self.live())[0]
         if len(live) == 0:
             return 0
@@ -317,9 +455,12 @@ class BatchedSelfPlay:
                                  "move_number": self.move_number,
                                  "value_pred": float(values[i])})
             if self.move_number < self.temperature_threshold and self.temperature > 0:
-                p = policy if self.temperature == 1.0 else np.power(policy, 1.0 / self.temperature)
-                p = p / p.sum()
-                action = int(self.rngs[g].choice(len(p), p=p))
+                if self.rng_kind == "counter":     # the device's draw (omq_selfplay_move)
+                    action = counter_choice(visits[i], counter_draw(self.seed, int(g), self.move_number))
+                else:
+                    p = policy if self.temperature == 1.0 else np.power(policy, 1.0 / self.temperature)
+                    p = p / p.sum()
+                    action = int(self.rngs[g].choice(len(p), p=p))
             else:
                 action = int(np.argmax(policy))
             self.positions[g] = self.game.apply(pos, action)
@@ -344,9 +485,11 @@ class BatchedSelfPlay:
         for _ in range(max_moves):
             if self.step() == 0:
                 break
+        self._sync_device()
         return self.records
 
     def examples(self) -> List[GameExample]:
+        self._sync_device()
         out: List[GameExample] = []
         for r in self.records:
             out.extend(r.training_examples())

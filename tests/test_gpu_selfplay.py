@@ -1,0 +1,53 @@
+"""Self-play with the moves drawn and played on the device (omq_selfplay_move): the same games as
+the host driver replaying the device's counter-based draws - moves, examples (position, visit
+policy, root value, player, move number), game ends, winners and resignations - for the built-in
+synthetic evaluator and the tensor-core ResNet, with and without subtree reuse."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _roots(G):
+    from omoknuni_quantum_b200.roots import random_roots
+    r = random_roots(77, G)
+    r[1] = 0
+    r[1, 7, 3:7] = 1                  # black to move with an open four
+    r[1, 2, 2] = r[1, 3, 10] = r[1, 11, 4] = r[1, 12, 12] = 2
+    return r
+
+
+def _play(sampling, evaluator, reuse, resign):
+    from omoknuni_quantum_b200.selfplay import BatchedSelfPlay
+    kw = dict(num_simulations=96, wave_size=32, capacity=60000, seed=11, temperature_threshold=4,
+              roots=_roots(6), subtree_reuse=reuse, evaluator=evaluator,
+              resign_threshold=resign, resign_min_move=2)
+    if sampling == "device":
+        sp = BatchedSelfPlay(6, sampling="device", max_moves=16, **kw)
+    else:
+        sp = BatchedSelfPlay(6, sampling="host", rng="counter", **kw)
+    recs = sp.play(7)
+    sp.close()
+    return recs
+
+
+@pytest.mark.parametrize("evaluator,reuse,resign", [("synthetic", "none", -0.98), ("synthetic", "keep", 0.05),
+                                                     ("resnet", "carry", -0.98)])
+def test_device_selfplay_equals_host_replay(evaluator, reuse, resign):
+    if evaluator == "resnet":
+        from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec
+        evaluator = ResNetEvaluator.random(ResNetSpec(num_blocks=2, filters=128), seed=2, max_batch=6 * 32)
+    dev = _play("device", evaluator, reuse, resign)
+    host = _play("host", evaluator, reuse, resign)
+    assert sum(len(r.moves) for r in dev) > 6
+    for a, b in zip(dev, host):
+        assert a.moves == b.moves
+        assert (a.finished, a.winner, a.resigned) == (b.finished, b.winner, b.resigned)
+        assert len(a.examples) == len(b.examples) == len(a.moves)
+        for x, y in zip(a.examples, b.examples):
+            assert np.array_equal(x["state"], y["state"])
+            assert np.array_equal(x["policy"], y["policy"])
+            assert x["player"] == y["player"] and x["move_number"] == y["move_number"]
+            assert np.float32(x["value_pred"]) == np.float32(y["value_pred"])
+    if resign > 0:
+        assert any(r.resigned for r in dev)

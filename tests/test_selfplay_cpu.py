@@ -178,3 +178,24 @@ def test_go_selfplay_engine_follows_the_rule_set(monkeypatch):
     sp2 = BatchedSelfPlay(2, num_simulations=8, game="go", board_size=9, roots=mixed)
     with pytest.raises(ValueError):
         sp2.step()
+
+
+def test_counter_draws_are_visit_proportional_and_replayed_by_the_host_driver():
+    """counter_choice (the device's draw, omq_selfplay_move) samples in proportion to the visit
+    counts, uniformly when nothing was visited, and the host driver with rng="counter" plays
+    exactly those draws."""
+    from omoknuni_quantum_b200.selfplay import counter_choice, counter_draw
+    visits = np.zeros(225, np.int64)
+    visits[[3, 40, 200]] = [10, 30, 60]
+    picks = np.bincount([counter_choice(visits, counter_draw(5, g, m)) for g in range(40) for m in range(250)],
+                        minlength=225)
+    assert picks.sum() == 10000 and set(np.nonzero(picks)[0]) == {3, 40, 200}
+    assert np.allclose(picks[[3, 40, 200]] / 10000, [0.1, 0.3, 0.6], atol=0.02)
+    assert 0 <= counter_choice(np.zeros(225, np.int64), counter_draw(1, 2, 3)) < 225
+    assert counter_draw(1, 2, 3) == counter_draw(1, 2, 3) != counter_draw(1, 2, 4)
+    sp = BatchedSelfPlay(3, search=_fake_search, temperature_threshold=3, seed=9, rng="counter")
+    recs = sp.play(5)
+    for g, r in enumerate(recs):
+        for m in range(3):
+            v = _fake_search(r.examples[m]["state"][None])[0]
+            assert r.moves[m] == counter_choice(v, counter_draw(9, g, m))
