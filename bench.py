@@ -426,8 +426,8 @@ def run_b200(args):
     traffic = None
     if traffic_per_pos is not None and conv_launches:
         traffic = traffic_per_pos * positions / len(trunk_ms)
-    roofline = {"kernel": ("k_conv3x3_halo_t (tcgen05 implicit-GEMM 3x3 conv, 128 ch x 256 px UMMAs over one halo load per channel block)"
-                          if args.filters == 128 else "k_conv3x3_pair<256> (tcgen05 cta_group::2 implicit-GEMM 3x3 conv)"),
+    roofline = {"kernel": "k_conv3x3_halo_t (tcgen05 implicit-GEMM 3x3 conv, 128 ch x 256 px UMMAs over one halo "
+                          "load per channel block)",
                 "bound": "tensor",
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_kind": f"bf16_tflops_sustained of {peak_kind}", "traffic": traffic,
@@ -672,7 +672,8 @@ def run_b200_selfplay(args, inner=False):
                        "games_per_gpu": G, "global_batch": games_total, "parallelism": f"dp{ws}"},
             "leaf_evals_per_s": int(counts.sum()) * ws / (ms / 1000.0),
             "moves_per_s": total_moves / (ms / 1000.0),
-            "roofline": {"kernel": "k_conv3x3_pair<256> (cta_group::2 tcgen05 conv)", "bound": "tensor",
+            "roofline": {"kernel": "k_conv3x3_halo_t (tcgen05 conv, two 128-channel halves of 256 filters)",
+                         "bound": "tensor",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_kind": f"bf16_tflops_sustained of {kind}", "traffic": traffic},
             "cpu_baseline": None, "e2e": None, "clocks": clk.summary(),
@@ -767,8 +768,8 @@ def run_b200_go(args, game="go", inner=False):
     # (profiles/conv3x3_pair256_resnet20x256.md), scaled by the positions a launch processes
     per_pos = profile_value("conv3x3_pair256_resnet20x256.md", f"dram_bytes_per_position_per_launch_{game}")
     traffic = per_pos * positions / len(trunk_ms) if per_pos is not None and len(trunk_ms) else None
-    roofline = {"kernel": f"k_conv3x3_pair<256> (tcgen05 cta_group::2 implicit-GEMM 3x3 conv, "
-                          f"{n_board + 1}x{n_board + 1} padded pixel grid)", "bound": "tensor", "achieved": achieved, "peak": peak,
+    roofline = {"kernel": f"k_conv3x3_halo_t (tcgen05 implicit-GEMM 3x3 conv, two 128-channel halves of 256 "
+                          f"filters, {n_board + 1}x{n_board + 1} padded pixel grid)", "bound": "tensor", "achieved": achieved, "peak": peak,
                 "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_kind": f"bf16_tflops_sustained of {peak_kind}", "traffic": traffic,
                 "algorithmic_flops_per_launch": flops / max(1, conv_launches),

@@ -3,20 +3,23 @@
 // ResNetEvaluator._forward_model, resnet_evaluator.py:231-265 -> policy = exp(log_softmax)).
 //
 // Trunk: every 3x3 convolution (BN folded into weight + bias) is one persistent implicit-GEMM
-// kernel on the 5th-generation tensor cores:
-//   M = positions x padded pixels, N = output channels, K = 9 taps x input channels.
+// kernel on the 5th-generation tensor cores, k_conv3x3_halo_t, in transposed form:
+//   M = 128 output channels (from the weights), N = 256 pixels, K = 9 taps x input channels;
+// with 256 filters every 256-pixel tile is two work items, one per half of the output channels.
 // Activations live in a padded pixel space: each position is a (S+1) x (S+1) grid whose last
 // row and last column are zero (S = board size). Flattened row-major, the grid makes every 3x3
 // tap a constant row shift (dy*(S+1) + dx) of the same matrix - the zero column serves as both
 // the left and the right border, and the zero row of position b as the top border of b+1 - so
-// each A tile is one plain 2D TMA box (rows before the tensor start read as zeros). For 15x15
-// Gomoku the padded grid is 16x16 = 256 rows = two 128-row tiles per position.
+// one TMA load per 64-channel block brings a tile's pixels plus a halo of rows on each side into
+// shared memory, and each tap's UMMA reads a row-shifted window of it (rows before the tensor
+// start read as zeros).
 // Warp roles per CTA: warp 0 TMA producer, warp 1 MMA issuer (single thread, tcgen05.mma with
-// both operands in 128B-swizzled shared memory), warps 2-5 epilogue (TMEM -> registers, + bias,
-// + residual, ReLU, zero the pad pixels, bf16 store). Accumulators are double-buffered in TMEM
-// so the epilogue of one tile overlaps the MMAs of the next.
-// Heads: 1x1 convolutions (2 policy + 1 value channel, BN folded) and the small FC layers run
-// as SIMT fp32 kernels over groups of positions.
+// both operands in 128B-swizzled shared memory), warps 2-9 epilogue (TMEM -> registers, + bias,
+// + residual, ReLU, zero the pad pixels, 16-bit TMA store). Accumulators are double-buffered in
+// TMEM so the epilogue of one tile overlaps the MMAs of the next.
+// Heads: 1x1 convolutions into 16-bit rows, then the fully connected layers on the tensor cores
+// (k_dense) with fused bias/ReLU, softmax or value dot + tanh; SIMT k_heads where the widths do
+// not fit the dense tiles and in the no-allocation entry point.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
@@ -31,7 +34,6 @@
 namespace omq {
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait before giving up
-constexpr int kTileM = 128;
 constexpr int kBlockK = 64;     // 64 bf16 = one 128-byte swizzle row
 constexpr int kInPad = 64;      // input planes padded to one K block (two for more than 64 planes)
 __host__ __device__ constexpr int in_pad_of(int planes) { return planes <= kInPad ? kInPad : 2 * kInPad; }
@@ -49,234 +51,12 @@ struct ConvArgs {
   int32_t kb_per_tap;
   int32_t relu;
   int32_t* error;
+  int32_t halves;  // transposed halo kernel: output channels / 128 (each work item is one half)
 };
 
-// CTA-pair variant (cta_group::2). A cluster of 2 CTAs computes 256-row tiles with one UMMA of
-// M = 256: each CTA stages its own 128 rows of A and half (BN/2 rows) of the weight tile, so a
-// K=16 step reads 4 KB + BN/2 * 32 B of shared memory per SM instead of 4 KB + BN * 32 B - the
-// shared-memory feed that limits the single-CTA N = 128 kernel. The leader (rank 0) issues the
-// MMAs; both CTAs' TMA loads complete on the leader's stage barrier; the leader's commits arrive
-// on both CTAs' barriers (one plain commit per CTA, no multicast); each CTA's epilogue drains its
-// own TMEM rows and arrives on the leader's accumulator-empty barrier.
-template <int BN>
-struct PairCfg {
-  static constexpr int kA = kTileM * kBlockK * 2;          // 16 KB
-  static constexpr int kB = (BN / 2) * kBlockK * 2;        // this CTA's half of the weights
-  static constexpr int kStage = kA + kB;
-  static constexpr int kStages = (196608 / kStage) < 8 ? (196608 / kStage) : 8;
-  static constexpr int kThreads = 192;                     // producer, MMA, 4 epilogue warps
-  static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kStaging = 4 * 2 * 2048;             // per epilogue warp: 2 x (32 x 64 B)
-  static constexpr int kStageBufs = 2;                       // epilogue staging buffers per warp
-  static constexpr int kSmem = kStages * kStage + kStaging + 1024 + 256 + BN * 4;
-  static_assert(kSmem <= 232448, "227 KB of shared memory per CTA");
-};
+constexpr int kHaloWStages = 4, kHaloEpiWarps = 8;
 
-template <int BN, bool F16>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::kThreads, 1)
-    k_conv3x3_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmO, ConvArgs args) {
-  using Cfg = PairCfg<BN>;
-  constexpr int kStages = Cfg::kStages;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  uint8_t* staging = smem + kStages * Cfg::kStage;
-  uint64_t* full = reinterpret_cast<uint64_t*>(staging + Cfg::kStaging);
-  uint64_t* empty = full + kStages;
-  uint64_t* tfull = empty + kStages;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* s_bias = reinterpret_cast<float*>(staging + Cfg::kStaging + 256);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = ptx::cluster_ctarank();
-  const int pair = (int)ptx::cluster_id_x(), npairs = (int)ptx::nclusters_x();
-  const int n_pos = args.d_count ? min(*args.d_count, args.count) : args.count;
-  const int rows = n_pos * args.P;
-  const int tiles = (rows + 2 * kTileM - 1) / (2 * kTileM);
-  const int KB = 9 * args.kb_per_tap;
-  const int rowstride = args.S + 1;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) { ptx::mbar_init(&full[s], 1); ptx::mbar_init(&empty[s], 1); }
-    for (int i = 0; i < 2; ++i) { ptx::mbar_init(&tfull[i], 1); ptx::mbar_init(&tempty[i], 8); }
-    ptx::mbar_init(drain, 1);
-    *abort_flag = 0;
-    ptx::fence_barrier_init();
-    ptx::prefetch_tmap(&tmA);
-    ptx::prefetch_tmap(&tmB);
-    ptx::prefetch_tmap(&tmO);
-  }
-  for (int i = threadIdx.x; i < BN; i += blockDim.x) s_bias[i] = args.bias[i];
-  ptx::cluster_sync();  // both CTAs' barriers exist before any remote arrive
-  if (warp == 1) {
-    ptx::tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
-    ptx::tmem_relinquish_pair();
-  }
-  ptx::tc_fence_before();
-  __syncthreads();
-  ptx::tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer (both CTAs) ----------------
-    int s = 0;
-    uint32_t ph = 0;
-    int issued[kStages];
-    for (int i = 0; i < kStages; ++i) issued[i] = -1;
-    for (int tile = pair; tile < tiles && !*abort_flag; tile += npairs) {
-      const int m0 = tile * 2 * kTileM + (int)rank * kTileM;
-      for (int kb = 0; kb < KB; ++kb) {
-        if (!ptx::mbar_wait(&empty[s], ph ^ 1, abort_flag, kWaitLimitNs)) goto producer_done;
-        const int tap = kb / args.kb_per_tap, cb = kb - tap * args.kb_per_tap;
-        const int dy = tap / 3 - 1, dx = tap % 3 - 1;
-        const uint32_t bar = ptx::mapa(ptx::smem_u32(&full[s]), 0);
-        if (rank == 0) ptx::mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStage);
-        ptx::tma_load_2d_pair(smem + s * Cfg::kStage, &tmA, bar, cb * kBlockK, m0 + dy * rowstride + dx);
-        ptx::tma_load_2d_pair(smem + s * Cfg::kStage + Cfg::kA, &tmB, bar, kb * kBlockK,
-                              (int)rank * (BN / 2));
-        issued[s] = (int)ph;
-        if (++s == kStages) { s = 0; ph ^= 1; }
-      }
-    }
-  producer_done:
-    // the leader waits (bounded) until every issued stage has landed before it may leave
-    if (rank == 0)
-      for (int i = 0; i < kStages; ++i)
-        if (issued[i] >= 0) {
-          volatile int dummy = 0;
-          ptx::mbar_wait(&full[i], (uint32_t)issued[i], &dummy, kWaitLimitNs);
-        }
-  } else if (warp == 1 && lane == 0 && rank == 0) {
-    // ---------------- MMA issuer (leader only) ----------------
-    constexpr uint32_t idesc = ptx::idesc_f16_f32(2 * kTileM, BN, F16);
-    int s = 0;
-    uint32_t ph = 0;
-    bool any = false;
-    int t = 0;
-    for (int tile = pair; tile < tiles; tile += npairs, ++t) {
-      const int ab = t & 1;
-      const uint32_t aph = (t >> 1) & 1;
-      if (!ptx::mbar_wait_cluster(&tempty[ab], aph ^ 1, abort_flag, kWaitLimitNs)) break;
-      ptx::tc_fence_after();
-      const uint32_t d = tmem + ab * BN;
-      bool ok = true;
-      for (int kb = 0; kb < KB; ++kb) {
-        if (!ptx::mbar_wait(&full[s], ph, abort_flag, kWaitLimitNs)) { ok = false; break; }
-        ptx::tc_fence_after();
-        const uint32_t a_addr = ptx::smem_u32(smem + s * Cfg::kStage);
-        const uint32_t b_addr = a_addr + Cfg::kA;
-#pragma unroll
-        for (int k = 0; k < kBlockK / 16; ++k)
-          ptx::mma_bf16_pair(d, ptx::smem_desc_sw128(a_addr + k * 32),
-                             ptx::smem_desc_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
-        any = true;
-        const uint32_t e_local = ptx::smem_u32(&empty[s]);
-        ptx::mma_commit_pair(e_local);
-        ptx::mma_commit_pair(ptx::mapa(e_local, 1));
-        if (++s == kStages) { s = 0; ph ^= 1; }
-      }
-      if (!ok) break;
-      const uint32_t f_local = ptx::smem_u32(&tfull[ab]);
-      ptx::mma_commit_pair(f_local);
-      ptx::mma_commit_pair(ptx::mapa(f_local, 1));
-    }
-    if (any) {
-      ptx::mma_commit_pair(ptx::smem_u32(drain));
-      volatile int dummy = 0;
-      ptx::mbar_wait(drain, 0, &dummy, kWaitLimitNs);
-    }
-  } else if (warp >= 2) {
-    // ---------------- epilogue (both CTAs, own 128 rows; TMA-store staging as above) ---------
-    const int q = warp & 3;
-    const uint32_t tempty_leader0 = ptx::mapa(ptx::smem_u32(&tempty[0]), 0);
-    const uint32_t tempty_leader1 = ptx::mapa(ptx::smem_u32(&tempty[1]), 0);
-    uint8_t* my_stage = staging + (warp - 2) * Cfg::kStageBufs * 2048;
-    int buf = 0;
-    int t = 0;
-    for (int tile = pair; tile < tiles; tile += npairs, ++t) {
-      const int ab = t & 1;
-      const uint32_t aph = (t >> 1) & 1;
-      if (!ptx::mbar_wait(&tfull[ab], aph, abort_flag, kWaitLimitNs)) break;
-      ptx::tc_fence_after();
-      const int row0 = tile * 2 * kTileM + (int)rank * kTileM + q * 32;
-      const int m = row0 + lane;
-      const bool valid = m < rows;
-      const int pix = m % args.P;
-      const int y = pix / rowstride, x = pix - y * rowstride;
-      const bool pad = !valid || (y == args.S) || (x == args.S);
-      const h16* rrow = args.residual ? args.residual + (size_t)m * BN : nullptr;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + ab * BN + c0, r);
-        ptx::tmem_ld_wait();
-        uint4 packed[4];
-        uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
-        if (pad) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) pw[j] = 0u;
-        } else {
-          float res[32];
-          if (rrow) {
-            const uint4* rp = reinterpret_cast<const uint4*>(rrow + c0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint4 u = rp[j];
-              const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 f = unpack2_h16<F16>(uw[e]);
-                res[8 * j + 2 * e] = f.x;
-                res[8 * j + 2 * e + 1] = f.y;
-              }
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) res[j] = 0.0f;
-          }
-#pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            float v0 = __uint_as_float(r[j]) + s_bias[c0 + j] + res[j];
-            float v1 = __uint_as_float(r[j + 1]) + s_bias[c0 + j + 1] + res[j + 1];
-            if (args.relu) { v0 = fmaxf(v0, 0.0f); v1 = fmaxf(v1, 0.0f); }
-            pw[j / 2] = pack2_h16<F16>(v0, v1);
-          }
-        }
-        if (lane == 0) ptx::bulk_wait_read<1>();
-        __syncwarp();
-        uint8_t* sb = my_stage + buf * 2048;
-        const int sw = (lane >> 1) & 3;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(sb + lane * 64 + ((j ^ sw) * 16)) = packed[j];
-        ptx::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          ptx::tma_store_2d(&tmO, sb, c0, row0);
-          ptx::bulk_commit();
-        }
-        buf ^= 1;
-      }
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive_cluster(ab ? tempty_leader1 : tempty_leader0);
-    }
-    if (lane == 0) ptx::bulk_wait<0>();
-  }
-  __syncthreads();
-  ptx::cluster_sync();  // neither CTA leaves while the pair still reads its shared memory
-  if (warp == 1) {
-    ptx::tc_fence_after();
-    ptx::tmem_dealloc_pair(tmem, Cfg::kTmemCols);
-  }
-  if (threadIdx.x == 0 && *abort_flag) atomicExch(args.error, OMQ_TIMEOUT);
-}
-
-
-// Transposed halo variant for 128 filters: D[channel][pixel] = W[channel][K] . X[pixel][K]^T, so
+// Transposed halo kernel (128 and 256 filters): D[channel][pixel] = W[channel][K] . X[pixel][K]^T, so
 // each UMMA is M = 128 output channels x N = 256 pixels x K = 16. The pixel operand is the same
 // row-shifted window of the halo buffer as in k_conv3x3_halo (one 304-row TMA load per 64-channel
 // block). A 128 x 256 x 16 UMMA keeps the tensor pipe busy for 128 cycles, twice as long as a
@@ -285,7 +65,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::kThread
 // tensor pipe; with 128 x 256 x 16 none does). The epilogue receives channel-major accumulators
 // (TMEM lane = channel) and transposes them through a swizzled fp32 buffer per warp, so that each
 // lane then owns one pixel row: residual loads, padding and the TMA-store staging stay row-major.
-struct HaloTCfg {
+template <int WS, int EW>
+struct HaloTCfgT {
   static constexpr int kRows = 256;                          // pixels per tile (UMMA N)
   static constexpr int kLead = 24;                           // halo rows before the tile (>= S+2)
   static constexpr int kHaloRows = 304;
@@ -293,22 +74,24 @@ struct HaloTCfg {
   static constexpr int kX = kHaloRows * 128;                 // one 64-channel halo block, 38,912 B
   static constexpr int kXStages = 2;
   static constexpr int kW = 128 * 128;                       // one tap's weights (128 ch x 64 K), 16 KB
-  static constexpr int kWStages = 4;
-  static constexpr int kEpiWarps = 8;
+  static constexpr int kWStages = WS;                          // weight stages in flight
+  static constexpr int kEpiWarps = EW;                         // a multiple of 4 (TMEM lane quarters)
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr int kTmemCols = 512;                      // 2 buffers x 256 pixel columns
   static constexpr int kStagePerWarp = 2 * 2048 + 4096;      // 2 bf16 store buffers + fp32 transpose
   static constexpr int kStaging = kEpiWarps * kStagePerWarp;
-  static constexpr int kSmem = kXStages * kX + kWStages * kW + kStaging + 1024 + 512 + 128 * 4;
+  static constexpr int kSmem = kXStages * kX + kWStages * kW + kStaging + 1024 + 512 + 256 * 4;
   static_assert(kSmem <= 232448, "227 KB of shared memory per CTA");
+  static_assert(EW % 4 == 0, "epilogue warps cover the 4 TMEM lane quarters");
 };
+using HaloTCfg = HaloTCfgT<kHaloWStages, kHaloEpiWarps>;
 
 template <bool F16>
 __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
     k_conv3x3_halo_t(const __grid_constant__ CUtensorMap tmH, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmO, ConvArgs args) {
   using Cfg = HaloTCfg;
-  constexpr int BN = 128;  // output channels
+  constexpr int BN = 128;  // output channels of one work item (one half of 256 filters)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -330,6 +113,10 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
   const int n_pos = args.d_count ? min(*args.d_count, args.count) : args.count;
   const int rows = n_pos * args.P;
   const int tiles = (rows + Cfg::kRows - 1) / Cfg::kRows;
+  // work item w: pixel tile w / halves, output channels [128 * (w % halves), +128)
+  const int halves = args.halves;
+  const int items = tiles * halves;
+  const int cout = BN * halves;
   const int CB = args.kb_per_tap;
   const int rowstride = args.S + 1;
 
@@ -344,7 +131,7 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
     ptx::prefetch_tmap(&tmB);
     ptx::prefetch_tmap(&tmO);
   }
-  for (int i = threadIdx.x; i < BN; i += blockDim.x) s_bias[i] = args.bias[i];
+  for (int i = threadIdx.x; i < cout; i += blockDim.x) s_bias[i] = args.bias[i];
   if (warp == 1) {
     ptx::tmem_alloc(tmem_slot, Cfg::kTmemCols);
     ptx::tmem_relinquish();
@@ -361,7 +148,8 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
     int x_issued[Cfg::kXStages], w_issued[Cfg::kWStages];
     for (int i = 0; i < Cfg::kXStages; ++i) x_issued[i] = -1;
     for (int i = 0; i < Cfg::kWStages; ++i) w_issued[i] = -1;
-    for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+    for (int w = blockIdx.x; w < items && !*abort_flag; w += gridDim.x) {
+      const int tile = w / halves, half = w - tile * halves;
       const int h0 = tile * Cfg::kRows - Cfg::kLead;
       for (int cb = 0; cb < CB; ++cb) {
         if (!ptx::mbar_wait(&xempty[sx], px ^ 1, abort_flag, kWaitLimitNs)) goto producer_done;
@@ -374,7 +162,7 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
         for (int tap = 0; tap < 9; ++tap) {
           if (!ptx::mbar_wait(&wempty[sw], pw ^ 1, abort_flag, kWaitLimitNs)) goto producer_done;
           ptx::mbar_arrive_expect_tx(&wfull[sw], Cfg::kW);
-          ptx::tma_load_2d(w_ring + sw * Cfg::kW, &tmB, &wfull[sw], (tap * CB + cb) * kBlockK, 0);
+          ptx::tma_load_2d(w_ring + sw * Cfg::kW, &tmB, &wfull[sw], (tap * CB + cb) * kBlockK, half * BN);
           w_issued[sw] = (int)pw;
           if (++sw == Cfg::kWStages) { sw = 0; pw ^= 1; }
         }
@@ -404,7 +192,7 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
     uint32_t px = 0, pw = 0;
     bool any = false;
     int t = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+    for (int w = blockIdx.x; w < items; w += gridDim.x, ++t) {
       const int ab = t & 1;
       const uint32_t aph = (t >> 1) & 1;
       if (!ptx::mbar_wait(&tempty[ab], aph ^ 1, abort_flag, kWaitLimitNs)) break;
@@ -422,9 +210,9 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
           const int off = Cfg::kLead + (tap / 3 - 1) * rowstride + (tap % 3 - 1);
           const uint64_t xd = x_desc0 + (uint64_t)(off * 8);             // off rows of 128 B
           const uint64_t wd = w_desc0 + (uint64_t)(sw * (Cfg::kW >> 4));
-          ptx::mma_bf16(d, wd, xd, idesc, (cb | tap) != 0);
+          ptx::mma_f16(d, wd, xd, idesc, (cb | tap) != 0);
 #pragma unroll
-          for (int k = 1; k < kBlockK / 16; ++k) ptx::mma_bf16(d, wd + 2 * k, xd + 2 * k, idesc, 1u);
+          for (int k = 1; k < kBlockK / 16; ++k) ptx::mma_f16(d, wd + 2 * k, xd + 2 * k, idesc, 1u);
           any = true;
           ptx::mma_commit(&wempty[sw]);
           if (++sw == Cfg::kWStages) { sw = 0; pw ^= 1; }
@@ -449,16 +237,18 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
     const int wq = (warp - 2) >> 2;
     uint8_t* my_stage = staging + (warp - 2) * Cfg::kStagePerWarp;
     float* tr = reinterpret_cast<float*>(my_stage + 2 * 2048);  // [32 px][32 ch] fp32, swizzled
-    const float bias = s_bias[q * 32 + lane];
     int buf = 0;
     int t = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+    for (int w = blockIdx.x; w < items; w += gridDim.x, ++t) {
+      const int tile = w / halves, half = w - tile * halves;
+      const int ch0 = half * BN + q * 32;  // this warp's first output channel
+      const float bias = s_bias[ch0 + lane];
       const int ab = t & 1;
       const uint32_t aph = (t >> 1) & 1;
       if (!ptx::mbar_wait(&tfull[ab], aph, abort_flag, kWaitLimitNs)) break;
       ptx::tc_fence_after();
 #pragma unroll 1
-      for (int j = wq; j < Cfg::kRows / 32; j += 2) {
+      for (int j = wq; j < Cfg::kRows / 32; j += Cfg::kEpiWarps / 4) {
         uint32_t r[32];
         ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + ab * Cfg::kRows + j * 32, r);
         ptx::tmem_ld_wait();
@@ -488,7 +278,7 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
             v[4 * c4] = f.x; v[4 * c4 + 1] = f.y; v[4 * c4 + 2] = f.z; v[4 * c4 + 3] = f.w;
           }
           if (args.residual) {
-            const uint4* rp = reinterpret_cast<const uint4*>(args.residual + (size_t)m * BN + q * 32);
+            const uint4* rp = reinterpret_cast<const uint4*>(args.residual + (size_t)m * cout + ch0);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const uint4 u = rp[i];
@@ -518,7 +308,7 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
         ptx::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          ptx::tma_store_2d(&tmO, sbuf, q * 32, row0);
+          ptx::tma_store_2d(&tmO, sbuf, ch0, row0);
           ptx::bulk_commit();
         }
         buf ^= 1;
@@ -654,7 +444,7 @@ __global__ void __launch_bounds__(kDenseThreads)
       const uint64_t ad = d0 + (uint64_t)(s * ((kA + kW) >> 4));
       const uint64_t wd = ad + (uint64_t)(kA >> 4);
 #pragma unroll
-      for (int k = 0; k < kBlockK / 16; ++k) ptx::mma_bf16(tmem, ad + 2 * k, wd + 2 * k, idesc, (kb | k) != 0);
+      for (int k = 0; k < kBlockK / 16; ++k) ptx::mma_f16(tmem, ad + 2 * k, wd + 2 * k, idesc, (kb | k) != 0);
       ptx::mma_commit(&empty[s]);
     }
     ptx::mma_commit(tfull);
@@ -1003,7 +793,6 @@ struct omq_resnet {
   int k1p, k3p, n1pad, n2pad, n3pad, nt3;  // padded K of fc1 policy / fc1 value, padded rows
   h16 *pin, *vin, *hid, *w1b, *w2b, *w3b;
   CUtensorMap tm_pin, tm_vin, tm_hid, tm_w1, tm_w2, tm_w3;
-  int pair;                // conv variant: 1 CTA pair (cta_group::2), 4 transposed halo
   bool f16;                // 16-bit storage is fp16 (OMQ_DTYPE_F16), else bf16
   // optional timing of the conv trunk of each forward call (CUDA events on the caller's stream)
   int prof_cap, prof_n;
@@ -1075,15 +864,12 @@ static int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t o
   return OMQ_OK;
 }
 
-// Conv kernel per filter count: 1 = CTA pair (256 filters), 4 = transposed halo (128 filters).
-static int conv_variant(int filters) { return filters == 256 ? 1 : 4; }
-
-// Tensor maps of a net's activation buffers and weights. Box heights follow the kernel variant:
-// A boxes are 128 rows (pair) or two 152-row halo boxes (transposed halo); weight boxes are the
-// CTA's half of the output channels (pair) or all of them.
+// Tensor maps of a net's activation buffers and weights: activation boxes are 152-row halves of a
+// tile's halo window, weight boxes 128 output channels (one work item's half of 256 filters, or all
+// of 128).
 static int build_maps(omq_resnet* n) {
-  const uint32_t a_rows = n->pair == 1 ? kTileM : HaloTCfg::kHaloBox;
-  const uint32_t b_rows = n->pair == 1 ? n->C / 2 : n->C;
+  const uint32_t a_rows = HaloTCfg::kHaloBox;
+  const uint32_t b_rows = 128;
   int st = make_map(&n->tmA_in, n->x_in, n->in_pad, n->rows, a_rows, n->f16);
   for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_map(&n->tmA[i], n->act[i], n->C, n->rows, a_rows, n->f16);
   for (int i = 0; st == OMQ_OK && i < 3; ++i) st = make_out_map(&n->tmO[i], n->act[i], n->C, n->rows, n->f16);
@@ -1212,7 +998,6 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
   // activations start zeroed so that never-written padding rows read as zeros
   cudaMemset(b + off[3], 0, tot - off[3]);
   n->tmB = new (std::nothrow) CUtensorMap[2 * n->NB + 1];
-  n->pair = conv_variant(n->C);
   int st = build_maps(n);
   if (st != OMQ_OK) {
     cudaFree(arena);
@@ -1300,37 +1085,18 @@ static int launch_conv_halo_tr(const omq_resnet* n, const CUtensorMap& tH, const
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, HaloTCfg::kSmem);
     if (e != cudaSuccess) return cuda_status(e, "transposed halo conv smem attribute");
   }
-  const int max_tiles = (int)((n->rows + HaloTCfg::kRows - 1) / HaloTCfg::kRows);
-  const int grid = max(1, min(max_tiles, n->sm_count));
+  const int max_items = (int)((n->rows + HaloTCfg::kRows - 1) / HaloTCfg::kRows) * a.halves;
+  const int grid = max(1, min(max_items, n->sm_count));
   count_launches(1);
   k_conv3x3_halo_t<F16><<<grid, HaloTCfg::kThreads, HaloTCfg::kSmem, s>>>(tH, tB, tO, a);
   return cuda_status(cudaGetLastError(), "k_conv3x3_halo_t");
-}
-
-template <int BN, bool F16>
-static int launch_conv_pair(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB,
-                            const CUtensorMap& tO, const ConvArgs& a, cudaStream_t s) {
-  using Cfg = PairCfg<BN>;
-  static std::atomic<uint64_t> attr_set{0};
-  {
-    const cudaError_t e = set_smem_attr_once(attr_set, k_conv3x3_pair<BN, F16>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
-    if (e != cudaSuccess) return cuda_status(e, "pair conv smem attribute");
-  }
-  const int max_tiles = (int)((n->rows + 2 * kTileM - 1) / (2 * kTileM));
-  const int pairs = max(1, min(max_tiles, n->sm_count / 2));
-  count_launches(1);
-  k_conv3x3_pair<BN, F16><<<2 * pairs, Cfg::kThreads, Cfg::kSmem, s>>>(tA, tB, tO, a);
-  return cuda_status(cudaGetLastError(), "k_conv3x3_pair");
 }
 
 static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tO,
                 const float* bias,
                 const h16* res, h16* out, int kb_per_tap, const int32_t* d_count,
                 int count, cudaStream_t s) {
-  const ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error};
-  if (n->pair == 1)
-    return n->f16 ? launch_conv_pair<256, true>(n, tA, tB, tO, a, s) : launch_conv_pair<256, false>(n, tA, tB, tO, a, s);
+  const ConvArgs a{bias, res, out, d_count, count, n->P, n->S, kb_per_tap, 1, n->error, n->C / 128};
   return n->f16 ? launch_conv_halo_tr<true>(n, tA, tB, tO, a, s) : launch_conv_halo_tr<false>(n, tA, tB, tO, a, s);
 }
 
@@ -1688,7 +1454,6 @@ extern "C" int omq_resnet_forward_noalloc(const omq_resnet_config* cfg, const ui
   n.error = reinterpret_cast<int32_t*>(base + kNoAllocErrorOffset);
   n.tmB = maps;
   n.loaded = 1;
-  n.pair = conv_variant(n.C);
   st = build_maps(&n);
   if (st) return st;
   // the error word keeps the previous call's value: clear it

@@ -40,18 +40,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   return ok != 0;
 }
 
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t phase) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(phase)
-      : "memory");
-  return ok != 0;
-}
-
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -66,23 +54,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, volatil
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, phase)) return true;
-    if ((i & 63) == 0) {
-      if (*abort) return false;
-      if (globaltimer() - t0 > limit_ns) {
-        *abort = 1;
-        return false;
-      }
-    }
-  }
-}
-
-// As mbar_wait, with cluster-scope acquire (for barriers that the peer CTA arrives on).
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t phase, volatile int* abort,
-                                                  uint64_t limit_ns) {
-  if (mbar_try_wait_cluster(bar, phase)) return true;
-  const uint64_t t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait_cluster(bar, phase)) return true;
     if ((i & 63) == 0) {
       if (*abort) return false;
       if (globaltimer() - t0 > limit_ns) {
@@ -126,8 +97,9 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T, bf16 inputs, fp32 accumulation.
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, 16-bit inputs (bf16 or fp16, as the instruction
+// descriptor says), fp32 accumulation.
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                          uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
@@ -194,74 +166,6 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool f16) {
          | ((uint32_t)(M >> 4) << 24);  // M / 16
 }
 
-
-// ---- CTA pairs (cta_group::2): one MMA over the two CTAs of a cluster of 2 --------------------
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t nclusters_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// Address of the same shared-memory variable in CTA `rank` of this cluster (shared::cluster).
-__device__ __forceinline__ uint32_t mapa(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
-}
-// 2D tiled TMA load into this CTA's shared memory whose completion is counted on an mbarrier
-// that may live in either CTA of the pair (no multicast).
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map,
-                                                 uint32_t bar_cluster_addr, int32_t x, int32_t y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster_addr)
-      : "memory");
-}
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                   smem_u32(dst_smem)), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-               : "memory");
-}
-// D[tmem of both CTAs] (+)= A (128 rows from each CTA) * B (N/2 rows from each CTA)^T.
-__device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                              uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrive once on the mbarrier at `bar_cluster_addr` (this CTA's or the peer's) when every pair
-// MMA issued so far by this thread has completed.
-__device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster_addr) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar_cluster_addr)
-               : "memory");
-}
 
 // ---- TMA stores ------------------------------------------------------------------------------
 __device__ __forceinline__ void fence_proxy_async_smem() {
