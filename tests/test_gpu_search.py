@@ -227,7 +227,9 @@ def test_cuda_graph_waves_equal_plain_waves():
             a, c = plain.export_tree(r), graph.export_tree(r)
             for k in ("parent", "action", "priors", "visits", "value_sums", "terminal"):
                 assert np.array_equal(a[k], c[k]), (sims, k)
-        assert n_graph == n_plain, (n_graph, n_plain)
+        # the one-call search (omq_search) reads the tree headers with one copy at its end; the
+        # host-sequenced graph path checks them with one k_status launch
+        assert n_graph == n_plain + 1, (n_graph, n_plain)
     assert len(graph._graphs) == 1
 
 
