@@ -656,7 +656,7 @@ def run_b200_selfplay(args, inner=False):
     launches = len(trunk_ms) * ev.conv_launches_per_call
     flops = int(counts.sum()) * ev.trunk_flops_per_position()
     # DRAM bytes per launch from the committed capture of this kernel on 15x15 boards
-    per_pos = profile_value("conv3x3_pair256_resnet20x256.md", "dram_bytes_per_position_per_launch_gomoku")
+    per_pos = profile_value("conv3x3_halot256_resnet20x256.md", "dram_bytes_per_position_per_launch_gomoku")
     traffic = per_pos * int(counts.sum()) / len(trunk_ms) if per_pos is not None and len(trunk_ms) else None
     avg_s = float(trunk_ms.sum()) / 1000.0 / max(1, launches)
     achieved = flops / max(1, launches) / avg_s / 1e12 if avg_s > 0 else 0.0
@@ -765,8 +765,8 @@ def run_b200_go(args, game="go", inner=False):
     achieved = (flops / max(1, conv_launches)) / avg_launch_s / 1e12 if avg_launch_s > 0 else 0.0
     peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
     # DRAM bytes per launch: the committed ncu capture of this kernel on the same board shape
-    # (profiles/conv3x3_pair256_resnet20x256.md), scaled by the positions a launch processes
-    per_pos = profile_value("conv3x3_pair256_resnet20x256.md", f"dram_bytes_per_position_per_launch_{game}")
+    # (profiles/conv3x3_halot256_resnet20x256.md), scaled by the positions a launch processes
+    per_pos = profile_value("conv3x3_halot256_resnet20x256.md", f"dram_bytes_per_position_per_launch_{game}")
     traffic = per_pos * positions / len(trunk_ms) if per_pos is not None and len(trunk_ms) else None
     roofline = {"kernel": f"k_conv3x3_halo_t (tcgen05 implicit-GEMM 3x3 conv, two 128-channel halves of 256 "
                           f"filters, {n_board + 1}x{n_board + 1} padded pixel grid)", "bound": "tensor", "achieved": achieved, "peak": peak,
