@@ -33,15 +33,10 @@ constexpr int kWarps = kThreads / 32;
 // five must contain the new stone. Lane y holds row y's stone mask; a cell completes a five in direction (dr, dc) when one
 // of the five windows of 5 cells containing it has its other 4 cells occupied by `p`. Row j of
 // a window comes from lane y + j*dr by shuffle, its column offset is a shift by j*dc.
-__device__ void warp_five_masks(const int8_t* b, int S, int p, uint32_t* fm) {
+// The board comes as bit rows: lane y holds `row` (the mover's stones of row y, bit x) and `occ`
+// (all stones of row y); lanes >= S hold zeros.
+__device__ void warp_five_masks(uint32_t row, uint32_t occ, int S, uint32_t* fm) {
   const int lane = threadIdx.x & 31;
-  uint32_t row = 0, occ = 0;
-  if (lane < S)
-    for (int x = 0; x < S; ++x) {
-      const int q = b[lane * S + x];
-      row |= (q == p ? 1u : 0u) << x;
-      occ |= (q != 0 ? 1u : 0u) << x;
-    }
   const uint32_t full = (1u << S) - 1u;
   uint32_t five = 0;
 #pragma unroll
@@ -56,14 +51,10 @@ __device__ void warp_five_masks(const int8_t* b, int S, int p, uint32_t* fm) {
       const int sh = j * dc;
       t[j + 4] = sh >= 0 ? (m >> sh) : ((m << -sh) & full);
     }
-#pragma unroll
-    for (int k = 0; k <= 4; ++k) {                  // window covering offsets -k .. 4-k
-      uint32_t w = full;
-#pragma unroll
-      for (int j = -4; j <= 4; ++j)
-        if (j != 0 && j >= -k && j <= 4 - k) w &= t[j + 4];
-      five |= w;
-    }
+    // a window covering offsets -k .. 4-k: stones at the k cells before and the 4-k cells after
+    const uint32_t l1 = t[3], l2 = l1 & t[2], l3 = l2 & t[1], l4 = l3 & t[0];
+    const uint32_t r1 = t[5], r2 = r1 & t[6], r3 = r2 & t[7], r4 = r3 & t[8];
+    five |= l4 | (l3 & r1) | (l2 & r2) | (l1 & r3) | r4;
   }
   // flat form: bit (y * S + x) % 32 of word (y * S + x) / 32, so a child's action indexes it
   // without a division by S
@@ -578,6 +569,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
       }
       const int cs = __shfl_sync(0xFFFFFFFFu, ptp.child_start, t);
       const int32_t np = __shfl_sync(0xFFFFFFFFu, pn, t);
+      unsigned long long lanebest = 0;
+      bool regbest = false;
       if (e.node == 0 && v.noise_eps > 0.0f) {
         // One Dirichlet(alpha) vector per wave at the root (wave_search.py:1160-1170): gamma draws
         // normalised in the engine's fixed summation order (lane-strided partials, butterfly).
@@ -608,26 +601,38 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
       } else {
         // children statistics: the first two per lane came with the prefetch, the rest four
         // independent 16-byte loads in flight per lane
+        // (one simulation at this parent: only the arg-max is needed, kept in registers)
         const NodeStats* cst = v.stats + base + cs;
         const float sq = parent_sqrt(np);
-        if (lane < n) keys[lane] = rank_key(ucb_score_sq(cur0, sq, v.c_puct, v.vl_value, v.enable_vl), lane);
+        auto put = [&](int j, unsigned long long key) {
+          if (e.k == 1) lanebest = key > lanebest ? key : lanebest;
+          else keys[j] = key;
+        };
+        if (lane < n) put(lane, rank_key(ucb_score_sq(cur0, sq, v.c_puct, v.vl_value, v.enable_vl), lane));
         if (lane + 32 < n)
-          keys[lane + 32] = rank_key(ucb_score_sq(cur1, sq, v.c_puct, v.vl_value, v.enable_vl), lane + 32);
+          put(lane + 32, rank_key(ucb_score_sq(cur1, sq, v.c_puct, v.vl_value, v.enable_vl), lane + 32));
         int j = lane + 64;
         for (; j + 96 < n; j += 128) {
           const NodeStats s0 = cst[j], s1 = cst[j + 32], s2 = cst[j + 64], s3 = cst[j + 96];
-          keys[j] = rank_key(ucb_score_sq(s0, sq, v.c_puct, v.vl_value, v.enable_vl), j);
-          keys[j + 32] = rank_key(ucb_score_sq(s1, sq, v.c_puct, v.vl_value, v.enable_vl), j + 32);
-          keys[j + 64] = rank_key(ucb_score_sq(s2, sq, v.c_puct, v.vl_value, v.enable_vl), j + 64);
-          keys[j + 96] = rank_key(ucb_score_sq(s3, sq, v.c_puct, v.vl_value, v.enable_vl), j + 96);
+          put(j, rank_key(ucb_score_sq(s0, sq, v.c_puct, v.vl_value, v.enable_vl), j));
+          put(j + 32, rank_key(ucb_score_sq(s1, sq, v.c_puct, v.vl_value, v.enable_vl), j + 32));
+          put(j + 64, rank_key(ucb_score_sq(s2, sq, v.c_puct, v.vl_value, v.enable_vl), j + 64));
+          put(j + 96, rank_key(ucb_score_sq(s3, sq, v.c_puct, v.vl_value, v.enable_vl), j + 96));
         }
         for (; j < n; j += 32) {
           const NodeStats st = cst[j];
-          keys[j] = rank_key(ucb_score_sq(st, sq, v.c_puct, v.vl_value, v.enable_vl), j);
+          put(j, rank_key(ucb_score_sq(st, sq, v.c_puct, v.vl_value, v.enable_vl), j));
         }
+        regbest = e.k == 1;
       }
       __syncwarp();
-      if (e.k <= n && e.k <= 8) {
+      if (regbest) {
+        const unsigned long long best = warp_max_u64(lanebest);
+        if (lane == 0)
+          emit_child(v, r, F[cur ^ 1], &sh.cnt[cur ^ 1], log, &sh.nlog, &sh.overflow, cs + key_slot(best),
+                     e.lo, 1, e.depth + 1);
+        __syncwarp();
+      } else if (e.k <= n && e.k <= 8) {
         // k best children, one simulation each, by repeated arg-max
         for (int rr = 0; rr < e.k; ++rr) {
           unsigned long long best = 0;
@@ -735,7 +740,6 @@ struct ExpandWarpSmem {
   int16_t acts[kMaxDepthCap];
   int16_t legal[kMaxCells + 1];
   float pv[kMaxCells + 1];
-  int8_t board[kMaxCells + 3];
 };
 
 // Sum of the legal-move policy pv[0..n) in exactly the order in which torch's CPU sum kernel adds
@@ -810,6 +814,32 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
 
   const bool go = v.game == OMQ_GAME_GO;
   const bool chs = v.game == OMQ_GAME_CHESS;
+  // Gomoku: the root position as bit rows per player and as a flat occupancy bit set (bit c % 32
+  // of word c / 32); a leaf's position is these plus the few stones of its path
+  __shared__ uint32_t s_rows[2][32];
+  __shared__ uint32_t s_occ[(kMaxCells + 31) / 32];
+  if (!go && !chs) {
+    const int8_t* rb = v.root_board + (size_t)r * v.C;
+    if (tid < 32) {
+      uint32_t p1 = 0, p2 = 0;
+      if (tid < v.S)
+        for (int x = 0; x < v.S; ++x) {
+          const int q = rb[tid * v.S + x];
+          p1 |= (q == 1 ? 1u : 0u) << x;
+          p2 |= (q == 2 ? 1u : 0u) << x;
+        }
+      s_rows[0][tid] = p1;
+      s_rows[1][tid] = p2;
+    } else if (tid < 32 + (kMaxCells + 31) / 32) {
+      const int w = tid - 32;
+      uint32_t o = 0;
+      for (int b = 0; b < 32; ++b) {
+        const int c = 32 * w + b;
+        if (c < v.C && rb[c] != 0) o |= 1u << b;
+      }
+      s_occ[w] = o;
+    }
+  }
   GoPos* gpos = reinterpret_cast<GoPos*>(expand_smem + (blockDim.x >> 5) * sizeof(ExpandWarpSmem));
   ChessWarpSmem* cws = reinterpret_cast<ChessWarpSmem*>(expand_smem + (blockDim.x >> 5) * sizeof(ExpandWarpSmem));
   if (chs) {
@@ -949,22 +979,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
       const int16_t* P = gpath + (size_t)i * kMaxDepthCap;
       const int d = P[kMaxDepthCap - 1];
       if (d < 0) { if (lane == 0) H->status = OMQ_BAD_ARG; continue; }
-      for (int c = lane; c < v.C; c += 32) W.board[c] = v.root_board[(size_t)r * v.C + c];
-      __syncwarp();
-      for (int j = lane; j < d; j += 32)
-        W.board[P[j]] = (int8_t)((j % 2 == 0) ? H->root_player : 3 - H->root_player);
-      __syncwarp();
+      // the leaf's position as bit rows (lane y) and flat occupancy words (lane w): the root's plus
+      // the path's stones, black and white alternating from the root's side to move
+      // (y = a / S by a multiply-shift: floor(a * (2^16 / S + 1) / 2^16) is exact for a < 361 and
+      // S <= 19, the error term a / 2^16 staying below 1 / S)
+      uint32_t p1 = s_rows[0][lane], p2 = s_rows[1][lane];
+      uint32_t occw = lane < (kMaxCells + 31) / 32 ? s_occ[lane] : 0u;
+      const uint32_t rdiv = 65536u / (uint32_t)v.S + 1u;
+      for (int j = 0; j < d; ++j) {
+        const int a = P[j];
+        const int y = (int)(((uint32_t)a * rdiv) >> 16), x = a - y * v.S;
+        const bool black = ((j % 2 == 0) ? H->root_player : 3 - H->root_player) == 1;
+        if (lane == y) { if (black) p1 |= 1u << x; else p2 |= 1u << x; }
+        if (lane == (a >> 5)) occw |= 1u << (a & 31);
+      }
       const int player = (d % 2 == 0) ? H->root_player : 3 - H->root_player;
       const int mc = H->root_mc + d;
-      warp_five_masks(W.board, v.S, player, W.five);
+      warp_five_masks(player == 1 ? p1 : p2, p1 | p2, v.S, W.five);
       const bool root_five = H->root_five != 0;
-      // legal actions in ascending order and their policy values
+      // legal actions in ascending order and their policy values: cell c = lane + 32 t is word t
+      // of the occupancy, bit lane
       int n = 0;
 #pragma unroll
       for (int t = 0; t < kChunks; ++t) {
         const int c = lane + 32 * t;
-        const bool legal = c < v.C && W.board[c] == 0;
-        const unsigned m = __ballot_sync(0xFFFFFFFFu, legal);
+        const int rem = v.C - 32 * t;
+        const uint32_t valid = rem >= 32 ? 0xFFFFFFFFu : (rem > 0 ? (1u << rem) - 1u : 0u);
+        const unsigned m = ~__shfl_sync(0xFFFFFFFFu, occw, t) & valid;
+        const bool legal = (m >> lane) & 1u;
         if (legal) {
           const int j = n + __popc(m & ((1u << lane) - 1));
           W.legal[j] = (int16_t)c;
