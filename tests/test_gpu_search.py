@@ -358,8 +358,8 @@ def test_device_prior_sum_is_torchs_order():
     assert not bad, bad[:10]
 
 
-@pytest.mark.parametrize("game", ["gomoku", "go", "chess"])
-def test_one_call_search_equals_stepwise_search(game):
+@pytest.mark.parametrize("game,dtype", [("gomoku", "bf16"), ("go", "bf16"), ("chess", "bf16"), ("gomoku", "fp16")])
+def test_one_call_search_equals_stepwise_search(game, dtype):
     """omq_search / omq_search_go / omq_search_chess (one C-ABI call: begin, root expansion and
     every wave with the tensor-core ResNet on the leaf queues) build the same trees as the same
     search sequenced step by step from the host (begin, root_expand, wave, ...)."""
@@ -386,7 +386,7 @@ def test_one_call_search_equals_stepwise_search(game):
         boards, meta = torch.from_numpy(random_roots(8, R)).cuda(), None
         spec = ResNetSpec(num_blocks=2, filters=128)
         n = 15
-    ev = ResNetEvaluator.random(spec, seed=4, max_batch=R * wave)
+    ev = ResNetEvaluator.random(spec, seed=4, max_batch=R * wave, dtype=dtype)
     engines = [WaveEngine(R, board_size=n, capacity=80000, max_wave_size=wave, game=game)
                for _ in range(2)]
     a, b = engines

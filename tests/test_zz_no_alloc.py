@@ -83,6 +83,32 @@ def test_noalloc_forward_matches_allocating_forward(game, filters):
     assert f"scratch limit of {limit}".encode() in L.omq_last_error()
 
 
+def test_noalloc_forward_in_fp16_matches_allocating_forward():
+    """The fixed-scratch forward with fp16 weights and activations (omq_resnet_config.dtype =
+    OMQ_DTYPE_F16) equals the allocating fp16 forward, on two calls in a row."""
+    from omoknuni_quantum_b200 import _lib
+    from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec, init_state_dict, pack_parameters
+    spec = ResNetSpec(num_blocks=2, filters=128, fc_value_hidden=128)
+    sd = init_state_dict(spec, seed=12)
+    ref = ResNetEvaluator(sd, max_batch=64, dtype="fp16")
+    L = _lib.load()
+    conv_w, conv_b, head = (t.cuda().contiguous() for t in pack_parameters(sd, spec, "fp16"))
+    dev = torch.cuda.current_device()
+    cfg = _lib.ResNetConfig(15, 19, spec.num_blocks, 128, 225, spec.fc_policy_hidden, spec.fc_value_hidden, 0, dev,
+                            _lib.OMQ_DTYPE_F16)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for n, seed in ((30, 4), (9, 5)):
+        x = _features(n, 15, 19, seed)
+        p = torch.full((n, 225), float("nan"), device="cuda")
+        v = torch.full((n,), float("nan"), device="cuda")
+        _lib.check(L.omq_resnet_forward_noalloc(ctypes.byref(cfg), ctypes.c_void_p(conv_w.data_ptr()),
+                                                ctypes.c_void_p(conv_b.data_ptr()), ctypes.c_void_p(head.data_ptr()),
+                                                ctypes.c_void_p(x.data_ptr()), n, ctypes.c_void_p(p.data_ptr()),
+                                                ctypes.c_void_p(v.data_ptr()), stream), "omq_resnet_forward_noalloc")
+        pr, vr = ref.evaluate_batch(x)
+        assert (p - pr).abs().max().item() < TOL and (v - vr).abs().max().item() < TOL
+
+
 def test_noalloc_rejects_a_device_that_does_not_exist():
     from omoknuni_quantum_b200 import _lib
     L = _lib.load()
