@@ -255,6 +255,17 @@ OMQ_API int omq_selfplay_move(omq_engine* e, const omq_selfplay_step_config* cfg
                               int32_t* d_game, int32_t* d_actions, int32_t* d_moves_hist,
                               int32_t* d_visits_hist, float* d_values_hist, int8_t* d_states_hist,
                               void* stream);
+/* The same step for chess engines, on the roots of omq_search_chess: d_records [G][1 + 100]
+ * 80-byte position records (the position, then the earlier ones, most recent first) and d_nprior
+ * int32 [G], both updated in place so that they are the next search's roots; d_states_hist
+ * [G][max_moves] records of the searched positions (8-byte aligned, as d_records). The move is
+ * played as ChessState::makeMove (chess_state.cpp:1232-1346) and the game ends as
+ * ChessState::getGameResult (chess_state.cpp:623-676); d_game[g][1] is +1 white, -1 black, 0
+ * draw. An action that is not a legal move ends the game with d_game[g][3] = OMQ_BAD_ARG. */
+OMQ_API int omq_selfplay_move_chess(omq_engine* e, const omq_selfplay_step_config* cfg, void* d_records,
+                                    int32_t* d_nprior, int32_t* d_game, int32_t* d_actions,
+                                    int32_t* d_moves_hist, int32_t* d_visits_hist, float* d_values_hist,
+                                    void* d_states_hist, void* stream);
 
 
 /* ---------------------------------------------------------------------------------------------

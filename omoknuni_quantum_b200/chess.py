@@ -382,6 +382,20 @@ class ChessPosition:
         return c
 
     # -- engine records ------------------------------------------------------------------------
+    @classmethod
+    def from_records(cls, records: np.ndarray, nprior: int) -> "ChessPosition":
+        """The position of engine root records (POS_DTYPE [1 + PRIOR], as ``root_records``
+        writes them) with ``nprior`` earlier positions; the inverse of ``root_records``."""
+        r = records[0]
+        c = cls.__new__(cls)
+        c.sq = [int(x) for x in r["sq"]]
+        c.side, c.castle, c.ep = int(r["side"]), int(r["castle"]), int(r["ep"])
+        c.halfmove, c.fullmove = int(r["halfmove"]), int(r["fullmove"])
+        c.c960, c.rook_file = bool(r["c960"]), [int(x) for x in r["rook_file"]]
+        c.reps = int(r["reps"])
+        c.prior = [np.array(records[1 + i]) for i in range(min(int(nprior), PRIOR))]
+        return c
+
     def root_records(self) -> np.ndarray:
         """POS_DTYPE [1 + PRIOR]: the position, then earlier positions (most recent first); the
         engine's root input together with ``len(self.prior)``."""

@@ -1,4 +1,4 @@
-// Self-play move step on the device (Gomoku): after a batched search of every game's position,
+// Self-play move step on the device (Gomoku and chess): after a batched search of every game's position,
 // one kernel records each live game's training example (position, root visit counts, root
 // value), chooses its move, plays it, and applies the game-end and resignation rules, without a
 // host round trip. It follows SelfPlayGame.play_single_move
@@ -12,6 +12,7 @@
 // (seed, game, move), so a run is reproducible and the host can replay it exactly
 // (omoknuni_quantum_b200.selfplay.counter_draw): the sampled action is the first one whose
 // cumulative visit count exceeds floor(u * total) with u = hash / 2^64, i.e. visit-proportional.
+#include "chess_device.cuh"
 #include "omq_internal.cuh"
 
 namespace omq {
@@ -45,56 +46,37 @@ __device__ bool block_has_five(const int8_t* b, int S, int* flag) {
   return *flag != 0;
 }
 
-// One block per game. game[g] = {finished, winner (+1 black, -1 white, 0 draw), resigned, error,
-// moves played, 0, 0, 0}.
-__global__ void __launch_bounds__(kSelfplayThreads) k_selfplay_move(EngineView v, omq_selfplay_step_config c,
-                                                                    int8_t* boards, int32_t* game,
-                                                                    int32_t* actions, int32_t* moves_hist,
-                                                                    int32_t* visits_hist, float* values_hist,
-                                                                    int8_t* states_hist) {
-  __shared__ int8_t board[kMaxCells];
-  __shared__ int s_total, s_action, s_flag, s_stones;
-  __shared__ int s_chunk[kSelfplayThreads];
-  const int g = blockIdx.x, tid = threadIdx.x;
-  int32_t* st = game + 8 * (size_t)g;
-  if (st[0]) {  // finished: no move, and the next search starts a fresh tree for it
-    if (tid == 0) actions[g] = -1;
-    return;
-  }
-  const int C = v.C, A = v.A, m = c.move_number;
-  const size_t slot = (size_t)g * c.max_moves + m;
-  int32_t* vis = visits_hist + slot * A;
+// Root visit counts of game g's search by action into vis[A] (zeroed first) and their total,
+// and the root value W / N from the side to move's perspective (MCTS._extract_policy,
+// mcts.py:1069; MCTS.get_root_value). Block-collective; *s_total must be 0 on entry.
+__device__ float block_root_visits(const EngineView& v, int g, int32_t* vis, int* s_total) {
+  const int tid = threadIdx.x;
   const size_t base = (size_t)g * v.T;
-  // position and root visit counts of this move's search (MCTS._extract_policy, mcts.py:1069)
-  if (tid == 0) { s_total = 0; s_stones = 0; }
-  for (int i = tid; i < C; i += blockDim.x) {
-    board[i] = boards[(size_t)g * C + i];
-    states_hist[slot * C + i] = board[i];
-  }
-  for (int a = tid; a < A; a += blockDim.x) vis[a] = 0;
+  for (int a = tid; a < v.A; a += blockDim.x) vis[a] = 0;
   __syncthreads();
   const NodeTopo rt = v.topo[base];
   const int n = topo_count(rt);
-  int local = 0, stones = 0;
+  int local = 0;
   for (int j = tid; j < n; j += blockDim.x) {
     const int32_t cnt = v.stats[base + rt.child_start + j].N;
     vis[topo_action(v.topo[base + rt.child_start + j])] = cnt;
     local += cnt;
   }
-  for (int i = tid; i < C; i += blockDim.x) stones += board[i] != 0;
-  atomicAdd(&s_total, local);
-  atomicAdd(&s_stones, stones);
-  __syncthreads();
-  const int total = s_total;
-  const int player = (s_stones % 2 == 0) ? 1 : 2;
-  // root value W / N from the side to move's perspective (MCTS.get_root_value)
+  atomicAdd(s_total, local);
   const NodeStats rs = v.stats[base];
-  const float value = rs.N > 0 ? __fdiv_rn(rs.W, __int2float_rn(rs.N)) : 0.0f;
-  // the move: sampled in proportion to the visits (temperature 1) or the first most-visited
+  return rs.N > 0 ? __fdiv_rn(rs.W, __int2float_rn(rs.N)) : 0.0f;
+}
+
+// The move of game g at move m (block-collective, after the visits are complete): sampled in
+// proportion to the visits (temperature 1, while m < temperature_threshold) or the first
+// most-visited action. s_chunk holds blockDim.x ints.
+__device__ int block_choose(const omq_selfplay_step_config& c, int g, int m, const int32_t* vis, int A,
+                            int total, int* s_chunk, int* s_action) {
+  const int tid = threadIdx.x;
   if (m < c.temperature_threshold && c.temperature > 0.0f) {
     const uint64_t h = selfplay_hash(c.seed, g, m);
     if (total == 0) {
-      if (tid == 0) s_action = (int)__umul64hi(h, (uint64_t)A);  // uniform policy
+      if (tid == 0) *s_action = (int)__umul64hi(h, (uint64_t)A);  // uniform policy
     } else {
       const int64_t target = (int64_t)__umul64hi(h, (uint64_t)total);  // in [0, total)
       // block-wide inclusive scan of the visits in action order, chunk by chunk
@@ -115,19 +97,62 @@ __global__ void __launch_bounds__(kSelfplayThreads) k_selfplay_move(EngineView v
           acc += vis[a];
           if (acc > target) break;
         }
-        s_action = a;
+        *s_action = a;
       }
     }
-  } else {
-    if (tid == 0) {
-      int best = 0, bv = vis[0];
-      for (int a = 1; a < A; ++a)
-        if (vis[a] > bv) { bv = vis[a]; best = a; }
-      s_action = best;
-    }
+  } else if (tid == 0) {
+    int best = 0, bv = vis[0];
+    for (int a = 1; a < A; ++a)
+      if (vis[a] > bv) { bv = vis[a]; best = a; }
+    *s_action = best;
   }
   __syncthreads();
-  const int action = s_action;
+  return *s_action;
+}
+
+// Resignation after the move (self_play_manager.py:350-365), also when the move ended the game
+// (it then decides the winner): the player who moved (1 first, 2 second) resigns.
+__device__ __forceinline__ void apply_resign(const omq_selfplay_step_config& c, int m, float value, int player,
+                                             int32_t* st) {
+  if (c.enable_resign && m + 1 > c.resign_min_move && (double)value < (double)c.resign_threshold) {
+    st[0] = 1;
+    st[2] = 1;
+    st[1] = player == 1 ? -1 : 1;
+  }
+}
+
+// One block per game. game[g] = {finished, winner (+1 black, -1 white, 0 draw), resigned, error,
+// moves played, 0, 0, 0}.
+__global__ void __launch_bounds__(kSelfplayThreads) k_selfplay_move(EngineView v, omq_selfplay_step_config c,
+                                                                    int8_t* boards, int32_t* game,
+                                                                    int32_t* actions, int32_t* moves_hist,
+                                                                    int32_t* visits_hist, float* values_hist,
+                                                                    int8_t* states_hist) {
+  __shared__ int8_t board[kMaxCells];
+  __shared__ int s_total, s_action, s_flag, s_stones;
+  __shared__ int s_chunk[kSelfplayThreads];
+  const int g = blockIdx.x, tid = threadIdx.x;
+  int32_t* st = game + 8 * (size_t)g;
+  if (st[0]) {  // finished: no move, and the next search starts a fresh tree for it
+    if (tid == 0) actions[g] = -1;
+    return;
+  }
+  const int C = v.C, A = v.A, m = c.move_number;
+  const size_t slot = (size_t)g * c.max_moves + m;
+  int32_t* vis = visits_hist + slot * A;
+  if (tid == 0) { s_total = 0; s_stones = 0; }
+  for (int i = tid; i < C; i += blockDim.x) {
+    board[i] = boards[(size_t)g * C + i];
+    states_hist[slot * C + i] = board[i];
+  }
+  __syncthreads();
+  const float value = block_root_visits(v, g, vis, &s_total);
+  int stones = 0;
+  for (int i = tid; i < C; i += blockDim.x) stones += board[i] != 0;
+  atomicAdd(&s_stones, stones);
+  __syncthreads();
+  const int player = (s_stones % 2 == 0) ? 1 : 2;
+  const int action = block_choose(c, g, m, vis, A, s_total, s_chunk, &s_action);
   if (action < 0 || action >= C || board[action] != 0) {  // an illegal move ends the game with an error
     if (tid == 0) { st[0] = 1; st[3] = OMQ_BAD_ARG; actions[g] = -1; }
     return;
@@ -143,12 +168,104 @@ __global__ void __launch_bounds__(kSelfplayThreads) k_selfplay_move(EngineView v
     st[4] = m + 1;
     if (five) { st[0] = 1; st[1] = player == 1 ? 1 : -1; }
     else if (s_stones + 1 >= C) { st[0] = 1; st[1] = 0; }
-    // resignation after the move, also when the move ended the game (it then decides the winner)
-    if (c.enable_resign && m + 1 > c.resign_min_move && (double)value < (double)c.resign_threshold) {
+    apply_resign(c, m, value, player, st);
+  }
+}
+
+// Chess: the same step on the engine's root records (records[g][1 + 100] position records, the
+// position then the earlier ones, most recent first; nprior[g] of them present). The move is
+// played as ChessPosition.play / ChessState::makeMove: the played position becomes the most
+// recent earlier one (the list keeps 100), and the new position's repetition count is 1 + the
+// earlier positions with the same piece placement (compared square by square). The game ends as
+// ChessState::getGameResult (chess_state.cpp:623-676): no legal move (mate: the side not to move
+// wins; stalemate: draw), insufficient material, halfmove clock >= 100 or a third occurrence
+// (draws). game[g] = {finished, winner (+1 white, -1 black, 0 draw), resigned, error, moves
+// played, 0, 0, 0}; states_hist[g][move] holds the 80-byte record of the searched position.
+__global__ void __launch_bounds__(kSelfplayThreads) k_selfplay_move_chess(
+    EngineView v, omq_selfplay_step_config c, ChessRec* records, int32_t* nprior, int32_t* game,
+    int32_t* actions, int32_t* moves_hist, int32_t* visits_hist, float* values_hist, ChessRec* states_hist) {
+  __shared__ ChessRec s_rec[1 + kChessPrior];
+  __shared__ ChessRec s_new;
+  __shared__ uint32_t s_mask[kChessMaskWords];
+  __shared__ ChessMoveList s_list;
+  __shared__ int s_total, s_action, s_reps, s_legal;
+  __shared__ int s_chunk[kSelfplayThreads];
+  const int g = blockIdx.x, tid = threadIdx.x;
+  int32_t* st = game + 8 * (size_t)g;
+  if (st[0]) {
+    if (tid == 0) actions[g] = -1;
+    return;
+  }
+  const int A = v.A, m = c.move_number;
+  const size_t slot = (size_t)g * c.max_moves + m;
+  int32_t* vis = visits_hist + slot * A;
+  ChessRec* rec = records + (size_t)g * (1 + kChessPrior);
+  const int np = min(max(nprior[g], 0), kChessPrior);
+  // the records as 8-byte words (ChessRec is 8-byte aligned, 80 bytes)
+  constexpr int kW = (int)(sizeof(ChessRec) / 8);
+  for (int i = tid; i < (1 + np) * kW; i += blockDim.x)
+    reinterpret_cast<uint64_t*>(s_rec)[i] = reinterpret_cast<const uint64_t*>(rec)[i];
+  if (tid == 0) { s_total = 0; s_reps = 0; }
+  __syncthreads();
+  if (tid < kW) reinterpret_cast<uint64_t*>(states_hist + slot)[tid] = reinterpret_cast<const uint64_t*>(s_rec)[tid];
+  const float value = block_root_visits(v, g, vis, &s_total);
+  __syncthreads();
+  const int player = s_rec[0].side;
+  const int action = block_choose(c, g, m, vis, A, s_total, s_chunk, &s_action);
+  // the action must be a legal move of the position
+  if (tid < 32) warp_ch_legal(s_rec[0], s_mask, s_list);
+  __syncthreads();
+  const bool legal = action >= 0 && action < kChessActions && ((s_mask[action >> 5] >> (action & 31)) & 1u);
+  if (!legal) {
+    if (tid == 0) { st[0] = 1; st[3] = OMQ_BAD_ARG; actions[g] = -1; }
+    return;
+  }
+  if (tid == 0) {
+    s_new = s_rec[0];
+    ch_play(s_new, ch_move(s_rec[0], action));
+  }
+  __syncthreads();
+  // repetitions among the new list of earlier positions: the played one, then the old list
+  const int np2 = min(np + 1, kChessPrior);
+  int same = 0;
+  for (int i = tid; i < np2; i += blockDim.x) {
+    const uint64_t* a = reinterpret_cast<const uint64_t*>(s_rec[i].sq);
+    const uint64_t* b = reinterpret_cast<const uint64_t*>(s_new.sq);
+    bool eq = true;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) eq &= a[w] == b[w];
+    same += eq;
+  }
+  atomicAdd(&s_reps, same);
+  __syncthreads();
+  if (tid == 0) {
+    const int reps = 1 + s_reps;
+    s_new.reps = (int8_t)(reps < 127 ? reps : 127);
+  }
+  __syncthreads();
+  if (tid < 32) {
+    const int n = warp_ch_legal(s_new, s_mask, s_list);
+    if (tid == 0) s_legal = n;
+  }
+  __syncthreads();
+  // the shifted list: record i + 1 = old record i, record 0 = the new position
+  for (int i = tid; i < np2 * kW; i += blockDim.x)
+    reinterpret_cast<uint64_t*>(rec + 1)[i] = reinterpret_cast<const uint64_t*>(s_rec)[i];
+  if (tid < kW) reinterpret_cast<uint64_t*>(rec)[tid] = reinterpret_cast<const uint64_t*>(&s_new)[tid];
+  if (tid == 0) {
+    nprior[g] = np2;
+    actions[g] = action;
+    moves_hist[slot] = action;
+    values_hist[slot] = value;
+    st[4] = m + 1;
+    if (s_legal == 0) {
       st[0] = 1;
-      st[2] = 1;
-      st[1] = player == 1 ? -1 : 1;
+      st[1] = ch_in_check(s_new, s_new.side) ? (s_new.side == chess::WHITE ? -1 : 1) : 0;
+    } else if (ch_terminal(s_new, s_legal)) {
+      st[0] = 1;
+      st[1] = 0;
     }
+    apply_resign(c, m, value, player, st);
   }
 }
 
@@ -165,7 +282,7 @@ extern "C" int omq_selfplay_move(omq_engine* e, const omq_selfplay_step_config* 
     set_error("null argument");
     return OMQ_BAD_ARG;
   }
-  if (e->v.game != OMQ_GAME_GOMOKU) { set_error("device self-play moves are Gomoku only"); return OMQ_BAD_ARG; }
+  if (e->v.game != OMQ_GAME_GOMOKU) { set_error("omq_selfplay_move is for Gomoku engines (omq_selfplay_move_chess for chess)"); return OMQ_BAD_ARG; }
   const omq_selfplay_step_config c = *cfg;
   if (c.move_number < 0 || c.move_number >= c.max_moves || !(c.temperature == 0.0f || c.temperature == 1.0f)) {
     set_error("bad self-play step (move %d of %d, temperature %g: 0 or 1 on the device)", c.move_number,
@@ -177,4 +294,32 @@ extern "C" int omq_selfplay_move(omq_engine* e, const omq_selfplay_step_config* 
   k_selfplay_move<<<e->v.R, kSelfplayThreads, 0, (cudaStream_t)stream>>>(
       e->v, c, d_boards, d_game, d_actions, d_moves_hist, d_visits_hist, d_values_hist, d_states_hist);
   return cuda_status(cudaGetLastError(), "k_selfplay_move");
+}
+
+extern "C" int omq_selfplay_move_chess(omq_engine* e, const omq_selfplay_step_config* cfg, void* d_records,
+                                       int32_t* d_nprior, int32_t* d_game, int32_t* d_actions,
+                                       int32_t* d_moves_hist, int32_t* d_visits_hist, float* d_values_hist,
+                                       void* d_states_hist, void* stream) {
+  if (!e || !cfg || !d_records || !d_nprior || !d_game || !d_actions || !d_moves_hist || !d_visits_hist ||
+      !d_values_hist || !d_states_hist) {
+    set_error("null argument");
+    return OMQ_BAD_ARG;
+  }
+  if (e->v.game != OMQ_GAME_CHESS) { set_error("omq_selfplay_move_chess on a non-chess engine"); return OMQ_BAD_ARG; }
+  if ((reinterpret_cast<uintptr_t>(d_records) | reinterpret_cast<uintptr_t>(d_states_hist)) & 7) {
+    set_error("chess records must be 8-byte aligned");
+    return OMQ_BAD_ARG;
+  }
+  const omq_selfplay_step_config c = *cfg;
+  if (c.move_number < 0 || c.move_number >= c.max_moves || !(c.temperature == 0.0f || c.temperature == 1.0f)) {
+    set_error("bad self-play step (move %d of %d, temperature %g: 0 or 1 on the device)", c.move_number,
+              c.max_moves, (double)c.temperature);
+    return OMQ_BAD_ARG;
+  }
+  DeviceGuard g(e->cfg.device);
+  count_launches(1);
+  k_selfplay_move_chess<<<e->v.R, kSelfplayThreads, 0, (cudaStream_t)stream>>>(
+      e->v, c, reinterpret_cast<ChessRec*>(d_records), d_nprior, d_game, d_actions, d_moves_hist, d_visits_hist,
+      d_values_hist, reinterpret_cast<ChessRec*>(d_states_hist));
+  return cuda_status(cudaGetLastError(), "k_selfplay_move_chess");
 }

@@ -16,8 +16,9 @@ the leaf queue of every wave holds all games' leaves. Two ways to choose and pla
   * ``sampling="host"`` (every game type): bookkeeping on the host, one seeded numpy generator per
     game (``rng="numpy"``), or the device's counter-based draws (``rng="counter"``, temperature 0
     or 1) so that a host run replays a device run exactly;
-  * ``sampling="device"`` (Gomoku, temperature 0 or 1, the built-in engine): positions, histories
-    and game states stay in device memory, and one kernel per move (``omq_selfplay_move``)
+  * ``sampling="device"`` (Gomoku and chess, temperature 0 or 1, the built-in engine): positions
+    (boards, or the chess engine's root records), histories and game states stay in device
+    memory, and one kernel per move (``omq_selfplay_move`` / ``omq_selfplay_move_chess``)
     records the examples, draws and plays the moves and applies the end and resignation rules,
     so a move costs no host round trip beyond the search's status check. Tree g is game g for
     the whole run (finished games get a one-node fresh tree each move); the trees are
@@ -161,6 +162,19 @@ class _GomokuGame:
     def outcome(self, pos):
         return game_result(pos)
 
+    # device-resident games (omq_selfplay_move)
+    actions = property(lambda self: self.n * self.n)
+    state_bytes = property(lambda self: self.n * self.n)
+
+    def device_roots(self, positions):
+        return {"boards": np.stack(positions).astype(np.int8).reshape(len(positions), -1)}
+
+    def device_state(self, row):
+        return np.asarray(row, np.int8).reshape(self.n, self.n).copy()
+
+    def device_position(self, roots, g):
+        return roots["boards"][g].reshape(self.n, self.n).copy()
+
 
 class _GoGame:
     """Positions are GoPosition objects; the game ends with two passes, scored by area."""
@@ -232,6 +246,24 @@ class _ChessGame:
         r = pos.result()
         return None if r == 0 else {1: 1, 2: -1, 3: 0}[r]
 
+    # device-resident games (omq_selfplay_move_chess): the engine's root records
+    actions = 4672
+    state_bytes = 80
+
+    def device_roots(self, positions):
+        recs = np.stack([p.root_records() for p in positions])
+        return {"records": np.ascontiguousarray(recs).view(np.uint8).reshape(len(positions), -1),
+                "nprior": np.array([min(len(p.prior), 100) for p in positions], np.int32)}
+
+    def device_state(self, row):
+        from .chess import POS_DTYPE
+        return np.frombuffer(np.asarray(row, np.uint8).tobytes(), POS_DTYPE).reshape(()).copy()
+
+    def device_position(self, roots, g):
+        from .chess import POS_DTYPE, ChessPosition
+        recs = np.frombuffer(np.asarray(roots["records"][g], np.uint8).tobytes(), POS_DTYPE)
+        return ChessPosition.from_records(recs, int(roots["nprior"][g]))
+
 
 _GAMES = {"gomoku": _GomokuGame, "go": _GoGame, "chess": _ChessGame}
 
@@ -260,8 +292,8 @@ class BatchedSelfPlay:
             raise ValueError("sampling is 'host' or 'device', rng 'numpy' or 'counter'")
         if (sampling == "device" or rng == "counter") and temperature not in (0.0, 1.0):
             raise ValueError("counter-based draws take temperature 0 or 1")
-        if sampling == "device" and (game != "gomoku" or search is not None):
-            raise ValueError("device sampling runs Gomoku games on the built-in engine")
+        if sampling == "device" and (game not in ("gomoku", "chess") or search is not None):
+            raise ValueError("device sampling runs Gomoku and chess games on the built-in engine")
         self.sampling, self.rng_kind, self.seed = sampling, rng, int(seed)
         if subtree_reuse not in ("none", "carry", "keep"):
             raise ValueError("subtree_reuse must be 'none', 'carry' or 'keep'")
@@ -312,23 +344,23 @@ class BatchedSelfPlay:
         eng = WaveEngine(self.G, **self._engine_args)
         self._engines[("device", self.G)] = eng
         dev = eng.device
-        G, C, A = self.G, self.n * self.n, self.n * self.n
+        G, A = self.G, self.game.actions
+        roots = {k: torch.from_numpy(v).to(dev) for k, v in self.game.device_roots(self.positions).items()}
         self._dev = {
-            "engine": eng,
-            "boards": torch.from_numpy(np.stack(self.positions).astype(np.int8)).to(dev),
+            "engine": eng, "roots": roots,
             "game": torch.zeros(G, 8, dtype=torch.int32, device=dev),
             "actions": torch.full((G,), -1, dtype=torch.int32, device=dev),
             "moves": torch.full((G, max_moves), -1, dtype=torch.int32, device=dev),
             "visits": torch.zeros(G, max_moves, A, dtype=torch.int32, device=dev),
             "values": torch.zeros(G, max_moves, dtype=torch.float32, device=dev),
-            "states": torch.zeros(G, max_moves, C, dtype=torch.int8, device=dev),
+            "states": torch.zeros(G, max_moves, self.game.state_bytes, dtype=torch.uint8, device=dev),
             "max_moves": max_moves, "synced": 0,
         }
         # games whose start position is already decided begin finished, as the host driver
         # finds them when it checks the outcome (it never searches them)
         for g, pos in enumerate(self.positions):
-            if self.game.outcome(pos) is not None:
-                res = self.game.outcome(pos)
+            res = self.game.outcome(pos)
+            if res is not None:
                 self.records[g].finished, self.records[g].winner = True, res
                 self._dev["game"][g, 0] = 1
                 self._dev["game"][g, 1] = res
@@ -343,19 +375,25 @@ class BatchedSelfPlay:
         live = int((d["game"][:, 0] == 0).sum().item())
         if live == 0:
             return 0
-        eng = d["engine"]
+        eng, roots = d["engine"], d["roots"]
         # subtree reuse while the set of live games is unchanged, as the host driver has it
         if self.subtree_reuse != "none" and self.move_number > 0 and live == d.get("live"):
             eng.reroot(d["actions"], keep=self.subtree_reuse == "keep")
         d["live"] = live
-        eng.search(d["boards"], self.sims, self._evaluator)
         cfg = _lib.SelfplayStepConfig(self.move_number, d["max_moves"], self.temperature_threshold,
                                       self.temperature, int(self.enable_resign), self.resign_min_move,
                                       self.resign_threshold, self.seed & _MASK64)
         p = lambda t: ctypes.c_void_p(t.data_ptr())
-        _lib.check(eng.L.omq_selfplay_move(eng._h, ctypes.byref(cfg), p(d["boards"]), p(d["game"]),
-                                           p(d["actions"]), p(d["moves"]), p(d["visits"]), p(d["values"]),
-                                           p(d["states"]), _stream_ptr()), "omq_selfplay_move")
+        hist = (p(d["game"]), p(d["actions"]), p(d["moves"]), p(d["visits"]), p(d["values"]), p(d["states"]))
+        if self.game.name == "chess":
+            eng.search(roots["records"], self.sims, self._evaluator, meta=roots["nprior"])
+            _lib.check(eng.L.omq_selfplay_move_chess(eng._h, ctypes.byref(cfg), p(roots["records"]),
+                                                     p(roots["nprior"]), *hist, _stream_ptr()),
+                       "omq_selfplay_move_chess")
+        else:
+            eng.search(roots["boards"].view(self.G, self.n, self.n), self.sims, self._evaluator)
+            _lib.check(eng.L.omq_selfplay_move(eng._h, ctypes.byref(cfg), p(roots["boards"]), *hist, _stream_ptr()),
+                       "omq_selfplay_move")
         self.move_number += 1
         return live
 
@@ -373,21 +411,25 @@ class BatchedSelfPlay:
         visits = d["visits"][:, m0:m1].cpu().numpy()
         values = d["values"][:, m0:m1].cpu().numpy()
         states = d["states"][:, m0:m1].cpu().numpy()
-        boards = d["boards"].cpu().numpy()
+        roots = {k: v.cpu().numpy() for k, v in d["roots"].items()}
         for g, rec in enumerate(self.records):
             for m in range(m0, min(m1, int(game[g, 4]))):
                 k = m - m0
                 v = visits[g, k].astype(np.float64)
                 tot = v.sum()
-                st = states[g, k].reshape(self.n, self.n).copy()
+                st = self.game.device_state(states[g, k])
                 rec.examples.append({"state": st, "policy": v / tot if tot > 0 else np.full(v.shape, 1.0 / v.size),
-                                     "player": self.game.player(st), "move_number": m,
+                                     "player": self._state_player(st), "move_number": m,
                                      "value_pred": float(values[g, k])})
                 rec.moves.append(int(moves[g, k]))
-            self.positions[g] = boards[g].reshape(self.n, self.n).copy()
+            self.positions[g] = self.game.device_position(roots, g)
             if game[g, 0] and not rec.finished:
                 rec.finished, rec.winner, rec.resigned = True, int(game[g, 1]), bool(game[g, 2])
         d["synced"] = m1
+
+    def _state_player(self, st) -> int:
+        """The side to move of a recorded state (a board, or a chess record)."""
+        return int(st["side"]) if self.game.name == "chess" else self.game.player(st)
 
     # -- search ----------------------------------------------------------------------------
     @property

@@ -51,3 +51,48 @@ def test_device_selfplay_equals_host_replay(evaluator, reuse, resign):
             assert np.float32(x["value_pred"]) == np.float32(y["value_pred"])
     if resign > 0:
         assert any(r.resigned for r in dev)
+
+
+def _chess_roots():
+    from omoknuni_quantum_b200.chess import ChessPosition, random_position
+    r = [random_position(5 * 1_000_003 + i) for i in range(4)]
+    r.append(ChessPosition("8/8/8/4k3/8/8/8/R3K3 w - - 99 80"))    # every move ends it: fifty moves
+    r.append(ChessPosition("6k1/5ppp/8/8/8/8/5PPP/R5K1 w - - 0 30"))  # mate in one on the board
+    return r
+
+
+def _play_chess(sampling, reuse, resign):
+    from omoknuni_quantum_b200.selfplay import BatchedSelfPlay
+    kw = dict(num_simulations=64, wave_size=16, capacity=60000, seed=5, temperature_threshold=3,
+              roots=_chess_roots(), subtree_reuse=reuse, evaluator="synthetic", game="chess",
+              resign_threshold=resign, resign_min_move=2)
+    if sampling == "device":
+        sp = BatchedSelfPlay(6, sampling="device", max_moves=12, **kw)
+    else:
+        sp = BatchedSelfPlay(6, sampling="host", rng="counter", **kw)
+    recs = sp.play(6)
+    final = [p.root_records().tobytes() for p in sp.positions]
+    sp.close()
+    return recs, final
+
+
+@pytest.mark.parametrize("reuse,resign", [("none", -0.98), ("keep", 0.05)])
+def test_device_chess_selfplay_equals_host_replay(reuse, resign):
+    """Chess games played by omq_selfplay_move_chess equal the host driver's (the reference
+    engine's rules in chess.py): moves, examples (the 80-byte records), ends and the final root
+    records with their repetition counts and earlier positions."""
+    (dev, dfinal), (host, hfinal) = _play_chess("device", reuse, resign), _play_chess("host", reuse, resign)
+    assert sum(len(r.moves) for r in dev) > 6
+    assert dev[4].finished and dev[4].winner == 0 and len(dev[4].moves) == 1   # the fifty-move draw
+    for a, b in zip(dev, host):
+        assert a.moves == b.moves
+        assert (a.finished, a.winner, a.resigned) == (b.finished, b.winner, b.resigned)
+        assert len(a.examples) == len(b.examples) == len(a.moves)
+        for x, y in zip(a.examples, b.examples):
+            assert x["state"].tobytes() == y["state"].tobytes()
+            assert np.array_equal(x["policy"], y["policy"])
+            assert x["player"] == y["player"] and x["move_number"] == y["move_number"]
+            assert np.float32(x["value_pred"]) == np.float32(y["value_pred"])
+    assert dfinal == hfinal
+    if resign > 0:
+        assert any(r.resigned for r in dev)
