@@ -232,7 +232,7 @@ OMQ_API int omq_export_tree(omq_engine* e, int32_t tree, int32_t count, int32_t*
                     float* d_value_sums, float* d_priors, int32_t* d_virtual_loss,
                     int32_t* d_parent, int32_t* d_action, uint8_t* d_terminal, void* stream);
 
-/* One self-play move of every game on the device (Gomoku), after a search of all the engine's
+/* One self-play move of every game on the device (Gomoku; chess and Go below), after a search of all the engine's
  * trees, tree g = game g (SelfPlayGame.play_single_move, self_play_manager.py:218-370). */
 typedef struct {
   int32_t move_number;            /* 0-based index of this move in every game */
@@ -266,6 +266,21 @@ OMQ_API int omq_selfplay_move_chess(omq_engine* e, const omq_selfplay_step_confi
                                     int32_t* d_nprior, int32_t* d_game, int32_t* d_actions,
                                     int32_t* d_moves_hist, int32_t* d_visits_hist, float* d_values_hist,
                                     void* d_states_hist, void* stream);
+/* The same step for Go engines, on the roots of omq_search_go, updated in place as the next
+ * search's roots: d_history int8 [G][8][n][n], d_meta int32 [G][3] = {side to move, ko point,
+ * consecutive passes}, d_keys uint64 [G][OMQ_GO_MAX_KEYS] with d_nkeys int32 [G] the game's
+ * position keys in game order (a full list drops its oldest key). The move is played as
+ * GoState::makeMove (go_state.cpp:227-356; captures, ko point, superko refusal under the engine's
+ * go_superko, the repetition rule under go_cycle). Two consecutive passes end the game, scored
+ * by area (area_scoring = 1, Chinese) or by territory and prisoners (0, Japanese / Korean) with
+ * `komi` for white (go_rules.cpp:211-260, 343-380); a third repetition ends it with winner 0.
+ * d_game[g] = {finished, winner (+1 black, -1 white, 0), resigned, error, moves played, black's
+ * prisoners, white's prisoners, ended by repetition}; d_states_hist [G][max_moves][8][n][n]. */
+OMQ_API int omq_selfplay_move_go(omq_engine* e, const omq_selfplay_step_config* cfg, float komi,
+                                 int32_t area_scoring, int8_t* d_history, int32_t* d_meta, uint64_t* d_keys,
+                                 int32_t* d_nkeys, int32_t* d_game, int32_t* d_actions, int32_t* d_moves_hist,
+                                 int32_t* d_visits_hist, float* d_values_hist, int8_t* d_states_hist,
+                                 void* stream);
 
 
 /* ---------------------------------------------------------------------------------------------

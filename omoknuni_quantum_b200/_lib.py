@@ -124,6 +124,8 @@ SIGNATURES = {
     "omq_selftest_prior_sum": [_P, _P, _I, _P, _P],
     "omq_selfplay_move": [_P, ctypes.POINTER(SelfplayStepConfig), _P, _P, _P, _P, _P, _P, _P, _P],
     "omq_selfplay_move_chess": [_P, ctypes.POINTER(SelfplayStepConfig), _P, _P, _P, _P, _P, _P, _P, _P, _P],
+    "omq_selfplay_move_go": [_P, ctypes.POINTER(SelfplayStepConfig), ctypes.c_float, ctypes.c_int32, _P, _P, _P,
+                             _P, _P, _P, _P, _P, _P, _P, _P],
     "omq_resnet_forward_noalloc": [ctypes.POINTER(ResNetConfig), _P, _P, _P, _P, _I, _P, _P, _P],
     "omq_resnet_noalloc_error": [_I, ctypes.POINTER(_I), _P],
 }

@@ -1,4 +1,4 @@
-// Self-play move step on the device (Gomoku and chess): after a batched search of every game's position,
+// Self-play move step on the device (Gomoku, chess and Go): after a batched search of every game's position,
 // one kernel records each live game's training example (position, root visit counts, root
 // value), chooses its move, plays it, and applies the game-end and resignation rules, without a
 // host round trip. It follows SelfPlayGame.play_single_move
@@ -13,6 +13,7 @@
 // (omoknuni_quantum_b200.selfplay.counter_draw): the sampled action is the first one whose
 // cumulative visit count exceeds floor(u * total) with u = hash / 2^64, i.e. visit-proportional.
 #include "chess_device.cuh"
+#include "go_device.cuh"
 #include "omq_internal.cuh"
 
 namespace omq {
@@ -269,6 +270,187 @@ __global__ void __launch_bounds__(kSelfplayThreads) k_selfplay_move_chess(
   }
 }
 
+// Go: score of a finished game (GoRules::calculateScores / getTerritoryOwnership,
+// go_rules.cpp:211-260, 343-380): every empty region bordered by one colour only counts for that
+// colour; area scoring adds the stones on the board, territory scoring the prisoners; komi goes
+// to white. No stones are marked dead. Returns +1 (black wins), -1 (white wins) or 0.
+// Warp-collective; g.par / g.libs are used as the regions' union-find and border colours.
+__device__ int warp_go_winner(const int8_t* b, int S, GoScratch& g, bool area, int prisoners_b,
+                              int prisoners_w, float komi) {
+  const int lane = threadIdx.x & 31, C = S * S;
+  for (int c = lane; c < C; c += 32) { g.par[c] = c; g.libs[c] = 0; }
+  __syncwarp();
+  for (int c = lane; c < C; c += 32) {
+    if (b[c]) continue;
+    const int x = c % S;
+    if (x < S - 1 && !b[c + 1]) go_unite(g.par, c, c + 1);
+    if (c + S < C && !b[c + S]) go_unite(g.par, c, c + S);
+  }
+  __syncwarp();
+  for (int c = lane; c < C; c += 32)
+    if (!b[c]) g.par[c] = go_find(g.par, c);
+  __syncwarp();
+  int stones_b = 0, stones_w = 0;
+  for (int c = lane; c < C; c += 32) {
+    if (b[c]) { stones_b += b[c] == 1; stones_w += b[c] == 2; continue; }
+    int nb[4];
+    go_neighbours(c, S, nb);
+    int col = 0;
+    for (int k = 0; k < 4; ++k)
+      if (nb[k] >= 0 && b[nb[k]]) col |= b[nb[k]];
+    if (col) atomicOr(&g.libs[g.par[c]], col);
+  }
+  __syncwarp();
+  int terr_b = 0, terr_w = 0;
+  for (int c = lane; c < C; c += 32) {
+    if (b[c]) continue;
+    const int f = g.libs[g.par[c]];
+    terr_b += f == 1;
+    terr_w += f == 2;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    stones_b += __shfl_xor_sync(0xFFFFFFFFu, stones_b, o);
+    stones_w += __shfl_xor_sync(0xFFFFFFFFu, stones_w, o);
+    terr_b += __shfl_xor_sync(0xFFFFFFFFu, terr_b, o);
+    terr_w += __shfl_xor_sync(0xFFFFFFFFu, terr_w, o);
+  }
+  const double black = (double)((area ? stones_b : prisoners_b) + terr_b);
+  const double white = (double)((area ? stones_w : prisoners_w) + terr_w) + (double)komi;
+  return black > white ? 1 : (white > black ? -1 : 0);
+}
+
+// Go: the same step on the engine's Go roots, updated in place (GoState::makeMove,
+// go_state.cpp:227-356): hist[g][8][C] (the position, then the 7 before it), meta[g] = {side to
+// move, ko point, consecutive passes}, keys[g][OMQ_GO_MAX_KEYS] / nkeys[g] the game's position
+// keys in game order (after every non-pass move without the repetition rule - superko's
+// history; after every move, with the side to move, under the repetition rule). The game ends
+// after two consecutive passes (scored) or a third repetition (no result / draw: winner 0).
+// game[g] = {finished, winner (+1 black, -1 white, 0 draw), resigned, error, moves played,
+// black's prisoners, white's prisoners, repetition ended it}; states_hist[g][move] holds the
+// searched position's 8 history boards.
+__global__ void __launch_bounds__(kSelfplayThreads) k_selfplay_move_go(
+    EngineView v, omq_selfplay_step_config c, float komi, int area, int8_t* hist, int32_t* meta, uint64_t* keys,
+    int32_t* nkeys, int32_t* game, int32_t* actions, int32_t* moves_hist, int32_t* visits_hist,
+    float* values_hist, int8_t* states_hist) {
+  __shared__ int8_t s_hist[kGoHistory * kMaxCells];
+  __shared__ int8_t s_board[kMaxCells + 3];
+  __shared__ GoScratch s_g;
+  __shared__ uint32_t s_mask[kGoMaskWords + 4];
+  __shared__ uint64_t s_key;
+  __shared__ int s_total, s_action, s_ok, s_ko, s_passes, s_captured;
+  __shared__ int s_chunk[kSelfplayThreads];
+  const int g = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  int32_t* st = game + 8 * (size_t)g;
+  if (st[0]) {
+    if (tid == 0) actions[g] = -1;
+    return;
+  }
+  const int C = v.C, S = v.S, A = v.A, m = c.move_number;
+  const size_t slot = (size_t)g * c.max_moves + m;
+  int32_t* vis = visits_hist + slot * A;
+  int8_t* H = hist + (size_t)g * kGoHistory * C;
+  for (int i = tid; i < kGoHistory * C; i += blockDim.x) {
+    s_hist[i] = H[i];
+    states_hist[slot * kGoHistory * C + i] = s_hist[i];
+  }
+  if (tid == 0) s_total = 0;
+  __syncthreads();
+  const float value = block_root_visits(v, g, vis, &s_total);
+  __syncthreads();
+  const int player = meta[3 * g], ko0 = meta[3 * g + 1], passes0 = meta[3 * g + 2];
+  const int action = block_choose(c, g, m, vis, A, s_total, s_chunk, &s_action);
+  uint64_t* K = keys + (size_t)g * OMQ_GO_MAX_KEYS;
+  const int nk = min(max(nkeys[g], 0), OMQ_GO_MAX_KEYS);
+  if (tid < 32) {
+    // legality (GoState::isLegalMove): the basic rules, then positional superko
+    for (int i = lane; i < C; i += 32) s_board[i] = s_hist[i];
+    __syncwarp();
+    bool ok = action >= 0 && action <= C;
+    if (ok && action < C) {
+      warp_go_analyze(s_board, S, s_g);
+      warp_go_legal(s_board, S, player, ko0, s_g, s_mask);
+      ok = (s_mask[action >> 5] >> (action & 31)) & 1u;
+    }
+    int opp_before = 0;
+    for (int i = lane; i < C; i += 32) opp_before += s_board[i] == 3 - player;
+    for (int o = 16; o > 0; o >>= 1) opp_before += __shfl_xor_sync(0xFFFFFFFFu, opp_before, o);
+    int ko = ko0, passes = passes0;
+    if (ok) warp_go_play(s_board, S, player, action, s_g, ko, passes);
+    int opp_after = 0;
+    for (int i = lane; i < C; i += 32) opp_after += s_board[i] == 3 - player;
+    for (int o = 16; o > 0; o >>= 1) opp_after += __shfl_xor_sync(0xFFFFFFFFu, opp_after, o);
+    const uint64_t key = warp_go_board_key(s_board, C) ^ (ko >= 0 ? go_ko_key(ko) : 0ull);
+    if (ok && v.go_superko && action < C) {
+      bool seen = false;
+      for (int i = lane; i < nk; i += 32) seen |= K[i] == key;
+      ok = !__any_sync(0xFFFFFFFFu, seen);
+    }
+    if (lane == 0) {
+      s_ok = ok;
+      s_ko = ko;
+      s_passes = passes;
+      s_captured = opp_before - opp_after;
+      s_key = key;
+    }
+  }
+  __syncthreads();
+  if (!s_ok) {
+    if (tid == 0) { st[0] = 1; st[3] = OMQ_BAD_ARG; actions[g] = -1; }
+    return;
+  }
+  // the game's keys: superko history (non-pass moves) or the repetition rule's (every move)
+  const bool cycle = v.go_cycle != 0;
+  const bool add = cycle ? st[7] == 0 : action < C;
+  const uint64_t newkey = cycle ? (s_key ^ go_side_key(3 - player)) : s_key;
+  int nk2 = nk;
+  if (add) {
+    if (nk == OMQ_GO_MAX_KEYS) {  // full: keep the most recent keys
+      uint64_t tmp[(OMQ_GO_MAX_KEYS + kSelfplayThreads - 1) / kSelfplayThreads];
+      int j = 0;
+      for (int i = tid; i + 1 < nk; i += blockDim.x) tmp[j++] = K[i + 1];
+      __syncthreads();
+      j = 0;
+      for (int i = tid; i + 1 < nk; i += blockDim.x) K[i] = tmp[j++];
+      nk2 = nk - 1;
+    }
+    if (tid == 0) K[nk2] = newkey;
+    ++nk2;
+  }
+  __syncthreads();
+  int repeated = st[7];
+  if (cycle && add) {
+    int cnt = 0;
+    for (int i = tid; i < nk2; i += blockDim.x) cnt += K[i] == newkey;
+    if (tid == 0) s_total = 0;
+    __syncthreads();
+    atomicAdd(&s_total, cnt);
+    __syncthreads();
+    repeated = s_total >= 3;
+  }
+  // history: the new board first, the 7 most recent before it
+  for (int i = tid; i < (kGoHistory - 1) * C; i += blockDim.x) H[C + i] = s_hist[i];
+  for (int i = tid; i < C; i += blockDim.x) H[i] = s_board[i];
+  int winner = 0;
+  const bool over = s_passes >= 2 || repeated;
+  if (tid < 32 && over && !repeated)
+    winner = warp_go_winner(s_board, S, s_g, area != 0, st[5] + (player == 1 ? s_captured : 0),
+                            st[6] + (player == 2 ? s_captured : 0), komi);
+  if (tid == 0) {
+    nkeys[g] = nk2;
+    meta[3 * g] = 3 - player;
+    meta[3 * g + 1] = s_ko;
+    meta[3 * g + 2] = s_passes;
+    actions[g] = action;
+    moves_hist[slot] = action;
+    values_hist[slot] = value;
+    st[4] = m + 1;
+    st[player == 1 ? 5 : 6] += s_captured;
+    st[7] = repeated;
+    if (over) { st[0] = 1; st[1] = winner; }
+    apply_resign(c, m, value, player, st);
+  }
+}
+
 }  // namespace omq
 
 using namespace omq;
@@ -322,4 +504,29 @@ extern "C" int omq_selfplay_move_chess(omq_engine* e, const omq_selfplay_step_co
       e->v, c, reinterpret_cast<ChessRec*>(d_records), d_nprior, d_game, d_actions, d_moves_hist, d_visits_hist,
       d_values_hist, reinterpret_cast<ChessRec*>(d_states_hist));
   return cuda_status(cudaGetLastError(), "k_selfplay_move_chess");
+}
+
+extern "C" int omq_selfplay_move_go(omq_engine* e, const omq_selfplay_step_config* cfg, float komi,
+                                    int32_t area_scoring, int8_t* d_history, int32_t* d_meta, uint64_t* d_keys,
+                                    int32_t* d_nkeys, int32_t* d_game, int32_t* d_actions, int32_t* d_moves_hist,
+                                    int32_t* d_visits_hist, float* d_values_hist, int8_t* d_states_hist,
+                                    void* stream) {
+  if (!e || !cfg || !d_history || !d_meta || !d_keys || !d_nkeys || !d_game || !d_actions || !d_moves_hist ||
+      !d_visits_hist || !d_values_hist || !d_states_hist) {
+    set_error("null argument");
+    return OMQ_BAD_ARG;
+  }
+  if (e->v.game != OMQ_GAME_GO) { set_error("omq_selfplay_move_go on a non-Go engine"); return OMQ_BAD_ARG; }
+  const omq_selfplay_step_config c = *cfg;
+  if (c.move_number < 0 || c.move_number >= c.max_moves || !(c.temperature == 0.0f || c.temperature == 1.0f)) {
+    set_error("bad self-play step (move %d of %d, temperature %g: 0 or 1 on the device)", c.move_number,
+              c.max_moves, (double)c.temperature);
+    return OMQ_BAD_ARG;
+  }
+  DeviceGuard g(e->cfg.device);
+  count_launches(1);
+  k_selfplay_move_go<<<e->v.R, kSelfplayThreads, 0, (cudaStream_t)stream>>>(
+      e->v, c, komi, area_scoring, d_history, d_meta, d_keys, d_nkeys, d_game, d_actions, d_moves_hist,
+      d_visits_hist, d_values_hist, d_states_hist);
+  return cuda_status(cudaGetLastError(), "k_selfplay_move_go");
 }

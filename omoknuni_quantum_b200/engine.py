@@ -167,8 +167,16 @@ class WaveEngine:
     # -- search phases -------------------------------------------------------------------------
     def _go_keys(self, keys):
         """Per-root superko keys (a list of uint64 arrays, or None) -> device [R, 512] + counts;
-        a game with more keys keeps its most recent 512."""
+        a game with more keys keeps its most recent 512. A pair of device tensors (keys, counts)
+        in that layout is used as it is."""
         R = self.num_trees
+        if isinstance(keys, tuple) and len(keys) == 2 and torch.is_tensor(keys[0]):
+            # (int64 [R, GO_MAX_KEYS], int32 [R]) already on the device (device self-play)
+            k, cnt = keys
+            if tuple(k.shape) != (R, _lib.GO_MAX_KEYS) or k.dtype != torch.int64 or tuple(cnt.shape) != (R,) \
+                    or cnt.dtype != torch.int32 or not k.is_contiguous() or not cnt.is_contiguous():
+                raise ValueError(f"Go keys on the device must be int64 [{R}, {_lib.GO_MAX_KEYS}] and int32 [{R}]")
+            return k.to(self.device), cnt.to(self.device)
         k = torch.zeros(R, _lib.GO_MAX_KEYS, dtype=torch.int64)
         cnt = torch.zeros(R, dtype=torch.int32)
         if keys is not None:

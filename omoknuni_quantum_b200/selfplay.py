@@ -16,9 +16,10 @@ the leaf queue of every wave holds all games' leaves. Two ways to choose and pla
   * ``sampling="host"`` (every game type): bookkeeping on the host, one seeded numpy generator per
     game (``rng="numpy"``), or the device's counter-based draws (``rng="counter"``, temperature 0
     or 1) so that a host run replays a device run exactly;
-  * ``sampling="device"`` (Gomoku and chess, temperature 0 or 1, the built-in engine): positions
-    (boards, or the chess engine's root records), histories and game states stay in device
-    memory, and one kernel per move (``omq_selfplay_move`` / ``omq_selfplay_move_chess``)
+  * ``sampling="device"`` (every game, temperature 0 or 1, the built-in engine): positions (boards,
+    the chess engine's root records, or Go's history boards, side / ko / passes and position
+    keys), histories and game states stay in device memory, and one kernel per move
+    (``omq_selfplay_move``, ``omq_selfplay_move_chess``, ``omq_selfplay_move_go``)
     records the examples, draws and plays the moves and applies the end and resignation rules,
     so a move costs no host round trip beyond the search's status check. Tree g is game g for
     the whole run (finished games get a one-node fresh tree each move); the trees are
@@ -172,7 +173,7 @@ class _GomokuGame:
     def device_state(self, row):
         return np.asarray(row, np.int8).reshape(self.n, self.n).copy()
 
-    def device_position(self, roots, g):
+    def device_position(self, roots, g, start, game_row):
         return roots["boards"][g].reshape(self.n, self.n).copy()
 
 
@@ -211,8 +212,44 @@ class _GoGame:
         return q
 
     def outcome(self, pos):
+        # 4 is the Japanese rules' "no result" of a third repetition: no winner, as a draw
         r = pos.result()
-        return None if r == 0 else {1: 1, 2: -1, 3: 0}[r]
+        return None if r == 0 else {1: 1, 2: -1, 3: 0, 4: 0}[r]
+
+    # device-resident games (omq_selfplay_move_go): the engine's Go roots
+    actions = property(lambda self: self.n * self.n + 1)
+    state_bytes = property(lambda self: 8 * self.n * self.n)
+
+    def device_roots(self, positions):
+        from . import _lib
+        G, K = len(positions), _lib.GO_MAX_KEYS
+        keys = np.zeros((G, K), np.uint64)
+        nkeys = np.zeros(G, np.int32)
+        for g, p in enumerate(positions):
+            k = p.root_keys()
+            keys[g, :k.size] = k
+            nkeys[g] = k.size
+        return {"history": np.stack([p.history_planes() for p in positions]),
+                "meta": np.stack([p.meta() for p in positions]).astype(np.int32),
+                "keys": keys.view(np.int64), "nkeys": nkeys}
+
+    def device_game(self, pos):
+        """Columns 5-7 of the device game record: prisoners of black and white, repetition end."""
+        return [pos.prisoners[1], pos.prisoners[2], int(pos.repeated)]
+
+    def device_state(self, row):
+        return np.asarray(row, np.int8).reshape(8, self.n, self.n).copy()
+
+    def device_position(self, roots, g, start, game_row):
+        q = start.copy()
+        h = roots["history"][g].reshape(8, self.n, self.n)
+        q.board = h[0].copy()
+        q.history = [h[k].copy() for k in range(7, -1, -1)]
+        q.to_move, q.ko, q.passes = (int(x) for x in roots["meta"][g])
+        q.keys = [int(k) for k in roots["keys"][g][: int(roots["nkeys"][g])].view(np.uint64)]
+        q.prisoners = [0, int(game_row[5]), int(game_row[6])]
+        q.repeated = bool(game_row[7])
+        return q
 
 
 class _ChessGame:
@@ -259,7 +296,7 @@ class _ChessGame:
         from .chess import POS_DTYPE
         return np.frombuffer(np.asarray(row, np.uint8).tobytes(), POS_DTYPE).reshape(()).copy()
 
-    def device_position(self, roots, g):
+    def device_position(self, roots, g, start, game_row):
         from .chess import POS_DTYPE, ChessPosition
         recs = np.frombuffer(np.asarray(roots["records"][g], np.uint8).tobytes(), POS_DTYPE)
         return ChessPosition.from_records(recs, int(roots["nprior"][g]))
@@ -292,8 +329,8 @@ class BatchedSelfPlay:
             raise ValueError("sampling is 'host' or 'device', rng 'numpy' or 'counter'")
         if (sampling == "device" or rng == "counter") and temperature not in (0.0, 1.0):
             raise ValueError("counter-based draws take temperature 0 or 1")
-        if sampling == "device" and (game not in ("gomoku", "chess") or search is not None):
-            raise ValueError("device sampling runs Gomoku and chess games on the built-in engine")
+        if sampling == "device" and search is not None:
+            raise ValueError("device sampling runs the games on the built-in engine")
         self.sampling, self.rng_kind, self.seed = sampling, rng, int(seed)
         if subtree_reuse not in ("none", "carry", "keep"):
             raise ValueError("subtree_reuse must be 'none', 'carry' or 'keep'")
@@ -341,10 +378,21 @@ class BatchedSelfPlay:
     def _init_device(self, max_moves: int, device) -> None:
         import torch
         from .engine import WaveEngine
-        eng = WaveEngine(self.G, **self._engine_args)
+        args = dict(self._engine_args)
+        if self.game.name == "go":
+            from . import _lib
+            p0 = self.positions[0]
+            if any((p.rules, p.superko, p.komi) != (p0.rules, p0.superko, p0.komi) for p in self.positions):
+                raise ValueError("device Go self-play needs one rule set, superko setting and komi")
+            if max(len(p.keys) for p in self.positions) + max_moves > _lib.GO_MAX_KEYS:
+                raise ValueError(f"device Go self-play keeps {_lib.GO_MAX_KEYS} position keys per game: "
+                                 "the roots' keys plus max_moves must fit")
+            args.update(go_rules=p0.rules, go_superko=p0.superko)
+        eng = WaveEngine(self.G, **args)
         self._engines[("device", self.G)] = eng
         dev = eng.device
         G, A = self.G, self.game.actions
+        self._start = [p.copy() for p in self.positions]
         roots = {k: torch.from_numpy(v).to(dev) for k, v in self.game.device_roots(self.positions).items()}
         self._dev = {
             "engine": eng, "roots": roots,
@@ -364,6 +412,8 @@ class BatchedSelfPlay:
                 self.records[g].finished, self.records[g].winner = True, res
                 self._dev["game"][g, 0] = 1
                 self._dev["game"][g, 1] = res
+            if hasattr(self.game, "device_game"):
+                self._dev["game"][g, 5:8] = torch.tensor(self.game.device_game(pos), dtype=torch.int32)
 
     def _device_step(self) -> int:
         import ctypes
@@ -385,7 +435,15 @@ class BatchedSelfPlay:
                                       self.resign_threshold, self.seed & _MASK64)
         p = lambda t: ctypes.c_void_p(t.data_ptr())
         hist = (p(d["game"]), p(d["actions"]), p(d["moves"]), p(d["visits"]), p(d["values"]), p(d["states"]))
-        if self.game.name == "chess":
+        if self.game.name == "go":
+            pos0 = self._start[0]
+            eng.search(roots["history"], self.sims, self._evaluator, meta=roots["meta"],
+                       keys=(roots["keys"], roots["nkeys"]))
+            _lib.check(eng.L.omq_selfplay_move_go(eng._h, ctypes.byref(cfg), ctypes.c_float(pos0.komi),
+                                                  int(pos0.rules == "chinese"), p(roots["history"]),
+                                                  p(roots["meta"]), p(roots["keys"]), p(roots["nkeys"]), *hist,
+                                                  _stream_ptr()), "omq_selfplay_move_go")
+        elif self.game.name == "chess":
             eng.search(roots["records"], self.sims, self._evaluator, meta=roots["nprior"])
             _lib.check(eng.L.omq_selfplay_move_chess(eng._h, ctypes.byref(cfg), p(roots["records"]),
                                                      p(roots["nprior"]), *hist, _stream_ptr()),
@@ -419,17 +477,22 @@ class BatchedSelfPlay:
                 tot = v.sum()
                 st = self.game.device_state(states[g, k])
                 rec.examples.append({"state": st, "policy": v / tot if tot > 0 else np.full(v.shape, 1.0 / v.size),
-                                     "player": self._state_player(st), "move_number": m,
+                                     "player": self._state_player(st, g, m), "move_number": m,
                                      "value_pred": float(values[g, k])})
                 rec.moves.append(int(moves[g, k]))
-            self.positions[g] = self.game.device_position(roots, g)
+            self.positions[g] = self.game.device_position(roots, g, self._start[g], game[g])
             if game[g, 0] and not rec.finished:
                 rec.finished, rec.winner, rec.resigned = True, int(game[g, 1]), bool(game[g, 2])
         d["synced"] = m1
 
-    def _state_player(self, st) -> int:
-        """The side to move of a recorded state (a board, or a chess record)."""
-        return int(st["side"]) if self.game.name == "chess" else self.game.player(st)
+    def _state_player(self, st, g: int, m: int) -> int:
+        """The side to move of a recorded state (a board, a chess record, or Go history planes)."""
+        if self.game.name == "chess":
+            return int(st["side"])
+        if self.game.name == "go":      # every move (passes included) changes the side to move
+            p0 = self._start[g].to_move
+            return p0 if m % 2 == 0 else 3 - p0
+        return self.game.player(st)
 
     # -- search ----------------------------------------------------------------------------
     @property

@@ -96,3 +96,66 @@ def test_device_chess_selfplay_equals_host_replay(reuse, resign):
     assert dfinal == hfinal
     if resign > 0:
         assert any(r.resigned for r in dev)
+
+
+def _go_roots(rules):
+    from omoknuni_quantum_b200.go import GoPosition
+    out = []
+    for i in range(4):
+        g = GoPosition(9, rules=rules)
+        rng = np.random.default_rng(40 + i)
+        for _ in range(24):
+            cand = np.flatnonzero(g.legal_mask()[:-1])
+            g.play(int(rng.choice(cand)))
+        out.append(g)
+    # white to move after a pass, and every point is a one-point eye of black's single group:
+    # white can only pass, which ends the game (scored)
+    g = GoPosition(9, rules=rules)
+    g.board[:] = 1
+    for y, x in ((1, 1), (1, 7), (7, 1), (7, 7), (4, 4)):
+        g.board[y, x] = 0
+    g.history = [g.board.copy()]
+    g.to_move, g.passes = 2, 1
+    out.append(g)
+    out.append(GoPosition(9, rules=rules))                 # the empty board
+    return out
+
+
+def _play_go(sampling, rules, reuse, resign):
+    from omoknuni_quantum_b200.selfplay import BatchedSelfPlay
+    kw = dict(num_simulations=64, wave_size=16, capacity=60000, seed=9, temperature_threshold=3,
+              roots=_go_roots(rules), board_size=9, subtree_reuse=reuse, evaluator="synthetic", game="go",
+              resign_threshold=resign, resign_min_move=2)
+    if sampling == "device":
+        sp = BatchedSelfPlay(6, sampling="device", max_moves=12, **kw)
+    else:
+        sp = BatchedSelfPlay(6, sampling="host", rng="counter", **kw)
+    recs = sp.play(7)
+    final = [(p.history_planes().tobytes(), p.meta().tobytes(), list(p.keys), list(p.prisoners), p.repeated)
+             for p in sp.positions]
+    sp.close()
+    return recs, final
+
+
+@pytest.mark.parametrize("rules,reuse,resign", [("chinese", "none", -0.98), ("japanese", "keep", 0.05),
+                                                ("korean", "carry", -0.98)])
+def test_device_go_selfplay_equals_host_replay(rules, reuse, resign):
+    """Go games played by omq_selfplay_move_go equal the host driver's (go.py, the reference
+    engine's rules): moves, examples (the 8 history boards), ends, scores and the final
+    positions (history, side to move, ko, passes, keys, prisoners)."""
+    (dev, dfinal), (host, hfinal) = _play_go("device", rules, reuse, resign), _play_go("host", rules, reuse, resign)
+    assert sum(len(r.moves) for r in dev) > 6
+    # white's forced pass ends it: black's area 81 against komi 7.5; by territory 5 against 6.5
+    assert dev[4].finished and dev[4].moves == [81] and dev[4].winner == (1 if rules == "chinese" else -1)
+    for a, b in zip(dev, host):
+        assert a.moves == b.moves
+        assert (a.finished, a.winner, a.resigned) == (b.finished, b.winner, b.resigned)
+        assert len(a.examples) == len(b.examples) == len(a.moves)
+        for x, y in zip(a.examples, b.examples):
+            assert np.array_equal(x["state"], y["state"])
+            assert np.array_equal(x["policy"], y["policy"])
+            assert x["player"] == y["player"] and x["move_number"] == y["move_number"]
+            assert np.float32(x["value_pred"]) == np.float32(y["value_pred"])
+    assert dfinal == hfinal
+    if resign > 0:
+        assert any(r.resigned for r in dev)
