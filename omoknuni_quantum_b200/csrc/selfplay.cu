@@ -358,6 +358,7 @@ __global__ void __launch_bounds__(kSelfplayThreads) k_selfplay_move_go(
   const float value = block_root_visits(v, g, vis, &s_total);
   __syncthreads();
   const int player = meta[3 * g], ko0 = meta[3 * g + 1], passes0 = meta[3 * g + 2];
+  const int repeated0 = st[7];  // read before thread 0 rewrites it below
   const int action = block_choose(c, g, m, vis, A, s_total, s_chunk, &s_action);
   uint64_t* K = keys + (size_t)g * OMQ_GO_MAX_KEYS;
   const int nk = min(max(nkeys[g], 0), OMQ_GO_MAX_KEYS);
@@ -400,7 +401,7 @@ __global__ void __launch_bounds__(kSelfplayThreads) k_selfplay_move_go(
   }
   // the game's keys: superko history (non-pass moves) or the repetition rule's (every move)
   const bool cycle = v.go_cycle != 0;
-  const bool add = cycle ? st[7] == 0 : action < C;
+  const bool add = cycle ? repeated0 == 0 : action < C;
   const uint64_t newkey = cycle ? (s_key ^ go_side_key(3 - player)) : s_key;
   int nk2 = nk;
   if (add) {
@@ -417,7 +418,7 @@ __global__ void __launch_bounds__(kSelfplayThreads) k_selfplay_move_go(
     ++nk2;
   }
   __syncthreads();
-  int repeated = st[7];
+  int repeated = repeated0;
   if (cycle && add) {
     int cnt = 0;
     for (int i = tid; i < nk2; i += blockDim.x) cnt += K[i] == newkey;
