@@ -115,12 +115,8 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
   float* s_bias = reinterpret_cast<float*>(staging + Cfg::kStaging + 512);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_pos = args.d_count ? min(*args.d_count, args.count) : args.count;
-  const int rows = n_pos * args.P;
-  const int tiles = (rows + Cfg::kRows - 1) / Cfg::kRows;
   // work item w: pixel tile w / halves, output channels [128 * (w % halves), +128)
   const int halves = args.halves;
-  const int items = tiles * halves;
   const int cout = BN * halves;
   const int CB = args.kb_per_tap;
   const int rowstride = args.S + 1;
@@ -145,6 +141,14 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Launched as a programmatic dependent of the previous kernel in the stream, the setup above
+  // (barriers, TMEM, tensor-map prefetch, bias) overlaps that kernel's tail; every global read
+  // of its outputs and every global write comes after this wait for its completion.
+  ptx::griddep_wait();
+  const int n_pos = args.d_count ? min(*args.d_count, args.count) : args.count;
+  const int rows = n_pos * args.P;
+  const int tiles = (rows + Cfg::kRows - 1) / Cfg::kRows;
+  const int items = tiles * halves;
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer: per 64-channel block one halo, then 9 weight taps -------
@@ -1093,8 +1097,19 @@ static int launch_conv_halo_tr(const omq_resnet* n, const CUtensorMap& tH, const
   const int max_items = (int)((n->rows + HaloTCfg::kRows - 1) / HaloTCfg::kRows) * a.halves;
   const int grid = max(1, min(max_items, n->sm_count));
   count_launches(1);
-  k_conv3x3_halo_t<F16><<<grid, HaloTCfg::kThreads, HaloTCfg::kSmem, s>>>(tH, tB, tO, a);
-  return cuda_status(cudaGetLastError(), "k_conv3x3_halo_t");
+  // programmatic dependent launch: the CTAs may start (and run their setup) while the previous
+  // kernel's last CTAs finish; the kernel waits for that kernel before touching global memory
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(HaloTCfg::kThreads);
+  cfg.dynamicSmemBytes = HaloTCfg::kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, k_conv3x3_halo_t<F16>, tH, tB, tO, a), "k_conv3x3_halo_t");
 }
 
 static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tO,

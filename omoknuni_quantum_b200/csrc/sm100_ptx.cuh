@@ -97,6 +97,10 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// Programmatic dependent launch: wait until the grids this one depends on have completed and
+// their memory is visible (a no-op for a kernel launched without the attribute).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // D[tmem] (+)= A[smem desc] * B[smem desc]^T, 16-bit inputs (bf16 or fp16, as the instruction
 // descriptor says), fp32 accumulation.
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
