@@ -388,12 +388,18 @@ struct DenseArgs {
 
 constexpr int kDenseStages = 2;
 constexpr int kDenseThreads = 192;  // TMA warp, MMA warp, 4 epilogue warps
+// The fused softmax epilogue splits each 128-row tile over 16 epilogue warps (4 per TMEM lane
+// quarter, 64 columns each): its per-row exponentials would otherwise run on 128 threads per
+// tile, which at small batches (2 tiles for a 256-position call) sets the head's latency.
+constexpr int kSoftmaxSlices = 4;
+template <int MODE>
+constexpr int dense_threads() { return MODE == kDenseSoftmax ? 64 + 32 * 4 * kSoftmaxSlices : kDenseThreads; }
 // Shared memory requested by every dense launch: two stages of the widest tile, so that at most
 // two CTAs (2 x 256 TMEM columns) share an SM.
 constexpr int kDenseSmem = kDenseStages * (128 * 128 + 256 * 128) + 1024 + 256;
 
 template <int NT, int MODE, bool F16>
-__global__ void __launch_bounds__(kDenseThreads)
+__global__ void __launch_bounds__(dense_threads<MODE>())
     k_dense(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, DenseArgs a) {
   constexpr int kA = 128 * 128, kW = NT * 128;            // bytes per 64-wide K block
   extern __shared__ uint8_t smem_raw[];
@@ -500,37 +506,63 @@ __global__ void __launch_bounds__(kDenseThreads)
             if (c0 + j < ncols) out[c0 + j] = __uint_as_float(v[j]) + a.bias[col0 + c0 + j];
         }
       }
-    } else if (ok && MODE == kDenseSoftmax) {
-      // the whole policy row is this tile's (n_total <= NT): max, sum, then the probabilities
-      float mx = -INFINITY;
-      for (int c0 = 0; c0 < NT; c0 += 32) {
+    } else if (MODE == kDenseSoftmax) {
+      // the whole policy row is this tile's (n_total <= NT); warp 2 + q + 4 s takes columns
+      // [s * NT / 4, +NT / 4) of rows 32 q + lane: row max and exponential sums are combined over
+      // the 4 slices in slice order through shared memory. Every epilogue warp reaches both
+      // barriers, also after a timed-out wait (it then stores nothing).
+      constexpr int kCols = NT / kSoftmaxSlices;
+      static_assert(MODE != kDenseSoftmax || kDenseStages * (kA + kW) >= 4 * kSoftmaxSlices * 32 * 33 * 4,
+                    "transpose buffers fit the ring");
+      __shared__ float s_red[2][kSoftmaxSlices][4][32];
+      const int slice = (warp - 2) >> 2;
+      const int cb = slice * kCols;
+      float x[kCols];
+#pragma unroll
+      for (int c0 = 0; c0 < kCols; c0 += 32) {
         uint32_t v[32];
-        ptx::tmem_ld_32x32b_x32(taddr + c0, v);
+        ptx::tmem_ld_32x32b_x32(taddr + cb + c0, v);
         ptx::tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c0 + j < ncols) mx = fmaxf(mx, __uint_as_float(v[j]) + a.bias[c0 + j]);
-      }
-      float sum = 0.f;
-      for (int c0 = 0; c0 < NT; c0 += 32) {
-        uint32_t v[32];
-        ptx::tmem_ld_32x32b_x32(taddr + c0, v);
-        ptx::tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c0 + j < ncols) sum += expf(__uint_as_float(v[j]) + a.bias[c0 + j] - mx);
-      }
-      const float inv = 1.0f / sum;
-      float* out = static_cast<float*>(a.out) + (size_t)r * a.ld;
-      for (int c0 = 0; c0 < NT; c0 += 32) {
-        uint32_t v[32];
-        ptx::tmem_ld_32x32b_x32(taddr + c0, v);
-        ptx::tmem_ld_wait();
-        if (live) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (c0 + j < ncols) out[c0 + j] = expf(__uint_as_float(v[j]) + a.bias[c0 + j] - mx) * inv;
+        for (int j = 0; j < 32; ++j) {
+          const int c = cb + c0 + j;
+          x[c0 + j] = (ok && c < ncols) ? __uint_as_float(v[j]) + a.bias[c] : -INFINITY;
         }
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < kCols; ++j) mx = fmaxf(mx, x[j]);
+      s_red[0][slice][q][lane] = mx;
+      ptx::named_barrier(1, 32 * 4 * kSoftmaxSlices);
+#pragma unroll
+      for (int t = 0; t < kSoftmaxSlices; ++t) mx = fmaxf(mx, s_red[0][t][q][lane]);
+      float part = 0.f;
+#pragma unroll
+      for (int j = 0; j < kCols; ++j) {
+        x[j] = (ok && cb + j < ncols) ? expf(x[j] - mx) : 0.f;
+        part += x[j];
+      }
+      s_red[1][slice][q][lane] = part;
+      ptx::named_barrier(1, 32 * 4 * kSoftmaxSlices);
+      float sum = 0.f;
+#pragma unroll
+      for (int t = 0; t < kSoftmaxSlices; ++t) sum += s_red[1][t][q][lane];
+      const float inv = 1.0f / sum;
+      // stores through a 32 x 33 transpose buffer per warp (in the operand ring, idle once the
+      // MMAs completed): lane l writes column l of each of the warp's 32 rows, so a warp store
+      // covers 128 contiguous bytes of one row instead of one word in each of 32 rows
+      float* tb = reinterpret_cast<float*>(ring) + (warp - 2) * (32 * 33);
+      const int nrows = min(32, n - (row0 + q * 32));
+      float* out0 = static_cast<float*>(a.out) + (size_t)(row0 + q * 32) * a.ld;
+#pragma unroll
+      for (int c0 = 0; c0 < kCols; c0 += 32) {
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tb[lane * 33 + j] = x[c0 + j] * inv;
+        __syncwarp();
+        const int c = cb + c0 + lane;
+        if (ok && c < ncols)
+          for (int rr = 0; rr < nrows; ++rr) out0[(size_t)rr * a.ld + c] = tb[rr * 33 + lane];
       }
     } else if (ok && MODE == kDenseValue) {
       float acc = 0.f;
@@ -1130,7 +1162,7 @@ static int launch_dense_t(const CUtensorMap& tA, const CUtensorMap& tW, const De
     if (e != cudaSuccess) return cuda_status(e, "dense smem attribute");
   }
   count_launches(1);
-  k_dense<NT, MODE, F16><<<dim3((rows_cap + 127) / 128, ntiles), kDenseThreads, kDenseSmem, s>>>(tA, tW, a);
+  k_dense<NT, MODE, F16><<<dim3((rows_cap + 127) / 128, ntiles), dense_threads<MODE>(), kDenseSmem, s>>>(tA, tW, a);
   return cuda_status(cudaGetLastError(), "k_dense");
 }
 

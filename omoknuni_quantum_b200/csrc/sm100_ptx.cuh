@@ -99,6 +99,11 @@ __device__ __forceinline__ void tc_fence_after() {
 
 // Programmatic dependent launch: wait until the grids this one depends on have completed and
 // their memory is visible (a no-op for a kernel launched without the attribute).
+// Barrier `id` (1..15) over `count` threads (a multiple of 32) of the CTA.
+__device__ __forceinline__ void named_barrier(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]^T, 16-bit inputs (bf16 or fp16, as the instruction
