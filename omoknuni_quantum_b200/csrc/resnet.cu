@@ -833,7 +833,7 @@ struct omq_resnet {
   int tc_heads;
   int k1p, k3p, n1pad, n2pad, n3pad, nt3;  // padded K of fc1 policy / fc1 value, padded rows
   h16 *pin, *vin, *hid, *w1b, *w2b, *w3b;
-  CUtensorMap tm_pin, tm_vin, tm_hid, tm_w1, tm_w2, tm_w3;
+  CUtensorMap tm_pin, tm_vin, tm_hid, tm_w1, tm_w1h, tm_w2, tm_w3;  // tm_w1h: 128-row boxes
   bool f16;                // 16-bit storage is fp16 (OMQ_DTYPE_F16), else bf16
   // optional timing of the conv trunk of each forward call (CUDA events on the caller's stream)
   int prof_cap, prof_n;
@@ -923,6 +923,7 @@ static int build_maps(omq_resnet* n) {
     if (st == OMQ_OK) st = make_map(&n->tm_vin, n->vin, n->k3p, n->max_batch, 128, n->f16);
     if (st == OMQ_OK) st = make_map(&n->tm_hid, n->hid, n->Hp, n->max_batch, 128, n->f16);
     if (st == OMQ_OK) st = make_map(&n->tm_w1, n->w1b, n->k1p, n->n1pad, 256, n->f16);
+    if (st == OMQ_OK) st = make_map(&n->tm_w1h, n->w1b, n->k1p, n->n1pad, 128, n->f16);
     if (st == OMQ_OK) st = make_map(&n->tm_w2, n->w2b, n->Hp, n->n2pad, 256, n->f16);
     if (st == OMQ_OK) st = make_map(&n->tm_w3, n->w3b, n->k3p, n->n3pad, n->nt3, n->f16);
   }
@@ -1200,7 +1201,12 @@ static int run_tc_heads(omq_resnet* n, const h16* act, const int32_t* d_count, i
   a.error = n->error;
   // policy fc1 -> hidden (16-bit, ReLU)
   a.bias = b1p; a.out = n->hid; a.ld = n->Hp; a.n_total = n->Hp; a.kblocks = n->k1p / 64;
-  st = launch_dense<256, kDenseRelu16>(n, n->tm_pin, n->tm_w1, a, count, n->n1pad / 256, s);
+  // a batch that fills fewer than half the SMs with 256-wide tiles takes 128-wide ones (twice the
+  // CTAs, each loading half the weights; the K loop is the same, so are the results)
+  if ((count + 127) / 128 * (n->n1pad / 256) * 2 <= n->sm_count)
+    st = launch_dense<128, kDenseRelu16>(n, n->tm_pin, n->tm_w1h, a, count, n->n1pad / 128, s);
+  else
+    st = launch_dense<256, kDenseRelu16>(n, n->tm_pin, n->tm_w1, a, count, n->n1pad / 256, s);
   if (st) return st;
   // policy fc2 -> probabilities
   a.bias = b2p; a.out = policy; a.ld = n->A; a.n_total = n->A; a.kblocks = n->Hp / 64;

@@ -178,6 +178,11 @@ def test_forward_is_batch_invariant():
     assert torch.equal(p1[perm], p2) and torch.equal(v1[perm], v2)
     p3, v3 = ev.evaluate_batch(x[:5])
     assert torch.equal(p1[:5], p3) and torch.equal(v1[:5], v3)
+    # a call large enough for the heads' 256-wide tiles (small calls take 128-wide fc1 tiles)
+    big = ResNetEvaluator(ev.state_dict, max_batch=12000)
+    xb = torch.cat([x, _features(12000 - 257, seed=6).cuda()])
+    p4, v4 = big.evaluate_batch(xb)
+    assert torch.equal(p1, p4[:257]) and torch.equal(v1, v4[:257])
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "fp16"])
