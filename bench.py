@@ -535,11 +535,23 @@ def run_b200(args):
 
 
 def run_extra_configs(args):
-    """Configs 2, 3 and 4 with one warm-up and one timed step each (the default bench line's
-    `other_configs`): the same code as --workload config2|config3|config4, without the e2e and
-    CPU legs. Runs on every rank (the timings are maxima over ranks)."""
+    """Config 0 (20 single-tree searches) and configs 2, 3 and 4 with one warm-up and one timed
+    step each (the default bench line's `other_configs`): the same code as --evaluator synthetic
+    and --workload config2|config3|config4, without the e2e and CPU legs. Runs on every rank (the
+    timings are maxima over ranks)."""
     import copy
     out = {}
+    # config 0: one tree, 800 simulations, wave 256, the synthetic evaluator (the tree kernels
+    # alone), 20 timed searches; 400k nodes, since the stated 100k overflows the reference's own
+    # full expansion (about 160k nodes per search)
+    a = copy.copy(args)
+    a.roots, a.sims, a.wave, a.capacity, a.steps, a.warmup = 1, 800, 256, 400000, 20, 3
+    line = run_b200_synthetic(a, inner=True)
+    torch.cuda.synchronize()
+    out["config0"] = {"value": line["value"], "unit": line["unit"], "ms_per_step": line["ms_per_step"],
+                      "steps": line["steps"], "warmup": line["warmup"], "scaling": line["scaling"],
+                      "config": line["config"], "clocks": line.get("clocks"),
+                      "gpu_launches": line.get("gpu_launches")}
     for name, fn in (("config2", lambda a: run_b200_selfplay(a, inner=True)),
                      ("config3", lambda a: run_b200_go(a, "go", inner=True)),
                      ("config4", lambda a: run_b200_go(a, "chess", inner=True))):
@@ -561,7 +573,7 @@ def run_extra_configs(args):
     return out
 
 
-def run_b200_synthetic(args):
+def run_b200_synthetic(args, inner=False):
     """benchmark config 0 on the device: the integer-exact synthetic evaluator, so the step is the
     tree kernels alone (select, expand, backup, evaluation kernel)."""
     from omoknuni_quantum_b200 import _lib, parallel
@@ -571,8 +583,7 @@ def run_b200_synthetic(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if ws > 1:
-        import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=dev)
+        init_dist(dev)
     R = args.roots
     roots = torch.from_numpy(random_roots(args.seed * 1000 + rank, R)).to(dev)
     eng = WaveEngine(R, capacity=args.capacity, max_wave_size=args.wave, device=dev)
@@ -588,8 +599,9 @@ def run_b200_synthetic(args):
         s1.record()
         torch.cuda.synchronize()
     ms = parallel.max_over_ranks(s0.elapsed_time(s1), dev)
-    if rank == 0:
-        print(json.dumps({
+    eng.close()
+    if inner or rank == 0:
+        line = {
             "metric": METRIC, "value": args.sims * R * args.steps * ws / (ms / 1000.0), "unit": UNIT,
             "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32/int32",
@@ -598,7 +610,10 @@ def run_b200_synthetic(args):
                                    "synthetic evaluator; roots searched in lockstep per GPU",
                        "roots_per_gpu": R, "capacity": args.capacity, "parallelism": f"dp{ws}"},
             "roofline": None, "cpu_baseline": None, "e2e": None, "clocks": clk.summary(),
-            "gpu_launches": _lib.kernel_launches() - n0}), flush=True)
+            "gpu_launches": _lib.kernel_launches() - n0}
+        if inner:
+            return line
+        print(json.dumps(line), flush=True)
     if ws > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
