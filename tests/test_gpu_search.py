@@ -60,6 +60,41 @@ def test_multi_tree_lockstep_matches_oracle(oracle_lib):
         assert np.array_equal(eng.policy_from_visits(visits[r]), o.policy)
 
 
+def _edge_roots():
+    """A root that already holds five in a row, a board with three empty cells and no five (runs
+    of at most two in every direction), a random root and the empty board."""
+    from omoknuni_quantum_b200.roots import random_roots
+    r = random_roots(23, 4)
+    r[0, 7, 2:7] = 1                              # five for black, and one more white stone
+    r[0, 3, 3] = 2
+    y, x = np.mgrid[0:15, 0:15]
+    full = (1 + ((x // 2 + y) % 2)).astype(np.int8)
+    full[0, 0] = full[7, 7] = full[14, 5] = 0
+    r[1] = full
+    r[3] = 0
+    return r
+
+
+@pytest.mark.parametrize("sims,wave", [(300, 64), (5, 64), (64, 64)])
+def test_edge_roots_and_short_searches_match_oracle(oracle_lib, sims, wave):
+    """Roots the reference searches without special cases (a decided board: every child is
+    terminal; a nearly full board: children reach the full board), and searches shorter than one
+    wave or exactly one wave, against the oracle."""
+    from omoknuni_quantum_b200.engine import WaveEngine
+    roots = _edge_roots()
+    eng = WaveEngine(4, capacity=80000, max_wave_size=wave)
+    eng.search(torch.from_numpy(roots).cuda(), sims)
+    visits = eng.root_visits().cpu().numpy()
+    assert visits[1].sum() == sims and np.count_nonzero(visits[1]) <= 3
+    for r in range(4):
+        o = oracle_lib.Oracle(80000).search(roots[r], sims, wave)
+        t = eng.export_tree(r)
+        for k, ok in (("visits", o.visits), ("value_sums", o.value_sums), ("priors", o.priors),
+                      ("parent", o.parent), ("action", o.action)):
+            assert np.array_equal(t[k], ok), (r, k)
+        assert np.array_equal(eng.policy_from_visits(visits[r]), o.policy)
+
+
 class _RecordingTorchEvaluator:
     """A float-valued evaluator on the GPU (fixed random linear policy/value heads on the
     features). Records every output keyed by the feature bytes so that the oracle can replay
