@@ -100,7 +100,7 @@ struct TreeHeader {
   int32_t kept;
   int32_t carry_n;
   float carry_w;
-  int32_t pad;
+  int32_t exp_total;     // children created by the expansion in flight (sliced k_expand)
 };
 
 constexpr int kPlanes = 19;

@@ -11,6 +11,8 @@
 // exactly one record per wave, which makes backup free of atomics and lets it add the values
 // of [lo, lo+k) in ascending simulation order - the reference's sequential order
 // (python/mcts/gpu/mcts_gpu_accelerator.py:378-393) - so W is bit-exact for any evaluator.
+#include <atomic>
+
 #include "chess_device.cuh"
 #include "go_device.cuh"
 #include "omq_internal.cuh"
@@ -803,6 +805,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
   __shared__ int warp_tot[kWarps + 1];
   __shared__ int s_fbase;
   const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // Slices: with few trees (Gomoku), gridDim.y CTAs share one tree, CTA y taking the leaves
+  // i with i % gridDim.y == y; H->num_nodes is then left unchanged here (every slice reads it)
+  // and k_expand_commit applies the node count and the final-node queue afterwards.
+  const int slices = (int)gridDim.y, slice = (int)blockIdx.y;
   TreeHeader* H = &v.hdr[r];
   if (H->status != OMQ_OK) return;
   const size_t base = (size_t)r * v.T;
@@ -900,19 +906,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
     if (tid == 0) H->status = OMQ_TREE_FULL;
     return;
   }
+  if (slices > 1 && slice == 0 && tid == 0) H->exp_total = total;
   ExpandWarpSmem& W = ws[warp];
   // Gomoku: every thread walks one expandable leaf's parent chain into the path scratch (slot
   // kMaxDepthCap - 1 holds the depth), so the chains' dependent loads overlap across leaves
   int16_t* gpath = v.leaf_paths + (size_t)r * v.WCAP * kMaxDepthCap;
   if (!go && !chs) {
-    for (int i = tid; i < nleaf; i += blockDim.x)
+    for (int i = slice + slices * tid; i < nleaf; i += slices * blockDim.x)
       if (lf[i].y >= 0) {
         int16_t* P = gpath + (size_t)i * kMaxDepthCap;
         P[kMaxDepthCap - 1] = (int16_t)path_actions(v.topo + base, leaves[i].node, kMaxDepthCap - 2, P);
       }
     __syncthreads();
   }
-  for (int i = warp; i < nleaf; i += (int)(blockDim.x >> 5)) {
+  for (int i = slice + slices * warp; i < nleaf; i += slices * (int)(blockDim.x >> 5)) {
     const Visit e = leaves[i];
     const int q = lf[i].y;
     int final_node = e.node, ext = 0;
@@ -1066,9 +1073,38 @@ __global__ void __launch_bounds__(kThreads, 1) k_expand(EngineView v, int root_m
     if (lane == 0) lf[i] = make_int2(final_node, ext << 30);
     __syncwarp();
   }
+  if (slices > 1) return;  // k_expand_commit finishes the sliced expansion
   __syncthreads();
   if (tid == 0) {
     H->num_nodes = num_nodes + total;
+    if (!root_mode) {
+      s_fbase = atomicAdd(&v.q_count[1], nleaf);
+      H->fin_off = s_fbase;
+      H->fin_cnt = nleaf;
+    }
+  }
+  __syncthreads();
+  if (!root_mode) {
+    for (int i = tid; i < nleaf; i += blockDim.x) {
+      const int2 x = lf[i];
+      v.q_entries[1][s_fbase + i] = make_int2(r, x.x);
+      lf[i] = make_int2(x.x, (s_fbase + i) | (x.y & (1 << 30)));
+    }
+  }
+}
+
+// The end of a sliced k_expand: the tree's node count and its final-node queue entries (the
+// single-CTA k_expand does this itself).
+__global__ void k_expand_commit(EngineView v, int root_mode) {
+  const int r = blockIdx.x, tid = threadIdx.x;
+  TreeHeader* H = &v.hdr[r];
+  if (H->status != OMQ_OK) return;
+  const int nleaf = H->nleaves;
+  int2* lf = v.leaf_final + (size_t)r * v.WCAP;
+  __shared__ int s_fbase;
+  if (tid == 0) {
+    H->num_nodes += H->exp_total;
+    H->exp_total = 0;
     if (!root_mode) {
       s_fbase = atomicAdd(&v.q_count[1], nleaf);
       H->fin_off = s_fbase;
@@ -1175,14 +1211,24 @@ __global__ void k_status(EngineView v, int32_t* status, int32_t* num_nodes) {
 // ---------------------------------------------------------------------------------------------
 // launchers
 // ---------------------------------------------------------------------------------------------
-static int tree_threads(const EngineView& v) {
-  static int sms = 0;
-  if (!sms) {
+// SMs of the device (every device of the pool is the same part)
+static int device_sms() {
+  static std::atomic<int> sms{0};
+  int n = sms.load(std::memory_order_relaxed);
+  if (!n) {
     int dev = 0;
     cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 148;
+    }
+    sms.store(n, std::memory_order_relaxed);
   }
+  return n;
+}
+
+static int tree_threads(const EngineView& v) {
+  const int sms = device_sms();
   return v.R >= 2 * sms ? 256 : kThreads;
 }
 
@@ -1228,7 +1274,16 @@ void launch_expand(const EngineView& v, int root_mode, cudaStream_t s) {
   const int threads = v.game == OMQ_GAME_GO ? min(tree_threads(v), 512) : tree_threads(v);
   const int sm = (int)((threads / 32) * (sizeof(ExpandWarpSmem) + extra));
   cudaFuncSetAttribute(k_expand, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-  k_expand<<<v.R, threads, sm, s>>>(v, root_mode);
+  // few Gomoku trees: several CTAs (SMs) per tree, one leaf per warp at a full wave
+  const int sm_count = device_sms();
+  const int slices = (v.game == OMQ_GAME_GOMOKU && 4 * v.R <= sm_count)
+                         ? max(1, min(8, min(sm_count / (2 * v.R), (v.WCAP + threads / 32 - 1) / (threads / 32))))
+                         : 1;
+  k_expand<<<dim3(v.R, slices), threads, sm, s>>>(v, root_mode);
+  if (slices > 1) {
+    count_launches(1);
+    k_expand_commit<<<v.R, 256, 0, s>>>(v, root_mode);
+  }
 }
 
 void launch_backup(const EngineView& v, cudaStream_t s) {
