@@ -338,7 +338,9 @@ OMQ_API int omq_resnet_forward_packed(omq_resnet* net, const uint16_t* d_input,
                                       float* d_value, void* stream);
 OMQ_API int omq_resnet_input_buffer(omq_resnet* net, uint16_t** d_input);
 /* Evaluate an engine leaf queue in place: the queued positions are packed on the device and
- * the queue's policy/value buffers are written; no host synchronisation. */
+ * the queue's policy/value buffers are written; no host synchronisation. Queue 1 (the final
+ * nodes, whose policies the search never reads: wave_search.py:1337-1457 keeps only the values)
+ * gets its values only; its policy buffer is left as it was. */
 OMQ_API int omq_resnet_forward_queue(omq_resnet* net, omq_engine* engine, int32_t queue,
                                      void* stream);
 /* Whole search in one call, the native counterpart of MCTS.search / _run_search

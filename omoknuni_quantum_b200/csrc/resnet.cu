@@ -1178,7 +1178,7 @@ static int launch_dense(const omq_resnet* n, const CUtensorMap& tA, const CUtens
 // fc2 (policy) with the softmax fused when the policy fits one 256-wide tile, and the value
 // head's fc1 with the fc2 dot and tanh fused.
 static int run_tc_heads(omq_resnet* n, const h16* act, const int32_t* d_count, int count,
-                        float* policy, float* value, cudaStream_t s) {
+                        float* policy, float* value, bool value_only, cudaStream_t s) {
   const float* p = n->head;
   const float* w1x1 = p; p += 3 * n->C;
   const float* b1x1 = p; p += 3;
@@ -1199,28 +1199,30 @@ static int run_tc_heads(omq_resnet* n, const h16* act, const int32_t* d_count, i
   a.d_count = d_count;
   a.count = count;
   a.error = n->error;
-  // policy fc1 -> hidden (16-bit, ReLU)
-  a.bias = b1p; a.out = n->hid; a.ld = n->Hp; a.n_total = n->Hp; a.kblocks = n->k1p / 64;
-  // a batch that fills fewer than half the SMs with 256-wide tiles takes 128-wide ones (twice the
-  // CTAs, each loading half the weights; the K loop is the same, so are the results)
-  if ((count + 127) / 128 * (n->n1pad / 256) * 2 <= n->sm_count)
-    st = launch_dense<128, kDenseRelu16>(n, n->tm_pin, n->tm_w1h, a, count, n->n1pad / 128, s);
-  else
-    st = launch_dense<256, kDenseRelu16>(n, n->tm_pin, n->tm_w1, a, count, n->n1pad / 256, s);
-  if (st) return st;
-  // policy fc2 -> probabilities
-  a.bias = b2p; a.out = policy; a.ld = n->A; a.n_total = n->A; a.kblocks = n->Hp / 64;
-  if (n->A <= 256) {
-    st = launch_dense<256, kDenseSoftmax>(n, n->tm_hid, n->tm_w2, a, count, 1, s);
-  } else {
-    st = launch_dense<256, kDenseLogits>(n, n->tm_hid, n->tm_w2, a, count, n->n2pad / 256, s);
-    if (!st) {
-      count_launches(1);
-      k_softmax_rows<<<max(1, min((count + 7) / 8, 8 * n->sm_count)), 256, 0, s>>>(policy, n->A, n->A, d_count, count);
-      st = cuda_status(cudaGetLastError(), "k_softmax_rows");
+  if (!value_only) {
+    // policy fc1 -> hidden (16-bit, ReLU)
+    a.bias = b1p; a.out = n->hid; a.ld = n->Hp; a.n_total = n->Hp; a.kblocks = n->k1p / 64;
+    // a batch that fills fewer than half the SMs with 256-wide tiles takes 128-wide ones (twice the
+    // CTAs, each loading half the weights; the K loop is the same, so are the results)
+    if ((count + 127) / 128 * (n->n1pad / 256) * 2 <= n->sm_count)
+      st = launch_dense<128, kDenseRelu16>(n, n->tm_pin, n->tm_w1h, a, count, n->n1pad / 128, s);
+    else
+      st = launch_dense<256, kDenseRelu16>(n, n->tm_pin, n->tm_w1, a, count, n->n1pad / 256, s);
+    if (st) return st;
+    // policy fc2 -> probabilities
+    a.bias = b2p; a.out = policy; a.ld = n->A; a.n_total = n->A; a.kblocks = n->Hp / 64;
+    if (n->A <= 256) {
+      st = launch_dense<256, kDenseSoftmax>(n, n->tm_hid, n->tm_w2, a, count, 1, s);
+    } else {
+      st = launch_dense<256, kDenseLogits>(n, n->tm_hid, n->tm_w2, a, count, n->n2pad / 256, s);
+      if (!st) {
+        count_launches(1);
+        k_softmax_rows<<<max(1, min((count + 7) / 8, 8 * n->sm_count)), 256, 0, s>>>(policy, n->A, n->A, d_count, count);
+        st = cuda_status(cudaGetLastError(), "k_softmax_rows");
+      }
     }
+    if (st) return st;
   }
-  if (st) return st;
   // value fc1 + ReLU, fc2, tanh
   a.bias = b1v; a.w2 = fc2v; a.b2 = b2v; a.out = value; a.ld = 1; a.n_total = n->Hv; a.kblocks = n->k3p / 64;
   if (n->nt3 == 128) return launch_dense<128, kDenseValue>(n, n->tm_vin, n->tm_w3, a, count, 1, s);
@@ -1229,7 +1231,7 @@ static int run_tc_heads(omq_resnet* n, const h16* act, const int32_t* d_count, i
 
 // trunk + heads on n->x_in (already packed), count from d_count (device) or `count`.
 int resnet_run(omq_resnet* n, const int32_t* d_count, int count, float* policy, float* value,
-               cudaStream_t s) {
+               cudaStream_t s, bool value_only = false) {
   if (!n->loaded) { set_error("omq_resnet_load was not called"); return OMQ_NOT_READY; }
   const int pi = (n->prof_cap > 0 && n->prof_n < n->prof_cap) ? n->prof_n++ : -1;
   if (pi >= 0) {
@@ -1253,7 +1255,7 @@ int resnet_run(omq_resnet* n, const int32_t* d_count, int count, float* policy, 
   }
   if (st) return st;
   if (pi >= 0) cudaEventRecord(n->prof_ev[2 * pi + 1], s);
-  if (n->tc_heads) return run_tc_heads(n, n->act[x], d_count, count, policy, value, s);
+  if (n->tc_heads) return run_tc_heads(n, n->act[x], d_count, count, policy, value, value_only, s);
   HeadArgs h{};
   h.act = n->act[x];
   h.C = n->C; h.S = n->S; h.P = n->P; h.A = n->A; h.Hp = n->Hp; h.Hv = n->Hv;
@@ -1342,7 +1344,9 @@ int omq_resnet_forward_queue(omq_resnet* n, omq_engine* e, int32_t queue, void* 
   launch_pack_queue(e->v, queue, n->P, n->in_pad, n->x_in, n->f16, s);
   int st = cuda_status(cudaGetLastError(), "pack queue");
   if (st) return st;
-  return resnet_run(n, e->v.q_count + queue, cap, e->v.q_policy[queue], e->v.q_value[queue], s);
+  // the final-node queue's policies are never read by the search (the reference discards them,
+  // wave_search.py:1337-1457): its forward stops after the value head
+  return resnet_run(n, e->v.q_count + queue, cap, e->v.q_policy[queue], e->v.q_value[queue], s, queue == 1);
 }
 
 int omq_resnet_profile(omq_resnet* n, int32_t capacity) {
