@@ -120,6 +120,16 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   v.noise_seed = c.noise_seed;
   v.go_superko = (c.game == OMQ_GAME_GO && c.go_superko) ? 1 : 0;
   v.go_cycle = (c.game == OMQ_GAME_GO && c.go_cycle) ? 1 : 0;
+  // few trees: several CTAs (SMs) per tree in selection and expansion (4 trees or fewer per 148 SMs
+  // get up to 8 each)
+  {
+    int sms = 148;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c.device) != cudaSuccess || sms <= 0) {
+      cudaGetLastError();
+      sms = 148;
+    }
+    v.slices = 4 * v.R <= sms ? std::max(1, std::min(8, sms / (2 * v.R))) : 1;
+  }
   const size_t R = v.R, T = v.T, W = v.WCAP, QC = R * W;
   size_t off[40], n = 0, tot = 0;
   auto take = [&](size_t bytes) { off[n++] = tot; tot += align256(bytes); };
@@ -128,7 +138,7 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   const bool chess = c.game == OMQ_GAME_CHESS;
   take(chess ? R * 101 * 80 : R * v.C * (c.game == OMQ_GAME_GO ? 8 : 1));  // 2 roots (+ history)
   take(R * sizeof(TreeHeader));               // 3 headers
-  take(R * 2 * W * sizeof(Visit));            // 4 frontier
+  take(R * v.slices * 2 * W * sizeof(Visit)); // 4 frontier (per slice)
   take(R * (size_t)v.LOGCAP * sizeof(Visit)); // 5 visit log
   take(R * W * sizeof(Visit));                // 6 leaves
   take(R * W * sizeof(int2));                 // 7 leaf_final
@@ -147,6 +157,7 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   take(c.game == OMQ_GAME_GO ? R * OMQ_GO_MAX_KEYS * sizeof(uint64_t) : 16);  // 19 Go superko keys
   take(c.game == OMQ_GAME_GO ? R * 128 * sizeof(uint32_t) : 16);              // 20 Go key filter
   take(c.game == OMQ_GAME_GOMOKU ? R * W * 128 * sizeof(int16_t) : 16);       // 21 leaf paths
+  take(R * 4 * sizeof(int32_t));                                              // 22 select counters
   void* arena = nullptr;
   cudaError_t err = cudaMalloc(&arena, tot);
   if (err != cudaSuccess) {
@@ -176,6 +187,7 @@ int omq_engine_create(const omq_engine_config* cfg, omq_engine** out) {
   v.go_keys = reinterpret_cast<uint64_t*>(b + off[19]);
   v.go_bloom = reinterpret_cast<uint32_t*>(b + off[20]);
   v.leaf_paths = reinterpret_cast<int16_t*>(b + off[21]);
+  v.sel_ctr = reinterpret_cast<int32_t*>(b + off[22]);
   err = cudaMemset(v.hdr, 0, R * sizeof(TreeHeader));
   if (err == cudaSuccess) err = cudaMemset(v.q_count, 0, 2 * sizeof(int32_t));
   if (err == cudaSuccess) err = cudaMemset(v.root_noise, 0, R * (size_t)v.A * sizeof(float));

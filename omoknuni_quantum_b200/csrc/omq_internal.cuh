@@ -141,6 +141,8 @@ struct EngineView {
   float* q_policy[2];    // [R*WCAP][A]
   float* q_value[2];     // [R*WCAP]
   int32_t* q_count;      // [2]
+  int slices;            // CTAs per tree of k_select (and of the Gomoku k_expand) when trees are few
+  int32_t* sel_ctr;      // [R][4] sliced k_select: visit-log entries, leaves, overflow, 0
 };
 
 // UCB score of a child exactly as the reference evaluates it in fp32

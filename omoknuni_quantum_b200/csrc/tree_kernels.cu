@@ -457,6 +457,9 @@ __device__ __forceinline__ void emit_child(const EngineView& v, int r, Visit* ne
   if (li < v.LOGCAP) log[li] = x; else *overflow = 1;
 }
 
+__device__ void select_finish(const EngineView& v, int r, int wave, Visit* s_leaves, int* s_scan, int* warp_tot,
+                              int nleaf, int nlog, int overflow);
+
 __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) {
   extern __shared__ unsigned char smem_raw[];
   SelectShared& sh = *reinterpret_cast<SelectShared*>(smem_raw);
@@ -468,17 +471,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
   int* s_scan = reinterpret_cast<int*>(s_leaves + v.WCAP);
 
   const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // Slices: with few trees, gridDim.y CTAs share a tree. Every slice ranks the root's children
+  // the same way; slice y emits the children of rank i with i % gridDim.y == y and then descends
+  // their subtrees alone (its own frontier; subtrees are disjoint, so no slice waits on another).
+  // The visit log and the leaves go to per-tree global counters, and k_select_commit sorts the
+  // leaves and queues the expandable ones afterwards.
+  const int slices = (int)gridDim.y, slice = (int)blockIdx.y;
   TreeHeader* H = &v.hdr[r];
   if (H->status != OMQ_OK) return;
   const size_t base = (size_t)r * v.T;
-  Visit* F[2] = {v.frontier + (size_t)r * 2 * v.WCAP, v.frontier + (size_t)r * 2 * v.WCAP + v.WCAP};
+  Visit* F[2] = {v.frontier + ((size_t)r * slices + slice) * 2 * v.WCAP,
+                 v.frontier + ((size_t)r * slices + slice) * 2 * v.WCAP + v.WCAP};
   Visit* log = v.vlog + (size_t)r * v.LOGCAP;
   unsigned long long* keys = keys_all + (size_t)warp * p2;
+  int32_t* gctr = v.sel_ctr + 4 * (size_t)r;  // sliced: {log entries, leaves, overflow, 0}
+  int* nlogp = slices > 1 ? gctr : &sh.nlog;
+  int* ovfp = slices > 1 ? gctr + 2 : &sh.overflow;
+  // whether this slice emits the root child of rank `rank` (children of other nodes: always)
+  auto owns = [&](int node, int rank) { return node != 0 || rank % slices == slice; };
 
   if (tid == 0) {
     const Visit root{0, 0, wave, 0};
     F[0][0] = root;
-    log[0] = root;
+    if (slices == 1) {
+      log[0] = root;
+    } else if (slice == 0) {
+      const int li = atomicAdd(gctr, 1);
+      if (li < v.LOGCAP) log[li] = root; else gctr[2] = 1;
+    }
     sh.cnt[0] = 1; sh.cnt[1] = 0;
     sh.nleaf = 0; sh.nlog = 1; sh.overflow = 0;
   }
@@ -512,15 +532,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
         }
       if (wave <= n) {
         for (int rr = tid; rr < wave; rr += blockDim.x)
-          emit_child(v, r, F[1], &sh.cnt[1], log, &sh.nlog, &sh.overflow, cs + key_slot(bk[rr]),
-                     rr, 1, 1);
+          if (owns(0, rr))
+            emit_child(v, r, F[1], &sh.cnt[1], log, nlogp, ovfp, cs + key_slot(bk[rr]), rr, 1, 1);
       } else {
         const int basek = wave / n, extra = wave % n;
         for (int rr = tid; rr < n; rr += blockDim.x) {
           const int c = basek + (rr < extra ? 1 : 0);
           const int off = rr * basek + (rr < extra ? rr : extra);
-          emit_child(v, r, F[1], &sh.cnt[1], log, &sh.nlog, &sh.overflow, cs + key_slot(bk[rr]),
-                     off, c, 1);
+          if (owns(0, rr))
+            emit_child(v, r, F[1], &sh.cnt[1], log, nlogp, ovfp, cs + key_slot(bk[rr]), off, c, 1);
         }
       }
       __syncthreads();
@@ -563,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
                     __shfl_sync(0xFFFFFFFFu, pe.k, t), __shfl_sync(0xFFFFFFFFu, pe.depth, t)};
       const int n = topo_count(NodeTopo{0, 0, 0, __shfl_sync(0xFFFFFFFFu, ptp.cnt_flags, t)});
       if (n == 0) {  // no children: the simulation stops here (wave_search.py:762-768)
-        if (lane == 0) {
+        if (lane == 0 && (e.node != 0 || slice == 0)) {
           int li = atomicAdd(&sh.nleaf, 1);
           if (li < v.WCAP) s_leaves[li] = e; else sh.overflow = 1;
         }
@@ -588,7 +608,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
         }
         for (int o = 16; o > 0; o >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xFFFFFFFFu, part, o));
         float* out = v.root_noise + (size_t)r * v.A;
-        for (int a = lane; a < v.A; a += 32) out[a] = 0.0f;
+        if (slice == 0)
+          for (int a = lane; a < v.A; a += 32) out[a] = 0.0f;
         __syncwarp();
 #pragma unroll
         for (int t = 0; t < 12; ++t) {
@@ -598,7 +619,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
           NodeStats st = v.stats[base + cs + j];
           st.P = __fadd_rn(__fmul_rn(v.noise_keep, st.P), __fmul_rn(v.noise_eps, noise));
           keys[j] = rank_key(ucb_score(st, np, v.c_puct, v.vl_value, v.enable_vl), j);
-          out[topo_action(v.topo[base + cs + j])] = noise;
+          if (slice == 0) out[topo_action(v.topo[base + cs + j])] = noise;
         }
       } else {
         // children statistics: the first two per lane came with the prefetch, the rest four
@@ -630,9 +651,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
       __syncwarp();
       if (regbest) {
         const unsigned long long best = warp_max_u64(lanebest);
-        if (lane == 0)
-          emit_child(v, r, F[cur ^ 1], &sh.cnt[cur ^ 1], log, &sh.nlog, &sh.overflow, cs + key_slot(best),
-                     e.lo, 1, e.depth + 1);
+        if (lane == 0 && owns(e.node, 0))
+          emit_child(v, r, F[cur ^ 1], &sh.cnt[cur ^ 1], log, nlogp, ovfp, cs + key_slot(best), e.lo, 1,
+                     e.depth + 1);
         __syncwarp();
       } else if (e.k <= n && e.k <= 8) {
         // k best children, one simulation each, by repeated arg-max
@@ -643,8 +664,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
           const int slot = key_slot(best);
           if (lane == 0) {
             keys[slot] = 0;
-            emit_child(v, r, F[cur ^ 1], &sh.cnt[cur ^ 1], log, &sh.nlog, &sh.overflow,
-                       cs + slot, e.lo + rr, 1, e.depth + 1);
+            if (owns(e.node, rr))
+              emit_child(v, r, F[cur ^ 1], &sh.cnt[cur ^ 1], log, nlogp, ovfp, cs + slot, e.lo + rr, 1,
+                         e.depth + 1);
           }
           __syncwarp();
         }
@@ -654,15 +676,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
         warp_sort_desc(keys, p2);
         if (e.k <= n) {
           for (int rr = lane; rr < e.k; rr += 32)
-            emit_child(v, r, F[cur ^ 1], &sh.cnt[cur ^ 1], log, &sh.nlog, &sh.overflow,
-                       cs + key_slot(keys[rr]), e.lo + rr, 1, e.depth + 1);
+            if (owns(e.node, rr))
+              emit_child(v, r, F[cur ^ 1], &sh.cnt[cur ^ 1], log, nlogp, ovfp, cs + key_slot(keys[rr]),
+                         e.lo + rr, 1, e.depth + 1);
         } else {
           const int basek = e.k / n, extra = e.k % n;
           for (int rr = lane; rr < n; rr += 32) {
             const int c = basek + (rr < extra ? 1 : 0);
             const int off = rr * basek + (rr < extra ? rr : extra);
-            emit_child(v, r, F[cur ^ 1], &sh.cnt[cur ^ 1], log, &sh.nlog, &sh.overflow,
-                       cs + key_slot(keys[rr]), e.lo + off, c, e.depth + 1);
+            if (owns(e.node, rr))
+              emit_child(v, r, F[cur ^ 1], &sh.cnt[cur ^ 1], log, nlogp, ovfp, cs + key_slot(keys[rr]),
+                         e.lo + off, c, e.depth + 1);
           }
         }
       }
@@ -676,11 +700,38 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
   }
   // depth limit reached: the remaining simulations stop at nodes that still have children
   for (int i = tid; i < sh.cnt[cur]; i += blockDim.x) {
+    if (F[cur][i].node == 0 && slice != 0) continue;  // the root: slice 0's
     int li = atomicAdd(&sh.nleaf, 1);
     if (li < v.WCAP) s_leaves[li] = F[cur][i]; else sh.overflow = 1;
   }
   __syncthreads();
-  const int nleaf = min(sh.nleaf, v.WCAP);
+  if (slices > 1) {
+    // this slice's leaves into the tree's (unsorted) leaf list; k_select_commit finishes
+    __shared__ int s_off;
+    const int nl = min(sh.nleaf, v.WCAP);
+    if (tid == 0) {
+      s_off = atomicAdd(gctr + 1, nl);
+      if (sh.overflow) gctr[2] = 1;
+    }
+    __syncthreads();
+    Visit* gl = v.leaves + (size_t)r * v.WCAP;
+    for (int i = tid; i < nl; i += blockDim.x) {
+      if (s_off + i < v.WCAP) gl[s_off + i] = s_leaves[i];
+      else gctr[2] = 1;
+    }
+    return;
+  }
+  select_finish(v, r, wave, s_leaves, s_scan, sh.warp_tot, min(sh.nleaf, v.WCAP), sh.nlog, sh.overflow);
+}
+
+// Selection's end for tree r: sort its leaves (s_leaves, in shared memory) ascending by node id into
+// v.leaves, flag the expandable ones, reserve their expansion-queue entries, and set the header's
+// wave fields. Block-collective.
+__device__ void select_finish(const EngineView& v, int r, int wave, Visit* s_leaves, int* s_scan, int* warp_tot,
+                              int nleaf, int nlog, int overflow) {
+  const int tid = threadIdx.x;
+  TreeHeader* H = &v.hdr[r];
+  const size_t base = (size_t)r * v.T;
   // sort leaves ascending by node id (each node is a leaf at most once per wave)
   Visit* gleaves = v.leaves + (size_t)r * v.WCAP;
   for (int i = tid; i < nleaf; i += blockDim.x) {
@@ -700,7 +751,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
   int2* lf = v.leaf_final + (size_t)r * v.WCAP;
   for (int i = tid; i < nleaf; i += blockDim.x) lf[i] = make_int2(-1, s_scan[i]);
   __syncthreads();
-  const int nexp = block_exclusive_scan(s_scan, nleaf, sh.warp_tot);
+  const int nexp = block_exclusive_scan(s_scan, nleaf, warp_tot);
   __shared__ int s_qbase;
   if (tid == 0) s_qbase = nexp > 0 ? atomicAdd(&v.q_count[0], nexp) : 0;
   __syncthreads();
@@ -716,13 +767,30 @@ __global__ void __launch_bounds__(kThreads, 1) k_select(EngineView v, int wave) 
   }
   if (tid == 0) {
     H->nleaves = nleaf;
-    H->nlog = min(sh.nlog, v.LOGCAP);
+    H->nlog = min(nlog, v.LOGCAP);
     H->exp_off = qbase;
     H->exp_cnt = nexp;
     H->wave = wave;
     H->wave_idx += 1;
-    if (sh.overflow) H->status = OMQ_QUEUE_OVERFLOW;
+    if (overflow) H->status = OMQ_QUEUE_OVERFLOW;
   }
+}
+
+// The end of a sliced k_select: the tree's leaves (from every slice) into shared memory, then
+// select_finish. Dynamic shared memory: WCAP leaves and WCAP ints.
+__global__ void __launch_bounds__(kThreads) k_select_commit(EngineView v, int wave) {
+  extern __shared__ unsigned char commit_smem[];
+  Visit* s_leaves = reinterpret_cast<Visit*>(commit_smem);
+  int* s_scan = reinterpret_cast<int*>(s_leaves + v.WCAP);
+  __shared__ int warp_tot[kWarps + 1];
+  const int r = blockIdx.x, tid = threadIdx.x;
+  if (v.hdr[r].status != OMQ_OK) return;
+  const int32_t* gctr = v.sel_ctr + 4 * (size_t)r;
+  const int nleaf = min(gctr[1], v.WCAP);
+  const Visit* gl = v.leaves + (size_t)r * v.WCAP;
+  for (int i = tid; i < nleaf; i += blockDim.x) s_leaves[i] = gl[i];
+  __syncthreads();
+  select_finish(v, r, wave, s_leaves, s_scan, warp_tot, nleaf, gctr[0], gctr[2]);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -1261,8 +1329,15 @@ void launch_select(const EngineView& v, int wave, cudaStream_t s) {
   if (sm > 48 * 1024)
     cudaFuncSetAttribute(k_select, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   cudaMemsetAsync(v.q_count, 0, sizeof(int32_t), s);
+  if (v.slices > 1) cudaMemsetAsync(v.sel_ctr, 0, (size_t)v.R * 4 * sizeof(int32_t), s);
   count_launches(1);
-  k_select<<<v.R, tree_threads(v), sm, s>>>(v, wave);
+  k_select<<<dim3(v.R, v.slices), tree_threads(v), sm, s>>>(v, wave);
+  if (v.slices > 1) {
+    const int csm = (int)((size_t)v.WCAP * (sizeof(Visit) + sizeof(int)));
+    if (csm > 48 * 1024) cudaFuncSetAttribute(k_select_commit, cudaFuncAttributeMaxDynamicSharedMemorySize, csm);
+    count_launches(1);
+    k_select_commit<<<v.R, tree_threads(v), csm, s>>>(v, wave);
+  }
 }
 
 void launch_expand(const EngineView& v, int root_mode, cudaStream_t s) {
@@ -1275,9 +1350,8 @@ void launch_expand(const EngineView& v, int root_mode, cudaStream_t s) {
   const int sm = (int)((threads / 32) * (sizeof(ExpandWarpSmem) + extra));
   cudaFuncSetAttribute(k_expand, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
   // few Gomoku trees: several CTAs (SMs) per tree, one leaf per warp at a full wave
-  const int sm_count = device_sms();
-  const int slices = (v.game == OMQ_GAME_GOMOKU && 4 * v.R <= sm_count)
-                         ? max(1, min(8, min(sm_count / (2 * v.R), (v.WCAP + threads / 32 - 1) / (threads / 32))))
+  const int slices = v.game == OMQ_GAME_GOMOKU
+                         ? max(1, min(v.slices, (v.WCAP + threads / 32 - 1) / (threads / 32)))
                          : 1;
   k_expand<<<dim3(v.R, slices), threads, sm, s>>>(v, root_mode);
   if (slices > 1) {
