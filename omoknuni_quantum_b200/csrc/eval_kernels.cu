@@ -136,21 +136,22 @@ __device__ void synth_emit(const EngineView& v, int queue, int q, uint64_t h, co
   }
 }
 
-// Positions per warp in k_synth: the boards are rebuilt one after another by the whole warp, then
-// lane i runs position i's hash chain (a serial chain per position), then the policies are
-// emitted one position at a time.
+// Positions per warp in k_synth (at most): the boards are rebuilt one after another by the whole
+// warp, then lane i runs position i's hash chain (a serial chain per position), then the policies
+// are emitted one position at a time. Small queues take fewer per warp (`group`), so that more
+// warps share the work; every position's result is the same either way.
 constexpr int kSynthGroup = 8;
 
-__global__ void __launch_bounds__(kSynthWarps * 32) k_synth(EngineView v, int queue) {
+__global__ void __launch_bounds__(kSynthWarps * 32) k_synth(EngineView v, int queue, int group) {
   __shared__ WarpPos wps[kSynthWarps];
   __shared__ uint64_t gwords[kSynthWarps][kSynthGroup][kMaxWords];  // occupancy bit boards
   __shared__ int gmeta[kSynthWarps][kSynthGroup][4];                 // player, move count, depth, last
   __shared__ uint64_t ghash[kSynthWarps][kSynthGroup];
   const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
-  const int q0 = (blockIdx.x * kSynthWarps + wl) * kSynthGroup;
+  const int q0 = (blockIdx.x * kSynthWarps + wl) * group;
   const int count = v.q_count[queue];
   if (q0 >= count) return;
-  const int ng = min(kSynthGroup, count - q0);
+  const int ng = min(group, count - q0);
   WarpPos& wp = wps[wl];
   const int nwords = (v.C + 63) / 64;
   for (int i = 0; i < ng; ++i) {
@@ -506,8 +507,16 @@ void launch_synth_eval(const EngineView& v, int queue, cudaStream_t s) {
     k_synth_chess<<<(cap + kChessWarps - 1) / kChessWarps, kChessWarps * 32, 0, s>>>(v, queue);
     return;
   }
-  const int per_block = kSynthWarps * kSynthGroup;
-  k_synth<<<(cap + per_block - 1) / per_block, kSynthWarps * 32, 0, s>>>(v, queue);
+  // 8 positions per warp once the queue's capacity fills the SMs with such warps, fewer below
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+    cudaGetLastError();
+    sms = 148;
+  }
+  const int group = max(1, min(kSynthGroup, cap / (sms * 2 * kSynthWarps)));
+  const int per_block = kSynthWarps * group;
+  k_synth<<<(cap + per_block - 1) / per_block, kSynthWarps * 32, 0, s>>>(v, queue, group);
 }
 
 void launch_features(const EngineView& v, int queue, float* out, cudaStream_t s) {
