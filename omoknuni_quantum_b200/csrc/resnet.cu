@@ -337,6 +337,313 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------------
+// Whole trunk in one launch, for boards whose padded grid is exactly one 256-pixel tile (15x15)
+// with 128 filters: a tile is a whole position, so every layer of a position depends only on the
+// previous layer of the same position, and one CTA can run all 1 + 2 NB convs of its positions
+// with no other CTA involved. Each CTA keeps two positions in flight in the two TMEM accumulators
+// (items alternate position A layer l, position B layer l, A layer l+1, ...): while the MMAs of B
+// run, the epilogue of A drains and stores, and A's next layer starts once those stores have
+// completed (the per-slot `stored` barrier, which the TMA producer waits on before loading A's
+// next halo). The layers' activations live in a per-CTA scratch of 3 buffers x 2 slots (64 KB
+// per buffer and slot, L2-resident and rewritten in place) instead of three full-batch buffers:
+// only the input features and the trunk's output cross DRAM. Same MMAs, same epilogue arithmetic
+// and the same K order as the layer-by-layer kernel, so the results are identical to it.
+// ---------------------------------------------------------------------------------------------
+struct TrunkArgs {
+  const float* bias;       // [1 + 2 NB][128]
+  const h16* scratch;      // [3][nslots][256][128] (residual reads; writes go through tmSo)
+  const int32_t* d_count;
+  int32_t count;
+  int32_t layers;          // 1 + 2 NB
+  int32_t cb_in;           // 64-channel blocks of the input (1 or 2)
+  int32_t nslots;          // 2 x gridDim.x
+  int32_t* error;
+};
+
+// Scratch buffer (0..2) read by layer l >= 1 as its input, or as its residual (conv2 layers), and
+// written as its output. Block i = (l - 1) / 2 starts from buffer (2 i) % 3; conv1 writes the next
+// buffer, conv2 the one after (the rotation of the layer-by-layer forward).
+__device__ __forceinline__ int trunk_in_buf(int l) { const int x = (2 * ((l - 1) >> 1)) % 3; return (l & 1) ? x : (x + 1) % 3; }
+__device__ __forceinline__ int trunk_out_buf(int l) {
+  if (l == 0) return 0;
+  const int x = (2 * ((l - 1) >> 1)) % 3;
+  return (l & 1) ? (x + 1) % 3 : (x + 2) % 3;
+}
+__device__ __forceinline__ int trunk_res_buf(int l) { return (2 * ((l - 1) >> 1)) % 3; }
+
+template <bool F16>
+__global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
+    k_trunk_t(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ CUtensorMap tmWin,
+              const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmS,
+              const __grid_constant__ CUtensorMap tmSo, const __grid_constant__ CUtensorMap tmOut,
+              TrunkArgs args) {
+  using Cfg = HaloTCfg;
+  constexpr int C = 128, kP = 256, kStride = 16, kN = kP - kStride;  // 240 pixel columns per UMMA
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* x_ring = smem;
+  uint8_t* w_ring = smem + Cfg::kXStages * Cfg::kX;
+  uint8_t* staging = w_ring + Cfg::kWStages * Cfg::kW;
+  uint64_t* xfull = reinterpret_cast<uint64_t*>(staging + Cfg::kStaging);
+  uint64_t* xempty = xfull + Cfg::kXStages;
+  uint64_t* wfull = xempty + Cfg::kXStages;
+  uint64_t* wempty = wfull + Cfg::kWStages;
+  uint64_t* tfull = wempty + Cfg::kWStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* stored = tempty + 2;  // [2] per slot: the item's output stores have completed
+  uint64_t* drain = stored + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kXStages; ++s) { ptx::mbar_init(&xfull[s], 1); ptx::mbar_init(&xempty[s], 1); }
+    for (int s = 0; s < Cfg::kWStages; ++s) { ptx::mbar_init(&wfull[s], 1); ptx::mbar_init(&wempty[s], 1); }
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(&tfull[i], 1);
+      ptx::mbar_init(&tempty[i], Cfg::kEpiWarps);
+      ptx::mbar_init(&stored[i], Cfg::kEpiWarps);
+    }
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    ptx::fence_barrier_init();
+    ptx::prefetch_tmap(&tmIn);
+    ptx::prefetch_tmap(&tmWin);
+    ptx::prefetch_tmap(&tmW);
+    ptx::prefetch_tmap(&tmS);
+    ptx::prefetch_tmap(&tmSo);
+    ptx::prefetch_tmap(&tmOut);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  ptx::griddep_wait();
+  const int n_pos = args.d_count ? min(*args.d_count, args.count) : args.count;
+  // this CTA's positions: blockIdx.x + k * gridDim.x, k = 0 .. mine - 1, in pairs (2m, 2m + 1)
+  const int mine = n_pos > (int)blockIdx.x ? (n_pos - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+  const int L = args.layers;
+  // the item sequence every role walks: pair m, layer l, position k = 2m + j of the pair
+#define OMQ_TRUNK_ITEMS(...)                                            \
+  for (int m = 0; 2 * m < mine; ++m)                                    \
+    for (int l = 0; l < L; ++l)                                         \
+      for (int j = 0; j < 2 && 2 * m + j < mine; ++j) {                 \
+        const int k = 2 * m + j;                                        \
+        const int pos = (int)blockIdx.x + k * (int)gridDim.x;           \
+        const int sl = j, slot = 2 * (int)blockIdx.x + j;               \
+        __VA_ARGS__                                                     \
+      }
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    int sx = 0, sw = 0;
+    uint32_t px = 0, pw = 0;
+    int x_issued[Cfg::kXStages], w_issued[Cfg::kWStages];
+    for (int i = 0; i < Cfg::kXStages; ++i) x_issued[i] = -1;
+    for (int i = 0; i < Cfg::kWStages; ++i) w_issued[i] = -1;
+    int done_items[2] = {0, 0};  // items of each slot issued so far
+    bool ok = true;
+    OMQ_TRUNK_ITEMS({
+      if (ok) {
+        // the previous item of this slot (its previous layer, or the previous position's last
+        // one) must have stored its output before this item's input loads or output stores
+        if (done_items[sl] > 0) {
+          if (!ptx::mbar_wait(&stored[sl], (uint32_t)((done_items[sl] - 1) & 1), abort_flag, kWaitLimitNs)) ok = false;
+          ptx::fence_proxy_async_global();
+        }
+        ++done_items[sl];
+        const int CB = l == 0 ? args.cb_in : C / kBlockK;
+        const int h0 = l == 0 ? pos * kP - Cfg::kLead : (trunk_in_buf(l) * args.nslots + slot) * kP - Cfg::kLead;
+        const CUtensorMap* hm = l == 0 ? &tmIn : &tmS;
+        const CUtensorMap* wm = l == 0 ? &tmWin : &tmW;
+        const int wrow = l == 0 ? 0 : (l - 1) * C;
+        for (int cb = 0; cb < CB && ok; ++cb) {
+          if (!ptx::mbar_wait(&xempty[sx], px ^ 1, abort_flag, kWaitLimitNs)) { ok = false; break; }
+          ptx::mbar_arrive_expect_tx(&xfull[sx], Cfg::kX);
+          uint8_t* dst = x_ring + sx * Cfg::kX;
+          ptx::tma_load_2d(dst, hm, &xfull[sx], cb * kBlockK, h0);
+          ptx::tma_load_2d(dst + Cfg::kHaloBox * 128, hm, &xfull[sx], cb * kBlockK, h0 + Cfg::kHaloBox);
+          x_issued[sx] = (int)px;
+          if (++sx == Cfg::kXStages) { sx = 0; px ^= 1; }
+          for (int tap = 0; tap < 9; ++tap) {
+            if (!ptx::mbar_wait(&wempty[sw], pw ^ 1, abort_flag, kWaitLimitNs)) { ok = false; break; }
+            ptx::mbar_arrive_expect_tx(&wfull[sw], Cfg::kW);
+            ptx::tma_load_2d(w_ring + sw * Cfg::kW, wm, &wfull[sw], (tap * CB + cb) * kBlockK, wrow);
+            w_issued[sw] = (int)pw;
+            if (++sw == Cfg::kWStages) { sw = 0; pw ^= 1; }
+          }
+        }
+      }
+    })
+    for (int i = 0; i < Cfg::kXStages; ++i)
+      if (x_issued[i] >= 0) {
+        volatile int dummy = 0;
+        ptx::mbar_wait(&xfull[i], (uint32_t)x_issued[i], &dummy, kWaitLimitNs);
+      }
+    for (int i = 0; i < Cfg::kWStages; ++i)
+      if (w_issued[i] >= 0) {
+        volatile int dummy = 0;
+        ptx::mbar_wait(&wfull[i], (uint32_t)w_issued[i], &dummy, kWaitLimitNs);
+      }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    const uint32_t idesc = ptx::idesc_f16_f32(C, kN, F16);
+    const uint64_t w_desc0 = ptx::smem_desc_sw128(ptx::smem_u32(w_ring));
+    int sx = 0, sw = 0;
+    uint32_t px = 0, pw = 0;
+    bool any = false, ok = true;
+    int t = 0;
+    OMQ_TRUNK_ITEMS({
+      if (ok) {
+        (void)pos; (void)sl; (void)slot;
+        const int ab = t & 1;
+        const uint32_t aph = (t >> 1) & 1;
+        ++t;
+        if (!ptx::mbar_wait(&tempty[ab], aph ^ 1, abort_flag, kWaitLimitNs)) ok = false;
+        ptx::tc_fence_after();
+        const uint32_t d = tmem + ab * Cfg::kRows;
+        const int CB = l == 0 ? args.cb_in : C / kBlockK;
+        for (int cb = 0; cb < CB && ok; ++cb) {
+          if (!ptx::mbar_wait(&xfull[sx], px, abort_flag, kWaitLimitNs)) { ok = false; break; }
+          ptx::tc_fence_after();
+          const uint64_t x_desc0 = ptx::smem_desc_sw128(ptx::smem_u32(x_ring + sx * Cfg::kX));
+#pragma unroll
+          for (int tap = 0; tap < 9; ++tap) {
+            if (!ptx::mbar_wait(&wfull[sw], pw, abort_flag, kWaitLimitNs)) { ok = false; break; }
+            ptx::tc_fence_after();
+            const int off = Cfg::kLead + (tap / 3 - 1) * kStride + (tap % 3 - 1);
+            const uint64_t xd = x_desc0 + (uint64_t)(off * 8);
+            const uint64_t wd = w_desc0 + (uint64_t)(sw * (Cfg::kW >> 4));
+            ptx::mma_f16(d, wd, xd, idesc, (cb | tap) != 0);
+#pragma unroll
+            for (int kk = 1; kk < kBlockK / 16; ++kk) ptx::mma_f16(d, wd + 2 * kk, xd + 2 * kk, idesc, 1u);
+            any = true;
+            ptx::mma_commit(&wempty[sw]);
+            if (++sw == Cfg::kWStages) { sw = 0; pw ^= 1; }
+          }
+          if (!ok) break;
+          ptx::mma_commit(&xempty[sx]);
+          if (++sx == Cfg::kXStages) { sx = 0; px ^= 1; }
+        }
+        if (ok) ptx::mma_commit(&tfull[ab]);
+      }
+    })
+    if (any) {
+      ptx::mma_commit(drain);
+      volatile int dummy = 0;
+      ptx::mbar_wait(drain, 0, &dummy, kWaitLimitNs);
+    }
+  } else if (warp >= 2) {
+    // ---------------- epilogue (as in k_conv3x3_halo_t) ----------------
+    const int q = warp & 3;
+    const int wq = (warp - 2) >> 2;
+    uint8_t* my_stage = staging + (warp - 2) * Cfg::kStagePerWarp;
+    float* tr = reinterpret_cast<float*>(my_stage + Cfg::kStoreBufs * 2048);
+    int buf = 0, t = 0;
+    bool ok = true;
+    OMQ_TRUNK_ITEMS({
+      if (ok) {
+        const int ch0 = q * 32;
+        const float bias = args.bias[(size_t)l * C + ch0 + lane];
+        const int ab = t & 1;
+        const uint32_t aph = (t >> 1) & 1;
+        ++t;
+        if (!ptx::mbar_wait(&tfull[ab], aph, abort_flag, kWaitLimitNs)) ok = false;
+        ptx::tc_fence_after();
+        const bool last = l == L - 1;
+        const CUtensorMap* om = last ? &tmOut : &tmSo;
+        const int orow0 = last ? pos * kP : (trunk_out_buf(l) * args.nslots + slot) * kP;
+        const h16* res = (l >= 2 && !(l & 1))
+                             ? args.scratch + ((size_t)(trunk_res_buf(l) * args.nslots + slot) * kP) * C
+                             : nullptr;
+#pragma unroll 1
+        for (int jj = wq; ok && jj < Cfg::kRows / 32; jj += Cfg::kEpiWarps / 4) {
+          uint32_t r[32];
+          ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + ab * Cfg::kRows + jj * 32, r);
+          ptx::tmem_ld_wait();
+          __syncwarp();
+#pragma unroll
+          for (int pp = 0; pp < 32; ++pp)
+            tr[pp * 32 + (((lane >> 2) ^ (pp & 7)) << 2) + (lane & 3)] = __uint_as_float(r[pp]) + bias;
+          __syncwarp();
+          const int pix = jj * 32 + lane;
+          const int y = pix / kStride, x = pix - y * kStride;
+          const bool pad = (y == kStride - 1) || (x == kStride - 1);
+          uint4 packed[4];
+          uint32_t* pwd = reinterpret_cast<uint32_t*>(packed);
+          if (pad) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pwd[i] = 0u;
+          } else {
+            float v[32];
+#pragma unroll
+            for (int c4 = 0; c4 < 8; ++c4) {
+              const float4 f = *reinterpret_cast<const float4*>(tr + lane * 32 + ((c4 ^ (lane & 7)) << 2));
+              v[4 * c4] = f.x; v[4 * c4 + 1] = f.y; v[4 * c4 + 2] = f.z; v[4 * c4 + 3] = f.w;
+            }
+            if (res) {
+              // written by this CTA's TMA stores two items earlier: read from L2, never from a
+              // possibly stale L1 line of an earlier position in the same slot
+              const uint4* rp = reinterpret_cast<const uint4*>(res + (size_t)pix * C + ch0);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const uint4 u = __ldcg(rp + i);
+                const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 f = unpack2_h16<F16>(uw[e]);
+                  v[8 * i + 2 * e] += f.x;
+                  v[8 * i + 2 * e + 1] += f.y;
+                }
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) pwd[i / 2] = pack2_h16<F16>(fmaxf(v[i], 0.0f), fmaxf(v[i + 1], 0.0f));
+          }
+          if (lane == 0) ptx::bulk_wait_read<Cfg::kStoreBufs - 1>();
+          __syncwarp();
+          uint8_t* sbuf = my_stage + buf * 2048;
+          const int swz = (lane >> 1) & 3;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(sbuf + lane * 64 + ((i ^ swz) * 16)) = packed[i];
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            ptx::tma_store_2d(om, sbuf, ch0, orow0 + jj * 32);
+            ptx::bulk_commit();
+          }
+          if (++buf == Cfg::kStoreBufs) buf = 0;
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          ptx::mbar_arrive(&tempty[ab]);
+          // the item's stores complete (written, not only read from shared memory) before the
+          // producer may load them as the next layer's input
+          ptx::bulk_wait<0>();
+          ptx::fence_proxy_async_global();
+          ptx::mbar_arrive(&stored[sl]);
+        }
+        __syncwarp();
+      }
+    })
+    if (lane == 0) ptx::bulk_wait<0>();
+  }
+#undef OMQ_TRUNK_ITEMS
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(args.error, OMQ_TIMEOUT);
+}
+
+// ---------------------------------------------------------------------------------------------
 // input packing: reference fp32 features [n][planes][S][S] -> bf16 or fp16 [n][P][in_pad] padded
 // pixel space
 // ---------------------------------------------------------------------------------------------
@@ -834,6 +1141,12 @@ struct omq_resnet {
   int k1p, k3p, n1pad, n2pad, n3pad, nt3;  // padded K of fc1 policy / fc1 value, padded rows
   h16 *pin, *vin, *hid, *w1b, *w2b, *w3b;
   CUtensorMap tm_pin, tm_vin, tm_hid, tm_w1, tm_w1h, tm_w2, tm_w3;  // tm_w1h: 128-row boxes
+  // whole-trunk kernel (15x15 boards, 128 filters): per-CTA scratch [3][tslots][256][128] and its
+  // maps, and all residual blocks' weights as one [2 NB x 128][9 x 128] matrix
+  int fused;
+  int tslots;
+  h16* tscratch;
+  CUtensorMap tmS, tmSo, tmWall;
   bool f16;                // 16-bit storage is fp16 (OMQ_DTYPE_F16), else bf16
   // optional timing of the conv trunk of each forward call (CUDA events on the caller's stream)
   int prof_cap, prof_n;
@@ -918,6 +1231,12 @@ static int build_maps(omq_resnet* n) {
   const h16* wb = n->conv_w + (size_t)n->C * 9 * n->in_pad;
   for (int i = 0; st == OMQ_OK && i < 2 * n->NB; ++i)
     st = make_map(&n->tmB[i], wb + (size_t)i * n->C * 9 * n->C, 9 * n->C, n->C, b_rows, n->f16);
+  if (st == OMQ_OK && n->fused && n->tscratch) {
+    const uint64_t srows = (uint64_t)3 * n->tslots * n->P;
+    st = make_map(&n->tmS, n->tscratch, n->C, srows, a_rows, n->f16);
+    if (st == OMQ_OK) st = make_out_map(&n->tmSo, n->tscratch, n->C, srows, n->f16);
+    if (st == OMQ_OK) st = make_map(&n->tmWall, wb, 9 * n->C, (uint64_t)2 * n->NB * n->C, b_rows, n->f16);
+  }
   if (st == OMQ_OK && n->tc_heads) {
     st = make_map(&n->tm_pin, n->pin, n->k1p, n->max_batch, 128, n->f16);
     if (st == OMQ_OK) st = make_map(&n->tm_vin, n->vin, n->k3p, n->max_batch, 128, n->f16);
@@ -1018,6 +1337,9 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
   take(n->tc_heads ? (size_t)n->n1pad * n->k1p * 2 : 16);        // 11 W1
   take(n->tc_heads ? (size_t)n->n2pad * n->Hp * 2 : 16);         // 12 W2
   take(n->tc_heads ? (size_t)n->n3pad * n->k3p * 2 : 16);        // 13 W3
+  n->fused = (n->P == HaloTCfg::kRows && n->C == 128 && n->NB >= 1 && n->sm_count > 0) ? 1 : 0;
+  n->tslots = n->fused ? 2 * n->sm_count : 0;
+  take(n->fused ? (size_t)3 * n->tslots * n->P * n->C * 2 : 16);  // 14 trunk scratch
   void* arena = nullptr;
   cudaError_t e = cudaMalloc(&arena, tot);
   if (e != cudaSuccess) { delete n; return cuda_status(e, "cudaMalloc(resnet)"); }
@@ -1036,6 +1358,7 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
   n->w1b = reinterpret_cast<h16*>(b + off[11]);
   n->w2b = reinterpret_cast<h16*>(b + off[12]);
   n->w3b = reinterpret_cast<h16*>(b + off[13]);
+  n->tscratch = n->fused ? reinterpret_cast<h16*>(b + off[14]) : nullptr;
   cudaMemset(n->error, 0, 16);
   // activations start zeroed so that never-written padding rows read as zeros
   cudaMemset(b + off[3], 0, tot - off[3]);
@@ -1145,6 +1468,37 @@ static int launch_conv_halo_tr(const omq_resnet* n, const CUtensorMap& tH, const
   return cuda_status(cudaLaunchKernelEx(&cfg, k_conv3x3_halo_t<F16>, tH, tB, tO, a), "k_conv3x3_halo_t");
 }
 
+template <bool F16>
+static int launch_trunk_t(const omq_resnet* n, const TrunkArgs& a, cudaStream_t s) {
+  static std::atomic<uint64_t> attr_set{0};
+  {
+    const cudaError_t e = set_smem_attr_once(attr_set, k_trunk_t<F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             HaloTCfg::kSmem);
+    if (e != cudaSuccess) return cuda_status(e, "trunk kernel smem attribute");
+  }
+  count_launches(1);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n->sm_count);
+  cfg.blockDim = dim3(HaloTCfg::kThreads);
+  cfg.dynamicSmemBytes = HaloTCfg::kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, k_trunk_t<F16>, n->tmA_in, n->tmB_in, n->tmWall, n->tmS, n->tmSo,
+                                        n->tmO[0], a),
+                     "k_trunk_t");
+}
+
+// The whole trunk in one launch (k_trunk_t); the output lands in act[0].
+static int trunk(const omq_resnet* n, const int32_t* d_count, int count, cudaStream_t s) {
+  TrunkArgs a{n->conv_b, n->tscratch, d_count, count, 1 + 2 * n->NB, n->in_pad / kBlockK, 2 * n->sm_count,
+              n->error};
+  return n->f16 ? launch_trunk_t<true>(n, a, s) : launch_trunk_t<false>(n, a, s);
+}
+
 static int conv(const omq_resnet* n, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tO,
                 const float* bias,
                 const h16* res, h16* out, int kb_per_tap, const int32_t* d_count,
@@ -1241,10 +1595,15 @@ int resnet_run(omq_resnet* n, const int32_t* d_count, int count, float* policy, 
       n->prof_host_counts[pi] = count;
     cudaEventRecord(n->prof_ev[2 * pi], s);
   }
-  int st = conv(n, n->tmA_in, n->tmB_in, n->tmO[0], n->conv_b, nullptr, n->act[0], n->in_pad / kBlockK,
-                d_count, count, s);
+  int st = OMQ_OK;
   int x = 0;
-  for (int i = 0; st == OMQ_OK && i < n->NB; ++i) {
+  if (n->fused && n->tscratch) {
+    st = trunk(n, d_count, count, s);  // output in act[0]
+  } else {
+    st = conv(n, n->tmA_in, n->tmB_in, n->tmO[0], n->conv_b, nullptr, n->act[0], n->in_pad / kBlockK,
+              d_count, count, s);
+  }
+  for (int i = 0; !(n->fused && n->tscratch) && st == OMQ_OK && i < n->NB; ++i) {
     const int t = (x + 1) % 3, y = (x + 2) % 3;
     st = conv(n, n->tmA[x], n->tmB[2 * i], n->tmO[t], n->conv_b + (size_t)(1 + 2 * i) * n->C, nullptr,
               n->act[t], n->C / kBlockK, d_count, count, s);

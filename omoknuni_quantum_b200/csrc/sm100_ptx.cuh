@@ -187,6 +187,11 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                "r"(x), "r"(y), "r"(smem_u32(src))
                : "memory");
 }
+// Orders this thread's completed async-proxy global accesses (TMA stores) with its later
+// generic-proxy synchronisation, and generic synchronisation with later async-proxy accesses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void bulk_wait_read() {
