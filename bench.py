@@ -422,12 +422,19 @@ def run_b200(args):
     avg_launch_s = float(trunk_ms.sum()) / 1000.0 / max(1, conv_launches)
     achieved = (flops / max(1, conv_launches)) / avg_launch_s / 1e12 if avg_launch_s > 0 else 0.0
     peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
-    traffic_per_pos = profile_value("conv3x3_resnet10x128.md", "dram_bytes_per_position_per_launch")
+    fused = ev.fused_trunk
+    # DRAM bytes per position per launch from the committed ncu capture of the kernel that ran
+    traffic_per_pos = (profile_value("trunk_resnet10x128.md", "dram_bytes_per_position_per_launch") if fused
+                       else profile_value("conv3x3_resnet10x128.md", "dram_bytes_per_position_per_launch"))
     traffic = None
-    if traffic_per_pos is not None and conv_launches:
-        traffic = traffic_per_pos * positions / len(trunk_ms)
-    roofline = {"kernel": "k_conv3x3_halo_t (tcgen05 implicit-GEMM 3x3 conv, 128 ch x 256 px UMMAs over one halo "
-                          "load per channel block)",
+    if traffic_per_pos is not None and len(trunk_ms):
+        traffic = traffic_per_pos * positions / len(trunk_ms)  # every launch covers all of a call's positions
+    kernel_name = ("k_trunk_t (the whole 21-conv trunk per launch: every conv of a position in one CTA, tcgen05 "
+                   "128 ch x 240 px UMMAs over one halo load per channel block, activations in an L2-resident "
+                   "per-CTA scratch)" if fused else
+                   "k_conv3x3_halo_t (tcgen05 implicit-GEMM 3x3 conv, 128 ch x 256 px UMMAs over one halo "
+                   "load per channel block)")
+    roofline = {"kernel": kernel_name,
                 "bound": "tensor",
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_kind": f"bf16_tflops_sustained of {peak_kind}", "traffic": traffic,

@@ -310,6 +310,10 @@ enum { OMQ_DTYPE_BF16 = 0, OMQ_DTYPE_F16 = 1 };
 OMQ_API int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out);
 OMQ_API int omq_resnet_destroy(omq_resnet* net);
 OMQ_API int omq_resnet_memory(const omq_resnet* net, uint64_t* h_bytes);
+/* Kernel launches of the convolution trunk per forward call: 1 when the whole trunk runs as one
+ * kernel (15x15 boards with 128 filters: every conv of a position in one CTA), else 1 + 2 x
+ * num_blocks (one per conv). */
+OMQ_API int omq_resnet_trunk_launches(const omq_resnet* net, int32_t* h_launches);
 /* Element counts of the three packed parameter blobs omq_resnet_load expects:
  *  conv_w (16-bit, the config's dtype): input conv [F][9][Cin_pad] (input channels zero-padded to 64, or to 128 for
  *                 more than 64 planes), then per block

@@ -107,6 +107,7 @@ SIGNATURES = {
     "omq_resnet_create": [ctypes.POINTER(ResNetConfig), ctypes.POINTER(_P)],
     "omq_resnet_destroy": [_P],
     "omq_resnet_memory": [_P, ctypes.POINTER(ctypes.c_uint64)],
+    "omq_resnet_trunk_launches": [_P, ctypes.POINTER(ctypes.c_int32)],
     "omq_resnet_param_sizes": [_P, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
                                ctypes.POINTER(ctypes.c_uint64)],
     "omq_resnet_load": [_P, _P, _P, _P, _P],

@@ -1431,6 +1431,12 @@ int omq_resnet_load(omq_resnet* n, const uint16_t* d_conv_w, const float* d_conv
   return OMQ_OK;
 }
 
+int omq_resnet_trunk_launches(const omq_resnet* n, int32_t* launches) {
+  if (!n || !launches) { set_error("null argument"); return OMQ_BAD_ARG; }
+  *launches = (n->fused && n->tscratch) ? 1 : 1 + 2 * n->NB;
+  return OMQ_OK;
+}
+
 int omq_resnet_memory(const omq_resnet* n, uint64_t* bytes) {
   if (!n || !bytes) { set_error("null argument"); return OMQ_BAD_ARG; }
   *bytes = n->bytes;

@@ -291,7 +291,15 @@ class ResNetEvaluator:
 
     @property
     def conv_launches_per_call(self) -> int:
-        return 1 + 2 * self.spec.num_blocks
+        """Trunk kernel launches per forward: 1 for the whole-trunk kernel (15x15 boards, 128
+        filters), else one per conv."""
+        n = ctypes.c_int32()
+        _lib.check(self.L.omq_resnet_trunk_launches(self._net, ctypes.byref(n)), "omq_resnet_trunk_launches")
+        return int(n.value)
+
+    @property
+    def fused_trunk(self) -> bool:
+        return self.conv_launches_per_call == 1
 
     def trunk_flops_per_position(self) -> int:
         s = self.spec
