@@ -448,6 +448,7 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
     for (int i = 0; i < Cfg::kWStages; ++i) w_issued[i] = -1;
     int done_items[2] = {0, 0};  // items of each slot issued so far
     bool ok = true;
+    const uint64_t pol_last = ptx::l2_policy_evict_last(), pol_first = ptx::l2_policy_evict_first();
     OMQ_TRUNK_ITEMS({
       if (ok) {
         // the previous item of this slot (its previous layer, or the previous position's last
@@ -462,12 +463,15 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
         const CUtensorMap* hm = l == 0 ? &tmIn : &tmS;
         const CUtensorMap* wm = l == 0 ? &tmWin : &tmW;
         const int wrow = l == 0 ? 0 : (l - 1) * C;
+        // scratch lines are rewritten by the next positions: keep them in L2; the input features
+        // are read once
+        const uint64_t pol = l == 0 ? pol_first : pol_last;
         for (int cb = 0; cb < CB && ok; ++cb) {
           if (!ptx::mbar_wait(&xempty[sx], px ^ 1, abort_flag, kWaitLimitNs)) { ok = false; break; }
           ptx::mbar_arrive_expect_tx(&xfull[sx], Cfg::kX);
           uint8_t* dst = x_ring + sx * Cfg::kX;
-          ptx::tma_load_2d(dst, hm, &xfull[sx], cb * kBlockK, h0);
-          ptx::tma_load_2d(dst + Cfg::kHaloBox * 128, hm, &xfull[sx], cb * kBlockK, h0 + Cfg::kHaloBox);
+          ptx::tma_load_2d_hint(dst, hm, &xfull[sx], cb * kBlockK, h0, pol);
+          ptx::tma_load_2d_hint(dst + Cfg::kHaloBox * 128, hm, &xfull[sx], cb * kBlockK, h0 + Cfg::kHaloBox, pol);
           x_issued[sx] = (int)px;
           if (++sx == Cfg::kXStages) { sx = 0; px ^= 1; }
           for (int tap = 0; tap < 9; ++tap) {
@@ -546,6 +550,7 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
     float* tr = reinterpret_cast<float*>(my_stage + Cfg::kStoreBufs * 2048);
     int buf = 0, t = 0;
     bool ok = true;
+    const uint64_t pol_last = ptx::l2_policy_evict_last(), pol_first = ptx::l2_policy_evict_first();
     OMQ_TRUNK_ITEMS({
       if (ok) {
         const int ch0 = q * 32;
@@ -614,7 +619,7 @@ __global__ void __launch_bounds__(HaloTCfg::kThreads, 1)
           ptx::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            ptx::tma_store_2d(om, sbuf, ch0, orow0 + jj * 32);
+            ptx::tma_store_2d_hint(om, sbuf, ch0, orow0 + jj * 32, last ? pol_first : pol_last);
             ptx::bulk_commit();
           }
           if (++buf == Cfg::kStoreBufs) buf = 0;
