@@ -303,6 +303,9 @@ typedef struct {
   int32_t dtype;             /* OMQ_DTYPE_BF16 (0, default) or OMQ_DTYPE_F16: the 16-bit type of the
                                 conv weights, activations and dense-layer operands (fp32 accumulate);
                                 F16 is the precision of the reference evaluator's fp16 autocast */
+  int32_t trunk_per_layer;   /* 0 (default): the whole trunk in one kernel where it applies (15x15
+                                boards, 128 filters); 1: one launch per conv everywhere (same
+                                results; for comparisons) */
 } omq_resnet_config;
 
 enum { OMQ_DTYPE_BF16 = 0, OMQ_DTYPE_F16 = 1 };

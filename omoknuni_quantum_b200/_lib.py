@@ -58,7 +58,7 @@ class ResNetConfig(ctypes.Structure):
                 ("num_blocks", ctypes.c_int32), ("filters", ctypes.c_int32),
                 ("num_actions", ctypes.c_int32), ("fc_policy_hidden", ctypes.c_int32),
                 ("fc_value_hidden", ctypes.c_int32), ("max_batch", ctypes.c_int32),
-                ("device", ctypes.c_int32), ("dtype", ctypes.c_int32)]
+                ("device", ctypes.c_int32), ("dtype", ctypes.c_int32), ("trunk_per_layer", ctypes.c_int32)]
 
 
 OMQ_DTYPE_BF16, OMQ_DTYPE_F16 = 0, 1

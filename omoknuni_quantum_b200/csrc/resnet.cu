@@ -1291,7 +1291,8 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
       (c.filters != 128 && c.filters != 256) || c.num_blocks < 0 || c.num_blocks > 64 ||
       c.num_actions < 1 || c.num_actions > kMaxActions || c.fc_policy_hidden < 1 ||
       c.fc_policy_hidden > 1024 || c.fc_value_hidden < 1 || c.fc_value_hidden > 1024 ||
-      c.max_batch < 1 || (c.dtype != OMQ_DTYPE_BF16 && c.dtype != OMQ_DTYPE_F16)) {
+      c.max_batch < 1 || (c.dtype != OMQ_DTYPE_BF16 && c.dtype != OMQ_DTYPE_F16) ||
+      (c.trunk_per_layer != 0 && c.trunk_per_layer != 1)) {
     set_error("bad resnet config");
     return OMQ_BAD_ARG;
   }
@@ -1342,7 +1343,7 @@ int omq_resnet_create(const omq_resnet_config* cfg, omq_resnet** out) {
   take(n->tc_heads ? (size_t)n->n1pad * n->k1p * 2 : 16);        // 11 W1
   take(n->tc_heads ? (size_t)n->n2pad * n->Hp * 2 : 16);         // 12 W2
   take(n->tc_heads ? (size_t)n->n3pad * n->k3p * 2 : 16);        // 13 W3
-  n->fused = (n->P == HaloTCfg::kRows && n->C == 128 && n->NB >= 1 && n->sm_count > 0) ? 1 : 0;
+  n->fused = (n->P == HaloTCfg::kRows && n->C == 128 && n->NB >= 1 && n->sm_count > 0 && !c.trunk_per_layer) ? 1 : 0;
   n->tslots = n->fused ? 2 * n->sm_count : 0;
   take(n->fused ? (size_t)3 * n->tslots * n->P * n->C * 2 : 16);  // 14 trunk scratch
   void* arena = nullptr;

@@ -189,12 +189,15 @@ class ResNetEvaluator:
     the reference's autocast it overflows above 65504."""
 
     def __init__(self, state_dict: Dict[str, torch.Tensor], board_size: int = 15,
-                 max_batch: int = 4096, device=None, dtype: str = "bf16"):
+                 max_batch: int = 4096, device=None, dtype: str = "bf16", trunk: str = "auto"):
         if not torch.cuda.is_available():
             raise RuntimeError("ResNetEvaluator needs a CUDA device (B200); there is no CPU fallback")
         if dtype not in DTYPES:
             raise ValueError(f"dtype must be one of {sorted(DTYPES)}")
         self.dtype = dtype
+        if trunk not in ("auto", "per_layer"):
+            raise ValueError("trunk is 'auto' (the whole-trunk kernel where it applies) or 'per_layer'")
+        self.trunk = trunk
         self.spec = spec_from_state_dict(state_dict, board_size)
         self.state_dict = {k: v.detach().cpu() for k, v in state_dict.items()}
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -222,7 +225,7 @@ class ResNetEvaluator:
         s = self.spec
         cfg = _lib.ResNetConfig(s.board_size, s.input_channels, s.num_blocks, s.filters, s.num_actions,
                                 s.fc_policy_hidden, s.fc_value_hidden, int(max_batch), self.device.index or 0,
-                                DTYPES[self.dtype][0])
+                                DTYPES[self.dtype][0], int(self.trunk == "per_layer"))
         h = ctypes.c_void_p()
         with torch.cuda.device(self.device):
             _lib.check(self.L.omq_resnet_create(ctypes.byref(cfg), ctypes.byref(h)), "omq_resnet_create")

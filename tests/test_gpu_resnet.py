@@ -239,3 +239,25 @@ def test_distinct_handles_from_concurrent_host_threads():
         x.join()
     for t in range(2):
         assert np.array_equal(seq[t], par[t]), t
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_whole_trunk_kernel_equals_per_layer_convs(dtype):
+    """The whole-trunk kernel (15x15 boards, 128 filters: one launch per forward, activations in
+    a per-CTA scratch) gives the same policies and values, bit for bit, as one conv launch per
+    layer, on batches below, at and above one position per CTA pair."""
+    from omoknuni_quantum_b200.resnet import ResNetEvaluator, ResNetSpec, init_state_dict
+    sd = init_state_dict(ResNetSpec(num_blocks=4, filters=128, fc_value_hidden=128), seed=8)
+    fused = ResNetEvaluator(sd, max_batch=2000, dtype=dtype)
+    layered = ResNetEvaluator(sd, max_batch=2000, dtype=dtype, trunk="per_layer")
+    assert fused.conv_launches_per_call == 1 and layered.conv_launches_per_call == 9
+    for n, seed in ((1, 21), (150, 22), (297, 23), (2000, 24)):
+        x = _features(n, seed=seed).cuda()
+        pf, vf = fused.evaluate_batch(x)
+        pl, vl = layered.evaluate_batch(x)
+        assert torch.equal(pf, pl) and torch.equal(vf, vl), n
+    assert fused.error() == 0 and layered.error() == 0
+    # 19x19 and 256 filters keep the per-layer kernel
+    big = ResNetEvaluator(init_state_dict(ResNetSpec(num_blocks=1, filters=256, fc_value_hidden=128), seed=1),
+                          max_batch=8)
+    assert big.conv_launches_per_call == 3
