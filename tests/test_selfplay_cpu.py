@@ -199,3 +199,60 @@ def test_counter_draws_are_visit_proportional_and_replayed_by_the_host_driver():
         for m in range(3):
             v = _fake_search(r.examples[m]["state"][None])[0]
             assert r.moves[m] == counter_choice(v, counter_draw(9, g, m))
+
+
+def test_device_roots_round_trip_for_every_game():
+    """The host side of device self-play: positions -> the engine's device root layout (boards,
+    chess root records + earlier-position counts, Go history planes + side / ko / passes + game
+    keys) -> positions again, unchanged; and the recorded-state decoders."""
+    from omoknuni_quantum_b200.chess import ChessPosition, random_position as chess_random
+    from omoknuni_quantum_b200.go import GoPosition
+    from omoknuni_quantum_b200.selfplay import _ChessGame, _GoGame, _GomokuGame
+    from omoknuni_quantum_b200.roots import random_roots
+
+    gm = _GomokuGame(15)
+    boards = list(random_roots(3, 4))
+    d = gm.device_roots(boards)
+    assert d["boards"].shape == (4, 225) and d["boards"].dtype == np.int8
+    for g in range(4):
+        assert np.array_equal(gm.device_position(d, g, boards[g], None), boards[g])
+        assert np.array_equal(gm.device_state(d["boards"][g].view(np.uint8)), boards[g])
+
+    cg = _ChessGame(8)
+    pos = [chess_random(11 + i) for i in range(3)] + [ChessPosition()]
+    d = cg.device_roots(pos)
+    assert d["records"].shape == (4, 101 * 80) and list(d["nprior"]) == [min(len(p.prior), 100) for p in pos]
+    for g, p in enumerate(pos):
+        q = cg.device_position(d, g, p, None)
+        assert q.root_records().tobytes() == p.root_records().tobytes()
+        assert q.fen() == p.fen() and q.result() == p.result() and q.reps == p.reps
+        assert cg.device_state(d["records"][g][:80]).tobytes() == p.record().tobytes()
+
+    go = _GoGame(9)
+    rng = np.random.default_rng(5)
+    gpos = []
+    for rules in ("chinese", "japanese", "korean"):
+        p = GoPosition(9, rules=rules)
+        for _ in range(15):
+            p.play(int(rng.choice(np.flatnonzero(p.legal_mask()))))
+        gpos.append(p)
+    gpos.append(GoPosition(9))
+    d = go.device_roots(gpos)
+    assert d["keys"].dtype == np.int64 and list(d["nkeys"]) == [len(p.keys) for p in gpos]
+    for g, p in enumerate(gpos):
+        row = [0, 0, 0, 0, 0] + go.device_game(p)
+        q = go.device_position(d, g, p, row)
+        assert np.array_equal(q.history_planes(), p.history_planes())
+        assert np.array_equal(q.meta(), p.meta()) and q.keys == p.keys
+        assert q.prisoners == p.prisoners and q.repeated == p.repeated and q.rules == p.rules
+        assert q.result() == p.result()
+        assert np.array_equal(go.device_state(d["history"][g].reshape(-1)), p.history_planes())
+
+
+def test_go_no_result_counts_as_a_draw():
+    """A Japanese third repetition is the reference's "no result" (GameResult 4): no winner."""
+    from omoknuni_quantum_b200.go import GoPosition
+    from omoknuni_quantum_b200.selfplay import _GoGame
+    p = GoPosition(9, rules="japanese")
+    p.repeated = True
+    assert p.result() == 4 and _GoGame(9).outcome(p) == 0
